@@ -1,0 +1,186 @@
+/*
+ * specfit_b200 — C ABI of the B200 (sm_100a) MoE verification path.
+ *
+ * Every entry point takes plain device pointers, sizes, dtype codes and a
+ * cudaStream_t passed as `void*` (NULL = the legacy default stream).  None of
+ * them allocates device memory: scratch buffers ("workspace") are passed in
+ * by the caller.  All device work is enqueued asynchronously on the given
+ * stream; the return value is a status code (SF_OK on success), and on
+ * failure sf_last_error() returns a message for the calling thread.
+ *
+ * Interface map to the SpecFit reference (paths inside the SpecFit tree;
+ * "transformers/..." = transformers/models/qwen3_moe/modeling_qwen3_moe.py):
+ *   sf_router_topk        Qwen3MoeTopKRouter.forward            transformers/...:263-272
+ *   sf_moe_dispatch       grouping in Qwen3OffloadedExperts     src/specfit/runtime/qwen3_offloaded_experts.py:111-122,173-178
+ *   sf_moe_gather         hidden_states[route_tokens], weights  src/specfit/runtime/qwen3_offloaded_experts.py:189-190
+ *   sf_grouped_swiglu     _expert_forward + mul_(w), per expert src/specfit/runtime/qwen3_offloaded_experts.py:38-62,126-138,194-198
+ *   sf_moe_combine        index_add_ reduction                  src/specfit/runtime/qwen3_offloaded_experts.py:144-163,200-202
+ *   sf_slot_fill_batch    slot.tensor.copy_(source)             src/specfit/runtime/gpu_expert_cache.py:556-561
+ *   sf_tree_attention     SDPA under the tree mask              transformers/...:156-195 with the mask of
+ *                                                               src/specfit/runtime/eagle3_types.py:450-473
+ */
+#ifndef SPECFIT_B200_H_
+#define SPECFIT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SF_API __attribute__((visibility("default")))
+#else
+#define SF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SF_OK 0
+#define SF_ERR_INVALID_ARGUMENT 1 /* maps to ValueError in the Python layer */
+#define SF_ERR_CUDA 2             /* a CUDA runtime call failed */
+#define SF_ERR_UNSUPPORTED 3      /* shape/dtype/device not supported */
+#define SF_ERR_WORKSPACE 4        /* workspace too small */
+
+/* Element types. */
+#define SF_DTYPE_F32 0
+#define SF_DTYPE_BF16 1
+
+/* Reduction order of sf_moe_combine. */
+#define SF_REDUCE_MODEL_DTYPE 0 /* sequential adds rounded to the model dtype (reference index_add_) */
+#define SF_REDUCE_F32 1         /* fp32 accumulation, one rounding at the end */
+
+/* Implementation choice of sf_grouped_swiglu_ex. */
+#define SF_SWIGLU_AUTO 0    /* tcgen05 path when the shape allows it, else SIMT */
+#define SF_SWIGLU_SIMT 1    /* CUDA-core kernel, any shape, f32 or bf16 */
+#define SF_SWIGLU_TCGEN05 2 /* tcgen05/TMEM + TMA kernel: bf16, H%64==0, I%64==0 */
+
+/* Message describing the last failure on the calling thread ("" if none). */
+SF_API const char* sf_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+SF_API int sf_abi_version(void);
+
+/*
+ * Sticky device-side status of the current device: nonzero once a kernel of
+ * this library gave up a bounded wait (it then skipped its remaining work and
+ * returned).  Synchronous: reads (and with reset != 0 clears) the word.
+ * No reference counterpart; the reference's GPU work is PyTorch library calls.
+ */
+SF_API int sf_device_status(int* status, int reset);
+
+/*
+ * Router: logits = hidden[T,H] @ router_weight[E,H]^T, rounded once to the
+ * model dtype from an exact (fp64) dot product; probs = softmax(logits) in
+ * fp32; top_k experts by (logit desc, expert id asc); weights = the top-k
+ * probs, divided by their sum when norm_topk_prob.
+ * Replaces Qwen3MoeTopKRouter.forward (transformers/...:263-272), which returns
+ * (probs, weights, indices).  `logits_out` (nullable) receives the rounded
+ * logits in the model dtype.  Requires E <= 1024, top_k <= 32, top_k <= E.
+ * `workspace` must hold sf_router_topk_workspace_bytes(T, E) bytes.
+ */
+SF_API size_t sf_router_topk_workspace_bytes(int64_t tokens, int num_experts);
+SF_API int sf_router_topk(const void* hidden, const void* router_weight, int dtype, int64_t tokens,
+                   int hidden_size, int num_experts, int top_k, int norm_topk_prob,
+                   float* probs, float* topk_weights, int64_t* topk_index, void* logits_out,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Dispatch: stable grouping of the T*K routes by expert id.
+ *   counts[E], offsets[E+1] (exclusive prefix of counts),
+ *   sorted_pos[T*K]: route positions t*K+k in ascending (expert, position)
+ *     order == torch.sort(top_k_index.reshape(-1), stable=True).indices
+ *     (qwen3_offloaded_experts.py:173); its per-expert blocks are the token
+ *     groups of torch.where(top_k_index == e) (:120-122);
+ *   inv_pos[T*K]: inverse permutation (route position -> sorted row);
+ *   active[E]: experts with a non-empty group, ascending, -1 padded;
+ *   num_active[1].
+ * An expert id outside [0, E) sets *error_flag to 1 (device int32, caller
+ * zeroes it) and that route is dropped.  Requires E <= 1024.
+ */
+SF_API int sf_moe_dispatch(const int64_t* topk_index, int64_t tokens, int top_k, int num_experts,
+                    int32_t* counts, int32_t* offsets, int32_t* sorted_pos, int32_t* inv_pos,
+                    int32_t* active, int32_t* num_active, int32_t* error_flag, void* stream);
+
+/*
+ * Gather: hidden_sorted[i,:] = hidden[sorted_pos[i] / K, :] and
+ * weights_sorted[i] = (float) topk_weights.flat[sorted_pos[i]]
+ * (qwen3_offloaded_experts.py:189-190).  weight_dtype may differ from dtype.
+ */
+SF_API int sf_moe_gather(const void* hidden, int dtype, int64_t tokens, int hidden_size,
+                  const void* topk_weights, int weight_dtype, int top_k,
+                  const int32_t* sorted_pos, void* hidden_sorted, float* weights_sorted,
+                  void* stream);
+
+/*
+ * Grouped SwiGLU over the active experts of one layer.  For every active
+ * expert e (active[0..*num_active)) and its rows r in [offsets[e], offsets[e+1]):
+ *   g,u   = hidden_sorted[r] @ gate_e^T, @ up_e^T        (rounded to dtype)
+ *   act   = silu(g) * u                                  (each op rounded)
+ *   out   = act @ down_e^T                               (rounded to dtype)
+ *   out_sorted[r] = round(out * weights_sorted[r])
+ * Expert e's packed weights [gate(I*H) | up(I*H) | down(H*I)] start at
+ * slot_storage + expert_slot[e] * slot_stride_elems (elements of dtype).
+ * act_workspace holds rows*I elements of dtype.
+ * Replaces _expert_forward (qwen3_offloaded_experts.py:38-62) and the
+ * weighting mul_ (:132-138, :198), for all experts of a layer in one call.
+ */
+SF_API int sf_grouped_swiglu(const void* hidden_sorted, const float* weights_sorted, int dtype,
+                      const int32_t* offsets, const int32_t* active, const int32_t* num_active,
+                      const int32_t* expert_slot, const void* slot_storage, int64_t slot_count,
+                      int64_t slot_stride_elems, int num_experts, int hidden_size,
+                      int intermediate_size, int64_t rows, void* act_workspace, void* out_sorted,
+                      void* stream);
+SF_API int sf_grouped_swiglu_ex(const void* hidden_sorted, const float* weights_sorted, int dtype,
+                         const int32_t* offsets, const int32_t* active, const int32_t* num_active,
+                         const int32_t* expert_slot, const void* slot_storage, int64_t slot_count,
+                         int64_t slot_stride_elems, int num_experts, int hidden_size,
+                         int intermediate_size, int64_t rows, void* act_workspace,
+                         void* out_sorted, int impl, void* stream);
+
+/*
+ * Combine: out[t,:] = sum over the token's K routes of out_sorted[inv_pos[t*K+k],:],
+ * added in ascending expert_rank[expert] (ties: ascending k) order.
+ * expert_rank == NULL gives the canonical ascending-expert-id order
+ * (ReductionMode.CANONICAL, qwen3_offloaded_experts.py:155-163, :200-202);
+ * the rank of each expert in the execution order gives ARRIVAL_ORDER (:144-149).
+ * reduce = SF_REDUCE_MODEL_DTYPE reproduces index_add_'s rounding after every
+ * add; SF_REDUCE_F32 accumulates in fp32.  out may not alias out_sorted.
+ */
+SF_API int sf_moe_combine(const void* out_sorted, int dtype, const int32_t* inv_pos,
+                   const int64_t* topk_index, const int32_t* expert_rank, int num_experts,
+                   int64_t tokens, int top_k, int hidden_size, int reduce, void* out,
+                   void* stream);
+
+/*
+ * Slot fill: n host->device copies dst[i] <- src[i] (bytes[i] each) on
+ * `stream`, one cudaMemcpyAsync per copy, in order.  Sources should be pinned
+ * for the copy to be asynchronous (gpu_expert_cache.py:556-561).
+ */
+SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const size_t* bytes, int n,
+                       void* stream);
+
+/*
+ * Tree attention (GQA): for query row i of head h (kv head h / (Hq/Hkv)),
+ * key j is visible when j < prefix_len, or when bit (j - prefix_len) of
+ * tree_bits[i * bit_words + ...] is set (little-endian uint32 words).
+ * q: [Hq, Tq, D] with strides (q_head_stride, q_row_stride) in elements,
+ * k/v: [Hkv, Tk, D] with (kv_head_stride, kv_row_stride), bf16, D == 128.
+ * out: [Tq, Hq, D] bf16 (the layout the o_proj consumes).
+ * workspace: sf_tree_attention_workspace_bytes(Hq, Tq, Tk) bytes.
+ * Replaces SDPA under the verification mask (transformers/...:172-186 with
+ * eagle3_types.py:450-473).
+ */
+SF_API size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len, int64_t kv_len);
+SF_API int sf_tree_attention(const void* q, const void* k, const void* v, const uint32_t* tree_bits,
+                      int bit_words, int64_t q_len, int64_t kv_len, int64_t prefix_len,
+                      int num_heads, int num_kv_heads, int head_dim, int64_t q_head_stride,
+                      int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                      float scale, void* out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECFIT_B200_H_ */

@@ -1,0 +1,107 @@
+"""ctypes binding of the C ABI in ``include/specfit_b200.h``.
+
+The library is loaded from the package directory (built in-tree by
+``python -m specfit_b200.build``).  There is no fallback: if the library is
+missing or a symbol is absent, importing an op raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libspecfit_b200.so"
+HEADER = PKG.parent / "include" / "specfit_b200.h"
+
+SF_OK = 0
+SF_ERR_INVALID_ARGUMENT = 1
+SF_ERR_CUDA = 2
+SF_ERR_UNSUPPORTED = 3
+SF_ERR_WORKSPACE = 4
+
+SF_DTYPE_F32 = 0
+SF_DTYPE_BF16 = 1
+
+SF_REDUCE_MODEL_DTYPE = 0
+SF_REDUCE_F32 = 1
+
+SF_SWIGLU_AUTO = 0
+SF_SWIGLU_SIMT = 1
+SF_SWIGLU_TCGEN05 = 2
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "sf_last_error": (ctypes.c_char_p, []),
+    "sf_abi_version": (_i32, []),
+    "sf_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
+    "sf_router_topk_workspace_bytes": (_sz, [_i64, _i32]),
+    "sf_router_topk": (_i32, [_vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
+                              _vp, _sz, _vp]),
+    "sf_moe_dispatch": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sf_moe_gather": (_i32, [_vp, _i32, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "sf_grouped_swiglu": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
+                                 _i32, _i64, _vp, _vp, _vp]),
+    "sf_grouped_swiglu_ex": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32,
+                                    _i32, _i32, _i64, _vp, _vp, _i32, _vp]),
+    "sf_moe_combine": (_i32, [_vp, _i32, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "sf_slot_fill_batch": (_i32, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
+                                  _i32, _vp]),
+    "sf_tree_attention_workspace_bytes": (_sz, [_i32, _i64, _i64]),
+    "sf_tree_attention": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i32, _i32,
+                                 _i64, _i64, _i64, _i64, _f32, _vp, _vp, _sz, _vp]),
+}
+
+
+class NativeError(RuntimeError):
+    """A CUDA or unsupported-configuration failure reported by the library."""
+
+
+def declared_symbols() -> list:
+    """Every entry point declared in include/specfit_b200.h."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^SF_API [^(]*?\b(sf_\w+)\(", text, flags=re.M)))
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m specfit_b200.build` "
+            "(there is no CPU fallback for the specfit_b200 path)"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_LAZY | os.RTLD_GLOBAL)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)  # AttributeError -> loud failure
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    msg = lib.sf_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status == SF_OK:
+        return
+    msg = last_error()
+    if status == SF_ERR_INVALID_ARGUMENT:
+        raise ValueError(f"{what}: {msg}")
+    raise NativeError(f"{what} failed (status {status}): {msg}")
+
+
+def device_status(reset: bool = False) -> int:
+    out = _i32(0)
+    check(lib.sf_device_status(ctypes.byref(out), int(reset)), "sf_device_status")
+    return out.value

@@ -1,0 +1,63 @@
+// Shared helpers for the specfit_b200 CUDA library (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "specfit_b200.h"
+
+namespace sf {
+
+// Records a message for sf_last_error() and returns the status unchanged.
+int set_error(int status, const char* fmt, ...);
+inline int ok() { return SF_OK; }
+
+#define SF_CHECK_ARG(cond, ...)                                   \
+  do {                                                            \
+    if (!(cond)) return ::sf::set_error(SF_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+#define SF_CHECK_CUDA(expr)                                                        \
+  do {                                                                             \
+    cudaError_t _e = (expr);                                                       \
+    if (_e != cudaSuccess)                                                         \
+      return ::sf::set_error(SF_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,          \
+                             cudaGetErrorString(_e), __FILE__, __LINE__);          \
+  } while (0)
+
+#define SF_CHECK_LAUNCH() SF_CHECK_CUDA(cudaGetLastError())
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int num_sms();  // cached SM count of the current device
+
+// ---------------------------------------------------------------------------
+// dtype helpers shared by kernels
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Round an fp32 value to the model dtype and back (identity for fp32).
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return to_f32(from_f32<T>(v));
+}
+
+// SiLU in fp32: v * sigmoid(v) = v / (1 + exp(-v)).
+__device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + expf(-v)); }
+
+}  // namespace sf

@@ -1,0 +1,34 @@
+// Internal interface between the sf_grouped_swiglu entry point and its two
+// implementations (CUDA-core and tcgen05).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sf {
+
+struct SwigluArgs {
+  const void* hidden_sorted;
+  const float* weights_sorted;
+  int dtype;
+  const int32_t* offsets;
+  const int32_t* active;
+  const int32_t* num_active;
+  const int32_t* expert_slot;
+  const void* slot_storage;
+  int64_t slot_count;
+  int64_t slot_stride;  // elements between consecutive slots
+  int num_experts;
+  int hidden;
+  int inter;
+  int64_t rows;
+  void* act_workspace;
+  void* out_sorted;
+};
+
+int swiglu_simt(const SwigluArgs& a, cudaStream_t stream);
+// Returns SF_ERR_UNSUPPORTED (without a message) when the shape does not fit.
+int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream);
+bool swiglu_tcgen05_supports(const SwigluArgs& a);
+
+}  // namespace sf

@@ -1,0 +1,439 @@
+// K3 (tensor cores): grouped SwiGLU on tcgen05/TMEM, operands staged by TMA.
+//
+// Same contract as the CUDA-core path (see swiglu_simt.cu), which restates
+// _expert_forward (src/specfit/runtime/qwen3_offloaded_experts.py:38-62) and
+// the weighting mul_ (:132-138, :198), for bf16 models with H % 128 == 0 and
+// I % 64 == 0 (Qwen3-30B-A3B: H = 2048, I = 768).
+//
+// Layout ("swap AB"): at verification sizes an expert sees a handful of rows
+// (m_e ~ T*K/E), far below a 128-row MMA tile, so the WEIGHT rows fill the
+// MMA's M dimension and the expert's token rows form N (16..128 per pass):
+//   phase 1: D[128 weight rows, N tokens] = W_gate|up[rows, H] . X_e[N, H]^T
+//   phase 2: D[128 hidden rows, N tokens] = W_down[rows, I]   . Act_e[N, I]^T
+// Both operands are K-major, loaded by TMA with 128-byte swizzling.  A phase-1
+// tile holds 64 gate rows and the 64 matching up rows, so SiLU(gate)*up is
+// fused into its epilogue.  The routing weight is fused into phase 2's.
+//
+// Each launch is persistent (one CTA per SM, 192 threads):
+//   warp 0      TMA producer (one lane), 6-stage shared-memory ring
+//   warp 1      TMEM allocator and MMA issuer (one lane)
+//   warps 2..5  epilogue: TMEM -> registers -> rounding -> global stores
+// Two TMEM accumulators (128 columns each) let the epilogue of one tile
+// overlap the MMAs of the next.  At these sizes the kernel streams expert
+// weights: every weight byte is read from HBM exactly once per layer.
+//
+// No TMA multicast is used anywhere in this file.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+#include "swiglu.h"
+
+namespace sf {
+
+__device__ int g_device_status;  // sticky device-side error word, see sf_device_status
+
+namespace {
+
+constexpr int kBM = 128;       // MMA M: weight rows per tile
+constexpr int kBK = 64;        // K elements per stage (one 128-byte swizzle atom)
+constexpr int kBN = 128;       // max token rows per pass (MMA N)
+constexpr int kStages = 6;
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kBBytes = kBN * kBK * 2;
+constexpr int kBBox = 16;      // token rows per B TMA box
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 2 * kBN;
+constexpr int kUpPitch = 17;   // padded row pitch of the gate/up exchange buffer
+
+struct __align__(8) SmemTail {
+  float upbuf[64 * kUpPitch];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+  int epi_go;
+};
+
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + (size_t)kStages * (kABytes + kBBytes) +
+                              sizeof(SmemTail);
+
+// Work unit = (tile, pass).  A tile is one expert x one block of 128 weight
+// rows; a pass is up to kBN of that expert's token rows.
+struct Unit {
+  int e, slot, m_tile, n0, npass;
+};
+
+template <int kPhase>
+struct TileSpace {
+  int m_tiles;  // weight-row tiles per expert
+  int k_blocks;
+  __device__ TileSpace(int H, int I) {
+    m_tiles = (kPhase == 1) ? I / 64 : H / kBM;
+    k_blocks = (kPhase == 1) ? H / kBK : I / kBK;
+  }
+};
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Iterates this CTA's units in a fixed order; every role walks the same list.
+template <typename F>
+__device__ __forceinline__ void for_each_unit(int m_tiles, const int32_t* offsets,
+                                              const int32_t* active, int n_active,
+                                              const int32_t* expert_slot, F&& f) {
+  const int tiles = n_active * m_tiles;
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int e = active[tile / m_tiles];
+    const int mt = tile % m_tiles;
+    const int r0 = offsets[e], r1 = offsets[e + 1];
+    const int slot = expert_slot[e];
+    for (int n0 = r0; n0 < r1; n0 += kBN) {
+      Unit u{e, slot, mt, n0, min(kBN, r1 - n0)};
+      if (!f(u)) return;
+    }
+  }
+}
+
+template <int kPhase>
+__global__ void __launch_bounds__(kThreads, 1)
+swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                 const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                 const int32_t* __restrict__ num_active, const int32_t* __restrict__ expert_slot,
+                 const float* __restrict__ w_sorted, int H, int I,
+                 __nv_bfloat16* __restrict__ out) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* a_stage = smem;
+  uint8_t* b_stage = smem + (size_t)kStages * kABytes;
+  SmemTail* tail = reinterpret_cast<SmemTail*>(b_stage + (size_t)kStages * kBBytes);
+  volatile int* abort_flag = &tail->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const TileSpace<kPhase> space(H, I);
+  const int n_active = *num_active;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(&tail->full[s], 1);
+      ptx::mbar_init(&tail->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&tail->acc_full[b], 1);
+      ptx::mbar_init(&tail->acc_empty[b], 128);
+    }
+    ptx::mbar_init(&tail->mma_done, 1);
+    tail->abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_w);
+    ptx::prefetch_tensormap(&tm_x);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(&tail->tmem_base, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = tail->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
+        const int nb = (u.npass + kBBox - 1) / kBBox;
+        const uint32_t bytes = kABytes + nb * kBBox * kBK * 2;
+        for (int kb = 0; kb < space.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!ptx::mbar_wait(&tail->empty[s], ph ^ 1, abort_flag)) return false;
+          ptx::mbar_arrive_expect_tx(&tail->full[s], bytes);
+          uint8_t* a = a_stage + (size_t)s * kABytes;
+          if (kPhase == 1) {
+            const int g0 = u.m_tile * 64;
+            ptx::tma_load_3d(a, &tm_w, &tail->full[s], kb * kBK, g0, u.slot);
+            ptx::tma_load_3d(a + kABytes / 2, &tm_w, &tail->full[s], kb * kBK, I + g0, u.slot);
+          } else {
+            ptx::tma_load_3d(a, &tm_w, &tail->full[s], kb * kBK, u.m_tile * kBM, u.slot);
+          }
+          uint8_t* b = b_stage + (size_t)s * kBBytes;
+          for (int q = 0; q < nb; ++q)
+            ptx::tma_load_2d(b + q * kBBox * kBK * 2, &tm_x, &tail->full[s], kb * kBK,
+                             u.n0 + q * kBBox);
+        }
+        return true;
+      });
+      // Let every load this thread issued land before the CTA can exit.
+      volatile int never = 0;
+      for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
+        ptx::mbar_wait(&tail->full[i % kStages], (i / kStages) & 1, &never);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, unit = 0;
+      for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
+        const int buf = unit & 1;
+        const uint32_t aph = (unit >> 1) & 1;
+        if (!ptx::mbar_wait(&tail->acc_empty[buf], aph ^ 1, abort_flag)) return false;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        const uint32_t npad = (u.npass + 15) & ~15;
+        const uint32_t idesc = ptx::idesc_bf16_f32(kBM, npad);
+        for (int kb = 0; kb < space.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!ptx::mbar_wait(&tail->full[s], ph, abort_flag)) return false;
+          ptx::tc_fence_after();
+          const uint64_t adesc = ptx::smem_desc_k_sw128(ptx::smem_u32(a_stage + (size_t)s * kABytes));
+          const uint64_t bdesc = ptx::smem_desc_k_sw128(ptx::smem_u32(b_stage + (size_t)s * kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes per K=16 step inside the 128-byte swizzle atom.
+            ptx::umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                          (kb | k) != 0);
+          }
+          ptx::umma_commit(&tail->empty[s]);
+        }
+        ptx::umma_commit(&tail->acc_full[buf]);
+        ++unit;
+        return true;
+      });
+      // Drain: the barrier fires once every MMA issued above has completed.
+      ptx::umma_commit(&tail->mma_done);
+      volatile int never = 0;
+      ptx::mbar_wait(&tail->mma_done, 0, &never);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may read
+    const int row = quad * 32 + lane;      // accumulator row = TMEM lane
+    uint32_t unit = 0;
+    for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
+      const int buf = unit & 1;
+      const uint32_t aph = (unit >> 1) & 1;
+      ptx::mbar_wait(&tail->acc_full[buf], aph, abort_flag);
+      // The four epilogue warps take one consistent go/stop decision before
+      // any of them enters the per-chunk named barriers below.
+      ptx::named_bar_sync(2, 128);
+      if (threadIdx.x == 64) tail->epi_go = !*abort_flag;
+      ptx::named_bar_sync(2, 128);
+      if (!tail->epi_go) return false;
+      ptx::tc_fence_after();
+      const int chunks = (u.npass + 15) / 16;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * kBN;
+      for (int c = 0; c < chunks; ++c) {
+        float v[16];
+        ptx::tmem_ld_16(tbase + c * 16, v);
+        if (kPhase == 1) {
+          // Rows 0..63 hold gate rows g0.., rows 64..127 the matching up rows.
+          if (row >= 64) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) tail->upbuf[(row - 64) * kUpPitch + i] = v[i];
+          }
+          ptx::named_bar_sync(1, 128);
+          if (row < 64) {
+            const int col = u.m_tile * 64 + row;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int j = c * 16 + i;
+              if (j < u.npass) {
+                const float g = bf16r(v[i]);
+                const float up = bf16r(tail->upbuf[row * kUpPitch + i]);
+                const float act = bf16r(bf16r(silu_f32(g)) * up);
+                out[(int64_t)(u.n0 + j) * I + col] = __float2bfloat16_rn(act);
+              }
+            }
+          }
+          ptx::named_bar_sync(1, 128);
+        } else {
+          const int col = u.m_tile * kBM + row;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = c * 16 + i;
+            if (j < u.npass) {
+              const int r = u.n0 + j;
+              const float y = bf16r(v[i]);
+              out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w_sorted[r]);
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tail->acc_empty[buf]);
+      ++unit;
+      return true;
+    });
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && tail->abort_flag) atomicExch(&g_device_status, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps.
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint32_t elem_strides[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
+                  strides_bytes, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SF_OK;
+}
+
+}  // namespace
+
+bool swiglu_tcgen05_supports(const SwigluArgs& a) {
+  return a.dtype == SF_DTYPE_BF16 && a.hidden % kBM == 0 && a.inter % 64 == 0 && a.hidden > 0 &&
+         a.inter > 0 && a.slot_stride % 8 == 0 && a.slot_stride >= 3LL * a.hidden * a.inter &&
+         a.slot_count > 0 && aligned16(a.slot_storage) && aligned16(a.hidden_sorted) &&
+         aligned16(a.act_workspace) && a.rows < (1LL << 31) && a.slot_count < (1LL << 31);
+}
+
+int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
+  if (!swiglu_tcgen05_supports(a))
+    return set_error(SF_ERR_UNSUPPORTED,
+                     "tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0 and 16-byte aligned buffers");
+  if (a.rows == 0) return SF_OK;
+  int dev = 0, major = 0;
+  SF_CHECK_CUDA(cudaGetDevice(&dev));
+  SF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  if (major != 10) return set_error(SF_ERR_UNSUPPORTED, "tcgen05 SwiGLU needs an sm_100 device");
+
+  const int H = a.hidden, I = a.inter;
+  const uint64_t slot_bytes = (uint64_t)a.slot_stride * 2;
+  const __nv_bfloat16* storage = static_cast<const __nv_bfloat16*>(a.slot_storage);
+  CUtensorMap tm_w1, tm_x1, tm_w2, tm_x2;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)H, (cuuint64_t)(2 * I), (cuuint64_t)a.slot_count};
+    cuuint64_t strides[2] = {(cuuint64_t)H * 2, slot_bytes};
+    cuuint32_t box[3] = {kBK, 64, 1};
+    if (int rc = encode_bf16(&tm_w1, storage, 3, dims, strides, box)) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)a.rows};
+    cuuint64_t strides[1] = {(cuuint64_t)H * 2};
+    cuuint32_t box[2] = {kBK, kBBox};
+    if (int rc = encode_bf16(&tm_x1, a.hidden_sorted, 2, dims, strides, box)) return rc;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)I, (cuuint64_t)H, (cuuint64_t)a.slot_count};
+    cuuint64_t strides[2] = {(cuuint64_t)I * 2, slot_bytes};
+    cuuint32_t box[3] = {kBK, kBM, 1};
+    if (int rc = encode_bf16(&tm_w2, storage + 2LL * I * H, 3, dims, strides, box)) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)I, (cuuint64_t)a.rows};
+    cuuint64_t strides[1] = {(cuuint64_t)I * 2};
+    cuuint32_t box[2] = {kBK, kBBox};
+    if (int rc = encode_bf16(&tm_x2, a.act_workspace, 2, dims, strides, box)) return rc;
+  }
+  SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kSmemBytes));
+  SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kSmemBytes));
+  const int grid = num_sms();
+  auto* act = static_cast<__nv_bfloat16*>(a.act_workspace);
+  swiglu_tc_kernel<1><<<grid, kThreads, kSmemBytes, stream>>>(
+      tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot, a.weights_sorted, H, I, act);
+  SF_CHECK_LAUNCH();
+  swiglu_tc_kernel<2><<<grid, kThreads, kSmemBytes, stream>>>(
+      tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot, a.weights_sorted, H, I,
+      static_cast<__nv_bfloat16*>(a.out_sorted));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}
+
+}  // namespace sf
+
+extern "C" int sf_device_status(int* status, int reset) {
+  using namespace sf;
+  SF_CHECK_ARG(status, "null pointer argument");
+  SF_CHECK_CUDA(cudaMemcpyFromSymbol(status, g_device_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    SF_CHECK_CUDA(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)));
+  }
+  return SF_OK;
+}
+
+extern "C" int sf_grouped_swiglu_ex(const void* hidden_sorted, const float* weights_sorted,
+                                    int dtype, const int32_t* offsets, const int32_t* active,
+                                    const int32_t* num_active, const int32_t* expert_slot,
+                                    const void* slot_storage, int64_t slot_count,
+                                    int64_t slot_stride_elems, int num_experts, int hidden_size,
+                                    int intermediate_size, int64_t rows, void* act_workspace,
+                                    void* out_sorted, int impl, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(hidden_size > 0 && intermediate_size > 0 && num_experts > 0 && rows >= 0,
+               "invalid sizes");
+  SF_CHECK_ARG(slot_count > 0 && slot_stride_elems >= 3LL * hidden_size * intermediate_size,
+               "slot_stride_elems must cover one packed expert");
+  if (rows == 0) return SF_OK;
+  SF_CHECK_ARG(hidden_sorted && weights_sorted && offsets && active && num_active &&
+                   expert_slot && slot_storage && act_workspace && out_sorted,
+               "null pointer argument");
+  SwigluArgs a{hidden_sorted, weights_sorted, dtype,       offsets,         active,
+               num_active,    expert_slot,    slot_storage, slot_count,     slot_stride_elems,
+               num_experts,   hidden_size,    intermediate_size, rows,      act_workspace,
+               out_sorted};
+  cudaStream_t s = as_stream(stream);
+  if (impl == SF_SWIGLU_SIMT) return swiglu_simt(a, s);
+  if (impl == SF_SWIGLU_TCGEN05) return swiglu_tcgen05(a, s);
+  SF_CHECK_ARG(impl == SF_SWIGLU_AUTO, "unknown implementation %d", impl);
+  if (swiglu_tcgen05_supports(a)) {
+    int major = 0, dev = 0;
+    SF_CHECK_CUDA(cudaGetDevice(&dev));
+    SF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major == 10) return swiglu_tcgen05(a, s);
+  }
+  return swiglu_simt(a, s);
+}
+
+extern "C" int sf_grouped_swiglu(const void* hidden_sorted, const float* weights_sorted, int dtype,
+                                 const int32_t* offsets, const int32_t* active,
+                                 const int32_t* num_active, const int32_t* expert_slot,
+                                 const void* slot_storage, int64_t slot_count,
+                                 int64_t slot_stride_elems, int num_experts, int hidden_size,
+                                 int intermediate_size, int64_t rows, void* act_workspace,
+                                 void* out_sorted, void* stream) {
+  return sf_grouped_swiglu_ex(hidden_sorted, weights_sorted, dtype, offsets, active, num_active,
+                              expert_slot, slot_storage, slot_count, slot_stride_elems,
+                              num_experts, hidden_size, intermediate_size, rows, act_workspace,
+                              out_sorted, SF_SWIGLU_AUTO, stream);
+}

@@ -1,0 +1,307 @@
+// K6: tree-masked GQA attention of the verification pass.
+//
+// Restates the attention of Qwen3MoeAttention.forward after the KV-cache
+// update (transformers/models/qwen3_moe/modeling_qwen3_moe.py:172-186: SDPA,
+// scale head_dim**-0.5, GQA) under the verification mask of
+// Eagle3DraftTree.verification_attention_mask (src/specfit/runtime/
+// eagle3_types.py:450-473): every query sees the committed prefix and, inside
+// the tree block, itself and its ancestors.  The mask arrives as one bit per
+// tree column (little-endian uint32 words per query row); prefix keys need no
+// bits.
+//
+// Split-KV ("flash-decoding") on CUDA cores: a CTA owns one KV head, a block
+// of 8 query rows and one KV range; its 8 warps are the 8 query heads that
+// share the KV head, so each K/V tile is staged in shared memory once for all
+// of them.  Scores use an online softmax in fp32; a second kernel merges the
+// per-split partial results and writes bf16 [Tq, Hq, D].
+#include <math.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace sf {
+namespace {
+
+constexpr int kD = 128;        // head_dim
+constexpr int kRows = 8;       // query rows per CTA
+constexpr int kTile = 64;      // keys per shared-memory tile
+constexpr int kKPitch = kD + 2;  // bf16 pitch of the K tile (bank-conflict free)
+constexpr int kMaxGroup = 8;   // query heads per KV head handled by one CTA
+constexpr int kMaxSplits = 32;
+
+struct Params {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const uint32_t* bits;
+  int bit_words;
+  int q_len, kv_len, prefix_len;
+  int num_heads, num_kv_heads, group;
+  int64_t q_hs, q_rs, kv_hs, kv_rs;
+  float scale;
+  int splits, keys_per_split;
+  float* part_o;   // [splits, Hq, Tq, D]
+  float* part_ml;  // [splits, Hq, Tq, 2]
+};
+
+__device__ __forceinline__ bool visible(const Params& p, int row, int key) {
+  if (key < p.prefix_len) return true;
+  const int j = key - p.prefix_len;
+  return (p.bits[(int64_t)row * p.bit_words + (j >> 5)] >> (j & 31)) & 1u;
+}
+
+__global__ void __launch_bounds__(kMaxGroup * 32)
+tree_attn_split_kernel(Params p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [kTile][kD]
+  __nv_bfloat16* ks = vs + kTile * kD;                                      // [kTile][kKPitch]
+  __nv_bfloat16* qs = ks + kTile * kKPitch;                                 // [group][kRows][kD]
+
+  const int kvh = blockIdx.x;
+  const int row0 = blockIdx.y * kRows;
+  const int split = blockIdx.z;
+  const int warp = threadIdx.x >> 5;  // query head within the group
+  const int lane = threadIdx.x & 31;
+  const int head = kvh * p.group + warp;
+  const bool head_ok = warp < p.group;
+  const int key_lo = split * p.keys_per_split;
+  const int key_hi = min(p.kv_len, key_lo + p.keys_per_split);
+
+  // Stage this warp's query rows (bf16, exact copies; the scale is applied
+  // to the fp32 scores).
+  __nv_bfloat16* qw = qs + warp * kRows * kD;
+  for (int r = 0; r < kRows; ++r) {
+    const int row = row0 + r;
+    for (int d = lane; d < kD; d += 32) {
+      __nv_bfloat16 qv = __float2bfloat16_rn(0.f);
+      if (head_ok && row < p.q_len) qv = p.q[(int64_t)head * p.q_hs + (int64_t)row * p.q_rs + d];
+      qw[r * kD + d] = qv;
+    }
+  }
+
+  float m[kRows], l[kRows], o[kRows][4];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[r][c] = 0.f;
+  }
+
+  for (int t0 = key_lo; t0 < key_hi; t0 += kTile) {
+    const int nk = min(kTile, key_hi - t0);
+    __syncthreads();
+    // Stage K (padded pitch) and V tiles: 64 keys x 128 dims, 8 bytes/thread.
+    for (int i = threadIdx.x; i < kTile * (kD / 4); i += blockDim.x) {
+      const int key = i / (kD / 4);
+      const int d4 = (i % (kD / 4)) * 4;
+      uint2 kv = make_uint2(0, 0), vv = make_uint2(0, 0);
+      if (key < nk) {
+        const int64_t off = (int64_t)kvh * p.kv_hs + (int64_t)(t0 + key) * p.kv_rs + d4;
+        kv = *reinterpret_cast<const uint2*>(p.k + off);
+        vv = *reinterpret_cast<const uint2*>(p.v + off);
+      }
+      *reinterpret_cast<uint32_t*>(&ks[key * kKPitch + d4]) = kv.x;
+      *reinterpret_cast<uint32_t*>(&ks[key * kKPitch + d4 + 2]) = kv.y;
+      *reinterpret_cast<uint2*>(&vs[key * kD + d4]) = vv;
+    }
+    __syncthreads();
+    if (!head_ok) continue;
+
+    // Scores: lane owns keys lane and lane+32 of the tile, all rows.
+    float s[kRows][2];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) s[r][0] = s[r][1] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < kD; d += 2) {
+      const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ks[lane * kKPitch + d]));
+      const float2 k1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ks[(lane + 32) * kKPitch + d]));
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        const float2 qv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qw[r * kD + d]));
+        s[r][0] = fmaf(qv.x, k0.x, fmaf(qv.y, k0.y, s[r][0]));
+        s[r][1] = fmaf(qv.x, k1.x, fmaf(qv.y, k1.y, s[r][1]));
+      }
+    }
+    // Mask, online softmax, and P.V (lane owns dims 4*lane .. 4*lane+3).
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const int row = row0 + r;
+      const bool rok = row < p.q_len;
+      const bool v0 = rok && lane < nk && visible(p, row, t0 + lane);
+      const bool v1 = rok && lane + 32 < nk && visible(p, row, t0 + lane + 32);
+      const float a0 = v0 ? s[r][0] * p.scale : -INFINITY;
+      const float a1 = v1 ? s[r][1] * p.scale : -INFINITY;
+      float tmax = fmaxf(a0, a1);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+      if (tmax == -INFINITY) continue;  // nothing visible in this tile for this row
+      const float mnew = fmaxf(m[r], tmax);
+      const float corr = (m[r] == -INFINITY) ? 0.f : expf(m[r] - mnew);
+      const float p0 = v0 ? expf(a0 - mnew) : 0.f;
+      const float p1 = v1 ? expf(a1 - mnew) : 0.f;
+      float psum = p0 + p1;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+      l[r] = l[r] * corr + psum;
+      m[r] = mnew;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[r][c] *= corr;
+      for (int j = 0; j < 32; ++j) {
+        const float pj0 = __shfl_sync(0xffffffffu, p0, j);
+        const float pj1 = __shfl_sync(0xffffffffu, p1, j);
+        if (pj0 != 0.f) {
+          const uint2 vv = *reinterpret_cast<const uint2*>(&vs[j * kD + lane * 4]);
+          const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv.x));
+          const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv.y));
+          o[r][0] = fmaf(pj0, va.x, o[r][0]);
+          o[r][1] = fmaf(pj0, va.y, o[r][1]);
+          o[r][2] = fmaf(pj0, vb.x, o[r][2]);
+          o[r][3] = fmaf(pj0, vb.y, o[r][3]);
+        }
+        if (pj1 != 0.f) {
+          const uint2 vv = *reinterpret_cast<const uint2*>(&vs[(j + 32) * kD + lane * 4]);
+          const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv.x));
+          const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vv.y));
+          o[r][0] = fmaf(pj1, va.x, o[r][0]);
+          o[r][1] = fmaf(pj1, va.y, o[r][1]);
+          o[r][2] = fmaf(pj1, vb.x, o[r][2]);
+          o[r][3] = fmaf(pj1, vb.y, o[r][3]);
+        }
+      }
+    }
+  }
+
+  if (!head_ok) return;
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const int row = row0 + r;
+    if (row >= p.q_len) break;
+    const int64_t idx = ((int64_t)split * p.num_heads + head) * p.q_len + row;
+    float4 ov = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
+    *reinterpret_cast<float4*>(p.part_o + idx * kD + lane * 4) = ov;
+    if (lane == 0) {
+      p.part_ml[idx * 2] = m[r];
+      p.part_ml[idx * 2 + 1] = l[r];
+    }
+  }
+}
+
+// Merge the splits of one (head, row) per warp; lane owns 4 dims.
+__global__ void tree_attn_merge_kernel(Params p, __nv_bfloat16* __restrict__ out) {
+  const int64_t pair = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (pair >= (int64_t)p.num_heads * p.q_len) return;
+  const int head = (int)(pair / p.q_len);
+  const int row = (int)(pair % p.q_len);
+  float gm = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) {
+    const int64_t idx = ((int64_t)s * p.num_heads + head) * p.q_len + row;
+    gm = fmaxf(gm, p.part_ml[idx * 2]);
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float denom = 0.f;
+  if (gm != -INFINITY) {
+    for (int s = 0; s < p.splits; ++s) {
+      const int64_t idx = ((int64_t)s * p.num_heads + head) * p.q_len + row;
+      const float ms = p.part_ml[idx * 2];
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - gm);
+      denom += w * p.part_ml[idx * 2 + 1];
+      const float4 ov = *reinterpret_cast<const float4*>(p.part_o + idx * kD + lane * 4);
+      acc[0] += w * ov.x;
+      acc[1] += w * ov.y;
+      acc[2] += w * ov.z;
+      acc[3] += w * ov.w;
+    }
+  }
+  const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  __nv_bfloat16* dst = out + ((int64_t)row * p.num_heads + head) * kD + lane * 4;
+  __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+  __nv_bfloat162 hi = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
+  uint2 packed;
+  packed.x = *reinterpret_cast<uint32_t*>(&lo);
+  packed.y = *reinterpret_cast<uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(dst) = packed;
+}
+
+int choose_splits(int num_kv_heads, int64_t q_len, int64_t kv_len) {
+  const int64_t row_blocks = (q_len + kRows - 1) / kRows;
+  const int64_t tiles = (kv_len + kTile - 1) / kTile;
+  int64_t want = (2 * (int64_t)num_sms() + num_kv_heads * row_blocks - 1) / (num_kv_heads * row_blocks);
+  want = std::max<int64_t>(1, std::min<int64_t>(want, std::min<int64_t>(tiles, kMaxSplits)));
+  return (int)want;
+}
+
+}  // namespace
+}  // namespace sf
+
+extern "C" size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len, int64_t kv_len) {
+  if (num_heads <= 0 || q_len <= 0 || kv_len <= 0) return 0;
+  return (size_t)sf::kMaxSplits * num_heads * q_len * (sf::kD + 2) * sizeof(float);
+}
+
+extern "C" int sf_tree_attention(const void* q, const void* k, const void* v,
+                                 const uint32_t* tree_bits, int bit_words, int64_t q_len,
+                                 int64_t kv_len, int64_t prefix_len, int num_heads,
+                                 int num_kv_heads, int head_dim, int64_t q_head_stride,
+                                 int64_t q_row_stride, int64_t kv_head_stride,
+                                 int64_t kv_row_stride, float scale, void* out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(head_dim == kD, "head_dim must be 128");
+  SF_CHECK_ARG(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+               "num_heads must be a positive multiple of num_kv_heads");
+  SF_CHECK_ARG(num_heads / num_kv_heads <= kMaxGroup, "at most 8 query heads per KV head");
+  SF_CHECK_ARG(q_len >= 0 && kv_len >= 0 && prefix_len >= 0 && prefix_len <= kv_len,
+               "invalid lengths");
+  SF_CHECK_ARG(q_len < (1 << 30) && kv_len < (1 << 30), "sequence too long");
+  if (q_len == 0) return SF_OK;
+  SF_CHECK_ARG(q && k && v && out && workspace, "null pointer argument");
+  SF_CHECK_ARG(kv_len == prefix_len || (tree_bits && (int64_t)bit_words * 32 >= kv_len - prefix_len),
+               "tree_bits must cover kv_len - prefix_len columns");
+  SF_CHECK_ARG(q_row_stride % 2 == 0 && q_head_stride % 2 == 0, "q strides must be even");
+  SF_CHECK_ARG(kv_row_stride % 4 == 0 && kv_head_stride % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(k) & 7u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(v) & 7u) == 0,
+               "k/v rows must be 8-byte aligned");
+  if (workspace_bytes < sf_tree_attention_workspace_bytes(num_heads, q_len, kv_len))
+    return set_error(SF_ERR_WORKSPACE, "tree attention workspace needs %zu bytes",
+                     sf_tree_attention_workspace_bytes(num_heads, q_len, kv_len));
+  Params p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.bits = tree_bits;
+  p.bit_words = bit_words;
+  p.q_len = (int)q_len;
+  p.kv_len = (int)kv_len;
+  p.prefix_len = (int)prefix_len;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.group = num_heads / num_kv_heads;
+  p.q_hs = q_head_stride;
+  p.q_rs = q_row_stride;
+  p.kv_hs = kv_head_stride;
+  p.kv_rs = kv_row_stride;
+  p.scale = scale;
+  p.splits = choose_splits(num_kv_heads, q_len, kv_len);
+  const int64_t tiles = (kv_len + kTile - 1) / kTile;
+  p.keys_per_split = (int)(((tiles + p.splits - 1) / p.splits) * kTile);
+  p.splits = (int)((kv_len + p.keys_per_split - 1) / p.keys_per_split);
+  if (p.splits < 1) p.splits = 1;
+  p.part_o = static_cast<float*>(workspace);
+  p.part_ml = p.part_o + (size_t)p.splits * num_heads * q_len * kD;
+  cudaStream_t s = as_stream(stream);
+  dim3 grid((unsigned)num_kv_heads, (unsigned)((q_len + kRows - 1) / kRows), (unsigned)p.splits);
+  const size_t smem = (size_t)(kTile * kD + kTile * kKPitch + kMaxGroup * kRows * kD) * 2;
+  SF_CHECK_CUDA(cudaFuncSetAttribute(tree_attn_split_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  tree_attn_split_kernel<<<grid, kMaxGroup * 32, smem, s>>>(p);
+  SF_CHECK_LAUNCH();
+  const int64_t pairs = (int64_t)num_heads * q_len;
+  tree_attn_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(out));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}

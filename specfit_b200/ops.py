@@ -1,0 +1,291 @@
+"""Torch-tensor front end of the native kernels.
+
+Each function validates its tensors, allocates outputs and workspace with
+torch's caching allocator (the C ABI itself never allocates), and enqueues the
+kernel on the current CUDA stream.  Everything is asynchronous unless noted.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.SF_DTYPE_F32, torch.bfloat16: N.SF_DTYPE_BF16}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dtype}") from None
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise ValueError("specfit_b200 ops need CUDA tensors")
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+# ---------------------------------------------------------------------------
+# K1 router
+
+
+def router_topk(hidden: torch.Tensor, weight: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
+                return_logits: bool = False):
+    """``Qwen3MoeTopKRouter.forward`` on the GPU.
+
+    Returns ``(probs[T,E] f32, weights[T,K] f32, indices[T,K] int64)`` and,
+    with ``return_logits``, the rounded logits in the model dtype."""
+    dev = _require_cuda(hidden, weight)
+    h = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+    w = weight.contiguous()
+    if w.dtype != h.dtype:
+        raise ValueError("router weight and hidden states must share a dtype")
+    tokens, hid = h.shape
+    experts = w.shape[0]
+    if w.shape[1] != hid:
+        raise ValueError("router weight width must equal the hidden size")
+    probs = torch.empty(tokens, experts, dtype=torch.float32, device=dev)
+    topw = torch.empty(tokens, top_k, dtype=torch.float32, device=dev)
+    topi = torch.empty(tokens, top_k, dtype=torch.int64, device=dev)
+    logits = torch.empty(tokens, experts, dtype=h.dtype, device=dev) if return_logits else None
+    ws_bytes = N.lib.sf_router_topk_workspace_bytes(tokens, experts)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    N.check(
+        N.lib.sf_router_topk(h.data_ptr(), w.data_ptr(), dtype_code(h.dtype), tokens, hid, experts,
+                             top_k, int(bool(norm_topk_prob)), probs.data_ptr(), topw.data_ptr(),
+                             topi.data_ptr(), _ptr(logits), ws.data_ptr(), ws_bytes, _stream(dev)),
+        "sf_router_topk",
+    )
+    if return_logits:
+        return probs, topw, topi, logits
+    return probs, topw, topi
+
+
+# ---------------------------------------------------------------------------
+# K2 dispatch + gather
+
+
+@dataclass
+class Dispatch:
+    counts: torch.Tensor  # [E] int32
+    offsets: torch.Tensor  # [E+1] int32
+    sorted_pos: torch.Tensor  # [T*K] int32
+    inv_pos: torch.Tensor  # [T*K] int32
+    active: torch.Tensor  # [E] int32, -1 padded
+    num_active: torch.Tensor  # [1] int32
+    error: torch.Tensor  # [1] int32
+    tokens: int
+    top_k: int
+    num_experts: int
+
+
+def moe_dispatch(top_k_index: torch.Tensor, num_experts: int) -> Dispatch:
+    dev = _require_cuda(top_k_index)
+    if top_k_index.dtype != torch.int64 or top_k_index.ndim != 2:
+        raise ValueError("top_k_index must be int64 [tokens, top_k]")
+    idx = top_k_index.contiguous()
+    tokens, top_k = idx.shape
+    n = tokens * top_k
+    i32 = dict(dtype=torch.int32, device=dev)
+    # One allocation for every int32 output keeps the host overhead low.
+    buf = torch.empty(num_experts + (num_experts + 1) + 2 * n + num_experts + 2, **i32)
+    counts = buf[:num_experts]
+    offsets = buf[num_experts: 2 * num_experts + 1]
+    sorted_pos = buf[2 * num_experts + 1: 2 * num_experts + 1 + n]
+    inv_pos = buf[2 * num_experts + 1 + n: 2 * num_experts + 1 + 2 * n]
+    active = buf[2 * num_experts + 1 + 2 * n: 3 * num_experts + 1 + 2 * n]
+    num_active = buf[3 * num_experts + 1 + 2 * n: 3 * num_experts + 2 + 2 * n]
+    error = buf[3 * num_experts + 2 + 2 * n:]
+    error.zero_()
+    N.check(
+        N.lib.sf_moe_dispatch(idx.data_ptr(), tokens, top_k, num_experts, counts.data_ptr(),
+                              offsets.data_ptr(), sorted_pos.data_ptr(), inv_pos.data_ptr(),
+                              active.data_ptr(), num_active.data_ptr(), error.data_ptr(),
+                              _stream(dev)),
+        "sf_moe_dispatch",
+    )
+    return Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, error, tokens, top_k,
+                    num_experts)
+
+
+def moe_gather(hidden: torch.Tensor, top_k_weights: torch.Tensor, d: Dispatch,
+               out_hidden: torch.Tensor | None = None, out_weights: torch.Tensor | None = None):
+    dev = _require_cuda(hidden, top_k_weights)
+    h = hidden.contiguous()
+    w = top_k_weights.contiguous()
+    rows = d.tokens * d.top_k
+    xs = out_hidden if out_hidden is not None else torch.empty(rows, h.shape[1], dtype=h.dtype,
+                                                                device=dev)
+    ws = out_weights if out_weights is not None else torch.empty(rows, dtype=torch.float32,
+                                                                  device=dev)
+    N.check(
+        N.lib.sf_moe_gather(h.data_ptr(), dtype_code(h.dtype), d.tokens, h.shape[1], w.data_ptr(),
+                            dtype_code(w.dtype), d.top_k, d.sorted_pos.data_ptr(), xs.data_ptr(),
+                            ws.data_ptr(), _stream(dev)),
+        "sf_moe_gather",
+    )
+    return xs, ws
+
+
+# ---------------------------------------------------------------------------
+# K3 grouped SwiGLU
+
+
+def grouped_swiglu(hidden_sorted: torch.Tensor, weights_sorted: torch.Tensor, d: Dispatch,
+                   expert_slot: torch.Tensor, storage: torch.Tensor, hidden_size: int,
+                   intermediate_size: int, impl: int = N.SF_SWIGLU_AUTO,
+                   active: torch.Tensor | None = None, num_active: torch.Tensor | None = None,
+                   act_workspace: torch.Tensor | None = None, out: torch.Tensor | None = None):
+    """Weighted SwiGLU rows for every active expert, in dispatch order.
+
+    ``storage`` is ``[slots, >= 3*H*I]`` packed expert slots; ``expert_slot``
+    (int32 [E]) names the slot of each expert.  ``active``/``num_active``
+    default to the dispatch's (a subset may be passed to compute one wave)."""
+    dev = _require_cuda(hidden_sorted, weights_sorted, expert_slot, storage)
+    if storage.dtype != hidden_sorted.dtype:
+        raise ValueError("expert storage and hidden states must share a dtype")
+    rows = hidden_sorted.shape[0]
+    act = act_workspace if act_workspace is not None else torch.empty(
+        max(rows, 1), intermediate_size, dtype=hidden_sorted.dtype, device=dev)
+    y = out if out is not None else torch.empty(rows, hidden_size, dtype=hidden_sorted.dtype,
+                                                device=dev)
+    act_list = d.active if active is None else active
+    n_act = d.num_active if num_active is None else num_active
+    N.check(
+        N.lib.sf_grouped_swiglu_ex(
+            hidden_sorted.data_ptr(), weights_sorted.data_ptr(), dtype_code(hidden_sorted.dtype),
+            d.offsets.data_ptr(), act_list.data_ptr(), n_act.data_ptr(), expert_slot.data_ptr(),
+            storage.data_ptr(), storage.shape[0], storage.stride(0), d.num_experts, hidden_size,
+            intermediate_size, rows, act.data_ptr(), y.data_ptr(), impl, _stream(dev)),
+        "sf_grouped_swiglu",
+    )
+    return y
+
+
+# ---------------------------------------------------------------------------
+# K4 combine
+
+
+def moe_combine(out_sorted: torch.Tensor, d: Dispatch, top_k_index: torch.Tensor,
+                expert_rank: torch.Tensor | None = None, reduce: int = N.SF_REDUCE_MODEL_DTYPE,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _require_cuda(out_sorted, top_k_index)
+    res = out if out is not None else torch.empty(d.tokens, out_sorted.shape[1],
+                                                  dtype=out_sorted.dtype, device=dev)
+    if d.tokens == 0:
+        return res
+    N.check(
+        N.lib.sf_moe_combine(out_sorted.data_ptr(), dtype_code(out_sorted.dtype),
+                             d.inv_pos.data_ptr(), top_k_index.contiguous().data_ptr(),
+                             _ptr(expert_rank), d.num_experts, d.tokens, d.top_k,
+                             out_sorted.shape[1], reduce, res.data_ptr(), _stream(dev)),
+        "sf_moe_combine",
+    )
+    return res
+
+
+# ---------------------------------------------------------------------------
+# K5 slot fill
+
+
+def slot_fill_batch(dsts, srcs, stream: torch.cuda.Stream) -> None:
+    """Host->device copies ``dst[i].copy_(src[i])`` on ``stream``."""
+    n = len(dsts)
+    if n == 0:
+        return
+    d_arr = (ctypes.c_void_p * n)(*[t.data_ptr() for t in dsts])
+    s_arr = (ctypes.c_void_p * n)(*[t.data_ptr() for t in srcs])
+    b_arr = (ctypes.c_size_t * n)(*[t.numel() * t.element_size() for t in dsts])
+    for dst, src in zip(dsts, srcs):
+        if dst.numel() * dst.element_size() != src.numel() * src.element_size():
+            raise ValueError("slot fill source and destination sizes differ")
+    N.check(N.lib.sf_slot_fill_batch(d_arr, s_arr, b_arr, n, stream.cuda_stream),
+            "sf_slot_fill_batch")
+
+
+# ---------------------------------------------------------------------------
+# K6 tree attention
+
+
+def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits: torch.Tensor | None,
+                   prefix_len: int, scale: float | None = None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Masked GQA attention.  ``q[Hq, Tq, D]``, ``k/v[Hkv, Tk, D]`` (bf16, any
+    strides with unit stride on D); keys ``< prefix_len`` are visible to every
+    query, tree key j is visible to row i when bit j of ``tree_bits[i]`` is
+    set.  Returns ``[Tq, Hq, D]`` bf16."""
+    dev = _require_cuda(q, k, v)
+    hq, tq, dim = q.shape
+    hkv, tk, _ = k.shape
+    if q.stride(2) != 1 or k.stride(2) != 1 or v.stride(2) != 1:
+        raise ValueError("head_dim must be contiguous")
+    if k.stride() != v.stride():
+        raise ValueError("k and v must share strides")
+    res = out if out is not None else torch.empty(tq, hq, dim, dtype=q.dtype, device=dev)
+    if tree_bits is not None:
+        bits = tree_bits.contiguous()
+        words = bits.shape[1]
+    else:
+        bits, words = None, 0
+    ws_bytes = N.lib.sf_tree_attention_workspace_bytes(hq, tq, tk)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    sc = float(dim ** -0.5 if scale is None else scale)
+    N.check(
+        N.lib.sf_tree_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(bits), words, tq, tk,
+                                prefix_len, hq, hkv, dim, q.stride(0), q.stride(1), k.stride(0),
+                                k.stride(1), sc, res.data_ptr(), ws.data_ptr(), ws_bytes,
+                                _stream(dev)),
+        "sf_tree_attention",
+    )
+    return res
+
+
+def tree_bits_from_parents(parent_ids, device) -> torch.Tensor:
+    """Ancestor bitmask of a verification tree: row i (0 = the pending seed,
+    i >= 1 = node i) has bit j set when column j is i itself or an ancestor
+    (``Eagle3DraftTree.verification_attention_mask``,
+    ``runtime/eagle3_types.py:450-473``).  int32 words, little-endian bits."""
+    q = 1 + len(parent_ids)
+    words = (q + 31) // 32
+    rows = [0] * q  # python ints as bitsets
+    rows[0] = 1
+    for node, parent in enumerate(parent_ids, start=1):
+        rows[node] = rows[parent] | (1 << node)
+    data = []
+    for r in rows:
+        for w in range(words):
+            word = (r >> (32 * w)) & 0xFFFFFFFF
+            data.append(word - (1 << 32) if word >= (1 << 31) else word)
+    return torch.tensor(data, dtype=torch.int32).view(q, words).to(device)
+
+
+def tree_bits_from_mask(mask: torch.Tensor, prefix_len: int) -> torch.Tensor:
+    """Pack a boolean ``[Tq, Tk]`` mask's tree block (columns >= prefix_len)
+    into int32 words on the mask's device."""
+    tree = mask[:, prefix_len:].to(torch.int64)
+    tq, cols = tree.shape
+    words = max(1, (cols + 31) // 32)
+    pad = words * 32 - cols
+    if pad:
+        tree = torch.nn.functional.pad(tree, (0, pad))
+    tree = tree.view(tq, words, 32)
+    shifts = torch.arange(32, device=mask.device, dtype=torch.int64)
+    packed = (tree << shifts).sum(-1)
+    packed = torch.where(packed >= (1 << 31), packed - (1 << 32), packed)
+    return packed.to(torch.int32)

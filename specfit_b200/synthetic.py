@@ -1,0 +1,134 @@
+"""Seeded synthetic inputs for the verification-path workloads.
+
+No dataset or checkpoint is used anywhere: weights are random-init with the
+Qwen3-30B-A3B shapes, tokens are uniform over the vocabulary, and trees and
+routes come from fixed seeds.  Generation order is part of the contract (the
+committed golden fixtures were produced from exactly these draws), so do not
+reorder draws.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+# Qwen3-30B-A3B shapes (the reference's target model).
+HIDDEN = 2048
+NUM_EXPERTS = 128
+TOP_K = 8
+MOE_INTER = 768
+NUM_LAYERS = 48
+NUM_HEADS = 32
+NUM_KV_HEADS = 4
+HEAD_DIM = 128
+VOCAB = 151936
+ROPE_THETA = 1.0e6
+RMS_EPS = 1.0e-6
+
+
+@dataclass(frozen=True)
+class MoeLayerWeights:
+    router: torch.Tensor  # [E, H]
+    gate_up: torch.Tensor  # [E, 2I, H]
+    down: torch.Tensor  # [E, H, I]
+
+    def packed(self, expert: int) -> torch.Tensor:
+        """One packed slot ``[gate | up | down]`` flattened (the packed-v1
+        expert row, ``adapters/qwen3_packed_checkpoint.py:20-23``)."""
+        inter = self.down.shape[2]
+        return torch.cat(
+            (
+                self.gate_up[expert, :inter].reshape(-1),
+                self.gate_up[expert, inter:].reshape(-1),
+                self.down[expert].reshape(-1),
+            )
+        )
+
+    def packed_all(self) -> torch.Tensor:
+        """``[E, 3*H*I]`` packed slots."""
+        return torch.stack([self.packed(e) for e in range(self.router.shape[0])])
+
+
+def config1_inputs(seed: int = 0, tokens: int = 32):
+    """Configuration 1: one MoE block in fp32.
+
+    ``torch.Generator().manual_seed(seed)``; draws, in this order,
+    ``W_router[128,2048]``, ``W_gate_up[128,1536,2048]``, ``W_down[128,2048,768]``
+    (all N(0,1)*0.02, fp32), then ``x[tokens,2048]`` N(0,1).
+    """
+    g = torch.Generator().manual_seed(seed)
+    router = torch.randn(NUM_EXPERTS, HIDDEN, generator=g) * 0.02
+    gate_up = torch.randn(NUM_EXPERTS, 2 * MOE_INTER, HIDDEN, generator=g) * 0.02
+    down = torch.randn(NUM_EXPERTS, HIDDEN, MOE_INTER, generator=g) * 0.02
+    x = torch.randn(tokens, HIDDEN, generator=g)
+    return MoeLayerWeights(router, gate_up, down), x
+
+
+def bf16_layer_inputs(seed: int, tokens: int, hidden: int = HIDDEN, experts: int = NUM_EXPERTS,
+                      inter: int = MOE_INTER, x_scale: float = 1.0):
+    """One bf16 MoE layer: N(0,0.02) weights and N(0,1)*x_scale inputs.
+
+    Draw order: router, gate_up, down, x (each fp32 then cast to bf16)."""
+    g = torch.Generator().manual_seed(seed)
+    router = (torch.randn(experts, hidden, generator=g) * 0.02).to(torch.bfloat16)
+    gate_up = (torch.randn(experts, 2 * inter, hidden, generator=g) * 0.02).to(torch.bfloat16)
+    down = (torch.randn(experts, hidden, inter, generator=g) * 0.02).to(torch.bfloat16)
+    x = (torch.randn(tokens, hidden, generator=g) * x_scale).to(torch.bfloat16)
+    return MoeLayerWeights(router, gate_up, down), x
+
+
+def zipf_routes(tokens: int, layer: int, seed: int, experts: int = NUM_EXPERTS,
+                top_k: int = TOP_K, s: float = 1.1) -> np.ndarray:
+    """Configurations 3 and 5: per-layer Zipf(s) routes.
+
+    ``perm = randperm(experts)`` seeded by ``seed*1000+layer``; the expert of
+    rank r (1-based) has weight r**-s; each token draws ``top_k`` distinct
+    experts by Gumbel-top-k (sampling without replacement).  Returns
+    ``int64[tokens, top_k]`` in draw order."""
+    rng = np.random.default_rng(seed * 1000 + layer)
+    perm = rng.permutation(experts)
+    ranks = np.empty(experts, dtype=np.float64)
+    ranks[perm] = np.arange(1, experts + 1)
+    logw = -s * np.log(ranks)
+    gumbel = rng.gumbel(size=(tokens, experts))
+    keys = logw[None, :] + gumbel
+    return np.argsort(-keys, axis=1, kind="stable")[:, :top_k].astype(np.int64)
+
+
+def random_tree(num_nodes: int, max_depth: int, max_branch: int, seed: int, vocab: int = VOCAB):
+    """Deterministic synthetic draft tree.
+
+    Parents precede children (1-based ids, 0 = the pending seed), depth <=
+    ``max_depth``, at most ``max_branch`` children per node, distinct sibling
+    tokens: the invariants ``Eagle3DraftTree`` validates
+    (``runtime/eagle3_types.py:336-400``).  Later nodes are preferred as
+    parents so the tree reaches its depth.  Returns
+    ``(token_ids, parent_ids, depths)``."""
+    rng = np.random.default_rng(seed)
+    parents: list = []
+    depths: list = []
+    tokens: list = []
+    child_count = {0: 0}
+    node_depth = {0: 0}
+    sibling_tokens: dict = {0: set()}
+    while len(parents) < num_nodes:
+        candidates = [n for n in range(len(parents) + 1)
+                      if node_depth[n] < max_depth and child_count[n] < max_branch]
+        if not candidates:
+            raise ValueError("tree shape cannot hold that many nodes")
+        weights = np.array([1.0 + n for n in candidates], dtype=np.float64)
+        parent = int(rng.choice(candidates, p=weights / weights.sum()))
+        node = len(parents) + 1
+        token = int(rng.integers(0, vocab))
+        while token in sibling_tokens[parent]:
+            token = int(rng.integers(0, vocab))
+        sibling_tokens[parent].add(token)
+        parents.append(parent)
+        depths.append(node_depth[parent] + 1)
+        tokens.append(token)
+        child_count[parent] += 1
+        child_count[node] = 0
+        node_depth[node] = node_depth[parent] + 1
+        sibling_tokens[node] = set()
+    return tuple(tokens), tuple(parents), tuple(depths)

@@ -1,0 +1,317 @@
+"""Kernel parity on the GPU: each native kernel against the CPU oracle and the
+reference-generated golden fixtures.  Integer outputs must match bit for bit;
+floating-point outputs within the stated tolerances."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as mo
+from oracle import tree_oracle as to
+from specfit_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+# bf16 tolerance of the verification path (max abs error, cosine).
+ATOL_BF16 = 2e-2
+COS_MIN = 0.999
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from specfit_b200 import ops as _ops
+
+    return _ops
+
+
+def bits_to_f32(bits):
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+
+
+# ---------------------------------------------------------------- K1 router
+
+
+def test_router_cfg1_f32_matches_reference_golden(ops, golden_dir):
+    g = np.load(golden_dir / "moe_cfg1_f32.npz")
+    weights, x = synthetic.config1_inputs(seed=0, tokens=32)
+    probs, w, idx, logits = ops.router_topk(x.to(DEV), weights.router.to(DEV), 8, True,
+                                            return_logits=True)
+    assert np.array_equal(idx.cpu().numpy(), g["idx"])
+    np.testing.assert_allclose(w.cpu().numpy(), g["weights"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(probs.cpu().numpy(), g["probs"], rtol=1e-5, atol=1e-8)
+    # Logits: correctly rounded f32 == the oracle's, bit for bit.
+    _, _, _, olog = mo.router_topk(x.numpy(), weights.router.numpy(), 8, True, "f32")
+    assert np.array_equal(logits.cpu().numpy(), olog)
+
+
+@pytest.mark.parametrize("seed,tokens", [(11, 65), (12, 129), (13, 512), (14, 1), (15, 7)])
+def test_router_bf16_bit_exact_vs_oracle(ops, seed, tokens):
+    weights, x = synthetic.bf16_layer_inputs(seed=seed, tokens=tokens, inter=64)
+    probs, w, idx, logits = ops.router_topk(x.to(DEV), weights.router.to(DEV), 8, True,
+                                            return_logits=True)
+    op, ow, oi, ol = mo.router_topk(x.float().numpy(), weights.router.float().numpy(), 8, True, "bf16")
+    assert np.array_equal(logits.float().cpu().numpy(), ol)
+    assert np.array_equal(idx.cpu().numpy(), oi)
+    np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(probs.cpu().numpy(), op, rtol=2e-6, atol=1e-9)
+
+
+def test_router_bf16_t65_vs_reference_golden(ops, golden_dir):
+    """Against the reference's own bf16 router: the same expert set wherever
+    the reference's logits equal the exact ones and no tie sits at the cut."""
+    g = np.load(golden_dir / "moe_bf16_t65.npz")
+    weights, x = synthetic.bf16_layer_inputs(seed=11, tokens=65)
+    _, _, idx, logits = ops.router_topk(x.to(DEV), weights.router.to(DEV), 8, True, return_logits=True)
+    idx = idx.cpu().numpy()
+    ref_logits = bits_to_f32(g["logits_bits"])
+    mine = logits.float().cpu().numpy()
+    ties = mo.boundary_ties(ref_logits, 8)
+    same_logits = (mine == ref_logits).all(axis=1)
+    for t in range(idx.shape[0]):
+        if same_logits[t] and not ties[t]:
+            assert set(idx[t]) == set(g["idx"][t]), t
+
+
+def test_router_ties_pick_lowest_expert_id(ops):
+    """Forced exact ties: equal logits across many experts."""
+    e, h, t = 128, 256, 16
+    gen = torch.Generator().manual_seed(3)
+    w = torch.zeros(e, h)
+    base = torch.randn(8, h, generator=gen)
+    for i in range(e):  # groups of 16 experts share a weight row -> equal logits
+        w[i] = base[i % 8]
+    x = torch.randn(t, h, generator=gen)
+    for dtype, name in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+        _, _, idx = ops.router_topk(x.to(dtype).to(DEV), w.to(dtype).to(DEV), 8, True)
+        _, _, oi, _ = mo.router_topk(x.to(dtype).float().numpy(), w.to(dtype).float().numpy(), 8, True, name)
+        assert np.array_equal(idx.cpu().numpy(), oi)
+
+
+def test_router_small_shapes(ops):
+    gen = torch.Generator().manual_seed(9)
+    for (t, h, e, k) in [(2, 4, 3, 3), (5, 33, 7, 2), (3, 1, 4, 1), (70, 100, 128, 8), (9, 64, 300, 16)]:
+        x = torch.randn(t, h, generator=gen)
+        w = torch.randn(e, h, generator=gen)
+        for dtype, name in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+            probs, tw, idx = ops.router_topk(x.to(dtype).to(DEV), w.to(dtype).to(DEV), k, True)
+            op, ow, oi, _ = mo.router_topk(x.to(dtype).float().numpy(), w.to(dtype).float().numpy(), k, True, name)
+            assert np.array_equal(idx.cpu().numpy(), oi), (t, h, e, k, name)
+            np.testing.assert_allclose(tw.cpu().numpy(), ow, rtol=1e-5, atol=1e-7)
+
+
+# --------------------------------------------------------------- K2 dispatch
+
+
+@pytest.mark.parametrize("case", ["t65_uniform", "t1", "t512_zipf", "t129_zipf", "t7_k3_e5", "t4_one_expert"])
+def test_dispatch_matches_reference_grouping(ops, golden_dir, case):
+    g = np.load(golden_dir / "dispatch.npz")
+    idx = g[f"{case}__idx"]
+    e = 5 if case == "t7_k3_e5" else 128
+    d = ops.moe_dispatch(torch.from_numpy(idx).to(DEV), e)
+    n_act = int(d.num_active.item())
+    assert int(d.error.item()) == 0
+    assert np.array_equal(d.sorted_pos.cpu().numpy(), g[f"{case}__positions"])
+    assert np.array_equal(d.active.cpu().numpy()[:n_act], g[f"{case}__unique"])
+    assert np.array_equal(d.counts.cpu().numpy()[g[f"{case}__unique"]], g[f"{case}__counts"])
+    assert np.array_equal(d.sorted_pos.cpu().numpy() // idx.shape[1], g[f"{case}__where_tokens"])
+    oc, oo, osp, oip, oa, on = mo.dispatch(idx, e)
+    assert np.array_equal(d.offsets.cpu().numpy(), oo)
+    assert np.array_equal(d.inv_pos.cpu().numpy(), oip)
+    assert np.array_equal(d.active.cpu().numpy(), oa)
+
+
+def test_dispatch_large_and_invalid(ops):
+    rng = np.random.default_rng(0)
+    idx = rng.integers(0, 1024, size=(4000, 8))
+    d = ops.moe_dispatch(torch.from_numpy(idx).to(DEV), 1024)
+    _, oo, osp, oip, oa, _ = mo.dispatch(idx, 1024)
+    assert np.array_equal(d.sorted_pos.cpu().numpy(), osp)
+    assert np.array_equal(d.offsets.cpu().numpy(), oo)
+    bad = np.array([[0, 5], [130, 1]])
+    d = ops.moe_dispatch(torch.from_numpy(bad).to(DEV), 128)
+    assert int(d.error.item()) == 1
+    # Valid routes are still grouped stably; the invalid one is dropped.
+    assert d.sorted_pos.cpu().numpy().tolist() == [0, 3, 1, -1]
+    empty = ops.moe_dispatch(torch.zeros(0, 8, dtype=torch.int64, device=DEV), 128)
+    assert int(empty.num_active.item()) == 0
+
+
+def test_gather(ops):
+    gen = torch.Generator().manual_seed(4)
+    x = torch.randn(65, 2048, generator=gen).to(torch.bfloat16).to(DEV)
+    idx = torch.from_numpy(np.random.default_rng(1).integers(0, 128, size=(65, 8))).to(DEV)
+    w = torch.rand(65, 8, generator=gen).to(DEV)
+    d = ops.moe_dispatch(idx, 128)
+    xs, ws = ops.moe_gather(x, w, d)
+    pos = d.sorted_pos.long()
+    assert torch.equal(xs, x[pos // 8])
+    assert torch.equal(ws, w.reshape(-1)[pos])
+
+
+# ----------------------------------------------------------- K3 + K4 block
+
+
+def run_block(ops, x, weights, idx, topw, impl, reduce=0, rank=None):
+    """Dispatch -> gather -> grouped SwiGLU -> combine with all experts resident."""
+    e = weights.router.shape[0]
+    inter = weights.down.shape[2]
+    storage = weights.packed_all().to(x.dtype).to(DEV)
+    slot = torch.arange(e, dtype=torch.int32, device=DEV)
+    d = ops.moe_dispatch(idx, e)
+    xs, ws = ops.moe_gather(x, topw, d)
+    ys = ops.grouped_swiglu(xs, ws, d, slot, storage, x.shape[1], inter, impl=impl)
+    return ops.moe_combine(ys, d, idx, expert_rank=rank, reduce=reduce), ys, d
+
+
+@pytest.mark.parametrize("impl", [1, 2])
+def test_moe_block_bf16_t65_vs_reference_golden(ops, golden_dir, impl):
+    g = np.load(golden_dir / "moe_bf16_t65.npz")
+    weights, x = synthetic.bf16_layer_inputs(seed=11, tokens=65)
+    idx = torch.from_numpy(g["idx"]).to(DEV)
+    topw = torch.from_numpy(g["weights"]).to(DEV)
+    out, _, _ = run_block(ops, x.to(DEV), weights, idx, topw, impl)
+    ref = bits_to_f32(g["out_specfit_bits"])
+    got = out.float().cpu().numpy()
+    assert np.abs(got - ref).max() <= ATOL_BF16
+    assert cosine(got, ref) >= COS_MIN
+
+
+@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("tokens,routes", [(65, "uniform"), (129, "zipf"), (512, "zipf"), (3, "uniform")])
+def test_moe_block_bf16_vs_oracle(ops, impl, tokens, routes):
+    weights, x = synthetic.bf16_layer_inputs(seed=20 + tokens, tokens=tokens)
+    if routes == "zipf":
+        idx_np = synthetic.zipf_routes(tokens, layer=1, seed=5)
+    else:
+        idx_np = np.stack([np.random.default_rng(tokens + i).permutation(128)[:8] for i in range(tokens)])
+    topw_np = np.random.default_rng(7).dirichlet(np.ones(8), size=tokens).astype(np.float32)
+    idx = torch.from_numpy(idx_np).to(DEV)
+    topw = torch.from_numpy(topw_np).to(DEV)
+    out, _, _ = run_block(ops, x.to(DEV), weights, idx, topw, impl)
+    packed = {e: weights.packed(e).float().numpy() for e in np.unique(idx_np)}
+    ref = mo.moe_experts(x.float().numpy(), idx_np, topw_np, packed, 2048, 768, "bf16")
+    got = out.float().cpu().numpy()
+    assert np.abs(got - ref).max() <= ATOL_BF16
+    assert cosine(got, ref) >= COS_MIN
+
+
+def test_moe_block_cfg1_f32_vs_reference_golden(ops, golden_dir):
+    g = np.load(golden_dir / "moe_cfg1_f32.npz")
+    weights, x = synthetic.config1_inputs(seed=0, tokens=32)
+    idx = torch.from_numpy(g["idx"]).to(DEV)
+    topw = torch.from_numpy(g["weights"]).to(DEV)
+    out, _, _ = run_block(ops, x.to(DEV), weights, idx, topw, impl=0)
+    got = out.cpu().numpy()
+    np.testing.assert_allclose(got, g["out_specfit"], rtol=1e-3, atol=1e-4)
+
+
+def test_tc_and_simt_agree(ops):
+    weights, x = synthetic.bf16_layer_inputs(seed=3, tokens=300)
+    idx_np = synthetic.zipf_routes(300, layer=2, seed=3)
+    topw = torch.full((300, 8), 0.125, device=DEV)
+    idx = torch.from_numpy(idx_np).to(DEV)
+    _, y1, _ = run_block(ops, x.to(DEV), weights, idx, topw, impl=1)
+    _, y2, _ = run_block(ops, x.to(DEV), weights, idx, topw, impl=2)
+    a, b = y1.float().cpu().numpy(), y2.float().cpu().numpy()
+    assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= 0.9999
+
+
+def test_expert_kats(ops, golden_dir):
+    """Reference unit-test shapes (H=4, I=3) and the bf16 reduction-order KAT."""
+    g = np.load(golden_dir / "expert_kats.npz")
+    gate_up = torch.from_numpy(bits_to_f32(g["small_gate_up_bits"]))
+    down = torch.from_numpy(bits_to_f32(g["small_down_bits"]))
+    w = synthetic.MoeLayerWeights(torch.zeros(3, 4), gate_up, down)
+    x = torch.from_numpy(bits_to_f32(g["small_x_bits"])).to(torch.bfloat16).to(DEV)
+    idx = torch.from_numpy(g["small_idx"]).to(DEV)
+    topw = torch.from_numpy(bits_to_f32(g["small_w_bits"])).to(torch.bfloat16).to(DEV)
+    out, _, _ = run_block(ops, x, w, idx, topw, impl=0)
+    ref = bits_to_f32(g["small_out_012_bits"])
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=1.6e-2, rtol=1.6e-2)
+    # Reduction order: arrival (0,1,2) -> 0.0 ; (0,2,1) -> 2**-8 ; canonical -> 0.0.
+    kd = torch.from_numpy(bits_to_f32(g["kat_down_bits"]))
+    kat = synthetic.MoeLayerWeights(torch.zeros(3, 1), torch.ones(3, 2, 1), kd)
+    xk = torch.ones(1, 1, dtype=torch.bfloat16, device=DEV)
+    ik = torch.tensor([[0, 1, 2]], device=DEV)
+    wk = torch.ones(1, 3, dtype=torch.bfloat16, device=DEV)
+    rank_021 = torch.tensor([0, 2, 1], dtype=torch.int32, device=DEV)  # rank of each expert
+    a012, _, _ = run_block(ops, xk, kat, ik, wk, impl=0)
+    a021, _, _ = run_block(ops, xk, kat, ik, wk, impl=0, rank=rank_021)
+    assert a012.item() == float(g["kat_arrival_012"][0, 0]) == 0.0
+    assert a021.item() == float(g["kat_arrival_021"][0, 0]) == 2.0 ** -8
+
+
+def test_combine_bit_exact_sequential(ops):
+    """Combine alone: sequential bf16 adds in ascending expert order, exactly."""
+    rng = np.random.default_rng(2)
+    tokens = 65
+    idx_np = np.stack([rng.permutation(128)[:8] for _ in range(tokens)])
+    idx = torch.from_numpy(idx_np).to(DEV)
+    d = ops.moe_dispatch(idx, 128)
+    ys = torch.randn(tokens * 8, 2048, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    out = ops.moe_combine(ys.to(DEV), d, idx).float().cpu().numpy()
+    inv = d.inv_pos.cpu().numpy().reshape(tokens, 8)
+    y = ys.float().numpy()
+    ref = np.zeros((tokens, 2048), np.float32)
+    for t in range(tokens):
+        for k in np.argsort(idx_np[t], kind="stable"):
+            ref[t] = mo.bf16_round(ref[t] + y[inv[t, k]])
+    assert np.array_equal(out, ref)
+    f32 = ops.moe_combine(ys.to(DEV), d, idx, reduce=1).float().cpu().numpy()
+    assert np.abs(f32 - ref).max() < 0.05
+
+
+# --------------------------------------------------------- K6 tree attention
+
+
+@pytest.mark.parametrize("nodes,depth,ctx", [(4, 2, 2), (64, 6, 512), (128, 8, 300), (60, 8, 2048), (0, 0, 33)])
+def test_tree_attention_vs_oracle(ops, nodes, depth, ctx):
+    if nodes:
+        _, parents, _ = synthetic.random_tree(nodes, max_depth=depth, max_branch=4, seed=nodes)
+    else:
+        parents = ()
+    tq = 1 + len(parents)
+    tk = ctx + tq
+    gen = torch.Generator().manual_seed(nodes + ctx)
+    q = torch.randn(32, tq, 128, generator=gen).to(torch.bfloat16)
+    k = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16)
+    bits = ops.tree_bits_from_parents(parents, DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), bits, ctx)
+    mask = to.verification_attention_mask(parents, ctx)
+    ref = to.tree_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), mask)
+    got = out.float().cpu().numpy().transpose(1, 0, 2)
+    assert np.abs(got - ref).max() <= ATOL_BF16
+    assert cosine(got, ref) >= COS_MIN
+    # The packed mask equals the reference tree mask, bit for bit.
+    packed = ops.tree_bits_from_mask(torch.from_numpy(mask).to(DEV), ctx)
+    assert torch.equal(packed, bits)
+
+
+def test_tree_attention_strided_views(ops):
+    """Inputs as HF lays them out: q from a [1, T, Hq*D] projection viewed as
+    [Hq, T, D] (non-contiguous), K/V cache [Hkv, Tk, D]."""
+    parents = (0, 0, 1, 2)
+    tq, ctx = 5, 40
+    gen = torch.Generator().manual_seed(0)
+    qp = torch.randn(tq, 32 * 128, generator=gen).to(torch.bfloat16).to(DEV)
+    q = qp.view(tq, 32, 128).transpose(0, 1)
+    k = torch.randn(4, ctx + tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    v = torch.randn(4, ctx + tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    out = ops.tree_attention(q, k, v, ops.tree_bits_from_parents(parents, DEV), ctx)
+    mask = to.verification_attention_mask(parents, ctx)
+    ref = to.tree_attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), mask)
+    assert np.abs(out.float().cpu().numpy().transpose(1, 0, 2) - ref).max() <= ATOL_BF16
+
+
+def test_device_status_clean(ops):
+    from specfit_b200 import _native
+
+    torch.cuda.synchronize()
+    assert _native.device_status(reset=True) == 0
