@@ -15,6 +15,13 @@ from . import _native as N
 
 _DTYPES = {torch.float32: N.SF_DTYPE_F32, torch.bfloat16: N.SF_DTYPE_BF16}
 
+# Kernels of this library launched through this module (host-side count).
+LAUNCHES = [0]
+
+
+def _launched(n: int) -> None:
+    LAUNCHES[0] += n
+
 
 def dtype_code(dtype: torch.dtype) -> int:
     try:
@@ -72,6 +79,7 @@ def router_topk(hidden: torch.Tensor, weight: torch.Tensor, top_k: int, norm_top
                              topi.data_ptr(), _ptr(logits), ws.data_ptr(), ws_bytes, _stream(dev)),
         "sf_router_topk",
     )
+    _launched(2)
     if return_logits:
         return probs, topw, topi, logits
     return probs, topw, topi
@@ -120,6 +128,7 @@ def moe_dispatch(top_k_index: torch.Tensor, num_experts: int) -> Dispatch:
                               _stream(dev)),
         "sf_moe_dispatch",
     )
+    _launched(1)
     return Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, error, tokens, top_k,
                     num_experts)
 
@@ -140,6 +149,7 @@ def moe_gather(hidden: torch.Tensor, top_k_weights: torch.Tensor, d: Dispatch,
                             ws.data_ptr(), _stream(dev)),
         "sf_moe_gather",
     )
+    _launched(1)
     return xs, ws
 
 
@@ -175,6 +185,7 @@ def grouped_swiglu(hidden_sorted: torch.Tensor, weights_sorted: torch.Tensor, d:
             intermediate_size, rows, act.data_ptr(), y.data_ptr(), impl, _stream(dev)),
         "sf_grouped_swiglu",
     )
+    _launched(2)
     return y
 
 
@@ -197,6 +208,7 @@ def moe_combine(out_sorted: torch.Tensor, d: Dispatch, top_k_index: torch.Tensor
                              out_sorted.shape[1], reduce, res.data_ptr(), _stream(dev)),
         "sf_moe_combine",
     )
+    _launched(1)
     return res
 
 
@@ -253,6 +265,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits:
                                 _stream(dev)),
         "sf_tree_attention",
     )
+    _launched(2)
     return res
 
 

@@ -1,0 +1,190 @@
+"""Offloaded Qwen3-MoE experts on the B200 kernels.
+
+Drop-in for ``Qwen3OffloadedExperts`` (``src/specfit/runtime/
+qwen3_offloaded_experts.py:65-292``): same constructor, attributes, input
+validation (messages included), execution policies and reduction modes.
+The forward pass differs in how it is executed, not in what it computes:
+
+* routes are grouped on the device (``sf_moe_dispatch``, the stable grouping
+  of :173-178) and rows gathered once (``sf_moe_gather``, :189-190);
+* every expert of a lease wave runs in one grouped SwiGLU launch that reads
+  the weights straight from their cache slots (``sf_grouped_swiglu``,
+  :38-62 plus the ``mul_(w)`` of :132-138);
+* the reduction is one launch in canonical ascending-expert order or in
+  execution (arrival) order (``sf_moe_combine``, :144-163), with the same
+  rounding after every add as the reference's bf16 ``index_add_``.
+
+Cache protocol.  When the cache holds every expert of the layer (all
+resident, nothing in flight), the slot of each expert is fixed and the layer
+runs with no host synchronisation; hits are counted on the device.
+Otherwise the active experts are copied to the host (the reference
+synchronises here too, :112 / :175) and leased in execution order, as many
+at a time as the cache can pin (a "wave"); each wave's fills are ordered
+before its grouped launch and its leases are released right after the
+launch, so later fills into those slots wait for it.  With this protocol the
+resident hits, H2D submissions and evictions equal the reference's
+whenever the active experts fit in the cache, and in the reference's own
+one-slot and two-slot unit tests.
+"""
+from __future__ import annotations
+
+from enum import Enum
+from typing import Sequence
+
+import torch
+from torch import nn
+
+from .. import _native as N
+from .. import ops
+from .gpu_expert_cache import GpuExpertCache
+from .lease import NoEvictableSlotError
+from .state import ExpertKey
+
+
+class ReductionMode(str, Enum):
+    CANONICAL = "canonical"
+    ARRIVAL_ORDER = "arrival_order"
+
+
+class ExpertExecutionPolicy(str, Enum):
+    EXPERT_ID_ASCENDING = "expert_id_ascending"
+    RESIDENT_FIRST = "resident_first"
+
+
+class Qwen3OffloadedExperts(nn.Module):
+    def __init__(self, *, layer_id: int, cache: GpuExpertCache, hidden_size: int,
+                 intermediate_size: int, reduction_mode=ReductionMode.CANONICAL,
+                 execution_policy=ExpertExecutionPolicy.EXPERT_ID_ASCENDING,
+                 h2d_prefetch: bool = True, swiglu_impl: int = N.SF_SWIGLU_AUTO) -> None:
+        super().__init__()
+        if layer_id < 0:
+            raise ValueError("layer_id must be non-negative")
+        if hidden_size <= 0:
+            raise ValueError("hidden_size must be positive")
+        if intermediate_size <= 0:
+            raise ValueError("intermediate_size must be positive")
+        if type(h2d_prefetch) is not bool:
+            raise ValueError("h2d_prefetch must be a boolean")
+        self.layer_id = layer_id
+        self.cache = cache
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.reduction_mode = ReductionMode(reduction_mode)
+        self.execution_policy = ExpertExecutionPolicy(execution_policy)
+        self.h2d_prefetch = h2d_prefetch
+        self.swiglu_impl = swiglu_impl
+        self._prediction_scheduler = None
+        ids = [k.expert_id for k in cache.source_keys()
+               if isinstance(k, ExpertKey) and k.layer_id == layer_id]
+        self.num_experts = (max(ids) + 1) if ids else 0
+        self._keys = tuple(ExpertKey(layer_id, e) for e in range(self.num_experts))
+
+    # ------------------------------------------------------------ forward
+    def forward(self, hidden_states: torch.Tensor, top_k_index: torch.Tensor,
+                top_k_weights: torch.Tensor, *, execution_order: Sequence[int] | None = None):
+        self._validate_inputs(hidden_states, top_k_index, top_k_weights)
+        if self._prediction_scheduler is not None:
+            if execution_order is not None:
+                raise ValueError("explicit execution_order conflicts with dynamic predicted prefetch")
+            raise NotImplementedError("predicted cross-layer prefetch is not available in this build")
+        tokens = hidden_states.shape[0]
+        if tokens == 0:
+            return torch.zeros_like(hidden_states)
+        if self.num_experts == 0:
+            raise KeyError(f"unknown expert {ExpertKey(self.layer_id, int(top_k_index.reshape(-1)[0]))!r}")
+        h = hidden_states.contiguous()
+        d = ops.moe_dispatch(top_k_index, self.num_experts)
+        xs, ws = ops.moe_gather(h, top_k_weights, d)
+        storage = self.cache.storage.view(self.cache.slot_count, -1)
+        # With every expert resident, both policies order the experts by id,
+        # so arrival order equals the canonical order as well.
+        fixed = self.cache.device_slot_table(self._keys) if execution_order is None else None
+        if fixed is not None:
+            # Every expert resident: one launch, no host round trip.
+            ys = ops.grouped_swiglu(xs, ws, d, fixed, storage, self.hidden_size,
+                                    self.intermediate_size, impl=self.swiglu_impl)
+            self.cache.note_device_hits(d.num_active)
+            return ops.moe_combine(ys, d, top_k_index)
+        return self._forward_waves(h, top_k_index, d, xs, ws, storage, execution_order)
+
+    def _forward_waves(self, h, top_k_index, d, xs, ws, storage, execution_order):
+        dev = h.device
+        host = torch.cat((d.num_active, d.error, d.active)).cpu()  # the one host sync
+        n_active, err = int(host[0]), int(host[1])
+        if err:
+            bad = top_k_index[(top_k_index < 0) | (top_k_index >= self.num_experts)]
+            raise KeyError(f"unknown expert {ExpertKey(self.layer_id, max(int(bad[0]), 0))!r}")
+        active = tuple(int(e) for e in host[3:3 + n_active].tolist())
+        order = self._resolve_execution_order(active, execution_order)
+        ys = torch.empty(xs.shape[0], self.hidden_size, dtype=h.dtype, device=dev)
+        act = torch.empty(max(xs.shape[0], 1), self.intermediate_size, dtype=h.dtype, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        pos = 0
+        while pos < len(order):
+            wave = []
+            try:
+                for e in order[pos:]:
+                    wave.append((e, self.cache.acquire(ExpertKey(self.layer_id, e))))
+            except NoEvictableSlotError:
+                if not wave:
+                    raise
+            try:
+                table = torch.full((self.num_experts + 1 + len(wave),), -1, dtype=torch.int32)
+                for j, (e, lease) in enumerate(wave):
+                    lease.wait(stream)
+                    table[e] = lease.slot_id
+                    table[self.num_experts + 1 + j] = e
+                table[self.num_experts] = len(wave)
+                table = table.pin_memory().to(dev, non_blocking=True)
+                ops.grouped_swiglu(xs, ws, d, table[: self.num_experts], storage, self.hidden_size,
+                                   self.intermediate_size, impl=self.swiglu_impl,
+                                   active=table[self.num_experts + 1:],
+                                   num_active=table[self.num_experts: self.num_experts + 1],
+                                   act_workspace=act, out=ys)
+            finally:
+                for _, lease in wave:
+                    lease.release()
+            pos += len(wave)
+        rank = None
+        if self.reduction_mode is ReductionMode.ARRIVAL_ORDER:
+            r = torch.zeros(self.num_experts, dtype=torch.int32)
+            for i, e in enumerate(order):
+                r[e] = i
+            rank = r.to(dev)
+        return ops.moe_combine(ys, d, top_k_index, expert_rank=rank)
+
+    # --------------------------------------------------------- validation
+    def _validate_inputs(self, hidden_states, top_k_index, top_k_weights) -> None:
+        if hidden_states.ndim != 2:
+            raise ValueError("hidden_states must have shape [tokens, hidden]")
+        if hidden_states.shape[1] != self.hidden_size:
+            raise ValueError(f"hidden_states width is {hidden_states.shape[1]}, expected {self.hidden_size}")
+        if top_k_index.ndim != 2:
+            raise ValueError("top_k_index must have shape [tokens, top_k]")
+        if top_k_weights.shape != top_k_index.shape:
+            raise ValueError("top_k_weights must match top_k_index shape")
+        if top_k_index.shape[0] != hidden_states.shape[0]:
+            raise ValueError("routing tensors must match the token count")
+        if top_k_index.dtype is not torch.long:
+            raise ValueError("top_k_index must use torch.long")
+        if hidden_states.device != self.cache.device:
+            raise ValueError("hidden_states must be on the cache device")
+        if top_k_index.device != hidden_states.device:
+            raise ValueError("top_k_index must be on the hidden-state device")
+        if top_k_weights.device != hidden_states.device:
+            raise ValueError("top_k_weights must be on the hidden-state device")
+
+    def _resolve_execution_order(self, active_experts: tuple, execution_order) -> tuple:
+        """Same policy as the reference (qwen3_offloaded_experts.py:262-292)."""
+        if execution_order is not None:
+            order = tuple(int(e) for e in execution_order)
+            if len(order) != len(set(order)):
+                raise ValueError("execution_order must not contain duplicates")
+            if set(order) != set(active_experts):
+                raise ValueError("execution_order must contain every active expert exactly once")
+            return order
+        if self.execution_policy is ExpertExecutionPolicy.EXPERT_ID_ASCENDING:
+            return active_experts
+        resident = frozenset(self.cache.resident_expert_ids())
+        first = tuple(e for e in active_experts if ExpertKey(self.layer_id, e) in resident)
+        return first + tuple(e for e in active_experts if ExpertKey(self.layer_id, e) not in resident)

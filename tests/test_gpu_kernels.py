@@ -263,8 +263,13 @@ def test_combine_bit_exact_sequential(ops):
         for k in np.argsort(idx_np[t], kind="stable"):
             ref[t] = mo.bf16_round(ref[t] + y[inv[t, k]])
     assert np.array_equal(out, ref)
+    # fp32 accumulation: within one bf16 ulp of the exactly rounded sum.
     f32 = ops.moe_combine(ys.to(DEV), d, idx, reduce=1).float().cpu().numpy()
-    assert np.abs(f32 - ref).max() < 0.05
+    exact = np.zeros((tokens, 2048), np.float64)
+    for t in range(tokens):
+        exact[t] = y[inv[t]].astype(np.float64).sum(axis=0)
+    ulp = np.ldexp(1.0, np.frexp(np.abs(exact) + 1e-30)[1] - 8)
+    assert np.all(np.abs(f32 - exact) <= ulp)
 
 
 # --------------------------------------------------------- K6 tree attention
