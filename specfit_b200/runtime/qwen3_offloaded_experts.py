@@ -114,7 +114,7 @@ class Qwen3OffloadedExperts(nn.Module):
         if err:
             bad = top_k_index[(top_k_index < 0) | (top_k_index >= self.num_experts)]
             raise KeyError(f"unknown expert {ExpertKey(self.layer_id, max(int(bad[0]), 0))!r}")
-        active = tuple(int(e) for e in host[3:3 + n_active].tolist())
+        active = tuple(int(e) for e in host[2:2 + n_active].tolist())
         order = self._resolve_execution_order(active, execution_order)
         ys = torch.empty(xs.shape[0], self.hidden_size, dtype=h.dtype, device=dev)
         act = torch.empty(max(xs.shape[0], 1), self.intermediate_size, dtype=h.dtype, device=dev)
@@ -123,12 +123,12 @@ class Qwen3OffloadedExperts(nn.Module):
         while pos < len(order):
             wave = []
             try:
-                for e in order[pos:]:
-                    wave.append((e, self.cache.acquire(ExpertKey(self.layer_id, e))))
-            except NoEvictableSlotError:
-                if not wave:
-                    raise
-            try:
+                try:
+                    for e in order[pos:]:
+                        wave.append((e, self.cache.acquire(ExpertKey(self.layer_id, e))))
+                except NoEvictableSlotError:
+                    if not wave:
+                        raise
                 table = torch.full((self.num_experts + 1 + len(wave),), -1, dtype=torch.int32)
                 for j, (e, lease) in enumerate(wave):
                     lease.wait(stream)
