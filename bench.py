@@ -68,6 +68,11 @@ def parse_args(argv=None):
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
+    p.add_argument("--mode", choices=("verify", "block"), default="verify",
+                   help="block: the MoE verify block alone on one resident layer (kernel profiling)")
+    p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
+    p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
+                   help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
     return p.parse_args(argv)
 
 
@@ -245,10 +250,12 @@ def timed_steps(fn, steps, warmup, world, device):
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
+    torch.cuda.nvtx.range_push("timed")
     start.record()
     for _ in range(steps):
         results.append(fn())
     end.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(device)
     barrier(world)
     ms = start.elapsed_time(end)
@@ -556,10 +563,51 @@ def reference_arm(args):
     }), flush=True)
 
 
+def block_mode(args):
+    """The MoE verify block alone (router, dispatch, gather, grouped SwiGLU,
+    combine) on one layer whose 128 experts are resident in HBM; bf16
+    N(0,0.02) weights drawn on the GPU.  One step = one block call."""
+    from specfit_b200 import ops, synthetic
+
+    device = torch.device("cuda", 0)
+    peaks = measured_peaks()
+    g = torch.Generator(device=device).manual_seed(args.seed)
+    e, h, i = synthetic.NUM_EXPERTS, synthetic.HIDDEN, synthetic.MOE_INTER
+    storage = (torch.randn(e, 3 * h * i, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    router = (torch.randn(e, h, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    x = torch.randn(args.tokens, h, generator=g, device=device).to(torch.bfloat16)
+    slot = torch.arange(e, dtype=torch.int32, device=device)
+    zipf = None
+    if args.routes == "zipf":
+        zipf = torch.from_numpy(synthetic.zipf_routes(args.tokens, layer=0, seed=args.seed)).to(device)
+    elif args.routes == "uniform":
+        rng = np.random.default_rng(args.seed)
+        zipf = torch.from_numpy(np.stack([rng.permutation(e)[:8] for _ in range(args.tokens)])).to(device)
+
+    def block():
+        _, w, idx = ops.router_topk(x, router, 8, True)
+        if zipf is not None:
+            idx = zipf
+        d = ops.moe_dispatch(idx, e)
+        xs, ws = ops.moe_gather(x, w, d)
+        ys = ops.grouped_swiglu(xs, ws, d, slot, storage, h, i)
+        return ops.moe_combine(ys, d, idx), d
+
+    ms, outs = timed_steps(block, args.steps, args.warmup, 1, device)
+    uniq = int(outs[-1][1].num_active.item())
+    us = ms * 1e3 / args.steps
+    algo = uniq * EXPERT_BYTES + e * h * 2
+    print(json.dumps({"mode": "block", "tokens": args.tokens, "routes": args.routes, "experts": uniq,
+                      "us_per_block": round(us, 2), "algorithmic_GBps": round(algo / us / 1e3, 1),
+                      "frac_of_hbm_peak": round(algo / us / 1e3 / peaks["hbm_gbs"], 4)}), flush=True)
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         reference_arm(args)
+    elif args.mode == "block":
+        block_mode(args)
     else:
         b200_arm(args)
 
