@@ -86,6 +86,31 @@ SF_API int sf_router_topk(const void* hidden, const void* router_weight, int dty
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Allocation-free router: same contract and results as sf_router_topk, but it
+ * takes no workspace.  Its scratch is a 2 MiB array compiled into the library
+ * (one per GPU that loads it, held until the process exits), so callers that
+ * cannot allocate device memory can still route: code running under CUDA
+ * stream capture, plugins of a runtime that owns all device memory, and paths
+ * that cannot afford cudaMalloc's device synchronisation.
+ *   - tokens * num_experts must not exceed sf_router_topk_noalloc_max_elems()
+ *     (2^19); larger calls fail with SF_ERR_WORKSPACE and launch nothing.
+ *   - The first call on a device looks up the array's device address (a CUDA
+ *     runtime query, no allocation); make that first call before any stream
+ *     capture.
+ *   - All calls on a device share the array: calls that may overlap on the
+ *     GPU (different streams without ordering) race and must not be issued.
+ *     Nothing in the array needs to start at zero; each call overwrites every
+ *     element it later reads, and the array keeps the last call's contents.
+ * No counterpart in the reference (its router is a PyTorch module that
+ * allocates through the caching allocator).
+ */
+SF_API int64_t sf_router_topk_noalloc_max_elems(void);
+SF_API int sf_router_topk_noalloc(const void* hidden, const void* router_weight, int dtype,
+                                  int64_t tokens, int hidden_size, int num_experts, int top_k,
+                                  int norm_topk_prob, float* probs, float* topk_weights,
+                                  int64_t* topk_index, void* logits_out, void* stream);
+
+/*
  * Dispatch: stable grouping of the T*K routes by expert id.
  *   counts[E], offsets[E+1] (exclusive prefix of counts),
  *   sorted_pos[T*K]: route positions t*K+k in ascending (expert, position)

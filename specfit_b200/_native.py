@@ -45,6 +45,9 @@ SIGNATURES = {
     "sf_router_topk_workspace_bytes": (_sz, [_i64, _i32]),
     "sf_router_topk": (_i32, [_vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
                               _vp, _sz, _vp]),
+    "sf_router_topk_noalloc_max_elems": (_i64, []),
+    "sf_router_topk_noalloc": (_i32, [_vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                                      _vp, _vp]),
     "sf_moe_dispatch": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sf_moe_gather": (_i32, [_vp, _i32, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
     "sf_grouped_swiglu": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32,

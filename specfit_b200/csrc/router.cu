@@ -17,6 +17,8 @@
 // GPU (a CTA per 8 tokens x 16 experts), and a warp-per-token top-k kernel.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace sf {
@@ -220,6 +222,83 @@ extern "C" int sf_router_topk(const void* hidden, const void* router_weight, int
     return set_error(SF_ERR_WORKSPACE, "router workspace needs %zu bytes",
                      sf_router_topk_workspace_bytes(tokens, num_experts));
   float* ws = static_cast<float*>(workspace);
+  if (dtype == SF_DTYPE_BF16)
+    return launch_router<__nv_bfloat16>(hidden, router_weight, tokens, hidden_size, num_experts,
+                                        top_k, norm_topk_prob, probs, topk_weights, topk_index,
+                                        logits_out, ws, as_stream(stream));
+  if (dtype == SF_DTYPE_F32)
+    return launch_router<float>(hidden, router_weight, tokens, hidden_size, num_experts, top_k,
+                                norm_topk_prob, probs, topk_weights, topk_index, logits_out, ws,
+                                as_stream(stream));
+  return set_error(SF_ERR_UNSUPPORTED, "router dtype %d is not supported", dtype);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free router.
+//
+// Some callers cannot hand this library a workspace because they cannot
+// allocate device memory at the point of the call: code that runs while a
+// stream is being captured into a CUDA graph (cudaMalloc is not allowed
+// there), plugins hosted by a serving runtime that reserves the GPU's memory
+// for its own pools and gives extensions none, and latency-critical paths
+// where cudaMalloc's implicit device-wide synchronisation is unacceptable.
+// sf_router_topk_noalloc serves them: its scratch (the fp32 logits between
+// the two router passes) is this file-scope device array, which every GPU
+// that loads the library holds until the process exits.
+
+namespace sf {
+namespace {
+
+// Maximum tokens * experts of one allocation-free call: 2^19 floats = 2 MiB
+// (e.g. 4096 tokens at 128 experts).
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 19;
+static __device__ __align__(256) float g_router_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_router_scratch on the current device, looked up once
+// per device.  The host-side symbol is only a stand-in and must never be
+// passed to a kernel.
+int router_scratch(float** out) {
+  int dev = 0;
+  SF_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(SF_ERR_UNSUPPORTED, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    SF_CHECK_CUDA(cudaGetSymbolAddress(&p, g_router_scratch));
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return SF_OK;
+}
+
+}  // namespace
+}  // namespace sf
+
+extern "C" int64_t sf_router_topk_noalloc_max_elems(void) { return sf::kNoAllocScratchFloats; }
+
+extern "C" int sf_router_topk_noalloc(const void* hidden, const void* router_weight, int dtype,
+                                      int64_t tokens, int hidden_size, int num_experts, int top_k,
+                                      int norm_topk_prob, float* probs, float* topk_weights,
+                                      int64_t* topk_index, void* logits_out, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(tokens >= 0, "tokens must be non-negative");
+  SF_CHECK_ARG(hidden_size > 0, "hidden_size must be positive");
+  SF_CHECK_ARG(num_experts > 0 && num_experts <= 1024, "num_experts must be in [1, 1024]");
+  SF_CHECK_ARG(top_k > 0 && top_k <= 32 && top_k <= num_experts, "top_k must be in [1, min(32, E)]");
+  if (tokens * (int64_t)num_experts > kNoAllocScratchFloats)
+    return set_error(SF_ERR_WORKSPACE,
+                     "tokens * num_experts = %lld exceeds the allocation-free router's built-in "
+                     "scratch of %lld elements; use sf_router_topk with a workspace",
+                     (long long)(tokens * (int64_t)num_experts), (long long)kNoAllocScratchFloats);
+  if (tokens == 0) return SF_OK;
+  SF_CHECK_ARG(hidden && router_weight && probs && topk_weights && topk_index,
+               "null pointer argument");
+  float* ws = nullptr;
+  if (int rc = router_scratch(&ws)) return rc;
   if (dtype == SF_DTYPE_BF16)
     return launch_router<__nv_bfloat16>(hidden, router_weight, tokens, hidden_size, num_experts,
                                         top_k, norm_topk_prob, probs, topk_weights, topk_index,
