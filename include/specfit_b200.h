@@ -196,6 +196,11 @@ SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const si
  * Replaces SDPA under the verification mask (transformers/...:172-186 with
  * eagle3_types.py:450-473).
  */
+/* Implementation choice of sf_tree_attention_ex. */
+#define SF_ATTN_AUTO 0    /* tcgen05 kernel when supported (sm_100, D=128, Tk<=8192, 16-byte rows), else SIMT */
+#define SF_ATTN_SIMT 1    /* CUDA-core split kernel */
+#define SF_ATTN_TCGEN05 2 /* tcgen05/TMEM kernel; fails with SF_ERR_INVALID_ARGUMENT if unsupported */
+
 SF_API size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len, int64_t kv_len);
 SF_API int sf_tree_attention(const void* q, const void* k, const void* v, const uint32_t* tree_bits,
                       int bit_words, int64_t q_len, int64_t kv_len, int64_t prefix_len,
@@ -203,6 +208,12 @@ SF_API int sf_tree_attention(const void* q, const void* k, const void* v, const 
                       int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
                       float scale, void* out, void* workspace, size_t workspace_bytes,
                       void* stream);
+SF_API int sf_tree_attention_ex(const void* q, const void* k, const void* v, const uint32_t* tree_bits,
+                                int bit_words, int64_t q_len, int64_t kv_len, int64_t prefix_len,
+                                int num_heads, int num_kv_heads, int head_dim, int64_t q_head_stride,
+                                int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                                float scale, void* out, void* workspace, size_t workspace_bytes,
+                                int impl, void* stream);
 
 #ifdef __cplusplus
 }

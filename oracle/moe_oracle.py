@@ -11,11 +11,11 @@ means ``transformers/models/qwen3_moe/modeling_qwen3_moe.py`` (5.5.0 installed,
 Numeric contract (shared with the CUDA kernels, so kernel == oracle is exact
 for every integer output):
 
-* Router logits are the exact dot products rounded ONCE to the model dtype
-  (products of bf16/fp32 operands are exact in fp64 and the 2048-term fp64 sum
-  is accurate far below one ulp of the result).  The reference's cuBLAS / MKL
-  GEMM accumulates in fp32 instead, so its rounded logits can differ from these
-  by one ulp; tests count such cases explicitly.
+* Router logits: fp32 models use the exact dot product rounded once; bf16
+  models sum the (exact) bf16*bf16 products in fp32 in the fixed order of the
+  CUDA router (see ``router_logits``) and round once to bf16.  The reference's
+  cuBLAS / MKL GEMM also accumulates in fp32 but in its own order, so its
+  rounded logits can differ from these by one ulp; tests count such cases.
 * Top-k is taken over the logits, ordered by (logit descending, expert id
   ascending).  Softmax is monotone, so this is the reference's
   ``topk(softmax(logits))`` (transformers/...:267-268) with the tie rule made
@@ -46,11 +46,8 @@ def bf16_round(values: np.ndarray) -> np.ndarray:
 
 
 def f64_to_bf16(values: np.ndarray) -> np.ndarray:
-    """Round float64 values directly to bf16 (one rounding, ties to even).
-
-    Going through float32 first could round twice; the kernels use the same
-    single-rounding rule (``round_f64_to_bf16`` in the CUDA router).
-    """
+    """Round float64 values directly to bf16 (one rounding, ties to even);
+    going through float32 first could round twice."""
     a = np.asarray(values, dtype=np.float64)
     mant, exp = np.frexp(a)  # a = mant * 2**exp, 0.5 <= |mant| < 1
     # bf16 keeps 8 significant bits: scale the mantissa to [128, 256).
@@ -60,22 +57,44 @@ def f64_to_bf16(values: np.ndarray) -> np.ndarray:
     return out.astype(np.float32)
 
 
-def to_model_dtype(values64: np.ndarray, dtype: str) -> np.ndarray:
-    if dtype == "bf16":
-        return f64_to_bf16(values64)
-    if dtype == "f32":
-        return np.asarray(values64, dtype=np.float64).astype(np.float32)
-    raise ValueError(f"unsupported dtype {dtype!r}")
-
-
 # ---------------------------------------------------------------------------
 # K1: router (transformers/...:263-272, Qwen3MoeTopKRouter.forward)
 
 
 def router_logits(x: np.ndarray, weight: np.ndarray, dtype: str) -> np.ndarray:
-    """``F.linear(x, W)`` (transformers/...:265) rounded once to ``dtype``."""
-    exact = np.asarray(x, dtype=np.float64) @ np.asarray(weight, dtype=np.float64).T
-    return to_model_dtype(exact, dtype)
+    """``F.linear(x, W)`` (transformers/...:265) in the model dtype.
+
+    fp32: the exact dot product (fp64 sum of exact products) rounded once.
+    bf16: exact bf16*bf16 products summed in fp32 in the order the CUDA router
+    uses -- "lane" l = 0..31 adds positions h = 256 j + 8 l + v in (j, v)
+    order, then the 32 lane sums are combined by an xor butterfly with offsets
+    16, 8, 4, 2, 1 -- and rounded once to bf16 (RNE), i.e. an fp32-accumulated
+    GEMM like the reference's, with a reproducible order."""
+    if dtype == "f32":
+        exact = np.asarray(x, dtype=np.float64) @ np.asarray(weight, dtype=np.float64).T
+        return exact.astype(np.float32)
+    if dtype != "bf16":
+        raise ValueError(f"unsupported dtype {dtype!r}")
+    xs = np.asarray(x, dtype=np.float32)
+    ws = np.asarray(weight, dtype=np.float32)
+    tokens, hidden = xs.shape
+    experts = ws.shape[0]
+    blocks = -(-hidden // 256)
+    pad = blocks * 256 - hidden
+    xr = np.pad(xs, ((0, 0), (0, pad))).reshape(tokens, blocks, 32, 8)
+    wr = np.pad(ws, ((0, 0), (0, pad))).reshape(experts, blocks, 32, 8)
+    out = np.empty((tokens, experts), dtype=np.float32)
+    lanes = np.arange(32)
+    for t0 in range(0, tokens, 64):  # bound the temporary size
+        xt = xr[t0:t0 + 64]
+        acc = np.zeros((xt.shape[0], experts, 32), dtype=np.float32)
+        for j in range(blocks):
+            for v in range(8):
+                acc = acc + xt[:, None, j, :, v] * wr[None, :, j, :, v]  # exact products
+        for off in (16, 8, 4, 2, 1):
+            acc = acc + acc[..., lanes ^ off]
+        out[t0:t0 + 64] = acc[..., 0]
+    return bf16_round(out)
 
 
 def softmax_f32(logits: np.ndarray) -> np.ndarray:

@@ -31,6 +31,10 @@ SF_SWIGLU_AUTO = 0
 SF_SWIGLU_SIMT = 1
 SF_SWIGLU_TCGEN05 = 2
 
+SF_ATTN_AUTO = 0
+SF_ATTN_SIMT = 1
+SF_ATTN_TCGEN05 = 2
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int
 _i64 = ctypes.c_int64
@@ -60,6 +64,8 @@ SIGNATURES = {
     "sf_tree_attention_workspace_bytes": (_sz, [_i32, _i64, _i64]),
     "sf_tree_attention": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i32, _i32,
                                  _i64, _i64, _i64, _i64, _f32, _vp, _vp, _sz, _vp]),
+    "sf_tree_attention_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i32, _i32,
+                                    _i64, _i64, _i64, _i64, _f32, _vp, _vp, _sz, _i32, _vp]),
 }
 
 

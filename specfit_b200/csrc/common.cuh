@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "specfit_b200.h"
@@ -35,6 +36,20 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int num_sms();  // cached SM count of the current device
+
+// Runs f() once per device (per `done` flag word); later calls on that device
+// return SF_OK without calling f.  f must be idempotent: two threads may race
+// to run it the first time.
+template <typename F>
+int once_per_device(std::atomic<unsigned long long>& done, F&& f) {
+  int dev = 0;
+  SF_CHECK_CUDA(cudaGetDevice(&dev));
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return SF_OK;
+  const int rc = f();
+  if (rc == SF_OK) done.fetch_or(bit, std::memory_order_release);
+  return rc;
+}
 
 // ---------------------------------------------------------------------------
 // dtype helpers shared by kernels

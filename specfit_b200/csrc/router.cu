@@ -7,17 +7,19 @@
 //   top    = topk(probs, k)            -> (values, indices)
 //   top   /= top.sum() if norm_topk_prob
 //
-// Numerics: each logit is an exact fp64 dot product (bf16*bf16 and f32*f32
-// products are exact in fp64) rounded ONCE to the model dtype, so the result
-// is the correctly rounded logit and does not depend on a reduction order.
-// Top-k runs on the logits ordered by (value desc, expert id asc); softmax is
-// monotone, so this equals topk(probs) with the tie rule "lower id wins".
+// Numerics: bf16 logits sum exact bf16*bf16 products in fp32 in one fixed
+// order (below) and round once to bf16, like cuBLAS's fp32-accumulate GEMM
+// but with an order the oracle replays bit for bit; fp32 logits sum exact
+// products in fp64 and round once (the correctly rounded logit).  Top-k runs
+// on the logits ordered by (value desc, expert id asc); softmax is monotone,
+// so this equals topk(probs) with the tie rule "lower id wins".
 //
-// Two launches: a logits kernel that spreads T*E*H fp64 FMAs over the whole
-// GPU (a CTA per 8 tokens x 16 experts), and a warp-per-token top-k kernel.
+// Two launches: a logits kernel spread over the GPU (a CTA per 8 tokens x 16
+// experts) and a warp-per-token softmax / top-k kernel.
 #include <math.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -29,24 +31,20 @@ constexpr int kExpTile = 16;   // experts per logits CTA (2 per warp)
 constexpr int kWarps = 8;
 constexpr int kNone = 0x7fffffff;  // "no expert" marker in the top-k reduction
 
-// Correctly rounded double -> bf16 (as float): keep 8 significant bits,
-// round half to even.  frexp/rint/ldexp are exact.
-__device__ __forceinline__ float round_f64_to_bf16(double d) {
-  if (d == 0.0 || !isfinite(d)) return (float)d;
-  int e;
-  double m = frexp(d, &e);           // d = m * 2^e, 0.5 <= |m| < 1
-  double r = rint(m * 256.0);        // round to 8 significant bits (RNE)
-  return (float)ldexp(r / 256.0, e);  // exact in float (8-bit mantissa)
+// Rounding of the accumulated dot product to the model dtype.
+__device__ __forceinline__ float round_logit(double d, float*) { return __double2float_rn(d); }
+__device__ __forceinline__ float round_logit(float f, __nv_bfloat16*) {
+  return __bfloat162float(__float2bfloat16_rn(f));
 }
 
-template <typename T>
-__device__ __forceinline__ float round_logit(double d);
-template <>
-__device__ __forceinline__ float round_logit<float>(double d) { return __double2float_rn(d); }
-template <>
-__device__ __forceinline__ float round_logit<__nv_bfloat16>(double d) { return round_f64_to_bf16(d); }
-
-template <typename T, bool kVec>
+// Logits.  Lane l of a warp owns hidden positions h = 256 j + 8 l + v
+// (j = 0, 1, ...; v = 0..7) and adds its products in that (j, v) order; the
+// 32 lane sums are then combined by an xor butterfly (offsets 16, 8, 4, 2, 1).
+// The order is the same whatever the alignment or H, so the CPU oracle can
+// replay it exactly.  Acc is float for bf16 inputs (bf16*bf16 products are
+// exact in fp32) and double for fp32 inputs (exact products, and a sum whose
+// single rounding to fp32 is the correctly rounded logit).
+template <typename T, typename Acc, bool kVec>
 __global__ void __launch_bounds__(kWarps * 32)
 router_logits_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t tokens, int hidden,
                      int experts, float* __restrict__ logits_f32, T* __restrict__ logits_out) {
@@ -54,46 +52,50 @@ router_logits_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t t
   const int warp = threadIdx.x >> 5;
   const int64_t t0 = (int64_t)blockIdx.x * kTokTile;
   const int ntok = (int)((tokens - t0) < kTokTile ? (tokens - t0) : kTokTile);
-  constexpr int kV = 16 / sizeof(T);  // elements per 16-byte vector
 
   for (int ej = warp; ej < kExpTile; ej += kWarps) {
     const int e = blockIdx.y * kExpTile + ej;
     if (e >= experts) break;
-    double acc[kTokTile];
+    Acc acc[kTokTile];
 #pragma unroll
-    for (int i = 0; i < kTokTile; ++i) acc[i] = 0.0;
+    for (int i = 0; i < kTokTile; ++i) acc[i] = Acc(0);
     const T* wrow = w + (int64_t)e * hidden;
-    if (kVec) {
-      for (int h = lane * kV; h < hidden; h += 32 * kV) {
-        T wv[kV];
-        *reinterpret_cast<uint4*>(wv) = *reinterpret_cast<const uint4*>(wrow + h);
+    for (int h0 = 8 * lane; h0 < hidden; h0 += 256) {
+      T wv[8];
+      if (kVec) {
 #pragma unroll
-        for (int i = 0; i < kTokTile; ++i) {
-          if (i < ntok) {
-            T xv[kV];
-            *reinterpret_cast<uint4*>(xv) =
-                *reinterpret_cast<const uint4*>(x + (t0 + i) * hidden + h);
+        for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+          reinterpret_cast<uint4*>(wv)[q] = reinterpret_cast<const uint4*>(wrow + h0)[q];
+      } else {
 #pragma unroll
-            for (int v = 0; v < kV; ++v)
-              acc[i] = fma((double)to_f32(xv[v]), (double)to_f32(wv[v]), acc[i]);
-          }
-        }
+        for (int v = 0; v < 8; ++v) wv[v] = (h0 + v < hidden) ? wrow[h0 + v] : from_f32<T>(0.f);
       }
-    } else {
-      for (int h = lane; h < hidden; h += 32) {
-        const double wv = (double)to_f32(wrow[h]);
 #pragma unroll
-        for (int i = 0; i < kTokTile; ++i)
-          if (i < ntok) acc[i] = fma((double)to_f32(x[(t0 + i) * hidden + h]), wv, acc[i]);
+      for (int i = 0; i < kTokTile; ++i) {
+        if (i < ntok) {
+          const T* xrow = x + (t0 + i) * hidden;
+          T xv[8];
+          if (kVec) {
+#pragma unroll
+            for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+              reinterpret_cast<uint4*>(xv)[q] = reinterpret_cast<const uint4*>(xrow + h0)[q];
+          } else {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) xv[v] = (h0 + v < hidden) ? xrow[h0 + v] : from_f32<T>(0.f);
+          }
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            acc[i] = fma((Acc)to_f32(xv[v]), (Acc)to_f32(wv[v]), acc[i]);
+        }
       }
     }
 #pragma unroll
     for (int i = 0; i < kTokTile; ++i) {
-      double s = acc[i];
+      Acc s = acc[i];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
       if (lane == 0 && i < ntok) {
-        const float r = round_logit<T>(s);
+        const float r = round_logit(s, (T*)nullptr);
         logits_f32[(t0 + i) * experts + e] = r;
         if (logits_out) logits_out[(t0 + i) * experts + e] = from_f32<T>(r);
       }
@@ -101,7 +103,80 @@ router_logits_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t t
   }
 }
 
-// Warp per token.  Lane l owns experts l, l+32, ... (up to 32 per lane).
+// Staged variant for 16-byte aligned rows: the CTA's token rows and expert
+// rows are first copied into shared memory with one burst of asynchronous
+// 16-byte copies (cp.async), so the dot products run from shared memory
+// instead of waiting on one round of L2 loads per 256 columns.  Same lane
+// assignment and summation order as router_logits_kernel.
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(kWarps * 32)
+router_logits_staged(const T* __restrict__ x, const T* __restrict__ w, int64_t tokens, int hidden,
+                     int experts, float* __restrict__ logits_f32, T* __restrict__ logits_out) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  T* xs = reinterpret_cast<T*>(smem_raw);        // [kTokTile][hidden]
+  T* ws = xs + (size_t)kTokTile * hidden;         // [kExpTile][hidden]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t t0 = (int64_t)blockIdx.x * kTokTile;
+  const int ntok = (int)((tokens - t0) < kTokTile ? (tokens - t0) : kTokTile);
+  const int e0 = blockIdx.y * kExpTile;
+  const int nexp = (experts - e0) < kExpTile ? (experts - e0) : kExpTile;
+  const int vec_per_row = hidden * (int)sizeof(T) / 16;
+  const int total = (ntok + nexp) * vec_per_row;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int r = i / vec_per_row, c = i % vec_per_row;
+    const T* src = (r < ntok) ? x + (t0 + r) * hidden : w + (int64_t)(e0 + r - ntok) * hidden;
+    T* dst = (r < ntok) ? xs + (size_t)r * hidden : ws + (size_t)(r - ntok) * hidden;
+    const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(dst + c * (16 / sizeof(T))));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr),
+                 "l"(src + c * (16 / sizeof(T)))
+                 : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  for (int ej = warp; ej < nexp; ej += kWarps) {
+    Acc acc[kTokTile];
+#pragma unroll
+    for (int i = 0; i < kTokTile; ++i) acc[i] = Acc(0);
+    const T* wrow = ws + (size_t)ej * hidden;
+    for (int h0 = 8 * lane; h0 < hidden; h0 += 256) {
+      T wv[8];
+#pragma unroll
+      for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+        reinterpret_cast<uint4*>(wv)[q] = reinterpret_cast<const uint4*>(wrow + h0)[q];
+#pragma unroll
+      for (int i = 0; i < kTokTile; ++i) {
+        if (i < ntok) {
+          T xv[8];
+#pragma unroll
+          for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+            reinterpret_cast<uint4*>(xv)[q] =
+                reinterpret_cast<const uint4*>(xs + (size_t)i * hidden + h0)[q];
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            acc[i] = fma((Acc)to_f32(xv[v]), (Acc)to_f32(wv[v]), acc[i]);
+        }
+      }
+    }
+    const int e = e0 + ej;
+#pragma unroll
+    for (int i = 0; i < kTokTile; ++i) {
+      Acc s = acc[i];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (lane == 0 && i < ntok) {
+        const float r = round_logit(s, (T*)nullptr);
+        logits_f32[(t0 + i) * experts + e] = r;
+        if (logits_out) logits_out[(t0 + i) * experts + e] = from_f32<T>(r);
+      }
+    }
+  }
+}
+
+// Softmax + top-k, warp per token.  Lane l owns experts l + 32 j, j < kEpl,
+// held in registers.
+template <int kEpl>
 __global__ void __launch_bounds__(kWarps * 32)
 router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts, int top_k,
                    int norm, float* __restrict__ probs, float* __restrict__ topk_w,
@@ -110,25 +185,29 @@ router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts
   const int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (t >= tokens) return;
   const float* row = logits + t * experts;
-  const int per_lane = (experts + 31) / 32;
-
+  float val[kEpl];
   float m = -INFINITY;
-  for (int j = 0; j < per_lane; ++j) {
+#pragma unroll
+  for (int j = 0; j < kEpl; ++j) {
     const int e = lane + 32 * j;
-    if (e < experts) m = fmaxf(m, row[e]);
+    val[j] = e < experts ? row[e] : -INFINITY;
+    m = fmaxf(m, val[j]);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  float ex[kEpl];
   float s = 0.f;
-  for (int j = 0; j < per_lane; ++j) {
-    const int e = lane + 32 * j;
-    if (e < experts) s += expf(row[e] - m);
+#pragma unroll
+  for (int j = 0; j < kEpl; ++j) {
+    ex[j] = (lane + 32 * j < experts) ? expf(val[j] - m) : 0.f;
+    s += ex[j];
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  for (int j = 0; j < per_lane; ++j) {
+#pragma unroll
+  for (int j = 0; j < kEpl; ++j) {
     const int e = lane + 32 * j;
-    if (e < experts) probs[t * experts + e] = expf(row[e] - m) / s;
+    if (e < experts) probs[t * experts + e] = ex[j] / s;
   }
 
   // Top-k by (logit desc, id asc).  taken: bit j <-> expert lane + 32 j.
@@ -137,31 +216,32 @@ router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts
   int sel_e = 0;
   for (int k = 0; k < top_k; ++k) {
     // Lane-local best; e grows with j, so a strict '>' keeps the lower id on ties.
-    float bv = -INFINITY;
+    float bv = -INFINITY, bp = 0.f;
     int be = kNone;
-    for (int j = 0; j < per_lane; ++j) {
+#pragma unroll
+    for (int j = 0; j < kEpl; ++j) {
       const int e = lane + 32 * j;
-      if (e < experts && !((taken >> j) & 1u)) {
-        const float v = row[e];
-        if (be == kNone || v > bv) {
-          bv = v;
-          be = e;
-        }
+      if (e < experts && !((taken >> j) & 1u) && (be == kNone || val[j] > bv)) {
+        bv = val[j];
+        bp = ex[j];
+        be = e;
       }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const float op = __shfl_xor_sync(0xffffffffu, bp, off);
       const int oe = __shfl_xor_sync(0xffffffffu, be, off);
       if (oe != kNone && (be == kNone || ov > bv || (ov == bv && oe < be))) {
         bv = ov;
+        bp = op;
         be = oe;
       }
     }
     if (be != kNone && (be & 31) == lane) taken |= 1u << (be >> 5);
     if (lane == k) {
       sel_e = be;
-      sel_p = expf(bv - m) / s;
+      sel_p = bp / s;
     }
   }
   if (norm) {
@@ -176,23 +256,47 @@ router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts
   }
 }
 
+template <int kEpl>
+void launch_topk(const float* logits, int64_t tokens, int E, int K, int norm, float* probs,
+                 float* topk_w, int64_t* topk_idx, cudaStream_t stream) {
+  router_topk_kernel<kEpl><<<(unsigned)((tokens + kWarps - 1) / kWarps), kWarps * 32, 0, stream>>>(
+      logits, tokens, E, K, norm, probs, topk_w, topk_idx);
+}
+
 template <typename T>
 int launch_router(const void* hidden, const void* weight, int64_t tokens, int H, int E, int K,
                   int norm, float* probs, float* topk_w, int64_t* topk_idx, void* logits_out,
                   float* logits_ws, cudaStream_t stream) {
+  using Acc = typename std::conditional<std::is_same<T, float>::value, double, float>::type;
   const T* x = static_cast<const T*>(hidden);
   const T* w = static_cast<const T*>(weight);
   dim3 grid((unsigned)((tokens + kTokTile - 1) / kTokTile), (unsigned)((E + kExpTile - 1) / kExpTile));
-  const bool vec = (H % (16 / (int)sizeof(T)) == 0) && aligned16(x) && aligned16(w);
-  if (vec)
-    router_logits_kernel<T, true><<<grid, kWarps * 32, 0, stream>>>(x, w, tokens, H, E, logits_ws,
-                                                                    static_cast<T*>(logits_out));
+  const bool vec = (H % 8 == 0) && aligned16(x) && aligned16(w);
+  const size_t staged_smem = (size_t)(kTokTile + kExpTile) * H * sizeof(T);
+  if (vec && staged_smem <= 200 * 1024) {
+    static std::atomic<unsigned long long> configured{0};
+    if (int rc = once_per_device(configured, [] {
+          SF_CHECK_CUDA(cudaFuncSetAttribute(router_logits_staged<T, Acc>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+          return SF_OK;
+        }))
+      return rc;
+    router_logits_staged<T, Acc><<<grid, kWarps * 32, staged_smem, stream>>>(
+        x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+  } else if (vec)
+    router_logits_kernel<T, Acc, true><<<grid, kWarps * 32, 0, stream>>>(
+        x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
   else
-    router_logits_kernel<T, false><<<grid, kWarps * 32, 0, stream>>>(x, w, tokens, H, E, logits_ws,
-                                                                     static_cast<T*>(logits_out));
+    router_logits_kernel<T, Acc, false><<<grid, kWarps * 32, 0, stream>>>(
+        x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
   SF_CHECK_LAUNCH();
-  router_topk_kernel<<<(unsigned)((tokens + kWarps - 1) / kWarps), kWarps * 32, 0, stream>>>(
-      logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx);
+  const int epl = (E + 31) / 32;
+  if (epl <= 1) launch_topk<1>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);
+  else if (epl <= 2) launch_topk<2>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);
+  else if (epl <= 4) launch_topk<4>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);
+  else if (epl <= 8) launch_topk<8>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);
+  else if (epl <= 16) launch_topk<16>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);
+  else launch_topk<32>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

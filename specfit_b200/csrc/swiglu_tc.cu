@@ -316,6 +316,20 @@ int encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* 
   return SF_OK;
 }
 
+bool device_is_sm100() {
+  static std::atomic<int> cache[64];  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (v == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+    v = (major == 10) ? 1 : 2;
+    cache[dev & 63].store(v, std::memory_order_relaxed);
+  }
+  return v == 1;
+}
+
 }  // namespace
 
 bool swiglu_tcgen05_supports(const SwigluArgs& a) {
@@ -330,10 +344,19 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
     return set_error(SF_ERR_UNSUPPORTED,
                      "tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0 and 16-byte aligned buffers");
   if (a.rows == 0) return SF_OK;
-  int dev = 0, major = 0;
-  SF_CHECK_CUDA(cudaGetDevice(&dev));
-  SF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
-  if (major != 10) return set_error(SF_ERR_UNSUPPORTED, "tcgen05 SwiGLU needs an sm_100 device");
+  static std::atomic<unsigned long long> configured{0};
+  if (int rc = once_per_device(configured, [] {
+        int dev = 0, major = 0;
+        SF_CHECK_CUDA(cudaGetDevice(&dev));
+        SF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+        if (major != 10) return set_error(SF_ERR_UNSUPPORTED, "tcgen05 SwiGLU needs an sm_100 device");
+        SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<1>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+        SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+        return SF_OK;
+      }))
+    return rc;
 
   const int H = a.hidden, I = a.inter;
   const uint64_t slot_bytes = (uint64_t)a.slot_stride * 2;
@@ -363,10 +386,6 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
     cuuint32_t box[2] = {kBK, kBBox};
     if (int rc = encode_bf16(&tm_x2, a.act_workspace, 2, dims, strides, box)) return rc;
   }
-  SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kSmemBytes));
-  SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kSmemBytes));
   const int grid = num_sms();
   auto* act = static_cast<__nv_bfloat16*>(a.act_workspace);
   swiglu_tc_kernel<1><<<grid, kThreads, kSmemBytes, stream>>>(
@@ -416,12 +435,7 @@ extern "C" int sf_grouped_swiglu_ex(const void* hidden_sorted, const float* weig
   if (impl == SF_SWIGLU_SIMT) return swiglu_simt(a, s);
   if (impl == SF_SWIGLU_TCGEN05) return swiglu_tcgen05(a, s);
   SF_CHECK_ARG(impl == SF_SWIGLU_AUTO, "unknown implementation %d", impl);
-  if (swiglu_tcgen05_supports(a)) {
-    int major = 0, dev = 0;
-    SF_CHECK_CUDA(cudaGetDevice(&dev));
-    SF_CHECK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
-    if (major == 10) return swiglu_tcgen05(a, s);
-  }
+  if (swiglu_tcgen05_supports(a) && device_is_sm100()) return swiglu_tcgen05(a, s);
   return swiglu_simt(a, s);
 }
 

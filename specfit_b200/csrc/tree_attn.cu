@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "tree_attn.h"
 
 namespace sf {
 namespace {
@@ -30,20 +31,7 @@ constexpr int kKPitch = kD + 2;  // bf16 pitch of the K tile (bank-conflict free
 constexpr int kMaxGroup = 8;   // query heads per KV head handled by one CTA
 constexpr int kMaxSplits = 32;
 
-struct Params {
-  const __nv_bfloat16* q;
-  const __nv_bfloat16* k;
-  const __nv_bfloat16* v;
-  const uint32_t* bits;
-  int bit_words;
-  int q_len, kv_len, prefix_len;
-  int num_heads, num_kv_heads, group;
-  int64_t q_hs, q_rs, kv_hs, kv_rs;
-  float scale;
-  int splits, keys_per_split;
-  float* part_o;   // [splits, Hq, Tq, D]
-  float* part_ml;  // [splits, Hq, Tq, 2]
-};
+using Params = AttnParams;
 
 __device__ __forceinline__ bool visible(const Params& p, int row, int key) {
   if (key < p.prefix_len) return true;
@@ -242,13 +230,13 @@ extern "C" size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len
   return (size_t)sf::kMaxSplits * num_heads * q_len * (sf::kD + 2) * sizeof(float);
 }
 
-extern "C" int sf_tree_attention(const void* q, const void* k, const void* v,
-                                 const uint32_t* tree_bits, int bit_words, int64_t q_len,
-                                 int64_t kv_len, int64_t prefix_len, int num_heads,
-                                 int num_kv_heads, int head_dim, int64_t q_head_stride,
-                                 int64_t q_row_stride, int64_t kv_head_stride,
-                                 int64_t kv_row_stride, float scale, void* out, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
+                                    const uint32_t* tree_bits, int bit_words, int64_t q_len,
+                                    int64_t kv_len, int64_t prefix_len, int num_heads,
+                                    int num_kv_heads, int head_dim, int64_t q_head_stride,
+                                    int64_t q_row_stride, int64_t kv_head_stride,
+                                    int64_t kv_row_stride, float scale, void* out, void* workspace,
+                                    size_t workspace_bytes, int impl, void* stream) {
   using namespace sf;
   SF_CHECK_ARG(head_dim == kD, "head_dim must be 128");
   SF_CHECK_ARG(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
@@ -294,14 +282,42 @@ extern "C" int sf_tree_attention(const void* q, const void* k, const void* v,
   p.part_o = static_cast<float*>(workspace);
   p.part_ml = p.part_o + (size_t)p.splits * num_heads * q_len * kD;
   cudaStream_t s = as_stream(stream);
+  const int64_t pairs = (int64_t)num_heads * q_len;
+  if (impl != SF_ATTN_SIMT && tree_attention_tc_supports(p, head_dim)) {
+    int splits = 0;
+    if (int rc = tree_attention_tc(p, s, &splits)) return rc;
+    p.splits = splits;
+    p.part_ml = p.part_o + (size_t)p.splits * num_heads * q_len * kD;
+    tree_attn_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(out));
+    SF_CHECK_LAUNCH();
+    return SF_OK;
+  }
+  SF_CHECK_ARG(impl != SF_ATTN_TCGEN05, "the tcgen05 tree attention does not support this shape");
   dim3 grid((unsigned)num_kv_heads, (unsigned)((q_len + kRows - 1) / kRows), (unsigned)p.splits);
   const size_t smem = (size_t)(kTile * kD + kTile * kKPitch + kMaxGroup * kRows * kD) * 2;
-  SF_CHECK_CUDA(cudaFuncSetAttribute(tree_attn_split_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  static std::atomic<unsigned long long> configured{0};
+  if (int rc = once_per_device(configured, [&] {
+        SF_CHECK_CUDA(cudaFuncSetAttribute(tree_attn_split_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        return SF_OK;
+      }))
+    return rc;
   tree_attn_split_kernel<<<grid, kMaxGroup * 32, smem, s>>>(p);
   SF_CHECK_LAUNCH();
-  const int64_t pairs = (int64_t)num_heads * q_len;
   tree_attn_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(out));
   SF_CHECK_LAUNCH();
   return SF_OK;
+}
+
+extern "C" int sf_tree_attention(const void* q, const void* k, const void* v,
+                                 const uint32_t* tree_bits, int bit_words, int64_t q_len,
+                                 int64_t kv_len, int64_t prefix_len, int num_heads,
+                                 int num_kv_heads, int head_dim, int64_t q_head_stride,
+                                 int64_t q_row_stride, int64_t kv_head_stride,
+                                 int64_t kv_row_stride, float scale, void* out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  return sf_tree_attention_ex(q, k, v, tree_bits, bit_words, q_len, kv_len, prefix_len, num_heads,
+                              num_kv_heads, head_dim, q_head_stride, q_row_stride, kv_head_stride,
+                              kv_row_stride, scale, out, workspace, workspace_bytes, SF_ATTN_AUTO,
+                              stream);
 }

@@ -237,7 +237,7 @@ def slot_fill_batch(dsts, srcs, stream: torch.cuda.Stream) -> None:
 
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits: torch.Tensor | None,
                    prefix_len: int, scale: float | None = None,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
+                   out: torch.Tensor | None = None, impl: int = N.SF_ATTN_AUTO) -> torch.Tensor:
     """Masked GQA attention.  ``q[Hq, Tq, D]``, ``k/v[Hkv, Tk, D]`` (bf16, any
     strides with unit stride on D); keys ``< prefix_len`` are visible to every
     query, tree key j is visible to row i when bit j of ``tree_bits[i]`` is
@@ -259,10 +259,10 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits:
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     sc = float(dim ** -0.5 if scale is None else scale)
     N.check(
-        N.lib.sf_tree_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(bits), words, tq, tk,
-                                prefix_len, hq, hkv, dim, q.stride(0), q.stride(1), k.stride(0),
-                                k.stride(1), sc, res.data_ptr(), ws.data_ptr(), ws_bytes,
-                                _stream(dev)),
+        N.lib.sf_tree_attention_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(bits), words, tq,
+                                   tk, prefix_len, hq, hkv, dim, q.stride(0), q.stride(1),
+                                   k.stride(0), k.stride(1), sc, res.data_ptr(), ws.data_ptr(),
+                                   ws_bytes, impl, _stream(dev)),
         "sf_tree_attention",
     )
     _launched(2)

@@ -80,7 +80,11 @@ class ExpertHostPool:
         nbytes = self.data.numel() * self.data.element_size()
         rc = torch.cuda.cudart().cudaHostRegister(self.data.data_ptr(), nbytes, 0)
         if int(rc) != 0:
-            raise RuntimeError(f"cudaHostRegister of the expert pool failed ({int(rc)})")
+            import resource
+
+            soft, hard = resource.getrlimit(resource.RLIMIT_MEMLOCK)
+            raise RuntimeError(f"cudaHostRegister of the {nbytes / 1e9:.1f} GB expert pool failed "
+                               f"({int(rc)}); RLIMIT_MEMLOCK soft={soft} hard={hard}")
         self._registered = True
 
     @property

@@ -42,6 +42,12 @@ def _packed_bits(mask: torch.Tensor, q_len: int, kv_len: int, batch: int):
     return bits
 
 
+def clear_mask_cache() -> None:
+    """Forget the packed mask, so the next forward packs its mask again (a
+    CUDA-graph capture must record the packing, not reuse eager results)."""
+    _pack_cache.clear()
+
+
 _causal_cache: dict = {}
 
 

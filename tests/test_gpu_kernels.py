@@ -275,8 +275,10 @@ def test_combine_bit_exact_sequential(ops):
 # --------------------------------------------------------- K6 tree attention
 
 
-@pytest.mark.parametrize("nodes,depth,ctx", [(4, 2, 2), (64, 6, 512), (128, 8, 300), (60, 8, 2048), (0, 0, 33)])
-def test_tree_attention_vs_oracle(ops, nodes, depth, ctx):
+@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("nodes,depth,ctx", [(4, 2, 2), (64, 6, 512), (128, 8, 300), (60, 8, 2048), (0, 0, 33),
+                                             (200, 9, 700)])
+def test_tree_attention_vs_oracle(ops, nodes, depth, ctx, impl):
     if nodes:
         _, parents, _ = synthetic.random_tree(nodes, max_depth=depth, max_branch=4, seed=nodes)
     else:
@@ -288,7 +290,7 @@ def test_tree_attention_vs_oracle(ops, nodes, depth, ctx):
     k = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16)
     v = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16)
     bits = ops.tree_bits_from_parents(parents, DEV)
-    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), bits, ctx)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), bits, ctx, impl=impl)
     mask = to.verification_attention_mask(parents, ctx)
     ref = to.tree_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), mask)
     got = out.float().cpu().numpy().transpose(1, 0, 2)
@@ -299,7 +301,8 @@ def test_tree_attention_vs_oracle(ops, nodes, depth, ctx):
     assert torch.equal(packed, bits)
 
 
-def test_tree_attention_strided_views(ops):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_tree_attention_strided_views(ops, impl):
     """Inputs as HF lays them out: q from a [1, T, Hq*D] projection viewed as
     [Hq, T, D] (non-contiguous), K/V cache [Hkv, Tk, D]."""
     parents = (0, 0, 1, 2)
@@ -309,10 +312,30 @@ def test_tree_attention_strided_views(ops):
     q = qp.view(tq, 32, 128).transpose(0, 1)
     k = torch.randn(4, ctx + tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
     v = torch.randn(4, ctx + tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
-    out = ops.tree_attention(q, k, v, ops.tree_bits_from_parents(parents, DEV), ctx)
+    out = ops.tree_attention(q, k, v, ops.tree_bits_from_parents(parents, DEV), ctx, impl=impl)
     mask = to.verification_attention_mask(parents, ctx)
     ref = to.tree_attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), mask)
     assert np.abs(out.float().cpu().numpy().transpose(1, 0, 2) - ref).max() <= ATOL_BF16
+
+
+def test_tree_attention_full_mask_and_long_context(ops):
+    """Arbitrary boolean mask packed over every key (prefix_len 0), 4096-key
+    context with 8 query heads per KV head, tcgen05 vs CUDA-core vs oracle."""
+    gen = torch.Generator().manual_seed(7)
+    tq, tk = 65, 4161
+    q = torch.randn(32, tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    k = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    v = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    mask = torch.rand(tq, tk, generator=gen) < 0.3
+    mask[:, 0] = True
+    bits = ops.tree_bits_from_mask(mask.to(DEV), 0)
+    a = ops.tree_attention(q, k, v, bits, 0, impl=2).float().cpu().numpy()
+    b = ops.tree_attention(q, k, v, bits, 0, impl=1).float().cpu().numpy()
+    assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= COS_MIN
+    sub = slice(0, 8)  # oracle on a few heads (fp64, CPU)
+    ref = to.tree_attention(q[sub].float().cpu().numpy(), k[:1].float().cpu().numpy(),
+                            v[:1].float().cpu().numpy(), mask.numpy())
+    assert np.abs(a.transpose(1, 0, 2)[sub] - ref).max() <= ATOL_BF16
 
 
 def test_device_status_clean(ops):

@@ -125,3 +125,47 @@ def test_tree_nodes_equal_causal_paths(loaded):
 def test_pool_is_page_locked(loaded):
     assert loaded.pool.data[0, 0].is_pinned()
     assert all(c.sources_are_pinned for c in loaded.caches)
+
+
+def test_verify_graph_replay_equals_eager():
+    """A captured verify pass (every expert resident) replays bit for bit."""
+    from transformers import DynamicCache
+
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3
+    from specfit_b200.runtime.verify_graph import VerifyGraph
+
+    m = build_random_offloaded_qwen3(device=DEV, slots_per_layer=16, config=small_config(), seed=5,
+                                     std=0.05)
+    try:
+        m.warm_all_caches()
+        model = m.model
+        ctx = torch.randint(0, 512, (1, 37), generator=torch.Generator().manual_seed(2)).to(DEV)
+        cache = DynamicCache(config=model.config)
+        with torch.no_grad():
+            model(input_ids=ctx, past_key_values=cache, use_cache=True)
+        trees = [make_tree(nodes=9, depth=4, seed=s) for s in (1, 2)]
+        inputs = []
+        for tree in trees:
+            ids = tree.verification_token_ids(torch.tensor([[5]], device=DEV))
+            mask = tree.verification_attention_mask(base_kv_length=37, device=DEV)
+            pos = tree.verification_position_ids(base_kv_length=37, device=DEV)
+            inputs.append((ids, mask, pos))
+        eager = []
+        for ids, mask, pos in inputs:
+            with torch.no_grad():
+                out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
+                            use_cache=True)
+            eager.append(out.logits[0].clone())
+            cache.crop(37)
+        vg = VerifyGraph(model, cache, q_len=10, device=DEV)
+        vg.capture(*inputs[0])
+        hits_before = m.caches[0].stats().resident_hits
+        for (ids, mask, pos), ref in zip(inputs, eager):
+            vg.load(ids, mask, pos)
+            vg.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(vg.logits[0], ref)
+        assert cache.get_seq_length() == 37
+        assert m.caches[0].stats().resident_hits > hits_before  # replays count hits
+    finally:
+        m.close()
