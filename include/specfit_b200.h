@@ -62,9 +62,11 @@ SF_API const char* sf_last_error(void);
 SF_API int sf_abi_version(void);
 
 /*
- * Sticky device-side status of the current device: nonzero once a kernel of
- * this library gave up a bounded wait (it then skipped its remaining work and
- * returned).  Synchronous: reads (and with reset != 0 clears) the word.
+ * Sticky device-side status of the current device: 0, or the code of the first
+ * barrier wait of the tcgen05 grouped SwiGLU kernel that gave up after its
+ * one-second limit (site codes 1..6); that kernel then skipped its remaining
+ * work and returned.  Synchronous: reads (and with reset != 0
+ * clears) the words.
  * No reference counterpart; the reference's GPU work is PyTorch library calls.
  */
 SF_API int sf_device_status(int* status, int reset);
@@ -197,9 +199,8 @@ SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const si
  * eagle3_types.py:450-473).
  */
 /* Implementation choice of sf_tree_attention_ex. */
-#define SF_ATTN_AUTO 0    /* tcgen05 kernel when supported (sm_100, D=128, Tk<=8192, 16-byte rows), else SIMT */
-#define SF_ATTN_SIMT 1    /* CUDA-core split kernel */
-#define SF_ATTN_TCGEN05 2 /* tcgen05/TMEM kernel; fails with SF_ERR_INVALID_ARGUMENT if unsupported */
+#define SF_ATTN_AUTO 0 /* best available implementation for the shape */
+#define SF_ATTN_SIMT 1 /* CUDA-core split kernel */
 
 SF_API size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len, int64_t kv_len);
 SF_API int sf_tree_attention(const void* q, const void* k, const void* v, const uint32_t* tree_bits,

@@ -3,6 +3,7 @@
 #include <stdio.h>
 
 #include "common.cuh"
+#include "swiglu.h"
 
 namespace sf {
 
@@ -38,3 +39,9 @@ int num_sms() {
 extern "C" const char* sf_last_error(void) { return sf::g_last_error.c_str(); }
 
 extern "C" int sf_abi_version(void) { return 1; }
+
+extern "C" int sf_device_status(int* status, int reset) {
+  using namespace sf;
+  SF_CHECK_ARG(status, "null pointer argument");
+  return swiglu_status(status, reset);
+}

@@ -45,20 +45,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Poll limit for every barrier wait: try_wait itself suspends for a
-// hardware-defined interval per call, so this bounds a wait to seconds.
-constexpr uint32_t kWaitPolls = 1u << 24;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
-// Waits for the phase of `bar` with the given parity.  Returns false if the
-// wait gave up or another role already flagged an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+// Wall-clock limit of every barrier wait.  Normal waits last microseconds.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+// Waits for the phase of `bar` with the given parity.  Returns false when
+// another role already flagged an abort, or after kWaitLimitNs: then it sets
+// *abort_flag and records `site` (the first failure only) in *status_word so
+// the host can tell which wait gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status_word, int site) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort_flag) return false;
+    if ((i & 15u) == 15u) {
+      if (*abort_flag) return false;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        if (status_word) atomicCAS(status_word, 0, site);
+        return false;
+      }
+    }
   }
-  *abort_flag = 1;
-  return false;
 }
 
 // 2-D / 3-D TMA tile loads into shared memory, completing on `bar`.

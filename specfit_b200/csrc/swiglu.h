@@ -30,5 +30,7 @@ int swiglu_simt(const SwigluArgs& a, cudaStream_t stream);
 // Returns SF_ERR_UNSUPPORTED (without a message) when the shape does not fit.
 int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream);
 bool swiglu_tcgen05_supports(const SwigluArgs& a);
+// Reads (and with reset clears) the device status word of the tcgen05 kernels.
+int swiglu_status(int* status, int reset);
 
 }  // namespace sf

@@ -34,9 +34,11 @@
 
 namespace sf {
 
-__device__ int g_device_status;  // sticky device-side error word, see sf_device_status
-
 namespace {
+
+// Sticky device-side status of this file's kernels: 0, or the site code of
+// the first barrier wait that gave up (1..6).
+__device__ int g_swiglu_status;
 
 constexpr int kBM = 128;       // MMA M: weight rows per tile
 constexpr int kBK = 64;        // K elements per stage (one 128-byte swizzle atom)
@@ -156,7 +158,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
         for (int kb = 0; kb < space.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!ptx::mbar_wait(&tail->empty[s], ph ^ 1, abort_flag)) return false;
+          if (!ptx::mbar_wait(&tail->empty[s], ph ^ 1, abort_flag, &g_swiglu_status, 1)) return false;
           ptx::mbar_arrive_expect_tx(&tail->full[s], bytes);
           uint8_t* a = a_stage + (size_t)s * kABytes;
           if (kPhase == 1) {
@@ -176,7 +178,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       // Let every load this thread issued land before the CTA can exit.
       volatile int never = 0;
       for (uint32_t i = (it > (uint32_t)kStages ? it - kStages : 0u); i < it; ++i)
-        ptx::mbar_wait(&tail->full[i % kStages], (i / kStages) & 1, &never);
+        ptx::mbar_wait(&tail->full[i % kStages], (i / kStages) & 1, &never, &g_swiglu_status, 2);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -185,7 +187,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
         const int buf = unit & 1;
         const uint32_t aph = (unit >> 1) & 1;
-        if (!ptx::mbar_wait(&tail->acc_empty[buf], aph ^ 1, abort_flag)) return false;
+        if (!ptx::mbar_wait(&tail->acc_empty[buf], aph ^ 1, abort_flag, &g_swiglu_status, 3)) return false;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * kBN;
         const uint32_t npad = (u.npass + 15) & ~15;
@@ -193,7 +195,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
         for (int kb = 0; kb < space.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!ptx::mbar_wait(&tail->full[s], ph, abort_flag)) return false;
+          if (!ptx::mbar_wait(&tail->full[s], ph, abort_flag, &g_swiglu_status, 4)) return false;
           ptx::tc_fence_after();
           const uint64_t adesc = ptx::smem_desc_k_sw128(ptx::smem_u32(a_stage + (size_t)s * kABytes));
           const uint64_t bdesc = ptx::smem_desc_k_sw128(ptx::smem_u32(b_stage + (size_t)s * kBBytes));
@@ -212,7 +214,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       // Drain: the barrier fires once every MMA issued above has completed.
       ptx::umma_commit(&tail->mma_done);
       volatile int never = 0;
-      ptx::mbar_wait(&tail->mma_done, 0, &never);
+      ptx::mbar_wait(&tail->mma_done, 0, &never, &g_swiglu_status, 5);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
@@ -222,7 +224,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
       const int buf = unit & 1;
       const uint32_t aph = (unit >> 1) & 1;
-      ptx::mbar_wait(&tail->acc_full[buf], aph, abort_flag);
+      ptx::mbar_wait(&tail->acc_full[buf], aph, abort_flag, &g_swiglu_status, 6);
       // The four epilogue warps take one consistent go/stop decision before
       // any of them enters the per-chunk named barriers below.
       ptx::named_bar_sync(2, 128);
@@ -283,7 +285,6 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, kTmemCols);
   }
-  if (threadIdx.x == 0 && tail->abort_flag) atomicExch(&g_device_status, 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -398,18 +399,16 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
   return SF_OK;
 }
 
-}  // namespace sf
-
-extern "C" int sf_device_status(int* status, int reset) {
-  using namespace sf;
-  SF_CHECK_ARG(status, "null pointer argument");
-  SF_CHECK_CUDA(cudaMemcpyFromSymbol(status, g_device_status, sizeof(int)));
+int swiglu_status(int* status, int reset) {
+  SF_CHECK_CUDA(cudaMemcpyFromSymbol(status, g_swiglu_status, sizeof(int)));
   if (reset) {
     const int zero = 0;
-    SF_CHECK_CUDA(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)));
+    SF_CHECK_CUDA(cudaMemcpyToSymbol(g_swiglu_status, &zero, sizeof(int)));
   }
   return SF_OK;
 }
+
+}  // namespace sf
 
 extern "C" int sf_grouped_swiglu_ex(const void* hidden_sorted, const float* weights_sorted,
                                     int dtype, const int32_t* offsets, const int32_t* active,

@@ -1,6 +1,5 @@
-// Internal interface between sf_tree_attention and its two implementations
-// (CUDA-core split kernel and the tcgen05 kernel); both write split partials
-// that tree_attn_merge_kernel combines.
+// Parameters shared by the tree-attention split kernels and the merge kernel
+// that combines their partials.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -23,9 +22,5 @@ struct AttnParams {
   float* part_o;   // [splits, Hq, Tq, D] unnormalised outputs
   float* part_ml;  // [splits, Hq, Tq, 2] (row max of scaled scores, row sum)
 };
-
-bool tree_attention_tc_supports(const AttnParams& p, int head_dim);
-// Launches the tcgen05 split kernel; sets *splits (partials written).
-int tree_attention_tc(const AttnParams& p, cudaStream_t stream, int* splits);
 
 }  // namespace sf
