@@ -614,9 +614,29 @@ def block_mode(args):
     ms, outs = timed_steps(block, args.steps, args.warmup, 1, device)
     uniq = int(outs[-1][1].num_active.item())
     us = ms * 1e3 / args.steps
+
+    # Per-op device time of one more block (events between the launches).
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    ev[0].record()
+    _, w, idx = ops.router_topk(x, router, 8, True)
+    if zipf is not None:
+        idx = zipf
+    ev[1].record()
+    d = ops.moe_dispatch(idx, e)
+    ev[2].record()
+    xs, ws = ops.moe_gather(x, w, d)
+    ev[3].record()
+    ys = ops.grouped_swiglu(xs, ws, d, slot, storage, h, i)
+    ev[4].record()
+    ops.moe_combine(ys, d, idx)
+    ev[5].record()
+    torch.cuda.synchronize()
+    names = ("router", "dispatch", "gather", "grouped_swiglu", "combine")
+    per_op = {n: round(ev[j].elapsed_time(ev[j + 1]) * 1e3, 2) for j, n in enumerate(names)}
     algo = uniq * EXPERT_BYTES + e * h * 2
     print(json.dumps({"mode": "block", "tokens": args.tokens, "routes": args.routes, "experts": uniq,
-                      "us_per_block": round(us, 2), "algorithmic_GBps": round(algo / us / 1e3, 1),
+                      "us_per_block": round(us, 2), "per_op_us": per_op,
+                      "algorithmic_GBps": round(algo / us / 1e3, 1),
                       "frac_of_hbm_peak": round(algo / us / 1e3 / peaks["hbm_gbs"], 4)}), flush=True)
 
 

@@ -199,8 +199,9 @@ SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const si
  * eagle3_types.py:450-473).
  */
 /* Implementation choice of sf_tree_attention_ex. */
-#define SF_ATTN_AUTO 0 /* best available implementation for the shape */
+#define SF_ATTN_AUTO 0 /* tensor-core kernel when supported (D=128, q rows 4-byte and K/V rows 16-byte aligned), else CUDA cores */
 #define SF_ATTN_SIMT 1 /* CUDA-core split kernel */
+#define SF_ATTN_MMA 2  /* warp-level tensor-core (mma.sync) split kernel; SF_ERR_INVALID_ARGUMENT if unsupported */
 
 SF_API size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len, int64_t kv_len);
 SF_API int sf_tree_attention(const void* q, const void* k, const void* v, const uint32_t* tree_bits,

@@ -283,7 +283,15 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
   p.part_ml = p.part_o + (size_t)p.splits * num_heads * q_len * kD;
   cudaStream_t s = as_stream(stream);
   const int64_t pairs = (int64_t)num_heads * q_len;
-  SF_CHECK_ARG(impl == SF_ATTN_AUTO || impl == SF_ATTN_SIMT, "unknown attention implementation %d", impl);
+  SF_CHECK_ARG(impl == SF_ATTN_AUTO || impl == SF_ATTN_SIMT || impl == SF_ATTN_MMA,
+               "unknown attention implementation %d", impl);
+  if (impl != SF_ATTN_SIMT && tree_attention_mma_supports(p, head_dim)) {
+    if (int rc = tree_attention_mma(p, s)) return rc;
+    tree_attn_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(out));
+    SF_CHECK_LAUNCH();
+    return SF_OK;
+  }
+  SF_CHECK_ARG(impl != SF_ATTN_MMA, "the tensor-core tree attention does not support this layout");
   dim3 grid((unsigned)num_kv_heads, (unsigned)((q_len + kRows - 1) / kRows), (unsigned)p.splits);
   const size_t smem = (size_t)(kTile * kD + kTile * kKPitch + kMaxGroup * kRows * kD) * 2;
   static std::atomic<unsigned long long> configured{0};

@@ -23,4 +23,9 @@ struct AttnParams {
   float* part_ml;  // [splits, Hq, Tq, 2] (row max of scaled scores, row sum)
 };
 
+bool tree_attention_mma_supports(const AttnParams& p, int head_dim);
+// Launches the mma.sync split kernel: chooses p.splits / p.keys_per_split,
+// sets p.part_ml, writes the split partials.
+int tree_attention_mma(AttnParams& p, cudaStream_t stream);
+
 }  // namespace sf

@@ -275,7 +275,7 @@ def test_combine_bit_exact_sequential(ops):
 # --------------------------------------------------------- K6 tree attention
 
 
-@pytest.mark.parametrize("impl", [1])
+@pytest.mark.parametrize("impl", [1, 2])
 @pytest.mark.parametrize("nodes,depth,ctx", [(4, 2, 2), (64, 6, 512), (128, 8, 300), (60, 8, 2048), (0, 0, 33),
                                              (200, 9, 700)])
 def test_tree_attention_vs_oracle(ops, nodes, depth, ctx, impl):
@@ -301,7 +301,7 @@ def test_tree_attention_vs_oracle(ops, nodes, depth, ctx, impl):
     assert torch.equal(packed, bits)
 
 
-@pytest.mark.parametrize("impl", [1])
+@pytest.mark.parametrize("impl", [1, 2])
 def test_tree_attention_strided_views(ops, impl):
     """Inputs as HF lays them out: q from a [1, T, Hq*D] projection viewed as
     [Hq, T, D] (non-contiguous), K/V cache [Hkv, Tk, D]."""
@@ -329,7 +329,9 @@ def test_tree_attention_full_mask_and_long_context(ops):
     mask = torch.rand(tq, tk, generator=gen) < 0.3
     mask[:, 0] = True
     bits = ops.tree_bits_from_mask(mask.to(DEV), 0)
-    a = ops.tree_attention(q, k, v, bits, 0).float().cpu().numpy()
+    a = ops.tree_attention(q, k, v, bits, 0, impl=2).float().cpu().numpy()
+    b = ops.tree_attention(q, k, v, bits, 0, impl=1).float().cpu().numpy()
+    assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= COS_MIN
     sub = slice(0, 8)  # oracle on the 8 query heads of KV head 0 (fp64, CPU)
     ref = to.tree_attention(q[sub].float().cpu().numpy(), k[:1].float().cpu().numpy(),
                             v[:1].float().cpu().numpy(), mask.numpy())
