@@ -68,8 +68,9 @@ def parse_args(argv=None):
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
-    p.add_argument("--mode", choices=("verify", "block"), default="verify",
-                   help="block: the MoE verify block alone on one resident layer (kernel profiling)")
+    p.add_argument("--mode", choices=("verify", "block", "graph"), default="verify",
+                   help="block: the MoE verify block alone on one resident layer; graph: only the "
+                        "resident (128-slot) verify pass replayed from a CUDA graph")
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
     p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
                    help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
@@ -640,12 +641,39 @@ def block_mode(args):
                       "frac_of_hbm_peak": round(algo / us / 1e3 / peaks["hbm_gbs"], 4)}), flush=True)
 
 
+def graph_mode(args):
+    """Resident verify pass only: every expert in HBM (128 slots per layer),
+    one CUDA graph per pass, ``--steps`` replays inside the NVTX range
+    "timed" (kernel profiling of the verify pass)."""
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
+    from specfit_b200.runtime.verify_graph import VerifyGraph
+
+    device = torch.device("cuda", 0)
+    cfg = qwen3_moe_config(args.layers)
+    loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=cfg.num_experts, config=cfg,
+                                          seed=args.seed)
+    loaded.warm_all_caches()
+    gen = torch.Generator().manual_seed(1)
+    ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
+    tree = make_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
+    seed_tok = int(torch.randint(0, cfg.vocab_size, (1,), generator=gen))
+    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device)
+    vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device)
+    vg.capture(runner.d_ids, runner.d_mask, runner.d_pos)
+    ms, _ = timed_steps(vg.replay, args.steps, args.warmup, 1, device)
+    print(json.dumps({"mode": "graph", "layers": args.layers, "ms_per_pass": round(ms / args.steps, 3),
+                      "verify_tokens": 1 + args.nodes}), flush=True)
+    loaded.close()
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         reference_arm(args)
     elif args.mode == "block":
         block_mode(args)
+    elif args.mode == "graph":
+        graph_mode(args)
     else:
         b200_arm(args)
 

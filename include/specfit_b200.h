@@ -18,6 +18,7 @@
  *   sf_slot_fill_batch    slot.tensor.copy_(source)             src/specfit/runtime/gpu_expert_cache.py:556-561
  *   sf_tree_attention     SDPA under the tree mask              transformers/...:156-195 with the mask of
  *                                                               src/specfit/runtime/eagle3_types.py:450-473
+ *   sf_specfit_select     exact_specfit_selection               src/specfit/specfit_exact.py:58-94
  */
 #ifndef SPECFIT_B200_H_
 #define SPECFIT_B200_H_
@@ -216,6 +217,43 @@ SF_API int sf_tree_attention_ex(const void* q, const void* k, const void* v, con
                                 int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
                                 float scale, void* out, void* workspace, size_t workspace_bytes,
                                 int impl, void* stream);
+
+/*
+ * SpecFit exact subtree selection (host function, runs on the calling CPU
+ * thread; no GPU work).  Nodes are raw ids 1..num_nodes with parents[raw-1]
+ * < raw (0 = the verification seed) and cumulative log-probabilities
+ * cum_logp[raw-1].  footprints holds (num_nodes + 1) bitsets of `words`
+ * uint64 words (raw 0 = the seed): bit 128*layer + expert set for every
+ * routed (layer, expert) of that token.  resident (nullable, `words` words)
+ * marks cache-resident pairs.  Among all ancestor-closed subsets S with
+ * |S| <= max_nodes, maximises
+ *   (1 + sum_{i in S} exp(cum_logp_i)) /
+ *   (size_intercept_ns[|S|] + expert_ns*|F| + missing_ns*|F \ resident|)
+ * with F the union of the seed's and S's footprints (resident == NULL: every
+ * pair is missing), ties broken by the smallest (-reward, |F|, |S|, ids); the
+ * reward is summed with compensated (Neumaier) summation in id order.
+ * Writes the ids (increasing) to selected[0..*num_selected) and the score.
+ * Replaces exact_specfit_selection / _score_packed_routes
+ * (src/specfit/specfit_exact.py:58-94, topology of
+ * src/specfit/cache_selection_diagnostic.py:20-39), without the reference's
+ * restriction to pools of 2/6/10/14/18 nodes (num_nodes <= 63).
+ */
+SF_API int sf_specfit_select(int num_nodes, const int32_t* parents, const double* cum_logp,
+                             const uint64_t* footprints, int words, const uint64_t* resident,
+                             const double* size_intercept_ns, int max_nodes, double expert_ns,
+                             double missing_ns, int32_t* selected, int32_t* num_selected,
+                             double* best_score);
+
+/* Packs routes int32 [tokens][layers][top_k] into footprint bitsets
+ * [tokens][words] (bit layer*experts + expert); SF_ERR_INVALID_ARGUMENT on an
+ * expert id outside [0, experts) or a repeated id within a (token, layer).
+ * The packing of _pack_routes (src/specfit/specfit_exact.py:18-49). */
+SF_API int sf_specfit_pack_routes(const int32_t* routes, int tokens, int layers, int top_k,
+                                  int experts, uint64_t* footprints, int words);
+
+/* Compensated (Neumaier) left-to-right sum of n doubles, the summation the
+ * selection's reward uses (Python's builtin sum over floats). */
+SF_API double sf_compensated_sum(const double* values, int n);
 
 #ifdef __cplusplus
 }

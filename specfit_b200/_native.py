@@ -61,6 +61,10 @@ SIGNATURES = {
     "sf_moe_combine": (_i32, [_vp, _i32, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp]),
     "sf_slot_fill_batch": (_i32, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
                                   _i32, _vp]),
+    "sf_specfit_select": (_i32, [_i32, _vp, _vp, _vp, _i32, _vp, _vp, _i32, ctypes.c_double,
+                                 ctypes.c_double, _vp, _vp, _vp]),
+    "sf_compensated_sum": (ctypes.c_double, [_vp, _i32]),
+    "sf_specfit_pack_routes": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _i32]),
     "sf_tree_attention_workspace_bytes": (_sz, [_i32, _i64, _i64]),
     "sf_tree_attention": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i32, _i32,
                                  _i64, _i64, _i64, _i64, _f32, _vp, _vp, _sz, _vp]),

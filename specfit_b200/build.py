@@ -51,7 +51,8 @@ def _headers_mtime() -> float:
 
 
 def _compile(src: Path, obj: Path, verbose: bool) -> None:
-    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+    extra = ["-Xcompiler", "-mpopcnt"] if src.suffix == ".cpp" else []
+    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
@@ -65,7 +66,7 @@ def _compile(src: Path, obj: Path, verbose: bool) -> None:
 def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile (incrementally) and link the library; returns its path."""
     BUILD.mkdir(exist_ok=True)
-    sources = sorted(CSRC.glob("*.cu"))
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     hdr_time = _headers_mtime()
     jobs = []
     objs = []

@@ -132,3 +132,61 @@ def random_tree(num_nodes: int, max_depth: int, max_branch: int, seed: int, voca
         node_depth[node] = node_depth[parent] + 1
         sibling_tokens[node] = set()
     return tuple(tokens), tuple(parents), tuple(depths)
+
+
+# Natural-cache coefficients of the reference's frozen A100 selection model
+# (per node count 0..7, ns; and ns per distinct (layer, expert) in the
+# verification footprint), used as realistic synthetic cost models.
+SELECTION_INTERCEPT_NS = (142213640.2719444, 147532305.64501184, 150522238.9747455,
+                          152268786.28951707, 152742629.59439692, 163203998.73306817,
+                          155175323.9989069, 156067696.05019823)
+SELECTION_EXPERT_NS = 210715.51267433458
+
+
+@dataclass(frozen=True)
+class SelectionCase:
+    parents: tuple      # parent raw id of raw = 1..n (0 = the seed)
+    depths: tuple
+    cum_logp: tuple     # cumulative log-probability of raw = 1..n
+    routes: np.ndarray  # int64 [n + 1, 48, 8]: top-8 experts of raw 0..n per layer
+    resident: np.ndarray  # bool [48, 128]
+
+
+def selection_case(seed: int, nodes: int, *, shared_routes: bool = False, level_prob=None,
+                   resident_frac: float = 0.3) -> SelectionCase:
+    """A top-2 draft pool like the reference's (2 nodes at depth 1, then 4 per
+    level whose parents are 2 distinct nodes of the previous level), random
+    conditional probabilities (or ``level_prob`` = (p_odd_raw, p_even_raw)),
+    per-(raw, layer) top-8 routes of distinct experts (or experts 0..7 for
+    every raw when ``shared_routes``), and a random resident set (at most 48
+    experts per layer)."""
+    rng = np.random.default_rng(seed)
+    parents, depths = [0, 0], [1, 1]
+    prev = [1, 2]
+    while len(parents) < nodes:
+        chosen = sorted(rng.choice(prev, size=2, replace=False).tolist())
+        level = []
+        for par in chosen:
+            for _ in range(2):
+                parents.append(int(par))
+                depths.append(depths[par - 1] + 1)
+                level.append(len(parents))
+        prev = level
+    parents, depths = parents[:nodes], depths[:nodes]
+    cum = []
+    for raw, par in enumerate(parents, start=1):
+        if level_prob is None:
+            cond = float(np.log(rng.uniform(0.05, 0.95)))
+        else:
+            cond = float(np.log(level_prob[0] if raw % 2 else level_prob[1]))
+        cum.append((0.0 if par == 0 else cum[par - 1]) + cond)
+    if shared_routes:
+        routes = np.broadcast_to(np.arange(8), (nodes + 1, 48, 8)).copy()
+    else:
+        routes = np.stack([np.stack([rng.permutation(128)[:8] for _ in range(48)])
+                           for _ in range(nodes + 1)])
+    resident = np.zeros((48, 128), dtype=bool)
+    for layer in range(48):
+        count = int(min(48, rng.binomial(128, resident_frac)))
+        resident[layer, rng.permutation(128)[:count]] = True
+    return SelectionCase(tuple(parents), tuple(depths), tuple(cum), routes.astype(np.int64), resident)

@@ -282,6 +282,88 @@ def make_tree(out: Path):
     np.savez_compressed(out / "tree.npz", **res)
 
 
+def make_selection(out: Path):
+    """SpecFit exact selection (src/specfit/specfit_exact.py:58-94) and the
+    adaptive-depth rule of LevelSpecFit (src/specfit/main_comparison.py:63-103)
+    on seeded pools; inputs are regenerated from the stored parameters by
+    specfit_b200.synthetic.selection_case."""
+    import json
+    from types import SimpleNamespace
+
+    from specfit.main_comparison import LevelSpecFit
+    from specfit.selection_methods import SelectionCostModel, probability_ids
+    from specfit.selection_refinement import CacheCostModel
+    from specfit.specfit_exact import exact_specfit_selection
+
+    def objects(case):
+        n = len(case.parents)
+        nodes = [SimpleNamespace(raw_id=i + 1, parent_raw_id=case.parents[i], depth=case.depths[i],
+                                 generation_ordinal=i,
+                                 cumulative_log_probability=case.cum_logp[i]) for i in range(n)]
+        pool = SimpleNamespace(nodes=nodes)
+        atlas = SimpleNamespace(position_to_raw=tuple(range(n + 1)), expert_ids_by_raw_layer=tuple(
+            (raw, layer, tuple(int(e) for e in case.routes[raw, layer]))
+            for raw in range(n + 1) for layer in range(48)))
+        atlas48 = [tuple(tuple(int(e) for e in case.routes[raw, layer]) for raw in range(n + 1))
+                   for layer in range(48)]
+        resident = 0
+        for layer in range(48):
+            for e in np.nonzero(case.resident[layer])[0]:
+                resident |= 1 << (128 * layer + int(e))
+        return pool, atlas, atlas48, resident
+
+    B, beta = synthetic.SELECTION_INTERCEPT_NS, synthetic.SELECTION_EXPERT_NS
+    models = {
+        "natural": dict(kind="selection", intercept=list(B), expert_ns=beta, missing_ns=0.0),
+        "cache": dict(kind="cache", intercept=list(B), expert_ns=beta, missing_ns=0.9 * beta),
+        "flat": dict(kind="selection", intercept=[1.0] * 8, expert_ns=1.0, missing_ns=0.0),
+        "steep": dict(kind="selection", intercept=[1.0] + [1e12] * 7, expert_ns=1.0, missing_ns=0.0),
+    }
+
+    def build(m):
+        if m["kind"] == "cache":
+            return CacheCostModel(tuple(m["intercept"]), m["expert_ns"], m["missing_ns"])
+        return SelectionCostModel(tuple(m["intercept"]), tuple(m["intercept"]), m["expert_ns"])
+
+    cases = []
+    for n in (2, 6, 10, 14, 18):
+        for seed in range(8):
+            for name in ("natural", "cache"):
+                cases.append(dict(seed=seed, n=n, shared=False, level_prob=None, model=models[name],
+                                  resident=name == "cache"))
+    for seed in range(3):
+        for name in ("natural", "flat", "steep", "cache"):
+            cases.append(dict(seed=100 + seed, n=18, shared=True, level_prob=None, model=models[name],
+                              resident=name == "cache"))
+    # The reference's compensated-summation tie case (tests/unit/
+    # test_selection_refinement.py:65-78): equal footprints, intercepts equal
+    # to the probability-ranked rewards.
+    kat = synthetic.selection_case(7, 18, shared_routes=True,
+                                   level_prob=(0.47454250539060727, 0.35255387827663837))
+    kpool, _, _, _ = objects(kat)
+    probs = {nd.raw_id: math.exp(nd.cumulative_log_probability) for nd in kpool.nodes}
+    offsets = [1.0 + sum((probs[i] for i in probability_ids(kpool, k)), start=0.0) for k in range(8)]
+    cases.append(dict(seed=7, n=18, shared=True, level_prob=[0.47454250539060727, 0.35255387827663837],
+                      model=dict(kind="selection", intercept=offsets, expert_ns=0.0, missing_ns=0.0),
+                      resident=False))
+    for c in cases:
+        case = synthetic.selection_case(c["seed"], c["n"], shared_routes=c["shared"],
+                                        level_prob=c["level_prob"])
+        pool, atlas, atlas48, resident = objects(case)
+        model = build(c["model"])
+        c["selected"] = list(exact_specfit_selection(pool, atlas, model,
+                                                     resident if c["resident"] else 0))
+        if c["model"]["kind"] == "selection":
+            level = LevelSpecFit(model, atlas48)
+            stops = []
+            for prefix in range(2, c["n"] + 1, 4):
+                stop, ids = level.stop(pool.nodes[:prefix])
+                stops.append([prefix, bool(stop), list(ids)])
+            c["stops"] = stops
+    (out / "selection.json").write_text(json.dumps(cases))
+    print("selection cases", len(cases), "kat selection", cases[-1]["selected"])
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=os.environ.get("SPECFIT_REFERENCE", ""),
@@ -303,6 +385,7 @@ def main():
         "dispatch": lambda: make_dispatch(out),
         "kats": lambda: make_expert_kats(ref, out),
         "tree": lambda: make_tree(out),
+        "selection": lambda: make_selection(out),
     }
     for name, job in jobs.items():
         if args.only and name not in args.only.split(","):
