@@ -19,6 +19,7 @@
  *   sf_tree_attention     SDPA under the tree mask              transformers/...:156-195 with the mask of
  *                                                               src/specfit/runtime/eagle3_types.py:450-473
  *   sf_specfit_select     exact_specfit_selection               src/specfit/specfit_exact.py:58-94
+ *   sf_ep_*               (none: the reference is single-GPU, scripts/run_specfit_main_comparison.py:465)
  */
 #ifndef SPECFIT_B200_H_
 #define SPECFIT_B200_H_
@@ -254,6 +255,55 @@ SF_API int sf_specfit_pack_routes(const int32_t* routes, int tokens, int layers,
 /* Compensated (Neumaier) left-to-right sum of n doubles, the summation the
  * selection's reward uses (Python's builtin sum over floats). */
 SF_API double sf_compensated_sum(const double* values, int n);
+
+/*
+ * Expert parallelism of the MoE block over `world` GPUs (no counterpart in
+ * the reference, which refuses more than one GPU).  Rank r owns experts
+ * [r*E/world, (r+1)*E/world).  A token travels at most once to each rank it
+ * has routes on, as one row of sf_ep_row_bytes() bytes:
+ *   [hidden (H elements of dtype) | int32 local_ids[K] | float weights[K] | pad]
+ * local_ids ascending, -1 padded (weights 0 padded).  Per layer:
+ *   source:      sf_ep_send_pack     -> rows grouped by destination rank, then token;
+ *                send_counts[2d] = rows (pairs) and [2d+1] = routes for rank d
+ *   exchange:    all-to-all of the rows (split by pairs per rank)
+ *   destination: sf_ep_recv_group    -> stable grouping by local expert
+ *                sf_ep_recv_gather   -> sorted hidden rows + weights
+ *                sf_grouped_swiglu   (local experts)
+ *                sf_ep_return_pack   -> one output row per received route, in
+ *                                       (pair, slot) order
+ *   exchange:    all-to-all back (split by routes per rank)
+ *   source:      sf_moe_combine with inv_pos = route_row
+ * With sources in rank order the per-expert groups and the combine order are
+ * those of one GPU, so the result is bit-identical to the one-GPU block.
+ */
+/* Row size in bytes (a multiple of 16), or -1 for an unsupported dtype. */
+SF_API int64_t sf_ep_row_bytes(int dtype, int hidden_size, int top_k);
+/* send_rows: [tokens*world, row_bytes] capacity; send_counts: int64 [2*world];
+ * route_row: int32 [tokens*top_k], the row of each route's output in the
+ * returned buffer (-1 for an invalid route, which also sets *error_flag);
+ * pair_token: int32 [tokens*world] workspace.  top_k <= 16, world <= 32. */
+SF_API int sf_ep_send_pack(const void* hidden, int dtype, int64_t tokens, int hidden_size,
+                           const int64_t* topk_index, const void* topk_weights, int weight_dtype,
+                           int top_k, int num_experts, int world, void* send_rows,
+                           int64_t row_bytes, int64_t* send_counts, int32_t* route_row,
+                           int32_t* pair_token, int32_t* error_flag, void* stream);
+/* Groups the pairs*top_k received route slots by local expert (slots with
+ * id -1 are padding).  Outputs as sf_moe_dispatch over local_experts, plus
+ * return_src[q] = sorted row of the q-th valid slot in (pair, slot) order. */
+SF_API int sf_ep_recv_group(const void* recv_rows, int64_t row_bytes, int dtype, int64_t pairs,
+                            int hidden_size, int top_k, int local_experts, int32_t* counts,
+                            int32_t* offsets, int32_t* sorted_pos, int32_t* inv_pos,
+                            int32_t* active, int32_t* num_active, int32_t* return_src,
+                            int32_t* error_flag, void* stream);
+/* hidden_sorted[i] = hidden of pair sorted_pos[i] / top_k, weights_sorted[i]
+ * = its weight at slot sorted_pos[i] % top_k, for i < routes. */
+SF_API int sf_ep_recv_gather(const void* recv_rows, int64_t row_bytes, int dtype, int hidden_size,
+                             int top_k, const int32_t* sorted_pos, int64_t routes,
+                             void* hidden_sorted, float* weights_sorted, void* stream);
+/* return_rows[q] = out_sorted[return_src[q]] for q < routes. */
+SF_API int sf_ep_return_pack(const void* out_sorted, int dtype, int hidden_size,
+                             const int32_t* return_src, int64_t routes, void* return_rows,
+                             void* stream);
 
 #ifdef __cplusplus
 }

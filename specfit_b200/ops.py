@@ -302,3 +302,130 @@ def tree_bits_from_mask(mask: torch.Tensor, prefix_len: int) -> torch.Tensor:
     packed = (tree << shifts).sum(-1)
     packed = torch.where(packed >= (1 << 31), packed - (1 << 32), packed)
     return packed.to(torch.int32)
+
+
+# ---------------------------------------------------------------------------
+# K7 expert parallelism (dispatch / return rows of the all-to-all exchange)
+
+
+def ep_row_bytes(dtype: torch.dtype, hidden_size: int, top_k: int) -> int:
+    """Bytes of one exchanged row: hidden, K local expert ids, K weights."""
+    n = N.lib.sf_ep_row_bytes(dtype_code(dtype), hidden_size, top_k)
+    if n < 0:
+        raise ValueError("unsupported expert-parallel row shape")
+    return int(n)
+
+
+@dataclass
+class EpSend:
+    rows: torch.Tensor  # uint8 [tokens*world, row_bytes] (the first sum(pairs) rows are used)
+    counts: torch.Tensor  # int64 [world, 2]: (pairs, routes) per destination rank
+    route_row: torch.Tensor  # int32 [tokens*top_k]: row of each route's output on return
+    error: torch.Tensor  # int32 [1]
+    tokens: int
+    top_k: int
+    num_experts: int
+    world: int
+
+
+def ep_send_pack(hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor,
+                 num_experts: int, world: int) -> EpSend:
+    """Rows to send to each rank (grouped by rank, then token) and the plan."""
+    dev = _require_cuda(hidden, top_k_index, top_k_weights)
+    if top_k_index.dtype != torch.int64 or top_k_index.ndim != 2:
+        raise ValueError("top_k_index must be int64 [tokens, top_k]")
+    h = hidden.contiguous()
+    idx = top_k_index.contiguous()
+    w = top_k_weights.contiguous()
+    tokens, top_k = idx.shape
+    rb = ep_row_bytes(h.dtype, h.shape[1], top_k)
+    rows = torch.empty(max(tokens * world, 1), rb, dtype=torch.uint8, device=dev)
+    i32 = torch.empty(tokens * top_k + tokens * world + 1, dtype=torch.int32, device=dev)
+    route_row = i32[: tokens * top_k]
+    pair_token = i32[tokens * top_k: tokens * top_k + tokens * world]
+    error = i32[tokens * top_k + tokens * world:]
+    error.zero_()
+    counts = torch.empty(world, 2, dtype=torch.int64, device=dev)
+    N.check(N.lib.sf_ep_send_pack(h.data_ptr(), dtype_code(h.dtype), tokens, h.shape[1],
+                                  idx.data_ptr(), w.data_ptr(), dtype_code(w.dtype), top_k,
+                                  num_experts, world, rows.data_ptr(), rb, counts.data_ptr(),
+                                  route_row.data_ptr(), pair_token.data_ptr(), error.data_ptr(),
+                                  _stream(dev)), "sf_ep_send_pack")
+    _launched(1 if tokens == 0 else 2)
+    return EpSend(rows, counts, route_row, error, tokens, top_k, num_experts, world)
+
+
+def ep_recv_group(recv_rows: torch.Tensor, pairs: int, hidden_size: int, top_k: int,
+                  local_experts: int, dtype: torch.dtype):
+    """Groups the received route slots by local expert.  Returns the
+    ``Dispatch`` over the local experts (``tokens`` = pairs) and
+    ``return_src`` (int32 [pairs*top_k]; its first ``routes`` entries name
+    the sorted row of each valid slot in (pair, slot) order)."""
+    dev = _require_cuda(recv_rows)
+    rb = ep_row_bytes(dtype, hidden_size, top_k)
+    if recv_rows.dtype != torch.uint8 or recv_rows.shape[0] < pairs or recv_rows.shape[-1] != rb:
+        raise ValueError("recv_rows must be uint8 [>= pairs, row_bytes]")
+    n = pairs * top_k
+    E = local_experts
+    i32 = dict(dtype=torch.int32, device=dev)
+    buf = torch.empty(E + (E + 1) + 3 * n + E + 2, **i32)
+    counts = buf[:E]
+    offsets = buf[E: 2 * E + 1]
+    sorted_pos = buf[2 * E + 1: 2 * E + 1 + n]
+    inv_pos = buf[2 * E + 1 + n: 2 * E + 1 + 2 * n]
+    return_src = buf[2 * E + 1 + 2 * n: 2 * E + 1 + 3 * n]
+    active = buf[2 * E + 1 + 3 * n: 3 * E + 1 + 3 * n]
+    num_active = buf[3 * E + 1 + 3 * n: 3 * E + 2 + 3 * n]
+    error = buf[3 * E + 2 + 3 * n:]
+    error.zero_()
+    N.check(N.lib.sf_ep_recv_group(recv_rows.data_ptr(), rb, dtype_code(dtype), pairs, hidden_size,
+                                   top_k, E, counts.data_ptr(), offsets.data_ptr(),
+                                   sorted_pos.data_ptr(), inv_pos.data_ptr(), active.data_ptr(),
+                                   num_active.data_ptr(), return_src.data_ptr(), error.data_ptr(),
+                                   _stream(dev)), "sf_ep_recv_group")
+    _launched(1)
+    d = Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, error, pairs, top_k, E)
+    return d, return_src
+
+
+def ep_recv_gather(recv_rows: torch.Tensor, d: Dispatch, hidden_size: int, dtype: torch.dtype,
+                   routes: int):
+    """Sorted hidden rows ``[routes, H]`` and their routing weights (fp32)."""
+    dev = _require_cuda(recv_rows)
+    rb = ep_row_bytes(dtype, hidden_size, d.top_k)
+    xs = torch.empty(max(routes, 1), hidden_size, dtype=dtype, device=dev)[:routes]
+    ws = torch.empty(max(routes, 1), dtype=torch.float32, device=dev)[:routes]
+    N.check(N.lib.sf_ep_recv_gather(recv_rows.data_ptr(), rb, dtype_code(dtype), hidden_size,
+                                    d.top_k, d.sorted_pos.data_ptr(), routes, xs.data_ptr(),
+                                    ws.data_ptr(), _stream(dev)), "sf_ep_recv_gather")
+    _launched(1 if routes else 0)
+    return xs, ws
+
+
+def ep_return_pack(out_sorted: torch.Tensor, return_src: torch.Tensor, routes: int) -> torch.Tensor:
+    """One output row per received route, in (pair, slot) order."""
+    dev = _require_cuda(out_sorted, return_src)
+    H = out_sorted.shape[1]
+    rows = torch.empty(max(routes, 1), H, dtype=out_sorted.dtype, device=dev)[:routes]
+    N.check(N.lib.sf_ep_return_pack(out_sorted.data_ptr(), dtype_code(out_sorted.dtype), H,
+                                    return_src.data_ptr(), routes, rows.data_ptr(), _stream(dev)),
+            "sf_ep_return_pack")
+    _launched(1 if routes else 0)
+    return rows
+
+
+def ep_combine(returned: torch.Tensor, send: EpSend, top_k_index: torch.Tensor,
+               reduce: int = N.SF_REDUCE_MODEL_DTYPE, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The single-GPU combine over the returned rows (ascending expert id)."""
+    dev = _require_cuda(top_k_index)
+    H = returned.shape[1]
+    res = out if out is not None else torch.empty(send.tokens, H, dtype=returned.dtype, device=dev)
+    if send.tokens == 0:
+        return res
+    _require_cuda(returned)
+    N.check(N.lib.sf_moe_combine(returned.data_ptr(), dtype_code(returned.dtype),
+                                 send.route_row.data_ptr(), top_k_index.contiguous().data_ptr(),
+                                 None, send.num_experts, send.tokens, send.top_k, H, reduce,
+                                 res.data_ptr(), _stream(dev)), "sf_moe_combine")
+    _launched(1)
+    return res
