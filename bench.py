@@ -68,9 +68,13 @@ def parse_args(argv=None):
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
-    p.add_argument("--mode", choices=("verify", "block", "graph"), default="verify",
-                   help="block: the MoE verify block alone on one resident layer; graph: only the "
+    p.add_argument("--mode", choices=("auto", "verify", "ep", "block", "graph"), default="auto",
+                   help="auto: verify on one GPU, ep under torchrun with N > 1; verify: BASELINE "
+                        "config 2; ep: config 5 (8 requests, experts sharded over the ranks); "
+                        "block: the MoE verify block alone on one resident layer; graph: only the "
                         "resident (128-slot) verify pass replayed from a CUDA graph")
+    p.add_argument("--requests", type=int, default=8, help="--mode ep: concurrent requests in total")
+    p.add_argument("--ep-ctx", type=int, default=4096, help="--mode ep: context tokens per request")
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
     p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
                    help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
@@ -555,6 +559,223 @@ def b200_arm(args):
             pass
 
 
+class EpRunner:
+    """BASELINE configuration 5 on one rank: ``requests / world`` requests
+    with ``ep_ctx``-token contexts, each verifying the same 64-node tree in
+    one batched forward; per-layer routes replaced by seeded Zipf(1.1)
+    routes over the global (request, token) order."""
+
+    def __init__(self, args, loaded, cfg, device, rank, world):
+        from transformers import DynamicCache
+
+        from specfit_b200 import synthetic
+
+        self.model = loaded.model
+        self.device = device
+        self.batch = args.requests // world
+        self.ctx = args.ep_ctx
+        self.tree = make_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
+        q = 1 + self.tree.draft_node_count
+        gen = torch.Generator().manual_seed(1)
+        ctx_all = torch.randint(0, cfg.vocab_size, (args.requests, self.ctx), generator=gen)
+        seeds = torch.randint(0, cfg.vocab_size, (args.requests,), generator=gen)
+        lo, hi = rank * self.batch, (rank + 1) * self.batch
+        self.cache = DynamicCache(config=cfg)
+        with torch.no_grad():
+            self.model(input_ids=ctx_all[lo:hi].to(device), past_key_values=self.cache, use_cache=True,
+                       logits_to_keep=1)
+        torch.cuda.synchronize(device)
+        self.h_ids = torch.cat([self.tree.verification_token_ids(seeds[b].view(1, 1))
+                                for b in range(lo, hi)]).pin_memory()
+        mask = self.tree.verification_attention_mask(base_kv_length=self.ctx, device="cpu")
+        self.h_mask = mask.expand(self.batch, -1, -1, -1).contiguous().pin_memory()
+        pos = self.tree.verification_position_ids(base_kv_length=self.ctx, device="cpu")
+        self.h_pos = pos.expand(self.batch, -1).contiguous().pin_memory()
+        self.d_ids, self.d_mask, self.d_pos = (t.to(device) for t in (self.h_ids, self.h_mask, self.h_pos))
+        # Zipf routes of every layer for the global verify tokens; this rank's rows.
+        self.routes = [torch.from_numpy(synthetic.zipf_routes(args.requests * q, l, args.seed)
+                                        [lo * q:hi * q]).to(device)
+                       for l in range(cfg.num_hidden_layers)]
+        self.override = False
+        self.hooks = [layer.mlp.gate.register_forward_hook(self._route_hook(l))
+                      for l, layer in enumerate(self.model.model.layers)]
+
+    def _route_hook(self, l):
+        def hook(mod, args, out):
+            if self.override:
+                return out[0], out[1], self.routes[l]
+            return None
+        return hook
+
+    def _forward(self, ids, mask, pos):
+        self.override = True
+        try:
+            with torch.no_grad():
+                out = self.model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                                 past_key_values=self.cache, use_cache=True)
+                am = out.logits.argmax(-1)
+        finally:
+            self.override = False
+        self.cache.crop(self.ctx)
+        return am
+
+    def committed(self, am_host) -> int:
+        return sum(len(self.tree.accepted_path(am_host[b:b + 1])) + 1 for b in range(self.batch))
+
+    def step_device(self):
+        return self._forward(self.d_ids, self.d_mask, self.d_pos)
+
+    def step_e2e(self) -> int:
+        ids = self.h_ids.to(self.device, non_blocking=True)
+        mask = self.h_mask.to(self.device, non_blocking=True)
+        pos = self.h_pos.to(self.device, non_blocking=True)
+        return self.committed(self._forward(ids, mask, pos).cpu())
+
+    @property
+    def h2d_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.h_ids, self.h_mask, self.h_pos))
+
+    @property
+    def d2h_bytes(self) -> int:
+        return self.h_ids.numel() * 8
+
+
+def ep_swiglu_roofline(runner, moe, rank, world, device, peaks, iters=20):
+    """The grouped SwiGLU on this rank's experts over the rows it receives in
+    layer 0 of a verify pass (all ranks' tokens routed by the Zipf routes)."""
+    from specfit_b200 import ops
+    from specfit_b200.synthetic import zipf_routes
+
+    q = runner.h_ids.shape[1]
+    T = q * runner.batch * world
+    idx = torch.from_numpy(zipf_routes(T, 0, 0)).to(device)
+    g = torch.Generator(device=device).manual_seed(5)
+    x = torch.randn(T, moe.hidden, generator=g, device=device).to(torch.bfloat16)
+    w = torch.rand(T, idx.shape[1], generator=g, device=device)
+    send = ops.ep_send_pack(x, idx, w, moe.num_experts, world)
+    counts = send.counts.cpu().tolist()
+    lo = sum(c[0] for c in counts[:rank])
+    pairs, routes = counts[rank]
+    rows = send.rows[lo:lo + pairs]
+    d, _ = ops.ep_recv_group(rows, pairs, moe.hidden, moe.top_k, moe.local_experts, torch.bfloat16)
+    xs, ws = ops.ep_recv_gather(rows, d, moe.hidden, torch.bfloat16, routes)
+    act = torch.empty(max(routes, 1), moe.inter, dtype=torch.bfloat16, device=device)
+    ys = torch.empty(max(routes, 1), moe.hidden, dtype=torch.bfloat16, device=device)
+    run = lambda: ops.grouped_swiglu(xs, ws, d, moe.slot, moe.storage, moe.hidden, moe.inter,
+                                     act_workspace=act, out=ys[:routes])
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        run()
+    e.record()
+    torch.cuda.synchronize(device)
+    us = s.elapsed_time(e) * 1e3 / iters
+    uniq = int(d.num_active.item())
+    algo = uniq * EXPERT_BYTES + routes * moe.hidden * 2 * 2 + routes * moe.inter * 2 * 2 + routes * 4
+    achieved = algo / (us * 1e-6) / 1e9
+    return {"bound": "hbm", "kernel": "swiglu_tc_kernel (phase 1 + 2)", "achieved": round(achieved, 1),
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "traffic": None, "launch_us": round(us, 2), "experts": uniq, "rows": routes,
+            "algorithmic_bytes": algo, "peak_source": peaks["source"] + " hbm_gbs (burst copy)",
+            "rank": rank}
+
+
+def ep_arm(args):
+    """expert-parallel verify over the ranks."""
+    rank, world, local = dist_info()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if args.requests % world:
+        raise SystemExit("--requests must be a multiple of the number of GPUs")
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    from specfit_b200 import ops
+    from specfit_b200.runtime.ep_verifier import build_random_ep_qwen3
+    from specfit_b200.runtime.qwen3_verifier import qwen3_moe_config
+
+    peaks = measured_peaks()
+    cfg = qwen3_moe_config(args.layers)
+    t0 = time.perf_counter()
+    loaded = build_random_ep_qwen3(device=device, rank=rank, world=world, config=cfg, seed=args.seed)
+    runner = EpRunner(args, loaded, cfg, device, rank, world)
+    setup_s = time.perf_counter() - t0
+
+    launches0 = ops.LAUNCHES[0]
+    with ClockSampler(device.index) as clocks:
+        ms, ams = timed_steps(runner.step_device, args.steps, args.warmup, world, device)
+    launches = (ops.LAUNCHES[0] - launches0) // (args.steps + args.warmup) * args.steps
+    committed = sum(runner.committed(a.cpu()) for a in ams)
+    value = sum_over_ranks(committed, world, device) / (ms / 1e3)
+    e2e_ms, e2e_comm = timed_steps(runner.step_e2e, args.steps, 1, world, device)
+    e2e_value = sum_over_ranks(sum(e2e_comm), world, device) / (e2e_ms / 1e3)
+
+    moes = [layer.mlp.experts.moe for layer in loaded.model.model.layers]
+    times, _ = moe_block_profile(runner)
+    plans = [m.last_plan for m in moes]
+    row_bytes = ops.ep_row_bytes(torch.bfloat16, cfg.hidden_size, cfg.num_experts_per_tok)
+    sent = [sum(p.send_pairs) * row_bytes + sum(p.send_routes) * cfg.hidden_size * 2 for p in plans]
+    local_rows = statistics.median([sum(p.recv_routes) for p in plans])
+    block_us = statistics.median(times) * 1e3
+    block_us_max = max_over_ranks(block_us, world, device)
+    q = 1 + runner.tree.draft_node_count
+    result = {
+        "metric": "committed tokens/s (Qwen3-30B-A3B shape, 8 requests, expert-parallel)",
+        "value": round(value, 3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random context tokens, seeded "
+                "64-node tree, seeded Zipf(1.1) routes per layer)",
+        "config": {
+            "workload": (f"BASELINE config 5: {args.layers}-layer Qwen3-30B-A3B-shaped verify over "
+                         f"{args.requests} concurrent requests x {args.nodes}-node tree ({args.requests * q} "
+                         f"verify tokens per step), {args.ep_ctx}-token context each, Zipf(1.1) routes, "
+                         f"{cfg.num_experts} experts sharded over {world} GPU(s) "
+                         f"({cfg.num_experts // world} resident per GPU per layer), dispatch/return as "
+                         "NCCL all-to-all"),
+            "requests_per_gpu": runner.batch,
+            "verify_tokens_per_step": args.requests * q,
+            "parallelism": f"ep{world}, attention data-parallel over requests",
+            "l2_flush": (f"not needed: each step reads {args.layers * cfg.num_experts // world} resident "
+                         f"experts ({args.layers * cfg.num_experts // world * EXPERT_BYTES / 1e9:.1f} GB) "
+                         "per GPU, >> 126 MB L2"),
+        },
+        "gpu_launches": int(launches),
+        "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s",
+                "h2d_bytes_per_step": runner.h2d_bytes, "d2h_bytes_per_step": runner.d2h_bytes,
+                "ms_per_step": round(e2e_ms / args.steps, 3)},
+        "clocks": clocks.summary(),
+        "moe_block": {
+            "us_per_layer_median_max_over_ranks": round(block_us_max, 1),
+            "rows_per_rank_median": local_rows,
+            "nvlink_bytes_sent_per_layer_rank0": int(statistics.median(sent)),
+            "note": "CUDA events around each layer.mlp (router, send pack, 3 all-to-alls with one host "
+                    "sync for the counts, receive grouping, grouped SwiGLU, return, combine)",
+        },
+        "roofline": ep_swiglu_roofline(runner, moes[0], rank, world, device, peaks),
+        "setup_s": round(setup_s, 1),
+    }
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def reference_arm(args):
     rank, world, local = dist_info()
     if rank != 0:
@@ -674,6 +895,8 @@ def main(argv=None):
         block_mode(args)
     elif args.mode == "graph":
         graph_mode(args)
+    elif args.mode == "ep" or (args.mode == "auto" and dist_info()[1] > 1):
+        ep_arm(args)
     else:
         b200_arm(args)
 

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the kernels use:
-// mbarriers, TMA tile loads (no multicast), and tcgen05 (TMEM alloc, UMMA,
+// mbarriers, TMA tile loads (each CTA loads its own tiles), and tcgen05 (TMEM alloc, UMMA,
 // commit, TMEM loads).  Every wait is bounded: it gives up after a fixed
 // number of polls and reports failure, so a kernel can record an error and
 // return instead of spinning forever.

@@ -22,7 +22,7 @@
 // overlap the MMAs of the next.  At these sizes the kernel streams expert
 // weights: every weight byte is read from HBM exactly once per layer.
 //
-// No TMA multicast is used anywhere in this file.
+// Every TMA load here is issued by one CTA for its own shared memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

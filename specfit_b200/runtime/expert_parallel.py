@@ -78,6 +78,7 @@ class ExpertParallelMoE:
         self.inter = intermediate_size
         self.storage = local_storage
         self.slot = torch.arange(self.local_experts, dtype=torch.int32, device=local_storage.device)
+        self.last_plan: RecvPlan | None = None  # split sizes of the latest forward (host ints)
 
     @classmethod
     def from_process_group(cls, group=None, **kw) -> "ExpertParallelMoE":
@@ -107,10 +108,15 @@ class ExpertParallelMoE:
 
     def forward(self, hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor):
         send = self.send(hidden, top_k_index, top_k_weights)
+        if self.world == 1:  # the exchange with oneself is the identity
+            counts = send.counts.cpu()
+            plan = self.last_plan = plan_from_counts(counts, counts)
+            out_rows = self.compute(send.rows, plan.send_pairs[0], plan.send_routes[0], hidden.dtype)
+            return self.combine(out_rows, send, top_k_index)
         recv_counts = torch.empty_like(send.counts)
         dist.all_to_all_single(recv_counts, send.counts, group=self.group)
         both = torch.stack((send.counts, recv_counts)).cpu()  # the one host sync per layer
-        plan = plan_from_counts(both[0], both[1])
+        plan = self.last_plan = plan_from_counts(both[0], both[1])
         recv_rows = all_to_all_rows(send.rows, plan.send_pairs, plan.recv_pairs, self.group)
         out_rows = self.compute(recv_rows, sum(plan.recv_pairs), sum(plan.recv_routes), hidden.dtype)
         returned = all_to_all_rows(out_rows, plan.recv_routes, plan.send_routes, self.group)

@@ -161,6 +161,26 @@ def _init_layer_(module: torch.nn.Module, gen: torch.Generator, std: float) -> N
             p.data.normal_(0.0, std, generator=gen)
 
 
+def materialize_random_(model, cfg, device, seed: int, std: float, dtype) -> None:
+    """Allocate a meta-built model on ``device`` and draw its non-expert
+    weights: layer l from a generator seeded ``seed + l``, embeddings and
+    lm_head from ``seed + layers`` and ``seed + layers + 1``; norms are 1."""
+    model.to_empty(device=device)
+    with torch.no_grad():
+        for l, layer in enumerate(model.model.layers):
+            _init_layer_(layer, torch.Generator(device=device).manual_seed(seed + l), std)
+        g = torch.Generator(device=device).manual_seed(seed + cfg.num_hidden_layers)
+        model.model.embed_tokens.weight.normal_(0.0, std, generator=g)
+        model.model.norm.weight.fill_(1.0)
+        g = torch.Generator(device=device).manual_seed(seed + cfg.num_hidden_layers + 1)
+        model.lm_head.weight.normal_(0.0, std, generator=g)
+    model.to(dtype)
+    # RoPE frequencies stay fp32 (rebuilt after the dtype cast), as a model
+    # loaded in bf16 keeps them.
+    model.model.rotary_emb = type(model.model.rotary_emb)(config=cfg, device=device)
+    model.eval()
+
+
 def build_random_offloaded_qwen3(*, device, slots_per_layer: int, num_layers: int = synthetic.NUM_LAYERS,
                                  seed: int = 0, dtype=torch.bfloat16, config=None,
                                  pool: ExpertHostPool | None = None,
@@ -196,18 +216,5 @@ def build_random_offloaded_qwen3(*, device, slots_per_layer: int, num_layers: in
                                    cfg.norm_topk_prob, device="meta")
         layer.mlp = Qwen3B200SparseMoeBlock(gate, experts)
         caches.append(cache)
-    model.to_empty(device=device)
-    with torch.no_grad():
-        for l, layer in enumerate(model.model.layers):
-            _init_layer_(layer, torch.Generator(device=device).manual_seed(seed + l), std)
-        g = torch.Generator(device=device).manual_seed(seed + cfg.num_hidden_layers)
-        model.model.embed_tokens.weight.normal_(0.0, std, generator=g)
-        model.model.norm.weight.fill_(1.0)
-        g = torch.Generator(device=device).manual_seed(seed + cfg.num_hidden_layers + 1)
-        model.lm_head.weight.normal_(0.0, std, generator=g)
-    model.to(dtype)
-    # RoPE frequencies stay fp32 (rebuilt after the dtype cast), as a model
-    # loaded in bf16 keeps them.
-    model.model.rotary_emb = type(model.model.rotary_emb)(config=cfg, device=device)
-    model.eval()
+    materialize_random_(model, cfg, device, seed, std, dtype)
     return LoadedB200Qwen3(model, tuple(caches), pool)

@@ -153,3 +153,27 @@ def test_nccl_two_ranks_equal_single_gpu():
 
     mp.start_processes(ep_ranks.nccl_rank, args=(2, _free_port(), 21, [65, 40]), nprocs=2, join=True,
                        start_method="spawn")
+
+
+def test_one_rank_ep_model_equals_single_gpu_model():
+    """A one-rank expert-parallel verifier (2 layers) gives the same logits,
+    bit for bit, as the single-GPU verifier with every expert resident."""
+    from transformers import DynamicCache
+
+    from specfit_b200.runtime.ep_verifier import build_random_ep_qwen3
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
+
+    dev = torch.device("cuda", 0)
+    cfg = qwen3_moe_config(2)
+    single = build_random_offloaded_qwen3(device=dev, slots_per_layer=E, config=cfg, seed=3)
+    single.warm_all_caches()
+    epm = build_random_ep_qwen3(device=dev, rank=0, world=1, config=qwen3_moe_config(2), seed=3)
+    gen = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (2, 40), generator=gen).to(dev)
+    outs = []
+    for model in (single.model, epm.model):
+        cache = DynamicCache(config=cfg)
+        with torch.no_grad():
+            outs.append(model(input_ids=ids, past_key_values=cache, use_cache=True).logits)
+    single.close()
+    assert torch.equal(outs[0], outs[1])
