@@ -199,14 +199,14 @@ def make_tree(nodes, depth, branch, seed, vocab):
 
 class VerifyRunner:
     def __init__(self, loaded, ctx_ids, tree, seed_tok, device):
-        from transformers import DynamicCache
+        from specfit_b200.runtime.kv_cache import ReservedCache
 
         self.loaded = loaded
         self.model = loaded.model
         self.tree = tree
         self.device = device
         self.ctx = ctx_ids.shape[1]
-        self.cache = DynamicCache(config=self.model.config)
+        self.cache = ReservedCache(config=self.model.config, capacity=self.ctx + 1 + tree.draft_node_count)
         with torch.no_grad():
             self.model(input_ids=ctx_ids, past_key_values=self.cache, use_cache=True)
         seed = torch.tensor([[seed_tok]])
@@ -566,9 +566,8 @@ class EpRunner:
     routes over the global (request, token) order."""
 
     def __init__(self, args, loaded, cfg, device, rank, world):
-        from transformers import DynamicCache
-
         from specfit_b200 import synthetic
+        from specfit_b200.runtime.kv_cache import ReservedCache
 
         self.model = loaded.model
         self.device = device
@@ -580,7 +579,7 @@ class EpRunner:
         ctx_all = torch.randint(0, cfg.vocab_size, (args.requests, self.ctx), generator=gen)
         seeds = torch.randint(0, cfg.vocab_size, (args.requests,), generator=gen)
         lo, hi = rank * self.batch, (rank + 1) * self.batch
-        self.cache = DynamicCache(config=cfg)
+        self.cache = ReservedCache(config=cfg, capacity=self.ctx + q)
         with torch.no_grad():
             self.model(input_ids=ctx_all[lo:hi].to(device), past_key_values=self.cache, use_cache=True,
                        logits_to_keep=1)
@@ -684,7 +683,11 @@ def ep_swiglu_roofline(runner, moe, rank, world, device, peaks, iters=20):
 
 
 def ep_arm(args):
-    """expert-parallel verify over the ranks."""
+    """expert-parallel verify over the ranks.
+
+    The prefill and a reference timing use the NCCL exchange; the headline
+    runs the verify pass with the peer-memory exchange, captured as one CUDA
+    graph per rank (no host synchronisation inside a pass)."""
     rank, world, local = dist_info()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -698,32 +701,54 @@ def ep_arm(args):
     from specfit_b200 import ops
     from specfit_b200.runtime.ep_verifier import build_random_ep_qwen3
     from specfit_b200.runtime.qwen3_verifier import qwen3_moe_config
+    from specfit_b200.runtime.verify_graph import VerifyGraph
 
     peaks = measured_peaks()
     cfg = qwen3_moe_config(args.layers)
     t0 = time.perf_counter()
     loaded = build_random_ep_qwen3(device=device, rank=rank, world=world, config=cfg, seed=args.seed)
     runner = EpRunner(args, loaded, cfg, device, rank, world)
+    q = 1 + runner.tree.draft_node_count
     setup_s = time.perf_counter() - t0
 
-    launches0 = ops.LAUNCHES[0]
+    # Reference point: the NCCL exchange, eager (one host sync per layer).
+    nccl_ms, _ = timed_steps(runner.step_device, args.steps, 2, world, device)
+    moes = loaded.moes()
+    plans = [m.last_plan for m in moes]
+
+    # Peer-memory exchange: eager, then one CUDA graph per verify pass.
+    peer = loaded.attach_peer_exchange(max_tokens=runner.batch * q)
+    loaded.use_peer(True)
+    peer_eager_ms, _ = timed_steps(runner.step_device, args.steps, 2, world, device)
+    times, _ = moe_block_profile(runner)
+    vg = VerifyGraph(loaded.model, runner.cache, q_len=q, device=device, batch=runner.batch)
+    barrier(world)
+    runner.override = True
+    try:
+        before = ops.LAUNCHES[0]
+        vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
+        graph_launches = (ops.LAUNCHES[0] - before) // 3  # two warm-up passes + the captured one
+    finally:
+        runner.override = False
+    barrier(world)
     with ClockSampler(device.index) as clocks:
-        ms, ams = timed_steps(runner.step_device, args.steps, args.warmup, world, device)
-    launches = (ops.LAUNCHES[0] - launches0) // (args.steps + args.warmup) * args.steps
+        ms, ams = timed_steps(lambda: vg.replay().clone(), args.steps, args.warmup, world, device)
     committed = sum(runner.committed(a.cpu()) for a in ams)
     value = sum_over_ranks(committed, world, device) / (ms / 1e3)
-    e2e_ms, e2e_comm = timed_steps(runner.step_e2e, args.steps, 1, world, device)
-    e2e_value = sum_over_ranks(sum(e2e_comm), world, device) / (e2e_ms / 1e3)
 
-    moes = [layer.mlp.experts.moe for layer in loaded.model.model.layers]
-    times, _ = moe_block_profile(runner)
-    plans = [m.last_plan for m in moes]
+    def graph_e2e():
+        vg.load(runner.h_ids, runner.h_mask, runner.h_pos)
+        return runner.committed(vg.replay().cpu())
+
+    e2e_ms, e2e_comm = timed_steps(graph_e2e, args.steps, 1, world, device)
+    e2e_value = sum_over_ranks(sum(e2e_comm), world, device) / (e2e_ms / 1e3)
+    peer.check()
+
     row_bytes = ops.ep_row_bytes(torch.bfloat16, cfg.hidden_size, cfg.num_experts_per_tok)
     sent = [sum(p.send_pairs) * row_bytes + sum(p.send_routes) * cfg.hidden_size * 2 for p in plans]
     local_rows = statistics.median([sum(p.recv_routes) for p in plans])
     block_us = statistics.median(times) * 1e3
     block_us_max = max_over_ranks(block_us, world, device)
-    q = 1 + runner.tree.draft_node_count
     result = {
         "metric": "committed tokens/s (Qwen3-30B-A3B shape, 8 requests, expert-parallel)",
         "value": round(value, 3),
@@ -743,8 +768,8 @@ def ep_arm(args):
                          f"{args.requests} concurrent requests x {args.nodes}-node tree ({args.requests * q} "
                          f"verify tokens per step), {args.ep_ctx}-token context each, Zipf(1.1) routes, "
                          f"{cfg.num_experts} experts sharded over {world} GPU(s) "
-                         f"({cfg.num_experts // world} resident per GPU per layer), dispatch/return as "
-                         "NCCL all-to-all"),
+                         f"({cfg.num_experts // world} resident per GPU per layer), dispatch/return "
+                         "through peer memory over NVLink, one CUDA graph per verify pass"),
             "requests_per_gpu": runner.batch,
             "verify_tokens_per_step": args.requests * q,
             "parallelism": f"ep{world}, attention data-parallel over requests",
@@ -752,21 +777,29 @@ def ep_arm(args):
                          f"experts ({args.layers * cfg.num_experts // world * EXPERT_BYTES / 1e9:.1f} GB) "
                          "per GPU, >> 126 MB L2"),
         },
-        "gpu_launches": int(launches),
+        "gpu_launches": int(graph_launches) * args.steps,
         "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s",
                 "h2d_bytes_per_step": runner.h2d_bytes, "d2h_bytes_per_step": runner.d2h_bytes,
                 "ms_per_step": round(e2e_ms / args.steps, 3)},
         "clocks": clocks.summary(),
+        "exchange_variants_ms_per_step": {
+            "nccl_all_to_all_eager": round(nccl_ms / args.steps, 3),
+            "peer_memory_eager": round(peer_eager_ms / args.steps, 3),
+            "peer_memory_cuda_graph": round(ms / args.steps, 3),
+        },
         "moe_block": {
             "us_per_layer_median_max_over_ranks": round(block_us_max, 1),
             "rows_per_rank_median": local_rows,
             "nvlink_bytes_sent_per_layer_rank0": int(statistics.median(sent)),
-            "note": "CUDA events around each layer.mlp (router, send pack, 3 all-to-alls with one host "
-                    "sync for the counts, receive grouping, grouped SwiGLU, return, combine)",
+            "note": "CUDA events around each layer.mlp in an eager peer-memory pass (router, send "
+                    "plan + push, receive wait + grouping + gather, grouped SwiGLU, return, combine)",
         },
         "roofline": ep_swiglu_roofline(runner, moes[0], rank, world, device, peaks),
         "setup_s": round(setup_s, 1),
     }
+    del vg
+    torch.cuda.synchronize(device)
+    loaded.close()
     if world > 1:
         import torch.distributed as dist
 

@@ -3,8 +3,9 @@
  *
  * Every entry point takes plain device pointers, sizes, dtype codes and a
  * cudaStream_t passed as `void*` (NULL = the legacy default stream).  None of
- * them allocates device memory: scratch buffers ("workspace") are passed in
- * by the caller.  All device work is enqueued asynchronously on the given
+ * them allocates device memory except sf_ipc_alloc (the shared region of the
+ * peer-memory exchange): scratch buffers ("workspace") are passed in by the
+ * caller.  All device work is enqueued asynchronously on the given
  * stream; the return value is a status code (SF_OK on success), and on
  * failure sf_last_error() returns a message for the calling thread.
  *
@@ -281,7 +282,7 @@ SF_API int64_t sf_ep_row_bytes(int dtype, int hidden_size, int top_k);
 /* send_rows: [tokens*world, row_bytes] capacity; send_counts: int64 [2*world];
  * route_row: int32 [tokens*top_k], the row of each route's output in the
  * returned buffer (-1 for an invalid route, which also sets *error_flag);
- * pair_token: int32 [tokens*world] workspace.  top_k <= 16, world <= 32. */
+ * pair_token: int32 [tokens*world] workspace.  top_k <= 16, world <= 8. */
 SF_API int sf_ep_send_pack(const void* hidden, int dtype, int64_t tokens, int hidden_size,
                            const int64_t* topk_index, const void* topk_weights, int weight_dtype,
                            int top_k, int num_experts, int world, void* send_rows,
@@ -304,6 +305,71 @@ SF_API int sf_ep_recv_gather(const void* recv_rows, int64_t row_bytes, int dtype
 SF_API int sf_ep_return_pack(const void* out_sorted, int dtype, int hidden_size,
                              const int32_t* return_src, int64_t routes, void* return_rows,
                              void* stream);
+
+/*
+ * Expert parallelism over peer memory: the same exchange as above without
+ * NCCL and without host synchronisation (every count is read on the
+ * device), so a verify pass of all layers can be one CUDA graph.  Each rank
+ * owns one region of sf_ep_peer_layout() bytes (sf_ipc_alloc), maps every
+ * other rank's region with sf_ipc_open (CUDA IPC, peer access over NVLink)
+ * and lists all bases, in rank order, in the device array `peers`.  Sources
+ * store their rows straight into the destinations' regions; arrival counters
+ * (system-scope fence + atomic add per CTA) tell the readers when a layer's
+ * data is complete.  Waits give up after wait_limit_ms and record
+ * status[0] = site (1 receive, 2 return) and status[1] |= bit of every rank
+ * that did not arrive; the host reads `status` after a step.  Every rank must
+ * run the same sequence of layers with the same `grid`.
+ * Per layer: sf_ep_peer_send -> sf_ep_peer_recv -> sf_grouped_swiglu (rows =
+ * world * cap_routes, offsets/active from sf_ep_peer_recv) ->
+ * sf_ep_peer_return -> sf_ep_peer_finish.
+ */
+typedef struct sf_ep_peer {
+  int world, rank, top_k, hidden_size, dtype, local_experts;
+  int grid;           /* CTAs of the push/gather/return kernels, equal on every rank */
+  int wait_limit_ms;  /* bounded waits (e.g. 2000) */
+  int64_t cap_pairs;  /* max tokens a rank sends per layer (rows per source block) */
+  int64_t cap_routes; /* max routes per source block: cap_pairs * top_k covers every case */
+  int64_t row_bytes;  /* sf_ep_row_bytes(dtype, hidden_size, top_k) */
+  int64_t out_row_bytes; /* hidden_size * element size */
+  const uint64_t* peers; /* device [world]: region base of every rank */
+  void* local;           /* this rank's region (peers[rank]) */
+  uint64_t* epochs;      /* device [2], this rank only, zeroed with the regions */
+  int32_t* status;       /* device [2], this rank only */
+  int64_t off_recv_rows, off_ret_rows, off_recv_counts, off_recv_arrive, off_ret_arrive;
+} sf_ep_peer;
+
+/* Fills the off_* fields from world, capacities and row sizes; returns the
+ * region size in bytes (-1 for a null descriptor). */
+SF_API int64_t sf_ep_peer_layout(sf_ep_peer* d);
+/* cudaMalloc + zero + IPC handle (64 bytes) of a region; the one allocating
+ * entry point of the library, paired with sf_ipc_free. */
+SF_API int sf_ipc_alloc(size_t bytes, void** ptr, void* handle);
+SF_API int sf_ipc_free(void* ptr);
+/* Maps another process's region into the current device's context. */
+SF_API int sf_ipc_open(const void* handle, void** ptr);
+SF_API int sf_ipc_close(void* ptr);
+/* Plan + push of this rank's tokens (tokens <= cap_pairs).  staging_rows:
+ * [tokens*world, row_bytes]; route_row: [tokens*top_k] rows of the returned
+ * outputs in this rank's ret_rows ([d][cap_routes] layout). */
+SF_API int sf_ep_peer_send(const sf_ep_peer* d, const void* hidden, int64_t tokens,
+                           const int64_t* topk_index, const void* topk_weights, int weight_dtype,
+                           int num_experts, void* staging_rows, int64_t* send_counts,
+                           int32_t* route_row, int32_t* pair_token, int32_t* error_flag,
+                           void* stream);
+/* Wait for every source, group the received slots by local expert (outputs
+ * sized as sf_ep_recv_group with pairs = world*cap_pairs) and gather them
+ * into hidden_sorted [world*cap_routes, H] / weights_sorted. */
+SF_API int sf_ep_peer_recv(const sf_ep_peer* d, int32_t* counts, int32_t* offsets,
+                           int32_t* sorted_pos, int32_t* inv_pos, int32_t* active,
+                           int32_t* num_active, int32_t* return_src, int32_t* error_flag,
+                           void* hidden_sorted, float* weights_sorted, void* stream);
+/* Store each weighted output row into its source's region. */
+SF_API int sf_ep_peer_return(const sf_ep_peer* d, const void* out_sorted,
+                             const int32_t* return_src, const int32_t* offsets, void* stream);
+/* Wait for every destination's outputs and combine them (sf_moe_combine). */
+SF_API int sf_ep_peer_finish(const sf_ep_peer* d, const int64_t* topk_index,
+                             const int32_t* route_row, int64_t tokens, int num_experts,
+                             int reduce, void* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -41,6 +41,19 @@ _i64 = ctypes.c_int64
 _f32 = ctypes.c_float
 _sz = ctypes.c_size_t
 
+class EpPeer(ctypes.Structure):
+    """``sf_ep_peer`` (include/specfit_b200.h)."""
+
+    _fields_ = [("world", _i32), ("rank", _i32), ("top_k", _i32), ("hidden_size", _i32),
+                ("dtype", _i32), ("local_experts", _i32), ("grid", _i32), ("wait_limit_ms", _i32),
+                ("cap_pairs", _i64), ("cap_routes", _i64), ("row_bytes", _i64),
+                ("out_row_bytes", _i64), ("peers", _vp), ("local", _vp), ("epochs", _vp),
+                ("status", _vp), ("off_recv_rows", _i64), ("off_ret_rows", _i64),
+                ("off_recv_counts", _i64), ("off_recv_arrive", _i64), ("off_ret_arrive", _i64)]
+
+
+_peer_p = ctypes.POINTER(EpPeer)
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "sf_last_error": (ctypes.c_char_p, []),
@@ -77,6 +90,16 @@ SIGNATURES = {
                                 _vp, _vp, _vp, _vp]),
     "sf_ep_recv_gather": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp, _vp, _vp]),
     "sf_ep_return_pack": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp, _vp]),
+    "sf_ep_peer_layout": (_i64, [_peer_p]),
+    "sf_ipc_alloc": (_i32, [_sz, ctypes.POINTER(_vp), _vp]),
+    "sf_ipc_free": (_i32, [_vp]),
+    "sf_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "sf_ipc_close": (_i32, [_vp]),
+    "sf_ep_peer_send": (_i32, [_peer_p, _vp, _i64, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
+                               _vp]),
+    "sf_ep_peer_recv": (_i32, [_peer_p, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sf_ep_peer_return": (_i32, [_peer_p, _vp, _vp, _vp, _vp]),
+    "sf_ep_peer_finish": (_i32, [_peer_p, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
 }
 
 

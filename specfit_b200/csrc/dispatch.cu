@@ -18,6 +18,7 @@ namespace {
 // outside [0, 2^31) maps to -2, which the grouping reports as invalid.
 struct RouteIds {
   const int64_t* idx;
+  __device__ __forceinline__ int size() const { return 0; }  // the count is passed explicitly
   __device__ __forceinline__ int operator()(int p) const {
     const int64_t e = idx[p];
     return (e >= 0 && e < 0x7fffffff) ? (int)e : -2;

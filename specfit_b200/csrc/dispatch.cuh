@@ -8,7 +8,8 @@
 // 32-route chunks in order, ranking equal ids within a chunk with
 // __match_any_sync, so the scatter is stable and deterministic.
 //
-// The expert id of position p comes from `src(p)`.  An id of -1 is a padding
+// The expert id of position p comes from `src(p)`; when n < 0 the number of
+// positions is `src.size()`, read on the device.  An id of -1 is a padding
 // slot when `pad_ok` (skipped silently); any other id outside [0, E) sets
 // *error_flag and is skipped.  When `compact` is non-null it receives, for
 // the q-th valid position in increasing position order, that route's sorted
@@ -69,6 +70,7 @@ group_kernel(Src src, int n, int E, bool pad_ok, int32_t* __restrict__ counts,
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  if (n < 0) n = src.size();
   const int seg_len = (n + kSegs - 1) / kSegs;
   const int seg_lo = min(n, warp * seg_len);
   const int seg_hi = min(n, seg_lo + seg_len);

@@ -16,126 +16,10 @@
 // of its routes' outputs lands (route_row) and reduces them with the single-
 // GPU combine, so the layer's result is the one-GPU result bit for bit.
 #include "dispatch.cuh"
+#include "ep.cuh"
 
 namespace sf {
 namespace {
-
-constexpr int kMaxWorld = 32;
-constexpr int kMaxK = 16;
-constexpr int kPlanThreads = 1024;
-
-int64_t row_bytes_of(int es, int H, int K) {
-  const int64_t raw = (int64_t)H * es + 8LL * K;
-  return (raw + 15) / 16 * 16;
-}
-
-template <typename W>
-__global__ void __launch_bounds__(kPlanThreads)
-ep_plan_kernel(const int64_t* __restrict__ idx, const W* __restrict__ topk_w, int T, int K, int E,
-               int world, uint8_t* __restrict__ send, int64_t row_bytes, int64_t meta_off,
-               int64_t* __restrict__ send_counts, int32_t* __restrict__ route_row,
-               int32_t* __restrict__ pair_token, int32_t* __restrict__ error_flag) {
-  __shared__ int tot_pairs[kMaxWorld], tot_routes[kMaxWorld];
-  __shared__ int pair_off[kMaxWorld], route_off[kMaxWorld];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int per = E / world;
-
-  // Pass A: pairs and routes per destination (warp r counts rank r).
-  if (warp < world) {
-    int pc = 0, rc = 0;
-    for (int t = lane; t < T; t += 32) {
-      int c = 0;
-      for (int k = 0; k < K; ++k) {
-        const int64_t e = idx[(int64_t)t * K + k];
-        if (e >= 0 && e < E) {
-          c += (int)(e / per) == warp;
-        } else if (warp == 0) {
-          *error_flag = 1;
-        }
-      }
-      pc += c > 0;
-      rc += c;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      pc += __shfl_xor_sync(0xffffffffu, pc, o);
-      rc += __shfl_xor_sync(0xffffffffu, rc, o);
-    }
-    if (lane == 0) {
-      tot_pairs[warp] = pc;
-      tot_routes[warp] = rc;
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int p = 0, r = 0;
-    for (int d = 0; d < world; ++d) {
-      pair_off[d] = p;
-      route_off[d] = r;
-      send_counts[2 * d] = tot_pairs[d];
-      send_counts[2 * d + 1] = tot_routes[d];
-      p += tot_pairs[d];
-      r += tot_routes[d];
-    }
-  }
-  __syncthreads();
-
-  // Pass B: warp r walks the tokens in order and writes rank r's pairs.
-  if (warp >= world) return;
-  const int r = warp;
-  int carry_p = pair_off[r], carry_r = route_off[r];
-  const unsigned lt = (1u << lane) - 1u;
-  for (int t0 = 0; t0 < T; t0 += 32) {
-    const int t = t0 + lane;
-    int ids[kMaxK], ks[kMaxK];
-    float ws[kMaxK];
-    int cnt = 0;
-    if (t < T) {
-      for (int k = 0; k < K; ++k) {
-        const int64_t e = idx[(int64_t)t * K + k];
-        if (e < 0 || e >= E) {
-          if (r == 0) route_row[(int64_t)t * K + k] = -1;
-          continue;
-        }
-        if ((int)(e / per) != r) continue;
-        const int le = (int)(e - (int64_t)r * per);
-        int j = cnt++;
-        while (j > 0 && ids[j - 1] > le) {  // ascending local id
-          ids[j] = ids[j - 1];
-          ks[j] = ks[j - 1];
-          ws[j] = ws[j - 1];
-          --j;
-        }
-        ids[j] = le;
-        ks[j] = k;
-        ws[j] = to_f32(topk_w[(int64_t)t * K + k]);
-      }
-    }
-    const unsigned has = __ballot_sync(0xffffffffu, cnt > 0);
-    int incl = cnt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int x = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += x;
-    }
-    if (cnt > 0) {
-      const int pair = carry_p + __popc(has & lt);
-      const int rbase = carry_r + incl - cnt;
-      pair_token[pair] = t;
-      uint8_t* meta = send + (int64_t)pair * row_bytes + meta_off;
-      int32_t* mid = reinterpret_cast<int32_t*>(meta);
-      float* mw = reinterpret_cast<float*>(meta + 4 * K);
-      for (int j = 0; j < K; ++j) {
-        mid[j] = j < cnt ? ids[j] : -1;
-        mw[j] = j < cnt ? ws[j] : 0.f;
-      }
-      for (int j = 0; j < cnt; ++j) route_row[(int64_t)t * K + ks[j]] = rbase + j;
-    }
-    carry_p += __popc(has);
-    carry_r += __shfl_sync(0xffffffffu, incl, 31);
-  }
-}
 
 // dst row i <- src row index(i) (H bytes each, 16-byte vectors; one warp per
 // row).  Rows whose index is negative are zero-filled.  When `total` is
@@ -169,6 +53,7 @@ struct RecvIds {
   const uint8_t* rows;
   int64_t row_bytes, meta_off;
   int K;
+  __device__ __forceinline__ int size() const { return 0; }  // sizes are passed explicitly
   __device__ __forceinline__ int operator()(int p) const {
     const int pair = p / K;
     return reinterpret_cast<const int32_t*>(rows + (int64_t)pair * row_bytes + meta_off)[p - pair * K];
@@ -198,16 +83,6 @@ __global__ void recv_gather_kernel(const uint8_t* __restrict__ rows, int64_t row
     for (int64_t v = lane; v < vecs; v += 32) d[v] = a[v];
     if (lane == 0) w_sorted[i] = reinterpret_cast<const float*>(row + meta_off + 4 * K)[p - pair * K];
   }
-}
-
-int elem_size(int dtype) {
-  return dtype == SF_DTYPE_BF16 ? 2 : dtype == SF_DTYPE_F32 ? 4 : 0;
-}
-
-int copy_grid(int64_t rows) {
-  const int64_t need = (rows + 7) / 8;  // 8 warps per CTA
-  const int64_t cap = 4LL * num_sms();
-  return (int)(need < 1 ? 1 : need < cap ? need : cap);
 }
 
 }  // namespace
@@ -245,16 +120,14 @@ extern "C" int sf_ep_send_pack(const void* hidden, int dtype, int64_t tokens, in
                "hidden and send_rows must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   const int64_t meta_off = (int64_t)hidden_size * es;
+  uint8_t* rows = static_cast<uint8_t*>(send_rows);
   if (weight_dtype == SF_DTYPE_F32)
-    ep_plan_kernel<float><<<1, kPlanThreads, 0, s>>>(
-        topk_index, static_cast<const float*>(topk_weights), (int)tokens, top_k, num_experts, world,
-        static_cast<uint8_t*>(send_rows), row_bytes, meta_off, send_counts, route_row, pair_token,
-        error_flag);
+    launch_plan(top_k, topk_index, static_cast<const float*>(topk_weights), (int)tokens, num_experts,
+                world, 0, rows, row_bytes, meta_off, send_counts, route_row, pair_token, error_flag, s);
   else
-    ep_plan_kernel<__nv_bfloat16><<<1, kPlanThreads, 0, s>>>(
-        topk_index, static_cast<const __nv_bfloat16*>(topk_weights), (int)tokens, top_k,
-        num_experts, world, static_cast<uint8_t*>(send_rows), row_bytes, meta_off, send_counts,
-        route_row, pair_token, error_flag);
+    launch_plan(top_k, topk_index, static_cast<const __nv_bfloat16*>(topk_weights), (int)tokens,
+                num_experts, world, 0, rows, row_bytes, meta_off, send_counts, route_row,
+                pair_token, error_flag, s);
   SF_CHECK_LAUNCH();
   if (tokens == 0) return SF_OK;
   // Hidden rows of the pairs; the pair count is read on the device.

@@ -62,10 +62,62 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Visibility of keys prefix_len + j0 + i, i in [0, 64), as bit i: keys before
+// the tree block (j < 0) are visible; bits past the mask's words are 0.
+__device__ __forceinline__ uint64_t mask_window(const uint32_t* __restrict__ bits, int words,
+                                                int j0) {
+  if (j0 + 64 <= 0) return ~0ull;
+  if (j0 >= 0) {
+    const int w = j0 >> 5, sh = j0 & 31;
+    const uint64_t lo = w < words ? bits[w] : 0u;
+    const uint64_t mid = w + 1 < words ? bits[w + 1] : 0u;
+    uint64_t x = lo | (mid << 32);
+    if (sh) {
+      const uint64_t hi = w + 2 < words ? bits[w + 2] : 0u;
+      x = (x >> sh) | (hi << (64 - sh));
+    }
+    return x;
+  }
+  const int d = -j0;  // 1..63 keys of the block precede the tree
+  const uint64_t x = (uint64_t)(words > 0 ? bits[0] : 0u) |
+                     ((uint64_t)(words > 1 ? bits[1] : 0u) << 32);
+  return (x << d) | ((1ull << d) - 1);
+}
+
+// Stages keys [b0, b0 + 64) of one KV head into one K/V buffer pair with
+// cp.async (one commit group); rows at or past key_hi are zero-filled.
+__device__ __forceinline__ void stage_block(__nv_bfloat16* ks, __nv_bfloat16* vs,
+                                            const __nv_bfloat16* kbase,
+                                            const __nv_bfloat16* vbase, int64_t kv_rs, int b0,
+                                            int key_hi) {
+  for (int i = threadIdx.x; i < kKeys * (kD / 8); i += kWarps * 32) {
+    const int r = i / (kD / 8), col = (i % (kD / 8)) * 8;
+    const int key = b0 + r;
+    __nv_bfloat16* kd = ks + r * kPitch + col;
+    __nv_bfloat16* vd = vs + r * kPitch + col;
+    if (key < key_hi) {
+      const uint32_t ka = static_cast<uint32_t>(__cvta_generic_to_shared(kd));
+      const uint32_t va = static_cast<uint32_t>(__cvta_generic_to_shared(vd));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ka),
+                   "l"(kbase + (int64_t)key * kv_rs + col)
+                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(va),
+                   "l"(vbase + (int64_t)key * kv_rs + col)
+                   : "memory");
+    } else {
+      *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+constexpr int kStageElems = kKeys * kPitch;  // one K (or V) buffer
+constexpr size_t kSmemBytes = 4 * kStageElems * sizeof(__nv_bfloat16);  // 2 stages x (K, V)
+
 __global__ void __launch_bounds__(kWarps * 32)
 tree_attn_mma_kernel(AttnParams p) {
-  __shared__ __align__(16) __nv_bfloat16 ks[kKeys * kPitch];
-  __shared__ __align__(16) __nv_bfloat16 vs[kKeys * kPitch];
+  extern __shared__ __align__(16) __nv_bfloat16 smem[];
 
   const int kvh = blockIdx.x;
   const int split = blockIdx.z;
@@ -108,29 +160,32 @@ tree_attn_mma_kernel(AttnParams p) {
   const __nv_bfloat16* kbase = p.k + (int64_t)kvh * p.kv_hs;
   const __nv_bfloat16* vbase = p.v + (int64_t)kvh * p.kv_hs;
 
-  for (int b0 = key_lo; b0 < key_hi; b0 += kKeys) {
-    __syncthreads();  // previous block fully consumed
-    for (int i = threadIdx.x; i < kKeys * (kD / 8); i += kWarps * 32) {
-      const int r = i / (kD / 8), col = (i % (kD / 8)) * 8;
-      const int key = b0 + r;
-      __nv_bfloat16* kd = ks + r * kPitch + col;
-      __nv_bfloat16* vd = vs + r * kPitch + col;
-      if (key < key_hi) {
-        const uint32_t ka = static_cast<uint32_t>(__cvta_generic_to_shared(kd));
-        const uint32_t va = static_cast<uint32_t>(__cvta_generic_to_shared(vd));
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ka),
-                     "l"(kbase + (int64_t)key * p.kv_rs + col)
-                     : "memory");
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(va),
-                     "l"(vbase + (int64_t)key * p.kv_rs + col)
-                     : "memory");
-      } else {
-        *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
-      }
+  const uint32_t* rbits[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) rbits[h] = p.bits ? p.bits + (int64_t)trow[h] * p.bit_words : nullptr;
+
+  // Two-stage pipeline: block i+1 streams in while block i is computed.
+  if (key_lo < key_hi) stage_block(smem, smem + kStageElems, kbase, vbase, p.kv_rs, key_lo, key_hi);
+  int it = 0;
+  for (int b0 = key_lo; b0 < key_hi; b0 += kKeys, ++it) {
+    const __nv_bfloat16* ks = smem + (it & 1) * 2 * kStageElems;
+    const __nv_bfloat16* vs = ks + kStageElems;
+    if (b0 + kKeys < key_hi) {
+      __nv_bfloat16* nk = smem + ((it + 1) & 1) * 2 * kStageElems;
+      stage_block(nk, nk + kStageElems, kbase, vbase, p.kv_rs, b0 + kKeys, key_hi);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
+
+    uint64_t win[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      win[h] = rbits[h] ? mask_window(rbits[h], p.bit_words, b0 - p.prefix_len)
+                        : (b0 + kKeys <= p.prefix_len ? ~0ull
+                                                      : (b0 >= p.prefix_len ? 0ull
+                                                                            : (1ull << (p.prefix_len - b0)) - 1));
 
     // S = Q K^T for this warp's 16 rows x 64 keys (8 n-tiles of 8 keys).
     float s[8][4];
@@ -151,18 +206,13 @@ tree_attn_mma_kernel(AttnParams p) {
     // Mask, online softmax (a row lives on the 4 lanes of a quad).
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const uint32_t* bits = p.bits + (int64_t)trow[h] * p.bit_words;
       float mx = -INFINITY;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int key = b0 + nt * 8 + 2 * c + e;
-          bool vis = rok[h] && key < key_hi;
-          if (vis && key >= p.prefix_len) {
-            const int j = key - p.prefix_len;
-            vis = (bits[j >> 5] >> (j & 31)) & 1u;
-          }
+          const int kb = nt * 8 + 2 * c + e;
+          const bool vis = rok[h] && b0 + kb < key_hi && ((win[h] >> kb) & 1ull);
           const float a = vis ? s[nt][2 * h + e] * p.scale : -INFINITY;
           s[nt][2 * h + e] = a;
           mx = fmaxf(mx, a);
@@ -217,6 +267,7 @@ tree_attn_mma_kernel(AttnParams p) {
         mma_bf16(o[2 * dp + 1], pa, vb[2], vb[3]);
       }
     }
+    __syncthreads();  // this stage is consumed before it is refilled
   }
 
   // Row sums across the quad, then the split partials.
@@ -255,7 +306,14 @@ int tree_attention_mma(AttnParams& p, cudaStream_t stream) {
   p.splits = (int)((p.kv_len + p.keys_per_split - 1) / p.keys_per_split);
   p.part_ml = p.part_o + (size_t)p.splits * p.num_heads * p.q_len * kD;
   dim3 grid((unsigned)p.num_kv_heads, (unsigned)row_blocks, (unsigned)p.splits);
-  tree_attn_mma_kernel<<<grid, kWarps * 32, 0, stream>>>(p);
+  static std::atomic<unsigned long long> attr_done{0};
+  const int rc = once_per_device(attr_done, [] {
+    SF_CHECK_CUDA(cudaFuncSetAttribute(tree_attn_mma_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    return SF_OK;
+  });
+  if (rc != SF_OK) return rc;
+  tree_attn_mma_kernel<<<grid, kWarps * 32, kSmemBytes, stream>>>(p);
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

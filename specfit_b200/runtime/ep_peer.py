@@ -1,0 +1,161 @@
+"""Peer-memory regions of an expert-parallel group (the sync-free exchange).
+
+Each rank allocates one region (``sf_ipc_alloc``), the ranks trade CUDA IPC
+handles through the process group, and every rank maps the others' regions
+into its own device context (``sf_ipc_open``: peer access over NVLink).  The
+``sf_ep_peer`` descriptor then lets the K7 peer kernels push rows into, and
+read arrivals from, any rank's region with no host involvement.
+
+With one rank the region is only this process's own, and the same kernels
+run the exchange with itself (each wait is satisfied by the push launched
+before it on the same stream).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from .. import _native as N
+from .. import ops
+
+
+class PeerExchange:
+    def __init__(self, *, rank: int, world: int, max_tokens: int, hidden_size: int, top_k: int,
+                 local_experts: int, device, dtype=torch.bfloat16, group=None, grid: int = 64,
+                 wait_limit_ms: int = 2000) -> None:
+        self.rank, self.world, self.group = rank, world, group
+        self.device = torch.device(device)
+        self.dtype = dtype
+        d = N.EpPeer()
+        d.world, d.rank, d.top_k, d.hidden_size = world, rank, top_k, hidden_size
+        d.dtype = ops.dtype_code(dtype)
+        d.local_experts = local_experts
+        d.grid, d.wait_limit_ms = grid, wait_limit_ms
+        d.cap_pairs = max_tokens
+        d.cap_routes = max_tokens * top_k
+        d.row_bytes = ops.ep_row_bytes(dtype, hidden_size, top_k)
+        d.out_row_bytes = hidden_size * torch.empty((), dtype=dtype).element_size()
+        self.bytes = int(N.lib.sf_ep_peer_layout(ctypes.byref(d)))
+        self.desc = d
+        self._opened: list = []
+        self._base = None
+        with torch.cuda.device(self.device):
+            base = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            N.check(N.lib.sf_ipc_alloc(self.bytes, ctypes.byref(base), handle), "sf_ipc_alloc")
+            self._base = base.value
+            bases = [0] * world
+            bases[rank] = base.value
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+                for r, h in enumerate(handles):
+                    if r == rank:
+                        continue
+                    p = ctypes.c_void_p()
+                    hb = ctypes.create_string_buffer(h, 64)
+                    N.check(N.lib.sf_ipc_open(hb, ctypes.byref(p)), "sf_ipc_open")
+                    self._opened.append(p.value)
+                    bases[r] = p.value
+            self.peers = torch.tensor(bases, dtype=torch.int64, device=self.device)
+            self.state = torch.zeros(4, dtype=torch.int64, device=self.device)  # epochs[2], status
+            d.peers = self.peers.data_ptr()
+            d.local = base.value
+            d.epochs = self.state.data_ptr()
+            d.status = self.state[2:].data_ptr()
+            torch.cuda.synchronize(self.device)
+        if world > 1:
+            dist.barrier(group=group)  # every region zeroed and mapped before any push
+
+    @property
+    def cap_pairs(self) -> int:
+        return self.desc.cap_pairs
+
+    def status(self) -> tuple:
+        """(site, missing ranks bitmask) of the first wait that gave up, or (0, 0)."""
+        st = self.state[2:].view(torch.int32).cpu()
+        return int(st[0]), int(st[1])
+
+    def check(self) -> None:
+        site, missing = self.status()
+        if site:
+            where = {1: "receive", 2: "return"}.get(site, str(site))
+            ranks = [r for r in range(self.world) if missing >> r & 1]
+            raise RuntimeError(f"expert-parallel peer exchange: {where} wait gave up; "
+                               f"ranks {ranks} did not arrive")
+
+    def close(self) -> None:
+        if self._base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                N.lib.sf_ipc_close(p)
+            self._opened = []
+            if self.world > 1:
+                dist.barrier(group=self.group)  # nobody maps this region any more
+            N.lib.sf_ipc_free(self._base)
+        self._base = None
+
+    # -- one layer -----------------------------------------------------------------
+
+    def layer(self, moe, hidden: torch.Tensor, top_k_index: torch.Tensor,
+              top_k_weights: torch.Tensor) -> torch.Tensor:
+        """The MoE experts of one layer through the peer exchange (``moe``:
+        an ``ExpertParallelMoE`` of this rank).  No host synchronisation."""
+        d = self.desc
+        dev = hidden.device
+        T, K = top_k_index.shape
+        if T > d.cap_pairs:
+            raise ValueError(f"{T} tokens exceed the peer exchange capacity {d.cap_pairs}")
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        h = hidden.contiguous()
+        idx = top_k_index.contiguous()
+        w = top_k_weights.contiguous()
+        E = moe.num_experts
+        El = moe.local_experts
+        staging = torch.empty(max(T * self.world, 1), d.row_bytes, dtype=torch.uint8, device=dev)
+        send_i32 = torch.empty(T * K + T * self.world + 1, dtype=torch.int32, device=dev)
+        route_row = send_i32[: T * K]
+        pair_token = send_i32[T * K: T * K + T * self.world]
+        send_err = send_i32[T * K + T * self.world:]
+        send_err.zero_()
+        send_counts = torch.empty(self.world, 2, dtype=torch.int64, device=dev)
+        N.check(N.lib.sf_ep_peer_send(ctypes.byref(d), h.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
+                                      ops.dtype_code(w.dtype), E, staging.data_ptr(),
+                                      send_counts.data_ptr(), route_row.data_ptr(),
+                                      pair_token.data_ptr(), send_err.data_ptr(), stream),
+                "sf_ep_peer_send")
+        n = self.world * d.cap_pairs * K
+        rows = self.world * d.cap_routes
+        buf = torch.empty(El + (El + 1) + 3 * n + El + 2, dtype=torch.int32, device=dev)
+        counts = buf[:El]
+        offsets = buf[El: 2 * El + 1]
+        sorted_pos = buf[2 * El + 1: 2 * El + 1 + n]
+        inv_pos = buf[2 * El + 1 + n: 2 * El + 1 + 2 * n]
+        return_src = buf[2 * El + 1 + 2 * n: 2 * El + 1 + 3 * n]
+        active = buf[2 * El + 1 + 3 * n: 3 * El + 1 + 3 * n]
+        num_active = buf[3 * El + 1 + 3 * n: 3 * El + 2 + 3 * n]
+        err = buf[3 * El + 2 + 3 * n:]
+        err.zero_()
+        xs = torch.empty(rows, d.hidden_size, dtype=self.dtype, device=dev)
+        ws = torch.empty(rows, dtype=torch.float32, device=dev)
+        N.check(N.lib.sf_ep_peer_recv(ctypes.byref(d), counts.data_ptr(), offsets.data_ptr(),
+                                      sorted_pos.data_ptr(), inv_pos.data_ptr(), active.data_ptr(),
+                                      num_active.data_ptr(), return_src.data_ptr(), err.data_ptr(),
+                                      xs.data_ptr(), ws.data_ptr(), stream), "sf_ep_peer_recv")
+        disp = ops.Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, err,
+                            self.world * d.cap_pairs, K, El)
+        ys = ops.grouped_swiglu(xs, ws, disp, moe.slot, moe.storage, moe.hidden, moe.inter)
+        N.check(N.lib.sf_ep_peer_return(ctypes.byref(d), ys.data_ptr(), return_src.data_ptr(),
+                                        offsets.data_ptr(), stream), "sf_ep_peer_return")
+        out = torch.empty(T, d.hidden_size, dtype=self.dtype, device=dev)
+        N.check(N.lib.sf_ep_peer_finish(ctypes.byref(d), idx.data_ptr(), route_row.data_ptr(), T, E,
+                                        N.SF_REDUCE_MODEL_DTYPE, out.data_ptr(), stream),
+                "sf_ep_peer_finish")
+        ops._launched(8 if T else 7)  # the grouped SwiGLU counts its own two
+        return out

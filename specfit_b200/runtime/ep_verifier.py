@@ -59,9 +59,33 @@ class LoadedEpQwen3:
     model: nn.Module
     rank: int
     world: int
+    peer: object = None  # PeerExchange shared by every layer, once attached
+
+    def moes(self) -> list:
+        return [layer.mlp.experts.moe for layer in self.model.model.layers]
+
+    def attach_peer_exchange(self, max_tokens: int, group=None, **kw):
+        """Allocate and map the peer regions (collective over the group) and
+        give every layer the same exchange (layers run one after another)."""
+        from .ep_peer import PeerExchange
+
+        m = self.moes()[0]
+        self.peer = PeerExchange(rank=self.rank, world=self.world, max_tokens=max_tokens,
+                                 hidden_size=m.hidden, top_k=m.top_k, local_experts=m.local_experts,
+                                 device=m.storage.device, dtype=m.storage.dtype, group=group, **kw)
+        for moe in self.moes():
+            moe.peer = self.peer
+        return self.peer
+
+    def use_peer(self, on: bool) -> None:
+        for moe in self.moes():
+            moe.use_peer = bool(on)
 
     def close(self) -> None:
         torch.cuda.synchronize()
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
 
 def build_random_ep_qwen3(*, device, rank: int, world: int, group=None,

@@ -18,6 +18,12 @@ its own tokens (attention stays data-parallel).  Per layer:
 4. the rows travel back, and ``combine`` reduces every token's routes with
    the single-GPU combine (ascending expert id, bf16 rounding per add).
 
+Two exchanges implement steps 2 and 4: NCCL ``all_to_all_single`` (one host
+synchronisation per layer for the split sizes), and, when a ``PeerExchange``
+is attached and ``use_peer`` is set, stores straight into the other ranks'
+memory with device-side arrival counters (no host synchronisation, so a
+verify pass can be captured in a CUDA graph).  Both give the same result.
+
 So the block's output is the one-GPU output bit for bit.  The exchange goes
 through NCCL over NVLink / NVSwitch; the phases are plain functions so a
 test can also drive several ranks' phases on one device.
@@ -79,6 +85,8 @@ class ExpertParallelMoE:
         self.storage = local_storage
         self.slot = torch.arange(self.local_experts, dtype=torch.int32, device=local_storage.device)
         self.last_plan: RecvPlan | None = None  # split sizes of the latest forward (host ints)
+        self.peer = None  # PeerExchange shared by the layers of this rank, if any
+        self.use_peer = False
 
     @classmethod
     def from_process_group(cls, group=None, **kw) -> "ExpertParallelMoE":
@@ -107,6 +115,10 @@ class ExpertParallelMoE:
     # -- one layer over the process group -------------------------------------
 
     def forward(self, hidden: torch.Tensor, top_k_index: torch.Tensor, top_k_weights: torch.Tensor):
+        if self.use_peer:
+            if self.peer is None:
+                raise RuntimeError("use_peer is set but no PeerExchange is attached")
+            return self.peer.layer(self, hidden, top_k_index, top_k_weights)
         send = self.send(hidden, top_k_index, top_k_weights)
         if self.world == 1:  # the exchange with oneself is the identity
             counts = send.counts.cpu()

@@ -137,6 +137,14 @@ def nccl_rank(rank: int, world: int, port: int, seed: int, tokens_per_rank) -> N
                                 local_storage=storage[rank * per:(rank + 1) * per], rank=rank,
                                 world=world)
         got = moe.forward(x[lo:hi], idx[lo:hi], w[lo:hi])
+        from specfit_b200.runtime.ep_peer import PeerExchange
+
+        peer = PeerExchange(rank=rank, world=world, max_tokens=max(tokens_per_rank), hidden_size=H,
+                            top_k=K, local_experts=per, device=device)
+        moe.peer, moe.use_peer = peer, True
+        got_peer = [moe.forward(x[lo:hi], idx[lo:hi], w[lo:hi]) for _ in range(3)]
+        torch.cuda.synchronize()
+        peer.check()
         d = ops.moe_dispatch(idx, E)
         xs, ws = ops.moe_gather(x, w, d)
         slot = torch.arange(E, dtype=torch.int32, device=device)
@@ -144,5 +152,8 @@ def nccl_rank(rank: int, world: int, port: int, seed: int, tokens_per_rank) -> N
         want = ops.moe_combine(ys, d, idx)[lo:hi]
         torch.cuda.synchronize()
         assert torch.equal(got, want), f"rank {rank}: NCCL expert-parallel output differs"
+        for gp in got_peer:
+            assert torch.equal(gp, want), f"rank {rank}: peer-memory expert-parallel output differs"
+        peer.close()
     finally:
         dist.destroy_process_group()

@@ -177,3 +177,62 @@ def test_one_rank_ep_model_equals_single_gpu_model():
             outs.append(model(input_ids=ids, past_key_values=cache, use_cache=True).logits)
     single.close()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("tokens", [65, 520, 0])
+def test_peer_exchange_one_rank_equals_single_gpu(tokens, expert_storage):
+    """The peer-memory exchange run with oneself (push, bounded wait,
+    grouping, gather, SwiGLU, return, wait, combine) gives the single-GPU
+    block bit for bit, repeatedly (arrival counters advance per layer)."""
+    from specfit_b200.runtime.ep_peer import PeerExchange
+
+    g = torch.Generator(device="cuda").manual_seed(tokens)
+    moe = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, intermediate_size=I,
+                            local_storage=expert_storage, rank=0, world=1)
+    peer = PeerExchange(rank=0, world=1, max_tokens=520, hidden_size=H, top_k=K, local_experts=E,
+                        device="cuda")
+    moe.peer, moe.use_peer = peer, True
+    try:
+        for rep in range(3):
+            x = (torch.randn(tokens, H, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+            idx = _routes(tokens, rep)
+            w = torch.rand(tokens, K, generator=g, device="cuda")
+            got = moe.forward(x, idx, w)
+            want = _single_gpu_block(x, idx, w, expert_storage) if tokens else got
+            torch.cuda.synchronize()
+            assert torch.equal(got, want)
+        assert peer.status() == (0, 0)
+    finally:
+        peer.close()
+
+
+def test_peer_wait_gives_up_and_reports():
+    """A receive wait whose arrivals never come (no push was issued) returns
+    after its limit with the site and the missing rank recorded; the GPU
+    stays usable."""
+    import ctypes
+
+    from specfit_b200 import _native as N
+    from specfit_b200.runtime.ep_peer import PeerExchange
+
+    peer = PeerExchange(rank=0, world=1, max_tokens=8, hidden_size=H, top_k=K, local_experts=16,
+                        device="cuda", wait_limit_ms=100)
+    try:
+        n = peer.desc.cap_pairs * K
+        i32 = torch.zeros(16 + 17 + 3 * n + 16 + 2, dtype=torch.int32, device="cuda")
+        xs = torch.empty(peer.desc.cap_routes, H, dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty(peer.desc.cap_routes, dtype=torch.float32, device="cuda")
+        p = i32.data_ptr()
+        ptr = lambda off: p + 4 * off
+        rc = N.lib.sf_ep_peer_recv(ctypes.byref(peer.desc), ptr(0), ptr(16), ptr(33), ptr(33 + n),
+                                   ptr(33 + 3 * n), ptr(33 + 3 * n + 16), ptr(33 + 2 * n),
+                                   ptr(33 + 3 * n + 17), xs.data_ptr(), ws.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream)
+        assert rc == N.SF_OK
+        torch.cuda.synchronize()
+        assert peer.status() == (1, 1)
+        with pytest.raises(RuntimeError, match="receive wait gave up"):
+            peer.check()
+        assert torch.ones(4, device="cuda").sum().item() == 4.0  # the context is fine
+    finally:
+        peer.close()

@@ -127,10 +127,14 @@ def test_pool_is_page_locked(loaded):
     assert all(c.sources_are_pinned for c in loaded.caches)
 
 
-def test_verify_graph_replay_equals_eager():
-    """A captured verify pass (every expert resident) replays bit for bit."""
+@pytest.mark.parametrize("reserved", [False, True])
+def test_verify_graph_replay_equals_eager(reserved):
+    """A captured verify pass (every expert resident) replays bit for bit,
+    over a DynamicCache or an in-place ReservedCache; the eager reference
+    always uses Hugging Face's DynamicCache."""
     from transformers import DynamicCache
 
+    from specfit_b200.runtime.kv_cache import ReservedCache
     from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3
     from specfit_b200.runtime.verify_graph import VerifyGraph
 
@@ -157,6 +161,16 @@ def test_verify_graph_replay_equals_eager():
                             use_cache=True)
             eager.append(out.logits[0].clone())
             cache.crop(37)
+        if reserved:
+            cache = ReservedCache(config=model.config, capacity=47)
+            with torch.no_grad():
+                model(input_ids=ctx, past_key_values=cache, use_cache=True)
+            for (ids, mask, pos), ref in zip(inputs, eager):  # eager passes over the reserved cache
+                with torch.no_grad():
+                    out = model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                                past_key_values=cache, use_cache=True)
+                assert torch.equal(out.logits[0], ref)
+                cache.crop(37)
         vg = VerifyGraph(model, cache, q_len=10, device=DEV)
         vg.capture(*inputs[0])
         hits_before = m.caches[0].stats().resident_hits
