@@ -86,7 +86,7 @@ class Qwen3OffloadedExperts(nn.Module):
         if self._prediction_scheduler is not None:
             if execution_order is not None:
                 raise ValueError("explicit execution_order conflicts with dynamic predicted prefetch")
-            raise NotImplementedError("predicted cross-layer prefetch is not available in this build")
+            return self._forward_scheduled(hidden_states, top_k_index, top_k_weights)
         tokens = hidden_states.shape[0]
         if tokens == 0:
             return torch.zeros_like(hidden_states)
@@ -152,6 +152,55 @@ class Qwen3OffloadedExperts(nn.Module):
                 r[e] = i
             rank = r.to(dev)
         return ops.moe_combine(ys, d, top_k_index, expert_rank=rank)
+
+    def _forward_scheduled(self, hidden_states, top_k_index, top_k_weights):
+        """Under ``Qwen3ExpertPrefetch`` (``_forward_prefetched``,
+        qwen3_offloaded_experts.py:166-203): the layer's real experts are
+        handed over one at a time, completed fills first; each runs as a
+        one-expert grouped launch on its rows of the dispatch order, and the
+        contributions are reduced once, canonically."""
+        scheduler = self._prediction_scheduler
+        dev = hidden_states.device
+        if hidden_states.shape[0] == 0:
+            for _ in scheduler.experts(self.layer_id, ()):
+                pass
+            return torch.zeros_like(hidden_states)
+        if self.num_experts == 0:
+            raise KeyError(f"unknown expert {ExpertKey(self.layer_id, int(top_k_index.reshape(-1)[0]))!r}")
+        h = hidden_states.contiguous()
+        d = ops.moe_dispatch(top_k_index, self.num_experts)
+        host = torch.cat((d.num_active, d.error, d.active)).cpu()  # the router's experts
+        n_active, err = int(host[0]), int(host[1])
+        if err:
+            bad = top_k_index[(top_k_index < 0) | (top_k_index >= self.num_experts)]
+            raise KeyError(f"unknown expert {ExpertKey(self.layer_id, max(int(bad[0]), 0))!r}")
+        active = tuple(int(e) for e in host[2:2 + n_active].tolist())
+        E = self.num_experts
+        # One pinned row per expert: slot table (E entries) | count 1 | the id.
+        rows = torch.full((max(n_active, 1), E + 2), -1, dtype=torch.int32, pin_memory=True)
+        storage = self.cache.storage.view(self.cache.slot_count, -1)
+        stream = torch.cuda.current_stream(dev)
+        xs = ws = ys = act = None
+        with_tables = torch.empty(max(n_active, 1), E + 2, dtype=torch.int32, device=dev)
+        for j, (expert_id, lease) in enumerate(scheduler.experts(self.layer_id, active)):
+            with lease:
+                if xs is None:
+                    # The scheduler has submitted the real misses; gather now.
+                    xs, ws = ops.moe_gather(h, top_k_weights, d)
+                    ys = torch.empty(xs.shape[0], self.hidden_size, dtype=h.dtype, device=dev)
+                    act = torch.empty(max(xs.shape[0], 1), self.intermediate_size, dtype=h.dtype,
+                                      device=dev)
+                lease.wait(stream)
+                rows[j, expert_id] = lease.slot_id
+                rows[j, E] = 1
+                rows[j, E + 1] = expert_id
+                table = with_tables[j]
+                table.copy_(rows[j], non_blocking=True)
+                ops.grouped_swiglu(xs, ws, d, table[:E], storage, self.hidden_size,
+                                   self.intermediate_size, impl=self.swiglu_impl,
+                                   active=table[E + 1:], num_active=table[E:E + 1],
+                                   act_workspace=act, out=ys)
+        return ops.moe_combine(ys, d, top_k_index)
 
     # --------------------------------------------------------- validation
     def _validate_inputs(self, hidden_states, top_k_index, top_k_weights) -> None:

@@ -115,7 +115,18 @@ class LoadedB200Qwen3:
 
     model: torch.nn.Module
     caches: tuple
-    pool: ExpertHostPool | None
+    pool: ExpertHostPool | None = None
+
+    @property
+    def expert_caches(self) -> tuple:
+        """The reference's name for the per-layer caches."""
+        return self.caches
+
+    def _expert_modules(self) -> tuple:
+        modules = tuple(layer.mlp.experts for layer in self.model.model.layers)
+        if not all(isinstance(m, Qwen3OffloadedExperts) for m in modules):
+            raise RuntimeError("every decoder layer must contain offloaded experts")
+        return modules
 
     def cache_stats(self) -> dict:
         totals = dict(h2d_submissions=0, resident_hits=0, inflight_joins=0, evictions=0,
@@ -134,6 +145,8 @@ class LoadedB200Qwen3:
         for c in self.caches:
             c.cold_reset()
 
+    cold_reset_expert_caches = cold_reset_caches
+
     def warm_all_caches(self) -> None:
         """Fill every slot that can hold an expert (all experts when the
         cache is as large as the layer)."""
@@ -142,15 +155,49 @@ class LoadedB200Qwen3:
         torch.cuda.synchronize()
 
     def set_expert_execution_policy(self, policy) -> None:
-        for layer in self.model.model.layers:
-            layer.mlp.experts.execution_policy = ExpertExecutionPolicy(policy)
+        policy = ExpertExecutionPolicy(policy)
+        modules = self._expert_modules()
+        if any(m._prediction_scheduler is not None for m in modules):
+            raise RuntimeError("cannot switch execution policy during predicted prefetch")
+        for m in modules:
+            m.execution_policy = policy
+
+    def set_expert_h2d_prefetch(self, enabled: bool) -> None:
+        if type(enabled) is not bool:
+            raise ValueError("h2d_prefetch must be a boolean")
+        modules = self._expert_modules()
+        if any(m._prediction_scheduler is not None for m in modules):
+            raise RuntimeError("cannot switch H2D policy during predicted prefetch")
+        if any(c.closed or c.active_lease_count for c in self.caches):
+            raise RuntimeError("prefetch switching requires open caches without active leases")
+        for m in modules:
+            m.h2d_prefetch = enabled
+
+    def prefetch_experts(self, predictions, *, lookahead_layers: int = 1, max_inflight: int = 2,
+                         max_prefetch_per_layer: int | None = None, trace: bool = False,
+                         prediction_probabilities=None, eviction_policy: str = "lru"):
+        """A ``Qwen3ExpertPrefetch`` context for one forward
+        (``qwen3_offloaded_model.py:217-227``)."""
+        from .qwen3_expert_prefetch import Qwen3ExpertPrefetch
+
+        return Qwen3ExpertPrefetch(self, predictions, lookahead_layers=lookahead_layers,
+                                   max_inflight=max_inflight,
+                                   max_prefetch_per_layer=max_prefetch_per_layer, trace=trace,
+                                   prediction_probabilities=prediction_probabilities,
+                                   eviction_policy=eviction_policy)
 
     def close(self) -> None:
+        if any(getattr(layer.mlp.experts, "_prediction_scheduler", None) is not None
+               for layer in self.model.model.layers):
+            raise RuntimeError("cannot close the model during predicted prefetch")
         torch.cuda.synchronize()
         for c in self.caches:
             c.close()
         if self.pool is not None:
             self.pool.close()
+
+
+LoadedOffloadedQwen3 = LoadedB200Qwen3  # the reference's name
 
 
 def _init_layer_(module: torch.nn.Module, gen: torch.Generator, std: float) -> None:
