@@ -443,6 +443,26 @@ def b200_arm(args):
     e2e_ms, e2e_comm = timed_steps(runner.step_e2e, args.steps, 1, world, device)
     e2e_total = sum_over_ranks(sum(e2e_comm), world, device)
 
+    # The same passes under predicted cross-layer prefetch (the reference
+    # runner's Qwen3ExpertPrefetch: lookahead 1, 2 copies in flight), each
+    # pass predicted from the routes of the previous one.
+    routes: dict = {}
+    hooks = [layer.mlp.gate.register_forward_hook(
+        lambda mod, a, out, l=l: routes.__setitem__(l, out[2])) for l, layer in
+        enumerate(loaded.model.model.layers)]
+    runner.step_device()
+    for h in hooks:
+        h.remove()
+    preds = {l: tuple(sorted(set(r.reshape(-1).tolist()))) for l, r in routes.items()}
+
+    def step_prefetch():
+        with loaded.prefetch_experts(preds, lookahead_layers=1, max_inflight=2):
+            return runner.step_device()
+
+    pf_ms, pf_ams = timed_steps(step_prefetch, args.steps, args.warmup, world, device)
+    pf_committed = sum(len(tree.accepted_path(a.cpu().unsqueeze(0))) + 1 for a in pf_ams)
+    pf_value = sum_over_ranks(pf_committed, world, device) / (pf_ms / 1e3)
+
     result = {
         "metric": "committed tokens/s (Qwen3-30B-A3B shape, bs1)",
         "value": round(value, 4),
@@ -466,6 +486,10 @@ def b200_arm(args):
             "l2_flush": "not needed: each step streams > 57 GB of expert weights (>> 126 MB L2)",
         },
         "cache_stats_after_timing": stats24,
+        "predicted_prefetch": {"value": round(pf_value, 4), "unit": "tokens/s",
+                               "ms_per_step": round(pf_ms / args.steps, 3),
+                               "predictions": "routes of the previous verify pass",
+                               "lookahead_layers": 1, "max_inflight": 2},
         "gpu_launches": int(launches),
         "e2e": {"value": round(e2e_total / (e2e_ms / 1e3), 4), "unit": "tokens/s",
                 "h2d_bytes_per_step": runner.h2d_bytes, "d2h_bytes_per_step": runner.d2h_bytes,
