@@ -68,13 +68,19 @@ def parse_args(argv=None):
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
-    p.add_argument("--mode", choices=("auto", "verify", "ep", "block", "graph"), default="auto",
+    p.add_argument("--mode", choices=("auto", "verify", "ep", "decode", "block", "graph"), default="auto",
                    help="auto: verify on one GPU, ep under torchrun with N > 1; verify: BASELINE "
                         "config 2; ep: config 5 (8 requests, experts sharded over the ranks); "
+                        "decode: config 4 (end-to-end speculative decoding with a drafter stand-in "
+                        "and SpecFit selection); "
                         "block: the MoE verify block alone on one resident layer; graph: only the "
                         "resident (128-slot) verify pass replayed from a CUDA graph")
     p.add_argument("--requests", type=int, default=8, help="--mode ep: concurrent requests in total")
     p.add_argument("--ep-ctx", type=int, default=4096, help="--mode ep: context tokens per request")
+    p.add_argument("--decode-ctx", type=int, default=2048, help="--mode decode: context tokens")
+    p.add_argument("--new-tokens", type=int, default=256, help="--mode decode: tokens to generate")
+    p.add_argument("--eager-decode", action="store_true",
+                   help="--mode decode: verify passes without CUDA graphs")
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
     p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
                    help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
@@ -833,6 +839,174 @@ def ep_arm(args):
         print(json.dumps(result), flush=True)
 
 
+def cpu_decode_sample(cfg, verify_tokens: int, ctx: int, rows_per_level: int, levels: int):
+    """Host-core time of one speculative-decoding cycle of the reference's
+    CPU path: the Hugging Face decoder layer (SDPA under the tree mask over a
+    ``ctx``-token cache, stock sparse-MoE block) for ``verify_tokens`` rows,
+    scaled to all layers, plus the target lm_head, plus the drafter's GEMMs
+    (its decoder layer and lm_head over ``rows_per_level`` rows, ``levels``
+    times).  Returns (seconds per cycle, description, threads)."""
+    from transformers import DynamicCache
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import (Qwen3MoeDecoderLayer,
+                                                                   Qwen3MoeRotaryEmbedding)
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfgc = type(cfg).from_dict(cfg.to_dict())
+    cfgc._attn_implementation = "sdpa"
+    gen = torch.Generator().manual_seed(11)
+    layer = Qwen3MoeDecoderLayer(cfgc, 0).to(torch.bfloat16).eval()
+    H, V = cfgc.hidden_size, cfgc.vocab_size
+    bf = dict(dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.02, generator=gen)
+        rope = Qwen3MoeRotaryEmbedding(cfgc)
+        head = torch.randn(V, H, generator=gen).mul_(0.02).to(**bf)
+        kv = DynamicCache(config=cfgc)
+        ch = torch.randn(1, ctx, H, generator=gen).to(**bf)
+        cpos = torch.arange(ctx).unsqueeze(0)
+        layer(ch, attention_mask=None, position_ids=cpos, past_key_values=kv, use_cache=True,
+              position_embeddings=rope(ch, cpos))
+        x = torch.randn(1, verify_tokens, H, generator=gen).to(**bf)
+        mask = torch.ones(1, 1, verify_tokens, ctx + verify_tokens, dtype=torch.bool)
+        mask[..., ctx:] = torch.tril(torch.ones(verify_tokens, verify_tokens, dtype=torch.bool))
+        pos = torch.arange(ctx, ctx + verify_tokens).unsqueeze(0)
+        pe = rope(x, pos)
+
+        def one_layer():
+            layer(x, attention_mask=mask, position_ids=pos, past_key_values=kv, use_cache=True,
+                  position_embeddings=pe)
+            kv.crop(ctx)
+
+        one_layer()
+        t0 = time.perf_counter()
+        one_layer()
+        layer_s = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        torch.nn.functional.linear(x, head).argmax(-1)
+        head_s = time.perf_counter() - t0
+        # Drafter per level: q/k/v from [rows, 2H], o_proj, gate/up/down (6144), lm_head + top-k.
+        r = torch.randn(rows_per_level, 2 * H, generator=gen).to(**bf)
+        w_qkv = torch.randn(4096 + 2 * 512, 2 * H, generator=gen).to(**bf)
+        w_o = torch.randn(H, 4096, generator=gen).to(**bf)
+        w_gu = torch.randn(2 * 6144, H, generator=gen).to(**bf)
+        w_d = torch.randn(H, 6144, generator=gen).to(**bf)
+        hq = torch.randn(rows_per_level, H, generator=gen).to(**bf)
+        a_o = torch.randn(rows_per_level, 4096, generator=gen).to(**bf)
+        a_d = torch.randn(rows_per_level, 6144, generator=gen).to(**bf)
+        t0 = time.perf_counter()
+        torch.nn.functional.linear(r, w_qkv)
+        torch.nn.functional.linear(a_o, w_o)
+        torch.nn.functional.linear(hq, w_gu)
+        torch.nn.functional.linear(a_d, w_d)
+        torch.log_softmax(torch.nn.functional.linear(hq, head).float(), -1).topk(4)
+        level_s = time.perf_counter() - t0
+    cycle = layer_s * cfgc.num_hidden_layers + head_s + level_s * levels
+    desc = (f"HF Qwen3MoeDecoderLayer (sdpa, stock MoE) x1 on CPU at {verify_tokens} verify rows over a "
+            f"{ctx}-token cache, scaled to {cfgc.num_hidden_layers} layers, + lm_head, + drafter GEMMs "
+            f"({levels} levels x {rows_per_level} rows incl. the 151,936-way lm_head); bf16")
+    return cycle, desc, torch.get_num_threads()
+
+
+def decode_mode(args):
+    """end-to-end speculative decoding on one B200."""
+    from specfit_b200 import ops, synthetic
+    from specfit_b200.runtime.eagle3_drafter import build_random_drafter
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
+    from specfit_b200.runtime.speculator import B200TreeSpeculator, BernoulliAcceptance
+    from specfit_b200.selection import SelectionCostModel
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = qwen3_moe_config(args.layers)
+    t0 = time.perf_counter()
+    loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=cfg.num_experts, config=cfg,
+                                          seed=args.seed)
+    loaded.warm_all_caches()
+    L = cfg.num_hidden_layers
+    aux = (1, 23, 44) if L == 48 else tuple(sorted({1 % L, (L * 23) // 48, (L * 44) // 48}))
+    drafter = build_random_drafter(loaded.model, seed=args.seed + 1000, aux_layers=aux)
+    cost = SelectionCostModel(synthetic.SELECTION_SIZE_MEAN_NS, synthetic.SELECTION_INTERCEPT_NS,
+                              synthetic.SELECTION_EXPERT_NS)
+    gen = torch.Generator().manual_seed(1)
+    ctx_host = torch.randint(0, cfg.vocab_size, (1, args.decode_ctx), generator=gen).pin_memory()
+    spec = B200TreeSpeculator(loaded, drafter, cost_model=cost, acceptance=BernoulliAcceptance(0),
+                              route_seed=args.seed, graphs=not args.eager_decode,
+                              reserve_tokens=args.decode_ctx + args.new_tokens + 16)
+    setup_s = time.perf_counter() - t0
+
+    def run(new_tokens, acceptance_seed):
+        spec.acceptance = BernoulliAcceptance(acceptance_seed)
+        t = time.perf_counter()
+        ids = ctx_host.to(device, non_blocking=True)
+        res = spec.generate(ids, new_tokens)
+        return res, time.perf_counter() - t
+
+    for w in range(max(args.warmup, 1)):
+        run(32, 100 + w)
+    launches0 = ops.LAUNCHES[0]
+    with ClockSampler(device.index) as clocks:
+        res, wall = run(args.new_tokens, 7)
+    launches = ops.LAUNCHES[0] - launches0
+    cyc = res.cycles
+    value = res.committed / res.decode_s
+    mean = lambda xs: float(statistics.mean(xs)) if xs else 0.0
+    per_cycle = res.committed / max(len(cyc), 1)
+    result = {
+        "metric": "committed tokens/s (Qwen3-30B-A3B shape, EAGLE-3 drafting, bs1)",
+        "value": round(value, 3),
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": len(cyc),
+        "warmup": args.warmup,
+        "ms_per_step": round(res.decode_s * 1e3 / max(len(cyc), 1), 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init bf16 N(0,0.02) target and drafter, uniform random context; "
+                "per-token Zipf(1.1) routes; acceptance Bernoulli(p_depth), p_depth ~ Beta(4,2))",
+        "config": {
+            "workload": (f"BASELINE config 4: end-to-end speculative decoding, {args.layers}-layer "
+                         f"Qwen3-30B-A3B-shaped target (all 128 experts resident), EAGLE-3-shaped drafter "
+                         f"stand-in (1 layer, fc over target layers {list(aux)}, 151,936 vocab) drafting "
+                         f"60-node pools of depth <= 8, SpecFit exact selection (<= 7 nodes, the "
+                         f"reference's natural/legacy cost model), {args.decode_ctx}-token context, "
+                         f"{args.new_tokens} generated tokens"),
+            "step": "one speculative cycle (draft, select, verify, commit)",
+            "verify": "eager" if args.eager_decode else "one CUDA graph per tree size (1-8 rows)",
+            "l2_flush": "not needed: each verify pass reads the routed experts of every layer (GBs)",
+        },
+        "gpu_launches": int(launches),
+        "e2e": {"value": round(res.committed / wall, 3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(ctx_host.numel() * 8 / max(len(cyc), 1)),
+                "d2h_bytes_per_step": 8 * int(round(per_cycle)),
+                "includes": "context H2D, prefill of the context, every cycle, token read-back"},
+        "clocks": clocks.summary(),
+        "cycle": {"committed_per_cycle": round(per_cycle, 3),
+                  "selected_nodes_mean": round(mean([c.selected for c in cyc]), 3),
+                  "accepted_mean": round(mean([c.accepted for c in cyc]), 3),
+                  "pool_nodes_mean": round(mean([c.pool_nodes for c in cyc]), 2),
+                  "host_ms": {"draft": round(mean([c.draft_ms for c in cyc]), 3),
+                              "select": round(mean([c.select_ms for c in cyc]), 3),
+                              "verify": round(mean([c.verify_ms for c in cyc]), 3),
+                              "commit": round(mean([c.commit_ms for c in cyc]), 3)},
+                  "prefill_s": round(res.prefill_s, 3)},
+        "setup_s": round(setup_s, 1),
+    }
+    if not args.no_cpu_baseline:
+        vt = 1 + int(round(mean([c.selected for c in cyc])))
+        cycle_s, desc, cores = cpu_decode_sample(cfg, vt, args.decode_ctx, 8, 8)
+        result["cpu_baseline"] = {"value": round(per_cycle / cycle_s, 5), "unit": "tokens/s",
+                                  "cores": cores, "kind": "reference",
+                                  "sample": desc + f"; {per_cycle:.3f} committed tokens per cycle as "
+                                            "measured on the GPU run (same seeds)",
+                                  "seconds_per_cycle": round(cycle_s, 3)}
+    print(json.dumps(result), flush=True)
+    spec.release_graphs()
+    loaded.close()
+
+
 def reference_arm(args):
     rank, world, local = dist_info()
     if rank != 0:
@@ -952,6 +1126,8 @@ def main(argv=None):
         block_mode(args)
     elif args.mode == "graph":
         graph_mode(args)
+    elif args.mode == "decode":
+        decode_mode(args)
     elif args.mode == "ep" or (args.mode == "auto" and dist_info()[1] > 1):
         ep_arm(args)
     else:

@@ -1,0 +1,233 @@
+"""EAGLE-3-shaped tree drafter stand-in on the B200 kernels.
+
+The reference drafts with an EAGLE-3 model from ``speculators`` (absent here,
+so drafter parity is unpinned); BASELINE configuration 4 specifies a
+stand-in of the same shape with random weights: one decoder layer, hidden
+2048, an ``fc`` fusing the target's hidden states of layers (1, 23, 44)
+(``QWEN3_EAGLE3_LAYER_INDICES``, ``src/specfit/runtime/eagle3_chain.py:23``)
+into 2048, the target's token embedding, and a 151,936-way lm_head.
+
+Alignment (EAGLE): the drafter row of token ``x_p`` uses ``embed(x_p)`` and
+the fused target feature of position ``p - 1``; a drafted node uses its
+token's embedding and its parent's drafter output in place of the target
+feature.  Rows of committed tokens stay in the drafter's own KV buffer; a
+cycle's tree rows are appended after them and dropped after drafting, except
+the pending seed's row, which is exactly the committed row it will become.
+
+Random weights give a nearly flat softmax over 151,936 tokens (top-1 mass
+~1e-5), which would make every drafted node worthless to SpecFit; the
+stand-in therefore scales its logits by ``logit_scale`` (default 4.5, a
+logit standard deviation near 4, top-1 mass ~0.2-0.8) so its confidences are
+in the range of the simulated acceptance rates.
+
+Drafting (``build_candidate_pool``) grows a candidate pool level by level:
+level 1 holds the seed's ``first_width`` most likely children, and every
+later level the ``level_width`` most likely children (by cumulative
+log-probability) of the previous level's nodes, each node offering its
+``top_k`` most likely tokens, up to ``max_depth`` levels.  Attention runs on
+``sf_tree_attention`` (the committed rows as prefix, the tree rows under
+their ancestor mask); projections are cuBLAS GEMMs.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from .. import ops
+from .eagle3_types import Eagle3DraftCandidate, Eagle3DraftCandidatePool
+
+AUX_LAYERS = (1, 23, 44)
+
+
+def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+def _rope(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
+    """Rotary embedding (half-split convention) of ``x [heads, n, D]``."""
+    d = x.shape[-1]
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, device=x.device, dtype=torch.float32) / d))
+    ang = pos.float()[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    xf = x.float()
+    a, b = xf[..., : d // 2], xf[..., d // 2:]
+    return torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1).to(x.dtype)
+
+
+def _bits(rows: list, device) -> torch.Tensor:
+    """int32 words of per-row visibility bitsets (Python ints)."""
+    width = max(1, max((r.bit_length() for r in rows), default=1))
+    words = (width + 31) // 32
+    data = []
+    for r in rows:
+        for w in range(words):
+            word = (r >> (32 * w)) & 0xFFFFFFFF
+            data.append(word - (1 << 32) if word >= (1 << 31) else word)
+    return torch.tensor(data, dtype=torch.int32).view(len(rows), words).to(device)
+
+
+class Eagle3DrafterStandIn(nn.Module):
+    def __init__(self, *, hidden: int, heads: int, kv_heads: int, head_dim: int, inter: int,
+                 vocab: int, embed: nn.Embedding, rope_theta: float, eps: float,
+                 aux_layers=AUX_LAYERS, logit_scale: float = 4.5, device=None,
+                 dtype=torch.bfloat16) -> None:
+        super().__init__()
+        self.hidden, self.heads, self.kv_heads, self.head_dim = hidden, heads, kv_heads, head_dim
+        self.vocab, self.theta, self.eps = vocab, rope_theta, eps
+        self.logit_scale = float(logit_scale)
+        self.layer_indices = tuple(aux_layers)
+        kw = dict(device=device, dtype=dtype)
+        self.fc = nn.Linear(len(self.layer_indices) * hidden, hidden, bias=False, **kw)
+        self.emb_norm = nn.Parameter(torch.ones(hidden, **kw))
+        self.hid_norm = nn.Parameter(torch.ones(hidden, **kw))
+        self.q_proj = nn.Linear(2 * hidden, heads * head_dim, bias=False, **kw)
+        self.k_proj = nn.Linear(2 * hidden, kv_heads * head_dim, bias=False, **kw)
+        self.v_proj = nn.Linear(2 * hidden, kv_heads * head_dim, bias=False, **kw)
+        self.o_proj = nn.Linear(heads * head_dim, hidden, bias=False, **kw)
+        self.post_norm = nn.Parameter(torch.ones(hidden, **kw))
+        self.gate_proj = nn.Linear(hidden, inter, bias=False, **kw)
+        self.up_proj = nn.Linear(hidden, inter, bias=False, **kw)
+        self.down_proj = nn.Linear(inter, hidden, bias=False, **kw)
+        self.final_norm = nn.Parameter(torch.ones(hidden, **kw))
+        self.lm_head = nn.Linear(hidden, vocab, bias=False, **kw)
+        self.embed = embed  # the target's token embedding (shared, not re-drawn)
+        self._k = self._v = None
+        self._len = 0  # rows of committed tokens (and the kept seed row) in the KV buffer
+        self._fed = 0  # committed tokens those rows cover
+
+    # ---------------------------------------------------------------- state
+    def begin_generation(self, capacity: int) -> None:
+        dev = self.fc.weight.device
+        shape = (self.kv_heads, capacity, self.head_dim)
+        self._k = torch.zeros(shape, dtype=self.fc.weight.dtype, device=dev)
+        self._v = torch.zeros(shape, dtype=self.fc.weight.dtype, device=dev)
+        self._len = self._fed = 0
+
+    def end_generation(self) -> None:
+        self._k = self._v = None
+        self._len = self._fed = 0
+
+    # --------------------------------------------------------------- forward
+    def _rows(self, tokens: torch.Tensor, feats: torch.Tensor, pos: torch.Tensor,
+              bits: torch.Tensor | None, prefix: int) -> torch.Tensor:
+        """Drafter layer over ``n`` rows appended at ``self._len``; returns
+        the layer output ``[n, H]`` (rows stay in the buffer)."""
+        n = tokens.shape[0]
+        if self._len + n > self._k.shape[1]:
+            raise RuntimeError("drafter KV buffer is full")
+        x = torch.cat((_rms_norm(self.embed(tokens), self.emb_norm, self.eps),
+                       _rms_norm(feats, self.hid_norm, self.eps)), dim=-1)
+        q = self.q_proj(x).view(n, self.heads, self.head_dim).transpose(0, 1)
+        k = self.k_proj(x).view(n, self.kv_heads, self.head_dim).transpose(0, 1)
+        v = self.v_proj(x).view(n, self.kv_heads, self.head_dim).transpose(0, 1)
+        q = _rope(q, pos, self.theta).contiguous()
+        end = self._len + n
+        self._k[:, self._len:end].copy_(_rope(k, pos, self.theta))
+        self._v[:, self._len:end].copy_(v)
+        self._len = end
+        attn = ops.tree_attention(q, self._k[:, :end], self._v[:, :end], bits, prefix,
+                                  scale=self.head_dim ** -0.5)
+        h = feats + self.o_proj(attn.reshape(n, self.heads * self.head_dim))
+        m = _rms_norm(h, self.post_norm, self.eps)
+        return h + self.down_proj(torch.nn.functional.silu(self.gate_proj(m)) * self.up_proj(m))
+
+    def _log_probs(self, h: torch.Tensor) -> torch.Tensor:
+        logits = self.lm_head(_rms_norm(h, self.final_norm, self.eps)).float()
+        return torch.log_softmax(logits * self.logit_scale, dim=-1)
+
+    # -------------------------------------------------------------- drafting
+    def build_candidate_pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
+                             pending_seed: torch.Tensor, top_k: int = 4, max_depth: int = 8,
+                             first_width: int = 4, level_width: int = 8) -> Eagle3DraftCandidatePool:
+        """``fed_ids [1, L]`` committed tokens, ``aux_history [L, 3H]`` their
+        target features (layers ``layer_indices`` concatenated), the pending
+        seed ``[1, 1]``.  Returns the candidate pool in generation order."""
+        dev = self.fc.weight.device
+        L = fed_ids.shape[1]
+        if aux_history.shape[0] != L:
+            raise ValueError("aux history must cover every fed token")
+        # Rows of the newly committed tokens (catch-up) and the seed row: token
+        # p uses the target feature of position p - 1 (zero for p = 0).
+        start = self._fed
+        feats = self.fc(aux_history[max(start - 1, 0):L])
+        if start == 0:
+            feats = torch.cat((torch.zeros_like(feats[:1]), feats), dim=0)
+        toks = torch.cat((fed_ids[0, start:L], pending_seed.reshape(1)))
+        n_new = toks.shape[0]
+        pos = torch.arange(start, L + 1, device=dev)
+        chain = [(1 << (i + 1)) - 1 for i in range(n_new)]  # causal among the new rows
+        h = self._rows(toks, feats, pos, _bits(chain, dev), self._len)
+        committed_rows = self._len - 1  # the tree block starts at the seed row
+        seed_hidden = h[-1]
+        vals, idx = torch.topk(self._log_probs(h[-1:])[0], min(top_k, first_width))
+        cands: list = []
+        vis = {0: 1}  # raw id -> visibility bitset inside the tree block (seed = bit 0)
+        rows_in_block = 1
+        hidden_of = {0: seed_hidden}
+        frontier = []
+        for v, t in zip(vals.tolist(), idx.tolist()):
+            raw = len(cands) + 1
+            cands.append(Eagle3DraftCandidate(raw, 0, 1, int(t), float(v), float(v), raw - 1, (int(t),)))
+            frontier.append(raw)
+        steps = 1
+        for depth in range(1, max_depth):
+            rows = []
+            for j, raw in enumerate(frontier):
+                vis[raw] = vis[cands[raw - 1].parent_raw_id] | (1 << (rows_in_block + j))
+                rows.append(vis[raw])
+            rows_in_block += len(frontier)
+            tok = torch.tensor([cands[r - 1].target_token_id for r in frontier], device=dev)
+            parent_feats = torch.stack([hidden_of[cands[r - 1].parent_raw_id] for r in frontier])
+            lvl_pos = torch.full((len(frontier),), L + depth, device=dev)
+            hl = self._rows(tok, parent_feats, lvl_pos, _bits(rows, dev), committed_rows)
+            steps += 1
+            for j, raw in enumerate(frontier):
+                hidden_of[raw] = hl[j]
+            v, t = torch.topk(self._log_probs(hl), top_k, dim=-1)
+            options = []
+            for j, raw in enumerate(frontier):
+                base = cands[raw - 1].cumulative_log_probability
+                for vv, tt in zip(v[j].tolist(), t[j].tolist()):
+                    options.append((base + vv, raw, int(tt), float(vv)))
+            options.sort(key=lambda o: (-o[0], o[1], o[2]))
+            frontier = []
+            for _, parent, tok_id, cond in options[:level_width]:
+                p = cands[parent - 1]
+                raw = len(cands) + 1
+                cands.append(Eagle3DraftCandidate(raw, parent, depth + 1, tok_id, cond,
+                                                  p.cumulative_log_probability + cond, raw - 1,
+                                                  p.path + (tok_id,)))
+                frontier.append(raw)
+        # Keep the committed rows and the seed row; drop the tree rows.
+        self._len = committed_rows + 1
+        self._fed = L + 1
+        return Eagle3DraftCandidatePool(int(pending_seed.reshape(-1)[0]), top_k, max_depth,
+                                        tuple(cands), path_score_calls=steps,
+                                        draft_transformer_steps=steps, draft_forward_calls=steps,
+                                        draft_query_tokens=n_new + rows_in_block - 1)
+
+
+def build_random_drafter(target, *, seed: int = 0, std: float = 0.02, inter: int = 6144,
+                         aux_layers=AUX_LAYERS, logit_scale: float = 4.5) -> Eagle3DrafterStandIn:
+    """Random-init stand-in shaped for ``target`` (a Qwen3-MoE HF model),
+    sharing its token embedding; weights N(0, std) from ``seed``."""
+    cfg = target.config
+    dev = target.model.embed_tokens.weight.device
+    d = Eagle3DrafterStandIn(hidden=cfg.hidden_size, heads=cfg.num_attention_heads,
+                             kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, inter=inter,
+                             vocab=cfg.vocab_size, embed=target.model.embed_tokens,
+                             rope_theta=cfg.rope_parameters["rope_theta"], eps=cfg.rms_norm_eps,
+                             aux_layers=aux_layers, logit_scale=logit_scale, device=dev,
+                             dtype=target.model.embed_tokens.weight.dtype)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in sorted(d.named_parameters(), key=lambda kv: kv[0]):
+            if name.startswith("embed."):
+                continue
+            if p.ndim == 1:
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, std, generator=g)
+    d.eval()
+    return d

@@ -141,3 +141,144 @@ class Eagle3DraftTree:
             parent = match[0]
             accepted.append(parent)
         return tuple(accepted)
+
+
+def _check_nonneg_int(value, message: str) -> None:
+    if not _is_int(value) or value < 0:
+        raise ValueError(message)
+
+
+@dataclass(frozen=True, slots=True)
+class Eagle3DraftCandidate:
+    """One drafted candidate (``src/specfit/runtime/eagle3_types.py:86-143``):
+    raw ids count from 1 in generation order, parents precede children."""
+
+    raw_id: int
+    parent_raw_id: int
+    depth: int
+    target_token_id: int
+    conditional_log_probability: float
+    cumulative_log_probability: float
+    generation_ordinal: int
+    path: tuple
+
+    def __post_init__(self) -> None:
+        if not _is_int(self.raw_id) or self.raw_id <= 0:
+            raise ValueError("candidate raw IDs must be positive integers")
+        if not _is_int(self.parent_raw_id) or not 0 <= self.parent_raw_id < self.raw_id:
+            raise ValueError("candidate parents must precede their children")
+        if not _is_int(self.depth) or self.depth <= 0:
+            raise ValueError("candidate depths must be positive integers")
+        _check_nonneg_int(self.target_token_id, "candidate token IDs must be non-negative integers")
+        if not isfinite(self.conditional_log_probability) or self.conditional_log_probability > 0.0:
+            raise ValueError("conditional log probabilities must be finite and <= 0")
+        if not isfinite(self.cumulative_log_probability):
+            raise ValueError("cumulative log probabilities must be finite")
+        _check_nonneg_int(self.generation_ordinal, "generation ordinals must be non-negative integers")
+        if not isinstance(self.path, tuple):
+            raise ValueError("candidate paths must be immutable tuples")
+        if len(self.path) != self.depth or self.path[-1] != self.target_token_id:
+            raise ValueError("candidate path must end at the candidate token")
+
+    @property
+    def conditional_probability(self) -> float:
+        from math import exp
+
+        return exp(self.conditional_log_probability)
+
+
+@dataclass(frozen=True, slots=True)
+class Eagle3DraftCandidatePool:
+    """A drafted candidate pool (``eagle3_types.py:146-300``) and its
+    ancestor-closed sub-trees (``to_tree``)."""
+
+    seed_token_id: int
+    top_k: int
+    max_depth: int
+    candidates: tuple
+    path_score_calls: int
+    draft_transformer_steps: int
+    draft_forward_calls: int = 0
+    draft_query_tokens: int = 0
+
+    def __post_init__(self) -> None:
+        _check_nonneg_int(self.seed_token_id, "candidate-pool seed must be a non-negative token ID")
+        if not _is_int(self.top_k) or self.top_k <= 0:
+            raise ValueError("candidate-pool top_k must be a positive integer")
+        if not _is_int(self.max_depth) or self.max_depth <= 0:
+            raise ValueError("candidate-pool depth must be a positive integer")
+        if not isinstance(self.candidates, tuple) or not self.candidates:
+            raise ValueError("candidate pool must contain at least one node")
+        if not _is_int(self.path_score_calls) or self.path_score_calls <= 0:
+            raise ValueError("path_score_calls must be a positive integer")
+        if not _is_int(self.draft_transformer_steps) or self.draft_transformer_steps < self.path_score_calls:
+            raise ValueError("draft_transformer_steps must cover every path score call")
+        for name in ("draft_forward_calls", "draft_query_tokens"):
+            _check_nonneg_int(getattr(self, name), f"{name} must be a non-negative integer")
+        seen: dict = {}
+        sibling_tokens: dict = {}
+        for expected, c in enumerate(self.candidates, start=1):
+            if c.raw_id != expected:
+                raise ValueError("candidate raw IDs must be consecutive")
+            if c.generation_ordinal != expected - 1:
+                raise ValueError("candidate ordinals must follow generation order")
+            if c.depth > self.max_depth:
+                raise ValueError("candidate depth exceeds the pool depth")
+            if c.parent_raw_id == 0:
+                pdepth, ppath, pscore = 0, (), 0.0
+            else:
+                parent = seen.get(c.parent_raw_id)
+                if parent is None:
+                    raise ValueError("candidate parent is absent from the pool")
+                pdepth, ppath, pscore = parent.depth, parent.path, parent.cumulative_log_probability
+            if c.depth != pdepth + 1:
+                raise ValueError("candidate depth differs from its parent")
+            if c.path != ppath + (c.target_token_id,):
+                raise ValueError("candidate path differs from its parent path")
+            if not isclose(c.cumulative_log_probability, pscore + c.conditional_log_probability,
+                           rel_tol=1e-5, abs_tol=1e-6):
+                raise ValueError("candidate cumulative score is inconsistent")
+            toks = sibling_tokens.setdefault(c.parent_raw_id, set())
+            if c.target_token_id in toks:
+                raise ValueError("candidate siblings must use distinct token IDs")
+            toks.add(c.target_token_id)
+            seen[c.raw_id] = c
+
+    @property
+    def nodes(self) -> tuple:
+        """The candidates, under the name the selection code reads."""
+        return self.candidates
+
+    @property
+    def raw_candidate_count(self) -> int:
+        return len(self.candidates)
+
+    @property
+    def actual_depth(self) -> int:
+        return max(c.depth for c in self.candidates)
+
+    def to_tree(self, selected_raw_ids: tuple) -> Eagle3DraftTree:
+        if not isinstance(selected_raw_ids, tuple):
+            raise ValueError("selected raw IDs must be an immutable tuple")
+        if any(not _is_int(r) or r <= 0 for r in selected_raw_ids):
+            raise ValueError("selected raw IDs must be positive integers")
+        if len(set(selected_raw_ids)) != len(selected_raw_ids):
+            raise ValueError("selected raw IDs must be unique")
+        by_raw = {c.raw_id: c for c in self.candidates}
+        try:
+            chosen = [by_raw[r] for r in selected_raw_ids]
+        except KeyError as error:
+            raise ValueError("selected raw ID is absent from the pool") from error
+        keep = set(selected_raw_ids)
+        if any(c.parent_raw_id != 0 and c.parent_raw_id not in keep for c in chosen):
+            raise ValueError("selected candidates must be ancestor-closed")
+        chosen.sort(key=lambda c: c.generation_ordinal)
+        node_of = {c.raw_id: i for i, c in enumerate(chosen, start=1)}
+        return Eagle3DraftTree(
+            token_ids=tuple(c.target_token_id for c in chosen),
+            parent_ids=tuple(0 if c.parent_raw_id == 0 else node_of[c.parent_raw_id] for c in chosen),
+            depths=tuple(c.depth for c in chosen),
+            conditional_probabilities=tuple(c.conditional_probability for c in chosen),
+            cumulative_log_probabilities=tuple(c.cumulative_log_probability for c in chosen),
+            source_raw_ids=tuple(c.raw_id for c in chosen),
+        )

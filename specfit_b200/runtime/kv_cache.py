@@ -13,6 +13,12 @@ with row stride D and head stride capacity*D.
 
 Because the buffers never move, a CUDA graph captured over a verify pass
 writes the same rows on every replay, and rolling back is ``crop``.
+
+Static mode (``ReservedCache.set_static``) serves graphs that must work at
+any committed length: ``update`` writes at the device-side offset and returns
+the whole reserved buffer, and the attention mask (over all reserved rows)
+decides what is visible.  Buffers start zeroed, so rows never written hold
+finite values that a zero attention weight cancels.
 """
 from __future__ import annotations
 
@@ -29,13 +35,16 @@ class ReservedLayer(DynamicLayer):
         self.length = 0
         self._kbuf = None
         self._vbuf = None
+        self.static_offset = None  # device int64 scalar: write position in static mode
+        self.static_length = 0     # sequence length reported in static mode
+        self._arange = None
 
     def lazy_initialization(self, key_states: torch.Tensor, value_states: torch.Tensor) -> None:
         self.dtype, self.device = key_states.dtype, key_states.device
         b, h, n, d = key_states.shape
         cap = max(self.capacity, n)
-        self._kbuf = torch.empty(b, h, cap, d, dtype=self.dtype, device=self.device)
-        self._vbuf = torch.empty(b, h, cap, value_states.shape[-1], dtype=self.dtype, device=self.device)
+        self._kbuf = torch.zeros(b, h, cap, d, dtype=self.dtype, device=self.device)
+        self._vbuf = torch.zeros(b, h, cap, value_states.shape[-1], dtype=self.dtype, device=self.device)
         self.capacity = cap
         self.length = 0
         self._publish()
@@ -47,8 +56,8 @@ class ReservedLayer(DynamicLayer):
 
     def _grow(self, need: int) -> None:
         cap = max(need, 2 * self.capacity)
-        k = torch.empty(*self._kbuf.shape[:2], cap, self._kbuf.shape[3], dtype=self.dtype, device=self.device)
-        v = torch.empty(*self._vbuf.shape[:2], cap, self._vbuf.shape[3], dtype=self.dtype, device=self.device)
+        k = torch.zeros(*self._kbuf.shape[:2], cap, self._kbuf.shape[3], dtype=self.dtype, device=self.device)
+        v = torch.zeros(*self._vbuf.shape[:2], cap, self._vbuf.shape[3], dtype=self.dtype, device=self.device)
         k[..., : self.length, :].copy_(self._kbuf[..., : self.length, :])
         v[..., : self.length, :].copy_(self._vbuf[..., : self.length, :])
         self._kbuf, self._vbuf, self.capacity = k, v, cap
@@ -58,6 +67,14 @@ class ReservedLayer(DynamicLayer):
             self.lazy_initialization(key_states, value_states)
         if key_states.shape[:2] != self._kbuf.shape[:2]:
             raise ValueError("batch or head count differs from the reserved cache")
+        if self.static_offset is not None:
+            n = key_states.shape[-2]
+            if self._arange is None or self._arange.numel() < n:
+                self._arange = torch.arange(max(n, 16), device=self.device)
+            rows = self.static_offset + self._arange[:n]
+            self._kbuf.index_copy_(-2, rows, key_states)
+            self._vbuf.index_copy_(-2, rows, value_states)
+            return self._kbuf, self._vbuf
         end = self.length + key_states.shape[-2]
         if end > self.capacity:
             self._grow(end)
@@ -68,6 +85,8 @@ class ReservedLayer(DynamicLayer):
         return self.keys, self.values
 
     def get_seq_length(self) -> int:
+        if self.static_offset is not None:
+            return self.static_length
         return self.length if self.is_initialized else 0
 
     def crop(self, max_length: int) -> None:
@@ -99,3 +118,47 @@ class ReservedCache(DynamicCache):
         super().__init__(config=config)
         self.layers = [ReservedLayer(capacity) if type(layer) is DynamicLayer else layer
                        for layer in self.layers]
+
+    def set_static(self, offset: torch.Tensor | None, reported_length: int = 0) -> None:
+        """Enter static mode (writes at the device scalar ``offset``, whole
+        buffers returned, ``reported_length`` as the sequence length) or, with
+        ``None``, leave it."""
+        for layer in self.layers:
+            if isinstance(layer, ReservedLayer):
+                if offset is not None and not layer.is_initialized:
+                    raise RuntimeError("static mode needs initialised layers (run a prefill first)")
+                layer.static_offset = offset
+                layer.static_length = reported_length
+
+    def set_length(self, length: int) -> None:
+        """Host-side length of every reserved layer (after a static pass)."""
+        for layer in self.layers:
+            if isinstance(layer, ReservedLayer):
+                if length > layer.capacity:
+                    raise ValueError("length exceeds the reserved capacity")
+                layer.length = length
+                layer._publish()
+
+
+def compact_tree_cache_(cache, *, base_kv_length: int, verification_positions: tuple,
+                        verification_node_count: int) -> None:
+    """Keep the accepted verification rows: rows ``base + p`` for ``p`` in
+    ``verification_positions`` move to ``base, base + 1, ...`` and the cache
+    is cropped after them (``_compact_tree_cache``,
+    src/specfit/runtime/eagle3_tree.py:833-858).  Works on any cache whose
+    layers expose ``keys`` / ``values``; reserved layers move rows inside
+    their buffers."""
+    expected = base_kv_length + verification_node_count
+    src = None
+    n = len(verification_positions)
+    for layer in cache.layers:
+        if layer.get_seq_length() != expected:
+            raise RuntimeError("target cache layer has an unexpected length")
+        if src is None or src.device != layer.keys.device:
+            src = torch.tensor([base_kv_length + p for p in verification_positions], dtype=torch.long,
+                               device=layer.keys.device)
+        k = layer.keys.index_select(-2, src)  # owns its result: overlapping moves are safe
+        v = layer.values.index_select(-2, src)
+        layer.keys[..., base_kv_length:base_kv_length + n, :].copy_(k)
+        layer.values[..., base_kv_length:base_kv_length + n, :].copy_(v)
+    cache.crop(base_kv_length + n)

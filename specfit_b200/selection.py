@@ -117,6 +117,19 @@ def _footprint_rows(routes: np.ndarray) -> np.ndarray:
     return out
 
 
+def footprints(routes: np.ndarray, experts: int = EXPERTS) -> np.ndarray:
+    """Any-shape packing: ``routes`` int [tokens, layers, top_k] ->
+    uint64 [tokens, ceil(layers * experts / 64)] with bit layer*experts+expert."""
+    r = np.ascontiguousarray(routes, dtype=np.int32)
+    if r.ndim != 3:
+        raise ValueError("routes must be [tokens, layers, top_k]")
+    words = (r.shape[1] * experts + 63) // 64
+    out = np.empty((r.shape[0], words), dtype=np.uint64)
+    N.check(N.lib.sf_specfit_pack_routes(r.ctypes.data, r.shape[0], r.shape[1], r.shape[2], experts,
+                                         out.ctypes.data, words), "sf_specfit_pack_routes")
+    return out
+
+
 def pack_routes(pool, atlas) -> np.ndarray:
     """Validate complete top-8 routes of the seed (raw 0) and every node and
     pack them (cf. ``_pack_routes``, ``specfit_exact.py:18-49``)."""

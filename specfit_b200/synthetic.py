@@ -141,6 +141,9 @@ SELECTION_INTERCEPT_NS = (142213640.2719444, 147532305.64501184, 150522238.97474
                           152268786.28951707, 152742629.59439692, 163203998.73306817,
                           155175323.9989069, 156067696.05019823)
 SELECTION_EXPERT_NS = 210715.51267433458
+# Mean pass time per node count of the same (natural, legacy) model.
+SELECTION_SIZE_MEAN_NS = (223128397.1388889, 274429869.9444444, 306112232.25, 334490879.0833333,
+                          357604933.5833333, 389313450.25, 394875926.0833333, 410155485.0833333)
 
 
 @dataclass(frozen=True)
@@ -190,3 +193,33 @@ def selection_case(seed: int, nodes: int, *, shared_routes: bool = False, level_
         count = int(min(48, rng.binomial(128, resident_frac)))
         resident[layer, rng.permutation(128)[:count]] = True
     return SelectionCase(tuple(parents), tuple(depths), tuple(cum), routes.astype(np.int64), resident)
+
+
+def token_routes(tokens, layers: int = NUM_LAYERS, *, experts: int = NUM_EXPERTS, top_k: int = TOP_K,
+                 s: float = 1.1, seed: int = 0):
+    """Configuration 4: a token's route at every layer, Zipf(s) over experts
+    under a per-layer permutation, ``top_k`` distinct experts drawn by
+    Gumbel-top-k whose uniforms are a hash of (seed, layer, token, expert).
+    The same token always takes the same route, so a drafted candidate's
+    expert footprint is known before it is verified.  ``tokens``: int64
+    tensor ``[n]`` on any device; returns int64 ``[n, layers, top_k]`` on
+    that device."""
+    dev = tokens.device
+    t = tokens.to(torch.int64).reshape(-1, 1, 1)
+    l = torch.arange(layers, device=dev, dtype=torch.int64).reshape(1, -1, 1)
+    e = torch.arange(experts, device=dev, dtype=torch.int64).reshape(1, 1, -1)
+    mask = (1 << 62) - 1
+    x = ((seed * 1_000_003 + l) * 1_000_033 + t) * 131 + e
+    # multiply-xorshift mixing kept below 2**62, so int64 never overflows
+    for mult, shift in ((0x1CE4E5B9, 29), (0x133111EB, 31), (0x2545F491, 27)):
+        x = (x * mult) & mask
+        x = x ^ (x >> shift)
+    u = ((x & ((1 << 52) - 1)).to(torch.float64) + 0.5) / float(1 << 52)
+    gumbel = -torch.log(-torch.log(u))
+    rng = np.random.default_rng(seed * 7919 + 17)
+    perms = np.stack([rng.permutation(experts) for _ in range(layers)])
+    ranks = np.empty((layers, experts), dtype=np.float64)
+    for li in range(layers):
+        ranks[li, perms[li]] = np.arange(1, experts + 1)
+    logw = torch.from_numpy(-s * np.log(ranks)).to(dev).unsqueeze(0)
+    return torch.topk(logw + gumbel, top_k, dim=-1).indices

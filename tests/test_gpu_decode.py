@@ -1,0 +1,105 @@
+"""End-to-end speculative decoding on the GPU (configuration 4 pieces).
+
+* The drafter stand-in grows a valid candidate pool (4 + 8 per level, depth
+  <= 8) whose scores are its own log-probabilities.
+* ``B200TreeSpeculator.generate`` commits exactly the requested number of
+  tokens; after every cycle's in-place compaction the KV cache holds the
+  context plus every committed token but the pending one.
+* Commit audit: the compacted cache rows equal, within bf16 tolerance, the
+  rows a plain causal forward over the same committed sequence produces
+  (the reference's commit audit compares the same rows), with eager verify
+  passes and with the per-tree-size CUDA graphs over the static cache."""
+import pytest
+import torch
+
+from specfit_b200 import synthetic
+from specfit_b200.runtime.eagle3_drafter import build_random_drafter
+from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
+from specfit_b200.runtime.speculator import B200TreeSpeculator, BernoulliAcceptance
+from specfit_b200.selection import SelectionCostModel
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def small():
+    cfg = qwen3_moe_config(3, hidden=256, experts=16, top_k=4, moe_inter=128, heads=8, kv_heads=2,
+                           head_dim=128, vocab=512)
+    m = build_random_offloaded_qwen3(device=DEV, slots_per_layer=16, config=cfg, seed=6, std=0.05)
+    m.warm_all_caches()
+    d = build_random_drafter(m.model, seed=9, std=0.05, inter=512, aux_layers=(0, 1, 2))
+    return cfg, m, d
+
+
+def cost():
+    return SelectionCostModel(synthetic.SELECTION_SIZE_MEAN_NS, synthetic.SELECTION_INTERCEPT_NS,
+                              synthetic.SELECTION_EXPERT_NS)
+
+
+def test_drafter_pool_shape():
+    cfg, m, d = small()
+    try:
+        ids = torch.randint(0, 512, (1, 30), generator=torch.Generator().manual_seed(1)).to(DEV)
+        d.begin_generation(200)
+        aux = torch.randn(30, 3 * 256, device=DEV).to(torch.bfloat16)
+        pool = d.build_candidate_pool(fed_ids=ids, aux_history=aux, pending_seed=ids[:, -1:],
+                                      top_k=4, max_depth=8, first_width=4, level_width=8)
+        assert len(pool.candidates) == 4 + 8 * 7
+        assert pool.actual_depth == 8
+        assert sum(c.depth == 1 for c in pool.candidates) == 4
+        assert all(c.cumulative_log_probability <= 0 for c in pool.candidates)
+        assert d._len == 31  # committed rows + the seed row
+        d.end_generation()
+    finally:
+        m.close()
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_generate_commits_and_audit_matches_causal_forward(graphs):
+    from transformers import DynamicCache
+
+    import specfit_b200.runtime.speculator as sp
+
+    cfg, m, d = small()
+    try:
+        ctx = torch.randint(0, 512, (1, 40), generator=torch.Generator().manual_seed(2)).to(DEV)
+        spec = B200TreeSpeculator(m, d, cost_model=cost(), acceptance=BernoulliAcceptance(3),
+                                  graphs=graphs)
+        keep = {}
+        real = sp.compact_tree_cache_
+
+        def spy(cache, **kw):  # keep the cache of the last compaction
+            real(cache, **kw)
+            keep["cache"] = cache
+        sp.compact_tree_cache_ = spy
+        try:
+            res = spec.generate(ctx, 24)
+        finally:
+            sp.compact_tree_cache_ = real
+        assert res.committed == 24
+        assert all(c.selected <= 7 and c.accepted <= c.selected for c in res.cycles)
+        assert sum(c.selected for c in res.cycles) > 0  # SpecFit verifies drafted nodes
+        cache = keep["cache"]
+        n = cache.get_seq_length() - 40
+        assert 0 < n <= 24
+        # Causal forward over the context + the committed tokens held in the
+        # cache, with the per-token routes the verify passes used.
+        seq = torch.cat((ctx, torch.tensor([res.tokens[:n]], device=DEV)), dim=1)
+        routes = synthetic.token_routes(seq[0], cfg.num_hidden_layers, experts=16, top_k=4)
+        hooks = [layer.mlp.gate.register_forward_hook(
+            lambda mod, a, out, l=l: (out[0], out[1], routes[40:, l, :]) if out[2].shape[0] == n else None)
+            for l, layer in enumerate(m.model.model.layers)]
+        try:
+            ref = DynamicCache(config=m.model.config)
+            with torch.no_grad():
+                m.model(input_ids=seq[:, :40], past_key_values=ref, use_cache=True)
+                m.model(input_ids=seq[:, 40:], past_key_values=ref, use_cache=True)
+        finally:
+            for h in hooks:
+                h.remove()
+        for a, b in zip(cache.layers, ref.layers):
+            assert torch.allclose(a.keys[..., 40:, :].float(), b.keys[..., 40:, :].float(), atol=2e-2, rtol=0)
+            assert torch.allclose(a.values[..., 40:, :].float(), b.values[..., 40:, :].float(), atol=2e-2, rtol=0)
+        spec.release_graphs()
+    finally:
+        m.close()
