@@ -27,6 +27,13 @@ log-probability) of the previous level's nodes, each node offering its
 ``top_k`` most likely tokens, up to ``max_depth`` levels.  Attention runs on
 ``sf_tree_attention`` (the committed rows as prefix, the tree rows under
 their ancestor mask); projections are cuBLAS GEMMs.
+
+``DeviceDraft`` runs the same drafting with no host round trip: the level
+expansions (top-k per node, cumulative scores, the best ``level_width``
+children) are tensor ops, rows are written at device-side offsets, each
+row's visibility is a 64-bit ancestor set inside the tree block expanded
+into a mask over the whole KV buffer, and the pool comes back in one copy.
+Its fixed shapes let it be one CUDA graph per number of catch-up rows.
 """
 from __future__ import annotations
 
@@ -98,13 +105,22 @@ class Eagle3DrafterStandIn(nn.Module):
 
     # ---------------------------------------------------------------- state
     def begin_generation(self, capacity: int) -> None:
-        dev = self.fc.weight.device
-        shape = (self.kv_heads, capacity, self.head_dim)
-        self._k = torch.zeros(shape, dtype=self.fc.weight.dtype, device=dev)
-        self._v = torch.zeros(shape, dtype=self.fc.weight.dtype, device=dev)
+        """Start a sequence; the KV buffer (``capacity`` rows, rounded up to
+        a multiple of 32) is kept and reused while it is large enough, so
+        graphs captured over it stay valid."""
+        capacity = (capacity + 31) // 32 * 32
+        if self._k is None or self._k.shape[1] < capacity:
+            dev = self.fc.weight.device
+            shape = (self.kv_heads, capacity, self.head_dim)
+            self._k = torch.zeros(shape, dtype=self.fc.weight.dtype, device=dev)
+            self._v = torch.zeros(shape, dtype=self.fc.weight.dtype, device=dev)
         self._len = self._fed = 0
 
     def end_generation(self) -> None:
+        self._len = self._fed = 0
+
+    def release(self) -> None:
+        """Free the KV buffer."""
         self._k = self._v = None
         self._len = self._fed = 0
 
@@ -231,3 +247,166 @@ def build_random_drafter(target, *, seed: int = 0, std: float = 0.02, inter: int
                 p.normal_(0.0, std, generator=g)
     d.eval()
     return d
+
+
+class DeviceDraft:
+    """Graph-capturable drafting for one drafter and fixed widths.
+
+    The drafter's KV buffer must have been started with ``begin_generation``
+    and its committed rows filled by one eager ``build_candidate_pool`` (the
+    prefill catch-up).  ``pool`` then drafts a full ``max_depth`` pool from up
+    to ``max_new`` new rows (the newly committed tokens and the pending seed),
+    replaying a CUDA graph captured per row count."""
+
+    def __init__(self, drafter: Eagle3DrafterStandIn, *, top_k: int = 4, max_depth: int = 8,
+                 first_width: int = 4, level_width: int = 8, max_new: int = 8) -> None:
+        d = drafter
+        self.d = d
+        self.top_k, self.max_depth = top_k, max_depth
+        self.first_width, self.level_width, self.max_new = first_width, level_width, max_new
+        self.widths = [first_width] + [level_width] * (max_depth - 1)
+        self.n_cand = sum(self.widths)
+        rows_block = 1 + sum(self.widths[:-1])
+        if rows_block > 64:
+            raise ValueError("the tree block must fit a 64-bit ancestor set")
+        dev = d.fc.weight.device
+        self.dev = dev
+        z = lambda *shape, dt=torch.long: torch.zeros(*shape, dtype=dt, device=dev)
+        self.tokens = z(max_new)                      # new rows: committed tokens, then the seed
+        self.aux = z(max_new, d.fc.in_features, dt=d.fc.weight.dtype)  # their features' sources
+        self.start = z(())                            # committed rows before this cycle
+        self.out = torch.zeros(self.n_cand, 5, dtype=torch.float64, device=dev)
+        self._graphs: dict = {}
+        self._shift = torch.arange(32, dtype=torch.int64, device=dev)
+
+    def _mask_words(self, vis: torch.Tensor, block_start: torch.Tensor, cap: int) -> torch.Tensor:
+        """int32 words [n, cap/32]: column c visible when c < block_start or
+        bit (c - block_start) of the row's 64-bit ancestor set is set."""
+        cols = torch.arange(cap, device=self.dev)
+        rel = cols - block_start
+        inside = (rel >= 0) & (rel < 64)
+        bits = (vis[:, None] >> rel.clamp(0, 63)[None, :]) & 1
+        m = (cols < block_start)[None, :] | (inside[None, :] & (bits == 1))
+        words = (m.view(m.shape[0], cap // 32, 32).to(torch.int64) << self._shift).sum(-1)
+        return torch.where(words >= (1 << 31), words - (1 << 32), words).to(torch.int32)
+
+    def _rows(self, tokens, feats, pos, vis, block_start, write_at):
+        d = self.d
+        n = tokens.shape[0]
+        cap = d._k.shape[1]
+        x = torch.cat((_rms_norm(d.embed(tokens), d.emb_norm, d.eps),
+                       _rms_norm(feats, d.hid_norm, d.eps)), dim=-1)
+        q = d.q_proj(x).view(n, d.heads, d.head_dim).transpose(0, 1)
+        k = d.k_proj(x).view(n, d.kv_heads, d.head_dim).transpose(0, 1)
+        v = d.v_proj(x).view(n, d.kv_heads, d.head_dim).transpose(0, 1)
+        q = _rope(q, pos, d.theta).contiguous()
+        rows = write_at + torch.arange(n, device=self.dev)
+        d._k.index_copy_(1, rows, _rope(k, pos, d.theta))
+        d._v.index_copy_(1, rows, v)
+        attn = ops.tree_attention(q, d._k, d._v, self._mask_words(vis, block_start, cap), 0,
+                                  scale=d.head_dim ** -0.5)
+        h = feats + d.o_proj(attn.reshape(n, d.heads * d.head_dim))
+        m = _rms_norm(h, d.post_norm, d.eps)
+        return h + d.down_proj(torch.nn.functional.silu(d.gate_proj(m)) * d.up_proj(m))
+
+    def _draft(self, n_new: int) -> None:
+        """The whole drafting of one cycle as device work (captured)."""
+        d = self.d
+        dev = self.dev
+        toks = self.tokens[:n_new]
+        feats = d.fc(self.aux[:n_new])
+        seed_pos = self.start + (n_new - 1)  # position of the seed = committed tokens
+        pos = self.start + torch.arange(n_new, device=dev)
+        chain = (torch.ones((), dtype=torch.int64, device=dev) << torch.arange(1, n_new + 1, device=dev)) - 1
+        # Catch-up rows are causal among themselves after the committed rows;
+        # the seed row (last) opens the tree block at row seed_pos.
+        h = self._rows(toks, feats, pos, chain, self.start, self.start)
+        block = seed_pos
+        seed_h = h[-1:]
+        one = torch.ones((), dtype=torch.int64, device=dev)
+        lp = d._log_probs(seed_h)[0]
+        cond, tok = torch.topk(lp, self.widths[0])
+        cum = cond.double()
+        parent = torch.full((self.widths[0],), -1, dtype=torch.long, device=dev)  # -1 = the seed
+        par_vis = torch.ones(self.widths[0], dtype=torch.int64, device=dev)       # seed = bit 0
+        out_tok, out_par, out_cond, out_cum, out_depth = [tok], [parent], [cond.double()], [cum], []
+        out_depth.append(torch.ones(self.widths[0], dtype=torch.float64, device=dev))
+        hidden_parent = seed_h.expand(self.widths[0], -1)
+        first = 0                      # candidate index of the frontier's first node
+        row_next = 1                   # next row inside the tree block
+        for depth in range(1, self.max_depth):
+            w = tok.shape[0]
+            own = one << torch.arange(row_next, row_next + w, device=dev)
+            vis = par_vis | own
+            hl = self._rows(tok, hidden_parent, seed_pos + depth + 0 * tok, vis, block, block + row_next)
+            row_next += w
+            v, t = torch.topk(d._log_probs(hl), self.top_k, dim=-1)          # [w, k]
+            score = cum[:, None] + v.double()
+            best, flat = torch.topk(score.reshape(-1), self.widths[depth])    # the level's nodes
+            pj = torch.div(flat, self.top_k, rounding_mode="floor")
+            tok = t.reshape(-1)[flat]
+            cond = v.reshape(-1)[flat]
+            cum = best
+            parent = first + pj
+            par_vis = vis[pj]
+            hidden_parent = hl[pj]
+            first += w
+            out_tok.append(tok)
+            out_par.append(parent)
+            out_cond.append(cond.double())
+            out_cum.append(cum)
+            out_depth.append(torch.full((tok.shape[0],), float(depth + 1), dtype=torch.float64, device=dev))
+        self.out.copy_(torch.stack((torch.cat(out_tok).double(), torch.cat(out_par).double(),
+                                    torch.cat(out_cond), torch.cat(out_cum), torch.cat(out_depth)), dim=1))
+
+    def _graph(self, n_new: int):
+        if getattr(self, "_kptr", None) != self.d._k.data_ptr():
+            self._graphs.clear()  # a new KV buffer: earlier graphs point at the old one
+            self._kptr = self.d._k.data_ptr()
+        g = self._graphs.get(n_new)
+        if g is not None:
+            return g
+        side = torch.cuda.Stream(device=self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(2):
+                self._draft(n_new)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph), torch.no_grad():
+            self._draft(n_new)
+        self._graphs[n_new] = graph
+        return graph
+
+    def pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
+             pending_seed: torch.Tensor) -> Eagle3DraftCandidatePool:
+        d = self.d
+        L = fed_ids.shape[1]
+        start = d._fed
+        n_new = L + 1 - start
+        if start == 0 or not 1 <= n_new <= self.max_new:
+            raise ValueError("device drafting needs 1..max_new new rows after an eager catch-up")
+        self.tokens[: n_new - 1].copy_(fed_ids[0, start:L])
+        self.tokens[n_new - 1].copy_(pending_seed.reshape(()))
+        self.aux[:n_new].copy_(aux_history[start - 1:L])
+        self.start.fill_(d._len)
+        self._graph(n_new).replay()
+        rows = self.out.cpu().tolist()
+        d._len += n_new       # committed rows + the seed row stay; tree rows are dropped
+        d._fed = L + 1
+        cands = []
+        for i, (t, par, cond, _, depth) in enumerate(rows):
+            par = int(par)
+            pc = 0.0 if par < 0 else cands[par].cumulative_log_probability
+            pp = () if par < 0 else cands[par].path
+            cands.append(Eagle3DraftCandidate(i + 1, par + 1, int(depth), int(t), min(float(cond), 0.0),
+                                              pc + min(float(cond), 0.0), i, pp + (int(t),)))
+        steps = self.max_depth
+        return Eagle3DraftCandidatePool(int(pending_seed.reshape(-1)[0]), self.top_k, self.max_depth,
+                                        tuple(cands), path_score_calls=steps,
+                                        draft_transformer_steps=steps, draft_forward_calls=steps,
+                                        draft_query_tokens=n_new + sum(self.widths[:-1]))
+
+    def release(self) -> None:
+        self._graphs.clear()

@@ -24,7 +24,9 @@ exact route footprints; and acceptance is simulated — a node at depth d is
 accepted with probability p_d, p_d ~ Beta(4, 2) drawn once per depth from a
 seed — with the greedy path through accepted nodes in node order.
 
-With ``graphs=True`` each verification tree size (1 to 8 rows) gets one
+With ``graphs=True`` drafting runs as device work replayed from one CUDA
+graph per number of new rows (``DeviceDraft``), and each verification tree
+size (1 to 8 rows) gets one
 CUDA graph of the target forward, captured once and replayed at any
 committed length: the reserved cache runs in static mode (keys/values
 written at a device-side offset, attention over every reserved row), and the
@@ -115,6 +117,13 @@ class B200TreeSpeculator:
         self._graphs: dict = {}
         self._offset = None
         self._cache = None
+        self._ddraft = None
+        if graphs:
+            from .eagle3_drafter import DeviceDraft
+
+            self._ddraft = DeviceDraft(drafter, top_k=top_k, max_depth=max_depth,
+                                       first_width=first_width, level_width=level_width,
+                                       max_new=1 + max_depth)
 
     # ------------------------------------------------------------- hooks
     def _install(self):
@@ -199,6 +208,58 @@ class B200TreeSpeculator:
 
     def release_graphs(self) -> None:
         self._graphs.clear()
+        if self._ddraft is not None:
+            self._ddraft.release()
+
+    def calibrate_cost_model(self, *, expert_ns: float, reps: int = 5, seed: int = 0):
+        """A ``SelectionCostModel`` fitted to this GPU, the way the reference
+        fits its own (``docs/results/selection-refinement-*.json``): for each
+        tree size n = 0..max_nodes the verify graph of a chain of n random
+        tokens is replayed ``reps`` times over the current cache (its rows go
+        past the committed length and are dropped), and
+        ``intercept[n] = median time - expert_ns * |footprint|``; the slope
+        ``expert_ns`` (one distinct (layer, expert) of the footprint) is given,
+        e.g. one packed expert's bytes over the measured HBM bandwidth.
+        Needs ``graphs=True`` and a cache left by ``generate``."""
+        from ..selection import SelectionCostModel
+        from .eagle3_types import Eagle3DraftTree
+
+        cache = self._cache
+        if not self.graphs or cache is None or not cache.layers[0].is_initialized:
+            raise RuntimeError("calibration needs the verify graphs and a prefilled cache")
+        dev = self._offset.device
+        base = cache.get_seq_length()
+        rng = np.random.default_rng(seed)
+        vocab = self.model.config.vocab_size
+        hooks = self._install()
+        intercepts, means = [], []
+        try:
+            for n in range(self.max_nodes + 1):
+                toks = [int(t) for t in rng.integers(0, vocab, size=n + 1)]
+                tree = Eagle3DraftTree(tuple(toks[1:]), tuple(range(n)), tuple(range(1, n + 1)),
+                                       (0.5,) * n, tuple(np.log(0.5) * np.arange(1, n + 1)))
+                routes = synthetic.token_routes(torch.tensor(toks, device=dev), self.layers,
+                                                experts=self.experts, top_k=self.route_k,
+                                                seed=self.route_seed)
+                union = int(np.unpackbits(np.bitwise_or.reduce(
+                    sel.footprints(routes.cpu().numpy(), self.experts), axis=0).view(np.uint8)).sum())
+                pending = torch.tensor([[toks[0]]], device=dev)
+                times = []
+                for _ in range(reps + 1):
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record()
+                    self._verify_graph(cache, tree, pending, routes, base)
+                    e.record()
+                    e.synchronize()
+                    cache.set_length(base)
+                    times.append(s.elapsed_time(e) * 1e6)
+                t = float(np.median(times[1:]))
+                means.append(t)
+                intercepts.append(max(t - expert_ns * union, 0.0))
+        finally:
+            for h in hooks:
+                h.remove()
+        return SelectionCostModel(tuple(means), tuple(intercepts), float(expert_ns))
 
     # ------------------------------------------------------------ generate
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int, *, sync_timing: bool = False):
@@ -247,11 +308,16 @@ class B200TreeSpeculator:
                     result.tokens.append(int(pending.reshape(-1)[0]))
                     break
                 ta = time.perf_counter()
+                n_new = fed.shape[1] + 1 - self.drafter._fed
                 with torch.no_grad():
-                    pool = self.drafter.build_candidate_pool(
-                        fed_ids=fed, aux_history=aux, pending_seed=pending, top_k=self.top_k,
-                        max_depth=min(self.max_depth, remaining - 1), first_width=self.first_width,
-                        level_width=self.level_width)
+                    if (self._ddraft is not None and self.drafter._fed > 0 and remaining - 1 >= self.max_depth
+                            and n_new <= self._ddraft.max_new):
+                        pool = self._ddraft.pool(fed_ids=fed, aux_history=aux, pending_seed=pending)
+                    else:
+                        pool = self.drafter.build_candidate_pool(
+                            fed_ids=fed, aux_history=aux, pending_seed=pending, top_k=self.top_k,
+                            max_depth=min(self.max_depth, remaining - 1), first_width=self.first_width,
+                            level_width=self.level_width)
                 tick()
                 tb = time.perf_counter()
                 toks = torch.tensor((pool.seed_token_id,) + tuple(c.target_token_id for c in pool.candidates),

@@ -103,3 +103,36 @@ def test_generate_commits_and_audit_matches_causal_forward(graphs):
         spec.release_graphs()
     finally:
         m.close()
+
+
+def test_device_drafting_matches_eager_drafting():
+    """From the same drafter state, the graph-replayed device drafting grows
+    the pool the eager drafting grows: the same level-1 tokens, log-probs
+    within bf16 tolerance, and (nearly) the same (parent, token) pairs
+    (scores computed in a different order may swap exact near-ties)."""
+    from specfit_b200.runtime.eagle3_drafter import DeviceDraft
+
+    cfg, m, d = small()
+    try:
+        g = torch.Generator().manual_seed(5)
+        ids = torch.randint(0, 512, (1, 33), generator=g).to(DEV)
+        aux = torch.randn(33, 3 * 256, generator=g).to(DEV).to(torch.bfloat16)
+        d.begin_generation(256)
+        d.build_candidate_pool(fed_ids=ids[:, :30], aux_history=aux[:30], pending_seed=ids[:, 30:31])
+        state = (d._k.clone(), d._v.clone(), d._len, d._fed)
+        kw = dict(fed_ids=ids[:, :33], aux_history=aux[:33], pending_seed=ids[:, 32:33] * 0 + 7)
+        eager = d.build_candidate_pool(top_k=4, max_depth=8, first_width=4, level_width=8, **kw)
+        d._k.copy_(state[0]); d._v.copy_(state[1]); d._len, d._fed = state[2], state[3]
+        dd = DeviceDraft(d, top_k=4, max_depth=8, first_width=4, level_width=8, max_new=9)
+        dev_pool = dd.pool(**kw)
+        assert d._fed == 34 and d._len == state[2] + 3  # 2 new committed rows + the new seed row
+        a, b = eager.candidates, dev_pool.candidates
+        assert len(a) == len(b) == 60
+        assert [c.target_token_id for c in a[:4]] == [c.target_token_id for c in b[:4]]
+        for x, y in zip(a[:4], b[:4]):
+            assert abs(x.conditional_log_probability - y.conditional_log_probability) < 5e-2
+        pairs = lambda p: {(c.parent_raw_id, c.target_token_id) for c in p}
+        assert len(pairs(a) & pairs(b)) >= 0.8 * 60
+        dd.release()
+    finally:
+        m.close()
