@@ -107,20 +107,23 @@ router_logits_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t t
 // rows are first copied into shared memory with one burst of asynchronous
 // 16-byte copies (cp.async), so the dot products run from shared memory
 // instead of waiting on one round of L2 loads per 256 columns.  Same lane
-// assignment and summation order as router_logits_kernel.
-template <typename T, typename Acc>
+// assignment and summation order as router_logits_kernel.  kET experts per
+// CTA: 16 normally, 4 when few token tiles would leave most SMs idle (a
+// verify pass of a handful of rows); every (token, expert) sum is still one
+// warp's, in the same order, so the logits are the same bits either way.
+template <typename T, typename Acc, int kET>
 __global__ void __launch_bounds__(kWarps * 32)
 router_logits_staged(const T* __restrict__ x, const T* __restrict__ w, int64_t tokens, int hidden,
                      int experts, float* __restrict__ logits_f32, T* __restrict__ logits_out) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   T* xs = reinterpret_cast<T*>(smem_raw);        // [kTokTile][hidden]
-  T* ws = xs + (size_t)kTokTile * hidden;         // [kExpTile][hidden]
+  T* ws = xs + (size_t)kTokTile * hidden;         // [kET][hidden]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t t0 = (int64_t)blockIdx.x * kTokTile;
   const int ntok = (int)((tokens - t0) < kTokTile ? (tokens - t0) : kTokTile);
-  const int e0 = blockIdx.y * kExpTile;
-  const int nexp = (experts - e0) < kExpTile ? (experts - e0) : kExpTile;
+  const int e0 = blockIdx.y * kET;
+  const int nexp = (experts - e0) < kET ? (experts - e0) : kET;
   const int vec_per_row = hidden * (int)sizeof(T) / 16;
   const int total = (ntok + nexp) * vec_per_row;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
@@ -272,17 +275,27 @@ int launch_router(const void* hidden, const void* weight, int64_t tokens, int H,
   const T* w = static_cast<const T*>(weight);
   dim3 grid((unsigned)((tokens + kTokTile - 1) / kTokTile), (unsigned)((E + kExpTile - 1) / kExpTile));
   const bool vec = (H % 8 == 0) && aligned16(x) && aligned16(w);
-  const size_t staged_smem = (size_t)(kTokTile + kExpTile) * H * sizeof(T);
+  const bool few = (int64_t)grid.x * grid.y < num_sms();
+  constexpr int kSmallTile = 4;
+  const size_t staged_smem = (size_t)(kTokTile + (few ? kSmallTile : kExpTile)) * H * sizeof(T);
   if (vec && staged_smem <= 200 * 1024) {
     static std::atomic<unsigned long long> configured{0};
     if (int rc = once_per_device(configured, [] {
-          SF_CHECK_CUDA(cudaFuncSetAttribute(router_logits_staged<T, Acc>,
+          SF_CHECK_CUDA(cudaFuncSetAttribute(router_logits_staged<T, Acc, kExpTile>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+          SF_CHECK_CUDA(cudaFuncSetAttribute(router_logits_staged<T, Acc, kSmallTile>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
           return SF_OK;
         }))
       return rc;
-    router_logits_staged<T, Acc><<<grid, kWarps * 32, staged_smem, stream>>>(
-        x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+    if (few) {
+      grid.y = (unsigned)((E + kSmallTile - 1) / kSmallTile);
+      router_logits_staged<T, Acc, kSmallTile><<<grid, kWarps * 32, staged_smem, stream>>>(
+          x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+    } else {
+      router_logits_staged<T, Acc, kExpTile><<<grid, kWarps * 32, staged_smem, stream>>>(
+          x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+    }
   } else if (vec)
     router_logits_kernel<T, Acc, true><<<grid, kWarps * 32, 0, stream>>>(
         x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));

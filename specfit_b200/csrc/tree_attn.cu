@@ -183,25 +183,51 @@ __global__ void tree_attn_merge_kernel(Params p, __nv_bfloat16* __restrict__ out
   if (pair >= (int64_t)p.num_heads * p.q_len) return;
   const int head = (int)(pair / p.q_len);
   const int row = (int)(pair % p.q_len);
+  const int64_t stride = (int64_t)p.num_heads * p.q_len;  // between splits
+  const int64_t base = (int64_t)head * p.q_len + row;
+  // Lanes read the splits' (max, sum) pairs in parallel (split lane + 32 k).
   float gm = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) {
-    const int64_t idx = ((int64_t)s * p.num_heads + head) * p.q_len + row;
-    gm = fmaxf(gm, p.part_ml[idx * 2]);
-  }
+  for (int s = lane; s < p.splits; s += 32) gm = fmaxf(gm, p.part_ml[(base + s * stride) * 2]);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float denom = 0.f;
   if (gm != -INFINITY) {
-    for (int s = 0; s < p.splits; ++s) {
-      const int64_t idx = ((int64_t)s * p.num_heads + head) * p.q_len + row;
-      const float ms = p.part_ml[idx * 2];
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - gm);
-      denom += w * p.part_ml[idx * 2 + 1];
-      const float4 ov = *reinterpret_cast<const float4*>(p.part_o + idx * kD + lane * 4);
-      acc[0] += w * ov.x;
-      acc[1] += w * ov.y;
-      acc[2] += w * ov.z;
-      acc[3] += w * ov.w;
+    for (int s = lane; s < p.splits; s += 32) {
+      const float ms = p.part_ml[(base + s * stride) * 2];
+      if (ms != -INFINITY) denom += expf(ms - gm) * p.part_ml[(base + s * stride) * 2 + 1];
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) denom += __shfl_xor_sync(0xffffffffu, denom, off);
+    // Weighted outputs, four splits' loads in flight at a time.
+    for (int s0 = 0; s0 < p.splits; s0 += 32) {
+      const int s = s0 + lane;
+      float w = 0.f;
+      if (s < p.splits) {
+        const float ms = p.part_ml[(base + s * stride) * 2];
+        w = (ms == -INFINITY) ? 0.f : expf(ms - gm);
+      }
+      const int n = min(32, p.splits - s0);
+      for (int j = 0; j < n; j += 4) {
+        float4 ov[4];
+        float wj[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          wj[u] = __shfl_sync(0xffffffffu, w, (j + u) & 31);
+          ov[u] = (j + u < n && wj[u] != 0.f)
+                      ? *reinterpret_cast<const float4*>(p.part_o + (base + (int64_t)(s0 + j + u) * stride) * kD + lane * 4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (j + u < n) {
+            acc[0] += wj[u] * ov[u].x;
+            acc[1] += wj[u] * ov[u].y;
+            acc[2] += wj[u] * ov[u].z;
+            acc[3] += wj[u] * ov[u].w;
+          }
+        }
+      }
     }
   }
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
