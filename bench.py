@@ -79,6 +79,8 @@ def parse_args(argv=None):
     p.add_argument("--ep-ctx", type=int, default=4096, help="--mode ep: context tokens per request")
     p.add_argument("--decode-ctx", type=int, default=2048, help="--mode decode: context tokens")
     p.add_argument("--new-tokens", type=int, default=256, help="--mode decode: tokens to generate")
+    p.add_argument("--hf-forward", action="store_true",
+                   help="run the Hugging Face layer forward instead of the lean fused forward")
     p.add_argument("--eager-decode", action="store_true",
                    help="--mode decode: verify passes without CUDA graphs")
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
@@ -203,18 +205,29 @@ def make_tree(nodes, depth, branch, seed, vocab):
 # --------------------------------------------------------------- B200 arm
 
 
+def make_forward(model, hf: bool):
+    """The target forward the runners call: the lean fused forward by
+    default, the stock Hugging Face forward with ``--hf-forward``."""
+    if hf:
+        return model
+    from specfit_b200.runtime.lean_forward import LeanQwen3Forward
+
+    return LeanQwen3Forward(model)
+
+
 class VerifyRunner:
-    def __init__(self, loaded, ctx_ids, tree, seed_tok, device):
+    def __init__(self, loaded, ctx_ids, tree, seed_tok, device, fwd=None):
         from specfit_b200.runtime.kv_cache import ReservedCache
 
         self.loaded = loaded
         self.model = loaded.model
+        self.fwd = fwd if fwd is not None else self.model
         self.tree = tree
         self.device = device
         self.ctx = ctx_ids.shape[1]
         self.cache = ReservedCache(config=self.model.config, capacity=self.ctx + 1 + tree.draft_node_count)
         with torch.no_grad():
-            self.model(input_ids=ctx_ids, past_key_values=self.cache, use_cache=True)
+            self.fwd(input_ids=ctx_ids, past_key_values=self.cache, use_cache=True)
         seed = torch.tensor([[seed_tok]])
         self.h_ids = tree.verification_token_ids(seed).pin_memory()
         self.h_mask = tree.verification_attention_mask(base_kv_length=self.ctx, device="cpu").pin_memory()
@@ -226,8 +239,8 @@ class VerifyRunner:
     def step_device(self):
         """Inputs already on the device; returns the device argmax."""
         with torch.no_grad():
-            out = self.model(input_ids=self.d_ids, attention_mask=self.d_mask, position_ids=self.d_pos,
-                             past_key_values=self.cache, use_cache=True)
+            out = self.fwd(input_ids=self.d_ids, attention_mask=self.d_mask, position_ids=self.d_pos,
+                           past_key_values=self.cache, use_cache=True)
             am = out.logits[0].argmax(-1)
         self.cache.crop(self.ctx)
         return am
@@ -238,8 +251,8 @@ class VerifyRunner:
         mask = self.h_mask.to(self.device, non_blocking=True)
         pos = self.h_pos.to(self.device, non_blocking=True)
         with torch.no_grad():
-            out = self.model(input_ids=ids, attention_mask=mask, position_ids=pos,
-                             past_key_values=self.cache, use_cache=True)
+            out = self.fwd(input_ids=ids, attention_mask=mask, position_ids=pos,
+                           past_key_values=self.cache, use_cache=True)
             am = out.logits[0].argmax(-1).cpu().unsqueeze(0)
         self.cache.crop(self.ctx)
         return len(self.tree.accepted_path(am)) + 1
@@ -434,7 +447,8 @@ def b200_arm(args):
     ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
     tree = make_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
     seed_tok = int(torch.randint(0, cfg.vocab_size, (1,), generator=gen))
-    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device)
+    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device,
+                          fwd=make_forward(loaded.model, args.hf_forward))
     build_s = time.perf_counter() - t_build
 
     launches0 = ops.LAUNCHES[0]
@@ -490,6 +504,8 @@ def b200_arm(args):
             "slots_per_layer": args.slots,
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             "l2_flush": "not needed: each step streams > 57 GB of expert weights (>> 126 MB L2)",
+            "forward": ("Hugging Face decoder layers" if args.hf_forward else
+                        "lean fused layer forward (runtime/lean_forward.py)"),
         },
         "cache_stats_after_timing": stats24,
         "predicted_prefetch": {"value": round(pf_value, 4), "unit": "tokens/s",
@@ -527,7 +543,8 @@ def b200_arm(args):
         eager_ms, _ = timed_steps(runner.step_device, rsteps, args.warmup, world, device)
         from specfit_b200.runtime.verify_graph import VerifyGraph
 
-        vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device)
+        vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device,
+                         forward=runner.fwd)
         before = ops.LAUNCHES[0]
         vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
         graph_launches = (ops.LAUNCHES[0] - before) // 3  # two warm-up passes + the captured one
@@ -600,6 +617,7 @@ class EpRunner:
         from specfit_b200.runtime.kv_cache import ReservedCache
 
         self.model = loaded.model
+        self.fwd = make_forward(loaded.model, args.hf_forward)
         self.device = device
         self.batch = args.requests // world
         self.ctx = args.ep_ctx
@@ -611,8 +629,8 @@ class EpRunner:
         lo, hi = rank * self.batch, (rank + 1) * self.batch
         self.cache = ReservedCache(config=cfg, capacity=self.ctx + q)
         with torch.no_grad():
-            self.model(input_ids=ctx_all[lo:hi].to(device), past_key_values=self.cache, use_cache=True,
-                       logits_to_keep=1)
+            self.fwd(input_ids=ctx_all[lo:hi].to(device), past_key_values=self.cache, use_cache=True,
+                     logits_to_keep=1)
         torch.cuda.synchronize(device)
         self.h_ids = torch.cat([self.tree.verification_token_ids(seeds[b].view(1, 1))
                                 for b in range(lo, hi)]).pin_memory()
@@ -640,8 +658,8 @@ class EpRunner:
         self.override = True
         try:
             with torch.no_grad():
-                out = self.model(input_ids=ids, attention_mask=mask, position_ids=pos,
-                                 past_key_values=self.cache, use_cache=True)
+                out = self.fwd(input_ids=ids, attention_mask=mask, position_ids=pos,
+                               past_key_values=self.cache, use_cache=True)
                 am = out.logits.argmax(-1)
         finally:
             self.override = False
@@ -751,7 +769,8 @@ def ep_arm(args):
     loaded.use_peer(True)
     peer_eager_ms, _ = timed_steps(runner.step_device, args.steps, 2, world, device)
     times, _ = moe_block_profile(runner)
-    vg = VerifyGraph(loaded.model, runner.cache, q_len=q, device=device, batch=runner.batch)
+    vg = VerifyGraph(loaded.model, runner.cache, q_len=q, device=device, batch=runner.batch,
+                     forward=runner.fwd)
     barrier(world)
     runner.override = True
     try:
@@ -803,6 +822,8 @@ def ep_arm(args):
             "requests_per_gpu": runner.batch,
             "verify_tokens_per_step": args.requests * q,
             "parallelism": f"ep{world}, attention data-parallel over requests",
+            "forward": ("Hugging Face decoder layers" if args.hf_forward else
+                        "lean fused layer forward (runtime/lean_forward.py)"),
             "l2_flush": (f"not needed: each step reads {args.layers * cfg.num_experts // world} resident "
                          f"experts ({args.layers * cfg.num_experts // world * EXPERT_BYTES / 1e9:.1f} GB) "
                          "per GPU, >> 126 MB L2"),
@@ -932,7 +953,8 @@ def decode_mode(args):
     ctx_host = torch.randint(0, cfg.vocab_size, (1, args.decode_ctx), generator=gen).pin_memory()
     spec = B200TreeSpeculator(loaded, drafter, cost_model=cost, acceptance=BernoulliAcceptance(0),
                               route_seed=args.seed, graphs=not args.eager_decode,
-                              reserve_tokens=args.decode_ctx + args.new_tokens + 16)
+                              reserve_tokens=args.decode_ctx + args.new_tokens + 16,
+                              lean=not args.hf_forward)
     setup_s = time.perf_counter() - t0
 
     def run(new_tokens, acceptance_seed):
@@ -985,6 +1007,8 @@ def decode_mode(args):
                          f"{args.new_tokens} generated tokens"),
             "step": "one speculative cycle (draft, select, verify, commit)",
             "verify": "eager" if args.eager_decode else "one CUDA graph per tree size (1-8 rows)",
+            "forward": ("Hugging Face decoder layers" if args.hf_forward else
+                        "lean fused layer forward (runtime/lean_forward.py)"),
             "l2_flush": "not needed: each verify pass reads the routed experts of every layer (GBs)",
         },
         "gpu_launches": int(launches),
@@ -1130,8 +1154,9 @@ def graph_mode(args):
     ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
     tree = make_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
     seed_tok = int(torch.randint(0, cfg.vocab_size, (1,), generator=gen))
-    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device)
-    vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device)
+    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device,
+                          fwd=make_forward(loaded.model, args.hf_forward))
+    vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device, forward=runner.fwd)
     vg.capture(runner.d_ids, runner.d_mask, runner.d_pos)
     ms, _ = timed_steps(vg.replay, args.steps, args.warmup, 1, device)
     print(json.dumps({"mode": "graph", "layers": args.layers, "ms_per_pass": round(ms / args.steps, 3),

@@ -21,6 +21,10 @@
  *                                                               src/specfit/runtime/eagle3_types.py:450-473
  *   sf_specfit_select     exact_specfit_selection               src/specfit/specfit_exact.py:58-94
  *   sf_ep_*               (none: the reference is single-GPU, scripts/run_specfit_main_comparison.py:465)
+ *   sf_add_rmsnorm        residual add + Qwen3MoeRMSNorm        transformers/...:Qwen3MoeRMSNorm.forward,
+ *                                                               Qwen3MoeDecoderLayer.forward (residual adds)
+ *   sf_qk_norm_rope       q_norm/k_norm + apply_rotary_pos_emb  transformers/...:Qwen3MoeAttention.forward
+ *                         + cache update (write k, v rows)
  */
 #ifndef SPECFIT_B200_H_
 #define SPECFIT_B200_H_
@@ -370,6 +374,32 @@ SF_API int sf_ep_peer_return(const sf_ep_peer* d, const void* out_sorted,
 SF_API int sf_ep_peer_finish(const sf_ep_peer* d, const int64_t* topk_index,
                              const int32_t* route_row, int64_t tokens, int num_experts,
                              int reduce, void* out, void* stream);
+
+/*
+ * Fused elementwise steps of a Qwen3-MoE decoder layer (bf16 only).
+ * sf_add_rmsnorm: per row, h = residual_in + x rounded to bf16 (h = x when
+ * residual_in is NULL), written to residual_out when non-NULL, and
+ * out = bf16(weight * bf16(h * rsqrt(mean(h^2) + eps))).  H % 8 == 0,
+ * H <= 8192, 16-byte aligned rows.
+ */
+SF_API int sf_add_rmsnorm(const void* x, const void* residual_in, void* residual_out,
+                          const void* weight, float eps, int64_t rows, int hidden_size, void* out,
+                          void* stream);
+/*
+ * sf_qk_norm_rope: qkv [batch*tokens, (Hq + 2*Hkv) * 128] (q heads, then k,
+ * then v); q and k heads get the head RMSNorm with their weights [128] and the
+ * rotary embedding x*cos + rotate_half(x)*sin with cos/sin [batch*tokens, 128]
+ * (each product and the sum rounded to bf16).  q goes to q_out
+ * [batch, Hq, tokens, 128]; k and v go to the cache rows row0 + t (row0 read
+ * from row0_device when non-NULL) of k_cache / v_cache laid out
+ * [batch][Hkv][rows][128] with the given batch and head strides (elements).
+ */
+SF_API int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
+                           int num_kv_heads, int head_dim, const void* q_norm_weight,
+                           const void* k_norm_weight, const void* cos, const void* sin, float eps,
+                           void* q_out, void* k_cache, void* v_cache, int64_t kv_batch_stride,
+                           int64_t kv_head_stride, int64_t row0, const int64_t* row0_device,
+                           void* stream);
 
 #ifdef __cplusplus
 }

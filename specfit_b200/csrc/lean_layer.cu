@@ -1,0 +1,194 @@
+// Fused elementwise steps of a Qwen3-MoE decoder layer for the verify pass.
+//
+// The Hugging Face layer (transformers/models/qwen3_moe/modeling_qwen3_moe.py)
+// runs each RMSNorm, residual add, per-head q/k norm and rotary embedding as
+// a chain of small torch kernels (about 50 per layer); at a few verify rows
+// those launches cost more than the layer's arithmetic.  Two kernels replace
+// them, keeping the bf16 rounding points of the torch code:
+//
+//   sf_add_rmsnorm   h = residual + x (bf16 add), out = bf16(w * bf16(h * rsqrt(mean(h^2) + eps)))
+//                    (Qwen3MoeRMSNorm.forward, and the residual adds of
+//                    Qwen3MoeDecoderLayer.forward)
+//   sf_qk_norm_rope  per head of a fused q|k|v projection row: q and k get the
+//                    head RMSNorm (q_norm / k_norm) and the rotary embedding
+//                    q*cos + rotate_half(q)*sin, each product and the sum
+//                    rounded to bf16 (apply_rotary_pos_emb); q is written
+//                    head-major for the attention kernel, k and v straight
+//                    into the KV cache rows (the cache update), at a row
+//                    offset given on the host or read from device memory.
+//
+// Sums of squares are fp32 in a fixed order (per-thread, then a butterfly),
+// which may differ from torch's reduction order in the last bit of the
+// variance; outputs agree with the torch chain to bf16 rounding.
+#include "common.cuh"
+
+namespace sf {
+namespace {
+
+constexpr int kNormThreads = 256;  // 8 bf16 per thread covers H = 2048
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ __nv_bfloat16 bf(float v) { return __float2bfloat16_rn(v); }
+__device__ __forceinline__ float fl(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// One CTA per row; H % 8 == 0, rows 16-byte aligned.
+__global__ void __launch_bounds__(kNormThreads)
+add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res_in,
+                   __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
+                   float eps, int H, __nv_bfloat16* __restrict__ out) {
+  __shared__ float part[kNormThreads / 32];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * H;
+  float h[8 * 4];  // up to 4 chunks of 8 per thread (H <= 8192)
+  float ss = 0.f;
+  int nch = 0;
+  for (int c0 = threadIdx.x * 8; c0 < H; c0 += kNormThreads * 8, ++nch) {
+    __nv_bfloat16 xv[8];
+    *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(xr + c0);
+    __nv_bfloat16 hv[8];
+    if (res_in) {
+      __nv_bfloat16 rv[8];
+      *reinterpret_cast<uint4*>(rv) = *reinterpret_cast<const uint4*>(res_in + row * H + c0);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) hv[v] = bf(fl(rv[v]) + fl(xv[v]));
+    } else {
+#pragma unroll
+      for (int v = 0; v < 8; ++v) hv[v] = xv[v];
+    }
+    if (res_out) *reinterpret_cast<uint4*>(res_out + row * H + c0) = *reinterpret_cast<uint4*>(hv);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const float f = fl(hv[v]);
+      h[nch * 8 + v] = f;
+      ss += f * f;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += part[i];
+  const float r = rsqrtf(tot / (float)H + eps);
+  int ch = 0;
+  for (int c0 = threadIdx.x * 8; c0 < H; c0 += kNormThreads * 8, ++ch) {
+    __nv_bfloat16 wv[8], ov[8];
+    *reinterpret_cast<uint4*>(wv) = *reinterpret_cast<const uint4*>(w + c0);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) ov[v] = bf(fl(wv[v]) * fl(bf(h[ch * 8 + v] * r)));
+    *reinterpret_cast<uint4*>(out + row * H + c0) = *reinterpret_cast<uint4*>(ov);
+  }
+}
+
+// One warp per (token, head) of the q|k|v row; D == 128 (4 values per lane).
+__global__ void qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t n_tokens, int T,
+                                    int hq, int hkv, const __nv_bfloat16* __restrict__ qw,
+                                    const __nv_bfloat16* __restrict__ kw,
+                                    const __nv_bfloat16* __restrict__ cos,
+                                    const __nv_bfloat16* __restrict__ sin, float eps,
+                                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ kbuf,
+                                    __nv_bfloat16* __restrict__ vbuf, int64_t kv_batch_stride,
+                                    int64_t kv_head_stride, int64_t row0_host,
+                                    const int64_t* __restrict__ row0_dev) {
+  constexpr int D = 128;
+  const int heads = hq + 2 * hkv;
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (item >= n_tokens * heads) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = item / heads;
+  const int head = (int)(item - n * heads);
+  const int b = (int)(n / T), t = (int)(n - (int64_t)b * T);
+  const __nv_bfloat16* src = qkv + n * (int64_t)heads * D + (int64_t)head * D + lane * 4;
+  __nv_bfloat16 xv[4];
+  *reinterpret_cast<uint2*>(xv) = *reinterpret_cast<const uint2*>(src);
+  const int64_t row = (row0_dev ? *row0_dev : row0_host) + t;
+  if (head >= hq + hkv) {  // v: straight into the cache
+    __nv_bfloat16* dst = vbuf + b * kv_batch_stride + (int64_t)(head - hq - hkv) * kv_head_stride + row * D;
+    *reinterpret_cast<uint2*>(dst + lane * 4) = *reinterpret_cast<uint2*>(xv);
+    return;
+  }
+  const __nv_bfloat16* w = head < hq ? qw : kw;
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) ss += fl(xv[v]) * fl(xv[v]);
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)D + eps);
+  float y[4];
+#pragma unroll
+  for (int v = 0; v < 4; ++v) y[v] = fl(bf(fl(w[lane * 4 + v]) * fl(bf(fl(xv[v]) * r))));
+  // rotate_half: dims d < 64 take -x[d + 64], dims d >= 64 take x[d - 64] (lane +- 16).
+  float other[4];
+#pragma unroll
+  for (int v = 0; v < 4; ++v) other[v] = __shfl_xor_sync(0xffffffffu, y[v], 16);
+  const bool low = lane < 16;
+  const __nv_bfloat16* cr = cos + n * D + lane * 4;
+  const __nv_bfloat16* sr = sin + n * D + lane * 4;
+  __nv_bfloat16 o[4];
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const float rot = low ? -other[v] : other[v];
+    o[v] = bf(fl(bf(y[v] * fl(cr[v]))) + fl(bf(rot * fl(sr[v]))));
+  }
+  if (head < hq) {
+    __nv_bfloat16* dst = q_out + (((int64_t)b * hq + head) * T + t) * D + lane * 4;
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<uint2*>(o);
+  } else {
+    __nv_bfloat16* dst = kbuf + b * kv_batch_stride + (int64_t)(head - hq) * kv_head_stride + row * D;
+    *reinterpret_cast<uint2*>(dst + lane * 4) = *reinterpret_cast<uint2*>(o);
+  }
+}
+
+}  // namespace
+}  // namespace sf
+
+extern "C" int sf_add_rmsnorm(const void* x, const void* residual_in, void* residual_out,
+                              const void* weight, float eps, int64_t rows, int hidden_size,
+                              void* out, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(rows >= 0 && hidden_size > 0, "invalid sizes");
+  SF_CHECK_ARG(hidden_size % 8 == 0 && hidden_size <= 8 * 4 * kNormThreads,
+               "hidden_size must be a multiple of 8 and at most %d", 8 * 4 * kNormThreads);
+  if (rows == 0) return SF_OK;
+  SF_CHECK_ARG(x && weight && out, "null pointer argument");
+  SF_CHECK_ARG(aligned16(x) && aligned16(out) && aligned16(weight) &&
+               (!residual_in || aligned16(residual_in)) && (!residual_out || aligned16(residual_out)),
+               "tensors must be 16-byte aligned");
+  add_rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual_in),
+      static_cast<__nv_bfloat16*>(residual_out), static_cast<const __nv_bfloat16*>(weight), eps,
+      hidden_size, static_cast<__nv_bfloat16*>(out));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}
+
+extern "C" int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
+                               int num_kv_heads, int head_dim, const void* q_norm_weight,
+                               const void* k_norm_weight, const void* cos, const void* sin,
+                               float eps, void* q_out, void* k_cache, void* v_cache,
+                               int64_t kv_batch_stride, int64_t kv_head_stride, int64_t row0,
+                               const int64_t* row0_device, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(head_dim == 128, "head_dim must be 128");
+  SF_CHECK_ARG(batch >= 0 && tokens >= 0 && num_heads > 0 && num_kv_heads > 0, "invalid sizes");
+  const int64_t n = batch * tokens;
+  if (n == 0) return SF_OK;
+  SF_CHECK_ARG(qkv && q_norm_weight && k_norm_weight && cos && sin && q_out && k_cache && v_cache,
+               "null pointer argument");
+  SF_CHECK_ARG(aligned16(qkv) && aligned16(q_out) && aligned16(k_cache) && aligned16(v_cache),
+               "tensors must be 16-byte aligned");
+  SF_CHECK_ARG(kv_batch_stride % 8 == 0 && kv_head_stride % 8 == 0, "cache strides must be multiples of 8");
+  const int64_t items = n * (num_heads + 2 * num_kv_heads);
+  qk_norm_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(qkv), n, (int)tokens, num_heads, num_kv_heads,
+      static_cast<const __nv_bfloat16*>(q_norm_weight), static_cast<const __nv_bfloat16*>(k_norm_weight),
+      static_cast<const __nv_bfloat16*>(cos), static_cast<const __nv_bfloat16*>(sin), eps,
+      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+      static_cast<__nv_bfloat16*>(v_cache), kv_batch_stride, kv_head_stride, row0, row0_device);
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}

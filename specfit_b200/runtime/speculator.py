@@ -97,9 +97,15 @@ class B200TreeSpeculator:
     def __init__(self, loaded, drafter, *, cost_model, acceptance: BernoulliAcceptance,
                  route_seed: int = 0, top_k: int = 4, max_depth: int = 8, first_width: int = 4,
                  level_width: int = 8, max_nodes: int = sel.MAX_DRAFT_NODES,
-                 graphs: bool = False, reserve_tokens: int = 0) -> None:
+                 graphs: bool = False, reserve_tokens: int = 0, lean: bool = False) -> None:
         self.loaded = loaded
         self.model = loaded.model
+        if lean:
+            from .lean_forward import LeanQwen3Forward
+
+            self.fwd = LeanQwen3Forward(self.model)
+        else:
+            self.fwd = self.model
         self.drafter = drafter
         self.cost_model = cost_model
         self.acceptance = acceptance
@@ -169,14 +175,14 @@ class B200TreeSpeculator:
             side.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(side), torch.no_grad():
                 for _ in range(2):
-                    self.model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                    self.fwd(input_ids=ids, attention_mask=mask, position_ids=pos,
                                past_key_values=cache, use_cache=True)
             torch.cuda.current_stream(dev).wait_stream(side)
             torch.cuda.synchronize(dev)
             clear_mask_cache()
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph), torch.no_grad():
-                out = self.model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                out = self.fwd(input_ids=ids, attention_mask=mask, position_ids=pos,
                                  past_key_values=cache, use_cache=True)
                 argmax = out.logits[0].argmax(-1)
                 feats = self._features()
@@ -291,7 +297,7 @@ class B200TreeSpeculator:
         try:
             t0 = time.perf_counter()
             with torch.no_grad():
-                out = self.model(input_ids=input_ids, past_key_values=cache, use_cache=True,
+                out = self.fwd(input_ids=input_ids, past_key_values=cache, use_cache=True,
                                  logits_to_keep=1)
             aux = self._features()
             pending = out.logits[:, -1:].argmax(-1)
@@ -341,7 +347,7 @@ class B200TreeSpeculator:
                     self._override = routes_sel
                     try:
                         with torch.no_grad():
-                            vout = self.model(input_ids=verify_ids, attention_mask=mask,
+                            vout = self.fwd(input_ids=verify_ids, attention_mask=mask,
                                               position_ids=pos, past_key_values=cache, use_cache=True)
                     finally:
                         self._override = None

@@ -30,8 +30,9 @@ class VerifyGraph:
     each; ``replay`` returns the argmax ``[q_len]`` (batch 1) or
     ``[batch, q_len]``."""
 
-    def __init__(self, model, kv_cache, *, q_len: int, device, batch: int = 1) -> None:
+    def __init__(self, model, kv_cache, *, q_len: int, device, batch: int = 1, forward=None) -> None:
         self.model = model
+        self.forward = forward if forward is not None else model  # e.g. a LeanQwen3Forward
         self.cache = kv_cache
         self.device = torch.device(device)
         self.prefix_len = kv_cache.get_seq_length()
@@ -55,8 +56,8 @@ class VerifyGraph:
 
     def _forward(self):
         with torch.no_grad():
-            out = self.model(input_ids=self.ids, attention_mask=self.mask, position_ids=self.pos,
-                             past_key_values=self.cache, use_cache=True)
+            out = self.forward(input_ids=self.ids, attention_mask=self.mask, position_ids=self.pos,
+                               past_key_values=self.cache, use_cache=True)
             am = out.logits[0].argmax(-1) if self.batch == 1 else out.logits.argmax(-1)
             return out.logits, am
 

@@ -183,3 +183,45 @@ def test_verify_graph_replay_equals_eager(reserved):
         assert m.caches[0].stats().resident_hits > hits_before  # replays count hits
     finally:
         m.close()
+
+
+def test_lean_forward_matches_hf_forward():
+    """The lean forward (fused norms, q/k norm + rotary + cache write, fused
+    q|k|v GEMM) gives the Hugging Face forward's logits within bf16
+    tolerance, for a prefill and a tree-masked verify pass, and leaves the
+    same cache rows."""
+    from specfit_b200.runtime.kv_cache import ReservedCache
+    from specfit_b200.runtime.lean_forward import LeanQwen3Forward
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3
+
+    m = build_random_offloaded_qwen3(device=DEV, slots_per_layer=16, config=small_config(), seed=5,
+                                     std=0.05)
+    try:
+        m.warm_all_caches()
+        model = m.model
+        lean = LeanQwen3Forward(model)
+        ctx = torch.randint(0, 512, (1, 37), generator=torch.Generator().manual_seed(2)).to(DEV)
+        tree = make_tree(nodes=9, depth=4, seed=1)
+        ids = tree.verification_token_ids(torch.tensor([[5]], device=DEV))
+        mask = tree.verification_attention_mask(base_kv_length=37, device=DEV)
+        pos = tree.verification_position_ids(base_kv_length=37, device=DEV)
+        outs = []
+        caches = []
+        for fwd in (model, lean):
+            cache = ReservedCache(config=model.config, capacity=64)
+            with torch.no_grad():
+                pre = fwd(input_ids=ctx, past_key_values=cache, use_cache=True).logits
+                ver = fwd(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
+                          use_cache=True).logits
+            outs.append((pre.float(), ver.float()))
+            caches.append(cache)
+        for a, b in zip(outs[0], outs[1]):
+            cos = torch.nn.functional.cosine_similarity(a.reshape(-1, a.shape[-1]), b.reshape(-1, b.shape[-1]), dim=-1)
+            assert cos.min().item() >= 0.999
+            assert (a - b).abs().max().item() <= 5e-2
+        for la, lb in zip(caches[0].layers, caches[1].layers):
+            assert la.get_seq_length() == lb.get_seq_length() == 47
+            assert torch.allclose(la.keys.float(), lb.keys.float(), atol=2e-2, rtol=0)
+            assert torch.allclose(la.values.float(), lb.values.float(), atol=2e-2, rtol=0)
+    finally:
+        m.close()
