@@ -25,6 +25,7 @@
  *                                                               Qwen3MoeDecoderLayer.forward (residual adds)
  *   sf_qk_norm_rope       q_norm/k_norm + apply_rotary_pos_emb  transformers/...:Qwen3MoeAttention.forward
  *                         + cache update (write k, v rows)
+ *   sf_kv_compact         _compact_tree_cache                   src/specfit/runtime/eagle3_tree.py:833-858
  */
 #ifndef SPECFIT_B200_H_
 #define SPECFIT_B200_H_
@@ -393,7 +394,28 @@ SF_API int sf_add_rmsnorm(const void* x, const void* residual_in, void* residual
  * [batch, Hq, tokens, 128]; k and v go to the cache rows row0 + t (row0 read
  * from row0_device when non-NULL) of k_cache / v_cache laid out
  * [batch][Hkv][rows][128] with the given batch and head strides (elements).
+ * With both norm weights NULL the head norm is skipped (rotary only).
  */
+/*
+ * KV compaction of the accepted verify rows (_compact_tree_cache,
+ * src/specfit/runtime/eagle3_tree.py:833-858) for all layers in two launches:
+ * buffers is a device array of 2*layers base pointers (k and v of each
+ * layer, batch 1) laid out [heads][rows][head_dim] with head_stride elements
+ * between heads; rows base + src_rows[i] (device int32 [n]) move to base + i.
+ * stage: 2 * layers * n * heads * head_dim bf16 elements of scratch.
+ */
+SF_API int sf_kv_compact(const uint64_t* buffers, int layers, int heads, int head_dim,
+                         int64_t head_stride, int64_t base, const int32_t* src_rows, int n,
+                         void* stage, void* stream);
+/*
+ * Visibility words for sf_tree_attention with prefix_len 0 over a whole KV
+ * buffer: out [rows][words] int32, column c visible when c < *start_device
+ * (the committed rows, read on the device) or when 0 <= c - start < 64 and
+ * bit c - start of ancestor_sets[row] (int64) is set (a tree block of at most
+ * 64 rows starting at row start).  New: serves drafting replayed from a graph.
+ */
+SF_API int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const int64_t* start_device,
+                              int words, int32_t* out, void* stream);
 SF_API int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
                            int num_kv_heads, int head_dim, const void* q_norm_weight,
                            const void* k_norm_weight, const void* cos, const void* sin, float eps,

@@ -113,14 +113,19 @@ __global__ void qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64
     return;
   }
   const __nv_bfloat16* w = head < hq ? qw : kw;
-  float ss = 0.f;
-#pragma unroll
-  for (int v = 0; v < 4; ++v) ss += fl(xv[v]) * fl(xv[v]);
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)D + eps);
   float y[4];
+  if (w) {
+    float ss = 0.f;
 #pragma unroll
-  for (int v = 0; v < 4; ++v) y[v] = fl(bf(fl(w[lane * 4 + v]) * fl(bf(fl(xv[v]) * r))));
+    for (int v = 0; v < 4; ++v) ss += fl(xv[v]) * fl(xv[v]);
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) y[v] = fl(bf(fl(w[lane * 4 + v]) * fl(bf(fl(xv[v]) * r))));
+  } else {  // no head norm
+#pragma unroll
+    for (int v = 0; v < 4; ++v) y[v] = fl(xv[v]);
+  }
   // rotate_half: dims d < 64 take -x[d + 64], dims d >= 64 take x[d - 64] (lane +- 16).
   float other[4];
 #pragma unroll
@@ -177,8 +182,9 @@ extern "C" int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, i
   SF_CHECK_ARG(batch >= 0 && tokens >= 0 && num_heads > 0 && num_kv_heads > 0, "invalid sizes");
   const int64_t n = batch * tokens;
   if (n == 0) return SF_OK;
-  SF_CHECK_ARG(qkv && q_norm_weight && k_norm_weight && cos && sin && q_out && k_cache && v_cache,
-               "null pointer argument");
+  SF_CHECK_ARG(qkv && cos && sin && q_out && k_cache && v_cache, "null pointer argument");
+  SF_CHECK_ARG((q_norm_weight == nullptr) == (k_norm_weight == nullptr),
+               "pass both head-norm weights or neither");
   SF_CHECK_ARG(aligned16(qkv) && aligned16(q_out) && aligned16(k_cache) && aligned16(v_cache),
                "tensors must be 16-byte aligned");
   SF_CHECK_ARG(kv_batch_stride % 8 == 0 && kv_head_stride % 8 == 0, "cache strides must be multiples of 8");
@@ -189,6 +195,104 @@ extern "C" int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, i
       static_cast<const __nv_bfloat16*>(cos), static_cast<const __nv_bfloat16*>(sin), eps,
       static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
       static_cast<__nv_bfloat16*>(v_cache), kv_batch_stride, kv_head_stride, row0, row0_device);
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}
+
+namespace sf {
+namespace {
+
+// KV compaction of a verify pass over every layer at once: row base + src[i]
+// of each K and V buffer moves to base + i.  The kept rows are first
+// gathered into a caller-provided stage and then written back, in two
+// launches, so moves whose source and destination overlap are safe.  One CTA
+// per (buffer, kept row); a row is `heads` runs of D contiguous elements,
+// head_stride apart.
+__global__ void kv_gather_kernel(const uint64_t* __restrict__ bufs, int layers, int heads,
+                                 int64_t head_stride, int64_t base, const int32_t* __restrict__ src,
+                                 int n, int D, __nv_bfloat16* __restrict__ stage) {
+  const int i = blockIdx.x % n;
+  const int l2 = blockIdx.x / n;  // layer * 2 + (k or v)
+  const __nv_bfloat16* buf = reinterpret_cast<const __nv_bfloat16*>(bufs[l2]);
+  __nv_bfloat16* st = stage + ((int64_t)l2 * n + i) * heads * D;
+  for (int e = threadIdx.x * 8; e < heads * D; e += blockDim.x * 8) {
+    const int h = e / D, d = e % D;
+    *reinterpret_cast<uint4*>(st + e) =
+        *reinterpret_cast<const uint4*>(buf + h * head_stride + (base + src[i]) * D + d);
+  }
+}
+
+__global__ void kv_scatter_kernel(const uint64_t* __restrict__ bufs, int layers, int heads,
+                                  int64_t head_stride, int64_t base, int n, int D,
+                                  const __nv_bfloat16* __restrict__ stage) {
+  const int i = blockIdx.x % n;
+  const int l2 = blockIdx.x / n;
+  __nv_bfloat16* buf = reinterpret_cast<__nv_bfloat16*>(bufs[l2]);
+  const __nv_bfloat16* st = stage + ((int64_t)l2 * n + i) * heads * D;
+  for (int e = threadIdx.x * 8; e < heads * D; e += blockDim.x * 8) {
+    const int h = e / D, d = e % D;
+    *reinterpret_cast<uint4*>(buf + h * head_stride + (base + i) * D + d) =
+        *reinterpret_cast<const uint4*>(st + e);
+  }
+}
+
+}  // namespace
+}  // namespace sf
+
+extern "C" int sf_kv_compact(const uint64_t* buffers, int layers, int heads, int head_dim,
+                             int64_t head_stride, int64_t base, const int32_t* src_rows, int n,
+                             void* stage, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(layers > 0 && heads > 0 && head_dim % 8 == 0 && n >= 0, "invalid sizes");
+  SF_CHECK_ARG(head_stride % 8 == 0 && base >= 0, "invalid strides");
+  if (n == 0) return SF_OK;
+  SF_CHECK_ARG(buffers && src_rows && stage, "null pointer argument");
+  SF_CHECK_ARG(aligned16(stage), "stage must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  const unsigned grid = (unsigned)(2 * layers * n);
+  kv_gather_kernel<<<grid, 128, 0, s>>>(buffers, layers, heads, head_stride, base, src_rows, n,
+                                         head_dim, static_cast<__nv_bfloat16*>(stage));
+  SF_CHECK_LAUNCH();
+  kv_scatter_kernel<<<grid, 128, 0, s>>>(buffers, layers, heads, head_stride, base, n, head_dim,
+                                          static_cast<const __nv_bfloat16*>(stage));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}
+
+namespace sf {
+namespace {
+
+// Word w of row r: column c = 32 w + bit is visible when c < start, or when
+// 0 <= c - start < 64 and bit (c - start) of the row's ancestor set is set.
+__global__ void tree_mask_words_kernel(const int64_t* __restrict__ vis, int n,
+                                       const int64_t* __restrict__ start_dev, int words,
+                                       int32_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n * words) return;
+  const int r = (int)(i / words), w = (int)(i - (int64_t)r * words);
+  const int64_t start = *start_dev;
+  const uint64_t set = (uint64_t)vis[r];
+  uint32_t word = 0;
+  for (int bit = 0; bit < 32; ++bit) {
+    const int64_t rel = (int64_t)w * 32 + bit - start;
+    const bool on = rel < 0 || (rel < 64 && ((set >> rel) & 1ull));
+    word |= (uint32_t)on << bit;
+  }
+  out[i] = (int32_t)word;
+}
+
+}  // namespace
+}  // namespace sf
+
+extern "C" int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const int64_t* start_device,
+                                  int words, int32_t* out, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(rows >= 0 && words > 0, "invalid sizes");
+  if (rows == 0) return SF_OK;
+  SF_CHECK_ARG(ancestor_sets && start_device && out, "null pointer argument");
+  const int64_t total = (int64_t)rows * words;
+  tree_mask_words_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_stream(stream)>>>(
+      ancestor_sets, rows, start_device, words, out);
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

@@ -32,7 +32,10 @@ their ancestor mask); projections are cuBLAS GEMMs.
 expansions (top-k per node, cumulative scores, the best ``level_width``
 children) are tensor ops, rows are written at device-side offsets, each
 row's visibility is a 64-bit ancestor set inside the tree block expanded
-into a mask over the whole KV buffer, and the pool comes back in one copy.
+into a mask over the whole KV buffer (``sf_tree_mask_words``), and the pool
+comes back in one copy.  Its layer runs on the fused kernels of the lean
+target forward (``sf_add_rmsnorm``, ``sf_qk_norm_rope`` without head norms,
+fused q|k|v and gate|up GEMMs).
 Its fixed shapes let it be one CUDA graph per number of catch-up rows.
 """
 from __future__ import annotations
@@ -40,6 +43,9 @@ from __future__ import annotations
 import torch
 from torch import nn
 
+import torch.nn.functional as F
+
+from .. import _native as N
 from .. import ops
 from .eagle3_types import Eagle3DraftCandidate, Eagle3DraftCandidatePool
 
@@ -277,37 +283,61 @@ class DeviceDraft:
         self.start = z(())                            # committed rows before this cycle
         self.out = torch.zeros(self.n_cand, 5, dtype=torch.float64, device=dev)
         self._graphs: dict = {}
-        self._shift = torch.arange(32, dtype=torch.int64, device=dev)
+        with torch.no_grad():
+            self.wqkv = torch.cat((d.q_proj.weight, d.k_proj.weight, d.v_proj.weight), 0).contiguous()
+            self.wgu = torch.cat((d.gate_proj.weight, d.up_proj.weight), 0).contiguous()
+        self.inter = d.gate_proj.weight.shape[0]
+        self.inv_freq = 1.0 / (d.theta ** (torch.arange(0, d.head_dim, 2, device=dev, dtype=torch.float32)
+                                           / d.head_dim))
 
-    def _mask_words(self, vis: torch.Tensor, block_start: torch.Tensor, cap: int) -> torch.Tensor:
-        """int32 words [n, cap/32]: column c visible when c < block_start or
-        bit (c - block_start) of the row's 64-bit ancestor set is set."""
-        cols = torch.arange(cap, device=self.dev)
-        rel = cols - block_start
-        inside = (rel >= 0) & (rel < 64)
-        bits = (vis[:, None] >> rel.clamp(0, 63)[None, :]) & 1
-        m = (cols < block_start)[None, :] | (inside[None, :] & (bits == 1))
-        words = (m.view(m.shape[0], cap // 32, 32).to(torch.int64) << self._shift).sum(-1)
-        return torch.where(words >= (1 << 31), words - (1 << 32), words).to(torch.int32)
+    def _norm(self, x, res_in, res_out, w, out):
+        N.check(N.lib.sf_add_rmsnorm(x.data_ptr(), None if res_in is None else res_in.data_ptr(),
+                                     None if res_out is None else res_out.data_ptr(), w.data_ptr(),
+                                     float(self.d.eps), x.shape[0], x.shape[1], out.data_ptr(),
+                                     torch.cuda.current_stream(self.dev).cuda_stream),
+                "sf_add_rmsnorm")
+        ops._launched(1)
 
     def _rows(self, tokens, feats, pos, vis, block_start, write_at):
+        """The drafter layer over ``n`` rows written at device row
+        ``write_at``; returns (layer output, its final-norm rows)."""
         d = self.d
         n = tokens.shape[0]
+        H, D = d.hidden, d.head_dim
         cap = d._k.shape[1]
-        x = torch.cat((_rms_norm(d.embed(tokens), d.emb_norm, d.eps),
-                       _rms_norm(feats, d.hid_norm, d.eps)), dim=-1)
-        q = d.q_proj(x).view(n, d.heads, d.head_dim).transpose(0, 1)
-        k = d.k_proj(x).view(n, d.kv_heads, d.head_dim).transpose(0, 1)
-        v = d.v_proj(x).view(n, d.kv_heads, d.head_dim).transpose(0, 1)
-        q = _rope(q, pos, d.theta).contiguous()
-        rows = write_at + torch.arange(n, device=self.dev)
-        d._k.index_copy_(1, rows, _rope(k, pos, d.theta))
-        d._v.index_copy_(1, rows, v)
-        attn = ops.tree_attention(q, d._k, d._v, self._mask_words(vis, block_start, cap), 0,
-                                  scale=d.head_dim ** -0.5)
-        h = feats + d.o_proj(attn.reshape(n, d.heads * d.head_dim))
-        m = _rms_norm(h, d.post_norm, d.eps)
-        return h + d.down_proj(torch.nn.functional.silu(d.gate_proj(m)) * d.up_proj(m))
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+        e_n = torch.empty(n, H, dtype=feats.dtype, device=self.dev)
+        f_n = torch.empty_like(e_n)
+        self._norm(d.embed(tokens), None, None, d.emb_norm, e_n)
+        self._norm(feats.contiguous(), None, None, d.hid_norm, f_n)
+        qkv = F.linear(torch.cat((e_n, f_n), dim=-1), self.wqkv)
+        ang = pos.float()[:, None] * self.inv_freq[None, :]
+        ang = torch.cat((ang, ang), dim=-1)
+        cos, sin = ang.cos().to(feats.dtype), ang.sin().to(feats.dtype)
+        q = torch.empty(d.heads, n, D, dtype=feats.dtype, device=self.dev)
+        N.check(N.lib.sf_qk_norm_rope(qkv.data_ptr(), 1, n, d.heads, d.kv_heads, D, None, None,
+                                      cos.data_ptr(), sin.data_ptr(), float(d.eps), q.data_ptr(),
+                                      d._k.data_ptr(), d._v.data_ptr(), d.kv_heads * cap * D, cap * D,
+                                      0, write_at.data_ptr(), stream), "sf_qk_norm_rope")
+        words = torch.empty(n, cap // 32, dtype=torch.int32, device=self.dev)
+        N.check(N.lib.sf_tree_mask_words(vis.data_ptr(), n, block_start.data_ptr(), cap // 32,
+                                         words.data_ptr(), stream), "sf_tree_mask_words")
+        ops._launched(2)
+        attn = ops.tree_attention(q, d._k, d._v, words, 0, scale=D ** -0.5)
+        o = F.linear(attn.reshape(n, d.heads * D), d.o_proj.weight)
+        h = torch.empty_like(e_n)
+        m = torch.empty_like(e_n)
+        self._norm(o, feats.contiguous(), h, d.post_norm, m)
+        gu = F.linear(m, self.wgu)
+        dn = F.linear(F.silu(gu[:, : self.inter]) * gu[:, self.inter:], d.down_proj.weight)
+        out = torch.empty_like(e_n)
+        hn = torch.empty_like(e_n)
+        self._norm(dn, h, out, d.final_norm, hn)
+        return out, hn
+
+    def _log_probs(self, hn):
+        logits = F.linear(hn, self.d.lm_head.weight).float()
+        return torch.log_softmax(logits * self.d.logit_scale, dim=-1)
 
     def _draft(self, n_new: int) -> None:
         """The whole drafting of one cycle as device work (captured)."""
@@ -320,11 +350,11 @@ class DeviceDraft:
         chain = (torch.ones((), dtype=torch.int64, device=dev) << torch.arange(1, n_new + 1, device=dev)) - 1
         # Catch-up rows are causal among themselves after the committed rows;
         # the seed row (last) opens the tree block at row seed_pos.
-        h = self._rows(toks, feats, pos, chain, self.start, self.start)
+        h, hn = self._rows(toks, feats, pos, chain, self.start, self.start)
         block = seed_pos
         seed_h = h[-1:]
         one = torch.ones((), dtype=torch.int64, device=dev)
-        lp = d._log_probs(seed_h)[0]
+        lp = self._log_probs(hn[-1:])[0]
         cond, tok = torch.topk(lp, self.widths[0])
         cum = cond.double()
         parent = torch.full((self.widths[0],), -1, dtype=torch.long, device=dev)  # -1 = the seed
@@ -338,9 +368,10 @@ class DeviceDraft:
             w = tok.shape[0]
             own = one << torch.arange(row_next, row_next + w, device=dev)
             vis = par_vis | own
-            hl = self._rows(tok, hidden_parent, seed_pos + depth + 0 * tok, vis, block, block + row_next)
+            hl, hln = self._rows(tok, hidden_parent, seed_pos + depth + 0 * tok, vis, block,
+                                 block + row_next)
             row_next += w
-            v, t = torch.topk(d._log_probs(hl), self.top_k, dim=-1)          # [w, k]
+            v, t = torch.topk(self._log_probs(hln), self.top_k, dim=-1)      # [w, k]
             score = cum[:, None] + v.double()
             best, flat = torch.topk(score.reshape(-1), self.widths[depth])    # the level's nodes
             pj = torch.div(flat, self.top_k, rounding_mode="floor")

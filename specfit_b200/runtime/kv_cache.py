@@ -149,9 +149,18 @@ def compact_tree_cache_(cache, *, base_kv_length: int, verification_positions: t
     layers expose ``keys`` / ``values``; reserved layers move rows inside
     their buffers."""
     expected = base_kv_length + verification_node_count
-    src = None
     n = len(verification_positions)
-    for layer in cache.layers:
+    layers = cache.layers
+    if (layers and all(isinstance(l, ReservedLayer) and l.is_initialized for l in layers)
+            and layers[0]._kbuf.is_cuda and layers[0]._kbuf.shape[0] == 1
+            and layers[0]._kbuf.dtype == torch.bfloat16):
+        if any(l.get_seq_length() != expected for l in layers):
+            raise RuntimeError("target cache layer has an unexpected length")
+        _compact_native(cache, base_kv_length, verification_positions)
+        cache.crop(base_kv_length + n)
+        return
+    src = None
+    for layer in layers:
         if layer.get_seq_length() != expected:
             raise RuntimeError("target cache layer has an unexpected length")
         if src is None or src.device != layer.keys.device:
@@ -162,3 +171,31 @@ def compact_tree_cache_(cache, *, base_kv_length: int, verification_positions: t
         layer.keys[..., base_kv_length:base_kv_length + n, :].copy_(k)
         layer.values[..., base_kv_length:base_kv_length + n, :].copy_(v)
     cache.crop(base_kv_length + n)
+
+
+def _compact_native(cache, base: int, positions: tuple) -> None:
+    """All layers' accepted rows moved in two launches (``sf_kv_compact``)."""
+    from .. import _native as N
+    from .. import ops
+
+    layers = cache.layers
+    l0 = layers[0]
+    dev = l0._kbuf.device
+    ptrs = tuple(p for l in layers for p in (l._kbuf.data_ptr(), l._vbuf.data_ptr()))
+    table = getattr(cache, "_compact_table", None)
+    if table is None or table[0] != ptrs:
+        heads, cap, d = l0._kbuf.shape[1], l0.capacity, l0._kbuf.shape[3]
+        if any(l._kbuf.shape[1:] != l0._kbuf.shape[1:] or l.capacity != cap for l in layers):
+            raise ValueError("every layer must share one reserved shape")
+        dev_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        stage = torch.empty(2 * len(layers) * 16 * heads * d, dtype=torch.bfloat16, device=dev)
+        table = cache._compact_table = (ptrs, dev_ptrs, stage, heads, cap, d)
+    _, dev_ptrs, stage, heads, cap, d = table
+    n = len(positions)
+    if n > 16:
+        raise ValueError("at most 16 kept rows per compaction")
+    src = torch.tensor(positions, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+    N.check(N.lib.sf_kv_compact(dev_ptrs.data_ptr(), len(layers), heads, d, cap * d, base,
+                                src.data_ptr(), n, stage.data_ptr(),
+                                torch.cuda.current_stream(dev).cuda_stream), "sf_kv_compact")
+    ops._launched(2)

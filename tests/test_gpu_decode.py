@@ -136,3 +136,30 @@ def test_device_drafting_matches_eager_drafting():
         dd.release()
     finally:
         m.close()
+
+
+def test_native_compaction_matches_generic():
+    """All-layer KV compaction in two launches (sf_kv_compact) moves the same
+    rows as per-layer index_select + copy, including overlapping moves."""
+    from specfit_b200.runtime.kv_cache import ReservedCache, compact_tree_cache_
+
+    cfg = qwen3_moe_config(3)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    caches = [ReservedCache(config=cfg, capacity=64) for _ in range(2)]
+    for n in (30, 8):
+        for layer in range(3):
+            k = torch.randn(1, 4, n, 128, generator=g, device="cuda").to(torch.bfloat16)
+            v = torch.randn(1, 4, n, 128, generator=g, device="cuda").to(torch.bfloat16)
+            for c in caches:
+                c.update(k, v, layer)
+    pos = (0, 1, 3, 4, 7)
+    compact_tree_cache_(caches[0], base_kv_length=30, verification_positions=pos, verification_node_count=8)
+    ref = caches[1]
+    for layer in ref.layers:
+        src = torch.tensor([30 + p for p in pos], device="cuda")
+        kk, vv = layer.keys.index_select(-2, src), layer.values.index_select(-2, src)
+        layer.keys[..., 30:35, :].copy_(kk)
+        layer.values[..., 30:35, :].copy_(vv)
+    ref.crop(35)
+    for a, b in zip(caches[0].layers, ref.layers):
+        assert torch.equal(a.keys, b.keys) and torch.equal(a.values, b.values)
