@@ -26,6 +26,8 @@
  *   sf_qk_norm_rope       q_norm/k_norm + apply_rotary_pos_emb  transformers/...:Qwen3MoeAttention.forward
  *                         + cache update (write k, v rows)
  *   sf_kv_compact         _compact_tree_cache                   src/specfit/runtime/eagle3_tree.py:833-858
+ *   sf_logsoftmax_topk    log_softmax + topk of a drafter level src/specfit/runtime/eagle3_tree.py:611-803
+ *                                                               (candidate-pool expansion)
  */
 #ifndef SPECFIT_B200_H_
 #define SPECFIT_B200_H_
@@ -416,6 +418,16 @@ SF_API int sf_kv_compact(const uint64_t* buffers, int layers, int heads, int hea
  */
 SF_API int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const int64_t* start_device,
                               int words, int32_t* out, void* stream);
+/*
+ * Log-softmax of scale * logits (bf16 [rows][vocab], row-major) and its k
+ * largest entries per row, in one launch (one CTA per row): top_values
+ * [rows][k] fp32 log-probabilities, top_indices [rows][k] int64, larger first
+ * and the lower index first among equal values.  1 <= k <= 8.  The
+ * log-probability of logit y is (scale*y - max) - log(sum exp(scale*y - max)),
+ * summed in fp32.
+ */
+SF_API int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, float scale, int k,
+                              float* top_values, int64_t* top_indices, void* stream);
 SF_API int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
                            int num_kv_heads, int head_dim, const void* q_norm_weight,
                            const void* k_norm_weight, const void* cos, const void* sin, float eps,

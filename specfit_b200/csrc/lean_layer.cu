@@ -296,3 +296,173 @@ extern "C" int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const 
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
+
+namespace sf {
+namespace {
+
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int kMaxTopk = 8;
+
+__device__ __forceinline__ bool topk_better(float a, int ai, float b, int bi) {
+  return a > b || (a == b && ai < bi);
+}
+
+// The K largest (value, index) pairs seen, larger value first and lower index
+// first among equal values; held in registers (fully unrolled insertion).
+template <int K>
+struct TopK {
+  float v[K];
+  int i[K];
+  __device__ void init() {
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      v[j] = -INFINITY;
+      i[j] = 0x7fffffff;
+    }
+  }
+  __device__ void push(float x, int xi) {
+    if (!topk_better(x, xi, v[K - 1], i[K - 1])) return;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      if (topk_better(x, xi, v[j], i[j])) {
+        const float tv = v[j];
+        const int ti = i[j];
+        v[j] = x;
+        i[j] = xi;
+        x = tv;
+        xi = ti;
+      }
+    }
+  }
+  __device__ void pop_front() {
+#pragma unroll
+    for (int j = 0; j + 1 < K; ++j) {
+      v[j] = v[j + 1];
+      i[j] = i[j + 1];
+    }
+    v[K - 1] = -INFINITY;
+    i[K - 1] = 0x7fffffff;
+  }
+  // The warp's k best over every lane's list; round r's winner in (bv, bi)
+  // is handed to emit(r, bv, bi) on every lane.
+  template <typename Emit>
+  __device__ void warp_merge(int k, Emit emit) {
+    for (int r = 0; r < k; ++r) {
+      float bv = v[0];
+      int bi = i[0];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (topk_better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      emit(r, bv, bi);
+      if (i[0] == bi && v[0] == bv) pop_front();  // indices are unique: only the owner pops
+    }
+  }
+};
+
+// Online (max, sum of exponentials) merge of two partial states.
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+  m = mm;
+}
+
+// One CTA per row of bf16 logits: log-softmax of scale * logits and its
+// top-k in one pass over the row (16-byte loads, online max / sum of
+// exponentials and a register top-k per thread, merged per warp and then
+// across warps).  Outputs (y - max) - log(sum), y = scale * logit in fp32.
+template <int K>
+__global__ void __launch_bounds__(kTopkThreads)
+logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, float scale, int k,
+                       float* __restrict__ top_v, int64_t* __restrict__ top_i) {
+  __shared__ float s_m[kTopkWarps], s_s[kTopkWarps];
+  __shared__ float c_v[kTopkWarps * K];
+  __shared__ int c_i[kTopkWarps * K];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* x = logits + row * vocab;
+  float m = -INFINITY, sum = 0.f;
+  TopK<K> t;
+  t.init();
+  auto take = [&](float y, int c) {
+    if (y > m) {
+      sum = sum * __expf(m - y) + 1.f;
+      m = y;
+    } else if (y != -INFINITY) {
+      sum += __expf(y - m);
+    }
+    t.push(y, c);
+  };
+  const bool vec = (vocab % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  if (vec) {
+    const int64_t n8 = vocab / 8;
+    const uint4* x8 = reinterpret_cast<const uint4*>(x);
+    for (int64_t c = threadIdx.x; c < n8; c += kTopkThreads) {
+      const uint4 u = __ldg(x8 + c);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) take(__bfloat162float(e[j]) * scale, (int)(c * 8 + j));
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < vocab; c += kTopkThreads) take(__bfloat162float(x[c]) * scale, (int)c);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+    lse_merge(m, sum, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, sum, o));
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_s[warp] = sum;
+  }
+  t.warp_merge(k, [&](int r, float bv, int bi) {
+    if (lane == 0) {
+      c_v[warp * K + r] = bv;
+      c_i[warp * K + r] = bi;
+    }
+  });
+  __syncthreads();
+  if (warp != 0) return;
+  float M = s_m[lane], S = s_s[lane];  // kTopkWarps == 32: one warp's state per lane
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+    lse_merge(M, S, __shfl_xor_sync(0xffffffffu, M, o), __shfl_xor_sync(0xffffffffu, S, o));
+  const float log_s = logf(S);
+  TopK<K> f;
+  f.init();
+  for (int r = 0; r < k; ++r) f.push(c_v[lane * K + r], c_i[lane * K + r]);
+  f.warp_merge(k, [&](int r, float bv, int bi) {
+    if (lane == 0) {
+      top_v[row * k + r] = (bv - M) - log_s;
+      top_i[row * k + r] = bi;
+    }
+  });
+}
+
+static_assert(kTopkWarps == 32, "the cross-warp merge maps one warp per lane");
+
+}  // namespace
+}  // namespace sf
+
+extern "C" int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, float scale, int k,
+                                  float* top_values, int64_t* top_indices, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(rows >= 0 && rows <= 0x7fffffff && vocab > 0 && vocab < (1LL << 31), "invalid sizes");
+  SF_CHECK_ARG(k >= 1 && k <= kMaxTopk && k <= vocab, "k must be in [1, %d] and at most vocab", kMaxTopk);
+  if (rows == 0) return SF_OK;
+  SF_CHECK_ARG(logits && top_values && top_indices, "null pointer argument");
+  auto* x = static_cast<const __nv_bfloat16*>(logits);
+  const dim3 grid((unsigned)rows);
+  cudaStream_t s = as_stream(stream);
+  if (k <= 1) logsoftmax_topk_kernel<1><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
+  else if (k <= 2) logsoftmax_topk_kernel<2><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
+  else if (k <= 4) logsoftmax_topk_kernel<4><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
+  else logsoftmax_topk_kernel<8><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}

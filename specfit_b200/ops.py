@@ -429,3 +429,26 @@ def ep_combine(returned: torch.Tensor, send: EpSend, top_k_index: torch.Tensor,
                                  res.data_ptr(), _stream(dev)), "sf_moe_combine")
     _launched(1)
     return res
+
+
+def logsoftmax_topk(logits: torch.Tensor, k: int, scale: float = 1.0,
+                    out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """``torch.topk(torch.log_softmax(logits.float() * scale, -1), k)`` over the
+    last dim of bf16 logits in one launch: (values fp32, indices int64), each
+    ``[..., k]``.  Among equal values the lower index comes first."""
+    dev = _require_cuda(logits)
+    if logits.dtype != torch.bfloat16:
+        raise TypeError("logsoftmax_topk takes bf16 logits")
+    x = logits.contiguous()
+    V = x.shape[-1]
+    rows = x.numel() // V if V else 0
+    shape = tuple(x.shape[:-1]) + (k,)
+    if out is None:
+        vals = torch.empty(shape, dtype=torch.float32, device=dev)
+        idx = torch.empty(shape, dtype=torch.int64, device=dev)
+    else:
+        vals, idx = out
+    N.check(N.lib.sf_logsoftmax_topk(x.data_ptr(), rows, V, float(scale), int(k), vals.data_ptr(),
+                                     idx.data_ptr(), _stream(dev)), "sf_logsoftmax_topk")
+    _launched(1 if rows else 0)
+    return vals, idx

@@ -154,9 +154,11 @@ class Eagle3DrafterStandIn(nn.Module):
         m = _rms_norm(h, self.post_norm, self.eps)
         return h + self.down_proj(torch.nn.functional.silu(self.gate_proj(m)) * self.up_proj(m))
 
-    def _log_probs(self, h: torch.Tensor) -> torch.Tensor:
-        logits = self.lm_head(_rms_norm(h, self.final_norm, self.eps)).float()
-        return torch.log_softmax(logits * self.logit_scale, dim=-1)
+    def _top(self, h: torch.Tensor, k: int):
+        """The k most likely next tokens of each row: (log-probs, ids), one
+        fused log-softmax + top-k launch over the lm_head logits."""
+        logits = self.lm_head(_rms_norm(h, self.final_norm, self.eps))
+        return ops.logsoftmax_topk(logits, k, self.logit_scale)
 
     # -------------------------------------------------------------- drafting
     def build_candidate_pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
@@ -182,7 +184,7 @@ class Eagle3DrafterStandIn(nn.Module):
         h = self._rows(toks, feats, pos, _bits(chain, dev), self._len)
         committed_rows = self._len - 1  # the tree block starts at the seed row
         seed_hidden = h[-1]
-        vals, idx = torch.topk(self._log_probs(h[-1:])[0], min(top_k, first_width))
+        vals, idx = (t[0] for t in self._top(h[-1:], min(top_k, first_width)))
         cands: list = []
         vis = {0: 1}  # raw id -> visibility bitset inside the tree block (seed = bit 0)
         rows_in_block = 1
@@ -206,7 +208,7 @@ class Eagle3DrafterStandIn(nn.Module):
             steps += 1
             for j, raw in enumerate(frontier):
                 hidden_of[raw] = hl[j]
-            v, t = torch.topk(self._log_probs(hl), top_k, dim=-1)
+            v, t = self._top(hl, top_k)
             options = []
             for j, raw in enumerate(frontier):
                 base = cands[raw - 1].cumulative_log_probability
@@ -335,9 +337,8 @@ class DeviceDraft:
         self._norm(dn, h, out, d.final_norm, hn)
         return out, hn
 
-    def _log_probs(self, hn):
-        logits = F.linear(hn, self.d.lm_head.weight).float()
-        return torch.log_softmax(logits * self.d.logit_scale, dim=-1)
+    def _top(self, hn, k):
+        return ops.logsoftmax_topk(F.linear(hn, self.d.lm_head.weight), k, self.d.logit_scale)
 
     def _draft(self, n_new: int) -> None:
         """The whole drafting of one cycle as device work (captured)."""
@@ -354,8 +355,7 @@ class DeviceDraft:
         block = seed_pos
         seed_h = h[-1:]
         one = torch.ones((), dtype=torch.int64, device=dev)
-        lp = self._log_probs(hn[-1:])[0]
-        cond, tok = torch.topk(lp, self.widths[0])
+        cond, tok = (t[0] for t in self._top(hn[-1:], self.widths[0]))
         cum = cond.double()
         parent = torch.full((self.widths[0],), -1, dtype=torch.long, device=dev)  # -1 = the seed
         par_vis = torch.ones(self.widths[0], dtype=torch.int64, device=dev)       # seed = bit 0
@@ -371,7 +371,7 @@ class DeviceDraft:
             hl, hln = self._rows(tok, hidden_parent, seed_pos + depth + 0 * tok, vis, block,
                                  block + row_next)
             row_next += w
-            v, t = torch.topk(self._log_probs(hln), self.top_k, dim=-1)      # [w, k]
+            v, t = self._top(hln, self.top_k)                                # [w, k]
             score = cum[:, None] + v.double()
             best, flat = torch.topk(score.reshape(-1), self.widths[depth])    # the level's nodes
             pj = torch.div(flat, self.top_k, rounding_mode="floor")
@@ -409,6 +409,17 @@ class DeviceDraft:
             self._draft(n_new)
         self._graphs[n_new] = graph
         return graph
+
+    def prepare(self) -> None:
+        """Capture the graph of every row count 1..max_new now (their warm-up
+        writes land past the committed rows and are overwritten later), so no
+        capture happens between cycles."""
+        d = self.d
+        if d._fed == 0:
+            raise RuntimeError("prepare after the eager catch-up of a sequence")
+        self.start.fill_(d._len)
+        for n in range(1, self.max_new + 1):
+            self._graph(n)
 
     def pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
              pending_seed: torch.Tensor) -> Eagle3DraftCandidatePool:

@@ -324,6 +324,8 @@ class B200TreeSpeculator:
                             fed_ids=fed, aux_history=aux, pending_seed=pending, top_k=self.top_k,
                             max_depth=min(self.max_depth, remaining - 1), first_width=self.first_width,
                             level_width=self.level_width)
+                        if self._ddraft is not None and len(self._ddraft._graphs) < self._ddraft.max_new:
+                            self._ddraft.prepare()  # every drafting graph, before the next cycle
                 tick()
                 tb = time.perf_counter()
                 toks = torch.tensor((pool.seed_token_id,) + tuple(c.target_token_id for c in pool.candidates),

@@ -339,6 +339,44 @@ def test_tree_attention_full_mask_and_long_context(ops):
     assert np.abs(got - ref).max() <= ATOL_BF16 and cosine(got, ref) >= COS_MIN
 
 
+# ------------------------------------------- drafter log-softmax + top-k
+
+
+@pytest.mark.parametrize("rows,vocab,k", [(1, 151936, 4), (8, 151936, 4), (3, 151936, 8), (5, 1001, 1),
+                                          (2, 7, 7), (1, 8, 8), (4, 4096, 2)])
+def test_logsoftmax_topk_matches_torch(ops, rows, vocab, k):
+    """One launch of log_softmax(scale * logits) + top-k equals torch's fp32
+    log_softmax then a stable descending sort: ids equal (equal values in
+    ascending id order), values within 2e-5 (fp32 sums in another order)."""
+    g = torch.Generator(device="cuda").manual_seed(rows * 131 + vocab + k)
+    x = (torch.randn(rows, vocab, generator=g, device=DEV) * 3).to(torch.bfloat16)
+    v, i = ops.logsoftmax_topk(x, k, scale=4.5)
+    ref = torch.log_softmax(x.float() * 4.5, dim=-1)
+    order = torch.sort(ref, dim=-1, descending=True, stable=True).indices[:, :k]  # ties: lower id first
+    for r in range(rows):
+        order_r = order[r].tolist()
+        assert i[r].tolist() == order_r
+        assert torch.allclose(v[r], ref[r, i[r]], atol=2e-5, rtol=0)
+
+
+def test_logsoftmax_topk_ties_and_shapes(ops):
+    """Equal logits come out lowest index first; leading dims are kept; an
+    unaligned row start takes the scalar path and agrees."""
+    x = torch.zeros(2, 3, 40, dtype=torch.bfloat16, device=DEV)
+    x[..., 5] = 1
+    x[..., 9] = 1
+    v, i = ops.logsoftmax_topk(x, 4)
+    assert v.shape == i.shape == (2, 3, 4)
+    assert i[0, 0].tolist() == [5, 9, 0, 1]
+    ref = torch.log_softmax(x.float(), -1)[0, 0]
+    assert torch.allclose(v[0, 0], ref[[5, 9, 0, 1]], atol=1e-6, rtol=0)
+    base = torch.randn(1, 1 + 2048, device=DEV).to(torch.bfloat16)
+    view = base[:, 1:]  # starts 2 bytes past a 16-byte boundary
+    a = ops.logsoftmax_topk(view, 8)
+    b = ops.logsoftmax_topk(view.clone(), 8)
+    assert torch.equal(a[1], b[1]) and torch.allclose(a[0], b[0], atol=1e-6, rtol=0)
+
+
 def test_device_status_clean(ops):
     from specfit_b200 import _native
 
