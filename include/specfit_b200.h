@@ -420,8 +420,9 @@ SF_API int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const int6
                               int words, int32_t* out, void* stream);
 /*
  * Log-softmax of scale * logits (bf16 [rows][vocab], row-major) and its k
- * largest entries per row, in one launch (one CTA per row): top_values
- * [rows][k] fp32 log-probabilities, top_indices [rows][k] int64, larger first
+ * largest entries per row, in one launch (a cluster of 8 CTAs per row;
+ * rows <= 65535): top_values [rows][k] fp32 log-probabilities, top_indices
+ * [rows][k] int64, larger first
  * and the lower index first among equal values.  1 <= k <= 8.  The
  * log-probability of logit y is (scale*y - max) - log(sum exp(scale*y - max)),
  * summed in fp32.

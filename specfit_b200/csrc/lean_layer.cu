@@ -20,6 +20,13 @@
 // Sums of squares are fp32 in a fixed order (per-thread, then a butterfly),
 // which may differ from torch's reduction order in the last bit of the
 // variance; outputs agree with the torch chain to bf16 rounding.
+//
+// Further down, the per-cycle steps around the verify pass: all-layer KV
+// compaction of the accepted rows (sf_kv_compact), visibility words of a
+// device-resident tree block (sf_tree_mask_words), and the drafter's fused
+// log-softmax + top-k over the vocabulary (sf_logsoftmax_topk).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace sf {
@@ -300,8 +307,11 @@ extern "C" int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const 
 namespace sf {
 namespace {
 
-constexpr int kTopkThreads = 1024;
+namespace cg = cooperative_groups;
+
+constexpr int kTopkThreads = 512;
 constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int kTopkCluster = 8;  // CTAs per row, merged through distributed shared memory
 constexpr int kMaxTopk = 8;
 
 __device__ __forceinline__ bool topk_better(float a, int ai, float b, int bi) {
@@ -344,8 +354,8 @@ struct TopK {
     v[K - 1] = -INFINITY;
     i[K - 1] = 0x7fffffff;
   }
-  // The warp's k best over every lane's list; round r's winner in (bv, bi)
-  // is handed to emit(r, bv, bi) on every lane.
+  // The warp's k best over every lane's list; round r's winner (bv, bi) is
+  // handed to emit(r, bv, bi) on every lane.
   template <typename Emit>
   __device__ void warp_merge(int k, Emit emit) {
     for (int r = 0; r < k; ++r) {
@@ -361,7 +371,7 @@ struct TopK {
         }
       }
       emit(r, bv, bi);
-      if (i[0] == bi && v[0] == bv) pop_front();  // indices are unique: only the owner pops
+      if (i[0] == bi && v[0] == bv) pop_front();  // real indices are unique: only the owner pops
     }
   }
 };
@@ -374,19 +384,28 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
   m = mm;
 }
 
-// One CTA per row of bf16 logits: log-softmax of scale * logits and its
-// top-k in one pass over the row (16-byte loads, online max / sum of
-// exponentials and a register top-k per thread, merged per warp and then
-// across warps).  Outputs (y - max) - log(sum), y = scale * logit in fp32.
+// Log-softmax of scale * logits (bf16 rows) and its top-k.  A cluster of 8
+// CTAs shares one row: each CTA streams one eighth of it (16-byte loads, two
+// in flight per thread), keeping an online max / sum of exponentials and a
+// register top-k per thread, merged per warp and then per CTA; CTA 0 of the
+// cluster merges the eight partials through distributed shared memory and
+// writes (y - max) - log(sum), y = scale * logit in fp32.
 template <int K>
-__global__ void __launch_bounds__(kTopkThreads)
+__global__ void __cluster_dims__(kTopkCluster, 1, 1) __launch_bounds__(kTopkThreads)
 logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, float scale, int k,
                        float* __restrict__ top_v, int64_t* __restrict__ top_i) {
   __shared__ float s_m[kTopkWarps], s_s[kTopkWarps];
   __shared__ float c_v[kTopkWarps * K];
   __shared__ int c_i[kTopkWarps * K];
-  const int64_t row = blockIdx.x;
+  __shared__ float p_ms[2];  // this CTA's (max, sum)
+  __shared__ float p_v[K];
+  __shared__ int p_i[K];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int64_t row = blockIdx.y;
   const __nv_bfloat16* x = logits + row * vocab;
+  const int64_t chunk = ((vocab + 7) / 8 + kTopkCluster - 1) / kTopkCluster * 8;
+  const int64_t lo = min(vocab, crank * chunk), hi = min(vocab, lo + chunk);
   float m = -INFINITY, sum = 0.f;
   TopK<K> t;
   t.init();
@@ -399,18 +418,25 @@ logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, 
     }
     t.push(y, c);
   };
-  const bool vec = (vocab % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-  if (vec) {
-    const int64_t n8 = vocab / 8;
-    const uint4* x8 = reinterpret_cast<const uint4*>(x);
-    for (int64_t c = threadIdx.x; c < n8; c += kTopkThreads) {
-      const uint4 u = __ldg(x8 + c);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+  auto take8 = [&](const uint4& u, int64_t c8) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) take(__bfloat162float(e[j]) * scale, (int)(c * 8 + j));
+    for (int j = 0; j < 8; ++j) take(__bfloat162float(e[j]) * scale, (int)(c8 * 8 + j));
+  };
+  const bool vec = (vocab % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  if (vec) {  // lo and hi are multiples of 8 here
+    const uint4* x8 = reinterpret_cast<const uint4*>(x);
+    const int64_t hi8 = hi / 8;
+    for (int64_t c = lo / 8 + threadIdx.x; c < hi8; c += 2 * kTopkThreads) {
+      const uint4 u0 = __ldg(x8 + c);
+      const bool two = c + kTopkThreads < hi8;
+      uint4 u1 = make_uint4(0, 0, 0, 0);
+      if (two) u1 = __ldg(x8 + c + kTopkThreads);
+      take8(u0, c);
+      if (two) take8(u1, c + kTopkThreads);
     }
   } else {
-    for (int64_t c = threadIdx.x; c < vocab; c += kTopkThreads) take(__bfloat162float(x[c]) * scale, (int)c);
+    for (int64_t c = lo + threadIdx.x; c < hi; c += kTopkThreads) take(__bfloat162float(x[c]) * scale, (int)c);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -427,24 +453,53 @@ logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, 
     }
   });
   __syncthreads();
-  if (warp != 0) return;
-  float M = s_m[lane], S = s_s[lane];  // kTopkWarps == 32: one warp's state per lane
+  if (warp == 0) {  // this CTA's partial
+    float M = lane < kTopkWarps ? s_m[lane] : -INFINITY;
+    float S = lane < kTopkWarps ? s_s[lane] : 0.f;
 #pragma unroll
-  for (int o = 16; o; o >>= 1)
-    lse_merge(M, S, __shfl_xor_sync(0xffffffffu, M, o), __shfl_xor_sync(0xffffffffu, S, o));
-  const float log_s = logf(S);
-  TopK<K> f;
-  f.init();
-  for (int r = 0; r < k; ++r) f.push(c_v[lane * K + r], c_i[lane * K + r]);
-  f.warp_merge(k, [&](int r, float bv, int bi) {
+    for (int o = 16; o; o >>= 1)
+      lse_merge(M, S, __shfl_xor_sync(0xffffffffu, M, o), __shfl_xor_sync(0xffffffffu, S, o));
+    TopK<K> f;
+    f.init();
+    if (lane < kTopkWarps)
+      for (int r = 0; r < k; ++r) f.push(c_v[lane * K + r], c_i[lane * K + r]);
+    f.warp_merge(k, [&](int r, float bv, int bi) {
+      if (lane == 0) {
+        p_v[r] = bv;
+        p_i[r] = bi;
+      }
+    });
     if (lane == 0) {
-      top_v[row * k + r] = (bv - M) - log_s;
-      top_i[row * k + r] = bi;
+      p_ms[0] = M;
+      p_ms[1] = S;
     }
-  });
+  }
+  cluster.sync();  // every CTA's partial is in its shared memory
+  if (crank == 0 && warp == 0) {
+    float M = -INFINITY, S = 0.f;
+    TopK<K> f;
+    f.init();
+    if (lane < kTopkCluster) {
+      const float* ms = cluster.map_shared_rank(p_ms, lane);
+      const float* pv = cluster.map_shared_rank(p_v, lane);
+      const int* pi = cluster.map_shared_rank(p_i, lane);
+      M = ms[0];
+      S = ms[1];
+      for (int r = 0; r < k; ++r) f.push(pv[r], pi[r]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      lse_merge(M, S, __shfl_xor_sync(0xffffffffu, M, o), __shfl_xor_sync(0xffffffffu, S, o));
+    const float log_s = logf(S);
+    f.warp_merge(k, [&](int r, float bv, int bi) {
+      if (lane == 0) {
+        top_v[row * k + r] = (bv - M) - log_s;
+        top_i[row * k + r] = bi;
+      }
+    });
+  }
+  cluster.sync();  // peers keep their shared memory until CTA 0 has read it
 }
-
-static_assert(kTopkWarps == 32, "the cross-warp merge maps one warp per lane");
 
 }  // namespace
 }  // namespace sf
@@ -452,12 +507,12 @@ static_assert(kTopkWarps == 32, "the cross-warp merge maps one warp per lane");
 extern "C" int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, float scale, int k,
                                   float* top_values, int64_t* top_indices, void* stream) {
   using namespace sf;
-  SF_CHECK_ARG(rows >= 0 && rows <= 0x7fffffff && vocab > 0 && vocab < (1LL << 31), "invalid sizes");
+  SF_CHECK_ARG(rows >= 0 && rows <= 65535 && vocab > 0 && vocab < (1LL << 31), "invalid sizes");
   SF_CHECK_ARG(k >= 1 && k <= kMaxTopk && k <= vocab, "k must be in [1, %d] and at most vocab", kMaxTopk);
   if (rows == 0) return SF_OK;
   SF_CHECK_ARG(logits && top_values && top_indices, "null pointer argument");
   auto* x = static_cast<const __nv_bfloat16*>(logits);
-  const dim3 grid((unsigned)rows);
+  const dim3 grid(kTopkCluster, (unsigned)rows);
   cudaStream_t s = as_stream(stream);
   if (k <= 1) logsoftmax_topk_kernel<1><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
   else if (k <= 2) logsoftmax_topk_kernel<2><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);

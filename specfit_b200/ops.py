@@ -269,6 +269,21 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits:
     return res
 
 
+def tree_mask_words(ancestor_sets: torch.Tensor, start: torch.Tensor, words: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Visibility words over a whole KV buffer for ``tree_attention`` with
+    prefix 0: row r sees column c when c < start (a device int64 scalar: the
+    committed rows) or when bit c - start of ``ancestor_sets[r]`` (int64) is
+    set.  Returns int32 ``[rows, words]`` (``sf_tree_mask_words``)."""
+    dev = _require_cuda(ancestor_sets, start)
+    rows = ancestor_sets.shape[0]
+    res = out if out is not None else torch.empty(rows, words, dtype=torch.int32, device=dev)
+    N.check(N.lib.sf_tree_mask_words(ancestor_sets.contiguous().data_ptr(), rows, start.data_ptr(),
+                                     words, res.data_ptr(), _stream(dev)), "sf_tree_mask_words")
+    _launched(1 if rows else 0)
+    return res
+
+
 def tree_bits_from_parents(parent_ids, device) -> torch.Tensor:
     """Ancestor bitmask of a verification tree: row i (0 = the pending seed,
     i >= 1 = node i) has bit j set when column j is i itself or an ancestor

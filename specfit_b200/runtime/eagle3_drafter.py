@@ -284,6 +284,11 @@ class DeviceDraft:
         self.aux = z(max_new, d.fc.in_features, dt=d.fc.weight.dtype)  # their features' sources
         self.start = z(())                            # committed rows before this cycle
         self.out = torch.zeros(self.n_cand, 5, dtype=torch.float64, device=dev)
+        self._host_out = torch.empty(self.n_cand, 5, dtype=torch.float64).pin_memory()
+        self._host_extra: dict = {}
+        # Optional device work appended to every drafting graph: called as
+        # post(seed [1] int64, out [n_cand, 5] float64) after the pool is built.
+        self.post = None
         self._graphs: dict = {}
         with torch.no_grad():
             self.wqkv = torch.cat((d.q_proj.weight, d.k_proj.weight, d.v_proj.weight), 0).contiguous()
@@ -389,6 +394,8 @@ class DeviceDraft:
             out_depth.append(torch.full((tok.shape[0],), float(depth + 1), dtype=torch.float64, device=dev))
         self.out.copy_(torch.stack((torch.cat(out_tok).double(), torch.cat(out_par).double(),
                                     torch.cat(out_cond), torch.cat(out_cum), torch.cat(out_depth)), dim=1))
+        if self.post is not None:
+            self.post(self.tokens[n_new - 1: n_new], self.out)
 
     def _graph(self, n_new: int):
         if getattr(self, "_kptr", None) != self.d._k.data_ptr():
@@ -421,8 +428,12 @@ class DeviceDraft:
         for n in range(1, self.max_new + 1):
             self._graph(n)
 
-    def pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
-             pending_seed: torch.Tensor) -> Eagle3DraftCandidatePool:
+    def pool_arrays(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
+                    pending_seed: torch.Tensor, extra: tuple = ()):
+        """Drafts one pool (graph replay) and reads back, with one host
+        synchronisation, the pool rows ``[n_cand, 5]`` (token, parent index or
+        -1, conditional and cumulative log-probability, depth; generation
+        order) as a numpy array, plus each device tensor in ``extra``."""
         d = self.d
         L = fed_ids.shape[1]
         start = d._fed
@@ -434,9 +445,24 @@ class DeviceDraft:
         self.aux[:n_new].copy_(aux_history[start - 1:L])
         self.start.fill_(d._len)
         self._graph(n_new).replay()
-        rows = self.out.cpu().tolist()
+        self._host_out.copy_(self.out, non_blocking=True)
+        hosts = []
+        for t in extra:
+            h = self._host_extra.get(t.data_ptr())
+            if h is None or h.shape != t.shape or h.dtype != t.dtype:
+                h = self._host_extra[t.data_ptr()] = torch.empty(t.shape, dtype=t.dtype).pin_memory()
+            h.copy_(t, non_blocking=True)
+            hosts.append(h.numpy())
+        torch.cuda.current_stream(self.dev).synchronize()
         d._len += n_new       # committed rows + the seed row stay; tree rows are dropped
         d._fed = L + 1
+        return self._host_out.numpy(), hosts
+
+    def pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,
+             pending_seed: torch.Tensor) -> Eagle3DraftCandidatePool:
+        n_new = fed_ids.shape[1] + 1 - self.d._fed
+        arr, _ = self.pool_arrays(fed_ids=fed_ids, aux_history=aux_history, pending_seed=pending_seed)
+        rows = arr.tolist()
         cands = []
         for i, (t, par, cond, _, depth) in enumerate(rows):
             par = int(par)

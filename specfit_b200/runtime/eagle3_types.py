@@ -282,3 +282,36 @@ class Eagle3DraftCandidatePool:
             cumulative_log_probabilities=tuple(c.cumulative_log_probability for c in chosen),
             source_raw_ids=tuple(c.raw_id for c in chosen),
         )
+
+
+def tree_from_arrays(selected_raw_ids: tuple, token_ids, parent_raw_ids, depths, conditional_log_probs,
+                     cumulative_log_probs) -> Eagle3DraftTree:
+    """``Eagle3DraftCandidatePool.to_tree`` for a pool held as arrays indexed
+    by raw id - 1 (parent raw id 0 = the seed; generation order = raw id
+    order), for callers that never build the candidate objects.  Same checks
+    on the selection; the tree validates itself."""
+    from math import exp
+
+    n = len(token_ids)
+    if not isinstance(selected_raw_ids, tuple):
+        raise ValueError("selected raw IDs must be an immutable tuple")
+    if any(not _is_int(r) or r <= 0 for r in selected_raw_ids):
+        raise ValueError("selected raw IDs must be positive integers")
+    if len(set(selected_raw_ids)) != len(selected_raw_ids):
+        raise ValueError("selected raw IDs must be unique")
+    if any(r > n for r in selected_raw_ids):
+        raise ValueError("selected raw ID is absent from the pool")
+    keep = set(selected_raw_ids)
+    chosen = sorted(int(r) for r in selected_raw_ids)
+    if any(int(parent_raw_ids[r - 1]) != 0 and int(parent_raw_ids[r - 1]) not in keep for r in chosen):
+        raise ValueError("selected candidates must be ancestor-closed")
+    node_of = {r: i for i, r in enumerate(chosen, start=1)}
+    return Eagle3DraftTree(
+        token_ids=tuple(int(token_ids[r - 1]) for r in chosen),
+        parent_ids=tuple(0 if int(parent_raw_ids[r - 1]) == 0 else node_of[int(parent_raw_ids[r - 1])]
+                         for r in chosen),
+        depths=tuple(int(depths[r - 1]) for r in chosen),
+        conditional_probabilities=tuple(exp(float(conditional_log_probs[r - 1])) for r in chosen),
+        cumulative_log_probabilities=tuple(float(cumulative_log_probs[r - 1]) for r in chosen),
+        source_raw_ids=tuple(chosen),
+    )

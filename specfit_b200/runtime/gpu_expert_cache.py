@@ -420,7 +420,7 @@ class GpuExpertCache:
         """Adds a device-side count of resident hits (no host sync)."""
         if self._device_hits is None:
             self._device_hits = torch.zeros((), dtype=torch.int64, device=self.device)
-        self._device_hits.add_(count.reshape(()).to(torch.int64))
+        self._device_hits.add_(count.reshape(()))  # int32 into the int64 total, one launch
 
     def _flush_device_hits(self) -> None:
         if self._device_hits is not None:

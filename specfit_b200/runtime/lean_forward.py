@@ -64,7 +64,10 @@ class LeanQwen3Forward:
 
     @torch.no_grad()
     def __call__(self, input_ids, attention_mask=None, position_ids=None, past_key_values=None,
-                 logits_to_keep: int = 0, use_cache: bool = True):
+                 logits_to_keep: int = 0, use_cache: bool = True, attention_words=None):
+        """``attention_words`` (int32 ``[B, T, words]``, e.g. from
+        ``ops.tree_mask_words``) replaces ``attention_mask``: visibility bits
+        over every cache row (prefix 0)."""
         cache = past_key_values
         if cache is None or not all(isinstance(l, ReservedLayer) for l in cache.layers):
             raise ValueError("the lean forward needs a ReservedCache")
@@ -115,7 +118,10 @@ class LeanQwen3Forward:
                                           None if row0_dev is None else row0_dev.data_ptr(), stream),
                     "sf_qk_norm_rope")
             ops._launched(1)
-            if attention_mask is None:
+            if attention_words is not None:
+                bits = [attention_words[b] for b in range(B)]
+                prefix = 0
+            elif attention_mask is None:
                 bits = [_causal_bits(T, dev)] * B
                 prefix = kv_len - T
             else:

@@ -42,8 +42,10 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from .. import ops
 from .. import selection as sel
 from .. import synthetic
+from .eagle3_types import tree_from_arrays
 from .kv_cache import ReservedCache, compact_tree_cache_
 from .tree_attention import clear_mask_cache
 
@@ -117,9 +119,10 @@ class B200TreeSpeculator:
         self.layers, self.experts, self.route_k = (cfg.num_hidden_layers, cfg.num_experts,
                                                    cfg.num_experts_per_tok)
         self.graphs = graphs
+        self.lean = lean
         self.reserve_tokens = reserve_tokens  # KV capacity to reserve (graphs keep one cache)
         self._aux: dict = {}
-        self._override = None  # [q, layers, K] routes of the verify rows
+        self._override = None  # [layers, q, K] routes of the verify rows (each layer contiguous)
         self._graphs: dict = {}
         self._offset = None
         self._cache = None
@@ -130,6 +133,17 @@ class B200TreeSpeculator:
             self._ddraft = DeviceDraft(drafter, top_k=top_k, max_depth=max_depth,
                                        first_width=first_width, level_width=level_width,
                                        max_new=1 + max_depth)
+            # The pool as device buffers (row 0 = the seed, row r = raw id r):
+            # tokens, their synthetic routes and route footprints, written by
+            # every drafting graph and read by every verify graph.
+            dev = drafter.fc.weight.device
+            rows = 1 + self._ddraft.n_cand
+            words = (self.layers * self.experts + 63) // 64
+            self._pool_tok = torch.zeros(rows, dtype=torch.long, device=dev)
+            self._pool_routes = torch.zeros(rows, self.layers, self.route_k, dtype=torch.long, device=dev)
+            self._pool_fp = torch.zeros(rows, words, dtype=torch.long, device=dev)
+            self._ddraft.post = self._post_draft
+        self._pos_host = torch.zeros(64, dtype=torch.long).pin_memory() if torch.cuda.is_available() else None
 
     # ------------------------------------------------------------- hooks
     def _install(self):
@@ -142,7 +156,7 @@ class B200TreeSpeculator:
             def route(mod, args, out, l=l):
                 if self._override is None:
                     return None
-                return out[0], out[1], self._override[:, l, :]
+                return out[0], out[1], self._override[l]
             hooks.append(layer.mlp.gate.register_forward_hook(route))
         return hooks
 
@@ -152,61 +166,98 @@ class B200TreeSpeculator:
                           for li in self.drafter.layer_indices], dim=-1)
 
     # ------------------------------------------------------------- graphs
+    def _routes_into(self) -> None:
+        """Routes and footprints of every pool row (device work)."""
+        r = synthetic.token_routes(self._pool_tok, self.layers, experts=self.experts,
+                                   top_k=self.route_k, seed=self.route_seed)
+        self._pool_routes.copy_(r)
+        sel.footprints_device(r, self.experts, out=self._pool_fp)
+
+    def _post_draft(self, seed: torch.Tensor, out: torch.Tensor) -> None:
+        """Appended to each drafting graph: the pool's tokens into the pool
+        buffers, then their routes and footprints."""
+        self._pool_tok[:1].copy_(seed)
+        self._pool_tok[1:].copy_(out[:, 0])
+        self._routes_into()
+
     def _graph(self, q: int, cache):
+        """The verify graph of ``q`` rows.  Its inputs are one device int64
+        block ``vin [3, q]`` (pool row of each verify row, position,
+        ancestor set over the tree block) plus the pool buffers; token ids,
+        the route override and the visibility words are built inside the
+        graph."""
         g = self._graphs.get(q)
         if g is not None:
             return g
         dev = self.model.model.embed_tokens.weight.device
         cap = cache.layers[0].capacity
-        ids = torch.zeros(1, q, dtype=torch.long, device=dev)
-        pos = torch.zeros(1, q, dtype=torch.long, device=dev)
-        mask = torch.zeros(1, 1, q, cap, dtype=torch.bool, device=dev)
-        routes = torch.zeros(q, self.layers, self.route_k, dtype=torch.long, device=dev)
         base = cache.get_seq_length()
         if base + q > cap:
             raise RuntimeError("the reserved cache cannot hold the verification rows")
+        vin = torch.zeros(3, q, dtype=torch.long, device=dev)
+        ar = torch.arange(q, device=dev)
+        vin[0] = ar
+        vin[1] = base + ar
+        vin[2] = (torch.ones_like(ar) << (ar + 1)) - 1  # a chain: warm-up and capture inputs
+        routes = torch.zeros(self.layers, q, self.route_k, dtype=torch.long, device=dev)
+        words = (cap + 31) // 32
         self._offset.fill_(base)  # warm-up writes land past the committed rows
-        mask[..., :base] = True
-        mask[..., base:base + q] = torch.tril(torch.ones(q, q, dtype=torch.bool, device=dev))
         cache.set_static(self._offset, cap - q)
         self._override = routes
+
+        def body():
+            rows, pos, anc = vin[0], vin[1], vin[2]
+            ids = self._pool_tok.index_select(0, rows).view(1, q)
+            routes.copy_(self._pool_routes.index_select(0, rows).transpose(0, 1))
+            if self.lean:
+                w = ops.tree_mask_words(anc, self._offset, words)
+                out = self.fwd(input_ids=ids, attention_words=w.view(1, q, words),
+                               position_ids=pos.view(1, q), past_key_values=cache, use_cache=True)
+            else:
+                rel = torch.arange(cap, device=dev) - self._offset
+                bit = (anc.view(q, 1) >> rel.clamp(0, 63).view(1, cap)) & 1
+                vis = (rel < 0).view(1, cap) | ((rel < 64).view(1, cap) & bit.bool())
+                out = self.fwd(input_ids=ids, attention_mask=vis.view(1, 1, q, cap),
+                               position_ids=pos.view(1, q), past_key_values=cache, use_cache=True)
+            return ids, out.logits[0].argmax(-1), self._features()
+
         try:
             side = torch.cuda.Stream(device=dev)
             side.wait_stream(torch.cuda.current_stream(dev))
             with torch.cuda.stream(side), torch.no_grad():
                 for _ in range(2):
-                    self.fwd(input_ids=ids, attention_mask=mask, position_ids=pos,
-                               past_key_values=cache, use_cache=True)
+                    body()
             torch.cuda.current_stream(dev).wait_stream(side)
             torch.cuda.synchronize(dev)
             clear_mask_cache()
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph), torch.no_grad():
-                out = self.fwd(input_ids=ids, attention_mask=mask, position_ids=pos,
-                                 past_key_values=cache, use_cache=True)
-                argmax = out.logits[0].argmax(-1)
-                feats = self._features()
+                ids, argmax, feats = body()
             clear_mask_cache()
         finally:
             self._override = None
             cache.set_static(None)
             cache.set_length(base)
-        g = dict(graph=graph, ids=ids, pos=pos, mask=mask, routes=routes, argmax=argmax, feats=feats)
+        # Every buffer the graph reads or writes that was allocated outside
+        # the capture stays referenced here (routes: the override buffer).
+        g = dict(graph=graph, vin=vin, vin_host=torch.zeros(3, q, dtype=torch.long).pin_memory(),
+                 routes=routes, ids=ids, argmax=argmax, feats=feats)
         self._graphs[q] = g
         return g
 
-    def _verify_graph(self, cache, tree, pending, routes_sel, base: int):
+    def _verify_graph(self, cache, tree, base: int):
+        """Replays the verify graph for ``tree`` over pool rows
+        ``(0,) + tree.source_raw_ids`` at committed length ``base``: one
+        host-to-device copy of the [3, q] input block."""
         q = 1 + tree.draft_node_count
         g = self._graph(q, cache)
-        dev = g["ids"].device
-        g["ids"].copy_(tree.verification_token_ids(pending))
-        g["pos"].copy_(tree.verification_position_ids(base_kv_length=base, device="cpu")
-                       .to(dev, non_blocking=True))
-        m = g["mask"]
-        m[..., : base + q].copy_(tree.verification_attention_mask(base_kv_length=base, device="cpu")
-                                 .to(dev, non_blocking=True))
-        m[..., base + q:] = False
-        g["routes"].copy_(routes_sel)
+        h = g["vin_host"].numpy()
+        h[0, 0], h[1, 0], h[2, 0] = 0, base, 1
+        anc = [1]
+        for i, (raw, par, dep) in enumerate(zip(tree.source_raw_ids, tree.parent_ids, tree.depths), 1):
+            anc.append(anc[par] | (1 << i))
+            h[0, i], h[1, i], h[2, i] = raw, base + dep, anc[i]
+        g["vin"].copy_(g["vin_host"], non_blocking=True)
         self._offset.fill_(base)
         g["graph"].replay()
         cache.set_length(base + q)
@@ -233,7 +284,6 @@ class B200TreeSpeculator:
         cache = self._cache
         if not self.graphs or cache is None or not cache.layers[0].is_initialized:
             raise RuntimeError("calibration needs the verify graphs and a prefilled cache")
-        dev = self._offset.device
         base = cache.get_seq_length()
         rng = np.random.default_rng(seed)
         vocab = self.model.config.vocab_size
@@ -244,17 +294,15 @@ class B200TreeSpeculator:
                 toks = [int(t) for t in rng.integers(0, vocab, size=n + 1)]
                 tree = Eagle3DraftTree(tuple(toks[1:]), tuple(range(n)), tuple(range(1, n + 1)),
                                        (0.5,) * n, tuple(np.log(0.5) * np.arange(1, n + 1)))
-                routes = synthetic.token_routes(torch.tensor(toks, device=dev), self.layers,
-                                                experts=self.experts, top_k=self.route_k,
-                                                seed=self.route_seed)
-                union = int(np.unpackbits(np.bitwise_or.reduce(
-                    sel.footprints(routes.cpu().numpy(), self.experts), axis=0).view(np.uint8)).sum())
-                pending = torch.tensor([[toks[0]]], device=dev)
+                self._pool_tok[: n + 1].copy_(torch.tensor(toks))
+                self._routes_into()
+                fp = self._pool_fp[: n + 1].cpu().numpy().view(np.uint64)
+                union = int(np.unpackbits(np.bitwise_or.reduce(fp, axis=0).view(np.uint8)).sum())
                 times = []
                 for _ in range(reps + 1):
                     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     s.record()
-                    self._verify_graph(cache, tree, pending, routes, base)
+                    self._verify_graph(cache, tree, base)
                     e.record()
                     e.synchronize()
                     cache.set_length(base)
@@ -299,9 +347,17 @@ class B200TreeSpeculator:
             with torch.no_grad():
                 out = self.fwd(input_ids=input_ids, past_key_values=cache, use_cache=True,
                                  logits_to_keep=1)
-            aux = self._features()
+            # Committed tokens and their target features live in preallocated
+            # buffers; fed / aux are views of their filled rows.
+            rows_max = ctx + max_new_tokens + q_max + 1
+            feats0 = self._features()
+            fed_buf = torch.empty(1, rows_max, dtype=input_ids.dtype, device=dev)
+            aux_buf = torch.empty(rows_max, feats0.shape[1], dtype=feats0.dtype, device=dev)
+            fed_buf[:, :ctx].copy_(input_ids)
+            aux_buf[:ctx].copy_(feats0)
+            L = ctx
+            fed, aux = fed_buf[:, :L], aux_buf[:L]
             pending = out.logits[:, -1:].argmax(-1)
-            fed = input_ids
             if self.graphs:
                 for q in range(1, q_max + 1):  # every tree size, captured once
                     self._graph(q, cache)
@@ -314,11 +370,27 @@ class B200TreeSpeculator:
                     result.tokens.append(int(pending.reshape(-1)[0]))
                     break
                 ta = time.perf_counter()
-                n_new = fed.shape[1] + 1 - self.drafter._fed
+                n_new = L + 1 - self.drafter._fed
+                max_nodes = min(self.max_nodes, remaining - 1)
+                routes = None
                 with torch.no_grad():
                     if (self._ddraft is not None and self.drafter._fed > 0 and remaining - 1 >= self.max_depth
                             and n_new <= self._ddraft.max_new):
-                        pool = self._ddraft.pool(fed_ids=fed, aux_history=aux, pending_seed=pending)
+                        # Device drafting: pool rows and footprints in one read-back.
+                        arr, (fp,) = self._ddraft.pool_arrays(fed_ids=fed, aux_history=aux,
+                                                              pending_seed=pending, extra=(self._pool_fp,))
+                        tb = time.perf_counter()
+                        tok = arr[:, 0].astype(np.int64)
+                        par = arr[:, 1].astype(np.int64) + 1  # raw parent ids (0 = the seed)
+                        cond = np.minimum(arr[:, 2], 0.0)
+                        depth = arr[:, 4].astype(np.int64)
+                        cum = np.empty_like(cond)
+                        for i in range(len(cum)):
+                            cum[i] = cond[i] + (cum[par[i] - 1] if par[i] else 0.0)
+                        ids = sel.search(par, cum, fp[: 1 + len(tok)].view(np.uint64), self.cost_model,
+                                         None, max_nodes=max_nodes)
+                        tree = tree_from_arrays(tuple(ids), tok, par, depth, cond, cum)
+                        n_pool = len(tok)
                     else:
                         pool = self.drafter.build_candidate_pool(
                             fed_ids=fed, aux_history=aux, pending_seed=pending, top_k=self.top_k,
@@ -326,31 +398,35 @@ class B200TreeSpeculator:
                             level_width=self.level_width)
                         if self._ddraft is not None and len(self._ddraft._graphs) < self._ddraft.max_new:
                             self._ddraft.prepare()  # every drafting graph, before the next cycle
+                        tb = time.perf_counter()
+                        toks = torch.tensor((pool.seed_token_id,) + tuple(c.target_token_id for c in pool.candidates))
+                        n_pool = len(pool.candidates)
+                        if self.graphs:
+                            self._pool_tok[: n_pool + 1].copy_(toks)
+                            self._routes_into()
+                            fp = self._pool_fp[: n_pool + 1].cpu().numpy().view(np.uint64)
+                        else:
+                            routes = synthetic.token_routes(toks.to(dev), self.layers, experts=self.experts,
+                                                            top_k=self.route_k, seed=self.route_seed)
+                            fp = sel.footprints(routes.cpu().numpy(), self.experts)
+                        ids = sel.search([c.parent_raw_id for c in pool.candidates],
+                                         [c.cumulative_log_probability for c in pool.candidates],
+                                         fp, self.cost_model, None, max_nodes=max_nodes)
+                        tree = pool.to_tree(tuple(ids))
                 tick()
-                tb = time.perf_counter()
-                toks = torch.tensor((pool.seed_token_id,) + tuple(c.target_token_id for c in pool.candidates),
-                                    device=dev)
-                routes = synthetic.token_routes(toks, self.layers, experts=self.experts,
-                                                top_k=self.route_k, seed=self.route_seed)
-                ids = sel.search([c.parent_raw_id for c in pool.candidates],
-                                 [c.cumulative_log_probability for c in pool.candidates],
-                                 sel.footprints(routes.cpu().numpy(), self.experts), self.cost_model,
-                                 None, max_nodes=min(self.max_nodes, remaining - 1))
-                tree = pool.to_tree(tuple(ids))
                 tc = time.perf_counter()
                 base = cache.get_seq_length()
-                routes_sel = routes[[0] + list(ids)]
                 if self.graphs:
-                    verify_ids, verifier, q_aux = self._verify_graph(cache, tree, pending, routes_sel, base)
+                    verify_ids, verifier, q_aux = self._verify_graph(cache, tree, base)
                 else:
                     verify_ids = tree.verification_token_ids(pending)
                     mask = tree.verification_attention_mask(base_kv_length=base, device=dev)
                     pos = tree.verification_position_ids(base_kv_length=base, device=dev)
-                    self._override = routes_sel
+                    self._override = routes[[0] + list(tree.source_raw_ids)].transpose(0, 1).contiguous()
                     try:
                         with torch.no_grad():
                             vout = self.fwd(input_ids=verify_ids, attention_mask=mask,
-                                              position_ids=pos, past_key_values=cache, use_cache=True)
+                                            position_ids=pos, past_key_values=cache, use_cache=True)
                     finally:
                         self._override = None
                     q_aux = self._features()
@@ -359,16 +435,20 @@ class B200TreeSpeculator:
                 td = time.perf_counter()
                 path = self.acceptance.path(tree)
                 positions = (0,) + path
+                n = len(positions)
                 compact_tree_cache_(cache, base_kv_length=base, verification_positions=positions,
                                     verification_node_count=verify_ids.shape[1])
-                ptens = torch.tensor(positions, device=dev)
-                committed = verify_ids[:, ptens]
-                fed = torch.cat((fed, committed), dim=1)
-                aux = torch.cat((aux, q_aux.index_select(0, ptens)), dim=0)
+                ph = self._pos_host[:n]
+                ph.numpy()[:] = positions
+                ptens = ph.to(dev, non_blocking=True)
+                torch.index_select(verify_ids, 1, ptens, out=fed_buf[:, L:L + n])
+                torch.index_select(q_aux, 0, ptens, out=aux_buf[L:L + n])
                 pending = verifier[positions[-1]].reshape(1, 1).clone()
-                result.tokens.extend(committed[0].tolist())
+                result.tokens.extend(fed_buf[0, L:L + n].tolist())
+                L += n
+                fed, aux = fed_buf[:, :L], aux_buf[:L]
                 te = time.perf_counter()
-                result.cycles.append(CycleRecord(len(pool.candidates), len(ids), len(path),
+                result.cycles.append(CycleRecord(n_pool, len(ids), len(path),
                                                  (tb - ta) * 1e3, (tc - tb) * 1e3, (td - tc) * 1e3,
                                                  (te - td) * 1e3))
             torch.cuda.synchronize(dev)

@@ -130,6 +130,24 @@ def footprints(routes: np.ndarray, experts: int = EXPERTS) -> np.ndarray:
     return out
 
 
+def footprints_device(routes, experts: int = EXPERTS, out=None):
+    """``footprints`` as device work (graph-capturable torch ops): ``routes``
+    int64 ``[tokens, layers, top_k]`` with distinct experts per (token,
+    layer) -> int64 ``[tokens, words]`` with the same bits (bit layer*experts
+    + expert).  Distinct bits make the scatter-add an OR (no carries); no
+    validation is done here (the native packer validates)."""
+    import torch
+
+    n, layers, k = routes.shape
+    words = (layers * experts + 63) // 64
+    bit = (torch.arange(layers, device=routes.device, dtype=torch.int64).view(1, layers, 1) * experts
+           + routes).reshape(n, layers * k)
+    res = out if out is not None else torch.empty(n, words, dtype=torch.int64, device=routes.device)
+    res.zero_()
+    res.scatter_add_(1, bit >> 6, torch.ones_like(bit) << (bit & 63))
+    return res
+
+
 def pack_routes(pool, atlas) -> np.ndarray:
     """Validate complete top-8 routes of the seed (raw 0) and every node and
     pack them (cf. ``_pack_routes``, ``specfit_exact.py:18-49``)."""

@@ -216,10 +216,16 @@ def token_routes(tokens, layers: int = NUM_LAYERS, *, experts: int = NUM_EXPERTS
         x = x ^ (x >> shift)
     u = ((x & ((1 << 52) - 1)).to(torch.float64) + 0.5) / float(1 << 52)
     gumbel = -torch.log(-torch.log(u))
-    rng = np.random.default_rng(seed * 7919 + 17)
-    perms = np.stack([rng.permutation(experts) for _ in range(layers)])
-    ranks = np.empty((layers, experts), dtype=np.float64)
-    for li in range(layers):
-        ranks[li, perms[li]] = np.arange(1, experts + 1)
-    logw = torch.from_numpy(-s * np.log(ranks)).to(dev).unsqueeze(0)
+    key = (layers, experts, float(s), seed, str(dev))
+    logw = _ZIPF_LOGW.get(key)
+    if logw is None:
+        rng = np.random.default_rng(seed * 7919 + 17)
+        perms = np.stack([rng.permutation(experts) for _ in range(layers)])
+        ranks = np.empty((layers, experts), dtype=np.float64)
+        for li in range(layers):
+            ranks[li, perms[li]] = np.arange(1, experts + 1)
+        logw = _ZIPF_LOGW[key] = torch.from_numpy(-s * np.log(ranks)).to(dev).unsqueeze(0)
     return torch.topk(logw + gumbel, top_k, dim=-1).indices
+
+
+_ZIPF_LOGW: dict = {}  # (layers, experts, s, seed, device) -> per-layer Zipf log-weights

@@ -44,6 +44,37 @@ def test_pool_to_tree_and_validation():
         Eagle3DraftCandidatePool(9, 2, 3, tuple(bad[:3]), 3, 3)
 
 
+def test_tree_from_arrays_matches_pool_to_tree():
+    """The array form of to_tree (the device-drafting fast path) builds the
+    same tree and refuses the same selections."""
+    from specfit_b200.runtime.eagle3_types import tree_from_arrays
+
+    pool = small_pool()
+    c = pool.candidates
+    arrays = (np.array([x.target_token_id for x in c]), np.array([x.parent_raw_id for x in c]),
+              np.array([x.depth for x in c]), np.array([x.conditional_log_probability for x in c]),
+              np.array([x.cumulative_log_probability for x in c]))
+    for sel_ids in ((1, 3, 4), (4, 3, 1), (2,), (1, 2, 3)):
+        a, b = pool.to_tree(sel_ids), tree_from_arrays(sel_ids, *arrays)
+        assert a.token_ids == b.token_ids and a.parent_ids == b.parent_ids and a.depths == b.depths
+        assert a.source_raw_ids == b.source_raw_ids
+        assert np.allclose(a.conditional_probabilities, b.conditional_probabilities)
+        assert np.allclose(a.cumulative_log_probabilities, b.cumulative_log_probabilities)
+    for bad, msg in (((3,), "ancestor-closed"), ((7,), "absent"), ((1, 1), "unique"), ([1], "tuple")):
+        with pytest.raises(ValueError, match=msg):
+            tree_from_arrays(bad, *arrays)
+
+
+def test_device_footprints_match_native_packer():
+    """footprints_device (the in-graph packing) sets the bits of the native
+    packer sf_specfit_pack_routes."""
+    from specfit_b200 import selection as sel
+
+    r = synthetic.token_routes(torch.arange(61) * 977 + 5, 48, experts=128, top_k=8, seed=3)
+    assert np.array_equal(sel.footprints(r.numpy(), 128),
+                          sel.footprints_device(r, 128).numpy().view(np.uint64))
+
+
 def test_acceptance_walk_follows_first_accepted_child():
     tree = small_pool().to_tree((1, 2, 3, 4))
     acc = BernoulliAcceptance(seed=3)
