@@ -132,8 +132,8 @@ SF_API int sf_router_topk_noalloc(const void* hidden, const void* router_weight,
  *   inv_pos[T*K]: inverse permutation (route position -> sorted row);
  *   active[E]: experts with a non-empty group, ascending, -1 padded;
  *   num_active[1].
- * An expert id outside [0, E) sets *error_flag to 1 (device int32, caller
- * zeroes it) and that route is dropped.  Requires E <= 1024.
+ * *error_flag (device int32) is set to 1 if an expert id lies outside
+ * [0, E) (that route is dropped), else to 0.  Requires E <= 1024.
  */
 SF_API int sf_moe_dispatch(const int64_t* topk_index, int64_t tokens, int top_k, int num_experts,
                     int32_t* counts, int32_t* offsets, int32_t* sorted_pos, int32_t* inv_pos,
@@ -420,12 +420,12 @@ SF_API int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const int6
                               int words, int32_t* out, void* stream);
 /*
  * Log-softmax of scale * logits (bf16 [rows][vocab], row-major) and its k
- * largest entries per row, in one launch (a cluster of 8 CTAs per row;
- * rows <= 65535): top_values [rows][k] fp32 log-probabilities, top_indices
- * [rows][k] int64, larger first
+ * largest entries per row, in one launch (a cluster of 16 CTAs per row, 8
+ * where 16 cannot be co-scheduled; rows <= 65535): top_values [rows][k] fp32
+ * log-probabilities, top_indices [rows][k] int64, larger first
  * and the lower index first among equal values.  1 <= k <= 8.  The
  * log-probability of logit y is (scale*y - max) - log(sum exp(scale*y - max)),
- * summed in fp32.
+ * summed in fp32.  Each row must hold at least k finite values of scale*y.
  */
 SF_API int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, float scale, int k,
                               float* top_values, int64_t* top_indices, void* stream);

@@ -19,6 +19,8 @@ template <typename T, int kV>
 __global__ void combine_kernel(const T* __restrict__ ys, const int32_t* __restrict__ inv_pos,
                                const int64_t* __restrict__ idx, const int32_t* __restrict__ rank,
                                int E, int K, int H, int reduce, T* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int order_rows[kMaxK];
   __shared__ int n_valid;
   const int64_t t = blockIdx.x;
@@ -86,12 +88,14 @@ int launch_combine(const void* ys, const int32_t* inv_pos, const int64_t* idx, c
   const int threads = 256;
   if (vec) {
     dim3 grid((unsigned)tokens, (unsigned)((H / kV + threads - 1) / threads));
-    combine_kernel<T, kV><<<grid, threads, 0, stream>>>(static_cast<const T*>(ys), inv_pos, idx,
-                                                        rank, E, K, H, reduce, static_cast<T*>(out));
+    SF_CHECK_CUDA(launch_pdl(combine_kernel<T, kV>, dim3(grid), dim3(threads), 0, stream,
+                             static_cast<const T*>(ys), inv_pos, idx, rank, E, K, H, reduce,
+                             static_cast<T*>(out)));
   } else {
     dim3 grid((unsigned)tokens, (unsigned)((H + threads - 1) / threads));
-    combine_kernel<T, 1><<<grid, threads, 0, stream>>>(static_cast<const T*>(ys), inv_pos, idx,
-                                                       rank, E, K, H, reduce, static_cast<T*>(out));
+    SF_CHECK_CUDA(launch_pdl(combine_kernel<T, 1>, dim3(grid), dim3(threads), 0, stream,
+                             static_cast<const T*>(ys), inv_pos, idx, rank, E, K, H, reduce,
+                             static_cast<T*>(out)));
   }
   SF_CHECK_LAUNCH();
   return SF_OK;

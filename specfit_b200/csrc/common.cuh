@@ -6,7 +6,9 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <string>
+#include <utility>
 
 #include "specfit_b200.h"
 
@@ -49,6 +51,68 @@ int once_per_device(std::atomic<unsigned long long>& done, F&& f) {
   const int rc = f();
   if (rc == SF_OK) done.fetch_or(bit, std::memory_order_release);
   return rc;
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.
+//
+// The kernels of a verify pass run back to back on one stream, most of them
+// for a few microseconds.  Launched with programmatic stream serialization,
+// a kernel's CTAs are scheduled while its predecessor is still running and
+// block in pdl_wait() until the predecessor has completed and its writes
+// are visible, so launch and rasterisation overlap the predecessor's tail.
+// Every kernel launched this way calls pdl_wait() before its first global
+// memory access (and before any early return), which also keeps the chain
+// transitive: a kernel's completion implies its predecessors'.  Each calls
+// pdl_trigger() right after, letting its own successor be scheduled once
+// all of its CTAs are resident.  Without the launch attribute both are
+// no-ops.  SF_PDL=0 in the environment launches everything plainly.
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SF_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// cudaLaunchKernelEx with programmatic stream serialization (when enabled)
+// and, if cluster_x > 0, a (cluster_x, cluster_y, 1) cluster shape.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, unsigned cluster_x, unsigned cluster_y,
+                               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, stream, 0u, 0u, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

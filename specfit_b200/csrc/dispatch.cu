@@ -17,6 +17,7 @@ namespace {
 // Expert ids of the routes as given by the router (int64).  Anything
 // outside [0, 2^31) maps to -2, which the grouping reports as invalid.
 struct RouteIds {
+  static constexpr bool kResetError = true;  // sf_moe_dispatch sets *error_flag to 0 or 1
   const int64_t* idx;
   __device__ __forceinline__ int size() const { return 0; }  // the count is passed explicitly
   __device__ __forceinline__ int operator()(int p) const {
@@ -30,6 +31,8 @@ __global__ void gather_kernel(const T* __restrict__ hidden, int H, const W* __re
                               int K, const int32_t* __restrict__ sorted_pos, int64_t rows,
                               T* __restrict__ hidden_sorted, float* __restrict__ w_sorted,
                               bool vec) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t r = blockIdx.x;
   if (r >= rows) return;
   const int32_t p = sorted_pos[r];
@@ -58,13 +61,15 @@ int launch_gather_w(const void* hidden, int64_t tokens, int H, const void* topk_
   const bool vec = (H % (16 / (int)sizeof(T)) == 0) && aligned16(hidden) && aligned16(hidden_sorted);
   const int threads = 128;
   if (wdt == SF_DTYPE_F32)
-    gather_kernel<T, float><<<(unsigned)rows, threads, 0, stream>>>(
-        static_cast<const T*>(hidden), H, static_cast<const float*>(topk_w), K, sorted_pos, rows,
-        static_cast<T*>(hidden_sorted), w_sorted, vec);
+    SF_CHECK_CUDA(launch_pdl(gather_kernel<T, float>, dim3((unsigned)rows), dim3(threads), 0,
+                             stream, static_cast<const T*>(hidden), H,
+                             static_cast<const float*>(topk_w), K, sorted_pos, rows,
+                             static_cast<T*>(hidden_sorted), w_sorted, vec));
   else
-    gather_kernel<T, __nv_bfloat16><<<(unsigned)rows, threads, 0, stream>>>(
-        static_cast<const T*>(hidden), H, static_cast<const __nv_bfloat16*>(topk_w), K, sorted_pos,
-        rows, static_cast<T*>(hidden_sorted), w_sorted, vec);
+    SF_CHECK_CUDA(launch_pdl(gather_kernel<T, __nv_bfloat16>, dim3((unsigned)rows), dim3(threads),
+                             0, stream, static_cast<const T*>(hidden), H,
+                             static_cast<const __nv_bfloat16*>(topk_w), K, sorted_pos, rows,
+                             static_cast<T*>(hidden_sorted), w_sorted, vec));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
@@ -89,9 +94,9 @@ extern "C" int sf_moe_dispatch(const int64_t* topk_index, int64_t tokens, int to
   if (smem > 48 * 1024)
     SF_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
-  kernel<<<1, grouping::kThreads, smem, as_stream(stream)>>>(
-      RouteIds{topk_index}, n, num_experts, false, counts, offsets, sorted_pos, inv_pos, active,
-      num_active, error_flag, nullptr);
+  SF_CHECK_CUDA(launch_pdl(kernel, dim3(1), dim3(grouping::kThreads), smem, as_stream(stream),
+                           RouteIds{topk_index}, n, num_experts, false, counts, offsets, sorted_pos,
+                           inv_pos, active, num_active, error_flag, nullptr));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

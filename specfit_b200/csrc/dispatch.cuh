@@ -11,7 +11,8 @@
 // The expert id of position p comes from `src(p)`; when n < 0 the number of
 // positions is `src.size()`, read on the device.  An id of -1 is a padding
 // slot when `pad_ok` (skipped silently); any other id outside [0, E) sets
-// *error_flag and is skipped.  When `compact` is non-null it receives, for
+// *error_flag and is skipped (with Src::kResetError the kernel first zeroes
+// the flag).  When `compact` is non-null it receives, for
 // the q-th valid position in increasing position order, that route's sorted
 // row: compact[q] = inv_pos[p].
 #pragma once
@@ -61,6 +62,8 @@ group_kernel(Src src, int n, int E, bool pad_ok, int32_t* __restrict__ counts,
              int32_t* __restrict__ inv_pos, int32_t* __restrict__ active,
              int32_t* __restrict__ num_active, int32_t* __restrict__ error_flag,
              int32_t* __restrict__ compact) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int smem[];
   int* seg_cnt = smem;                  // [kSegs][E]
   int* off = seg_cnt + kSegs * E;       // [E]
@@ -76,6 +79,7 @@ group_kernel(Src src, int n, int E, bool pad_ok, int32_t* __restrict__ counts,
   const int seg_hi = min(n, seg_lo + seg_len);
 
   for (int i = threadIdx.x; i < kSegs * E; i += kThreads) seg_cnt[i] = 0;
+  if (Src::kResetError && threadIdx.x == 0) *error_flag = 0;  // before any thread can set it
   __syncthreads();
 
   // Pass 1: per-segment counts.

@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(kNormThreads)
 add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res_in,
                    __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
                    float eps, int H, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float part[kNormThreads / 32];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * H;
@@ -102,6 +104,8 @@ __global__ void qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64
                                     __nv_bfloat16* __restrict__ vbuf, int64_t kv_batch_stride,
                                     int64_t kv_head_stride, int64_t row0_host,
                                     const int64_t* __restrict__ row0_dev) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = 128;
   const int heads = hq + 2 * hkv;
   const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -170,10 +174,12 @@ extern "C" int sf_add_rmsnorm(const void* x, const void* residual_in, void* resi
   SF_CHECK_ARG(aligned16(x) && aligned16(out) && aligned16(weight) &&
                (!residual_in || aligned16(residual_in)) && (!residual_out || aligned16(residual_out)),
                "tensors must be 16-byte aligned");
-  add_rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual_in),
-      static_cast<__nv_bfloat16*>(residual_out), static_cast<const __nv_bfloat16*>(weight), eps,
-      hidden_size, static_cast<__nv_bfloat16*>(out));
+  SF_CHECK_CUDA(launch_pdl(add_rmsnorm_kernel, dim3((unsigned)rows), dim3(kNormThreads), 0,
+                           as_stream(stream), static_cast<const __nv_bfloat16*>(x),
+                           static_cast<const __nv_bfloat16*>(residual_in),
+                           static_cast<__nv_bfloat16*>(residual_out),
+                           static_cast<const __nv_bfloat16*>(weight), eps, hidden_size,
+                           static_cast<__nv_bfloat16*>(out)));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
@@ -196,12 +202,16 @@ extern "C" int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, i
                "tensors must be 16-byte aligned");
   SF_CHECK_ARG(kv_batch_stride % 8 == 0 && kv_head_stride % 8 == 0, "cache strides must be multiples of 8");
   const int64_t items = n * (num_heads + 2 * num_kv_heads);
-  qk_norm_rope_kernel<<<(unsigned)((items + 7) / 8), 256, 0, as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(qkv), n, (int)tokens, num_heads, num_kv_heads,
-      static_cast<const __nv_bfloat16*>(q_norm_weight), static_cast<const __nv_bfloat16*>(k_norm_weight),
-      static_cast<const __nv_bfloat16*>(cos), static_cast<const __nv_bfloat16*>(sin), eps,
-      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
-      static_cast<__nv_bfloat16*>(v_cache), kv_batch_stride, kv_head_stride, row0, row0_device);
+  SF_CHECK_CUDA(launch_pdl(qk_norm_rope_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0,
+                           as_stream(stream), static_cast<const __nv_bfloat16*>(qkv), n,
+                           (int)tokens, num_heads, num_kv_heads,
+                           static_cast<const __nv_bfloat16*>(q_norm_weight),
+                           static_cast<const __nv_bfloat16*>(k_norm_weight),
+                           static_cast<const __nv_bfloat16*>(cos),
+                           static_cast<const __nv_bfloat16*>(sin), eps,
+                           static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+                           static_cast<__nv_bfloat16*>(v_cache), kv_batch_stride, kv_head_stride,
+                           row0, row0_device));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
@@ -218,6 +228,8 @@ namespace {
 __global__ void kv_gather_kernel(const uint64_t* __restrict__ bufs, int layers, int heads,
                                  int64_t head_stride, int64_t base, const int32_t* __restrict__ src,
                                  int n, int D, __nv_bfloat16* __restrict__ stage) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x % n;
   const int l2 = blockIdx.x / n;  // layer * 2 + (k or v)
   const __nv_bfloat16* buf = reinterpret_cast<const __nv_bfloat16*>(bufs[l2]);
@@ -232,6 +244,8 @@ __global__ void kv_gather_kernel(const uint64_t* __restrict__ bufs, int layers, 
 __global__ void kv_scatter_kernel(const uint64_t* __restrict__ bufs, int layers, int heads,
                                   int64_t head_stride, int64_t base, int n, int D,
                                   const __nv_bfloat16* __restrict__ stage) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x % n;
   const int l2 = blockIdx.x / n;
   __nv_bfloat16* buf = reinterpret_cast<__nv_bfloat16*>(bufs[l2]);
@@ -257,11 +271,13 @@ extern "C" int sf_kv_compact(const uint64_t* buffers, int layers, int heads, int
   SF_CHECK_ARG(aligned16(stage), "stage must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   const unsigned grid = (unsigned)(2 * layers * n);
-  kv_gather_kernel<<<grid, 128, 0, s>>>(buffers, layers, heads, head_stride, base, src_rows, n,
-                                         head_dim, static_cast<__nv_bfloat16*>(stage));
+  SF_CHECK_CUDA(launch_pdl(kv_gather_kernel, dim3(grid), dim3(128), 0, s, buffers, layers, heads,
+                           head_stride, base, src_rows, n, head_dim,
+                           static_cast<__nv_bfloat16*>(stage)));
   SF_CHECK_LAUNCH();
-  kv_scatter_kernel<<<grid, 128, 0, s>>>(buffers, layers, heads, head_stride, base, n, head_dim,
-                                          static_cast<const __nv_bfloat16*>(stage));
+  SF_CHECK_CUDA(launch_pdl(kv_scatter_kernel, dim3(grid), dim3(128), 0, s, buffers, layers, heads,
+                           head_stride, base, n, head_dim,
+                           static_cast<const __nv_bfloat16*>(stage)));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
@@ -274,6 +290,8 @@ namespace {
 __global__ void tree_mask_words_kernel(const int64_t* __restrict__ vis, int n,
                                        const int64_t* __restrict__ start_dev, int words,
                                        int32_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)n * words) return;
   const int r = (int)(i / words), w = (int)(i - (int64_t)r * words);
@@ -298,8 +316,8 @@ extern "C" int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const 
   if (rows == 0) return SF_OK;
   SF_CHECK_ARG(ancestor_sets && start_device && out, "null pointer argument");
   const int64_t total = (int64_t)rows * words;
-  tree_mask_words_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_stream(stream)>>>(
-      ancestor_sets, rows, start_device, words, out);
+  SF_CHECK_CUDA(launch_pdl(tree_mask_words_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256),
+                           0, as_stream(stream), ancestor_sets, rows, start_device, words, out));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
@@ -311,70 +329,30 @@ namespace cg = cooperative_groups;
 
 constexpr int kTopkThreads = 512;
 constexpr int kTopkWarps = kTopkThreads / 32;
-constexpr int kTopkCluster = 8;  // CTAs per row, merged through distributed shared memory
+constexpr int kTopkVecs = 4;          // 16-byte vectors (32 values) per thread per batch
+constexpr int kTopkSlots = kTopkVecs * 8;
+constexpr int kTopkMaxCluster = 16;   // CTAs per row (8 where 16 is not available)
 constexpr int kMaxTopk = 8;
+constexpr int kNoIndex = 0x7fffffff;
 
+// (value, index) order of the result: larger value first, lower index first
+// among equal values.
 __device__ __forceinline__ bool topk_better(float a, int ai, float b, int bi) {
   return a > b || (a == b && ai < bi);
 }
 
-// The K largest (value, index) pairs seen, larger value first and lower index
-// first among equal values; held in registers (fully unrolled insertion).
-template <int K>
-struct TopK {
-  float v[K];
-  int i[K];
-  __device__ void init() {
+// Every lane gets the warp's best (value, index).
+__device__ __forceinline__ void warp_best(float& v, int& i) {
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      v[j] = -INFINITY;
-      i[j] = 0x7fffffff;
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (topk_better(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
     }
   }
-  __device__ void push(float x, int xi) {
-    if (!topk_better(x, xi, v[K - 1], i[K - 1])) return;
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-      if (topk_better(x, xi, v[j], i[j])) {
-        const float tv = v[j];
-        const int ti = i[j];
-        v[j] = x;
-        i[j] = xi;
-        x = tv;
-        xi = ti;
-      }
-    }
-  }
-  __device__ void pop_front() {
-#pragma unroll
-    for (int j = 0; j + 1 < K; ++j) {
-      v[j] = v[j + 1];
-      i[j] = i[j + 1];
-    }
-    v[K - 1] = -INFINITY;
-    i[K - 1] = 0x7fffffff;
-  }
-  // The warp's k best over every lane's list; round r's winner (bv, bi) is
-  // handed to emit(r, bv, bi) on every lane.
-  template <typename Emit>
-  __device__ void warp_merge(int k, Emit emit) {
-    for (int r = 0; r < k; ++r) {
-      float bv = v[0];
-      int bi = i[0];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (topk_better(ov, oi, bv, bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      emit(r, bv, bi);
-      if (i[0] == bi && v[0] == bv) pop_front();  // real indices are unique: only the owner pops
-    }
-  }
-};
+}
 
 // Online (max, sum of exponentials) merge of two partial states.
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
@@ -384,86 +362,199 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
   m = mm;
 }
 
-// Log-softmax of scale * logits (bf16 rows) and its top-k.  A cluster of 8
-// CTAs shares one row: each CTA streams one eighth of it (16-byte loads, two
-// in flight per thread), keeping an online max / sum of exponentials and a
-// register top-k per thread, merged per warp and then per CTA; CTA 0 of the
-// cluster merges the eight partials through distributed shared memory and
+// A sorted list of K (value, index) pairs held by every lane of a warp.
+template <int K>
+struct WarpList {
+  float v[K];
+  int i[K];
+  __device__ void clear() {
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      v[j] = -INFINITY;
+      i[j] = kNoIndex;
+    }
+  }
+  __device__ void pop() {
+#pragma unroll
+    for (int j = 0; j + 1 < K; ++j) {
+      v[j] = v[j + 1];
+      i[j] = i[j + 1];
+    }
+    v[K - 1] = -INFINITY;
+    i[K - 1] = kNoIndex;
+  }
+};
+
+// Sorted lists held one per lane (lanes without one hold padding) merged
+// into the warp's best k, handed to emit(r, value, index) on every lane.
+template <int K, typename Emit>
+__device__ __forceinline__ void merge_lane_lists(WarpList<K>& mine, int k, Emit emit) {
+  for (int r = 0; r < k; ++r) {
+    float bv = mine.v[0];
+    int bi = mine.i[0];
+    warp_best(bv, bi);
+    emit(r, bv, bi);
+    if (mine.i[0] == bi && bi != kNoIndex) mine.pop();
+  }
+}
+
+// Log-softmax of scale * logits (bf16 rows) and its top-k.  A cluster of
+// 16 (or 8) CTAs shares one row, each streaming a contiguous part of it.
+// A thread takes 32 values per batch (four 16-byte loads in flight), adds
+// their exponentials against the running maximum (rescaled once per batch),
+// and its warp selects the batch's k best together with the k best so far
+// in k rounds of a warp-wide argmax over each lane's best remaining value;
+// only the lane that supplied a round's winner rescans its values.  The 16
+// warps' lists are merged per CTA, and CTA 0 of the cluster merges the
+// CTAs' lists and (max, sum) pairs through distributed shared memory and
 // writes (y - max) - log(sum), y = scale * logit in fp32.
 template <int K>
-__global__ void __cluster_dims__(kTopkCluster, 1, 1) __launch_bounds__(kTopkThreads)
+__global__ void __launch_bounds__(kTopkThreads)
 logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, float scale, int k,
                        float* __restrict__ top_v, int64_t* __restrict__ top_i) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float s_m[kTopkWarps], s_s[kTopkWarps];
-  __shared__ float c_v[kTopkWarps * K];
-  __shared__ int c_i[kTopkWarps * K];
+  __shared__ float w_v[kTopkWarps][K];
+  __shared__ int w_i[kTopkWarps][K];
   __shared__ float p_ms[2];  // this CTA's (max, sum)
   __shared__ float p_v[K];
   __shared__ int p_i[K];
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = blockIdx.y;
   const __nv_bfloat16* x = logits + row * vocab;
-  const int64_t chunk = ((vocab + 7) / 8 + kTopkCluster - 1) / kTopkCluster * 8;
+  const int64_t chunk = ((vocab + 7) / 8 + csize - 1) / csize * 8;
   const int64_t lo = min(vocab, crank * chunk), hi = min(vocab, lo + chunk);
-  float m = -INFINITY, sum = 0.f;
-  TopK<K> t;
-  t.init();
-  auto take = [&](float y, int c) {
-    if (y > m) {
-      sum = sum * __expf(m - y) + 1.f;
-      m = y;
-    } else if (y != -INFINITY) {
-      sum += __expf(y - m);
-    }
-    t.push(y, c);
-  };
-  auto take8 = [&](const uint4& u, int64_t c8) {
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) take(__bfloat162float(e[j]) * scale, (int)(c8 * 8 + j));
-  };
   const bool vec = (vocab % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
-  if (vec) {  // lo and hi are multiples of 8 here
-    const uint4* x8 = reinterpret_cast<const uint4*>(x);
-    const int64_t hi8 = hi / 8;
-    for (int64_t c = lo / 8 + threadIdx.x; c < hi8; c += 2 * kTopkThreads) {
-      const uint4 u0 = __ldg(x8 + c);
-      const bool two = c + kTopkThreads < hi8;
-      uint4 u1 = make_uint4(0, 0, 0, 0);
-      if (two) u1 = __ldg(x8 + c + kTopkThreads);
-      take8(u0, c);
-      if (two) take8(u1, c + kTopkThreads);
+  // One batch covers kTopkThreads * kTopkSlots consecutive values of [lo, hi).
+  constexpr int64_t kBatch = (int64_t)kTopkThreads * kTopkSlots;
+
+  float m = -INFINITY, sum = 0.f;
+  WarpList<K> best;
+  best.clear();
+  for (int64_t b0 = lo; b0 < hi; b0 += kBatch) {
+    float y[kTopkSlots];
+    // Index of slot s: vec: (c + v T) * 8 + j with c = b0 / 8 + tid (s = 8 v + j);
+    // scalar: b0 + s T + tid.  Both grow with s.
+    if (vec) {
+      const uint4* x8 = reinterpret_cast<const uint4*>(x);
+      uint4 u[kTopkVecs];
+#pragma unroll
+      for (int v = 0; v < kTopkVecs; ++v) {
+        const int64_t c = b0 / 8 + threadIdx.x + (int64_t)v * kTopkThreads;
+        u[v] = c * 8 < hi ? __ldg(x8 + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int v = 0; v < kTopkVecs; ++v) {
+        const bool ok = (b0 / 8 + threadIdx.x + (int64_t)v * kTopkThreads) * 8 < hi;
+        const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&u[v]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(e[j]);
+          y[v * 8 + 2 * j] = ok ? f.x * scale : -INFINITY;
+          y[v * 8 + 2 * j + 1] = ok ? f.y * scale : -INFINITY;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int sl = 0; sl < kTopkSlots; ++sl) {
+        const int64_t e = b0 + (int64_t)sl * kTopkThreads + threadIdx.x;
+        y[sl] = e < hi ? __bfloat162float(x[e]) * scale : -INFINITY;
+      }
     }
-  } else {
-    for (int64_t c = lo + threadIdx.x; c < hi; c += kTopkThreads) take(__bfloat162float(x[c]) * scale, (int)c);
+    auto index_of = [&](int sl) -> int {
+      return vec ? (int)((b0 / 8 + threadIdx.x + (int64_t)(sl >> 3) * kTopkThreads) * 8 + (sl & 7))
+                 : (int)(b0 + (int64_t)sl * kTopkThreads + threadIdx.x);
+    };
+    // Sum of exponentials against the new running maximum.
+    float bm = -INFINITY;
+#pragma unroll
+    for (int sl = 0; sl < kTopkSlots; ++sl) bm = fmaxf(bm, y[sl]);
+    const float mn = fmaxf(m, bm);
+    if (mn != -INFINITY) {
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int sl = 0; sl < kTopkSlots; ++sl) a[sl & 3] += __expf(y[sl] - mn);
+      sum = (m == -INFINITY ? 0.f : sum * __expf(m - mn)) + ((a[0] + a[1]) + (a[2] + a[3]));
+      m = mn;
+    }
+    // This lane's best remaining slot (the first on ties: the lower index;
+    // -inf slots, including those past the row, are never taken).
+    float lv = -INFINITY;
+    int ls = -1;
+#pragma unroll
+    for (int sl = 0; sl < kTopkSlots; ++sl)
+      if (y[sl] > lv) {
+        lv = y[sl];
+        ls = sl;
+      }
+    WarpList<K> next;
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+      next.v[r] = -INFINITY;
+      next.i[r] = kNoIndex;
+      if (r >= k) continue;
+      int li = ls >= 0 ? index_of(ls) : kNoIndex;
+      float wv = lv;
+      int wi = li;
+      warp_best(wv, wi);
+      if (topk_better(best.v[0], best.i[0], wv, wi)) {  // the list so far wins this round
+        next.v[r] = best.v[0];
+        next.i[r] = best.i[0];
+        best.pop();
+      } else {
+        next.v[r] = wv;
+        next.i[r] = wi;
+        if (wi == li && wi != kNoIndex) {  // this lane supplied the winner: rescan
+#pragma unroll
+          for (int sl = 0; sl < kTopkSlots; ++sl)
+            if (sl == ls) y[sl] = -INFINITY;
+          lv = -INFINITY;
+          ls = -1;
+#pragma unroll
+          for (int sl = 0; sl < kTopkSlots; ++sl)
+            if (y[sl] > lv) {
+              lv = y[sl];
+              ls = sl;
+            }
+        }
+      }
+    }
+    best = next;
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Warp and CTA partials.
 #pragma unroll
   for (int o = 16; o; o >>= 1)
     lse_merge(m, sum, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, sum, o));
   if (lane == 0) {
     s_m[warp] = m;
     s_s[warp] = sum;
-  }
-  t.warp_merge(k, [&](int r, float bv, int bi) {
-    if (lane == 0) {
-      c_v[warp * K + r] = bv;
-      c_i[warp * K + r] = bi;
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+      w_v[warp][r] = best.v[r];
+      w_i[warp][r] = best.i[r];
     }
-  });
+  }
   __syncthreads();
-  if (warp == 0) {  // this CTA's partial
+  if (warp == 0) {
     float M = lane < kTopkWarps ? s_m[lane] : -INFINITY;
     float S = lane < kTopkWarps ? s_s[lane] : 0.f;
 #pragma unroll
     for (int o = 16; o; o >>= 1)
       lse_merge(M, S, __shfl_xor_sync(0xffffffffu, M, o), __shfl_xor_sync(0xffffffffu, S, o));
-    TopK<K> f;
-    f.init();
-    if (lane < kTopkWarps)
-      for (int r = 0; r < k; ++r) f.push(c_v[lane * K + r], c_i[lane * K + r]);
-    f.warp_merge(k, [&](int r, float bv, int bi) {
+    WarpList<K> mine;
+    mine.clear();
+    if (lane < kTopkWarps) {
+#pragma unroll
+      for (int r = 0; r < K; ++r) {
+        mine.v[r] = w_v[lane][r];
+        mine.i[r] = w_i[lane][r];
+      }
+    }
+    merge_lane_lists<K>(mine, k, [&](int r, float bv, int bi) {
       if (lane == 0) {
         p_v[r] = bv;
         p_i[r] = bi;
@@ -477,21 +568,25 @@ logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, 
   cluster.sync();  // every CTA's partial is in its shared memory
   if (crank == 0 && warp == 0) {
     float M = -INFINITY, S = 0.f;
-    TopK<K> f;
-    f.init();
-    if (lane < kTopkCluster) {
+    WarpList<K> mine;
+    mine.clear();
+    if (lane < csize) {
       const float* ms = cluster.map_shared_rank(p_ms, lane);
       const float* pv = cluster.map_shared_rank(p_v, lane);
       const int* pi = cluster.map_shared_rank(p_i, lane);
       M = ms[0];
       S = ms[1];
-      for (int r = 0; r < k; ++r) f.push(pv[r], pi[r]);
+#pragma unroll
+      for (int r = 0; r < K; ++r) {
+        mine.v[r] = r < k ? pv[r] : -INFINITY;
+        mine.i[r] = r < k ? pi[r] : kNoIndex;
+      }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1)
       lse_merge(M, S, __shfl_xor_sync(0xffffffffu, M, o), __shfl_xor_sync(0xffffffffu, S, o));
     const float log_s = logf(S);
-    f.warp_merge(k, [&](int r, float bv, int bi) {
+    merge_lane_lists<K>(mine, k, [&](int r, float bv, int bi) {
       if (lane == 0) {
         top_v[row * k + r] = (bv - M) - log_s;
         top_i[row * k + r] = bi;
@@ -501,23 +596,59 @@ logsoftmax_topk_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab, 
   cluster.sync();  // peers keep their shared memory until CTA 0 has read it
 }
 
+static_assert(kTopkWarps <= 32 && kTopkMaxCluster <= 32, "one list per lane in the merges");
+
+template <int K>
+int launch_topk_rows(const __nv_bfloat16* x, int64_t rows, int64_t vocab, float scale, int k,
+                     float* top_v, int64_t* top_i, cudaStream_t stream) {
+  static std::atomic<unsigned long long> configured{0};
+  static int cluster_size[64] = {};
+  int dev = 0;
+  SF_CHECK_CUDA(cudaGetDevice(&dev));
+  if (int rc = once_per_device(configured, [] {
+        SF_CHECK_CUDA(cudaFuncSetAttribute(logsoftmax_topk_kernel<K>,
+                                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        int d = 0;
+        SF_CHECK_CUDA(cudaGetDevice(&d));
+        // 16 CTAs per row where the device can co-schedule such clusters, else 8.
+        cudaLaunchConfig_t probe = {};
+        probe.gridDim = dim3(kTopkMaxCluster, 1, 1);
+        probe.blockDim = dim3(kTopkThreads, 1, 1);
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = kTopkMaxCluster;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = 1;
+        probe.attrs = a;
+        probe.numAttrs = 1;
+        int clusters = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, logsoftmax_topk_kernel<K>, &probe);
+        if (e != cudaSuccess) (void)cudaGetLastError();
+        if (d >= 0 && d < 64) cluster_size[d] = (e == cudaSuccess && clusters > 0) ? kTopkMaxCluster : 8;
+        return SF_OK;
+      }))
+    return rc;
+  const int cs = (dev >= 0 && dev < 64 && cluster_size[dev]) ? cluster_size[dev] : 8;
+  SF_CHECK_CUDA(launch_pdl_cluster(logsoftmax_topk_kernel<K>, dim3((unsigned)cs, (unsigned)rows, 1),
+                                   dim3(kTopkThreads), 0, stream, (unsigned)cs, 1u, x, vocab, scale,
+                                   k, top_v, top_i));
+  return SF_OK;
+}
+
 }  // namespace
 }  // namespace sf
 
 extern "C" int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, float scale, int k,
                                   float* top_values, int64_t* top_indices, void* stream) {
   using namespace sf;
-  SF_CHECK_ARG(rows >= 0 && rows <= 65535 && vocab > 0 && vocab < (1LL << 31), "invalid sizes");
+  SF_CHECK_ARG(rows >= 0 && rows <= 65535 && vocab > 0 && vocab < (1LL << 31) - 1, "invalid sizes");
   SF_CHECK_ARG(k >= 1 && k <= kMaxTopk && k <= vocab, "k must be in [1, %d] and at most vocab", kMaxTopk);
   if (rows == 0) return SF_OK;
   SF_CHECK_ARG(logits && top_values && top_indices, "null pointer argument");
   auto* x = static_cast<const __nv_bfloat16*>(logits);
-  const dim3 grid(kTopkCluster, (unsigned)rows);
   cudaStream_t s = as_stream(stream);
-  if (k <= 1) logsoftmax_topk_kernel<1><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
-  else if (k <= 2) logsoftmax_topk_kernel<2><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
-  else if (k <= 4) logsoftmax_topk_kernel<4><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
-  else logsoftmax_topk_kernel<8><<<grid, kTopkThreads, 0, s>>>(x, vocab, scale, k, top_values, top_indices);
-  SF_CHECK_LAUNCH();
-  return SF_OK;
+  if (k <= 1) return launch_topk_rows<1>(x, rows, vocab, scale, k, top_values, top_indices, s);
+  if (k <= 2) return launch_topk_rows<2>(x, rows, vocab, scale, k, top_values, top_indices, s);
+  if (k <= 4) return launch_topk_rows<4>(x, rows, vocab, scale, k, top_values, top_indices, s);
+  return launch_topk_rows<8>(x, rows, vocab, scale, k, top_values, top_indices, s);
 }

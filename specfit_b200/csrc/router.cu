@@ -15,7 +15,10 @@
 // so this equals topk(probs) with the tie rule "lower id wins".
 //
 // Two launches: a logits kernel spread over the GPU (a CTA per 8 tokens x 16
-// experts) and a warp-per-token softmax / top-k kernel.
+// experts) and a warp-per-token softmax / top-k kernel; for bf16 passes of
+// at most 8 tokens and 128 experts, one launch of a CTA cluster that does
+// both (router_fused_kernel, same bits).
+#include <cooperative_groups.h>
 #include <math.h>
 
 #include <mutex>
@@ -48,6 +51,8 @@ template <typename T, typename Acc, bool kVec>
 __global__ void __launch_bounds__(kWarps * 32)
 router_logits_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t tokens, int hidden,
                      int experts, float* __restrict__ logits_f32, T* __restrict__ logits_out) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t t0 = (int64_t)blockIdx.x * kTokTile;
@@ -115,6 +120,8 @@ template <typename T, typename Acc, int kET>
 __global__ void __launch_bounds__(kWarps * 32)
 router_logits_staged(const T* __restrict__ x, const T* __restrict__ w, int64_t tokens, int hidden,
                      int experts, float* __restrict__ logits_f32, T* __restrict__ logits_out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   T* xs = reinterpret_cast<T*>(smem_raw);        // [kTokTile][hidden]
   T* ws = xs + (size_t)kTokTile * hidden;         // [kET][hidden]
@@ -177,25 +184,17 @@ router_logits_staged(const T* __restrict__ x, const T* __restrict__ w, int64_t t
   }
 }
 
-// Softmax + top-k, warp per token.  Lane l owns experts l + 32 j, j < kEpl,
-// held in registers.
+// Softmax + top-k of token t's logits, one warp: lane l holds the logits of
+// experts l + 32 j, j < kEpl, in val (-inf past the last expert).
 template <int kEpl>
-__global__ void __launch_bounds__(kWarps * 32)
-router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts, int top_k,
-                   int norm, float* __restrict__ probs, float* __restrict__ topk_w,
-                   int64_t* __restrict__ topk_idx) {
-  const int lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (t >= tokens) return;
-  const float* row = logits + t * experts;
-  float val[kEpl];
+__device__ __forceinline__ void softmax_topk_warp(const float (&val)[kEpl], int lane, int64_t t,
+                                                  int experts, int top_k, int norm,
+                                                  float* __restrict__ probs,
+                                                  float* __restrict__ topk_w,
+                                                  int64_t* __restrict__ topk_idx) {
   float m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kEpl; ++j) {
-    const int e = lane + 32 * j;
-    val[j] = e < experts ? row[e] : -INFINITY;
-    m = fmaxf(m, val[j]);
-  }
+  for (int j = 0; j < kEpl; ++j) m = fmaxf(m, val[j]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
   float ex[kEpl];
@@ -259,11 +258,206 @@ router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts
   }
 }
 
+// Softmax + top-k, warp per token, over logits in global memory.
+template <int kEpl>
+__global__ void __launch_bounds__(kWarps * 32)
+router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts, int top_k,
+                   int norm, float* __restrict__ probs, float* __restrict__ topk_w,
+                   int64_t* __restrict__ topk_idx) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  const float* row = logits + t * experts;
+  float val[kEpl];
+#pragma unroll
+  for (int j = 0; j < kEpl; ++j) {
+    const int e = lane + 32 * j;
+    val[j] = e < experts ? row[e] : -INFINITY;
+  }
+  softmax_topk_warp<kEpl>(val, lane, t, experts, top_k, norm, probs, topk_w, topk_idx);
+}
+
+// One launch for a verify pass of at most kTokTile tokens: a cluster of
+// ceil(E / 8) CTAs (at most 16) of 16 warps.  Each CTA stages the tokens and
+// 8 router rows in shared memory; warp w computes the logits of router row
+// w % 8 for tokens 4 (w / 8) .. 4 (w / 8) + 3, each (token, expert) sum in
+// exactly the lane assignment and order of router_logits_staged, so the
+// logits are the same bits.  CTA 0 then reads every logit of its token rows
+// through distributed shared memory and runs the softmax / top-k of
+// router_topk_kernel.
+constexpr int kFusedET = 8;
+constexpr int kFusedGroups = 2;                       // token groups per router row
+constexpr int kFusedTok = kTokTile / kFusedGroups;    // tokens per warp
+constexpr int kFusedWarps = kFusedET * kFusedGroups;
+constexpr int kFusedMaxCluster = 16;
+
+template <typename T, typename Acc, int kEpl>
+__global__ void __launch_bounds__(kFusedWarps * 32)
+router_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, int tokens, int hidden,
+                    int experts, int top_k, int norm, float* __restrict__ probs,
+                    float* __restrict__ topk_w, int64_t* __restrict__ topk_idx,
+                    T* __restrict__ logits_out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ float lg[kTokTile][kFusedET];
+  T* xs = reinterpret_cast<T*>(smem_raw);        // [tokens][hidden]
+  T* ws = xs + (size_t)tokens * hidden;           // [kFusedET][hidden]
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ntok = tokens;
+  const int e0 = crank * kFusedET;
+  const int nexp = max(0, min(kFusedET, experts - e0));
+  const int vec_per_row = hidden * (int)sizeof(T) / 16;
+  const int total = (ntok + nexp) * vec_per_row;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int r = i / vec_per_row, c = i % vec_per_row;
+    const T* src = (r < ntok) ? x + (int64_t)r * hidden : w + (int64_t)(e0 + r - ntok) * hidden;
+    T* dst = (r < ntok) ? xs + (size_t)r * hidden : ws + (size_t)(r - ntok) * hidden;
+    const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(dst + c * (16 / sizeof(T))));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr),
+                 "l"(src + c * (16 / sizeof(T)))
+                 : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  const int ej = warp % kFusedET;
+  const int t0 = (warp / kFusedET) * kFusedTok;
+  if (ej < nexp && t0 < ntok) {
+    Acc acc[kFusedTok];
+#pragma unroll
+    for (int i = 0; i < kFusedTok; ++i) acc[i] = Acc(0);
+    const T* wrow = ws + (size_t)ej * hidden;
+    for (int h0 = 8 * lane; h0 < hidden; h0 += 256) {
+      T wv[8];
+#pragma unroll
+      for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+        reinterpret_cast<uint4*>(wv)[q] = reinterpret_cast<const uint4*>(wrow + h0)[q];
+#pragma unroll
+      for (int i = 0; i < kFusedTok; ++i) {
+        if (t0 + i < ntok) {
+          T xv[8];
+#pragma unroll
+          for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+            reinterpret_cast<uint4*>(xv)[q] =
+                reinterpret_cast<const uint4*>(xs + (size_t)(t0 + i) * hidden + h0)[q];
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            acc[i] = fma((Acc)to_f32(xv[v]), (Acc)to_f32(wv[v]), acc[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kFusedTok; ++i) {
+      Acc sum = acc[i];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (lane == 0 && t0 + i < ntok) {
+        const float r = round_logit(sum, (T*)nullptr);
+        lg[t0 + i][ej] = r;
+        if (logits_out) logits_out[(int64_t)(t0 + i) * experts + e0 + ej] = from_f32<T>(r);
+      }
+    }
+  }
+  cluster.sync();  // every CTA's logits are in its shared memory
+  if (crank == 0 && warp < ntok) {
+    float val[kEpl];
+#pragma unroll
+    for (int j = 0; j < kEpl; ++j) {
+      const int e = lane + 32 * j;
+      val[j] = e < experts ? *cluster.map_shared_rank(&lg[warp][e % kFusedET], e / kFusedET)
+                           : -INFINITY;
+    }
+    softmax_topk_warp<kEpl>(val, lane, warp, experts, top_k, norm, probs, topk_w, topk_idx);
+  }
+  cluster.sync();  // peers keep their shared memory until CTA 0 has read it
+}
+
 template <int kEpl>
 void launch_topk(const float* logits, int64_t tokens, int E, int K, int norm, float* probs,
                  float* topk_w, int64_t* topk_idx, cudaStream_t stream) {
-  router_topk_kernel<kEpl><<<(unsigned)((tokens + kWarps - 1) / kWarps), kWarps * 32, 0, stream>>>(
-      logits, tokens, E, K, norm, probs, topk_w, topk_idx);
+  // Launch errors surface through the caller's cudaGetLastError check.
+  (void)launch_pdl(router_topk_kernel<kEpl>, dim3((unsigned)((tokens + kWarps - 1) / kWarps)),
+                   dim3(kWarps * 32), 0, stream, logits, tokens, E, K, norm, probs, topk_w,
+                   topk_idx);
+}
+
+template <typename T, typename Acc, int kEpl>
+int launch_fused_epl(const T* x, const T* w, int tokens, int H, int E, int K, int norm,
+                     float* probs, float* topk_w, int64_t* topk_idx, T* logits_out, size_t smem,
+                     cudaStream_t stream) {
+  static std::atomic<unsigned long long> configured{0};
+  if (int rc = once_per_device(configured, [] {
+        SF_CHECK_CUDA(cudaFuncSetAttribute(router_fused_kernel<T, Acc, kEpl>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SF_CHECK_CUDA(cudaFuncSetAttribute(router_fused_kernel<T, Acc, kEpl>,
+                                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        return SF_OK;
+      }))
+    return rc;
+  const unsigned cluster = (unsigned)((E + kFusedET - 1) / kFusedET);  // <= kFusedMaxCluster
+  SF_CHECK_CUDA(launch_pdl_cluster(router_fused_kernel<T, Acc, kEpl>, dim3(1, cluster, 1),
+                                   dim3(kFusedWarps * 32), smem, stream, 1u, cluster, x, w, tokens,
+                                   H, E, K, norm, probs, topk_w, topk_idx, logits_out));
+  return SF_OK;
+}
+
+// Whether this device co-schedules clusters of `size` CTAs of the fused
+// kernel (16 exceeds the portable limit of 8), checked once per device and
+// size; the two-launch path serves devices that do not.
+template <typename T, typename Acc>
+bool fused_clusters_ok(int size, size_t smem) {
+  static std::mutex mu;
+  static int known[64][kFusedMaxCluster + 1] = {};  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  int& k = known[dev][size];
+  if (k == 0) {
+    bool ok = cudaFuncSetAttribute(router_fused_kernel<T, Acc, 4>,
+                                   cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+              cudaFuncSetAttribute(router_fused_kernel<T, Acc, 4>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess;
+    if (ok) {
+      cudaLaunchConfig_t probe = {};
+      probe.gridDim = dim3(1, (unsigned)size, 1);
+      probe.blockDim = dim3(kFusedWarps * 32, 1, 1);
+      probe.dynamicSmemBytes = smem;
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = 1;
+      a[0].val.clusterDim.y = (unsigned)size;
+      a[0].val.clusterDim.z = 1;
+      probe.attrs = a;
+      probe.numAttrs = 1;
+      int clusters = 0;
+      ok = cudaOccupancyMaxActiveClusters(&clusters, router_fused_kernel<T, Acc, 4>, &probe) ==
+               cudaSuccess && clusters > 0;
+    }
+    (void)cudaGetLastError();
+    k = ok ? 1 : 2;
+  }
+  return k == 1;
+}
+
+template <typename T, typename Acc>
+int launch_fused(const T* x, const T* w, int tokens, int H, int E, int K, int norm, float* probs,
+                 float* topk_w, int64_t* topk_idx, T* logits_out, size_t smem, cudaStream_t stream) {
+  const int epl = (E + 31) / 32;
+  if (epl <= 1)
+    return launch_fused_epl<T, Acc, 1>(x, w, tokens, H, E, K, norm, probs, topk_w, topk_idx,
+                                       logits_out, smem, stream);
+  if (epl <= 2)
+    return launch_fused_epl<T, Acc, 2>(x, w, tokens, H, E, K, norm, probs, topk_w, topk_idx,
+                                       logits_out, smem, stream);
+  return launch_fused_epl<T, Acc, 4>(x, w, tokens, H, E, K, norm, probs, topk_w, topk_idx,
+                                     logits_out, smem, stream);
 }
 
 template <typename T>
@@ -275,6 +469,12 @@ int launch_router(const void* hidden, const void* weight, int64_t tokens, int H,
   const T* w = static_cast<const T*>(weight);
   dim3 grid((unsigned)((tokens + kTokTile - 1) / kTokTile), (unsigned)((E + kExpTile - 1) / kExpTile));
   const bool vec = (H % 8 == 0) && aligned16(x) && aligned16(w);
+  const size_t fused_smem = (size_t)(tokens + kFusedET) * H * sizeof(T);
+  if (std::is_same<T, __nv_bfloat16>::value && vec && tokens <= kTokTile &&
+      E <= kFusedET * kFusedMaxCluster && fused_smem <= 200 * 1024 &&
+      fused_clusters_ok<T, Acc>((E + kFusedET - 1) / kFusedET, fused_smem))
+    return launch_fused<T, Acc>(x, w, (int)tokens, H, E, K, norm, probs, topk_w, topk_idx,
+                                static_cast<T*>(logits_out), fused_smem, stream);
   const bool few = (int64_t)grid.x * grid.y < num_sms();
   constexpr int kSmallTile = 4;
   const size_t staged_smem = (size_t)(kTokTile + (few ? kSmallTile : kExpTile)) * H * sizeof(T);
@@ -290,18 +490,20 @@ int launch_router(const void* hidden, const void* weight, int64_t tokens, int H,
       return rc;
     if (few) {
       grid.y = (unsigned)((E + kSmallTile - 1) / kSmallTile);
-      router_logits_staged<T, Acc, kSmallTile><<<grid, kWarps * 32, staged_smem, stream>>>(
-          x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+      SF_CHECK_CUDA(launch_pdl(router_logits_staged<T, Acc, kSmallTile>, dim3(grid),
+                               dim3(kWarps * 32), staged_smem, stream, x, w, tokens, H, E,
+                               logits_ws, static_cast<T*>(logits_out)));
     } else {
-      router_logits_staged<T, Acc, kExpTile><<<grid, kWarps * 32, staged_smem, stream>>>(
-          x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+      SF_CHECK_CUDA(launch_pdl(router_logits_staged<T, Acc, kExpTile>, dim3(grid),
+                               dim3(kWarps * 32), staged_smem, stream, x, w, tokens, H, E,
+                               logits_ws, static_cast<T*>(logits_out)));
     }
   } else if (vec)
-    router_logits_kernel<T, Acc, true><<<grid, kWarps * 32, 0, stream>>>(
-        x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+    SF_CHECK_CUDA(launch_pdl(router_logits_kernel<T, Acc, true>, dim3(grid), dim3(kWarps * 32), 0,
+                             stream, x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out)));
   else
-    router_logits_kernel<T, Acc, false><<<grid, kWarps * 32, 0, stream>>>(
-        x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out));
+    SF_CHECK_CUDA(launch_pdl(router_logits_kernel<T, Acc, false>, dim3(grid), dim3(kWarps * 32), 0,
+                             stream, x, w, tokens, H, E, logits_ws, static_cast<T*>(logits_out)));
   SF_CHECK_LAUNCH();
   const int epl = (E + 31) / 32;
   if (epl <= 1) launch_topk<1>(logits_ws, tokens, E, K, norm, probs, topk_w, topk_idx, stream);

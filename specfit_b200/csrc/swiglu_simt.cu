@@ -25,6 +25,8 @@ swiglu_up_simt(const T* __restrict__ xs, const int32_t* __restrict__ offsets,
                const int32_t* __restrict__ active, const int32_t* __restrict__ num_active,
                const int32_t* __restrict__ slot_of, const T* __restrict__ storage,
                int64_t slot_count, int64_t slot_stride, int H, int I, T* __restrict__ act) {
+  pdl_wait();
+  pdl_trigger();
   const int j = blockIdx.x;
   if (j >= *num_active) return;
   const int e = active[j];
@@ -75,6 +77,8 @@ swiglu_down_simt(const T* __restrict__ act, const float* __restrict__ ws,
                  const int32_t* __restrict__ num_active, const int32_t* __restrict__ slot_of,
                  const T* __restrict__ storage, int64_t slot_count, int64_t slot_stride, int H,
                  int I, T* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int j = blockIdx.x;
   if (j >= *num_active) return;
   const int e = active[j];
@@ -113,15 +117,14 @@ int launch_simt(const SwigluArgs& a, cudaStream_t stream) {
   T* act = static_cast<T*>(a.act_workspace);
   T* out = static_cast<T*>(a.out_sorted);
   dim3 g1((unsigned)a.num_experts, (unsigned)((a.inter + kWarps - 1) / kWarps));
-  swiglu_up_simt<T><<<g1, kWarps * 32, 0, stream>>>(xs, a.offsets, a.active, a.num_active,
-                                                     a.expert_slot, storage, a.slot_count,
-                                                     a.slot_stride, a.hidden, a.inter, act);
+  SF_CHECK_CUDA(launch_pdl(swiglu_up_simt<T>, dim3(g1), dim3(kWarps * 32), 0, stream, xs, a.offsets,
+                           a.active, a.num_active, a.expert_slot, storage, a.slot_count,
+                           a.slot_stride, a.hidden, a.inter, act));
   SF_CHECK_LAUNCH();
   dim3 g2((unsigned)a.num_experts, (unsigned)((a.hidden + kWarps - 1) / kWarps));
-  swiglu_down_simt<T><<<g2, kWarps * 32, 0, stream>>>(act, a.weights_sorted, a.offsets, a.active,
-                                                       a.num_active, a.expert_slot, storage,
-                                                       a.slot_count, a.slot_stride, a.hidden,
-                                                       a.inter, out);
+  SF_CHECK_CUDA(launch_pdl(swiglu_down_simt<T>, dim3(g2), dim3(kWarps * 32), 0, stream, act,
+                           a.weights_sorted, a.offsets, a.active, a.num_active, a.expert_slot,
+                           storage, a.slot_count, a.slot_stride, a.hidden, a.inter, out));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

@@ -109,6 +109,8 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
                  const int32_t* __restrict__ num_active, const int32_t* __restrict__ expert_slot,
                  const float* __restrict__ w_sorted, int H, int I,
                  __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -389,12 +391,13 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
   }
   const int grid = num_sms();
   auto* act = static_cast<__nv_bfloat16*>(a.act_workspace);
-  swiglu_tc_kernel<1><<<grid, kThreads, kSmemBytes, stream>>>(
-      tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot, a.weights_sorted, H, I, act);
+  SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
+                           tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot,
+                           a.weights_sorted, H, I, act));
   SF_CHECK_LAUNCH();
-  swiglu_tc_kernel<2><<<grid, kThreads, kSmemBytes, stream>>>(
-      tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot, a.weights_sorted, H, I,
-      static_cast<__nv_bfloat16*>(a.out_sorted));
+  SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
+                           tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot,
+                           a.weights_sorted, H, I, static_cast<__nv_bfloat16*>(a.out_sorted)));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

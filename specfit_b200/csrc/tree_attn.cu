@@ -41,6 +41,8 @@ __device__ __forceinline__ bool visible(const Params& p, int row, int key) {
 
 __global__ void __launch_bounds__(kMaxGroup * 32)
 tree_attn_split_kernel(Params p) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [kTile][kD]
   __nv_bfloat16* ks = vs + kTile * kD;                                      // [kTile][kKPitch]
@@ -178,6 +180,8 @@ tree_attn_split_kernel(Params p) {
 
 // Merge the splits of one (head, row) per warp; lane owns 4 dims.
 __global__ void tree_attn_merge_kernel(Params p, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t pair = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (pair >= (int64_t)p.num_heads * p.q_len) return;
@@ -313,7 +317,8 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
                "unknown attention implementation %d", impl);
   if (impl != SF_ATTN_SIMT && tree_attention_mma_supports(p, head_dim)) {
     if (int rc = tree_attention_mma(p, s)) return rc;
-    tree_attn_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(out));
+    SF_CHECK_CUDA(launch_pdl(tree_attn_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256),
+                             0, s, p, static_cast<__nv_bfloat16*>(out)));
     SF_CHECK_LAUNCH();
     return SF_OK;
   }
@@ -327,9 +332,10 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
         return SF_OK;
       }))
     return rc;
-  tree_attn_split_kernel<<<grid, kMaxGroup * 32, smem, s>>>(p);
+  SF_CHECK_CUDA(launch_pdl(tree_attn_split_kernel, dim3(grid), dim3(kMaxGroup * 32), smem, s, p));
   SF_CHECK_LAUNCH();
-  tree_attn_merge_kernel<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(out));
+  SF_CHECK_CUDA(launch_pdl(tree_attn_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0,
+                           s, p, static_cast<__nv_bfloat16*>(out)));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

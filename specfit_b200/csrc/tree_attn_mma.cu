@@ -117,6 +117,8 @@ constexpr size_t kSmemBytes = 4 * kStageElems * sizeof(__nv_bfloat16);  // 2 sta
 
 __global__ void __launch_bounds__(kWarps * 32)
 tree_attn_mma_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) __nv_bfloat16 smem[];
 
   const int kvh = blockIdx.x;
@@ -313,7 +315,8 @@ int tree_attention_mma(AttnParams& p, cudaStream_t stream) {
     return SF_OK;
   });
   if (rc != SF_OK) return rc;
-  tree_attn_mma_kernel<<<grid, kWarps * 32, kSmemBytes, stream>>>(p);
+  SF_CHECK_CUDA(launch_pdl(tree_attn_mma_kernel, dim3(grid), dim3(kWarps * 32), kSmemBytes, stream,
+                           p));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

@@ -119,8 +119,7 @@ def moe_dispatch(top_k_index: torch.Tensor, num_experts: int) -> Dispatch:
     inv_pos = buf[2 * num_experts + 1 + n: 2 * num_experts + 1 + 2 * n]
     active = buf[2 * num_experts + 1 + 2 * n: 3 * num_experts + 1 + 2 * n]
     num_active = buf[3 * num_experts + 1 + 2 * n: 3 * num_experts + 2 + 2 * n]
-    error = buf[3 * num_experts + 2 + 2 * n:]
-    error.zero_()
+    error = buf[3 * num_experts + 2 + 2 * n:]  # set to 0 / 1 by the kernel
     N.check(
         N.lib.sf_moe_dispatch(idx.data_ptr(), tokens, top_k, num_experts, counts.data_ptr(),
                               offsets.data_ptr(), sorted_pos.data_ptr(), inv_pos.data_ptr(),

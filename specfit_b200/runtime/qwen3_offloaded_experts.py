@@ -103,8 +103,9 @@ class Qwen3OffloadedExperts(nn.Module):
             # Every expert resident: one launch, no host round trip.
             ys = ops.grouped_swiglu(xs, ws, d, fixed, storage, self.hidden_size,
                                     self.intermediate_size, impl=self.swiglu_impl)
-            self.cache.note_device_hits(d.num_active)
-            return ops.moe_combine(ys, d, top_k_index)
+            out = ops.moe_combine(ys, d, top_k_index)
+            self.cache.note_device_hits(d.num_active)  # after the combine: the MoE kernels run back to back
+            return out
         return self._forward_waves(h, top_k_index, d, xs, ws, storage, execution_order)
 
     def _forward_waves(self, h, top_k_index, d, xs, ws, storage, execution_order):

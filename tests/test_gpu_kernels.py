@@ -95,7 +95,10 @@ def test_router_ties_pick_lowest_expert_id(ops):
 
 def test_router_small_shapes(ops):
     gen = torch.Generator().manual_seed(9)
-    for (t, h, e, k) in [(2, 4, 3, 3), (5, 33, 7, 2), (3, 1, 4, 1), (70, 100, 128, 8), (9, 64, 300, 16)]:
+    # (t <= 8, bf16, H % 8 == 0, E <= 128: the one-launch cluster router)
+    for (t, h, e, k) in [(2, 4, 3, 3), (5, 33, 7, 2), (3, 1, 4, 1), (70, 100, 128, 8), (9, 64, 300, 16),
+                         (8, 64, 16, 4), (3, 256, 48, 8), (8, 2048, 128, 8), (1, 128, 100, 8),
+                         (6, 2048, 128, 8), (2, 8, 1, 1)]:
         x = torch.randn(t, h, generator=gen)
         w = torch.randn(e, h, generator=gen)
         for dtype, name in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
