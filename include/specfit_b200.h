@@ -27,6 +27,8 @@
  *                         + cache update (write k, v rows)
  *   sf_kv_compact         _compact_tree_cache                   src/specfit/runtime/eagle3_tree.py:833-858
  *   sf_logsoftmax_topk    log_softmax + topk of a drafter level src/specfit/runtime/eagle3_tree.py:611-803
+ *   sf_linear_bf16        F.linear (q|k|v, o, lm_head, drafter)  transformers/...:Qwen3MoeAttention.forward,
+ *                                                               Qwen3MoeForCausalLM.forward (lm_head)
  *                                                               (candidate-pool expansion)
  */
 #ifndef SPECFIT_B200_H_
@@ -429,6 +431,17 @@ SF_API int sf_tree_mask_words(const int64_t* ancestor_sets, int rows, const int6
  */
 SF_API int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, float scale, int k,
                               float* top_values, int64_t* top_indices, void* stream);
+/*
+ * out[rows][out_features] = x[rows][in_features] . weight[out_features][in_features]^T
+ * in bf16 with fp32 accumulation, rounded once (F.linear without bias), on
+ * tcgen05 tensor cores with K split across a CTA cluster and the partial
+ * sums added in a fixed order.  For verify-sized inputs: rows <= 32,
+ * in_features % 64 == 0, x and weight contiguous and 16-byte aligned;
+ * otherwise returns SF_ERR_UNSUPPORTED without a message (use a library
+ * GEMM).
+ */
+SF_API int sf_linear_bf16(const void* x, int64_t rows, int64_t in_features, const void* weight,
+                          int64_t out_features, void* out, void* stream);
 SF_API int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
                            int num_kv_heads, int head_dim, const void* q_norm_weight,
                            const void* k_norm_weight, const void* cos, const void* sin, float eps,

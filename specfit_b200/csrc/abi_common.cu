@@ -43,5 +43,9 @@ extern "C" int sf_abi_version(void) { return 1; }
 extern "C" int sf_device_status(int* status, int reset) {
   using namespace sf;
   SF_CHECK_ARG(status, "null pointer argument");
-  return swiglu_status(status, reset);
+  int a = 0, b = 0;
+  if (int rc = swiglu_status(&a, reset)) return rc;
+  if (int rc = dense_status(&b, reset)) return rc;
+  *status = a ? a : b;
+  return SF_OK;
 }

@@ -1,0 +1,262 @@
+// Skinny bf16 projection GEMM on tcgen05 for verify-sized row counts.
+//
+//   Y[T, N] = X[T, K] . W[N, K]^T      (F.linear without bias), T <= 32
+//
+// The projections of a verify pass (q|k|v, o, the drafter's layers and
+// lm_head) see a handful of token rows against weight matrices of tens to
+// hundreds of MB, so they are weight-streaming problems: the bound is reading
+// W once from HBM.  Layout "swap AB" as in the grouped SwiGLU: 128 weight
+// rows fill the MMA's M dimension and the T token rows form N (16 or 32),
+// both operands K-major and loaded by TMA with 128-byte swizzling.
+//
+// Parallelism comes from splitting K: the CTAs of a thread-block cluster
+// (up to 8) share one 128-row tile, each accumulating its K range in TMEM.
+// CTA r owns rows [r*128/S, (r+1)*128/S) of the output: every CTA stores its
+// fp32 partial of those rows into the owner's shared memory (distributed
+// shared memory), and after one cluster barrier the owner adds the S
+// partials in rank order (a fixed order: the result does not depend on
+// timing) and rounds once to bf16.
+//
+// Roles per CTA (192 threads): warp 0 lane 0 issues TMA (weights for the
+// first stages before waiting on the preceding kernel, since they do not
+// depend on it), warp 1 lane 0 allocates TMEM and issues the MMAs, warps
+// 2..5 read the accumulator back.  Every TMA load is issued by a CTA for its
+// own shared memory.  Waits give up after a bounded time, record a site code
+// in the status word read by sf_device_status and let the kernel finish.
+#include <cooperative_groups.h>
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+#include "swiglu.h"
+
+namespace sf {
+namespace {
+
+namespace cg = cooperative_groups;
+
+__device__ int g_dense_status;
+
+constexpr int kBM = 128;       // weight rows per tile (MMA M)
+constexpr int kBK = 64;        // K per stage: one 128-byte swizzle atom of bf16
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kMaxSplit = 8;   // portable cluster size
+constexpr uint32_t kTmemCols = 32;
+
+template <int kBN>
+struct __align__(1024) DenseSmem {
+  uint8_t a[kStages][kABytes];
+  uint8_t b[kStages][kBN * kBK * 2];
+  // This CTA's rows of every split's partial tile: slot s * rows_per + r
+  // holds split s's accumulator of row r0 + r (rows_per = ceil(128 / S)).
+  float part[kBM + kMaxSplit][kBN + 1];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int kBN>
+constexpr size_t dense_smem_bytes() {
+  return sizeof(DenseSmem<kBN>) + 1024;  // + alignment slack
+}
+
+template <int kBN>
+__global__ void __launch_bounds__(kThreads)
+dense_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                int T, int N, int K, __nv_bfloat16* __restrict__ y) {
+  constexpr uint32_t kBBytes = kBN * kBK * 2;
+  extern __shared__ uint8_t smem_raw[];
+  auto* sm = reinterpret_cast<DenseSmem<kBN>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  cg::cluster_group cluster = cg::this_cluster();
+  const int split = (int)cluster.num_blocks();
+  const int crank = (int)cluster.block_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM;
+  const int kb_total = K / kBK;
+  const int per = (kb_total + split - 1) / split;
+  const int kb0 = min(kb_total, crank * per);
+  const int nkb = min(kb_total, kb0 + per) - kb0;
+  const int rows_per = (kBM + split - 1) / split;
+  volatile int* abort_flag = &sm->abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(&sm->full[s], 1);
+      ptx::mbar_init(&sm->empty[s], 1);
+    }
+    ptx::mbar_init(&sm->acc_full, 1);
+    sm->abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_w);
+    ptx::prefetch_tensormap(&tm_x);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(&sm->tmem_base, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = sm->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int pre = min(nkb, kStages);
+      // Weight tiles of the first stages: independent of the preceding kernel.
+      for (int i = 0; i < pre; ++i) {
+        ptx::mbar_arrive_expect_tx(&sm->full[i], kABytes + kBBytes);
+        ptx::tma_load_2d(sm->a[i], &tm_w, &sm->full[i], (kb0 + i) * kBK, m0);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int i = 0; i < pre; ++i)
+        ptx::tma_load_2d(sm->b[i], &tm_x, &sm->full[i], (kb0 + i) * kBK, 0);
+      int issued = pre;
+      for (int i = pre; i < nkb; ++i) {
+        const int s = i % kStages;
+        const uint32_t ph = (i / kStages) & 1;
+        if (!ptx::mbar_wait(&sm->empty[s], ph ^ 1, abort_flag, &g_dense_status, 11)) break;
+        ptx::mbar_arrive_expect_tx(&sm->full[s], kABytes + kBBytes);
+        ptx::tma_load_2d(sm->a[s], &tm_w, &sm->full[s], (kb0 + i) * kBK, m0);
+        ptx::tma_load_2d(sm->b[s], &tm_x, &sm->full[s], (kb0 + i) * kBK, 0);
+        issued = i + 1;
+      }
+      // Let every load issued above land before the CTA can exit.
+      volatile int never = 0;
+      for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i)
+        ptx::mbar_wait(&sm->full[i % kStages], (i / kStages) & 1, &never, &g_dense_status, 12);
+    } else {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      const uint32_t idesc = ptx::idesc_bf16_f32(kBM, kBN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % kStages;
+        const uint32_t ph = (i / kStages) & 1;
+        if (!ptx::mbar_wait(&sm->full[s], ph, abort_flag, &g_dense_status, 13)) break;
+        ptx::tc_fence_after();
+        const uint64_t adesc = ptx::smem_desc_k_sw128(ptx::smem_u32(sm->a[s]));
+        const uint64_t bdesc = ptx::smem_desc_k_sw128(ptx::smem_u32(sm->b[s]));
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          ptx::umma_f16(tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                        (i | k) != 0);
+        ptx::umma_commit(&sm->empty[s]);
+      }
+      ptx::umma_commit(&sm->acc_full);
+    }
+  } else {
+    pdl_wait();
+    // Epilogue: TMEM lane quadrant (warp % 4) -> accumulator row; the row's
+    // partial goes straight into the shared memory of the CTA that reduces
+    // it (asynchronous stores through distributed shared memory).
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int owner = row / rows_per;
+    float* dst = cluster.map_shared_rank(&sm->part[0][0], owner) +
+                 (crank * rows_per + (row - owner * rows_per)) * (kBN + 1);
+    bool have = nkb > 0;
+    if (have) have = ptx::mbar_wait(&sm->acc_full, 0, abort_flag, &g_dense_status, 14);
+    if (have) {
+      ptx::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kBN / 16; ++c) {
+        float v[16];
+        ptx::tmem_ld_16(tmem + ((uint32_t)(quad * 32) << 16) + c * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (c * 16 + i < T) dst[c * 16 + i] = v[i];
+      }
+    } else {
+      for (int i = 0; i < T; ++i) dst[i] = 0.f;
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();  // TMEM reads done
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+  cluster.sync();  // every split's partial rows have landed with their owner
+  const int r0 = min(kBM, crank * rows_per);
+  const int nr = min(kBM, r0 + rows_per) - r0;
+  for (int idx = threadIdx.x; idx < nr * T; idx += kThreads) {
+    const int t = idx / nr, r = idx % nr;
+    if (m0 + r0 + r >= N) continue;
+    float acc = 0.f;
+    for (int s = 0; s < split; ++s) acc += sm->part[s * rows_per + r][t];  // rank order
+    y[(int64_t)t * N + m0 + r0 + r] = __float2bfloat16_rn(acc);
+  }
+}
+
+template <int kBN>
+int launch_dense(const void* x, const void* w, void* y, int T, int N, int K, cudaStream_t stream) {
+  static std::atomic<unsigned long long> configured{0};
+  if (int rc = once_per_device(configured, [] {
+        SF_CHECK_CUDA(cudaFuncSetAttribute(dense_tc_kernel<kBN>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)dense_smem_bytes<kBN>()));
+        return SF_OK;
+      }))
+    return rc;
+  CUtensorMap tm_w, tm_x;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {kBK, kBM};
+    if (int rc = tma_encode_bf16(&tm_w, w, 2, dims, strides, box)) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {kBK, (cuuint32_t)kBN};  // rows past T read as zeros
+    if (int rc = tma_encode_bf16(&tm_x, x, 2, dims, strides, box)) return rc;
+  }
+  const int m_tiles = (N + kBM - 1) / kBM;
+  const int kb_total = K / kBK;
+  // Split K while the tiles alone are fewer than the SMs, keeping the whole
+  // grid in one wave (clusters are placed one CTA per SM).
+  int split = num_sms() / m_tiles;
+  split = std::max(1, std::min(std::min(split, kMaxSplit), kb_total));
+  SF_CHECK_CUDA(launch_pdl_cluster(dense_tc_kernel<kBN>, dim3((unsigned)split, (unsigned)m_tiles, 1),
+                                   dim3(kThreads), dense_smem_bytes<kBN>(), stream, (unsigned)split,
+                                   1u, tm_w, tm_x, T, N, K, static_cast<__nv_bfloat16*>(y)));
+  return SF_OK;
+}
+
+}  // namespace
+
+int dense_status(int* status, int reset) {
+  SF_CHECK_CUDA(cudaMemcpyFromSymbol(status, g_dense_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    SF_CHECK_CUDA(cudaMemcpyToSymbol(g_dense_status, &zero, sizeof(int)));
+  }
+  return SF_OK;
+}
+
+}  // namespace sf
+
+extern "C" int sf_linear_bf16(const void* x, int64_t rows, int64_t in_features, const void* weight,
+                              int64_t out_features, void* out, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(rows >= 0 && in_features > 0 && out_features > 0, "invalid sizes");
+  if (rows == 0) return SF_OK;
+  SF_CHECK_ARG(x && weight && out, "null pointer argument");
+  if (rows > 32 || in_features % kBK != 0 || in_features >= (1LL << 31) ||
+      out_features >= (1LL << 31) || !aligned16(x) || !aligned16(weight))
+    return SF_ERR_UNSUPPORTED;  // no message: callers fall back to a library GEMM
+  const int T = (int)rows, N = (int)out_features, K = (int)in_features;
+  if (T <= 16) return launch_dense<16>(x, weight, out, T, N, K, as_stream(stream));
+  return launch_dense<32>(x, weight, out, T, N, K, as_stream(stream));
+}

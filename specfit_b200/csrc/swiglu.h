@@ -2,6 +2,7 @@
 // implementations (CUDA-core and tcgen05).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -32,5 +33,11 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream);
 bool swiglu_tcgen05_supports(const SwigluArgs& a);
 // Reads (and with reset clears) the device status word of the tcgen05 kernels.
 int swiglu_status(int* status, int reset);
+int dense_status(int* status, int reset);
+
+// A bf16 tiled tensor map with 128-byte swizzling (rank 2 or 3; dims and
+// box innermost first, strides in bytes for dims 1..rank-1).
+int tma_encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                    const cuuint64_t* strides_bytes, const cuuint32_t* box);
 
 }  // namespace sf

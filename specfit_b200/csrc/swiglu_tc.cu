@@ -289,6 +289,22 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
   }
 }
 
+bool device_is_sm100() {
+  static std::atomic<int> cache[64];  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (v == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+    v = (major == 10) ? 1 : 2;
+    cache[dev & 63].store(v, std::memory_order_relaxed);
+  }
+  return v == 1;
+}
+
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // Host side: tensor maps.
 
@@ -306,7 +322,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-int encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+int tma_encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
                 const cuuint64_t* strides_bytes, const cuuint32_t* box) {
   auto fn = encode_fn();
   if (!fn) return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -318,22 +334,6 @@ int encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* 
   if (r != CUDA_SUCCESS) return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return SF_OK;
 }
-
-bool device_is_sm100() {
-  static std::atomic<int> cache[64];  // 0 unknown, 1 yes, 2 no
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  int v = cache[dev & 63].load(std::memory_order_relaxed);
-  if (v == 0) {
-    int major = 0;
-    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
-    v = (major == 10) ? 1 : 2;
-    cache[dev & 63].store(v, std::memory_order_relaxed);
-  }
-  return v == 1;
-}
-
-}  // namespace
 
 bool swiglu_tcgen05_supports(const SwigluArgs& a) {
   return a.dtype == SF_DTYPE_BF16 && a.hidden % kBM == 0 && a.inter % 64 == 0 && a.hidden > 0 &&
@@ -369,25 +369,25 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
     cuuint64_t dims[3] = {(cuuint64_t)H, (cuuint64_t)(2 * I), (cuuint64_t)a.slot_count};
     cuuint64_t strides[2] = {(cuuint64_t)H * 2, slot_bytes};
     cuuint32_t box[3] = {kBK, 64, 1};
-    if (int rc = encode_bf16(&tm_w1, storage, 3, dims, strides, box)) return rc;
+    if (int rc = tma_encode_bf16(&tm_w1, storage, 3, dims, strides, box)) return rc;
   }
   {
     cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)a.rows};
     cuuint64_t strides[1] = {(cuuint64_t)H * 2};
     cuuint32_t box[2] = {kBK, kBBox};
-    if (int rc = encode_bf16(&tm_x1, a.hidden_sorted, 2, dims, strides, box)) return rc;
+    if (int rc = tma_encode_bf16(&tm_x1, a.hidden_sorted, 2, dims, strides, box)) return rc;
   }
   {
     cuuint64_t dims[3] = {(cuuint64_t)I, (cuuint64_t)H, (cuuint64_t)a.slot_count};
     cuuint64_t strides[2] = {(cuuint64_t)I * 2, slot_bytes};
     cuuint32_t box[3] = {kBK, kBM, 1};
-    if (int rc = encode_bf16(&tm_w2, storage + 2LL * I * H, 3, dims, strides, box)) return rc;
+    if (int rc = tma_encode_bf16(&tm_w2, storage + 2LL * I * H, 3, dims, strides, box)) return rc;
   }
   {
     cuuint64_t dims[2] = {(cuuint64_t)I, (cuuint64_t)a.rows};
     cuuint64_t strides[1] = {(cuuint64_t)I * 2};
     cuuint32_t box[2] = {kBK, kBBox};
-    if (int rc = encode_bf16(&tm_x2, a.act_workspace, 2, dims, strides, box)) return rc;
+    if (int rc = tma_encode_bf16(&tm_x2, a.act_workspace, 2, dims, strides, box)) return rc;
   }
   const int grid = num_sms();
   auto* act = static_cast<__nv_bfloat16*>(a.act_workspace);

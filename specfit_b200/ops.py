@@ -466,3 +466,36 @@ def logsoftmax_topk(logits: torch.Tensor, k: int, scale: float = 1.0,
                                      idx.data_ptr(), _stream(dev)), "sf_logsoftmax_topk")
     _launched(1 if rows else 0)
     return vals, idx
+
+
+
+LINEAR_MAX_OUT = 4096  # measured on B200: wider weights stream as fast through cuBLAS
+LINEAR_MIN_IN = 4096
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear(x, weight)`` (no bias) for bf16 ``x [..., K]``: the tcgen05
+    split-K kernel (``sf_linear_bf16``) when the rows are few (<= 32) and the
+    weight is tall and narrow enough that splitting K is what fills the GPU
+    (out_features <= LINEAR_MAX_OUT, in_features >= LINEAR_MIN_IN: the o
+    projection and the drafter's 2048-wide outputs), else the library GEMM,
+    which streams wide weights as fast at these row counts."""
+    k = x.shape[-1]
+    rows = x.numel() // k if k else 0
+    n_out = weight.shape[0]
+    if (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and 0 < rows <= 32
+            and n_out <= LINEAR_MAX_OUT and k >= LINEAR_MIN_IN and x.is_contiguous()
+            and weight.is_contiguous()):
+        res = out if out is not None else torch.empty(*x.shape[:-1], n_out, dtype=x.dtype, device=x.device)
+        rc = N.lib.sf_linear_bf16(x.data_ptr(), rows, k, weight.data_ptr(), n_out, res.data_ptr(),
+                                  _stream(x.device))
+        if rc == N.SF_OK:
+            _launched(1)
+            return res
+        if rc != N.SF_ERR_UNSUPPORTED:
+            N.check(rc, "sf_linear_bf16")
+    y = torch.nn.functional.linear(x, weight)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y

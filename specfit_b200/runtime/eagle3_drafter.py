@@ -317,7 +317,7 @@ class DeviceDraft:
         f_n = torch.empty_like(e_n)
         self._norm(d.embed(tokens), None, None, d.emb_norm, e_n)
         self._norm(feats.contiguous(), None, None, d.hid_norm, f_n)
-        qkv = F.linear(torch.cat((e_n, f_n), dim=-1), self.wqkv)
+        qkv = ops.linear(torch.cat((e_n, f_n), dim=-1), self.wqkv)
         ang = pos.float()[:, None] * self.inv_freq[None, :]
         ang = torch.cat((ang, ang), dim=-1)
         cos, sin = ang.cos().to(feats.dtype), ang.sin().to(feats.dtype)
@@ -331,26 +331,26 @@ class DeviceDraft:
                                          words.data_ptr(), stream), "sf_tree_mask_words")
         ops._launched(2)
         attn = ops.tree_attention(q, d._k, d._v, words, 0, scale=D ** -0.5)
-        o = F.linear(attn.reshape(n, d.heads * D), d.o_proj.weight)
+        o = ops.linear(attn.reshape(n, d.heads * D), d.o_proj.weight)
         h = torch.empty_like(e_n)
         m = torch.empty_like(e_n)
         self._norm(o, feats.contiguous(), h, d.post_norm, m)
-        gu = F.linear(m, self.wgu)
-        dn = F.linear(F.silu(gu[:, : self.inter]) * gu[:, self.inter:], d.down_proj.weight)
+        gu = ops.linear(m, self.wgu)
+        dn = ops.linear(F.silu(gu[:, : self.inter]) * gu[:, self.inter:], d.down_proj.weight)
         out = torch.empty_like(e_n)
         hn = torch.empty_like(e_n)
         self._norm(dn, h, out, d.final_norm, hn)
         return out, hn
 
     def _top(self, hn, k):
-        return ops.logsoftmax_topk(F.linear(hn, self.d.lm_head.weight), k, self.d.logit_scale)
+        return ops.logsoftmax_topk(ops.linear(hn, self.d.lm_head.weight), k, self.d.logit_scale)
 
     def _draft(self, n_new: int) -> None:
         """The whole drafting of one cycle as device work (captured)."""
         d = self.d
         dev = self.dev
         toks = self.tokens[:n_new]
-        feats = d.fc(self.aux[:n_new])
+        feats = ops.linear(self.aux[:n_new], d.fc.weight)
         seed_pos = self.start + (n_new - 1)  # position of the seed = committed tokens
         pos = self.start + torch.arange(n_new, device=dev)
         chain = (torch.ones((), dtype=torch.int64, device=dev) << torch.arange(1, n_new + 1, device=dev)) - 1

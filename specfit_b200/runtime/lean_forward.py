@@ -8,7 +8,9 @@ chain of small torch kernels replaced by:
 * ``sf_add_rmsnorm`` — each residual add fused with the next RMSNorm (input
   norm of the layer, post-attention norm, and the next layer's input norm or
   the final norm);
-* one GEMM for the q|k|v projections (weights concatenated once);
+* one GEMM for the q|k|v projections (weights concatenated once); the
+  projections run on the tcgen05 split-K kernel (``ops.linear``) for
+  verify-sized row counts;
 * ``sf_qk_norm_rope`` — q/k head norms, rotary embedding, and the cache
   update writing k and v rows straight into the ``ReservedCache`` buffers
   (at the host length, or at the device-side offset in static mode);
@@ -108,7 +110,7 @@ class LeanQwen3Forward:
                 cl.length = kv_len
                 cl._publish()
             cap = cl.capacity
-            qkv = F.linear(hn, L.wqkv)
+            qkv = ops.linear(hn, L.wqkv)
             q = torch.empty(B, self.hq, T, self.D, dtype=x.dtype, device=dev)
             N.check(N.lib.sf_qk_norm_rope(qkv.data_ptr(), B, T, self.hq, self.hkv, self.D,
                                           L.qn.data_ptr(), L.kn.data_ptr(), cos.data_ptr(),
@@ -131,7 +133,7 @@ class LeanQwen3Forward:
             for b in range(B):
                 ops.tree_attention(q[b], cl._kbuf[b, :, :kv_len], cl._vbuf[b, :, :kv_len], bits[b],
                                    prefix, scale=self.D ** -0.5, out=attn[b])
-            o = F.linear(attn.view(Nt, self.hq * self.D), L.wo)
+            o = ops.linear(attn.view(Nt, self.hq * self.D), L.wo)
             self._norm(o, res, res, L.ln_post, hn, stream)
             moe = layer.mlp(hn.view(B, T, self.H)).reshape(Nt, self.H)
             nxt = self.layers[li + 1].ln_in if li + 1 < len(self.layers) else self.final
@@ -142,5 +144,5 @@ class LeanQwen3Forward:
                     hook(layer, (), out)
         keep = T if not logits_to_keep else min(int(logits_to_keep), T)
         rows = hn.view(B, T, self.H)[:, T - keep:, :]
-        logits = F.linear(rows, self.model.lm_head.weight)
+        logits = ops.linear(rows.contiguous(), self.model.lm_head.weight)
         return SimpleNamespace(logits=logits)

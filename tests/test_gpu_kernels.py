@@ -380,6 +380,45 @@ def test_logsoftmax_topk_ties_and_shapes(ops):
     assert torch.equal(a[1], b[1]) and torch.allclose(a[0], b[0], atol=1e-6, rtol=0)
 
 
+# ------------------------------------------- projection GEMM (sf_linear_bf16)
+
+
+@pytest.mark.parametrize("rows,n_out,k", [(1, 5120, 2048), (6, 2048, 4096), (16, 12288, 2048),
+                                          (17, 2048, 6144), (32, 300, 128), (3, 128, 64), (8, 151936, 2048)])
+def test_linear_matches_fp32_reference(ops, rows, n_out, k):
+    """The tcgen05 split-K projection against an fp32 reference of the same
+    op: every output within one bf16 rounding of the fp32 result (sums in a
+    different order may round the other way), and close to F.linear."""
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + n_out + k)
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n_out, k, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    from specfit_b200 import _native
+
+    y = torch.empty(rows, n_out, dtype=torch.bfloat16, device=DEV)
+    rc = _native.lib.sf_linear_bf16(x.data_ptr(), rows, k, w.data_ptr(), n_out, y.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+    assert rc == 0  # the kernel itself, whatever ops.linear would pick
+    ref = x.float() @ w.float().t()
+    tol = ref.abs() * 2 ** -7 + 1e-3  # one bf16 ulp of the result, plus fp32 summation noise
+    assert ((y.float() - ref).abs() <= tol).all()
+    lib = torch.nn.functional.linear(x, w)
+    assert (y.float() - lib.float()).abs().max() <= 2e-2 * ref.abs().max()
+
+
+def test_linear_is_deterministic_and_falls_back(ops):
+    """Fixed summation order: repeated calls give the same bits; shapes the
+    kernel does not take (many rows, K % 64 != 0) go to the library GEMM."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(6, 4096, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(2048, 4096, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    a, b = ops.linear(x, w), ops.linear(x, w)
+    assert torch.equal(a, b)
+    for xs, ws in (((64, 256), (128, 256)), ((4, 100), (128, 100))):
+        xx = torch.randn(*xs, generator=g, device=DEV).to(torch.bfloat16)
+        ww = torch.randn(*ws, generator=g, device=DEV).to(torch.bfloat16)
+        assert torch.equal(ops.linear(xx, ww), torch.nn.functional.linear(xx, ww))
+
+
 def test_device_status_clean(ops):
     from specfit_b200 import _native
 
