@@ -971,9 +971,13 @@ def decode_mode(args):
     # the model to the machine, so the headline uses one fitted on this B200.
     ref_res, _ = run(args.new_tokens, 7)
     peaks = measured_peaks()
-    calibrated = None
+    calibrated = verify_fit = None
     if not args.eager_decode:
-        calibrated = spec.calibrate_cost_model(expert_ns=EXPERT_BYTES / peaks["hbm_gbs"])
+        expert_ns = EXPERT_BYTES / peaks["hbm_gbs"]
+        verify_fit = spec.calibrate_cost_model(expert_ns=expert_ns)
+        spec.acceptance = BernoulliAcceptance(98)
+        calibrated = spec.calibrate_cycle_cost_model(ctx_host.to(device, non_blocking=True),
+                                                     expert_ns=expert_ns)
         spec.cost_model = calibrated
         run(32, 99)
     launches0 = ops.LAUNCHES[0]
@@ -1026,11 +1030,14 @@ def decode_mode(args):
                               "verify": round(mean([c.verify_ms for c in cyc]), 3),
                               "commit": round(mean([c.commit_ms for c in cyc]), 3)},
                   "prefill_s": round(res.prefill_s, 3)},
-        "cost_model": ({"kind": "SelectionCostModel fitted on this B200 (verify-graph replay per tree "
-                                "size; slope = one packed expert over the measured HBM bandwidth)",
+        "cost_model": ({"kind": "SelectionCostModel fitted on this B200 the reference's way: whole "
+                                "decode cycles timed per forced tree size; slope = one packed expert "
+                                "over the measured HBM bandwidth",
                         "size_intercept_ns": [round(x) for x in calibrated.size_intercept_ns],
-                        "expert_ns": round(calibrated.expert_ns, 1)} if calibrated is not None else
-                       {"kind": "reference natural/legacy coefficients"}),
+                        "size_mean_ns": [round(x) for x in calibrated.size_mean_ns],
+                        "expert_ns": round(calibrated.expert_ns, 1),
+                        "verify_only_intercept_ns": [round(x) for x in verify_fit.size_intercept_ns]}
+                       if calibrated is not None else {"kind": "reference natural/legacy coefficients"}),
         "reference_cost_model": {
             "value": round(ref_res.committed / ref_res.decode_s, 3), "unit": "tokens/s",
             "committed_per_cycle": round(ref_res.committed / max(len(ref_res.cycles), 1), 3),

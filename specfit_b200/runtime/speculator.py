@@ -81,6 +81,7 @@ class CycleRecord:
     select_ms: float
     verify_ms: float
     commit_ms: float
+    experts: int = 0  # distinct (layer, expert) pairs of the verified rows (the footprint)
 
 
 @dataclass
@@ -315,6 +316,39 @@ class B200TreeSpeculator:
                 h.remove()
         return SelectionCostModel(tuple(means), tuple(intercepts), float(expert_ns))
 
+    def calibrate_cycle_cost_model(self, input_ids: torch.Tensor, *, expert_ns: float,
+                                   tokens: int = 64):
+        """A ``SelectionCostModel`` fitted the way the reference fits its
+        own, on whole local cycles (``docs/results/selection-refinement-*.json``:
+        "fixed-state local cycles"): for each tree size n = 0..max_nodes a
+        generation of ``tokens`` tokens runs with the selection forced to
+        size n (a cost model under which only size-n trees have a finite
+        price), each cycle's wall time (draft, select, verify, commit) is
+        taken, and ``intercept[n] = median(cycle time - expert_ns *
+        |footprint|)`` over the cycles that verified n nodes (the first
+        cycle, with the eager catch-up, excluded).  ``expert_ns`` is given,
+        e.g. one packed expert's bytes over the measured HBM bandwidth."""
+        from ..selection import SelectionCostModel
+
+        keep = self.cost_model
+        sizes = self.max_nodes + 1
+        intercepts, means = [], []
+        try:
+            for n in range(sizes):
+                price = tuple(1e6 if i == n else 1e15 for i in range(sizes))
+                self.cost_model = SelectionCostModel(price, price, float(expert_ns))
+                res = self.generate(input_ids, tokens)
+                cyc = [c for c in res.cycles[1:] if c.selected == n]
+                if not cyc:
+                    raise RuntimeError(f"no cycle verified {n} nodes during calibration")
+                total = [1e6 * (c.draft_ms + c.select_ms + c.verify_ms + c.commit_ms) for c in cyc]
+                means.append(float(np.median(total)))
+                intercepts.append(max(float(np.median([t - expert_ns * c.experts
+                                                       for t, c in zip(total, cyc)])), 0.0))
+        finally:
+            self.cost_model = keep
+        return SelectionCostModel(tuple(means), tuple(intercepts), float(expert_ns))
+
     # ------------------------------------------------------------ generate
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int, *, sync_timing: bool = False):
         if input_ids.ndim != 2 or input_ids.shape[0] != 1:
@@ -413,6 +447,8 @@ class B200TreeSpeculator:
                                          [c.cumulative_log_probability for c in pool.candidates],
                                          fp, self.cost_model, None, max_nodes=max_nodes)
                         tree = pool.to_tree(tuple(ids))
+                rows_fp = np.asarray(fp)[[0] + list(tree.source_raw_ids)].view(np.uint64)
+                experts = int(np.unpackbits(np.bitwise_or.reduce(rows_fp, axis=0).view(np.uint8)).sum())
                 tick()
                 tc = time.perf_counter()
                 base = cache.get_seq_length()
@@ -450,7 +486,7 @@ class B200TreeSpeculator:
                 te = time.perf_counter()
                 result.cycles.append(CycleRecord(n_pool, len(ids), len(path),
                                                  (tb - ta) * 1e3, (tc - tb) * 1e3, (td - tc) * 1e3,
-                                                 (te - td) * 1e3))
+                                                 (te - td) * 1e3, experts))
             torch.cuda.synchronize(dev)
             result.decode_s = time.perf_counter() - t_start
             result.tokens = result.tokens[:max_new_tokens]

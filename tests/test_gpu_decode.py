@@ -163,3 +163,23 @@ def test_native_compaction_matches_generic():
     ref.crop(35)
     for a, b in zip(caches[0].layers, ref.layers):
         assert torch.equal(a.keys, b.keys) and torch.equal(a.values, b.values)
+
+
+def test_cycle_calibration_forces_every_tree_size():
+    """The reference-style fit times whole cycles at each forced tree size:
+    one intercept per size, every size actually verified, and the fitted
+    model selects drafted nodes again afterwards."""
+    cfg, m, d = small()
+    try:
+        ctx = torch.randint(0, 512, (1, 40), generator=torch.Generator().manual_seed(4)).to(DEV)
+        spec = B200TreeSpeculator(m, d, cost_model=cost(), acceptance=BernoulliAcceptance(5), graphs=True)
+        model = spec.calibrate_cycle_cost_model(ctx, expert_ns=500.0, tokens=32)
+        assert len(model.size_intercept_ns) == 8 and all(x >= 0 for x in model.size_intercept_ns)
+        assert all(x > 0 for x in model.size_mean_ns)
+        assert spec.cost_model is not model  # the speculator's own model is restored
+        spec.cost_model = model
+        res = spec.generate(ctx, 24)
+        assert res.committed == 24 and all(c.experts > 0 for c in res.cycles)
+        spec.release_graphs()
+    finally:
+        m.close()
