@@ -27,6 +27,8 @@
  *                         + cache update (write k, v rows)
  *   sf_kv_compact         _compact_tree_cache                   src/specfit/runtime/eagle3_tree.py:833-858
  *   sf_logsoftmax_topk    log_softmax + topk of a drafter level src/specfit/runtime/eagle3_tree.py:611-803
+ *   sf_draft_level        one level of the candidate-pool build  src/specfit/runtime/eagle3_tree.py:611-803
+ *   sf_rope_rows          rotary cos/sin rows                    transformers/...:Qwen3MoeRotaryEmbedding
  *   sf_linear_bf16        F.linear (q|k|v, o, lm_head, drafter)  transformers/...:Qwen3MoeAttention.forward,
  *                                                               Qwen3MoeForCausalLM.forward (lm_head)
  *                                                               (candidate-pool expansion)
@@ -442,6 +444,32 @@ SF_API int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, f
  */
 SF_API int sf_linear_bf16(const void* x, int64_t rows, int64_t in_features, const void* weight,
                           int64_t out_features, void* out, void* stream);
+/*
+ * One level of a drafted candidate pool (the tree builder's level step,
+ * src/specfit/runtime/eagle3_tree.py:611-803): among rows x k children
+ * (top_values / top_indices [rows][k]: each frontier row's k most likely next
+ * tokens and their log-probabilities), the `width` best by cum[row] + value
+ * (fp64), ties by lower frontier row then lower token, become the next
+ * frontier: next_tokens, next_cum, next_ancestor_sets (the parent's set plus
+ * bit row_base + slot), next_positions (*seed_pos + depth + 1) and
+ * next_hidden (the parent rows of hidden [rows][hidden_size] bf16).  Their
+ * pool rows (token, first + parent row, log-probability, cumulative,
+ * depth + 1) are written to out_rows [width][5] fp64.  rows * k <= 32,
+ * row_base + width <= 64.
+ */
+SF_API int sf_draft_level(const float* top_values, const int64_t* top_indices, int rows, int k,
+                          const double* cum, const int64_t* ancestor_sets, const void* hidden,
+                          int hidden_size, int width, int64_t first, int depth, int row_base,
+                          const int64_t* seed_pos, int64_t* next_tokens, double* next_cum,
+                          int64_t* next_ancestor_sets, int64_t* next_positions, void* next_hidden,
+                          double* out_rows, void* stream);
+/*
+ * Rotary embedding rows at device-side positions: cos_out / sin_out
+ * [rows][head_dim] bf16, column d and d + head_dim/2 = bf16(cos / sin(a)),
+ * a = float(positions[r]) * inv_freq[d] in fp32.
+ */
+SF_API int sf_rope_rows(const int64_t* positions, int rows, const float* inv_freq, int head_dim,
+                        void* cos_out, void* sin_out, void* stream);
 SF_API int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
                            int num_kv_heads, int head_dim, const void* q_norm_weight,
                            const void* k_norm_weight, const void* cos, const void* sin, float eps,

@@ -104,6 +104,9 @@ SIGNATURES = {
     "sf_kv_compact": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _vp, _i32, _vp, _vp]),
     "sf_logsoftmax_topk": (_i32, [_vp, _i64, _i64, _f32, _i32, _vp, _vp, _vp]),
     "sf_linear_bf16": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "sf_draft_level": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i64, _i32, _i32, _vp,
+                              _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sf_rope_rows": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp]),
     "sf_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _f32, _i64, _i32, _vp, _vp]),
     "sf_qk_norm_rope": (_i32, [_vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _f32, _vp, _vp,
                                _vp, _i64, _i64, _i64, _vp, _vp]),

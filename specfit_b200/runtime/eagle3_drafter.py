@@ -284,6 +284,14 @@ class DeviceDraft:
         self.aux = z(max_new, d.fc.in_features, dt=d.fc.weight.dtype)  # their features' sources
         self.start = z(())                            # committed rows before this cycle
         self.out = torch.zeros(self.n_cand, 5, dtype=torch.float64, device=dev)
+        # Frontier buffers, two sets used alternately by the levels: tokens,
+        # cumulative scores, ancestor sets, positions and parent hidden rows.
+        wmax = max(self.widths)
+        self._lv = [dict(tok=z(wmax), cum=z(wmax, dt=torch.float64), vis=z(wmax), pos=z(wmax),
+                         hid=z(wmax, d.hidden, dt=d.fc.weight.dtype)) for _ in range(2)]
+        self._seed_cum = z(1, dt=torch.float64)
+        self._seed_vis = torch.ones(1, dtype=torch.long, device=dev)
+        self._seed_pos = z(())                      # block row of the seed (= its position)
         self._host_out = torch.empty(self.n_cand, 5, dtype=torch.float64).pin_memory()
         self._host_extra: dict = {}
         # Optional device work appended to every drafting graph: called as
@@ -318,9 +326,10 @@ class DeviceDraft:
         self._norm(d.embed(tokens), None, None, d.emb_norm, e_n)
         self._norm(feats.contiguous(), None, None, d.hid_norm, f_n)
         qkv = ops.linear(torch.cat((e_n, f_n), dim=-1), self.wqkv)
-        ang = pos.float()[:, None] * self.inv_freq[None, :]
-        ang = torch.cat((ang, ang), dim=-1)
-        cos, sin = ang.cos().to(feats.dtype), ang.sin().to(feats.dtype)
+        cos = torch.empty(n, D, dtype=feats.dtype, device=self.dev)
+        sin = torch.empty_like(cos)
+        N.check(N.lib.sf_rope_rows(pos.data_ptr(), n, self.inv_freq.data_ptr(), D, cos.data_ptr(),
+                                   sin.data_ptr(), stream), "sf_rope_rows")
         q = torch.empty(d.heads, n, D, dtype=feats.dtype, device=self.dev)
         N.check(N.lib.sf_qk_norm_rope(qkv.data_ptr(), 1, n, d.heads, d.kv_heads, D, None, None,
                                       cos.data_ptr(), sin.data_ptr(), float(d.eps), q.data_ptr(),
@@ -329,7 +338,7 @@ class DeviceDraft:
         words = torch.empty(n, cap // 32, dtype=torch.int32, device=self.dev)
         N.check(N.lib.sf_tree_mask_words(vis.data_ptr(), n, block_start.data_ptr(), cap // 32,
                                          words.data_ptr(), stream), "sf_tree_mask_words")
-        ops._launched(2)
+        ops._launched(3)
         attn = ops.tree_attention(q, d._k, d._v, words, 0, scale=D ** -0.5)
         o = ops.linear(attn.reshape(n, d.heads * D), d.o_proj.weight)
         h = torch.empty_like(e_n)
@@ -351,49 +360,44 @@ class DeviceDraft:
         dev = self.dev
         toks = self.tokens[:n_new]
         feats = ops.linear(self.aux[:n_new], d.fc.weight)
-        seed_pos = self.start + (n_new - 1)  # position of the seed = committed tokens
+        torch.add(self.start, n_new - 1, out=self._seed_pos)  # the seed's position = committed tokens
         pos = self.start + torch.arange(n_new, device=dev)
         chain = (torch.ones((), dtype=torch.int64, device=dev) << torch.arange(1, n_new + 1, device=dev)) - 1
         # Catch-up rows are causal among themselves after the committed rows;
         # the seed row (last) opens the tree block at row seed_pos.
         h, hn = self._rows(toks, feats, pos, chain, self.start, self.start)
-        block = seed_pos
-        seed_h = h[-1:]
-        one = torch.ones((), dtype=torch.int64, device=dev)
-        cond, tok = (t[0] for t in self._top(hn[-1:], self.widths[0]))
-        cum = cond.double()
-        parent = torch.full((self.widths[0],), -1, dtype=torch.long, device=dev)  # -1 = the seed
-        par_vis = torch.ones(self.widths[0], dtype=torch.int64, device=dev)       # seed = bit 0
-        out_tok, out_par, out_cond, out_cum, out_depth = [tok], [parent], [cond.double()], [cum], []
-        out_depth.append(torch.ones(self.widths[0], dtype=torch.float64, device=dev))
-        hidden_parent = seed_h.expand(self.widths[0], -1)
+        block = self._seed_pos
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        H = d.hidden
+
+        def level(v, t, rows, k, cum, vis, hidden, width, first, depth, row_base, nxt, out_at):
+            N.check(N.lib.sf_draft_level(v.data_ptr(), t.data_ptr(), rows, k, cum.data_ptr(),
+                                         vis.data_ptr(), hidden.data_ptr(), H, width, first, depth,
+                                         row_base, self._seed_pos.data_ptr(), nxt["tok"].data_ptr(),
+                                         nxt["cum"].data_ptr(), nxt["vis"].data_ptr(),
+                                         nxt["pos"].data_ptr(), nxt["hid"].data_ptr(),
+                                         self.out[out_at].data_ptr(), stream), "sf_draft_level")
+            ops._launched(1)
+
+        # Level 1: the seed row's best first_width tokens (parent -1 = the seed,
+        # block row 0); their rows go at block rows 1.. .
+        v0, t0 = self._top(hn[-1:], self.widths[0])
+        level(v0, t0, 1, self.widths[0], self._seed_cum, self._seed_vis, h[-1:].contiguous(),
+              self.widths[0], -1, 0, 1, self._lv[0], 0)
         first = 0                      # candidate index of the frontier's first node
-        row_next = 1                   # next row inside the tree block
+        row_next = 1                   # block row of the frontier's first node
+        w = self.widths[0]
         for depth in range(1, self.max_depth):
-            w = tok.shape[0]
-            own = one << torch.arange(row_next, row_next + w, device=dev)
-            vis = par_vis | own
-            hl, hln = self._rows(tok, hidden_parent, seed_pos + depth + 0 * tok, vis, block,
+            cur, nxt = self._lv[(depth - 1) % 2], self._lv[depth % 2]
+            hl, hln = self._rows(cur["tok"][:w], cur["hid"][:w], cur["pos"][:w], cur["vis"][:w], block,
                                  block + row_next)
-            row_next += w
             v, t = self._top(hln, self.top_k)                                # [w, k]
-            score = cum[:, None] + v.double()
-            best, flat = torch.topk(score.reshape(-1), self.widths[depth])    # the level's nodes
-            pj = torch.div(flat, self.top_k, rounding_mode="floor")
-            tok = t.reshape(-1)[flat]
-            cond = v.reshape(-1)[flat]
-            cum = best
-            parent = first + pj
-            par_vis = vis[pj]
-            hidden_parent = hl[pj]
+            level(v, t, w, self.top_k, cur["cum"], cur["vis"], hl, self.widths[depth], first, depth,
+                  row_next + w, nxt, first + w)
             first += w
-            out_tok.append(tok)
-            out_par.append(parent)
-            out_cond.append(cond.double())
-            out_cum.append(cum)
-            out_depth.append(torch.full((tok.shape[0],), float(depth + 1), dtype=torch.float64, device=dev))
-        self.out.copy_(torch.stack((torch.cat(out_tok).double(), torch.cat(out_par).double(),
-                                    torch.cat(out_cond), torch.cat(out_cum), torch.cat(out_depth)), dim=1))
+            row_next += w
+            w = self.widths[depth]
+
         if self.post is not None:
             self.post(self.tokens[n_new - 1: n_new], self.out)
 

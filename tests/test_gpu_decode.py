@@ -183,3 +183,42 @@ def test_cycle_calibration_forces_every_tree_size():
         spec.release_graphs()
     finally:
         m.close()
+
+
+def test_draft_level_kernel_matches_the_eager_sort():
+    """sf_draft_level picks the level's nodes by the eager builder's rule
+    (score desc, parent asc, token asc; exact ties included) and writes the
+    pool rows, ancestor sets, positions and parent hidden rows."""
+    import numpy as np
+
+    from specfit_b200 import _native as N
+
+    g = torch.Generator().manual_seed(11)
+    rows, k, width, H = 8, 4, 8, 256
+    v = -torch.rand(rows, k, generator=g).sort(dim=1, descending=True).values
+    v[2, 1] = v[5, 0] = -0.5                       # equal log-probs ...
+    cum = (-torch.rand(rows, generator=g)).double()
+    cum[5] = cum[2]                                # ... and equal scores across parents
+    t = torch.randint(0, 1000, (rows, k), generator=g)
+    vis = torch.randint(1, 1 << 20, (rows,), generator=g)
+    hid = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    dev = [x.to(DEV) for x in (v, t, cum, vis, hid)]
+    seed_pos = torch.tensor(100, device=DEV)
+    nt, nc, nv, npos = (torch.zeros(width, dtype=dt, device=DEV)
+                        for dt in (torch.long, torch.float64, torch.long, torch.long))
+    nh = torch.zeros(width, H, dtype=torch.bfloat16, device=DEV)
+    out = torch.zeros(width, 5, dtype=torch.float64, device=DEV)
+    rc = N.lib.sf_draft_level(dev[0].data_ptr(), dev[1].data_ptr(), rows, k, dev[2].data_ptr(),
+                              dev[3].data_ptr(), dev[4].data_ptr(), H, width, 12, 3, 20,
+                              seed_pos.data_ptr(), nt.data_ptr(), nc.data_ptr(), nv.data_ptr(),
+                              npos.data_ptr(), nh.data_ptr(), out.data_ptr(),
+                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    opts = sorted(((float(cum[j]) + float(v[j, r]), j, int(t[j, r]), float(v[j, r]))
+                   for j in range(rows) for r in range(k)), key=lambda o: (-o[0], o[1], o[2]))[:width]
+    o = out.cpu().numpy()
+    for s, (score, j, tok, cond) in enumerate(opts):
+        assert int(nt[s]) == tok and float(nc[s]) == score
+        assert int(nv[s]) == int(vis[j]) | (1 << (20 + s)) and int(npos[s]) == 104
+        assert torch.equal(nh[s].cpu(), hid[j])
+        assert np.array_equal(o[s], [tok, 12 + j, cond, score, 4])
