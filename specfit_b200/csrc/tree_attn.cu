@@ -316,7 +316,9 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
   SF_CHECK_ARG(impl == SF_ATTN_AUTO || impl == SF_ATTN_SIMT || impl == SF_ATTN_MMA,
                "unknown attention implementation %d", impl);
   if (impl != SF_ATTN_SIMT && tree_attention_mma_supports(p, head_dim)) {
-    if (int rc = tree_attention_mma(p, s)) return rc;
+    bool merged = false;
+    if (int rc = tree_attention_mma(p, out, &merged, s)) return rc;
+    if (merged) return SF_OK;
     SF_CHECK_CUDA(launch_pdl(tree_attn_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256),
                              0, s, p, static_cast<__nv_bfloat16*>(out)));
     SF_CHECK_LAUNCH();

@@ -25,7 +25,10 @@ struct AttnParams {
 
 bool tree_attention_mma_supports(const AttnParams& p, int head_dim);
 // Launches the mma.sync split kernel: chooses p.splits / p.keys_per_split,
-// sets p.part_ml, writes the split partials.
-int tree_attention_mma(AttnParams& p, cudaStream_t stream);
+// sets p.part_ml, writes the split partials.  When the splits of a row block
+// fit one thread-block cluster (at most 16) and the device can place it, the
+// splits are merged inside the kernel through distributed shared memory and
+// `out` ([Tq, Hq, D] bf16) is written directly: *merged is set to true.
+int tree_attention_mma(AttnParams& p, void* out, bool* merged, cudaStream_t stream);
 
 }  // namespace sf

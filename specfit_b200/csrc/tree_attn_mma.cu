@@ -19,7 +19,10 @@
 // The CTA writes unnormalised O plus (row max, row sum) per split; the merge
 // kernel in tree_attn.cu combines the splits.  No barriers other than
 // __syncthreads, no TMEM, no TMA.
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "tree_attn.h"
@@ -114,9 +117,16 @@ __device__ __forceinline__ void stage_block(__nv_bfloat16* ks, __nv_bfloat16* vs
 
 constexpr int kStageElems = kKeys * kPitch;  // one K (or V) buffer
 constexpr size_t kSmemBytes = 4 * kStageElems * sizeof(__nv_bfloat16);  // 2 stages x (K, V)
+// In-kernel merge: the splits of a row block form one cluster (at most 16
+// CTAs); each CTA owns ceil(64 / S) of the 64 packed rows and receives every
+// split's unnormalised row output and (max, sum) for them.
+constexpr int kMaxFusedSplits = 16;
+constexpr int kRecvRows = kRowsCta + kMaxFusedSplits;  // >= S * ceil(64 / S)
+constexpr size_t kFusedSmemBytes = kSmemBytes + (size_t)kRecvRows * (kD + 2) * sizeof(float);
 
+template <bool kFused>
 __global__ void __launch_bounds__(kWarps * 32)
-tree_attn_mma_kernel(AttnParams p) {
+tree_attn_mma_kernel(AttnParams p, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) __nv_bfloat16 smem[];
@@ -272,20 +282,83 @@ tree_attn_mma_kernel(AttnParams p) {
     __syncthreads();  // this stage is consumed before it is refilled
   }
 
-  // Row sums across the quad, then the split partials.
+  // Row sums across the quad.
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
     l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
-    if (!rok[h]) continue;
-    const int64_t idx = ((int64_t)split * p.num_heads + head[h]) * p.q_len + trow[h];
-    float* dst = p.part_o + idx * kD;
+  }
+  if constexpr (!kFused) {
+    // The split partials, merged by tree_attn_merge_kernel.
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt)
-      *reinterpret_cast<float2*>(dst + dt * 8 + 2 * c) = make_float2(o[dt][2 * h], o[dt][2 * h + 1]);
-    if (c == 0) {
-      p.part_ml[idx * 2] = m[h];
-      p.part_ml[idx * 2 + 1] = l[h];
+    for (int h = 0; h < 2; ++h) {
+      if (!rok[h]) continue;
+      const int64_t idx = ((int64_t)split * p.num_heads + head[h]) * p.q_len + trow[h];
+      float* dst = p.part_o + idx * kD;
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt)
+        *reinterpret_cast<float2*>(dst + dt * 8 + 2 * c) = make_float2(o[dt][2 * h], o[dt][2 * h + 1]);
+      if (c == 0) {
+        p.part_ml[idx * 2] = m[h];
+        p.part_ml[idx * 2 + 1] = l[h];
+      }
+    }
+  } else {
+    // Each packed row goes to the CTA of the cluster that owns it (stores
+    // into its shared memory); after the cluster barrier every CTA merges
+    // its own rows over the S splits in split order and writes them.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = (int)cluster.num_blocks();  // == gridDim.z: one cluster per (head, row block)
+    const int rpo = (kRowsCta + S - 1) / S;
+    float* recv_o = reinterpret_cast<float*>(smem + 4 * kStageElems);  // [kRecvRows][kD]
+    float* recv_ml = recv_o + (size_t)kRecvRows * kD;                 // [kRecvRows][2]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int prow = warp * 16 + g + 8 * h;
+      const int owner = prow / rpo;
+      const int slot = split * rpo + (prow - owner * rpo);
+      float* dsto = cluster.map_shared_rank(recv_o, owner) + (size_t)slot * kD;
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt)
+        *reinterpret_cast<float2*>(dsto + dt * 8 + 2 * c) = make_float2(o[dt][2 * h], o[dt][2 * h + 1]);
+      if (c == 0) {
+        float* dml = cluster.map_shared_rank(recv_ml, owner) + (size_t)slot * 2;
+        dml[0] = m[h];
+        dml[1] = l[h];
+      }
+    }
+    cluster.sync();
+    for (int lr = warp; lr < rpo; lr += kWarps) {
+      const int prow = split * rpo + lr;  // this CTA's rank in the cluster is its split
+      const int pr = blockIdx.y * kRowsCta + prow;
+      if (prow >= kRowsCta || pr >= packed_rows) break;
+      float gm = -INFINITY;
+      for (int sp = 0; sp < S; ++sp) gm = fmaxf(gm, recv_ml[(sp * rpo + lr) * 2]);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float denom = 0.f;
+      if (gm != -INFINITY) {
+        for (int sp = 0; sp < S; ++sp) {
+          const float ms = recv_ml[(sp * rpo + lr) * 2];
+          if (ms == -INFINITY) continue;
+          const float w = expf(ms - gm);
+          denom += w * recv_ml[(sp * rpo + lr) * 2 + 1];
+          const float4 ov = *reinterpret_cast<const float4*>(recv_o + (size_t)(sp * rpo + lr) * kD + lane * 4);
+          acc[0] += w * ov.x;
+          acc[1] += w * ov.y;
+          acc[2] += w * ov.z;
+          acc[3] += w * ov.w;
+        }
+      }
+      const float inv = denom > 0.f ? 1.f / denom : 0.f;
+      const int hd = kvh * p.group + pr / p.q_len, t = pr % p.q_len;
+      __nv_bfloat16* dst = out + ((int64_t)t * p.num_heads + hd) * kD + lane * 4;
+      __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
+      uint2 packed;
+      packed.x = *reinterpret_cast<uint32_t*>(&lo);
+      packed.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(dst) = packed;
     }
   }
 }
@@ -298,11 +371,73 @@ bool tree_attention_mma_supports(const AttnParams& p, int head_dim) {
          (reinterpret_cast<uintptr_t>(p.q) & 3u) == 0 && p.q_len > 0 && p.kv_len > 0;
 }
 
-int tree_attention_mma(AttnParams& p, cudaStream_t stream) {
+namespace {
+
+// Whether clusters of `size` CTAs of the fused kernel can be placed (16 is
+// above the portable limit of 8), checked once per device and size.
+bool fused_clusters_ok(int size) {
+  static std::mutex mu;
+  static int known[64][kMaxFusedSplits + 1] = {};  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (size < 1 || size > kMaxFusedSplits || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return false;
+  std::lock_guard<std::mutex> lock(mu);
+  int& k = known[dev][size];
+  if (k == 0) {
+    bool ok = cudaFuncSetAttribute(tree_attn_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kFusedSmemBytes) == cudaSuccess &&
+              cudaFuncSetAttribute(tree_attn_mma_kernel<true>,
+                                   cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    if (ok) {
+      cudaLaunchConfig_t probe = {};
+      probe.gridDim = dim3(1, 1, (unsigned)size);
+      probe.blockDim = dim3(kWarps * 32, 1, 1);
+      probe.dynamicSmemBytes = kFusedSmemBytes;
+      cudaLaunchAttribute a[1];
+      a[0].id = cudaLaunchAttributeClusterDimension;
+      a[0].val.clusterDim.x = 1;
+      a[0].val.clusterDim.y = 1;
+      a[0].val.clusterDim.z = (unsigned)size;
+      probe.attrs = a;
+      probe.numAttrs = 1;
+      int clusters = 0;
+      ok = cudaOccupancyMaxActiveClusters(&clusters, tree_attn_mma_kernel<true>, &probe) == cudaSuccess &&
+           clusters > 0;
+    }
+    (void)cudaGetLastError();
+    k = ok ? 1 : 2;
+  }
+  return k == 1;
+}
+
+}  // namespace
+
+int tree_attention_mma(AttnParams& p, void* out, bool* merged, cudaStream_t stream) {
   const int64_t row_blocks = ((int64_t)p.group * p.q_len + kRowsCta - 1) / kRowsCta;
   const int64_t blocks = (p.kv_len + kKeys - 1) / kKeys;
   int64_t want = (2 * (int64_t)num_sms() + p.num_kv_heads * row_blocks - 1) /
                  (p.num_kv_heads * row_blocks);
+  *merged = false;
+  // In-kernel merge when the splits fit one cluster without giving a CTA
+  // more key blocks than the separate-merge launch would (a longer serial
+  // chain per CTA costs more than the merge launch saves: measured at 2,320
+  // keys and 6 query rows).
+  {
+    const int64_t fw = std::max<int64_t>(1, std::min<int64_t>(want, std::min<int64_t>(blocks, kMaxFusedSplits)));
+    const int64_t sw = std::max<int64_t>(1, std::min<int64_t>(want, std::min<int64_t>(blocks, kMaxSplitsMma)));
+    const int kps = (int)(((blocks + fw - 1) / fw) * kKeys);
+    const int splits = (int)((p.kv_len + kps - 1) / kps);
+    if (out && (blocks + fw - 1) / fw <= (blocks + sw - 1) / sw && fused_clusters_ok(splits)) {
+      p.keys_per_split = kps;
+      p.splits = splits;
+      dim3 grid((unsigned)p.num_kv_heads, (unsigned)row_blocks, (unsigned)splits);
+      SF_CHECK_CUDA(launch_pdl_cluster3(tree_attn_mma_kernel<true>, grid, dim3(kWarps * 32),
+                                        kFusedSmemBytes, stream, dim3(1, 1, (unsigned)splits), p,
+                                        static_cast<__nv_bfloat16*>(out)));
+      *merged = true;
+      return SF_OK;
+    }
+  }
   want = std::max<int64_t>(1, std::min<int64_t>(want, std::min<int64_t>(blocks, kMaxSplitsMma)));
   p.keys_per_split = (int)(((blocks + want - 1) / want) * kKeys);
   p.splits = (int)((p.kv_len + p.keys_per_split - 1) / p.keys_per_split);
@@ -310,13 +445,13 @@ int tree_attention_mma(AttnParams& p, cudaStream_t stream) {
   dim3 grid((unsigned)p.num_kv_heads, (unsigned)row_blocks, (unsigned)p.splits);
   static std::atomic<unsigned long long> attr_done{0};
   const int rc = once_per_device(attr_done, [] {
-    SF_CHECK_CUDA(cudaFuncSetAttribute(tree_attn_mma_kernel,
+    SF_CHECK_CUDA(cudaFuncSetAttribute(tree_attn_mma_kernel<false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     return SF_OK;
   });
   if (rc != SF_OK) return rc;
-  SF_CHECK_CUDA(launch_pdl(tree_attn_mma_kernel, dim3(grid), dim3(kWarps * 32), kSmemBytes, stream,
-                           p));
+  SF_CHECK_CUDA(launch_pdl(tree_attn_mma_kernel<false>, dim3(grid), dim3(kWarps * 32), kSmemBytes,
+                           stream, p, static_cast<__nv_bfloat16*>(nullptr)));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
