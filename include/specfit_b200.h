@@ -470,6 +470,18 @@ SF_API int sf_draft_level(const float* top_values, const int64_t* top_indices, i
  */
 SF_API int sf_rope_rows(const int64_t* positions, int rows, const float* inv_freq, int head_dim,
                         void* cos_out, void* sin_out, void* stream);
+/*
+ * sf_moe_combine (bf16) fused with the decoder layer's residual add and the
+ * next RMSNorm: for each token, moe = the combined row exactly as
+ * sf_moe_combine writes it, then exactly sf_add_rmsnorm(moe, residual_in,
+ * residual_out, norm_weight, eps, out).  hidden_size % 8 == 0, <= 8192; rows
+ * 16-byte aligned.  residual_out may equal residual_in.
+ */
+SF_API int sf_moe_combine_add_rmsnorm(const void* out_sorted, const int32_t* inv_pos,
+                                      const int64_t* topk_index, const int32_t* expert_rank,
+                                      int num_experts, int64_t tokens, int top_k, int hidden_size,
+                                      int reduce, const void* residual_in, void* residual_out,
+                                      const void* norm_weight, float eps, void* out, void* stream);
 SF_API int sf_qk_norm_rope(const void* qkv, int64_t batch, int64_t tokens, int num_heads,
                            int num_kv_heads, int head_dim, const void* q_norm_weight,
                            const void* k_norm_weight, const void* cos, const void* sin, float eps,

@@ -107,6 +107,8 @@ SIGNATURES = {
     "sf_draft_level": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i64, _i32, _i32, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sf_rope_rows": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp]),
+    "sf_moe_combine_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
+                                          _f32, _vp, _vp]),
     "sf_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _f32, _i64, _i32, _vp, _vp]),
     "sf_qk_norm_rope": (_i32, [_vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _f32, _vp, _vp,
                                _vp, _i64, _i64, _i64, _vp, _vp]),

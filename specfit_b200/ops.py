@@ -211,6 +211,24 @@ def moe_combine(out_sorted: torch.Tensor, d: Dispatch, top_k_index: torch.Tensor
     return res
 
 
+
+def moe_combine_add_rmsnorm(out_sorted: torch.Tensor, d: Dispatch, top_k_index: torch.Tensor,
+                            residual: torch.Tensor, norm_weight: torch.Tensor, eps: float,
+                            out: torch.Tensor, reduce: int = N.SF_REDUCE_MODEL_DTYPE) -> torch.Tensor:
+    """``moe_combine`` then the residual add (``residual`` updated in place)
+    and RMSNorm into ``out`` in one launch, bit-identical to the two steps."""
+    dev = _require_cuda(out_sorted, top_k_index, residual, out)
+    if d.tokens == 0:
+        return out
+    N.check(N.lib.sf_moe_combine_add_rmsnorm(out_sorted.data_ptr(), d.inv_pos.data_ptr(),
+                                             top_k_index.contiguous().data_ptr(), None, d.num_experts,
+                                             d.tokens, d.top_k, out_sorted.shape[1], reduce,
+                                             residual.data_ptr(), residual.data_ptr(),
+                                             norm_weight.data_ptr(), float(eps), out.data_ptr(),
+                                             _stream(dev)), "sf_moe_combine_add_rmsnorm")
+    _launched(1)
+    return out
+
 # ---------------------------------------------------------------------------
 # K5 slot fill
 

@@ -14,8 +14,11 @@ chain of small torch kernels replaced by:
 * ``sf_qk_norm_rope`` — q/k head norms, rotary embedding, and the cache
   update writing k and v rows straight into the ``ReservedCache`` buffers
   (at the host length, or at the device-side offset in static mode);
-* ``sf_tree_attention`` per request, the o projection, and the MoE block
-  module itself (its router hooks still fire).
+* ``sf_tree_attention`` per request, the o projection, and the MoE block:
+  its gate module (router hooks still fire) and, with every expert resident
+  and no hooks on the block, the experts up to the combine, which is fused
+  with the residual add and the next norm (``sf_moe_combine_add_rmsnorm``);
+  otherwise the block module itself.
 
 Hooks that the runtime relies on are honoured by hand: forward pre-hooks of
 ``self_attn`` (the prefetch scheduler's attention hook) run before each
@@ -33,6 +36,8 @@ import torch.nn.functional as F
 from .. import _native as N
 from .. import ops
 from .kv_cache import ReservedLayer
+from .moe_block import Qwen3B200SparseMoeBlock
+from .qwen3_offloaded_experts import Qwen3OffloadedExperts
 from .tree_attention import _causal_bits, _packed_bits
 
 
@@ -63,6 +68,20 @@ class LeanQwen3Forward:
                                      self.eps, x.shape[0], self.H, out.data_ptr(), stream),
                 "sf_add_rmsnorm")
         ops._launched(1)
+
+    @staticmethod
+    def _moe_sorted(mlp, hn):
+        """The MoE block up to its combine when the block and its experts
+        carry no hooks and every expert is resident: (ys, dispatch, ids),
+        else None.  The gate is still called as a module (its hooks fire)."""
+        experts = getattr(mlp, "experts", None)
+        if (not isinstance(mlp, Qwen3B200SparseMoeBlock) or not isinstance(experts, Qwen3OffloadedExperts)
+                or mlp._forward_hooks or mlp._forward_pre_hooks or experts._forward_hooks
+                or experts._forward_pre_hooks):
+            return None
+        _, weights, idx = mlp.gate(hn)
+        out = experts.forward_sorted(hn, idx, weights)
+        return None if out is None else (out[0], out[1], idx)
 
     @torch.no_grad()
     def __call__(self, input_ids, attention_mask=None, position_ids=None, past_key_values=None,
@@ -135,9 +154,15 @@ class LeanQwen3Forward:
                                    prefix, scale=self.D ** -0.5, out=attn[b])
             o = ops.linear(attn.view(Nt, self.hq * self.D), L.wo)
             self._norm(o, res, res, L.ln_post, hn, stream)
-            moe = layer.mlp(hn.view(B, T, self.H)).reshape(Nt, self.H)
             nxt = self.layers[li + 1].ln_in if li + 1 < len(self.layers) else self.final
-            self._norm(moe, res, res, nxt, hn, stream)
+            sorted_out = self._moe_sorted(layer.mlp, hn)
+            if sorted_out is not None:  # combine + residual add + next norm in one launch
+                ys, d, idx = sorted_out
+                ops.moe_combine_add_rmsnorm(ys, d, idx, res, nxt, self.eps, out=hn)
+                layer.mlp.experts.cache.note_device_hits(d.num_active)
+            else:
+                moe = layer.mlp(hn.view(B, T, self.H)).reshape(Nt, self.H)
+                self._norm(moe, res, res, nxt, hn, stream)
             if layer._forward_hooks:
                 out = res.view(B, T, self.H).clone()
                 for hook in tuple(layer._forward_hooks.values()):

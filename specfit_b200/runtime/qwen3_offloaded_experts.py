@@ -108,6 +108,27 @@ class Qwen3OffloadedExperts(nn.Module):
             return out
         return self._forward_waves(h, top_k_index, d, xs, ws, storage, execution_order)
 
+    def forward_sorted(self, hidden_states: torch.Tensor, top_k_index: torch.Tensor,
+                       top_k_weights: torch.Tensor):
+        """The resident fast path of ``forward`` up to, not including, the
+        combine: returns ``(ys, d)`` (weighted expert rows in sorted order and
+        the dispatch) for a caller that fuses the combine with what follows,
+        or ``None`` when that path does not apply (a prediction scheduler, an
+        empty input, experts not all resident)."""
+        self._validate_inputs(hidden_states, top_k_index, top_k_weights)
+        if self._prediction_scheduler is not None or hidden_states.shape[0] == 0 or self.num_experts == 0:
+            return None
+        fixed = self.cache.device_slot_table(self._keys)
+        if fixed is None:
+            return None
+        h = hidden_states.contiguous()
+        d = ops.moe_dispatch(top_k_index, self.num_experts)
+        xs, ws = ops.moe_gather(h, top_k_weights, d)
+        storage = self.cache.storage.view(self.cache.slot_count, -1)
+        ys = ops.grouped_swiglu(xs, ws, d, fixed, storage, self.hidden_size, self.intermediate_size,
+                                impl=self.swiglu_impl)
+        return ys, d
+
     def _forward_waves(self, h, top_k_index, d, xs, ws, storage, execution_order):
         dev = h.device
         host = torch.cat((d.num_active, d.error, d.active)).cpu()  # the one host sync

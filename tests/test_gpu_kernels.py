@@ -380,6 +380,32 @@ def test_logsoftmax_topk_ties_and_shapes(ops):
     assert torch.equal(a[1], b[1]) and torch.allclose(a[0], b[0], atol=1e-6, rtol=0)
 
 
+# ------------------------------------ combine + residual + RMSNorm (fused)
+
+
+@pytest.mark.parametrize("tokens,H", [(1, 2048), (6, 2048), (13, 256), (5, 4096)])
+def test_combine_add_rmsnorm_equals_the_two_steps(ops, tokens, H):
+    """sf_moe_combine_add_rmsnorm == sf_moe_combine then sf_add_rmsnorm,
+    bit for bit (residual and normed output)."""
+    from specfit_b200 import _native
+
+    g = torch.Generator(device="cuda").manual_seed(tokens * 31 + H)
+    E, K = 16, 4
+    idx = torch.stack([torch.randperm(E, generator=g, device=DEV)[:K] for _ in range(tokens)])
+    d = ops.moe_dispatch(idx, E)
+    ys = torch.randn(tokens * K, H, generator=g, device=DEV).to(torch.bfloat16)
+    res = torch.randn(tokens, H, generator=g, device=DEV).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
+    moe = ops.moe_combine(ys, d, idx)
+    res_a, out_a = res.clone(), torch.empty_like(res)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert _native.lib.sf_add_rmsnorm(moe.data_ptr(), res_a.data_ptr(), res_a.data_ptr(), w.data_ptr(),
+                                      1e-6, tokens, H, out_a.data_ptr(), stream) == 0
+    res_b, out_b = res.clone(), torch.empty_like(res)
+    ops.moe_combine_add_rmsnorm(ys, d, idx, res_b, w, 1e-6, out=out_b)
+    assert torch.equal(res_a, res_b) and torch.equal(out_a, out_b)
+
+
 # ------------------------------------------- projection GEMM (sf_linear_bf16)
 
 
