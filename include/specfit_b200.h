@@ -142,6 +142,13 @@ SF_API int sf_router_topk_noalloc(const void* hidden, const void* router_weight,
 SF_API int sf_moe_dispatch(const int64_t* topk_index, int64_t tokens, int top_k, int num_experts,
                     int32_t* counts, int32_t* offsets, int32_t* sorted_pos, int32_t* inv_pos,
                     int32_t* active, int32_t* num_active, int32_t* error_flag, void* stream);
+/* sf_moe_dispatch that also adds num_active to *active_total (device int64,
+ * optional: NULL skips it) -- a running count of expert hits kept on the
+ * device without a separate launch. */
+SF_API int sf_moe_dispatch_ex(const int64_t* topk_index, int64_t tokens, int top_k, int num_experts,
+                              int32_t* counts, int32_t* offsets, int32_t* sorted_pos,
+                              int32_t* inv_pos, int32_t* active, int32_t* num_active,
+                              int32_t* error_flag, int64_t* active_total, void* stream);
 
 /*
  * Gather: hidden_sorted[i,:] = hidden[sorted_pos[i] / K, :] and

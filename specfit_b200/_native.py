@@ -66,6 +66,7 @@ SIGNATURES = {
     "sf_router_topk_noalloc": (_i32, [_vp, _vp, _i32, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
                                       _vp, _vp]),
     "sf_moe_dispatch": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sf_moe_dispatch_ex": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sf_moe_gather": (_i32, [_vp, _i32, _i64, _i32, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
     "sf_grouped_swiglu": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
                                  _i32, _i64, _vp, _vp, _vp]),

@@ -19,6 +19,10 @@ namespace {
 struct RouteIds {
   static constexpr bool kResetError = true;  // sf_moe_dispatch sets *error_flag to 0 or 1
   const int64_t* idx;
+  unsigned long long* active_total;  // optional: += the number of active experts
+  __device__ __forceinline__ void on_done(int num_active) const {
+    if (active_total) atomicAdd(active_total, (unsigned long long)num_active);
+  }
   __device__ __forceinline__ int size() const { return 0; }  // the count is passed explicitly
   __device__ __forceinline__ int operator()(int p) const {
     const int64_t e = idx[p];
@@ -81,6 +85,15 @@ extern "C" int sf_moe_dispatch(const int64_t* topk_index, int64_t tokens, int to
                                int num_experts, int32_t* counts, int32_t* offsets,
                                int32_t* sorted_pos, int32_t* inv_pos, int32_t* active,
                                int32_t* num_active, int32_t* error_flag, void* stream) {
+  return sf_moe_dispatch_ex(topk_index, tokens, top_k, num_experts, counts, offsets, sorted_pos,
+                            inv_pos, active, num_active, error_flag, nullptr, stream);
+}
+
+extern "C" int sf_moe_dispatch_ex(const int64_t* topk_index, int64_t tokens, int top_k,
+                                  int num_experts, int32_t* counts, int32_t* offsets,
+                                  int32_t* sorted_pos, int32_t* inv_pos, int32_t* active,
+                                  int32_t* num_active, int32_t* error_flag,
+                                  int64_t* active_total, void* stream) {
   using namespace sf;
   SF_CHECK_ARG(tokens >= 0 && top_k > 0, "tokens must be >= 0 and top_k > 0");
   SF_CHECK_ARG(num_experts > 0 && num_experts <= grouping::kThreads,
@@ -95,8 +108,9 @@ extern "C" int sf_moe_dispatch(const int64_t* topk_index, int64_t tokens, int to
     SF_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
   SF_CHECK_CUDA(launch_pdl(kernel, dim3(1), dim3(grouping::kThreads), smem, as_stream(stream),
-                           RouteIds{topk_index}, n, num_experts, false, counts, offsets, sorted_pos,
-                           inv_pos, active, num_active, error_flag, nullptr));
+                           RouteIds{topk_index, reinterpret_cast<unsigned long long*>(active_total)},
+                           n, num_experts, false, counts, offsets, sorted_pos, inv_pos, active,
+                           num_active, error_flag, nullptr));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

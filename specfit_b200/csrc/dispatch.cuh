@@ -132,6 +132,7 @@ group_kernel(Src src, int n, int E, bool pad_ok, int32_t* __restrict__ counts,
   if (threadIdx.x == 0) {
     offsets[E] = total_routes;
     *num_active = total_active;
+    src.on_done(total_active);
   }
   for (int i = total_active + threadIdx.x; i < E; i += kThreads) active[i] = -1;
   for (int i = total_routes + threadIdx.x; i < n; i += kThreads) sorted_pos[i] = -1;

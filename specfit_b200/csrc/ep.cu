@@ -51,6 +51,7 @@ __global__ void copy_rows_kernel(const uint8_t* __restrict__ src, int64_t src_pi
 // Expert id of received route position p = pair * K + slot.
 struct RecvIds {
   static constexpr bool kResetError = false;  // the caller zeroes *error_flag
+  __device__ __forceinline__ void on_done(int) const {}
   const uint8_t* rows;
   int64_t row_bytes, meta_off;
   int K;

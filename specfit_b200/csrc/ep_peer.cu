@@ -160,6 +160,7 @@ __global__ void peer_wait_kernel(const unsigned long long* __restrict__ counter,
 // Received slot p = pair * K + slot over the sources' blocks in rank order.
 struct PeerRecvIds {
   static constexpr bool kResetError = false;  // the caller zeroes *error_flag
+  __device__ __forceinline__ void on_done(int) const {}
   const uint8_t* rows;
   const int32_t* counts;
   int64_t cap, row_bytes, meta_off;

@@ -103,7 +103,11 @@ class Dispatch:
     num_experts: int
 
 
-def moe_dispatch(top_k_index: torch.Tensor, num_experts: int) -> Dispatch:
+def moe_dispatch(top_k_index: torch.Tensor, num_experts: int,
+                 active_total: torch.Tensor | None = None) -> Dispatch:
+    """Stable grouping of the routes by expert; with ``active_total`` (a
+    device int64 scalar) the launch also adds the number of active experts
+    to it."""
     dev = _require_cuda(top_k_index)
     if top_k_index.dtype != torch.int64 or top_k_index.ndim != 2:
         raise ValueError("top_k_index must be int64 [tokens, top_k]")
@@ -121,10 +125,10 @@ def moe_dispatch(top_k_index: torch.Tensor, num_experts: int) -> Dispatch:
     num_active = buf[3 * num_experts + 1 + 2 * n: 3 * num_experts + 2 + 2 * n]
     error = buf[3 * num_experts + 2 + 2 * n:]  # set to 0 / 1 by the kernel
     N.check(
-        N.lib.sf_moe_dispatch(idx.data_ptr(), tokens, top_k, num_experts, counts.data_ptr(),
-                              offsets.data_ptr(), sorted_pos.data_ptr(), inv_pos.data_ptr(),
-                              active.data_ptr(), num_active.data_ptr(), error.data_ptr(),
-                              _stream(dev)),
+        N.lib.sf_moe_dispatch_ex(idx.data_ptr(), tokens, top_k, num_experts, counts.data_ptr(),
+                                 offsets.data_ptr(), sorted_pos.data_ptr(), inv_pos.data_ptr(),
+                                 active.data_ptr(), num_active.data_ptr(), error.data_ptr(),
+                                 _ptr(active_total), _stream(dev)),
         "sf_moe_dispatch",
     )
     _launched(1)

@@ -416,6 +416,14 @@ class GpuExpertCache:
             self._slot_table_cache = (self._state_version, keys, table)
             return table
 
+    def device_hit_counter(self) -> torch.Tensor:
+        """The device int64 scalar that kernels add resident hits to
+        (``ops.moe_dispatch(..., active_total=)``); read on the host only
+        when the statistics are read."""
+        if self._device_hits is None:
+            self._device_hits = torch.zeros((), dtype=torch.int64, device=self.device)
+        return self._device_hits
+
     def note_device_hits(self, count: torch.Tensor) -> None:
         """Adds a device-side count of resident hits (no host sync)."""
         if self._device_hits is None:

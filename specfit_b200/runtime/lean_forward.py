@@ -159,7 +159,6 @@ class LeanQwen3Forward:
             if sorted_out is not None:  # combine + residual add + next norm in one launch
                 ys, d, idx = sorted_out
                 ops.moe_combine_add_rmsnorm(ys, d, idx, res, nxt, self.eps, out=hn)
-                layer.mlp.experts.cache.note_device_hits(d.num_active)
             else:
                 moe = layer.mlp(hn.view(B, T, self.H)).reshape(Nt, self.H)
                 self._norm(moe, res, res, nxt, hn, stream)

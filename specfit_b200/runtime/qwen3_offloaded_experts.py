@@ -122,7 +122,8 @@ class Qwen3OffloadedExperts(nn.Module):
         if fixed is None:
             return None
         h = hidden_states.contiguous()
-        d = ops.moe_dispatch(top_k_index, self.num_experts)
+        # Every active expert is a resident hit: the dispatch launch counts them.
+        d = ops.moe_dispatch(top_k_index, self.num_experts, active_total=self.cache.device_hit_counter())
         xs, ws = ops.moe_gather(h, top_k_weights, d)
         storage = self.cache.storage.view(self.cache.slot_count, -1)
         ys = ops.grouped_swiglu(xs, ws, d, fixed, storage, self.hidden_size, self.intermediate_size,
