@@ -68,13 +68,15 @@ def parse_args(argv=None):
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
-    p.add_argument("--mode", choices=("auto", "verify", "ep", "decode", "block", "graph"), default="auto",
+    p.add_argument("--mode", choices=("auto", "verify", "ep", "decode", "block", "graph", "sweep"),
+                   default="auto",
                    help="auto: verify on one GPU, ep under torchrun with N > 1; verify: BASELINE "
                         "config 2; ep: config 5 (8 requests, experts sharded over the ranks); "
                         "decode: config 4 (end-to-end speculative decoding with a drafter stand-in "
                         "and SpecFit selection); "
                         "block: the MoE verify block alone on one resident layer; graph: only the "
-                        "resident (128-slot) verify pass replayed from a CUDA graph")
+                        "resident (128-slot) verify pass replayed from a CUDA graph; sweep: config 3 "
+                        "(12/24/48/128 slots, cold and warm, Zipf routes, a 128-node tree)")
     p.add_argument("--requests", type=int, default=8, help="--mode ep: concurrent requests in total")
     p.add_argument("--ep-ctx", type=int, default=4096, help="--mode ep: context tokens per request")
     p.add_argument("--decode-ctx", type=int, default=2048, help="--mode decode: context tokens")
@@ -83,6 +85,9 @@ def parse_args(argv=None):
                    help="run the Hugging Face layer forward instead of the lean fused forward")
     p.add_argument("--eager-decode", action="store_true",
                    help="--mode decode: verify passes without CUDA graphs")
+    p.add_argument("--sweep-slots", default="12,24,48,128", help="--mode sweep: slots per layer")
+    p.add_argument("--sweep-nodes", type=int, default=128, help="--mode sweep: tree nodes")
+    p.add_argument("--sweep-depth", type=int, default=8, help="--mode sweep: tree depth")
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
     p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
                    help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
@@ -1171,6 +1176,116 @@ def graph_mode(args):
     loaded.close()
 
 
+def sweep_mode(args):
+    """the expert-cache sweep.  One 48-layer target
+    whose caches are rebuilt at each slot count over one shared pinned host
+    pool; every layer's routes are replaced by seeded per-layer Zipf(1.1)
+    top-8 routes (``synthetic.zipf_routes``) for the 129 verify rows of a
+    128-node tree.  Per slot count: the cold pass (fresh caches), then warm
+    passes (each starting from the state the previous one left), with their
+    CUDA-event times and fills (H2D submissions).  Derived: H2D GB/s of the
+    warm pass, the fill time exposed beyond the resident (128-slot warm) pass,
+    overlap = 1 - exposed / (fill bytes / warm-up fill rate), and the grouped
+    SwiGLU's phase-1 tiles per SM (its occupancy: 148 persistent CTAs)."""
+    from specfit_b200 import synthetic
+    from specfit_b200.runtime import GpuExpertCache
+    from specfit_b200.runtime.qwen3_verifier import (ExpertHostPool, build_random_offloaded_qwen3,
+                                                     qwen3_moe_config)
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = qwen3_moe_config(args.layers)
+    L, E = cfg.num_hidden_layers, cfg.num_experts
+    elems = 3 * cfg.hidden_size * cfg.moe_intermediate_size
+    pool = ExpertHostPool(L, E, elems)
+    pool.fill_random(args.seed, device)
+    loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=E, config=cfg, seed=args.seed,
+                                          pool=pool)
+    nodes = args.sweep_nodes
+    T = 1 + nodes
+    routes = [torch.from_numpy(synthetic.zipf_routes(T, l, seed=args.seed + 3)).to(device) for l in range(L)]
+    layers = loaded.model.model.layers
+    hooks = [layer.mlp.gate.register_forward_hook(
+        lambda mod, a, out, l=l: (out[0], out[1], routes[l]) if out[2].shape[0] == T else None)
+        for l, layer in enumerate(layers)]
+    gen = torch.Generator().manual_seed(1)
+    ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
+    tree = make_tree(nodes, args.sweep_depth, args.branch, seed=2, vocab=cfg.vocab_size)
+    seed_tok = int(torch.randint(0, cfg.vocab_size, (1,), generator=gen))
+    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device,
+                          fwd=make_forward(loaded.model, args.hf_forward))
+
+    def set_slots(slots: int) -> None:
+        torch.cuda.synchronize()
+        new = []
+        for l, layer in enumerate(layers):
+            layer.mlp.experts.cache.close()
+            c = GpuExpertCache(pool.sources(l), slot_count=slots, device=device, adopt_pinned_sources=True)
+            layer.mlp.experts.cache = c
+            new.append(c)
+        loaded.caches = tuple(new)
+        torch.cuda.empty_cache()
+
+    def one_pass():
+        before = loaded.cache_stats()["h2d_submissions"]
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        runner.step_device()
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e), loaded.cache_stats()["h2d_submissions"] - before
+
+    set_slots(E)
+    t0 = time.perf_counter()
+    loaded.warm_all_caches()
+    fill_gbps = pool.nbytes / (time.perf_counter() - t0) / 1e9
+    one_pass()
+    resident_ms = statistics.median(one_pass()[0] for _ in range(max(args.steps, 3)))
+    active = [len(set(r.reshape(-1).tolist())) for r in routes]
+    tiles = statistics.mean(a * (cfg.moe_intermediate_size // 64) for a in active)
+    rows = []
+    with ClockSampler(device.index) as clocks:
+        for slots in [int(x) for x in args.sweep_slots.split(",")]:
+            set_slots(slots)
+            cold_ms, cold_fills = one_pass()
+            warm = [one_pass() for _ in range(max(args.steps, 3))]
+            warm_ms = statistics.median(w[0] for w in warm)
+            warm_fills = warm[-1][1]
+            fill_bytes = warm_fills * EXPERT_BYTES
+            exposed = max(warm_ms - resident_ms, 0.0)
+            busy = fill_bytes / (fill_gbps * 1e9) * 1e3
+            rows.append({"slots": slots, "cold_ms": round(cold_ms, 2), "cold_fills": cold_fills,
+                         "warm_ms": round(warm_ms, 2), "warm_fills": warm_fills,
+                         "warm_h2d_GBps": round(fill_bytes / (warm_ms * 1e-3) / 1e9, 1),
+                         "exposed_fill_ms": round(exposed, 2),
+                         "overlap": round(1.0 - exposed / busy, 3) if busy > 0 else 1.0})
+    for h in hooks:
+        h.remove()
+    head = next((r for r in rows if r["slots"] == args.slots), rows[0])
+    result = {
+        "metric": "verify passes/s (config 3 sweep, warm cache)",
+        "value": round(1e3 / head["warm_ms"], 3), "unit": "passes/s", "n_gpus": 1,
+        "steps": max(args.steps, 3), "warmup": 1, "ms_per_step": head["warm_ms"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init bf16 weights; per-layer Zipf(1.1) top-8 routes replace the router)",
+        "config": {"workload": (f"BASELINE config 3: {L}-layer target, {T} verify rows ({nodes}-node tree), "
+                                f"{args.ctx}-token context, slots {args.sweep_slots}, cold and warm"),
+                   "headline_slots": head["slots"]},
+        "rows": rows,
+        "resident_ms": round(resident_ms, 2),
+        "warm_fill_GBps": round(fill_gbps, 1),
+        "experts_per_layer_mean": round(statistics.mean(active), 1),
+        "swiglu_phase1_tiles_per_sm": round(tiles / num_sms_of(device), 2),
+        "clocks": clocks.summary(),
+    }
+    loaded.close()
+    print(json.dumps(result), flush=True)
+
+
+def num_sms_of(device) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
@@ -1181,6 +1296,8 @@ def main(argv=None):
         graph_mode(args)
     elif args.mode == "decode":
         decode_mode(args)
+    elif args.mode == "sweep":
+        sweep_mode(args)
     elif args.mode == "ep" or (args.mode == "auto" and dist_info()[1] > 1):
         ep_arm(args)
     else:
