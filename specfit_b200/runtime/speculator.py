@@ -72,6 +72,32 @@ class BernoulliAcceptance:
             cur = nxt
 
 
+def verify_input_rows(tree, base: int) -> list:
+    """The verify graph's per-row inputs for ``tree`` at committed length
+    ``base``: (pool row, position, ancestor set over the tree block) of the
+    seed (row 0) and each node -- the positions of
+    ``Eagle3DraftTree.verification_position_ids`` and, as bitsets, the rows
+    of its ``verification_attention_mask`` past the committed columns
+    (src/specfit/runtime/eagle3_types.py:429-473)."""
+    rows = [(0, base, 1)]
+    anc = [1]
+    for i, (raw, par, dep) in enumerate(zip(tree.source_raw_ids, tree.parent_ids, tree.depths), 1):
+        anc.append(anc[par] | (1 << i))
+        rows.append((int(raw), base + int(dep), anc[i]))
+    return rows
+
+
+def visibility_from_ancestors(anc: torch.Tensor, offset: torch.Tensor, cap: int) -> torch.Tensor:
+    """Boolean ``[q, cap]`` visibility over a whole reserved KV buffer: column
+    c is visible to row r when c < offset (committed rows) or when
+    0 <= c - offset < 64 and bit c - offset of ``anc[r]`` is set (graph-
+    capturable torch ops; the bool-mask form of ``sf_tree_mask_words``)."""
+    q = anc.shape[0]
+    rel = torch.arange(cap, device=anc.device) - offset
+    bit = (anc.view(q, 1) >> rel.clamp(0, 63).view(1, cap)) & 1
+    return (rel < 0).view(1, cap) | ((rel < 64).view(1, cap) & bit.bool())
+
+
 @dataclass
 class CycleRecord:
     pool_nodes: int
@@ -215,9 +241,7 @@ class B200TreeSpeculator:
                 out = self.fwd(input_ids=ids, attention_words=w.view(1, q, words),
                                position_ids=pos.view(1, q), past_key_values=cache, use_cache=True)
             else:
-                rel = torch.arange(cap, device=dev) - self._offset
-                bit = (anc.view(q, 1) >> rel.clamp(0, 63).view(1, cap)) & 1
-                vis = (rel < 0).view(1, cap) | ((rel < 64).view(1, cap) & bit.bool())
+                vis = visibility_from_ancestors(anc, self._offset, cap)
                 out = self.fwd(input_ids=ids, attention_mask=vis.view(1, 1, q, cap),
                                position_ids=pos.view(1, q), past_key_values=cache, use_cache=True)
             return ids, out.logits[0].argmax(-1), self._features()
@@ -253,11 +277,8 @@ class B200TreeSpeculator:
         q = 1 + tree.draft_node_count
         g = self._graph(q, cache)
         h = g["vin_host"].numpy()
-        h[0, 0], h[1, 0], h[2, 0] = 0, base, 1
-        anc = [1]
-        for i, (raw, par, dep) in enumerate(zip(tree.source_raw_ids, tree.parent_ids, tree.depths), 1):
-            anc.append(anc[par] | (1 << i))
-            h[0, i], h[1, i], h[2, i] = raw, base + dep, anc[i]
+        for i, (row, pos, anc) in enumerate(verify_input_rows(tree, base)):
+            h[0, i], h[1, i], h[2, i] = row, pos, anc
         g["vin"].copy_(g["vin_host"], non_blocking=True)
         self._offset.fill_(base)
         g["graph"].replay()

@@ -138,3 +138,28 @@ def test_static_mode_writes_at_the_device_offset():
     c.set_static(None)
     c.set_length(10)
     assert c.get_seq_length() == 10 and c.layers[0].keys.shape[-2] == 10
+
+
+def test_verify_inputs_restate_the_tree_rows():
+    """The graph path's [3, q] input block and its device-side visibility
+    rule reproduce Eagle3DraftTree's positions and verification mask."""
+    from specfit_b200.runtime.eagle3_types import Eagle3DraftTree
+    from specfit_b200.runtime.speculator import verify_input_rows, visibility_from_ancestors
+
+    rng = np.random.default_rng(4)
+    for n in (0, 1, 3, 7):
+        parents = tuple(int(rng.integers(0, i + 1)) for i in range(n))
+        depths = []
+        for p in parents:
+            depths.append(1 if p == 0 else depths[p - 1] + 1)
+        tree = Eagle3DraftTree(tuple(range(10, 10 + n)), parents, tuple(depths), (0.5,) * n,
+                               tuple(math.log(0.5) * d for d in depths), tuple(range(5, 5 + n)))
+        base, cap = 37, 37 + 8 + 5
+        rows = verify_input_rows(tree, base)
+        assert [r[0] for r in rows] == [0] + list(range(5, 5 + n))
+        assert [r[1] for r in rows] == tree.verification_position_ids(base_kv_length=base, device="cpu")[0].tolist()
+        anc = torch.tensor([r[2] for r in rows])
+        vis = visibility_from_ancestors(anc, torch.tensor(base), cap)
+        ref = tree.verification_attention_mask(base_kv_length=base, device="cpu")[0, 0]
+        assert torch.equal(vis[:, : base + 1 + n], ref)
+        assert not vis[:, base + 1 + n:].any()
