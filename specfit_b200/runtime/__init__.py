@@ -5,6 +5,7 @@ from .gpu_expert_cache import GpuExpertCache
 from .lease import ExpertCacheStats, ExpertLease, NoEvictableSlotError
 from .moe_block import Qwen3B200SparseMoeBlock, Qwen3B200TopKRouter
 from .qwen3_expert_prefetch import Qwen3ExpertPrefetch
+from .qwen3_loader import load_offloaded_qwen3
 from .qwen3_offloaded_experts import ExpertExecutionPolicy, Qwen3OffloadedExperts, ReductionMode
 from .state import ExpertKey, RuntimeEventKind
 
@@ -14,5 +15,5 @@ __all__ = [
     "NoEvictableSlotError", "PendingTransferSnapshot", "Qwen3B200SparseMoeBlock",
     "Qwen3B200TopKRouter", "Qwen3ExpertPrefetch", "Qwen3OffloadedExperts",
     "RecordingCacheTransitionObserver",
-    "ReductionMode", "RuntimeEventKind",
+    "ReductionMode", "RuntimeEventKind", "load_offloaded_qwen3",
 ]
