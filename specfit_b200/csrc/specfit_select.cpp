@@ -13,7 +13,12 @@
 //
 // Footprints are bitsets of `words` 64-bit words (48 layers x 128 experts =
 // 96 words in the reference), OR-ed incrementally along a depth-first walk,
-// so each subset costs one OR and one or two population counts.
+// so each subset costs one OR and one or two population counts.  A subtree
+// of the walk is skipped only when an upper bound on its best score is
+// strictly below the best found (reward: the r largest remaining
+// probabilities; elapsed: the smallest intercept of a larger size and the
+// current footprint, which only grows), so the winner and its tie order are
+// those of the full enumeration.
 //
 // The reward sum reproduces Python's builtin sum over floats (compensated,
 // Neumaier's variant of Kahan summation, in the order of the ids) because
@@ -87,7 +92,8 @@ struct Search {
     return count < best_count;
   }
 
-  void score(const uint64_t* f, int count) {
+  // Scores the subset in ids[0..count) with footprint f; returns |F|.
+  int score(const uint64_t* f, int count) {
     const int experts = popcount_words(f, words);
     double elapsed = intercept[count] + expert_ns * (double)experts;
     if (missing_ns != 0.0 && resident) elapsed += missing_ns * (double)missing_count(f);
@@ -112,21 +118,57 @@ struct Search {
         for (int i = 0; i < count; ++i) best_ids[i] = ids[i];
       }
     }
+    return experts;
+  }
+
+  // suffix_top[start * (max_nodes + 1) + r]: the sum of the r largest
+  // probabilities among raw ids >= start (an upper bound on what r more
+  // nodes can add to the reward).  min_intercept[c]: the smallest intercept
+  // over sizes c..max_nodes.
+  std::vector<double> suffix_top, min_intercept;
+
+  void prepare_bounds() {
+    const int m = max_nodes;
+    suffix_top.assign((size_t)(n + 2) * (m + 1), 0.0);
+    std::vector<double> top;  // the m largest probabilities of the suffix, descending
+    for (int start = n; start >= 1; --start) {
+      const double p = prob[start];
+      auto it = top.begin();
+      while (it != top.end() && *it >= p) ++it;
+      top.insert(it, p);
+      if ((int)top.size() > m) top.pop_back();
+      double acc = 0.0;
+      for (int r = 1; r <= m; ++r) {
+        if (r <= (int)top.size()) acc += top[r - 1];
+        suffix_top[(size_t)start * (m + 1) + r] = acc;
+      }
+    }
+    min_intercept.assign((size_t)m + 2, INFINITY);
+    for (int c = m; c >= 0; --c) min_intercept[c] = fmin(intercept[c], min_intercept[c + 1]);
   }
 
   // Depth-first over ancestor-closed subsets in increasing raw order; the
-  // subset in ids[0..count) with footprint at stack[count].
-  void visit(int start, uint64_t included, int count) {
-    if (count == max_nodes) return;
+  // subset in ids[0..count) with footprint at stack[count], `experts` bits
+  // and probability sum `psum`.  Extensions are skipped when even the best
+  // r remaining probabilities over the cheapest larger size and the current
+  // footprint score strictly below the best so far (a margin of 1e-9 keeps
+  // every possible tie), so the result is the full enumeration's.
+  void visit(int start, uint64_t included, int count, int experts, double psum) {
+    if (count == max_nodes || start > n) return;
     const uint64_t* f = &stack[(size_t)count * words];
+    const double reward_ub = 1.0 + psum + suffix_top[(size_t)start * (max_nodes + 1) + (max_nodes - count)];
+    double elapsed_lb = min_intercept[count + 1] + expert_ns * (double)experts;
+    if (missing_ns > 0.0 && resident) elapsed_lb += missing_ns * (double)missing_count(f);
+    else if (missing_ns > 0.0) elapsed_lb += missing_ns * (double)experts;
+    if (have && elapsed_lb > 0.0 && reward_ub / elapsed_lb * (1.0 + 1e-9) < best_score) return;
     uint64_t* child = &stack[(size_t)(count + 1) * words];
     for (int raw = start; raw <= n; ++raw) {
       if (!((included >> parents[raw - 1]) & 1ull)) continue;
       const uint64_t* g = footprints + (size_t)raw * words;
       for (int i = 0; i < words; ++i) child[i] = f[i] | g[i];
       ids[count] = raw;
-      score(child, count + 1);
-      visit(raw + 1, included | (1ull << raw), count + 1);
+      const int child_experts = score(child, count + 1);
+      visit(raw + 1, included | (1ull << raw), count + 1, child_experts, psum + prob[raw]);
     }
   }
 };
@@ -165,8 +207,9 @@ extern "C" int sf_specfit_select(int num_nodes, const int32_t* parents, const do
   for (int raw = 1; raw <= num_nodes; ++raw) s.prob[raw] = exp(cum_logp[raw - 1]);
   s.stack.assign((size_t)(max_nodes + 1) * words, 0);
   memcpy(s.stack.data(), footprints, sizeof(uint64_t) * words);  // the seed's routes
-  s.score(s.stack.data(), 0);
-  s.visit(1, 1ull, 0);
+  s.prepare_bounds();
+  const int seed_experts = s.score(s.stack.data(), 0);
+  s.visit(1, 1ull, 0, seed_experts, 0.0);
   *num_selected = s.best_count;
   for (int i = 0; i < s.best_count; ++i) selected[i] = s.best_ids[i];
   if (best_score) *best_score = s.best_score;
