@@ -127,6 +127,24 @@ def test_generic_pools_equal_brute_force(seed, n):
         assert got == brute(parents, cum, routes, model, resident), (seed, n, model)
 
 
+@pytest.mark.parametrize("seed", [11, 12, 13])
+def test_pruned_search_on_decode_like_pools(seed):
+    """Pools of 15 nodes with a B200-fitted-style model (intercepts of a
+    few ms nearly flat in the size, 1.44 us per expert), where the search's
+    bound prunes most subtrees: the result equals the brute force."""
+    rng = np.random.default_rng(seed)
+    n = 15
+    parents = [0, 0, 0] + [int(rng.integers(1, raw)) for raw in range(4, n + 1)]
+    cum = []
+    for raw, p in enumerate(parents, start=1):
+        cum.append((0.0 if p == 0 else cum[p - 1]) + float(np.log(rng.uniform(0.3, 0.99))))
+    routes = np.stack([np.stack([rng.permutation(128)[:8] for _ in range(48)]) for _ in range(n + 1)])
+    fp = sel._footprint_rows(routes)
+    ic = tuple(float(x) for x in 5.4e6 + np.sort(rng.uniform(0, 5e5, 8)))
+    model = sel.SelectionCostModel(ic, ic, 1439.6)
+    assert sel.search(parents, cum, fp, model, None) == brute(parents, cum, routes, model, set())
+
+
 def test_route_validation_errors(golden_dir):
     case = synthetic.selection_case(3, 6)
     pool, atlas, _, _ = objects(case)
