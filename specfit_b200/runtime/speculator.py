@@ -437,11 +437,9 @@ class B200TreeSpeculator:
                         tb = time.perf_counter()
                         tok = arr[:, 0].astype(np.int64)
                         par = arr[:, 1].astype(np.int64) + 1  # raw parent ids (0 = the seed)
-                        cond = np.minimum(arr[:, 2], 0.0)
+                        cond = np.minimum(arr[:, 2], 0.0)     # log-probabilities
                         depth = arr[:, 4].astype(np.int64)
-                        cum = np.empty_like(cond)
-                        for i in range(len(cum)):
-                            cum[i] = cond[i] + (cum[par[i] - 1] if par[i] else 0.0)
+                        cum = arr[:, 3]                       # parent's cum + cond, in fp64
                         ids = sel.search(par, cum, fp[: 1 + len(tok)].view(np.uint64), self.cost_model,
                                          None, max_nodes=max_nodes)
                         tree = tree_from_arrays(tuple(ids), tok, par, depth, cond, cum)
