@@ -17,14 +17,23 @@ the released Qwen3-MoE checkpoints) and the fused per-layer tensors of
 transformers 5 (``...mlp.experts.gate_up_proj [E, 2I, H]``, gate rows first,
 and ``...mlp.experts.down_proj [E, H, I]``).
 
-Not supported here: the reference's packed-v1 checkpoints and their
-registered-mmap backing (``packed_checkpoint_root``); passing one raises
-``ValueError``.
+Packed-v1 checkpoints (``packed_checkpoint_root``; the reference's
+``adapters/qwen3_packed_checkpoint.py``) are read too: ``manifest.json``
+(schema ``specfit.qwen3_packed_checkpoint`` version 1), one safetensors file
+per layer holding the tensor ``experts [E, 3*H*I]`` in the same
+``gate | up | down`` rows, and ``nonexperts.safetensors``.  Their experts are
+either copied into a pinned pool (``pinned_copy``) or, the default as in the
+reference, used in place: each layer file is memory-mapped and the mapped
+tensor registered with ``cudaHostRegister`` (``registered_mmap``), so the
+cache fills DMA straight from the page cache.
 """
 from __future__ import annotations
 
+import hashlib
 import json
 import re
+import struct
+from dataclasses import dataclass
 from pathlib import Path
 
 import torch
@@ -111,6 +120,170 @@ def nonexpert_names(files: dict) -> list:
     return sorted(n for n in files if not is_expert_tensor(n))
 
 
+PACKED_SCHEMA = "specfit.qwen3_packed_checkpoint"
+PACKED_VERSION = 1
+PACKED_LAYOUT = ("gate_proj", "up_proj", "down_proj")
+
+
+class PackedCheckpointError(ValueError):
+    """A packed-v1 checkpoint that does not match its manifest."""
+
+
+@dataclass(frozen=True)
+class PackedCheckpoint:
+    root: Path
+    manifest: dict
+    num_layers: int
+    num_experts: int
+    hidden_size: int
+    moe_intermediate_size: int
+    packed_elements: int
+    layer_files: tuple
+    nonexpert_file: Path
+
+
+def _sha256(path: Path) -> str:
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for block in iter(lambda: f.read(1 << 22), b""):
+            h.update(block)
+    return h.hexdigest()
+
+
+def open_packed_checkpoint(root, *, verify_hashes: bool = False,
+                           source_metadata_root=None) -> PackedCheckpoint:
+    """Read and check a packed-v1 manifest (the checks of the reference's
+    ``PackedQwen3Checkpoint.open``, qwen3_packed_checkpoint.py:156-377, that
+    a loader depends on): schema and version, completeness, the expert
+    layout and dtype, one file per layer in order with the packed shape,
+    file sizes, optionally every file's SHA-256, and optionally that the
+    source ``config.json`` under ``source_metadata_root`` is the one packed."""
+    root = Path(root).resolve()
+    mpath = root / "manifest.json"
+    if not mpath.is_file():
+        raise PackedCheckpointError(f"packed checkpoint manifest is missing: {mpath}")
+    try:
+        manifest = json.loads(mpath.read_text(encoding="utf-8"))
+    except (OSError, json.JSONDecodeError) as error:
+        raise PackedCheckpointError(f"packed checkpoint manifest is unreadable: {mpath}") from error
+    if not isinstance(manifest, dict):
+        raise PackedCheckpointError("packed checkpoint manifest must be an object")
+    if manifest.get("complete") is not True:
+        raise PackedCheckpointError("packed checkpoint manifest must declare complete=true")
+    if manifest.get("schema") != PACKED_SCHEMA:
+        raise PackedCheckpointError("packed checkpoint manifest schema does not match")
+    if manifest.get("schema_version") != PACKED_VERSION:
+        raise PackedCheckpointError("packed checkpoint manifest schema version does not match")
+    try:
+        model = manifest["model"]
+        census = model["census"]
+        L, E = int(census["num_hidden_layers"]), int(census["num_experts"])
+        H, I = int(census["hidden_size"]), int(census["moe_intermediate_size"])
+        packed = int(model["packed_expert_elements"])
+        files = manifest["files"]
+        layers = files["layers"]
+        nonexp = files["nonexperts"]
+    except (KeyError, TypeError, ValueError) as error:
+        raise PackedCheckpointError("packed checkpoint manifest lacks model or file records") from error
+    if tuple(model.get("expert_layout", ())) != PACKED_LAYOUT:
+        raise PackedCheckpointError("packed expert layout must be gate_proj|up_proj|down_proj")
+    if model.get("expert_dtype") != "BF16":
+        raise PackedCheckpointError("only BF16 packed experts are supported")
+    if packed != 3 * H * I:
+        raise PackedCheckpointError("packed expert elements differ from 3 * hidden * intermediate")
+    if len(layers) != L:
+        raise PackedCheckpointError("packed checkpoint must list one file per layer")
+    records = [(r, root / r["filename"]) for r in layers] + [(nonexp, root / nonexp["filename"])]
+    for l, rec in enumerate(layers):
+        if rec.get("layer_id") != l or rec.get("tensor_name") != "experts" or list(rec.get("shape", ())) != [E, packed]:
+            raise PackedCheckpointError(f"layer record {l} does not match the census")
+    for rec, path in records:
+        if not path.is_file():
+            raise PackedCheckpointError(f"packed checkpoint file is missing: {path}")
+        if path.stat().st_size != int(rec["size_bytes"]):
+            raise PackedCheckpointError(f"packed checkpoint file size differs: {path}")
+        if verify_hashes and _sha256(path) != rec["sha256"]:
+            raise PackedCheckpointError(f"packed checkpoint file hash differs: {path}")
+    if source_metadata_root is not None:
+        cfg = Path(source_metadata_root) / "config.json"
+        if cfg.is_file() and _sha256(cfg) != manifest.get("source", {}).get("config_sha256"):
+            raise PackedCheckpointError("source config.json differs from the packed checkpoint's")
+    return PackedCheckpoint(root, manifest, L, E, H, I, packed,
+                            tuple(root / r["filename"] for r in layers), root / nonexp["filename"])
+
+
+def _safetensors_span(path: Path, name: str) -> tuple:
+    """(byte offset, byte length, dtype, shape) of tensor ``name`` in a
+    safetensors file: an 8-byte little-endian header size, a JSON header with
+    each tensor's ``data_offsets`` relative to the data that follows it."""
+    with open(path, "rb") as f:
+        (n,) = struct.unpack("<Q", f.read(8))
+        header = json.loads(f.read(n))
+    if name not in header:
+        raise PackedCheckpointError(f"{path} has no tensor {name!r}")
+    meta = header[name]
+    begin, end = meta["data_offsets"]
+    return 8 + n + begin, end - begin, meta["dtype"], tuple(meta["shape"])
+
+
+def map_packed_layer(path: Path, experts: int, packed: int) -> torch.Tensor:
+    """The ``experts`` tensor of a packed layer file as a bf16 view of a
+    private memory mapping of the file (no copy)."""
+    off, nbytes, dtype, shape = _safetensors_span(path, "experts")
+    with open(path, "rb") as f:
+        (n,) = struct.unpack("<Q", f.read(8))
+        if set(json.loads(f.read(n))) - {"__metadata__"} != {"experts"}:
+            raise PackedCheckpointError(f"packed expert layer must contain only 'experts': {path}")
+    if dtype != "BF16" or shape != (experts, packed) or nbytes != experts * packed * 2:
+        raise PackedCheckpointError(f"{path}: experts tensor is not BF16 [{experts}, {packed}]")
+    size = path.stat().st_size
+    raw = torch.from_file(str(path), shared=False, size=size, dtype=torch.uint8)
+    return raw[off: off + nbytes].view(torch.bfloat16).view(experts, packed)
+
+
+_HOST_REGISTER_READ_ONLY = 0x08  # cudaHostRegisterReadOnly: the mapping is never written
+
+
+class MappedExpertPool:
+    """Expert sources in place in a packed-v1 checkpoint: one memory-mapped
+    ``[E, 3*H*I]`` tensor per layer, each registered read-only with
+    ``cudaHostRegister`` (the reference's ``RegisteredMmapExpertLayer``,
+    runtime/registered_mmap.py:12-97), with the ``sources`` / ``close``
+    interface of ``ExpertHostPool``."""
+
+    def __init__(self, ckpt: PackedCheckpoint, device) -> None:
+        self.layers = [map_packed_layer(p, ckpt.num_experts, ckpt.packed_elements) for p in ckpt.layer_files]
+        self.experts = ckpt.num_experts
+        self.device = torch.device(device)
+        self._registered = []
+        with torch.cuda.device(self.device):
+            for t in self.layers:
+                nbytes = t.numel() * t.element_size()
+                rc = int(torch.cuda.cudart().cudaHostRegister(t.data_ptr(), nbytes, _HOST_REGISTER_READ_ONLY))
+                if rc != 0:
+                    self.close()
+                    raise RuntimeError(f"cudaHostRegister of a packed expert layer failed ({rc})")
+                self._registered.append(t)
+                if not t.is_pinned():
+                    self.close()
+                    raise RuntimeError("a registered packed expert layer is not seen as pinned memory")
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.layers)
+
+    def sources(self, layer: int) -> dict:
+        from .state import ExpertKey
+
+        return {ExpertKey(layer, e): self.layers[layer][e] for e in range(self.experts)}
+
+    def close(self) -> None:
+        with torch.cuda.device(self.device):
+            for t in self._registered:
+                torch.cuda.cudart().cudaHostUnregister(t.data_ptr())
+        self._registered = []
+
+
 def load_offloaded_qwen3(model_root, *, device, slots_per_layer: int, packed_checkpoint_root=None,
                          packed_expert_backing=None, verify_packed_hashes: bool = False,
                          reduction_mode=ReductionMode.CANONICAL,
@@ -134,10 +307,18 @@ def load_offloaded_qwen3(model_root, *, device, slots_per_layer: int, packed_che
         raise ValueError("h2d_prefetch must be a boolean")
     policy = ExpertExecutionPolicy(expert_execution_policy)
     reduction = ReductionMode(reduction_mode)
-    if packed_checkpoint_root is not None or packed_expert_backing not in (None, "pinned_copy"):
-        raise ValueError("packed-v1 checkpoints (registered_mmap backing) are not supported by this loader")
-    del verify_packed_hashes  # meaningful only for packed-v1 checkpoints
+    if packed_expert_backing is None:
+        backing = "registered_mmap" if packed_checkpoint_root is not None else "pinned_copy"
+    else:
+        backing = getattr(packed_expert_backing, "value", packed_expert_backing)
+    if backing not in ("pinned_copy", "registered_mmap"):
+        raise ValueError(f"unknown packed expert backing {packed_expert_backing!r}")
+    if packed_checkpoint_root is None and backing != "pinned_copy":
+        raise ValueError("registered_mmap requires packed_checkpoint_root")
     root = Path(model_root).resolve()
+    packed = (open_packed_checkpoint(packed_checkpoint_root, verify_hashes=verify_packed_hashes,
+                                     source_metadata_root=root)
+              if packed_checkpoint_root is not None else None)
     dev = torch.device(device)
     if dev.type != "cuda":
         raise ValueError("offloaded Qwen3 requires a CUDA device")
@@ -156,13 +337,28 @@ def load_offloaded_qwen3(model_root, *, device, slots_per_layer: int, packed_che
     else:
         cfg._attn_implementation = attn_implementation
 
-    files = checkpoint_files(root)
-    shards = _Shards(files)
     L, E = cfg.num_hidden_layers, cfg.num_experts
     H, I = cfg.hidden_size, cfg.moe_intermediate_size
-    pool = ExpertHostPool(L, E, 3 * H * I, torch.bfloat16)
-    for layer in range(L):
-        read_expert_layer(shards, layer, E, H, I, pool.data[layer])
+    if packed is not None:
+        if (packed.num_layers, packed.num_experts, packed.hidden_size, packed.moe_intermediate_size) != (L, E, H, I):
+            raise PackedCheckpointError("packed checkpoint census differs from config.json")
+        from safetensors import safe_open
+
+        with safe_open(str(packed.nonexpert_file), framework="pt", device="cpu") as f:
+            files = {name: packed.nonexpert_file for name in f.keys()}
+        shards = _Shards(files)
+        if backing == "registered_mmap":
+            pool = MappedExpertPool(packed, dev)
+        else:
+            pool = ExpertHostPool(L, E, 3 * H * I, torch.bfloat16)
+            for layer in range(L):
+                pool.data[layer].copy_(map_packed_layer(packed.layer_files[layer], E, 3 * H * I))
+    else:
+        files = checkpoint_files(root)
+        shards = _Shards(files)
+        pool = ExpertHostPool(L, E, 3 * H * I, torch.bfloat16)
+        for layer in range(L):
+            read_expert_layer(shards, layer, E, H, I, pool.data[layer])
 
     with torch.device("meta"):
         model = Qwen3MoeForCausalLM(cfg)

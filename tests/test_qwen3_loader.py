@@ -69,3 +69,125 @@ def test_per_expert_layout(tmp_path):
         read_expert_layer(shards, layer, E, H, I, out)
         assert torch.equal(out, packed_reference(m, layer))
     assert nonexpert_names(files) == ["model.norm.weight"]
+
+
+# ---- packed-v1 checkpoints (fixture written by the reference's own packer) ----
+import json
+import shutil
+from pathlib import Path
+
+import pytest
+
+from specfit_b200.runtime.qwen3_loader import (PackedCheckpointError, map_packed_layer,
+                                               open_packed_checkpoint)
+
+FIXTURE = Path(__file__).resolve().parent / "golden" / "packed_v1_tiny"
+
+
+def test_packed_fixture_experts_equal_the_source_checkpoint():
+    ck = open_packed_checkpoint(FIXTURE / "packed", verify_hashes=True,
+                                source_metadata_root=FIXTURE / "source")
+    assert (ck.num_layers, ck.num_experts, ck.hidden_size, ck.moe_intermediate_size) == (L, E, H, I)
+    shards = _Shards(checkpoint_files(FIXTURE / "source"))
+    for layer in range(L):
+        want = torch.empty(E, 3 * H * I, dtype=torch.bfloat16)
+        read_expert_layer(shards, layer, E, H, I, want)
+        got = map_packed_layer(ck.layer_files[layer], E, 3 * H * I)
+        assert torch.equal(got, want)
+
+
+def test_packed_fixture_nonexperts_equal_the_source_checkpoint():
+    from safetensors import safe_open
+
+    ck = open_packed_checkpoint(FIXTURE / "packed")
+    src = _Shards(checkpoint_files(FIXTURE / "source"))
+    with safe_open(str(ck.nonexpert_file), framework="pt", device="cpu") as f:
+        names = sorted(f.keys())
+        assert names == nonexpert_names(src.files)
+        for n in names:
+            assert torch.equal(f.get_tensor(n), src.get(n))
+
+
+def _copy_fixture(tmp_path):
+    dst = tmp_path / "packed"
+    shutil.copytree(FIXTURE / "packed", dst)
+    return dst
+
+
+def _edit_manifest(root, fn):
+    m = json.loads((root / "manifest.json").read_text())
+    fn(m)
+    (root / "manifest.json").write_text(json.dumps(m))
+
+
+@pytest.mark.parametrize("edit,match", [
+    (lambda m: m.__setitem__("complete", False), "complete"),
+    (lambda m: m.__setitem__("schema", "other"), "schema"),
+    (lambda m: m.__setitem__("schema_version", 2), "version"),
+    (lambda m: m["model"].__setitem__("expert_layout", ["up_proj", "gate_proj", "down_proj"]), "layout"),
+    (lambda m: m["model"].__setitem__("expert_dtype", "F16"), "BF16"),
+    (lambda m: m["files"]["layers"].pop(), "one file per layer"),
+    (lambda m: m["files"]["layers"][1].__setitem__("shape", [E, 3 * H * I + 8]), "layer record 1"),
+    (lambda m: m["files"]["nonexperts"].__setitem__("size_bytes", 1), "size"),
+])
+def test_packed_manifest_mismatches_are_refused(tmp_path, edit, match):
+    root = _copy_fixture(tmp_path)
+    _edit_manifest(root, edit)
+    with pytest.raises(PackedCheckpointError, match=match):
+        open_packed_checkpoint(root)
+
+
+def test_packed_corruption_found_only_with_hash_verification(tmp_path):
+    root = _copy_fixture(tmp_path)
+    path = root / "experts" / "layer-001.safetensors"
+    raw = bytearray(path.read_bytes())
+    raw[-3] ^= 0x40  # a bit of the last expert's down rows; the size is unchanged
+    path.write_bytes(bytes(raw))
+    open_packed_checkpoint(root)  # sizes still match
+    with pytest.raises(PackedCheckpointError, match="hash"):
+        open_packed_checkpoint(root, verify_hashes=True)
+
+
+def test_packed_source_config_must_match(tmp_path):
+    src = tmp_path / "source"
+    shutil.copytree(FIXTURE / "source", src)
+    cfg = json.loads((src / "config.json").read_text())
+    cfg["rms_norm_eps"] = 1e-5
+    (src / "config.json").write_text(json.dumps(cfg))
+    with pytest.raises(PackedCheckpointError, match="config.json"):
+        open_packed_checkpoint(FIXTURE / "packed", source_metadata_root=src)
+
+
+def test_packed_missing_manifest(tmp_path):
+    with pytest.raises(PackedCheckpointError, match="missing"):
+        open_packed_checkpoint(tmp_path)
+
+
+@pytest.mark.gpu
+def test_gpu_source_and_packed_loads_give_equal_logits():
+    """The same checkpoint loaded from its Hugging Face files, from the packed
+    copy in a pinned pool, and from the packed files mapped and registered in
+    place gives bit-identical logits, with experts filled through the cache."""
+    from transformers import DynamicCache
+
+    from specfit_b200.runtime.qwen3_loader import load_offloaded_qwen3
+
+    dev = torch.device("cuda:0")
+    ctx = torch.randint(0, 100, (1, 12), generator=torch.Generator().manual_seed(3)).to(dev)
+    variants = ({}, {"packed_checkpoint_root": FIXTURE / "packed", "packed_expert_backing": "pinned_copy"},
+                {"packed_checkpoint_root": FIXTURE / "packed", "verify_packed_hashes": True})
+    logits = []
+    for kw in variants:
+        loaded = load_offloaded_qwen3(FIXTURE / "source", device=dev, slots_per_layer=2, **kw)
+        try:
+            with torch.no_grad():
+                cache = DynamicCache(config=loaded.model.config)
+                out = loaded.model(input_ids=ctx, past_key_values=cache, use_cache=True)
+            torch.cuda.synchronize()
+            logits.append(out.logits[0].float().cpu())
+            assert loaded.cache_stats()["h2d_submissions"] > 0
+        finally:
+            loaded.close()
+    assert torch.isfinite(logits[0]).all()
+    assert torch.equal(logits[0], logits[1])
+    assert torch.equal(logits[0], logits[2])
