@@ -72,7 +72,8 @@ def parse_args(argv=None):
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
-    p.add_argument("--mode", choices=("auto", "verify", "ep", "decode", "block", "graph", "sweep"),
+    p.add_argument("--mode", choices=("auto", "verify", "ep", "decode", "block", "graph", "sweep",
+                                      "kernels"),
                    default="auto",
                    help="auto: verify on one GPU, ep under torchrun with N > 1; verify: BASELINE "
                         "config 2; ep: config 5 (8 requests, experts sharded over the ranks); "
@@ -80,7 +81,8 @@ def parse_args(argv=None):
                         "and SpecFit selection); "
                         "block: the MoE verify block alone on one resident layer; graph: only the "
                         "resident (128-slot) verify pass replayed from a CUDA graph; sweep: config 3 "
-                        "(12/24/48/128 slots, cold and warm, Zipf routes, a 128-node tree)")
+                        "(12/24/48/128 slots, cold and warm, Zipf routes, a 128-node tree); kernels: each "
+                        "hot kernel alone at the configurations' sizes, L2 cold and warm")
     p.add_argument("--requests", type=int, default=8, help="--mode ep: concurrent requests in total")
     p.add_argument("--ep-ctx", type=int, default=4096, help="--mode ep: context tokens per request")
     p.add_argument("--decode-ctx", type=int, default=2048, help="--mode decode: context tokens")
@@ -95,6 +97,8 @@ def parse_args(argv=None):
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
     p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
                    help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
+    p.add_argument("--kernel", default="",
+                   help="--mode kernels: comma-separated kernel names to run (default: all)")
     return p.parse_args(argv)
 
 
@@ -1358,6 +1362,125 @@ def sweep_mode(args):
     print(json.dumps(result), flush=True)
 
 
+def kernel_cases(device, only=()):
+    """(name, case, launch, algorithmic bytes) for every hot kernel at the
+    sizes the configurations run it at: 7 rows (a decode verify pass), 65
+    (configuration 2), 512 (configuration 5's step); bf16 inputs drawn on the
+    device; routes Zipf(1.1) (configurations 3 and 5) or uniform."""
+    from specfit_b200 import ops, synthetic
+
+    H, E, K, I = synthetic.HIDDEN, synthetic.NUM_EXPERTS, synthetic.TOP_K, synthetic.MOE_INTER
+    HQ, HKV, D, V = synthetic.NUM_HEADS, synthetic.NUM_KV_HEADS, synthetic.HEAD_DIM, synthetic.VOCAB
+    g = torch.Generator(device=device).manual_seed(11)
+    bf = dict(dtype=torch.bfloat16, device=device)
+
+    def randn(*shape, std=1.0):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+    want = lambda name: not only or name in only
+    cases = []
+    storage = slot = router = None
+    if want("router") or want("grouped_swiglu"):
+        router = randn(E, H, std=0.02)
+    if want("grouped_swiglu"):
+        storage = randn(E, 3 * H * I, std=0.02)
+        slot = torch.arange(E, dtype=torch.int32, device=device)
+    for t in (7, 65, 512):
+        x = randn(t, H)
+        idx = torch.from_numpy(synthetic.zipf_routes(t, layer=0, seed=3)).to(device)
+        w = torch.softmax(torch.randn(t, K, generator=g, device=device), -1)
+        d = ops.moe_dispatch(idx, E)
+        xs, ws = ops.moe_gather(x, w, d)
+        if want("router"):
+            cases.append(("router", f"T={t}", lambda x=x: ops.router_topk(x, router, K, True),
+                          t * H * 2 + E * H * 2 + t * E * 4 + t * K * 12))
+        if want("dispatch"):
+            cases.append(("dispatch", f"T={t} zipf", lambda idx=idx: ops.moe_dispatch(idx, E),
+                          t * K * 8 + 2 * t * K * 4 + 3 * E * 4))
+        if want("gather"):
+            cases.append(("gather", f"T={t}", lambda x=x, w=w, d=d: ops.moe_gather(x, w, d),
+                          t * H * 2 + t * K * 4 + t * K * (H * 2 + 4)))
+        if want("combine"):
+            ys = randn(t * K, H)
+            cases.append(("combine", f"T={t}", lambda ys=ys, d=d, idx=idx: ops.moe_combine(ys, d, idx),
+                          t * K * H * 2 + t * H * 2 + t * K * 12))
+        if want("grouped_swiglu"):
+            for kind in ("zipf", "uniform"):
+                if kind == "uniform":
+                    rng = np.random.default_rng(t)
+                    uidx = torch.from_numpy(np.stack([rng.permutation(E)[:K] for _ in range(t)])).to(device)
+                    ud = ops.moe_dispatch(uidx, E)
+                    uxs, uws = ops.moe_gather(x, w, ud)
+                else:
+                    ud, uxs, uws = d, xs, ws
+                torch.cuda.synchronize(device)
+                n_act = int(ud.num_active.item())
+                cases.append(("grouped_swiglu", f"T={t} {kind} ({n_act} experts)",
+                              lambda a=uxs, b=uws, c=ud: ops.grouped_swiglu(a, b, c, slot, storage, H, I),
+                              n_act * EXPERT_BYTES + t * K * (H * 2 * 2 + 4)))
+    if want("tree_attention"):
+        for t, ctx in ((7, 2048), (65, 512), (65, 4096)):
+            q = randn(HQ, t, D)
+            kv = randn(2, HKV, ctx + t, D)
+            bits = ops.tree_bits_from_parents([max(0, i - 2) for i in range(1, t)], device)
+            cases.append(("tree_attention", f"T={t} ctx={ctx}",
+                          lambda q=q, kv=kv, bits=bits, ctx=ctx: ops.tree_attention(q, kv[0], kv[1], bits, ctx),
+                          (ctx + t) * HKV * D * 2 * 2 + 2 * t * HQ * D * 2))
+    if want("logsoftmax_topk"):
+        for rows in (1, 8):
+            logits = randn(rows, V)
+            cases.append(("logsoftmax_topk", f"rows={rows} vocab={V}",
+                          lambda logits=logits: ops.logsoftmax_topk(logits, 8, 4.5), rows * V * 2))
+    if want("linear"):
+        for rows, n_in, n_out in ((7, HQ * D, H), (8, 3 * H, H)):
+            xw = randn(rows, n_in)
+            wt = randn(n_out, n_in, std=0.02)
+            cases.append(("linear", f"rows={rows} {n_in}->{n_out}",
+                          lambda xw=xw, wt=wt: ops.linear(xw, wt), n_out * n_in * 2 + rows * (n_in + n_out) * 2))
+    return cases
+
+
+def kernels_mode(args):
+    """Each hot kernel alone (``kernel_cases``): per launch, CUDA events
+    around it with L2 flushed before it (a 256 MB write outside the events:
+    "cold"), and the mean of back-to-back launches ("warm", the in-pass case
+    where the producer's output is still in L2).  One JSON line per case:
+    us, algorithmic bytes, GB/s and the fraction of the measured HBM copy
+    peak (cold).  Small enough to run whole under a profiler with -k/-c."""
+    device = torch.device("cuda", 0)
+    peaks = measured_peaks()
+    only = tuple(k for k in args.kernel.split(",") if k)
+    cases = kernel_cases(device, only)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    iters = max(args.steps, 3)
+    for name, case, fn, algo in cases:
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        pairs = []
+        for r in range(iters):
+            flush.fill_(r & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            pairs.append((a, b))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(iters):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        cold = statistics.median(x.elapsed_time(y) * 1e3 for x, y in pairs)
+        warm = a.elapsed_time(b) * 1e3 / iters
+        print(json.dumps({"mode": "kernels", "kernel": name, "case": case, "us_cold": round(cold, 2),
+                          "us_warm": round(warm, 2), "algorithmic_bytes": int(algo),
+                          "GBps_cold": round(algo / cold / 1e3, 1),
+                          "frac_of_hbm_peak_cold": round(algo / cold / 1e3 / peaks["hbm_gbs"], 4),
+                          "us_at_peak": round(algo / peaks["hbm_gbs"] / 1e3, 2),
+                          "peak_source": peaks["source"] + " hbm_gbs"}), flush=True)
+
+
 def num_sms_of(device) -> int:
     return torch.cuda.get_device_properties(device).multi_processor_count
 
@@ -1374,6 +1497,8 @@ def main(argv=None):
         decode_mode(args)
     elif args.mode == "sweep":
         sweep_mode(args)
+    elif args.mode == "kernels":
+        kernels_mode(args)
     elif args.mode == "ep" or (args.mode == "auto" and dist_info()[1] > 1):
         ep_arm(args)
     else:
