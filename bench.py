@@ -1367,6 +1367,7 @@ def kernel_cases(device, only=()):
     sizes the configurations run it at: 7 rows (a decode verify pass), 65
     (configuration 2), 512 (configuration 5's step); bf16 inputs drawn on the
     device; routes Zipf(1.1) (configurations 3 and 5) or uniform."""
+    from specfit_b200 import _native as N
     from specfit_b200 import ops, synthetic
 
     H, E, K, I = synthetic.HIDDEN, synthetic.NUM_EXPERTS, synthetic.TOP_K, synthetic.MOE_INTER
@@ -1418,13 +1419,17 @@ def kernel_cases(device, only=()):
                 cases.append(("grouped_swiglu", f"T={t} {kind} ({n_act} experts)",
                               lambda a=uxs, b=uws, c=ud: ops.grouped_swiglu(a, b, c, slot, storage, H, I),
                               n_act * EXPERT_BYTES + t * K * (H * 2 * 2 + 4)))
-    if want("tree_attention"):
+    # tree_attention_tc (the tcgen05 kernel) runs only when named explicitly.
+    for name, impl in (("tree_attention", N.SF_ATTN_AUTO), ("tree_attention_tc", N.SF_ATTN_TCGEN05)):
+        if (name == "tree_attention" and not want(name)) or (name == "tree_attention_tc" and name not in only):
+            continue
         for t, ctx in ((7, 2048), (65, 512), (65, 4096)):
             q = randn(HQ, t, D)
             kv = randn(2, HKV, ctx + t, D)
             bits = ops.tree_bits_from_parents([max(0, i - 2) for i in range(1, t)], device)
-            cases.append(("tree_attention", f"T={t} ctx={ctx}",
-                          lambda q=q, kv=kv, bits=bits, ctx=ctx: ops.tree_attention(q, kv[0], kv[1], bits, ctx),
+            cases.append((name, f"T={t} ctx={ctx}",
+                          lambda q=q, kv=kv, bits=bits, ctx=ctx, impl=impl:
+                          ops.tree_attention(q, kv[0], kv[1], bits, ctx, impl=impl),
                           (ctx + t) * HKV * D * 2 * 2 + 2 * t * HQ * D * 2))
     if want("logsoftmax_topk"):
         for rows in (1, 8):

@@ -77,10 +77,10 @@ SF_API int sf_abi_version(void);
 
 /*
  * Sticky device-side status of the current device: 0, or the code of the first
- * barrier wait of the tcgen05 grouped SwiGLU kernel that gave up after its
- * one-second limit (site codes 1..6); that kernel then skipped its remaining
- * work and returned.  Synchronous: reads (and with reset != 0
- * clears) the words.
+ * barrier wait of a tcgen05 kernel (grouped SwiGLU, projection GEMM, tree
+ * attention) that gave up after its one-second limit (each kernel's site
+ * codes); that kernel then skipped its remaining work and returned.
+ * Synchronous: reads (and with reset != 0 clears) the words.
  * No reference counterpart; the reference's GPU work is PyTorch library calls.
  */
 SF_API int sf_device_status(int* status, int reset);
@@ -223,6 +223,7 @@ SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const si
 #define SF_ATTN_AUTO 0 /* tensor-core kernel when supported (D=128, q rows 4-byte and K/V rows 16-byte aligned), else CUDA cores */
 #define SF_ATTN_SIMT 1 /* CUDA-core split kernel */
 #define SF_ATTN_MMA 2  /* warp-level tensor-core (mma.sync) split kernel; SF_ERR_INVALID_ARGUMENT if unsupported */
+#define SF_ATTN_TCGEN05 3 /* tcgen05/TMEM kernel, K/V by TMA (D=128, 16-byte aligned q/k/v rows); SF_ERR_INVALID_ARGUMENT if unsupported */
 
 SF_API size_t sf_tree_attention_workspace_bytes(int num_heads, int64_t q_len, int64_t kv_len);
 SF_API int sf_tree_attention(const void* q, const void* k, const void* v, const uint32_t* tree_bits,

@@ -34,6 +34,7 @@ SF_SWIGLU_TCGEN05 = 2
 SF_ATTN_AUTO = 0
 SF_ATTN_SIMT = 1
 SF_ATTN_MMA = 2
+SF_ATTN_TCGEN05 = 3
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int

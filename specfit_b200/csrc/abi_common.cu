@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "swiglu.h"
+#include "tree_attn.h"
 
 namespace sf {
 
@@ -43,9 +44,10 @@ extern "C" int sf_abi_version(void) { return 1; }
 extern "C" int sf_device_status(int* status, int reset) {
   using namespace sf;
   SF_CHECK_ARG(status, "null pointer argument");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   if (int rc = swiglu_status(&a, reset)) return rc;
   if (int rc = dense_status(&b, reset)) return rc;
-  *status = a ? a : b;
+  if (int rc = tree_attention_tc_status(&c, reset)) return rc;
+  *status = a ? a : (b ? b : c);
   return SF_OK;
 }

@@ -174,6 +174,27 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major tile (the MN dimension
+// contiguous) written by TMA with 128-byte swizzling, as the B operand of an
+// MMA whose N spans several 64-element (128-byte) column regions: each key
+// (K) row is 128 B, 8-row atoms are 1024 B apart (SBO), and the next
+// 64-element region of N starts `region_bytes` later (LBO).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t smem_addr, uint32_t region_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);           // start address
+  d |= (uint64_t)((region_bytes >> 4) & 0x3FFFu) << 16;  // LBO: next 64 elements of N
+  d |= (uint64_t)(1024u >> 4) << 32;                      // SBO: next 8 rows of K
+  d |= (uint64_t)1u << 46;                                // version = 1
+  d |= (uint64_t)2u << 61;                                // SWIZZLE_128B
+  return d;
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (tcgen05.mma operands written by threads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Instruction descriptor, kind::f16: bf16 A and B (K-major), fp32 D.
 __device__ __forceinline__ uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
   return (1u << 4)            // D format: f32
@@ -182,6 +203,9 @@ __device__ __forceinline__ uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
          | ((n >> 3) << 17)   // N / 8
          | ((m >> 4) << 24);  // M / 16
 }
+
+// Bit 16 of the kind::f16 instruction descriptor: B is MN-major.
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -313,8 +313,20 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
   p.part_ml = p.part_o + (size_t)p.splits * num_heads * q_len * kD;
   cudaStream_t s = as_stream(stream);
   const int64_t pairs = (int64_t)num_heads * q_len;
-  SF_CHECK_ARG(impl == SF_ATTN_AUTO || impl == SF_ATTN_SIMT || impl == SF_ATTN_MMA,
+  SF_CHECK_ARG(impl == SF_ATTN_AUTO || impl == SF_ATTN_SIMT || impl == SF_ATTN_MMA ||
+                   impl == SF_ATTN_TCGEN05,
                "unknown attention implementation %d", impl);
+  if (impl == SF_ATTN_TCGEN05) {
+    SF_CHECK_ARG(tree_attention_tc_supports(p, head_dim),
+                 "the tcgen05 tree attention needs D=128 and 16-byte aligned q/k/v rows");
+    bool merged = false;
+    if (int rc = tree_attention_tc(p, out, &merged, s)) return rc;
+    if (merged) return SF_OK;
+    SF_CHECK_CUDA(launch_pdl(tree_attn_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256),
+                             0, s, p, static_cast<__nv_bfloat16*>(out)));
+    SF_CHECK_LAUNCH();
+    return SF_OK;
+  }
   if (impl != SF_ATTN_SIMT && tree_attention_mma_supports(p, head_dim)) {
     bool merged = false;
     if (int rc = tree_attention_mma(p, out, &merged, s)) return rc;

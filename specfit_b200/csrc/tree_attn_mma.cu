@@ -65,28 +65,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Visibility of keys prefix_len + j0 + i, i in [0, 64), as bit i: keys before
-// the tree block (j < 0) are visible; bits past the mask's words are 0.
-__device__ __forceinline__ uint64_t mask_window(const uint32_t* __restrict__ bits, int words,
-                                                int j0) {
-  if (j0 + 64 <= 0) return ~0ull;
-  if (j0 >= 0) {
-    const int w = j0 >> 5, sh = j0 & 31;
-    const uint64_t lo = w < words ? bits[w] : 0u;
-    const uint64_t mid = w + 1 < words ? bits[w + 1] : 0u;
-    uint64_t x = lo | (mid << 32);
-    if (sh) {
-      const uint64_t hi = w + 2 < words ? bits[w + 2] : 0u;
-      x = (x >> sh) | (hi << (64 - sh));
-    }
-    return x;
-  }
-  const int d = -j0;  // 1..63 keys of the block precede the tree
-  const uint64_t x = (uint64_t)(words > 0 ? bits[0] : 0u) |
-                     ((uint64_t)(words > 1 ? bits[1] : 0u) << 32);
-  return (x << d) | ((1ull << d) - 1);
-}
-
 // Stages keys [b0, b0 + 64) of one KV head into one K/V buffer pair with
 // cp.async (one commit group); rows at or past key_hi are zero-filled.
 __device__ __forceinline__ void stage_block(__nv_bfloat16* ks, __nv_bfloat16* vs,
@@ -194,7 +172,7 @@ tree_attn_mma_kernel(AttnParams p, __nv_bfloat16* __restrict__ out) {
     uint64_t win[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h)
-      win[h] = rbits[h] ? mask_window(rbits[h], p.bit_words, b0 - p.prefix_len)
+      win[h] = rbits[h] ? tree_mask_window(rbits[h], p.bit_words, b0 - p.prefix_len)
                         : (b0 + kKeys <= p.prefix_len ? ~0ull
                                                       : (b0 >= p.prefix_len ? 0ull
                                                                             : (1ull << (p.prefix_len - b0)) - 1));

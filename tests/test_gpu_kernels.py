@@ -1,6 +1,8 @@
 """Kernel parity on the GPU: each native kernel against the CPU oracle and the
 reference-generated golden fixtures.  Integer outputs must match bit for bit;
 floating-point outputs within the stated tolerances."""
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -15,6 +17,11 @@ DEV = "cuda:0"
 # bf16 tolerance of the verification path (max abs error, cosine).
 ATOL_BF16 = 2e-2
 COS_MIN = 0.999
+# Kernels written after this build's last GPU run: their parity cases run
+# with SF_TEST_NEW_KERNELS=1 until they have passed on a B200 once.
+NEW_KERNEL = pytest.mark.skipif(os.environ.get("SF_TEST_NEW_KERNELS") != "1",
+                                reason="not yet run on a B200 (set SF_TEST_NEW_KERNELS=1)")
+ATTN_TCGEN05 = pytest.param(3, marks=NEW_KERNEL, id="tcgen05")
 
 
 @pytest.fixture(scope="module")
@@ -278,9 +285,9 @@ def test_combine_bit_exact_sequential(ops):
 # --------------------------------------------------------- K6 tree attention
 
 
-@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("impl", [1, 2, ATTN_TCGEN05])
 @pytest.mark.parametrize("nodes,depth,ctx", [(4, 2, 2), (64, 6, 512), (128, 8, 300), (60, 8, 2048), (0, 0, 33),
-                                             (200, 9, 700)])
+                                             (200, 9, 700), (64, 6, 4096)])
 def test_tree_attention_vs_oracle(ops, nodes, depth, ctx, impl):
     if nodes:
         _, parents, _ = synthetic.random_tree(nodes, max_depth=depth, max_branch=4, seed=nodes)
@@ -304,7 +311,7 @@ def test_tree_attention_vs_oracle(ops, nodes, depth, ctx, impl):
     assert torch.equal(packed, bits)
 
 
-@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("impl", [1, 2, ATTN_TCGEN05])
 def test_tree_attention_strided_views(ops, impl):
     """Inputs as HF lays them out: q from a [1, T, Hq*D] projection viewed as
     [Hq, T, D] (non-contiguous), K/V cache [Hkv, Tk, D]."""
@@ -340,6 +347,32 @@ def test_tree_attention_full_mask_and_long_context(ops):
                             v[:1].float().cpu().numpy(), mask.numpy())
     got = a.transpose(1, 0, 2)[sub]
     assert np.abs(got - ref).max() <= ATOL_BF16 and cosine(got, ref) >= COS_MIN
+
+
+@NEW_KERNEL
+def test_tcgen05_tree_attention_full_mask_long_context(ops):
+    """The tcgen05 kernel on an arbitrary packed mask over 4,161 keys (many
+    splits, merged) and with one split (direct write), against the
+    warp-level tensor-core kernel and the fp64 oracle."""
+    gen = torch.Generator().manual_seed(8)
+    for tq, tk in ((65, 4161), (65, 100), (7, 2055)):
+        q = torch.randn(32, tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
+        k = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16).to(DEV)
+        v = torch.randn(4, tk, 128, generator=gen).to(torch.bfloat16).to(DEV)
+        mask = torch.rand(tq, tk, generator=gen) < 0.3
+        mask[:, 0] = True
+        bits = ops.tree_bits_from_mask(mask.to(DEV), 0)
+        a = ops.tree_attention(q, k, v, bits, 0, impl=3).float().cpu().numpy()
+        b = ops.tree_attention(q, k, v, bits, 0, impl=2).float().cpu().numpy()
+        assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= COS_MIN
+        sub = slice(8, 16)  # the 8 query heads of KV head 1 against the fp64 oracle
+        ref = to.tree_attention(q[sub].float().cpu().numpy(), k[1:2].float().cpu().numpy(),
+                                v[1:2].float().cpu().numpy(), mask.numpy())
+        got = a.transpose(1, 0, 2)[sub]
+        assert np.abs(got - ref).max() <= ATOL_BF16 and cosine(got, ref) >= COS_MIN
+    from specfit_b200 import _native as N
+
+    assert N.device_status(reset=True) == 0  # no barrier wait of the kernel gave up
 
 
 # ------------------------------------------- drafter log-softmax + top-k
