@@ -14,6 +14,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from math import isclose, isfinite, log
 
+import numpy as np
 import torch
 
 
@@ -306,12 +307,15 @@ def tree_from_arrays(selected_raw_ids: tuple, token_ids, parent_raw_ids, depths,
     if any(int(parent_raw_ids[r - 1]) != 0 and int(parent_raw_ids[r - 1]) not in keep for r in chosen):
         raise ValueError("selected candidates must be ancestor-closed")
     node_of = {r: i for i, r in enumerate(chosen, start=1)}
+    rows = [r - 1 for r in chosen]
+    # One gather per field (numpy arrays or sequences), then plain Python values.
+    tok, par, dep, cond, cum = (np.asarray(f)[rows].tolist() for f in (
+        token_ids, parent_raw_ids, depths, conditional_log_probs, cumulative_log_probs))
     return Eagle3DraftTree(
-        token_ids=tuple(int(token_ids[r - 1]) for r in chosen),
-        parent_ids=tuple(0 if int(parent_raw_ids[r - 1]) == 0 else node_of[int(parent_raw_ids[r - 1])]
-                         for r in chosen),
-        depths=tuple(int(depths[r - 1]) for r in chosen),
-        conditional_probabilities=tuple(exp(float(conditional_log_probs[r - 1])) for r in chosen),
-        cumulative_log_probabilities=tuple(float(cumulative_log_probs[r - 1]) for r in chosen),
+        token_ids=tuple(int(t) for t in tok),
+        parent_ids=tuple(0 if int(p) == 0 else node_of[int(p)] for p in par),
+        depths=tuple(int(d) for d in dep),
+        conditional_probabilities=tuple(exp(float(c)) for c in cond),
+        cumulative_log_probabilities=tuple(float(c) for c in cum),
         source_raw_ids=tuple(chosen),
     )

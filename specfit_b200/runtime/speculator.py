@@ -467,7 +467,7 @@ class B200TreeSpeculator:
                                          fp, self.cost_model, None, max_nodes=max_nodes)
                         tree = pool.to_tree(tuple(ids))
                 rows_fp = np.asarray(fp)[[0] + list(tree.source_raw_ids)].view(np.uint64)
-                experts = int(np.unpackbits(np.bitwise_or.reduce(rows_fp, axis=0).view(np.uint8)).sum())
+                experts = int(np.bitwise_count(np.bitwise_or.reduce(rows_fp, axis=0)).sum())
                 tick()
                 tc = time.perf_counter()
                 base = cache.get_seq_length()
