@@ -97,6 +97,8 @@ def parse_args(argv=None):
     p.add_argument("--tokens", type=int, default=65, help="rows per MoE block in --mode block")
     p.add_argument("--routes", choices=("router", "zipf", "uniform"), default="router",
                    help="--mode block: routes from the router, Zipf(1.1) or uniform top-8")
+    p.add_argument("--fused-gather", action="store_true",
+                   help="resident expert path: token rows read inside the grouped SwiGLU (TMA gather4)")
     p.add_argument("--kernel", default="",
                    help="--mode kernels: comma-separated kernel names to run (default: all)")
     return p.parse_args(argv)
@@ -226,6 +228,15 @@ def make_forward(model, hf: bool):
     from specfit_b200.runtime.lean_forward import LeanQwen3Forward
 
     return LeanQwen3Forward(model)
+
+
+def apply_kernel_options(loaded, args) -> None:
+    """``--fused-gather``: every layer's resident expert path reads its token
+    rows inside the grouped SwiGLU (TMA gather4) instead of gathering them
+    first."""
+    if getattr(args, "fused_gather", False):
+        for layer in loaded.model.model.layers:
+            layer.mlp.experts.fused_gather = True
 
 
 class VerifyRunner:
@@ -522,6 +533,7 @@ def b200_arm(args):
     t_build = time.perf_counter()
     loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=args.slots, config=cfg,
                                           seed=args.seed, pool=pool)
+    apply_kernel_options(loaded, args)
     gen = torch.Generator().manual_seed(1)
     ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
     tree = make_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
@@ -1028,6 +1040,7 @@ def decode_mode(args):
     t0 = time.perf_counter()
     loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=cfg.num_experts, config=cfg,
                                           seed=args.seed)
+    apply_kernel_options(loaded, args)
     loaded.warm_all_caches()
     L = cfg.num_hidden_layers
     aux = (1, 23, 44) if L == 48 else tuple(sorted({1 % L, (L * 23) // 48, (L * 44) // 48}))
@@ -1241,6 +1254,7 @@ def graph_mode(args):
     cfg = qwen3_moe_config(args.layers)
     loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=cfg.num_experts, config=cfg,
                                           seed=args.seed)
+    apply_kernel_options(loaded, args)
     loaded.warm_all_caches()
     gen = torch.Generator().manual_seed(1)
     ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
@@ -1281,6 +1295,7 @@ def sweep_mode(args):
     pool.fill_random(args.seed, device)
     loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=E, config=cfg, seed=args.seed,
                                           pool=pool)
+    apply_kernel_options(loaded, args)
     nodes = args.sweep_nodes
     T = 1 + nodes
     routes = [torch.from_numpy(synthetic.zipf_routes(T, l, seed=args.seed + 3)).to(device) for l in range(L)]

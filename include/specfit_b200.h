@@ -15,6 +15,7 @@
  *   sf_moe_dispatch       grouping in Qwen3OffloadedExperts     src/specfit/runtime/qwen3_offloaded_experts.py:111-122,173-178
  *   sf_moe_gather         hidden_states[route_tokens], weights  src/specfit/runtime/qwen3_offloaded_experts.py:189-190
  *   sf_grouped_swiglu     _expert_forward + mul_(w), per expert src/specfit/runtime/qwen3_offloaded_experts.py:38-62,126-138,194-198
+ *   sf_grouped_swiglu_gathered  the gather (:189-190) + sf_grouped_swiglu in one call
  *   sf_moe_combine        index_add_ reduction                  src/specfit/runtime/qwen3_offloaded_experts.py:144-163,200-202
  *   sf_slot_fill_batch    slot.tensor.copy_(source)             src/specfit/runtime/gpu_expert_cache.py:556-561
  *   sf_tree_attention     SDPA under the tree mask              transformers/...:156-195 with the mask of
@@ -185,6 +186,27 @@ SF_API int sf_grouped_swiglu_ex(const void* hidden_sorted, const float* weights_
                          int64_t slot_stride_elems, int num_experts, int hidden_size,
                          int intermediate_size, int64_t rows, void* act_workspace,
                          void* out_sorted, int impl, void* stream);
+
+/*
+ * sf_moe_gather + sf_grouped_swiglu (tcgen05) in one call, without the
+ * gathered copy: sorted row r reads hidden[sorted_pos[r] / top_k] (bf16
+ * [tokens, hidden_size]) by TMA gather4 straight into the MMA tiles and is
+ * weighted by topk_weights[sorted_pos[r]] (fp32 [tokens * top_k]); rows =
+ * tokens * top_k.  Results equal the two calls bit for bit.  Returns
+ * SF_ERR_UNSUPPORTED (no message) when the tcgen05 kernel does not apply
+ * (not bf16-shaped as sf_grouped_swiglu's tcgen05 path requires, unaligned
+ * buffers, or not an sm_100 device); the caller then gathers and calls
+ * sf_grouped_swiglu.
+ * Replaces the gather of qwen3_offloaded_experts.py:189-190 and
+ * _expert_forward + mul_(w) (:38-62, :198) for all experts of a layer.
+ */
+SF_API int sf_grouped_swiglu_gathered(const void* hidden, int64_t tokens, const float* topk_weights,
+                                      int top_k, const int32_t* sorted_pos, const int32_t* offsets,
+                                      const int32_t* active, const int32_t* num_active,
+                                      const int32_t* expert_slot, const void* slot_storage,
+                                      int64_t slot_count, int64_t slot_stride_elems, int num_experts,
+                                      int hidden_size, int intermediate_size, void* act_workspace,
+                                      void* out_sorted, void* stream);
 
 /*
  * Combine: out[t,:] = sum over the token's K routes of out_sorted[inv_pos[t*K+k],:],

@@ -73,6 +73,8 @@ SIGNATURES = {
                                  _i32, _i64, _vp, _vp, _vp]),
     "sf_grouped_swiglu_ex": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32,
                                     _i32, _i32, _i64, _vp, _vp, _i32, _vp]),
+    "sf_grouped_swiglu_gathered": (_i32, [_vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                          _i32, _i32, _i32, _vp, _vp, _vp]),
     "sf_moe_combine": (_i32, [_vp, _i32, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp]),
     "sf_slot_fill_batch": (_i32, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
                                   _i32, _vp]),

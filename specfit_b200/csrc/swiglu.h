@@ -27,10 +27,21 @@ struct SwigluArgs {
   void* out_sorted;
 };
 
+// The gathered variant's extra inputs: SwigluArgs::hidden_sorted is then the
+// unsorted hidden [tokens, H]; sorted row r reads hidden row
+// sorted_pos[r] / top_k and weight topk_weights[sorted_pos[r]] (fp32).
+struct SwigluGather {
+  int64_t tokens;
+  int top_k;
+  const int32_t* sorted_pos;
+  const float* topk_weights;
+};
+
 int swiglu_simt(const SwigluArgs& a, cudaStream_t stream);
 // Returns SF_ERR_UNSUPPORTED (without a message) when the shape does not fit.
 int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream);
 bool swiglu_tcgen05_supports(const SwigluArgs& a);
+int swiglu_tcgen05_gathered(const SwigluArgs& a, const SwigluGather& g, cudaStream_t stream);
 // Reads (and with reset clears) the device status word of the tcgen05 kernels.
 int swiglu_status(int* status, int reset);
 int dense_status(int* status, int reset);

@@ -53,6 +53,7 @@ constexpr int kUpPitch = 17;   // padded row pitch of the gate/up exchange buffe
 
 struct __align__(8) SmemTail {
   float upbuf[64 * kUpPitch];
+  int rowtok[kBN];  // gathered variant: token row of each row of the current pass
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full[2];
@@ -102,13 +103,19 @@ __device__ __forceinline__ void for_each_unit(int m_tiles, const int32_t* offset
   }
 }
 
-template <int kPhase>
+// kGather (the gathered variant): phase 1 reads each pass's token rows
+// straight from the unsorted hidden states [T, H] with TMA gather4 (row of
+// sorted row r = sorted_pos[r] / top_k) instead of from a gathered copy, and
+// phase 2 reads the routing weight of row r as topk_w[sorted_pos[r]].  The
+// staged tiles, and so every result, are the same as with the copy.
+template <int kPhase, bool kGather = false>
 __global__ void __launch_bounds__(kThreads, 1)
 swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                  const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                  const int32_t* __restrict__ num_active, const int32_t* __restrict__ expert_slot,
                  const float* __restrict__ w_sorted, int H, int I,
-                 __nv_bfloat16* __restrict__ out) {
+                 __nv_bfloat16* __restrict__ out, const int32_t* __restrict__ sorted_pos = nullptr,
+                 int top_k = 1, const float* __restrict__ topk_w = nullptr) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
@@ -157,6 +164,13 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
         const int nb = (u.npass + kBBox - 1) / kBBox;
         const uint32_t bytes = kABytes + nb * kBBox * kBK * 2;
+        if constexpr (kGather && kPhase == 1) {
+          // Token rows of this pass; rows past it read token 0 (their
+          // products are never stored).
+#pragma unroll 8
+          for (int i = 0; i < nb * kBBox; ++i)
+            tail->rowtok[i] = i < u.npass ? sorted_pos[u.n0 + i] / top_k : 0;
+        }
         for (int kb = 0; kb < space.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
@@ -171,9 +185,16 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
             ptx::tma_load_3d(a, &tm_w, &tail->full[s], kb * kBK, u.m_tile * kBM, u.slot);
           }
           uint8_t* b = b_stage + (size_t)s * kBBytes;
-          for (int q = 0; q < nb; ++q)
-            ptx::tma_load_2d(b + q * kBBox * kBK * 2, &tm_x, &tail->full[s], kb * kBK,
-                             u.n0 + q * kBBox);
+          if constexpr (kGather && kPhase == 1) {
+            for (int g = 0; g < nb * (kBBox / 4); ++g) {
+              const int* t = &tail->rowtok[g * 4];
+              ptx::tma_gather4(b + g * 4 * kBK * 2, &tm_x, &tail->full[s], kb * kBK, t[0], t[1], t[2], t[3]);
+            }
+          } else {
+            for (int q = 0; q < nb; ++q)
+              ptx::tma_load_2d(b + q * kBBox * kBK * 2, &tm_x, &tail->full[s], kb * kBK,
+                               u.n0 + q * kBBox);
+          }
         }
         return true;
       });
@@ -268,7 +289,8 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
             if (j < u.npass) {
               const int r = u.n0 + j;
               const float y = bf16r(v[i]);
-              out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w_sorted[r]);
+              const float w = kGather ? topk_w[sorted_pos[r]] : w_sorted[r];
+              out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w);
             }
           }
         }
@@ -342,11 +364,12 @@ bool swiglu_tcgen05_supports(const SwigluArgs& a) {
          aligned16(a.act_workspace) && a.rows < (1LL << 31) && a.slot_count < (1LL << 31);
 }
 
-int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
-  if (!swiglu_tcgen05_supports(a))
-    return set_error(SF_ERR_UNSUPPORTED,
-                     "tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0 and 16-byte aligned buffers");
-  if (a.rows == 0) return SF_OK;
+namespace {
+
+// Encodes the four tensor maps and launches both phases.  With `gather`
+// (the gathered variant) a.hidden_sorted is the unsorted hidden [tokens, H]
+// and phase 1 loads its rows one box row at a time with gather4.
+int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaStream_t stream) {
   static std::atomic<unsigned long long> configured{0};
   if (int rc = once_per_device(configured, [] {
         int dev = 0, major = 0;
@@ -356,6 +379,10 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
         SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<1>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+        SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<1, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+        SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2, true>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         return SF_OK;
       }))
@@ -372,9 +399,10 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
     if (int rc = tma_encode_bf16(&tm_w1, storage, 3, dims, strides, box)) return rc;
   }
   {
-    cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)a.rows};
+    const int64_t x_rows = gather ? gather->tokens : a.rows;
+    cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)x_rows};
     cuuint64_t strides[1] = {(cuuint64_t)H * 2};
-    cuuint32_t box[2] = {kBK, kBBox};
+    cuuint32_t box[2] = {kBK, gather ? 1u : (cuuint32_t)kBBox};  // gather4 boxes are one row high
     if (int rc = tma_encode_bf16(&tm_x1, a.hidden_sorted, 2, dims, strides, box)) return rc;
   }
   {
@@ -391,15 +419,50 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
   }
   const int grid = num_sms();
   auto* act = static_cast<__nv_bfloat16*>(a.act_workspace);
+  auto* out = static_cast<__nv_bfloat16*>(a.out_sorted);
+  if (gather) {
+    SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
+                             tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot,
+                             a.weights_sorted, H, I, act, gather->sorted_pos, gather->top_k,
+                             gather->topk_weights));
+    SF_CHECK_LAUNCH();
+    SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
+                             tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot,
+                             a.weights_sorted, H, I, out, gather->sorted_pos, gather->top_k,
+                             gather->topk_weights));
+    SF_CHECK_LAUNCH();
+    return SF_OK;
+  }
+  const int32_t* no_pos = nullptr;
+  const float* no_w = nullptr;
   SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
                            tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot,
-                           a.weights_sorted, H, I, act));
+                           a.weights_sorted, H, I, act, no_pos, 1, no_w));
   SF_CHECK_LAUNCH();
   SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
                            tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot,
-                           a.weights_sorted, H, I, static_cast<__nv_bfloat16*>(a.out_sorted)));
+                           a.weights_sorted, H, I, out, no_pos, 1, no_w));
   SF_CHECK_LAUNCH();
   return SF_OK;
+}
+
+}  // namespace
+
+int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
+  if (!swiglu_tcgen05_supports(a))
+    return set_error(SF_ERR_UNSUPPORTED,
+                     "tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0 and 16-byte aligned buffers");
+  if (a.rows == 0) return SF_OK;
+  return swiglu_tcgen05_launch(a, nullptr, stream);
+}
+
+int swiglu_tcgen05_gathered(const SwigluArgs& a, const SwigluGather& g, cudaStream_t stream) {
+  if (!swiglu_tcgen05_supports(a) || g.tokens <= 0 || g.tokens >= (1LL << 31) || g.top_k <= 0 ||
+      !g.sorted_pos || !g.topk_weights || a.rows != g.tokens * g.top_k)
+    return set_error(SF_ERR_UNSUPPORTED,
+                     "gathered tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0, 16-byte aligned buffers "
+                     "and rows == tokens * top_k");
+  return swiglu_tcgen05_launch(a, &g, stream);
 }
 
 int swiglu_status(int* status, int reset) {
@@ -439,6 +502,32 @@ extern "C" int sf_grouped_swiglu_ex(const void* hidden_sorted, const float* weig
   SF_CHECK_ARG(impl == SF_SWIGLU_AUTO, "unknown implementation %d", impl);
   if (swiglu_tcgen05_supports(a) && device_is_sm100()) return swiglu_tcgen05(a, s);
   return swiglu_simt(a, s);
+}
+
+extern "C" int sf_grouped_swiglu_gathered(const void* hidden, int64_t tokens, const float* topk_weights,
+                                          int top_k, const int32_t* sorted_pos, const int32_t* offsets,
+                                          const int32_t* active, const int32_t* num_active,
+                                          const int32_t* expert_slot, const void* slot_storage,
+                                          int64_t slot_count, int64_t slot_stride_elems, int num_experts,
+                                          int hidden_size, int intermediate_size, void* act_workspace,
+                                          void* out_sorted, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(hidden_size > 0 && intermediate_size > 0 && num_experts > 0 && tokens >= 0 && top_k > 0,
+               "invalid sizes");
+  SF_CHECK_ARG(slot_count > 0 && slot_stride_elems >= 3LL * hidden_size * intermediate_size,
+               "slot_stride_elems must cover one packed expert");
+  if (tokens == 0) return SF_OK;
+  SF_CHECK_ARG(hidden && topk_weights && sorted_pos && offsets && active && num_active && expert_slot &&
+                   slot_storage && act_workspace && out_sorted,
+               "null pointer argument");
+  SwigluArgs a{hidden,        nullptr,        SF_DTYPE_BF16,  offsets,           active,
+               num_active,    expert_slot,    slot_storage,   slot_count,        slot_stride_elems,
+               num_experts,   hidden_size,    intermediate_size, tokens * top_k, act_workspace,
+               out_sorted};
+  SwigluGather g{tokens, top_k, sorted_pos, topk_weights};
+  if (!swiglu_tcgen05_supports(a) || !device_is_sm100())
+    return SF_ERR_UNSUPPORTED;  // the caller gathers and calls sf_grouped_swiglu
+  return swiglu_tcgen05_gathered(a, g, as_stream(stream));
 }
 
 extern "C" int sf_grouped_swiglu(const void* hidden_sorted, const float* weights_sorted, int dtype,

@@ -192,6 +192,39 @@ def grouped_swiglu(hidden_sorted: torch.Tensor, weights_sorted: torch.Tensor, d:
     return y
 
 
+def grouped_swiglu_gathered(hidden: torch.Tensor, top_k_weights: torch.Tensor, d: Dispatch,
+                            expert_slot: torch.Tensor, storage: torch.Tensor, hidden_size: int,
+                            intermediate_size: int, act_workspace: torch.Tensor | None = None,
+                            out: torch.Tensor | None = None):
+    """``moe_gather`` then ``grouped_swiglu`` in one tcgen05 call that reads
+    each expert's token rows straight from ``hidden`` (``[T, H]`` bf16) by TMA
+    gather4 and the routing weights from ``top_k_weights`` (fp32 ``[T, K]``);
+    bit-identical to the two calls.  Where the tcgen05 kernel does not apply
+    it runs the two calls."""
+    dev = _require_cuda(hidden, top_k_weights, expert_slot, storage)
+    h = hidden.contiguous()
+    w = top_k_weights.contiguous()
+    rows = d.tokens * d.top_k
+    if (h.dtype == torch.bfloat16 and w.dtype == torch.float32 and storage.dtype == torch.bfloat16
+            and rows > 0):
+        act = act_workspace if act_workspace is not None else torch.empty(
+            rows, intermediate_size, dtype=h.dtype, device=dev)
+        y = out if out is not None else torch.empty(rows, hidden_size, dtype=h.dtype, device=dev)
+        rc = N.lib.sf_grouped_swiglu_gathered(
+            h.data_ptr(), d.tokens, w.data_ptr(), d.top_k, d.sorted_pos.data_ptr(), d.offsets.data_ptr(),
+            d.active.data_ptr(), d.num_active.data_ptr(), expert_slot.data_ptr(), storage.data_ptr(),
+            storage.shape[0], storage.stride(0), d.num_experts, hidden_size, intermediate_size,
+            act.data_ptr(), y.data_ptr(), _stream(dev))
+        if rc == N.SF_OK:
+            _launched(2)
+            return y
+        if rc != N.SF_ERR_UNSUPPORTED:
+            N.check(rc, "sf_grouped_swiglu_gathered")
+    xs, ws = moe_gather(h, w, d)
+    return grouped_swiglu(xs, ws, d, expert_slot, storage, hidden_size, intermediate_size,
+                          act_workspace=act_workspace, out=out)
+
+
 # ---------------------------------------------------------------------------
 # K4 combine
 

@@ -73,6 +73,9 @@ class Qwen3OffloadedExperts(nn.Module):
         self.execution_policy = ExpertExecutionPolicy(execution_policy)
         self.h2d_prefetch = h2d_prefetch
         self.swiglu_impl = swiglu_impl
+        # Resident fast path: read the token rows inside the grouped SwiGLU
+        # (TMA gather4) instead of gathering a sorted copy first.
+        self.fused_gather = False
         self._prediction_scheduler = None
         ids = [k.expert_id for k in cache.source_keys()
                if isinstance(k, ExpertKey) and k.layer_id == layer_id]
@@ -124,8 +127,12 @@ class Qwen3OffloadedExperts(nn.Module):
         h = hidden_states.contiguous()
         # Every active expert is a resident hit: the dispatch launch counts them.
         d = ops.moe_dispatch(top_k_index, self.num_experts, active_total=self.cache.device_hit_counter())
-        xs, ws = ops.moe_gather(h, top_k_weights, d)
         storage = self.cache.storage.view(self.cache.slot_count, -1)
+        if self.fused_gather and self.swiglu_impl != N.SF_SWIGLU_SIMT:
+            ys = ops.grouped_swiglu_gathered(h, top_k_weights, d, fixed, storage, self.hidden_size,
+                                             self.intermediate_size)
+            return ys, d
+        xs, ws = ops.moe_gather(h, top_k_weights, d)
         ys = ops.grouped_swiglu(xs, ws, d, fixed, storage, self.hidden_size, self.intermediate_size,
                                 impl=self.swiglu_impl)
         return ys, d

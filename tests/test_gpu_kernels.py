@@ -232,6 +232,31 @@ def test_tc_and_simt_agree(ops):
     assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= 0.9999
 
 
+@NEW_KERNEL
+@pytest.mark.parametrize("tokens,routes", [(1, "zipf"), (7, "zipf"), (65, "uniform"), (129, "zipf"), (512, "zipf")])
+def test_gathered_swiglu_equals_gather_then_swiglu(ops, tokens, routes):
+    """The gathered call (token rows by TMA gather4, weights through
+    sorted_pos) gives the gather + grouped SwiGLU rows bit for bit."""
+    weights, x = synthetic.bf16_layer_inputs(seed=40 + tokens, tokens=tokens)
+    if routes == "zipf":
+        idx_np = synthetic.zipf_routes(tokens, layer=3, seed=9)
+    else:
+        idx_np = np.stack([np.random.default_rng(tokens + i).permutation(128)[:8] for i in range(tokens)])
+    topw = torch.from_numpy(np.random.default_rng(3).dirichlet(np.ones(8), size=tokens).astype(np.float32)).to(DEV)
+    idx = torch.from_numpy(idx_np).to(DEV)
+    xd = x.to(DEV)
+    storage = weights.packed_all().to(DEV)
+    slot = torch.arange(128, dtype=torch.int32, device=DEV)
+    d = ops.moe_dispatch(idx, 128)
+    xs, ws = ops.moe_gather(xd, topw, d)
+    want = ops.grouped_swiglu(xs, ws, d, slot, storage, 2048, 768, impl=2)
+    got = ops.grouped_swiglu_gathered(xd, topw, d, slot, storage, 2048, 768)
+    assert torch.equal(got, want)
+    from specfit_b200 import _native as N
+
+    assert N.device_status(reset=True) == 0
+
+
 def test_expert_kats(ops, golden_dir):
     """Reference unit-test shapes (H=4, I=3) and the bf16 reduction-order KAT."""
     g = np.load(golden_dir / "expert_kats.npz")
