@@ -1396,9 +1396,9 @@ def kernel_cases(device, only=()):
     want = lambda name: not only or name in only
     cases = []
     storage = slot = router = None
-    if want("router") or want("grouped_swiglu"):
+    if want("router") or want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
         router = randn(E, H, std=0.02)
-    if want("grouped_swiglu"):
+    if want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
         storage = randn(E, 3 * H * I, std=0.02)
         slot = torch.arange(E, dtype=torch.int32, device=device)
     for t in (7, 65, 512):
@@ -1420,7 +1420,7 @@ def kernel_cases(device, only=()):
             ys = randn(t * K, H)
             cases.append(("combine", f"T={t}", lambda ys=ys, d=d, idx=idx: ops.moe_combine(ys, d, idx),
                           t * K * H * 2 + t * H * 2 + t * K * 12))
-        if want("grouped_swiglu"):
+        if want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
             for kind in ("zipf", "uniform"):
                 if kind == "uniform":
                     rng = np.random.default_rng(t)
@@ -1431,9 +1431,14 @@ def kernel_cases(device, only=()):
                     ud, uxs, uws = d, xs, ws
                 torch.cuda.synchronize(device)
                 n_act = int(ud.num_active.item())
-                cases.append(("grouped_swiglu", f"T={t} {kind} ({n_act} experts)",
-                              lambda a=uxs, b=uws, c=ud: ops.grouped_swiglu(a, b, c, slot, storage, H, I),
-                              n_act * EXPERT_BYTES + t * K * (H * 2 * 2 + 4)))
+                if want("grouped_swiglu"):
+                    cases.append(("grouped_swiglu", f"T={t} {kind} ({n_act} experts)",
+                                  lambda a=uxs, b=uws, c=ud: ops.grouped_swiglu(a, b, c, slot, storage, H, I),
+                                  n_act * EXPERT_BYTES + t * K * (H * 2 * 2 + 4)))
+                if "grouped_swiglu_gathered" in only:  # the gathered variant, only when named
+                    cases.append(("grouped_swiglu_gathered", f"T={t} {kind} ({n_act} experts)",
+                                  lambda c=ud, x=x, w=w: ops.grouped_swiglu_gathered(x, w, c, slot, storage, H, I),
+                                  n_act * EXPERT_BYTES + t * H * 2 + t * K * (H * 2 + 4)))
     # tree_attention_tc (the tcgen05 kernel) runs only when named explicitly.
     for name, impl in (("tree_attention", N.SF_ATTN_AUTO), ("tree_attention_tc", N.SF_ATTN_TCGEN05)):
         if (name == "tree_attention" and not want(name)) or (name == "tree_attention_tc" and name not in only):
