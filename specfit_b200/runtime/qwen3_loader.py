@@ -152,12 +152,15 @@ def _sha256(path: Path) -> str:
 
 def open_packed_checkpoint(root, *, verify_hashes: bool = False,
                            source_metadata_root=None) -> PackedCheckpoint:
-    """Read and check a packed-v1 manifest (the checks of the reference's
-    ``PackedQwen3Checkpoint.open``, qwen3_packed_checkpoint.py:156-377, that
-    a loader depends on): schema and version, completeness, the expert
-    layout and dtype, one file per layer in order with the packed shape,
-    file sizes, optionally every file's SHA-256, and optionally that the
-    source ``config.json`` under ``source_metadata_root`` is the one packed."""
+    """Read and check a packed-v1 manifest: the checks of the reference's
+    ``PackedQwen3Checkpoint.open`` (qwen3_packed_checkpoint.py:156-377) that
+    a loader depends on, with its error type and messages -- schema and
+    version, completeness, expert layout and dtype, the packed element
+    count, one record per layer in order with the packed shape, unique file
+    names, file presence and sizes, optionally every file's SHA-256, and,
+    with ``source_metadata_root``, that its ``config.json`` (and
+    ``model.safetensors.index.json`` when present) are the ones packed.
+    Only bf16 experts are accepted (the kernels' dtype)."""
     root = Path(root).resolve()
     mpath = root / "manifest.json"
     if not mpath.is_file():
@@ -183,31 +186,52 @@ def open_packed_checkpoint(root, *, verify_hashes: bool = False,
         files = manifest["files"]
         layers = files["layers"]
         nonexp = files["nonexperts"]
+        source = manifest.get("source", {})
     except (KeyError, TypeError, ValueError) as error:
         raise PackedCheckpointError("packed checkpoint manifest lacks model or file records") from error
-    if tuple(model.get("expert_layout", ())) != PACKED_LAYOUT:
-        raise PackedCheckpointError("packed expert layout must be gate_proj|up_proj|down_proj")
-    if model.get("expert_dtype") != "BF16":
-        raise PackedCheckpointError("only BF16 packed experts are supported")
+    dtype = model.get("expert_dtype")
+    if dtype != "BF16":
+        raise PackedCheckpointError(f"unsupported packed expert dtype: {dtype}")
+    if model.get("expert_layout") != list(PACKED_LAYOUT):
+        raise PackedCheckpointError("packed checkpoint expert layout does not match")
     if packed != 3 * H * I:
-        raise PackedCheckpointError("packed expert elements differ from 3 * hidden * intermediate")
+        raise PackedCheckpointError("packed expert element count does not match model dimensions")
+    if not isinstance(layers, list):
+        raise PackedCheckpointError("packed checkpoint layer files must be a list")
     if len(layers) != L:
-        raise PackedCheckpointError("packed checkpoint must list one file per layer")
-    records = [(r, root / r["filename"]) for r in layers] + [(nonexp, root / nonexp["filename"])]
+        raise PackedCheckpointError("packed checkpoint layer file count does not match census")
     for l, rec in enumerate(layers):
-        if rec.get("layer_id") != l or rec.get("tensor_name") != "experts" or list(rec.get("shape", ())) != [E, packed]:
-            raise PackedCheckpointError(f"layer record {l} does not match the census")
-    for rec, path in records:
+        if not isinstance(rec, dict):
+            raise PackedCheckpointError("packed checkpoint layer file record must be an object")
+        if rec.get("layer_id") != l:
+            raise PackedCheckpointError("packed checkpoint layer IDs must be contiguous")
+        if rec.get("tensor_name") != "experts":
+            raise PackedCheckpointError("packed checkpoint layer tensor name must be experts")
+        if rec.get("shape") != [E, packed]:
+            raise PackedCheckpointError("packed checkpoint layer tensor shape does not match")
+        if rec.get("dtype") != dtype:
+            raise PackedCheckpointError("packed checkpoint layer tensor dtype does not match")
+    records = [nonexp] + layers
+    names = [r.get("filename") for r in records]
+    if len(names) != len(set(names)):
+        raise PackedCheckpointError("packed checkpoint file names must be unique")
+    for rec in records:
+        path = root / rec["filename"]
         if not path.is_file():
             raise PackedCheckpointError(f"packed checkpoint file is missing: {path}")
         if path.stat().st_size != int(rec["size_bytes"]):
-            raise PackedCheckpointError(f"packed checkpoint file size differs: {path}")
+            raise PackedCheckpointError(f"packed checkpoint file size does not match: {path}")
         if verify_hashes and _sha256(path) != rec["sha256"]:
-            raise PackedCheckpointError(f"packed checkpoint file hash differs: {path}")
+            raise PackedCheckpointError(f"packed checkpoint file SHA256 does not match: {path}")
     if source_metadata_root is not None:
-        cfg = Path(source_metadata_root) / "config.json"
-        if cfg.is_file() and _sha256(cfg) != manifest.get("source", {}).get("config_sha256"):
-            raise PackedCheckpointError("source config.json differs from the packed checkpoint's")
+        meta = Path(source_metadata_root).resolve()
+        cfg, index = meta / "config.json", meta / "model.safetensors.index.json"
+        if not cfg.is_file():
+            raise PackedCheckpointError("source config or index metadata is missing")
+        if _sha256(cfg) != source.get("config_sha256"):
+            raise PackedCheckpointError("source config SHA256 does not match packed checkpoint")
+        if index.is_file() and _sha256(index) != source.get("index_sha256"):
+            raise PackedCheckpointError("source index SHA256 does not match packed checkpoint")
     return PackedCheckpoint(root, manifest, L, E, H, I, packed,
                             tuple(root / r["filename"] for r in layers), root / nonexp["filename"])
 

@@ -124,11 +124,13 @@ def _edit_manifest(root, fn):
     (lambda m: m.__setitem__("complete", False), "complete"),
     (lambda m: m.__setitem__("schema", "other"), "schema"),
     (lambda m: m.__setitem__("schema_version", 2), "version"),
-    (lambda m: m["model"].__setitem__("expert_layout", ["up_proj", "gate_proj", "down_proj"]), "layout"),
-    (lambda m: m["model"].__setitem__("expert_dtype", "F16"), "BF16"),
-    (lambda m: m["files"]["layers"].pop(), "one file per layer"),
-    (lambda m: m["files"]["layers"][1].__setitem__("shape", [E, 3 * H * I + 8]), "layer record 1"),
-    (lambda m: m["files"]["nonexperts"].__setitem__("size_bytes", 1), "size"),
+    (lambda m: m["model"].__setitem__("expert_layout", ["up_proj", "gate_proj", "down_proj"]), "expert layout does not match"),
+    (lambda m: m["model"].__setitem__("expert_dtype", "F16"), "unsupported packed expert dtype"),
+    (lambda m: m["files"]["layers"].pop(), "layer file count does not match"),
+    (lambda m: m["files"]["layers"][1].__setitem__("shape", [E, 3 * H * I + 8]), "layer tensor shape does not match"),
+    (lambda m: m["files"]["layers"][1].__setitem__("layer_id", 0), "layer IDs must be contiguous"),
+    (lambda m: m["files"]["layers"][0].__setitem__("filename", "nonexperts.safetensors"), "file names must be unique"),
+    (lambda m: m["files"]["nonexperts"].__setitem__("size_bytes", 1), "file size does not match"),
 ])
 def test_packed_manifest_mismatches_are_refused(tmp_path, edit, match):
     root = _copy_fixture(tmp_path)
@@ -144,7 +146,7 @@ def test_packed_corruption_found_only_with_hash_verification(tmp_path):
     raw[-3] ^= 0x40  # a bit of the last expert's down rows; the size is unchanged
     path.write_bytes(bytes(raw))
     open_packed_checkpoint(root)  # sizes still match
-    with pytest.raises(PackedCheckpointError, match="hash"):
+    with pytest.raises(PackedCheckpointError, match="SHA256 does not match"):
         open_packed_checkpoint(root, verify_hashes=True)
 
 
@@ -154,7 +156,7 @@ def test_packed_source_config_must_match(tmp_path):
     cfg = json.loads((src / "config.json").read_text())
     cfg["rms_norm_eps"] = 1e-5
     (src / "config.json").write_text(json.dumps(cfg))
-    with pytest.raises(PackedCheckpointError, match="config.json"):
+    with pytest.raises(PackedCheckpointError, match="source config SHA256 does not match"):
         open_packed_checkpoint(FIXTURE / "packed", source_metadata_root=src)
 
 
