@@ -287,3 +287,27 @@ def test_full_layer_cache_paths_match_oracle(rt, slots):
     ref = mo.moe_experts(x.float().numpy(), idx_np, w_np, pk, 2048, 768, "bf16")
     got = out.float().cpu().numpy()
     assert np.abs(got - ref).max() <= 2e-2
+
+
+@pytest.mark.parametrize("slots,experts,seed", [(4, 12, 0), (1, 3, 1), (6, 8, 2), (12, 12, 3)])
+def test_cache_state_follows_the_lru_replay_oracle(rt, slots, experts, seed):
+    """Access by access, the cache's fills, evictions and resident set equal
+    the reference's logical LRU replay (src/specfit/replay.py:156-285,
+    restated in oracle/cache_oracle.py) on Zipf-skewed random accesses."""
+    from oracle.cache_oracle import LruLayer
+
+    rng = np.random.default_rng(seed)
+    weights = 1.0 / np.arange(1, experts + 1) ** 1.1
+    seq = rng.choice(experts, size=150, p=weights / weights.sum())
+    cache = rt.GpuExpertCache(make_sources(experts, shape=(8, 16), seed=seed), slot_count=slots, device=DEV)
+    ref = LruLayer(slots)
+    for i, e in enumerate(seq):
+        with cache.acquire(int(e)) as lease:
+            lease.wait()
+        torch.cuda.synchronize()  # each fill lands before the next access, as in the replay
+        ref.access(int(e))
+        st = cache.stats()
+        assert (st.h2d_submissions, st.resident_hits, st.evictions) == \
+            (ref.h2d_submissions, ref.resident_hits, ref.evictions), i
+        assert set(cache.resident_expert_ids()) == set(ref.resident()), i
+    cache.close()
