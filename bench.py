@@ -54,6 +54,12 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 EXPERT_BYTES = 3 * 2048 * 768 * 2  # one packed bf16 expert slot
+# DRAM bytes (read + write) per active expert of one grouped SwiGLU call
+# (both phases), from the ncu capture summarised in
+# profiles/swiglu_tc_moe_block_t65_uniform.md: 801.3 + 5.7 + 400.4 + 5.9 MB
+# over 127 experts at 65 rows.  The roofline's `traffic` scales it by the
+# experts a launch processes.
+SWIGLU_DRAM_BYTES_PER_EXPERT = (801.3e6 + 5.7e6 + 400.4e6 + 5.9e6) / 127
 
 
 def parse_args(argv=None):
@@ -378,7 +384,9 @@ def swiglu_roofline(loaded, device, tokens, peaks, iters=20):
     achieved = algo / (us * 1e-6) / 1e9
     return {"bound": "hbm", "kernel": "swiglu_tc_kernel (phase 1 + 2)", "achieved": round(achieved, 1),
             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-            "traffic": None, "launch_us": round(us, 2), "experts": uniq, "tokens": tokens,
+            "traffic": round(SWIGLU_DRAM_BYTES_PER_EXPERT * uniq),
+            "traffic_source": "ncu dram__bytes_read+write per expert at 65 rows x 127 experts, scaled by experts",
+            "launch_us": round(us, 2), "experts": uniq, "tokens": tokens,
             "algorithmic_bytes": algo, "peak_source": peaks["source"] + " hbm_gbs (burst copy)"}
 
 
