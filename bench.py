@@ -1152,6 +1152,11 @@ def decode_mode(args):
                     "(210.7 us per distinct (layer, expert)): no drafted node pays for itself"},
         "setup_s": round(setup_s, 1),
     }
+    try:  # the grouped SwiGLU at the mean verify size, on layer 0's resident slots
+        result["roofline"] = swiglu_roofline(loaded, device, 1 + int(round(mean([c.selected for c in cyc]))),
+                                             peaks)
+    except Exception as err:  # reported, never fatal to the line
+        result["roofline"] = {"error": f"{type(err).__name__}: {err}"}
     if not args.no_cpu_baseline:
         vt = 1 + int(round(mean([c.selected for c in cyc])))
         cycle_s, desc, cores = cpu_decode_sample(cfg, vt, args.decode_ctx, 8, 8)
