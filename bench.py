@@ -1134,7 +1134,9 @@ def decode_mode(args):
                   "host_ms": {"draft": round(mean([c.draft_ms for c in cyc]), 3),
                               "select": round(mean([c.select_ms for c in cyc]), 3),
                               "verify": round(mean([c.verify_ms for c in cyc]), 3),
-                              "commit": round(mean([c.commit_ms for c in cyc]), 3)},
+                              "commit": round(mean([c.commit_ms for c in cyc]), 3),
+                              "draft_split": ({k: round(mean([t[k] for t in res.draft_split]), 3)
+                                               for k in res.draft_split[0]} if res.draft_split else {})},
                   "prefill_s": round(res.prefill_s, 3)},
         "cost_model": ({"kind": "SelectionCostModel fitted on this B200 the reference's way: whole "
                                 "decode cycles timed per forced tree size; slope = one packed expert "

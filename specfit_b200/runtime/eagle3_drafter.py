@@ -40,6 +40,8 @@ Its fixed shapes let it be one CUDA graph per number of catch-up rows.
 """
 from __future__ import annotations
 
+import time
+
 import torch
 from torch import nn
 
@@ -268,6 +270,7 @@ class DeviceDraft:
 
     def __init__(self, drafter: Eagle3DrafterStandIn, *, top_k: int = 4, max_depth: int = 8,
                  first_width: int = 4, level_width: int = 8, max_new: int = 8) -> None:
+        self.last_timing: dict = {}
         d = drafter
         self.d = d
         self.top_k, self.max_depth = top_k, max_depth
@@ -439,6 +442,7 @@ class DeviceDraft:
         -1, conditional and cumulative log-probability, depth; generation
         order) as a numpy array, plus each device tensor in ``extra``."""
         d = self.d
+        t0 = time.perf_counter()
         L = fed_ids.shape[1]
         start = d._fed
         n_new = L + 1 - start
@@ -448,7 +452,9 @@ class DeviceDraft:
         self.tokens[n_new - 1].copy_(pending_seed.reshape(()))
         self.aux[:n_new].copy_(aux_history[start - 1:L])
         self.start.fill_(d._len)
+        t1 = time.perf_counter()
         self._graph(n_new).replay()
+        t2 = time.perf_counter()
         self._host_out.copy_(self.out, non_blocking=True)
         hosts = []
         for t in extra:
@@ -457,9 +463,15 @@ class DeviceDraft:
                 h = self._host_extra[t.data_ptr()] = torch.empty(t.shape, dtype=t.dtype).pin_memory()
             h.copy_(t, non_blocking=True)
             hosts.append(h.numpy())
+        t3 = time.perf_counter()
         torch.cuda.current_stream(self.dev).synchronize()
+        t4 = time.perf_counter()
         d._len += n_new       # committed rows + the seed row stay; tree rows are dropped
         d._fed = L + 1
+        # Host-side split of the last call (ms): input copies, graph launch,
+        # read-back launch, wait for the GPU.
+        self.last_timing = {"inputs": (t1 - t0) * 1e3, "launch": (t2 - t1) * 1e3,
+                            "readback": (t3 - t2) * 1e3, "wait": (t4 - t3) * 1e3}
         return self._host_out.numpy(), hosts
 
     def pool(self, *, fed_ids: torch.Tensor, aux_history: torch.Tensor,

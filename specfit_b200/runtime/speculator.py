@@ -116,6 +116,7 @@ class DecodeResult:
     cycles: list = field(default_factory=list)
     decode_s: float = 0.0
     prefill_s: float = 0.0
+    draft_split: list = field(default_factory=list)  # DeviceDraft.last_timing of each device-drafted cycle
 
     @property
     def committed(self) -> int:
@@ -435,6 +436,7 @@ class B200TreeSpeculator:
                         arr, (fp,) = self._ddraft.pool_arrays(fed_ids=fed, aux_history=aux,
                                                               pending_seed=pending, extra=(self._pool_fp,))
                         tb = time.perf_counter()
+                        result.draft_split.append(self._ddraft.last_timing)
                         tok = arr[:, 0].astype(np.int64)
                         par = arr[:, 1].astype(np.int64) + 1  # raw parent ids (0 = the seed)
                         cond = np.minimum(arr[:, 2], 0.0)     # log-probabilities
