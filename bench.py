@@ -55,10 +55,11 @@ sys.path.insert(0, str(REPO))
 
 EXPERT_BYTES = 3 * 2048 * 768 * 2  # one packed bf16 expert slot
 # DRAM bytes (read + write) per active expert of one grouped SwiGLU call
-# (both phases), from the ncu capture summarised in
-# profiles/swiglu_tc_moe_block_t65_uniform.md: 801.3 + 5.7 + 400.4 + 5.9 MB
-# over 127 experts at 65 rows.  The roofline's `traffic` scales it by the
-# experts a launch processes.
+# (both phases), from an ncu capture of that kernel at 65 token rows over 127
+# active experts: 801.3 + 5.7 + 400.4 + 5.9 MB.  The roofline's `traffic`
+# scales it by the experts a launch processes, and only at the captured row
+# count (the activation bytes per expert change with the rows).
+SWIGLU_CAPTURE_ROWS = 65
 SWIGLU_DRAM_BYTES_PER_EXPERT = (801.3e6 + 5.7e6 + 400.4e6 + 5.9e6) / 127
 
 
@@ -69,6 +70,9 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--slots", type=int, default=24)
+    p.add_argument("--policy", choices=("expert_id_ascending", "resident_first"),
+                   default="expert_id_ascending",
+                   help="expert execution policy of the headline passes (the other one is also timed)")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--ctx", type=int, default=512)
     p.add_argument("--nodes", type=int, default=64)
@@ -156,6 +160,44 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def pinned_h2d_peak(pool, device, slots: int = 48, reps: int = 3) -> dict:
+    """Host-to-device copy rate of this box for the cache's fill pattern:
+    ``slots`` back-to-back copies of one packed expert (9,437,184 B) from the
+    page-locked expert pool into a device buffer on a side stream, CUDA
+    events, best of ``reps``."""
+    src = pool.data[0]
+    n = min(slots, src.shape[0])
+    dst = torch.empty(n, src.shape[1], dtype=src.dtype, device=device)
+    stream = torch.cuda.Stream(device)
+    best = None
+    with torch.cuda.stream(stream):
+        for _ in range(reps + 1):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for i in range(n):
+                dst[i].copy_(src[i], non_blocking=True)
+            b.record(stream)
+            b.synchronize()
+            ms = a.elapsed_time(b)
+            best = ms if best is None else min(best, ms)
+    nbytes = n * src.shape[1] * src.element_size()
+    del dst
+    return {"GBps": round(nbytes / (best * 1e-3) / 1e9, 2), "bytes": nbytes,
+            "how": f"{n} copies of one packed expert from the page-locked pool, best of {reps}"}
+
+
+def h2d_roofline_of(per_step: dict, ms_per_step: float, peak: dict) -> dict:
+    """H2D roofline of a cache-bound step: expert fill bytes per step (H2D
+    submissions x 9,437,184 B) over the step time, against the pinned-copy
+    rate measured in the same run."""
+    nbytes = per_step["h2d_submissions"] * EXPERT_BYTES
+    achieved = nbytes / (ms_per_step * 1e-3) / 1e9
+    return {"bound": "h2d", "fills_per_step": per_step["h2d_submissions"],
+            "bytes_per_step": int(nbytes), "achieved": round(achieved, 2), "peak": peak["GBps"],
+            "unit": "GB/s", "frac": round(achieved / peak["GBps"], 4),
+            "floor_ms": round(nbytes / (peak["GBps"] * 1e9) * 1e3, 3), "peak_source": peak["how"]}
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples while the timed region runs."""
 
@@ -209,11 +251,42 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def workload_tree(nodes, depth, branch, seed, vocab):
+    """The benchmark's seeded draft tree, shared by both arms: parents precede
+    children (1-based ids, 0 = the pending seed), depth <= ``depth``, at most
+    ``branch`` children per node, distinct sibling tokens, later nodes
+    preferred as parents so the tree reaches its depth.  Returns
+    ``(token_ids, parent_ids, depths)``; equals
+    ``specfit_b200.synthetic.random_tree`` (checked by a CPU test) but lives
+    here so the reference arm imports nothing from the package."""
+    rng = np.random.default_rng(seed)
+    parents, depths, tokens = [], [], []
+    child_count, node_depth, siblings = {0: 0}, {0: 0}, {0: set()}
+    while len(parents) < nodes:
+        cands = [n for n in range(len(parents) + 1) if node_depth[n] < depth and child_count[n] < branch]
+        if not cands:
+            raise ValueError("tree shape cannot hold that many nodes")
+        w = np.array([1.0 + n for n in cands], dtype=np.float64)
+        parent = int(rng.choice(cands, p=w / w.sum()))
+        node = len(parents) + 1
+        tok = int(rng.integers(0, vocab))
+        while tok in siblings[parent]:
+            tok = int(rng.integers(0, vocab))
+        siblings[parent].add(tok)
+        parents.append(parent)
+        depths.append(node_depth[parent] + 1)
+        tokens.append(tok)
+        child_count[parent] += 1
+        child_count[node] = 0
+        node_depth[node] = node_depth[parent] + 1
+        siblings[node] = set()
+    return tuple(tokens), tuple(parents), tuple(depths)
+
+
 def make_tree(nodes, depth, branch, seed, vocab):
-    from specfit_b200 import synthetic
     from specfit_b200.runtime.eagle3_types import Eagle3DraftTree
 
-    tok, par, dep = synthetic.random_tree(nodes, max_depth=depth, max_branch=branch, seed=seed, vocab=vocab)
+    tok, par, dep = workload_tree(nodes, depth, branch, seed, vocab)
     rng = np.random.default_rng(seed)
     cond, cum = [], []
     for p in par:
@@ -221,6 +294,34 @@ def make_tree(nodes, depth, branch, seed, vocab):
         cond.append(c)
         cum.append((0.0 if p == 0 else cum[p - 1]) + math.log(c))
     return Eagle3DraftTree(tok, par, dep, tuple(cond), tuple(cum))
+
+
+def reference_config(layers: int):
+    """Qwen3-30B-A3B shape built from transformers alone (48 layers, hidden
+    2048, 128 experts top-8, moe_intermediate 768, 32/4 heads of 128, vocab
+    151,936, RoPE theta 1e6, RMSNorm eps 1e-6); the B200 arm's
+    ``qwen3_moe_config`` gives the same values (checked by a CPU test)."""
+    from transformers import Qwen3MoeConfig
+
+    return Qwen3MoeConfig(
+        vocab_size=151936, hidden_size=2048, intermediate_size=6144, num_hidden_layers=layers,
+        num_attention_heads=32, num_key_value_heads=4, head_dim=128, max_position_embeddings=40960,
+        rms_norm_eps=1e-6, rope_parameters={"rope_type": "default", "rope_theta": 1000000.0},
+        tie_word_embeddings=False, moe_intermediate_size=768, num_experts=128, num_experts_per_tok=8,
+        norm_topk_prob=True, decoder_sparse_step=1, mlp_only_layers=[], attention_bias=False)
+
+
+def headline_config(args) -> dict:
+    """The workload description both arms print (identical by construction)."""
+    return {
+        "workload": (f"BASELINE config 2: {args.layers}-layer Qwen3-30B-A3B-shaped verify pass over a "
+                     f"{args.nodes}-node tree (depth {args.depth}, branching <= {args.branch}), "
+                     f"{args.ctx}-token context, {args.slots} expert-cache slots per layer"),
+        "verify_tokens_per_step": 1 + args.nodes,
+        "slots_per_layer": args.slots,
+        "parallelism": "single GPU",
+        "l2_flush": "not needed: each step streams > 57 GB of expert weights (>> 126 MB L2)",
+    }
 
 
 # --------------------------------------------------------------- B200 arm
@@ -296,11 +397,17 @@ class VerifyRunner:
         return self.h_ids.numel() * 8
 
 
-def timed_steps(fn, steps, warmup, world, device):
+def timed_steps(fn, steps, warmup, world, device, on_start=None):
+    """W untimed then K timed calls of ``fn`` between barriers and device
+    synchronisations, CUDA events on the current stream; ``on_start`` (if
+    given) runs after the warm-up, outside the timed region.  Returns the
+    max over ranks of the timed milliseconds and ``fn``'s results."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(device)
     barrier(world)
+    if on_start is not None:
+        on_start()
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
@@ -384,8 +491,12 @@ def swiglu_roofline(loaded, device, tokens, peaks, iters=20):
     achieved = algo / (us * 1e-6) / 1e9
     return {"bound": "hbm", "kernel": "swiglu_tc_kernel (phase 1 + 2)", "achieved": round(achieved, 1),
             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-            "traffic": round(SWIGLU_DRAM_BYTES_PER_EXPERT * uniq),
-            "traffic_source": "ncu dram__bytes_read+write per expert at 65 rows x 127 experts, scaled by experts",
+            "traffic": (round(SWIGLU_DRAM_BYTES_PER_EXPERT * uniq) if tokens == SWIGLU_CAPTURE_ROWS
+                        else None),
+            "traffic_source": ("estimated, not measured in this run: ncu dram__bytes_read+write per "
+                               "expert of a capture at 65 rows x 127 experts, times this launch's "
+                               "experts" if tokens == SWIGLU_CAPTURE_ROWS else
+                               f"null: the ncu capture was taken at {SWIGLU_CAPTURE_ROWS} rows, not {tokens}"),
             "launch_us": round(us, 2), "experts": uniq, "tokens": tokens,
             "algorithmic_bytes": algo, "peak_source": peaks["source"] + " hbm_gbs (burst copy)"}
 
@@ -456,58 +567,104 @@ def moe_block_graph(loaded, device, tokens, peaks, reps=20, warmup=3):
             "l2": "flushed before each replay (256 MB write outside the timed events)"}
 
 
-def cpu_reference_sample(args, layers=1):
-    """The reference's CPU path on a bounded sample: Hugging Face
-    Qwen3MoeDecoderLayer (SDPA under the 4-D tree mask over the cached
-    context, stock sparse-MoE block) for ``layers`` layer(s) plus the final
-    norm and lm_head, bf16, all host threads.  Returns seconds per verify
-    pass scaled to the full depth, and a description."""
-    from transformers import DynamicCache
-    from transformers.models.qwen3_moe.modeling_qwen3_moe import (Qwen3MoeDecoderLayer,
-                                                                   Qwen3MoeRotaryEmbedding)
+def reference_model(cfg, seed: int, std: float = 0.02):
+    """Stock Hugging Face ``Qwen3MoeForCausalLM`` on the host, bf16, every
+    linear weight N(0, std) and every norm weight 1 (the B200 arm's
+    initialisation; the draws differ, the distribution is the same).  Built
+    on the meta device and allocated in bf16 so no fp32 copy of the model is
+    ever held; weights are drawn in fp32 chunks of at most 64 Mi elements."""
+    from transformers import Qwen3MoeForCausalLM
 
-    from specfit_b200.runtime.qwen3_verifier import qwen3_moe_config
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device("meta"):
+            model = Qwen3MoeForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    model.to_empty(device="cpu")
+    gen = torch.Generator().manual_seed(seed)
+    chunk = 1 << 26
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            flat = p.data.view(-1)
+            if "norm" in name:
+                flat.fill_(1.0)
+                continue
+            for i in range(0, flat.numel(), chunk):
+                part = flat[i:i + chunk]
+                part.copy_(torch.randn(part.numel(), generator=gen).mul_(std))
+    model.model.rotary_emb = type(model.model.rotary_emb)(config=cfg)  # fp32 frequencies
+    model.requires_grad_(False)
+    return model.eval()
+
+
+def reference_model_bytes(layers: int) -> int:
+    """bf16 bytes of ``reference_model`` at the Qwen3-30B-A3B shape."""
+    per_layer = (128 * 3 * 2048 * 768 + 128 * 2048 + (32 + 2 * 4) * 128 * 2048 + 2048 * 32 * 128
+                 + 2 * 128 + 2 * 2048)
+    return 2 * (layers * per_layer + 2 * 151936 * 2048 + 2048)
+
+
+def cpu_reference_run(args, model_layers: int, steps: int, warmup: int):
+    """The reference's CPU path: a stock Hugging Face Qwen3-MoE target on the
+    host cores (all threads) — embedding, ``model_layers`` decoder layers
+    (SDPA under the 4-D ancestor mask, stock sparse-MoE block), final norm and
+    lm_head — verifying the benchmark's tree over a ``args.ctx``-token cache
+    (prefilled outside the timer), then the greedy accepted path and the
+    rollback to the context (``eagle3_tree.py:1202-1340``).  The tree mask,
+    positions and accepted path come from the CPU restatement in
+    ``oracle/tree_oracle.py`` (``eagle3_types.py:429-502``); nothing is
+    imported from ``specfit_b200``.  Returns (seconds per pass over the
+    timed steps, committed tokens per pass, threads)."""
+    from transformers import DynamicCache
+
+    from oracle import tree_oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
-    cfg = qwen3_moe_config(args.layers)
+    cfg = reference_config(model_layers)
     cfg._attn_implementation = "sdpa"
-    tree = make_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
-    q = 1 + tree.draft_node_count
-    gen = torch.Generator().manual_seed(11)
-    layer = Qwen3MoeDecoderLayer(cfg, 0).to(torch.bfloat16).eval()
+    tok, par, dep = workload_tree(args.nodes, args.depth, args.branch, seed=2, vocab=cfg.vocab_size)
+    model = reference_model(cfg, seed=args.seed)
+    gen = torch.Generator().manual_seed(1)
+    ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen)
+    seed_tok = int(torch.randint(0, cfg.vocab_size, (1,), generator=gen))
+    ids = torch.tensor([[seed_tok, *tok]])
+    mask = torch.from_numpy(tree_oracle.verification_attention_mask(par, args.ctx))[None, None]
+    pos = torch.from_numpy(tree_oracle.verification_position_ids(dep, args.ctx)).reshape(1, -1)
+    committed = []
     with torch.no_grad():
-        for p in layer.parameters():
-            p.normal_(0.0, 0.02, generator=gen)
-    rope = Qwen3MoeRotaryEmbedding(cfg)
-    head = torch.randn(cfg.vocab_size, cfg.hidden_size, generator=gen).mul_(0.02).to(torch.bfloat16)
-    ctx_h = torch.randn(1, args.ctx, cfg.hidden_size, generator=gen).to(torch.bfloat16)
-    x = torch.randn(1, q, cfg.hidden_size, generator=gen).to(torch.bfloat16)
-    mask = tree.verification_attention_mask(base_kv_length=args.ctx, device="cpu")
-    pos = tree.verification_position_ids(base_kv_length=args.ctx, device="cpu")
-    with torch.no_grad():
-        kv = DynamicCache(config=cfg)
-        cpos = torch.arange(args.ctx).unsqueeze(0)
-        layer(ctx_h, attention_mask=None, position_ids=cpos, past_key_values=kv, use_cache=True,
-              position_embeddings=rope(ctx_h, cpos))
-        pe = rope(x, pos)
+        cache = DynamicCache(config=cfg)
+        model(input_ids=ctx_ids, past_key_values=cache, use_cache=True)
 
-        def one_layer():
-            layer(x, attention_mask=mask, position_ids=pos, past_key_values=kv, use_cache=True,
-                  position_embeddings=pe)
-            kv.crop(args.ctx)
+        def step():
+            out = model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=cache,
+                        use_cache=True)
+            am = out.logits[0].argmax(-1).tolist()
+            cache.crop(args.ctx)
+            return len(tree_oracle.accepted_path(par, tok, am)) + 1
 
-        one_layer()
+        for _ in range(warmup):
+            step()
         t0 = time.perf_counter()
-        for _ in range(layers):
-            one_layer()
-        layer_s = (time.perf_counter() - t0) / layers
-        t0 = time.perf_counter()
-        torch.nn.functional.linear(x, head).argmax(-1)
-        head_s = time.perf_counter() - t0
-    per_pass = layer_s * args.layers + head_s
-    desc = (f"HF Qwen3MoeDecoderLayer (sdpa, stock MoE) x{layers} timed on CPU, scaled to "
-            f"{args.layers} layers, + lm_head; T={q}, ctx={args.ctx}, bf16")
-    return per_pass, desc, torch.get_num_threads()
+        for _ in range(steps):
+            committed.append(step())
+        elapsed = time.perf_counter() - t0
+    del model, cache
+    return elapsed / steps, sum(committed) / steps, torch.get_num_threads()
+
+
+def cpu_reference_sample(args, layers=1):
+    """Bounded sample of the reference's CPU path for the B200 arm's
+    ``cpu_baseline``: a ``layers``-layer model (two timed passes after one
+    warm-up) with the decoder-layer time scaled to ``args.layers`` layers; the
+    embedding + lm_head share is timed in the same way on a 0-layer model."""
+    t_n, _, cores = cpu_reference_run(args, layers, steps=2, warmup=1)
+    t_0, _, _ = cpu_reference_run(args, 0, steps=2, warmup=1)
+    per_pass = t_0 + (t_n - t_0) * args.layers / max(layers, 1)
+    desc = (f"stock HF Qwen3-MoE on the host cores, {layers} decoder layer(s) timed and scaled to "
+            f"{args.layers}, + embedding/norm/lm_head timed; T={1 + args.nodes}, ctx={args.ctx}, bf16")
+    return per_pass, desc, cores
 
 
 def b200_arm(args):
@@ -550,14 +707,44 @@ def b200_arm(args):
                           fwd=make_forward(loaded.model, args.hf_forward))
     build_s = time.perf_counter() - t_build
 
+    from specfit_b200.runtime import ExpertExecutionPolicy
+
+    h2d_peak = pinned_h2d_peak(pool, device)
+    policy = ExpertExecutionPolicy(args.policy)
+    loaded.set_expert_execution_policy(policy)
+    before: dict = {}
     launches0 = ops.LAUNCHES[0]
     with ClockSampler(device.index) as clocks:
-        ms, ams = timed_steps(runner.step_device, args.steps, args.warmup, world, device)
-    launches = (ops.LAUNCHES[0] - launches0) // (args.steps + args.warmup) * args.steps
+        ms, ams = timed_steps(runner.step_device, args.steps, args.warmup, world, device,
+                              on_start=lambda: before.update(loaded.cache_stats(),
+                                                             launches=ops.LAUNCHES[0]))
+    launches = ops.LAUNCHES[0] - before["launches"]
     committed = sum(len(tree.accepted_path(a.cpu().unsqueeze(0))) + 1 for a in ams)
     total_committed = sum_over_ranks(committed, world, device)
     value = total_committed / (ms / 1e3)
     stats24 = loaded.cache_stats()
+    timed_stats = {k: (stats24[k] - before[k]) / args.steps for k in stats24}
+    h2d_roofline = h2d_roofline_of(timed_stats, ms / args.steps, h2d_peak)
+
+    # The same passes under the other execution policy (outputs are the same:
+    # the canonical combine adds in expert-id order whatever the order the
+    # experts run in).
+    other = (ExpertExecutionPolicy.EXPERT_ID_ASCENDING if policy is ExpertExecutionPolicy.RESIDENT_FIRST
+             else ExpertExecutionPolicy.RESIDENT_FIRST)
+    loaded.set_expert_execution_policy(other)
+    obefore: dict = {}
+    oms, oams = timed_steps(runner.step_device, args.steps, args.warmup, world, device,
+                            on_start=lambda: obefore.update(loaded.cache_stats()))
+    ostats = loaded.cache_stats()
+    ostats = {k: (ostats[k] - obefore[k]) / args.steps for k in ostats}
+    assert all(torch.equal(a, ams[0]) for a in oams), "execution policies gave different argmaxes"
+    other_policy = {"execution_policy": other.value,
+                    "value": round(sum(len(tree.accepted_path(a.cpu().unsqueeze(0))) + 1 for a in oams)
+                                   / (oms / 1e3), 4),
+                    "unit": "tokens/s", "ms_per_step": round(oms / args.steps, 3),
+                    "cache_per_step": ostats,
+                    "h2d": h2d_roofline_of(ostats, oms / args.steps, h2d_peak)}
+    loaded.set_expert_execution_policy(policy)
 
     e2e_ms, e2e_comm = timed_steps(runner.step_e2e, args.steps, 1, world, device)
     e2e_total = sum_over_ranks(sum(e2e_comm), world, device)
@@ -595,18 +782,12 @@ def b200_arm(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random context tokens, seeded 64-node tree)",
-        "config": {
-            "workload": (f"BASELINE config 2: {args.layers}-layer Qwen3-30B-A3B-shaped verify pass over a "
-                         f"{args.nodes}-node tree (depth {args.depth}, branching <= {args.branch}), "
-                         f"{args.ctx}-token context, {args.slots} expert-cache slots per layer"),
-            "verify_tokens_per_step": 1 + args.nodes,
-            "slots_per_layer": args.slots,
-            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-            "l2_flush": "not needed: each step streams > 57 GB of expert weights (>> 126 MB L2)",
-            "forward": ("Hugging Face decoder layers" if args.hf_forward else
-                        "lean fused layer forward (runtime/lean_forward.py)"),
-        },
-        "cache_stats_after_timing": stats24,
+        "config": headline_config(args),
+        "forward": ("Hugging Face decoder layers" if args.hf_forward else
+                    "lean fused layer forward (runtime/lean_forward.py)"),
+        "execution_policy": policy.value,
+        "cache_per_step": timed_stats,
+        "other_policy": other_policy,
         "predicted_prefetch": {"value": round(pf_value, 4), "unit": "tokens/s",
                                "ms_per_step": round(pf_ms / args.steps, 3),
                                "predictions": "routes of the previous verify pass",
@@ -617,6 +798,7 @@ def b200_arm(args):
                 "ms_per_step": round(e2e_ms / args.steps, 3)},
         "clocks": clocks.summary(),
         "setup_s": round(build_s, 1),
+        "roofline": {"h2d": h2d_roofline},
     }
 
     if not args.no_resident and args.slots < cfg.num_experts:
@@ -689,7 +871,8 @@ def b200_arm(args):
             block = {"error": f"{type(err).__name__}: {err}"}
         result["moe_block"] = dict(block or {"error": "layer 0 slots not all resident"},
                                    eager_in_model=eager_block)
-        result["roofline"] = swiglu_roofline(loaded, device, 1 + args.nodes, peaks)
+        result["roofline"] = dict(swiglu_roofline(loaded, device, 1 + args.nodes, peaks) or {},
+                                  h2d=h2d_roofline)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         per_pass, desc, cores = cpu_reference_sample(args, layers=args.cpu_layers)
@@ -1173,28 +1356,40 @@ def decode_mode(args):
 
 
 def reference_arm(args):
+    """``--impl reference``: the reference's CPU path (``cpu_reference_run``)
+    on the B200 arm's workload.  The whole ``args.layers``-layer model is
+    materialised when the host has the memory for it (61 GB at 48 layers);
+    otherwise the largest layer count that fits is timed and scaled, and the
+    line says so."""
     rank, world, local = dist_info()
     if rank != 0:
         return
-    per = []
-    desc = cores = None
-    for i in range(args.warmup + args.steps):
-        per_pass, desc, cores = cpu_reference_sample(args, layers=args.cpu_layers)
-        if i >= args.warmup:
-            per.append(per_pass)
-    total = sum(per)
-    value = args.steps / total
+    import psutil
+
+    need = reference_model_bytes(args.layers)
+    avail = psutil.virtual_memory().available
+    if need * 1.15 + (8 << 30) <= avail:
+        per_pass, per_commit, cores = cpu_reference_run(args, args.layers, args.steps, args.warmup)
+        sample = (f"stock HF Qwen3-MoE, all {args.layers} decoder layers materialised on the host "
+                  f"({need / 1e9:.1f} GB bf16); every timed step is a full verify pass")
+        value = per_commit / per_pass
+    else:
+        fit = max(1, int((avail - (8 << 30)) / 1.15 - reference_model_bytes(0)) //
+                  (reference_model_bytes(1) - reference_model_bytes(0)))
+        fit = min(fit, args.layers, 8)
+        per_pass, sample, cores = cpu_reference_sample(args, layers=fit)
+        sample += f" (host has {avail / 1e9:.0f} GB available, the full model needs {need / 1e9:.0f} GB)"
+        value = 1.0 / per_pass
     print(json.dumps({
         "impl": "reference",
         "metric": "committed tokens/s (Qwen3-30B-A3B shape, bs1)",
         "value": round(value, 5), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 1),
+        "warmup": args.warmup, "ms_per_step": round(per_pass * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": {"workload": (
-            f"BASELINE config 2 on the host cores: {args.layers}-layer verify pass over a {args.nodes}-node "
-            f"tree, {args.ctx}-token context (sampled per step, see cpu_baseline.sample)")},
+        "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random context tokens, seeded 64-node tree)",
+        "config": headline_config(args),
         "cpu_baseline": {"value": round(value, 5), "unit": "tokens/s", "cores": cores, "kind": "reference",
-                         "sample": desc},
+                         "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

@@ -104,16 +104,24 @@ SF_API int sf_router_topk(const void* hidden, const void* router_weight, int dty
 
 /*
  * Allocation-free router: same contract and results as sf_router_topk, but it
- * takes no workspace.  Its scratch is a 2 MiB array compiled into the library
- * (one per GPU that loads it, held until the process exits), so callers that
- * cannot allocate device memory can still route: code running under CUDA
- * stream capture, plugins of a runtime that owns all device memory, and paths
- * that cannot afford cudaMalloc's device synchronisation.
+ * takes no workspace and allocates nothing.  It is for callers that cannot
+ * obtain device memory where they route: plugins loaded into a serving
+ * engine that reserves the GPU's memory for its own pools at start-up (a
+ * cudaMalloc there fails or fragments the engine's pool), hosts that bind
+ * this library through a plain C FFI and have no device allocator to carve
+ * a workspace from, and latency-critical paths where cudaMalloc's implicit
+ * device-wide synchronisation would stall every other stream.  Its scratch
+ * (the fp32 logits between the two router passes) is a 2 MiB array compiled
+ * into the library, which every GPU that loads the library holds until the
+ * process exits.
  *   - tokens * num_experts must not exceed sf_router_topk_noalloc_max_elems()
  *     (2^19); larger calls fail with SF_ERR_WORKSPACE and launch nothing.
- *   - The first call on a device looks up the array's device address (a CUDA
- *     runtime query, no allocation); make that first call before any stream
- *     capture.
+ *   - The first call on a device looks up the array's device address with
+ *     cudaGetSymbolAddress (a runtime query, no allocation) and keeps it for
+ *     that device; make that first call before any stream capture.  The
+ *     address belongs to the device's primary context: after
+ *     cudaDeviceReset the kept address is stale, so do not call this entry
+ *     point again in a process that has reset the device.
  *   - All calls on a device share the array: calls that may overlap on the
  *     GPU (different streams without ordering) race and must not be issued.
  *     Nothing in the array needs to start at zero; each call overwrites every
@@ -235,15 +243,17 @@ SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const si
  * key j is visible when j < prefix_len, or when bit (j - prefix_len) of
  * tree_bits[i * bit_words + ...] is set (little-endian uint32 words).
  * q: [Hq, Tq, D] with strides (q_head_stride, q_row_stride) in elements,
- * k/v: [Hkv, Tk, D] with (kv_head_stride, kv_row_stride), bf16, D == 128.
- * out: [Tq, Hq, D] bf16 (the layout the o_proj consumes).
+ * k/v: [Hkv, Tk, D] with (kv_head_stride, kv_row_stride), bf16.  D is 128
+ * for the tensor-core kernels; any multiple of 4 up to 128 on the CUDA-core
+ * kernel, which SF_ATTN_AUTO picks for D != 128.
+ * out: [Tq, Hq, D] bf16, 8-byte aligned (the layout the o_proj consumes).
  * workspace: sf_tree_attention_workspace_bytes(Hq, Tq, Tk) bytes.
  * Replaces SDPA under the verification mask (transformers/...:172-186 with
  * eagle3_types.py:450-473).
  */
 /* Implementation choice of sf_tree_attention_ex. */
 #define SF_ATTN_AUTO 0 /* tensor-core kernel when supported (D=128, q rows 4-byte and K/V rows 16-byte aligned), else CUDA cores */
-#define SF_ATTN_SIMT 1 /* CUDA-core split kernel */
+#define SF_ATTN_SIMT 1 /* CUDA-core split kernel (any D that is a multiple of 4, <= 128) */
 #define SF_ATTN_MMA 2  /* warp-level tensor-core (mma.sync) split kernel; SF_ERR_INVALID_ARGUMENT if unsupported */
 #define SF_ATTN_TCGEN05 3 /* tcgen05/TMEM kernel, K/V by TMA (D=128, 16-byte aligned q/k/v rows); SF_ERR_INVALID_ARGUMENT if unsupported */
 

@@ -555,15 +555,17 @@ extern "C" int sf_router_topk(const void* hidden, const void* router_weight, int
 // ---------------------------------------------------------------------------
 // Allocation-free router.
 //
-// Some callers cannot hand this library a workspace because they cannot
-// allocate device memory at the point of the call: code that runs while a
-// stream is being captured into a CUDA graph (cudaMalloc is not allowed
-// there), plugins hosted by a serving runtime that reserves the GPU's memory
-// for its own pools and gives extensions none, and latency-critical paths
-// where cudaMalloc's implicit device-wide synchronisation is unacceptable.
+// Some callers cannot hand this library a workspace because they cannot get
+// device memory at the point of the call: plugins loaded into a serving
+// engine that reserves the GPU's memory for its own pools at start-up (a
+// cudaMalloc there fails or fragments the engine's pool), hosts that bind the
+// library through a plain C FFI with no device allocator to carve a
+// workspace from, and latency-critical paths where cudaMalloc's implicit
+// device-wide synchronisation would stall every other stream.
 // sf_router_topk_noalloc serves them: its scratch (the fp32 logits between
 // the two router passes) is this file-scope device array, which every GPU
-// that loads the library holds until the process exits.
+// that loads the library holds until the process exits.  Calls on one device
+// share it, so calls that overlap on the GPU race.
 
 namespace sf {
 namespace {
@@ -578,8 +580,10 @@ std::mutex g_scratch_mu;
 float* g_scratch_ptr[kMaxDevices] = {};
 
 // Device address of g_router_scratch on the current device, looked up once
-// per device.  The host-side symbol is only a stand-in and must never be
-// passed to a kernel.
+// per device (the first call on a device, which must come before any stream
+// capture) and kept.  The host-side symbol is only a stand-in and must never
+// be passed to a kernel.  The kept address belongs to the device's primary
+// context and is stale after cudaDeviceReset.
 int router_scratch(float** out) {
   int dev = 0;
   SF_CHECK_CUDA(cudaGetDevice(&dev));

@@ -14,6 +14,12 @@
 // share the KV head, so each K/V tile is staged in shared memory once for all
 // of them.  Scores use an online softmax in fp32; a second kernel merges the
 // per-split partial results and writes bf16 [Tq, Hq, D].
+//
+// The tiles are laid out for head_dim 128 (the Qwen3-30B-A3B shape).  Smaller
+// head dims (a multiple of 4, e.g. the 8- and 16-wide heads of the tiny test
+// configurations) are staged with zeros past head_dim: the extra products are
+// exact zeros, so scores and outputs equal those of a D-wide kernel, and the
+// merge writes only the first head_dim dims of each output row.
 #include <math.h>
 
 #include <algorithm>
@@ -24,7 +30,7 @@
 namespace sf {
 namespace {
 
-constexpr int kD = 128;        // head_dim
+constexpr int kD = 128;        // tile width of head_dim (head_dim <= kD)
 constexpr int kRows = 8;       // query rows per CTA
 constexpr int kTile = 64;      // keys per shared-memory tile
 constexpr int kKPitch = kD + 2;  // bf16 pitch of the K tile (bank-conflict free)
@@ -65,7 +71,8 @@ tree_attn_split_kernel(Params p) {
     const int row = row0 + r;
     for (int d = lane; d < kD; d += 32) {
       __nv_bfloat16 qv = __float2bfloat16_rn(0.f);
-      if (head_ok && row < p.q_len) qv = p.q[(int64_t)head * p.q_hs + (int64_t)row * p.q_rs + d];
+      if (head_ok && row < p.q_len && d < p.head_dim)
+        qv = p.q[(int64_t)head * p.q_hs + (int64_t)row * p.q_rs + d];
       qw[r * kD + d] = qv;
     }
   }
@@ -87,7 +94,7 @@ tree_attn_split_kernel(Params p) {
       const int key = i / (kD / 4);
       const int d4 = (i % (kD / 4)) * 4;
       uint2 kv = make_uint2(0, 0), vv = make_uint2(0, 0);
-      if (key < nk) {
+      if (key < nk && d4 < p.head_dim) {
         const int64_t off = (int64_t)kvh * p.kv_hs + (int64_t)(t0 + key) * p.kv_rs + d4;
         kv = *reinterpret_cast<const uint2*>(p.k + off);
         vv = *reinterpret_cast<const uint2*>(p.v + off);
@@ -235,7 +242,8 @@ __global__ void tree_attn_merge_kernel(Params p, __nv_bfloat16* __restrict__ out
     }
   }
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
-  __nv_bfloat16* dst = out + ((int64_t)row * p.num_heads + head) * kD + lane * 4;
+  if (lane * 4 >= p.head_dim) return;
+  __nv_bfloat16* dst = out + ((int64_t)row * p.num_heads + head) * p.head_dim + lane * 4;
   __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
   __nv_bfloat162 hi = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
   uint2 packed;
@@ -268,7 +276,8 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
                                     int64_t kv_row_stride, float scale, void* out, void* workspace,
                                     size_t workspace_bytes, int impl, void* stream) {
   using namespace sf;
-  SF_CHECK_ARG(head_dim == kD, "head_dim must be 128");
+  SF_CHECK_ARG(head_dim > 0 && head_dim <= kD && head_dim % 4 == 0,
+               "head_dim must be a multiple of 4 in [4, 128]");
   SF_CHECK_ARG(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
                "num_heads must be a positive multiple of num_kv_heads");
   SF_CHECK_ARG(num_heads / num_kv_heads <= kMaxGroup, "at most 8 query heads per KV head");
@@ -299,6 +308,7 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
   p.num_heads = num_heads;
   p.num_kv_heads = num_kv_heads;
   p.group = num_heads / num_kv_heads;
+  p.head_dim = head_dim;
   p.q_hs = q_head_stride;
   p.q_rs = q_row_stride;
   p.kv_hs = kv_head_stride;
@@ -337,6 +347,7 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
     return SF_OK;
   }
   SF_CHECK_ARG(impl != SF_ATTN_MMA, "the tensor-core tree attention does not support this layout");
+  SF_CHECK_ARG((reinterpret_cast<uintptr_t>(out) & 7u) == 0, "out must be 8-byte aligned");
   dim3 grid((unsigned)num_kv_heads, (unsigned)((q_len + kRows - 1) / kRows), (unsigned)p.splits);
   const size_t smem = (size_t)(kTile * kD + kTile * kKPitch + kMaxGroup * kRows * kD) * 2;
   static std::atomic<unsigned long long> configured{0};

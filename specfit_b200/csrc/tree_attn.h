@@ -16,6 +16,7 @@ struct AttnParams {
   int bit_words;
   int q_len, kv_len, prefix_len;
   int num_heads, num_kv_heads, group;
+  int head_dim;  // <= 128; the split kernels zero-fill dims past it
   int64_t q_hs, q_rs, kv_hs, kv_rs;
   float scale;
   int splits, keys_per_split;

@@ -23,7 +23,7 @@ from .. import synthetic
 from .expert_parallel import ExpertParallelMoE
 from .moe_block import Qwen3B200SparseMoeBlock, Qwen3B200TopKRouter
 from .qwen3_verifier import materialize_random_, qwen3_moe_config
-from .tree_attention import ATTN_IMPL, register as register_attention
+from .tree_attention import install as install_tree_attention
 
 
 class ExpertParallelExperts(nn.Module):
@@ -94,9 +94,8 @@ def build_random_ep_qwen3(*, device, rank: int, world: int, group=None,
     from transformers import Qwen3MoeForCausalLM
 
     device = torch.device(device)
-    register_attention()
     cfg = config if config is not None else qwen3_moe_config(num_layers)
-    cfg._attn_implementation = ATTN_IMPL
+    cfg._attn_implementation = "sdpa"
     hidden, inter = cfg.hidden_size, cfg.moe_intermediate_size
     if cfg.num_experts % world:
         raise ValueError("the experts must shard evenly over the ranks")
@@ -114,4 +113,5 @@ def build_random_ep_qwen3(*, device, rank: int, world: int, group=None,
                                 hidden_size=hidden, intermediate_size=inter, local_storage=blocks[l],
                                 rank=rank, world=world, group=group)
         layer.mlp.experts = ExpertParallelExperts(l, moe)
+    install_tree_attention(model)
     return LoadedEpQwen3(model, rank, world)

@@ -325,7 +325,7 @@ def load_offloaded_qwen3(model_root, *, device, slots_per_layer: int, packed_che
     from .moe_block import Qwen3B200SparseMoeBlock, Qwen3B200TopKRouter
     from .qwen3_offloaded_experts import Qwen3OffloadedExperts
     from .qwen3_verifier import ExpertHostPool, LoadedB200Qwen3
-    from .tree_attention import ATTN_IMPL, register as register_attention
+    from .tree_attention import install as install_tree_attention
 
     if type(h2d_prefetch) is not bool:
         raise ValueError("h2d_prefetch must be a boolean")
@@ -355,11 +355,10 @@ def load_offloaded_qwen3(model_root, *, device, slots_per_layer: int, packed_che
         raise ValueError(f"slots_per_layer must be in [1, {cfg.num_experts}]")
     if cfg.mlp_only_layers or getattr(cfg, "decoder_sparse_step", 1) != 1:
         raise ValueError("P0 loader requires an MoE block in every layer")
-    if attn_implementation == "sdpa":
-        register_attention()
-        cfg._attn_implementation = ATTN_IMPL
-    else:
-        cfg._attn_implementation = attn_implementation
+    # The model's config keeps the requested implementation ("sdpa" by
+    # default, which the reference speculator requires); with "sdpa" the
+    # decoder layers' attention is then routed to the tree kernel.
+    cfg._attn_implementation = attn_implementation
 
     L, E = cfg.num_hidden_layers, cfg.num_experts
     H, I = cfg.hidden_size, cfg.moe_intermediate_size
@@ -419,6 +418,8 @@ def load_offloaded_qwen3(model_root, *, device, slots_per_layer: int, packed_che
     model.model.rotary_emb = type(model.model.rotary_emb)(config=cfg, device=dev)
     if (root / "generation_config.json").exists():
         model.generation_config = GenerationConfig.from_pretrained(root, local_files_only=True)
+    if attn_implementation == "sdpa":
+        install_tree_attention(model)
     model.requires_grad_(False)
     model.eval()
     torch.cuda.synchronize(dev)

@@ -29,7 +29,7 @@ from .gpu_expert_cache import GpuExpertCache
 from .moe_block import Qwen3B200SparseMoeBlock, Qwen3B200TopKRouter
 from .qwen3_offloaded_experts import ExpertExecutionPolicy, Qwen3OffloadedExperts, ReductionMode
 from .state import ExpertKey
-from .tree_attention import ATTN_IMPL, register as register_attention
+from .tree_attention import install as install_tree_attention
 
 
 def qwen3_moe_config(num_layers: int = synthetic.NUM_LAYERS, *, hidden: int = synthetic.HIDDEN,
@@ -243,9 +243,8 @@ def build_random_offloaded_qwen3(*, device, slots_per_layer: int, num_layers: in
     from transformers import Qwen3MoeForCausalLM
 
     device = torch.device(device)
-    register_attention()
     cfg = config if config is not None else qwen3_moe_config(num_layers)
-    cfg._attn_implementation = ATTN_IMPL
+    cfg._attn_implementation = "sdpa"
     hidden, inter = cfg.hidden_size, cfg.moe_intermediate_size
     if pool is None:
         pool = ExpertHostPool(cfg.num_hidden_layers, cfg.num_experts, 3 * hidden * inter, dtype)
@@ -264,4 +263,5 @@ def build_random_offloaded_qwen3(*, device, slots_per_layer: int, num_layers: in
         layer.mlp = Qwen3B200SparseMoeBlock(gate, experts)
         caches.append(cache)
     materialize_random_(model, cfg, device, seed, std, dtype)
+    install_tree_attention(model)
     return LoadedB200Qwen3(model, tuple(caches), pool)

@@ -1,10 +1,16 @@
 """Tree-masked attention registered as a Hugging Face attention function.
 
 The reference runs the verify pass through SDPA with a 4-D boolean mask
-(``src/specfit/runtime/eagle3_tree.py:1243-1250``; SDPA is required,
-:922-923).  Registering ``tree_attention_forward`` under ``ATTN_IMPL`` makes
-``Qwen3MoeAttention`` (transformers/models/qwen3_moe/modeling_qwen3_moe.py:
-172-186) call ``sf_tree_attention`` instead, with the same inputs: query
+(``src/specfit/runtime/eagle3_tree.py:1243-1250``) and its speculator refuses
+any model whose ``config._attn_implementation`` is not ``"sdpa"``
+(``eagle3_tree.py:922-923``).  ``install`` keeps that contract: the model's
+config still reads ``"sdpa"`` (so Hugging Face prepares SDPA-style masks and
+the reference speculator accepts the model), while every decoder layer's
+attention module holds a config view whose implementation is ``ATTN_IMPL``,
+under which ``tree_attention_forward`` is registered.  ``Qwen3MoeAttention``
+(transformers/models/qwen3_moe/modeling_qwen3_moe.py:172-186) looks its
+attention function up from its own ``self.config``, so it calls
+``sf_tree_attention`` with the same inputs SDPA would get: query
 ``[B, Hq, T, D]``, key/value ``[B, Hkv, Tk, D]`` after the cache update, and
 the mask as prepared by the caller (a 4-D mask is passed through unchanged).
 
@@ -15,6 +21,7 @@ cached prefix (prefill and plain decode).
 """
 from __future__ import annotations
 
+import copy
 import weakref
 
 import torch
@@ -84,3 +91,28 @@ def register() -> str:
 
     AttentionInterface.register(ATTN_IMPL, tree_attention_forward)
     return ATTN_IMPL
+
+
+def install(model) -> None:
+    """Route the attention of every decoder layer of a Hugging Face Qwen3-MoE
+    model (``model.model.layers[i].self_attn``) through ``sf_tree_attention``
+    while ``model.config._attn_implementation`` stays ``"sdpa"``.
+
+    The attention modules share one shallow copy of the model config that
+    differs only in ``_attn_implementation``; everything else the modules
+    read from it (head counts, dims, dropout) is the model's own value."""
+    register()
+    cfg = model.config
+    if cfg._attn_implementation != "sdpa":
+        cfg._attn_implementation = "sdpa"
+    view = copy.copy(cfg)
+    view._attn_implementation = ATTN_IMPL
+    for layer in model.model.layers:
+        layer.self_attn.config = view
+
+
+def installed(model) -> bool:
+    """Whether ``install`` routed ``model``'s attention to the tree kernel."""
+    layers = model.model.layers
+    return bool(layers) and all(
+        getattr(l.self_attn.config, "_attn_implementation", None) == ATTN_IMPL for l in layers)

@@ -1,8 +1,10 @@
 """Import shim that lets the SpecFit reference be imported in a container
 without its two absent third-party packages.
 
-Used only by ``make_golden.py`` (fixture generation, run where the reference
-source tree is present). Nothing on the product path imports it.
+Used by ``make_golden.py`` (fixture generation) and by the CPU test that
+constructs the reference speculator around this package's model
+(``tests/test_attention_install.py``), both run where the reference source
+tree is present.  Nothing on the product path imports it.
 
 * ``speculators`` 0.5.0 (pinned by the reference's requirements-test.txt:8)
   supplies the EAGLE-3 drafter; the reference imports it in

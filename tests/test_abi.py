@@ -32,9 +32,10 @@ def test_argument_errors_are_reported_before_any_launch():
         assert "top_k" in str(err)
     else:  # pragma: no cover
         raise AssertionError("ValueError expected")
-    rc = _native.lib.sf_tree_attention(None, None, None, None, 0, 1, 1, 0, 32, 4, 64, 0, 0, 0, 0,
-                                       1.0, None, None, 0, None)
-    assert rc == _native.SF_ERR_INVALID_ARGUMENT and "head_dim" in _native.last_error()
+    for head_dim in (130, 6, 0):  # above 128, not a multiple of 4, empty
+        rc = _native.lib.sf_tree_attention(None, None, None, None, 0, 1, 1, 0, 32, 4, head_dim, 0, 0, 0,
+                                           0, 1.0, None, None, 0, None)
+        assert rc == _native.SF_ERR_INVALID_ARGUMENT and "head_dim" in _native.last_error()
 
 
 def test_peer_layout_is_consistent():

@@ -336,6 +336,32 @@ def test_tree_attention_vs_oracle(ops, nodes, depth, ctx, impl):
     assert torch.equal(packed, bits)
 
 
+@pytest.mark.parametrize("hq,hkv,dim", [(4, 2, 8), (4, 2, 16), (32, 4, 64), (8, 1, 100)])
+@pytest.mark.parametrize("nodes,ctx", [(4, 2), (64, 300), (0, 70)])
+def test_tree_attention_small_head_dims_vs_oracle(ops, hq, hkv, dim, nodes, ctx):
+    """Head dims below 128 (the tiny Qwen3-MoE test configurations use 8 and
+    16) run on the CUDA-core kernel, with AUTO choosing it, against the fp64
+    oracle; every output column past head_dim stays untouched."""
+    parents = synthetic.random_tree(nodes, max_depth=6, max_branch=4, seed=nodes)[1] if nodes else ()
+    tq = 1 + len(parents)
+    tk = ctx + tq
+    gen = torch.Generator().manual_seed(dim + nodes)
+    q = torch.randn(hq, tq, dim, generator=gen).to(torch.bfloat16)
+    k = torch.randn(hkv, tk, dim, generator=gen).to(torch.bfloat16)
+    v = torch.randn(hkv, tk, dim, generator=gen).to(torch.bfloat16)
+    bits = ops.tree_bits_from_parents(parents, DEV)
+    mask = to.verification_attention_mask(parents, ctx)
+    ref = to.tree_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), mask)
+    for impl in (0, 1):
+        out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), bits, ctx, impl=impl)
+        assert out.shape == (tq, hq, dim)
+        got = out.float().cpu().numpy().transpose(1, 0, 2)
+        assert np.abs(got - ref).max() <= ATOL_BF16
+        assert cosine(got, ref) >= COS_MIN
+    with pytest.raises(ValueError, match="head_dim"):
+        ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), bits, ctx, impl=2)
+
+
 @pytest.mark.parametrize("impl", [1, 2, ATTN_TCGEN05])
 def test_tree_attention_strided_views(ops, impl):
     """Inputs as HF lays them out: q from a [1, T, Hq*D] projection viewed as

@@ -193,3 +193,59 @@ def test_gpu_source_and_packed_loads_give_equal_logits():
     assert torch.isfinite(logits[0]).all()
     assert torch.equal(logits[0], logits[1])
     assert torch.equal(logits[0], logits[2])
+    # Stock Hugging Face (SDPA attention, stock experts) on the same files.
+    from transformers import Qwen3MoeForCausalLM
+
+    ref = Qwen3MoeForCausalLM.from_pretrained(FIXTURE / "source", dtype=torch.bfloat16,
+                                              attn_implementation="sdpa").to(dev).eval()
+    with torch.no_grad():
+        theirs = ref(input_ids=ctx, past_key_values=DynamicCache(config=ref.config),
+                     use_cache=True).logits[0].float().cpu()
+    assert (logits[0] - theirs).abs().max().item() <= 2e-2
+    cos = torch.nn.functional.cosine_similarity(logits[0], theirs, dim=-1)
+    assert cos.min().item() >= 0.999
+
+
+@pytest.mark.gpu
+def test_gpu_loaded_model_reads_sdpa_and_runs_the_tree_kernel():
+    """The loaded model's config reports "sdpa" (the reference speculator's
+    requirement, eagle3_tree.py:922-923) while every layer's attention calls
+    the tree kernel; a 4-D tree mask gives the same logits as stock SDPA."""
+    from transformers import DynamicCache, Qwen3MoeForCausalLM
+
+    from specfit_b200.runtime.qwen3_loader import load_offloaded_qwen3
+    from specfit_b200.runtime.tree_attention import installed
+
+    dev = torch.device("cuda:0")
+    loaded = load_offloaded_qwen3(FIXTURE / "source", device=dev, slots_per_layer=4)
+    ref = Qwen3MoeForCausalLM.from_pretrained(FIXTURE / "source", dtype=torch.bfloat16,
+                                              attn_implementation="sdpa").to(dev).eval()
+    try:
+        assert loaded.model.config._attn_implementation == "sdpa"
+        assert installed(loaded.model)
+        ctx = torch.randint(0, 100, (1, 9), generator=torch.Generator().manual_seed(5)).to(dev)
+        ids = torch.tensor([[3, 17, 40, 41, 8]], device=dev)
+        parents = (0, 1, 1, 2)  # seed row 0, nodes 1..4
+        visible = torch.zeros(5, 9 + 5, dtype=torch.bool)
+        visible[:, :9] = True
+        for i in range(5):
+            n = i
+            while True:
+                visible[i, 9 + n] = True
+                if n == 0:
+                    break
+                n = parents[n - 1]
+        mask = visible[None, None].to(dev)
+        pos = torch.tensor([[9, 10, 11, 11, 12]], device=dev)
+        outs = []
+        for model in (loaded.model, ref):
+            cache = DynamicCache(config=model.config)
+            with torch.no_grad():
+                model(input_ids=ctx, past_key_values=cache, use_cache=True)
+                outs.append(model(input_ids=ids, attention_mask=mask, position_ids=pos,
+                                  past_key_values=cache, use_cache=True).logits[0].float().cpu())
+        assert (outs[0] - outs[1]).abs().max().item() <= 2e-2
+        cos = torch.nn.functional.cosine_similarity(outs[0], outs[1], dim=-1)
+        assert cos.min().item() >= 0.999
+    finally:
+        loaded.close()

@@ -1,11 +1,13 @@
 """The allocation-free router entry point, called through the C ABI.
 
-``sf_router_topk_noalloc`` exists for callers that cannot allocate device
-memory at the call site (code under CUDA stream capture, plugins of runtimes
-that keep all device memory for their own pools, paths that cannot take
-cudaMalloc's synchronisation).  It must give exactly what the workspace
-entry point ``sf_router_topk`` gives, on consecutive calls that reuse its
-built-in scratch, and refuse sizes beyond that scratch.
+``sf_router_topk_noalloc`` serves callers that cannot allocate device memory
+where they route: plugins of a serving engine that keeps the GPU's memory for
+its own pools, hosts binding the library through a plain C FFI without a
+device allocator, and paths that cannot take cudaMalloc's device-wide
+synchronisation.  It runs the same kernels as the workspace entry point
+``sf_router_topk`` with its scratch in an array built into the library, so
+on consecutive calls that reuse that array its four outputs must equal the
+workspace entry point's bit for bit; sizes beyond the array are refused.
 
 This file is collected last on purpose: it runs after every other test of a
 full run and also passes alone in a fresh process.
@@ -71,10 +73,15 @@ def test_noalloc_router_matches_workspace_router_on_consecutive_calls(dtype):
         ref = _call_with_workspace(N, x, w, 8)
         got = _call_noalloc(N, x, w, 8)
         torch.cuda.synchronize()
-        assert torch.equal(got[2], ref[2]), "expert indices differ"
-        np.testing.assert_allclose(got[1].cpu().numpy(), ref[1].cpu().numpy(), rtol=1e-5, atol=1e-7)
-        np.testing.assert_allclose(got[0].cpu().numpy(), ref[0].cpu().numpy(), rtol=1e-5, atol=1e-8)
-        assert torch.equal(got[3], ref[3]), "rounded logits differ"
+        for name, a, b in zip(("probs", "weights", "indices", "logits"), got, ref):
+            assert torch.equal(a, b), f"{name} differ from sf_router_topk"
+        if tokens == 65:
+            # The indices also equal the CPU restatement of the router.
+            from oracle import moe_oracle as mo
+
+            _, _, idx, _ = mo.router_topk(x.float().cpu().numpy(), w.float().cpu().numpy(), 8, True,
+                                          "bf16" if dtype == torch.bfloat16 else "f32")
+            assert np.array_equal(got[2].cpu().numpy(), idx)
 
 
 def test_noalloc_router_rejects_sizes_beyond_its_scratch():
