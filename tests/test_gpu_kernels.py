@@ -358,7 +358,7 @@ def test_tree_attention_small_head_dims_vs_oracle(ops, hq, hkv, dim, nodes, ctx)
         got = out.float().cpu().numpy().transpose(1, 0, 2)
         assert np.abs(got - ref).max() <= ATOL_BF16
         assert cosine(got, ref) >= COS_MIN
-    with pytest.raises(ValueError, match="head_dim"):
+    with pytest.raises(ValueError, match="does not support"):  # the mma.sync kernel is D = 128 only
         ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), bits, ctx, impl=2)
 
 
