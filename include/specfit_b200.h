@@ -56,6 +56,8 @@ extern "C" {
 #define SF_ERR_CUDA 2             /* a CUDA runtime call failed */
 #define SF_ERR_UNSUPPORTED 3      /* shape/dtype/device not supported */
 #define SF_ERR_WORKSPACE 4        /* workspace too small */
+#define SF_ERR_STATE 5            /* object state forbids the call (maps to RuntimeError) */
+#define SF_ERR_NO_SLOT 6          /* every expert-cache slot is leased (NoEvictableSlotError) */
 
 /* Element types. */
 #define SF_DTYPE_F32 0
@@ -237,6 +239,111 @@ SF_API int sf_moe_combine(const void* out_sorted, int dtype, const int32_t* inv_
  */
 SF_API int sf_slot_fill_batch(void* const* dst, const void* const* src, const size_t* bytes, int n,
                        void* stream);
+
+/*
+ * Expert-slot cache manager (host bookkeeping + fills).  Replaces the slot
+ * bookkeeping of GpuExpertCache (src/specfit/runtime/gpu_expert_cache.py:
+ * 196-266 acquire, 495-541 victim choice, 543-609 fills and their
+ * publication, 684-718 release).  One manager per cache: `slots` device
+ * slots of `slot_bytes` each at `storage`, `experts` page-locked host
+ * sources (source order), fills on `copy_stream`.  Experts are addressed by
+ * their index in source order; ready events are cudaEvent_t handles owned by
+ * the caller (one fresh, already-created event per potential miss), recorded
+ * here right behind each fill.  Use guards are events owned by the manager.
+ *
+ * sf_cache_acquire processes `experts[0..n)` in order, as n single acquires:
+ *   SF_CACHE_ACQUIRE       LRU victim among unleased slots (the fill queues
+ *                          behind the victim's readers); stops at the first
+ *                          expert with no unleased slot: SF_ERR_NO_SLOT if
+ *                          nothing was granted, else the grants so far;
+ *   SF_CACHE_NONBLOCKING   LRU victim among slots whose fill and readers are
+ *                          done, else not granted;
+ *   SF_CACHE_RESIDENT_ONLY hits and joins only;
+ *   SF_CACHE_PROBABILITY   as NONBLOCKING with the lowest-probability victim
+ *                          below the incoming expert's (`probabilities`
+ *                          indexed by expert).
+ * Each grant holds a lease (touched now unless `defer_touch`).  Leases are
+ * checked by (expert, slot, generation); sf_cache_wait orders `stream` after
+ * the slot's fill, sf_cache_release records a use guard on every stream that
+ * used the slot.  Not thread-safe across managers sharing a copy stream.
+ * No counterpart in the reference's ABI (the reference is Python).
+ */
+#define SF_CACHE_ACQUIRE 0
+#define SF_CACHE_NONBLOCKING 1
+#define SF_CACHE_RESIDENT_ONLY 2
+#define SF_CACHE_PROBABILITY 3
+#define SF_GRANT_NONE 0
+#define SF_GRANT_HIT 1
+#define SF_GRANT_JOIN 2
+#define SF_GRANT_MISS 3
+#define SF_CACHE_RESET_COLD 0    /* empty slots, generations and counters zeroed */
+#define SF_CACHE_RESET_DISCARD 1 /* empty slots, generations advanced, counters kept */
+#define SF_SLOT_EXPERT 0
+#define SF_SLOT_GENERATION 1
+#define SF_SLOT_STAMP 2
+#define SF_SLOT_READY 3
+#define SF_SLOT_GUARDS 4
+
+typedef struct {
+  int32_t kind;        /* SF_GRANT_* */
+  int32_t slot;
+  uint32_t generation;
+  int32_t victim;      /* evicted expert index, -1 none */
+  int64_t submission;  /* fill submission number (miss, join), else -1 */
+  uint64_t ready_event;
+} SfCacheGrant;
+
+typedef struct {
+  int64_t h2d_submissions, resident_hits, inflight_joins, evictions, pending_use_guards;
+  int64_t sequence, submission_sequence, state_version, outstanding_fills;
+} SfCacheCounters;
+
+typedef struct {
+  int32_t expert;      /* -1 empty */
+  uint32_t generation;
+  int32_t leases;
+  int32_t guards;          /* use guards held */
+  int64_t stamp;           /* last-used sequence */
+  uint64_t ready_event;
+  int32_t guards_pending;  /* of which not yet complete */
+  int32_t pad;
+} SfCacheSlot;
+
+typedef struct {
+  int32_t expert, slot;
+  uint32_t generation;
+  int32_t done;
+  int64_t submission;
+  uint64_t ready_event;
+} SfCacheFill;
+
+SF_API int sf_cache_create(int slots, int experts, void* storage, size_t slot_bytes,
+                           const void* const* sources, void* copy_stream, void** out);
+SF_API void sf_cache_destroy(void* cache);
+SF_API int sf_cache_set_copy_stream(void* cache, void* stream);
+SF_API int sf_cache_acquire(void* cache, const int32_t* experts, int n, int mode, int defer_touch,
+                            const uint64_t* fresh_events, const float* probabilities,
+                            SfCacheGrant* grants, int* granted);
+SF_API int sf_cache_touch(void* cache, int32_t expert, int32_t slot, uint32_t generation);
+SF_API int sf_cache_check(void* cache, int32_t expert, int32_t slot, uint32_t generation);
+SF_API int sf_cache_wait(void* cache, int32_t expert, int32_t slot, uint32_t generation, void* stream,
+                         int touch);
+SF_API int sf_cache_release(void* cache, int32_t expert, int32_t slot, uint32_t generation,
+                            const uint64_t* streams, int n_streams);
+/* refresh: bit 0 publishes completed fills, bit 1 drops completed use guards. */
+SF_API int sf_cache_state(void* cache, int refresh, SfCacheCounters* counters, SfCacheSlot* slots,
+                          int32_t* where, int32_t* home, int64_t* fill_seq);
+SF_API int sf_cache_fills(void* cache, SfCacheFill* out, int capacity, int* n);
+SF_API int sf_cache_quiescent(void* cache, int* quiescent);
+/* table[e] = slot of expert e when every expert is resident and slots >= experts. */
+SF_API int sf_cache_resident_table(void* cache, int32_t* table, int* complete);
+SF_API int sf_cache_add_hits(void* cache, int64_t hits);
+SF_API int sf_cache_reset(void* cache, int mode);
+SF_API int sf_cache_slot_edit(void* cache, int32_t slot, int field, int64_t value);
+SF_API int sf_cache_forget(void* cache, int which);
+SF_API int sf_cache_set_version(void* cache, int64_t version);
+SF_API int sf_cache_export(void* cache, void* image, size_t capacity, size_t* needed);
+SF_API int sf_cache_import(void* cache, const void* image, size_t size);
 
 /*
  * Tree attention (GQA): for query row i of head h (kv head h / (Hq/Hkv)),

@@ -20,6 +20,24 @@ SF_ERR_INVALID_ARGUMENT = 1
 SF_ERR_CUDA = 2
 SF_ERR_UNSUPPORTED = 3
 SF_ERR_WORKSPACE = 4
+SF_ERR_STATE = 5
+SF_ERR_NO_SLOT = 6
+
+SF_CACHE_ACQUIRE = 0
+SF_CACHE_NONBLOCKING = 1
+SF_CACHE_RESIDENT_ONLY = 2
+SF_CACHE_PROBABILITY = 3
+SF_GRANT_NONE = 0
+SF_GRANT_HIT = 1
+SF_GRANT_JOIN = 2
+SF_GRANT_MISS = 3
+SF_CACHE_RESET_COLD = 0
+SF_CACHE_RESET_DISCARD = 1
+SF_SLOT_EXPERT = 0
+SF_SLOT_GENERATION = 1
+SF_SLOT_STAMP = 2
+SF_SLOT_READY = 3
+SF_SLOT_GUARDS = 4
 
 SF_DTYPE_F32 = 0
 SF_DTYPE_BF16 = 1
@@ -54,6 +72,29 @@ class EpPeer(ctypes.Structure):
 
 
 _peer_p = ctypes.POINTER(EpPeer)
+_u32 = ctypes.c_uint32
+_u64 = ctypes.c_uint64
+
+
+class SfCacheGrant(ctypes.Structure):
+    _fields_ = [("kind", _i32), ("slot", _i32), ("generation", _u32), ("victim", _i32),
+                ("submission", _i64), ("ready_event", _u64)]
+
+
+class SfCacheCounters(ctypes.Structure):
+    _fields_ = [(name, _i64) for name in (
+        "h2d_submissions", "resident_hits", "inflight_joins", "evictions", "pending_use_guards",
+        "sequence", "submission_sequence", "state_version", "outstanding_fills")]
+
+
+class SfCacheSlot(ctypes.Structure):
+    _fields_ = [("expert", _i32), ("generation", _u32), ("leases", _i32), ("guards", _i32),
+                ("stamp", _i64), ("ready_event", _u64), ("guards_pending", _i32), ("pad", _i32)]
+
+
+class SfCacheFill(ctypes.Structure):
+    _fields_ = [("expert", _i32), ("slot", _i32), ("generation", _u32), ("done", _i32),
+                ("submission", _i64), ("ready_event", _u64)]
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -76,6 +117,25 @@ SIGNATURES = {
     "sf_grouped_swiglu_gathered": (_i32, [_vp, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
                                           _i32, _i32, _i32, _vp, _vp, _vp]),
     "sf_moe_combine": (_i32, [_vp, _i32, _vp, _vp, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "sf_cache_create": (_i32, [_i32, _i32, _vp, _sz, _vp, _vp, ctypes.POINTER(_vp)]),
+    "sf_cache_destroy": (None, [_vp]),
+    "sf_cache_set_copy_stream": (_i32, [_vp, _vp]),
+    "sf_cache_acquire": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, ctypes.POINTER(_i32)]),
+    "sf_cache_touch": (_i32, [_vp, _i32, _i32, _u32]),
+    "sf_cache_check": (_i32, [_vp, _i32, _i32, _u32]),
+    "sf_cache_wait": (_i32, [_vp, _i32, _i32, _u32, _vp, _i32]),
+    "sf_cache_release": (_i32, [_vp, _i32, _i32, _u32, _vp, _i32]),
+    "sf_cache_state": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "sf_cache_fills": (_i32, [_vp, _vp, _i32, ctypes.POINTER(_i32)]),
+    "sf_cache_quiescent": (_i32, [_vp, ctypes.POINTER(_i32)]),
+    "sf_cache_resident_table": (_i32, [_vp, _vp, ctypes.POINTER(_i32)]),
+    "sf_cache_add_hits": (_i32, [_vp, _i64]),
+    "sf_cache_reset": (_i32, [_vp, _i32]),
+    "sf_cache_slot_edit": (_i32, [_vp, _i32, _i32, _i64]),
+    "sf_cache_forget": (_i32, [_vp, _i32]),
+    "sf_cache_set_version": (_i32, [_vp, _i64]),
+    "sf_cache_export": (_i32, [_vp, _vp, _sz, ctypes.POINTER(_sz)]),
+    "sf_cache_import": (_i32, [_vp, _vp, _sz]),
     "sf_slot_fill_batch": (_i32, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
                                   _i32, _vp]),
     "sf_specfit_select": (_i32, [_i32, _vp, _vp, _vp, _i32, _vp, _vp, _i32, ctypes.c_double,
@@ -157,6 +217,8 @@ def check(status: int, what: str) -> None:
     msg = last_error()
     if status == SF_ERR_INVALID_ARGUMENT:
         raise ValueError(f"{what}: {msg}")
+    if status == SF_ERR_STATE:
+        raise RuntimeError(msg)
     raise NativeError(f"{what} failed (status {status}): {msg}")
 
 

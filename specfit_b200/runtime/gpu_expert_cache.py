@@ -1,82 +1,54 @@
-"""GPU expert cache: fixed device slots filled from pinned host copies.
+"""GPU expert cache: a Python face over the native slot manager.
 
 Drop-in for ``GpuExpertCache`` (``src/specfit/runtime/gpu_expert_cache.py``):
-same constructor, public methods, error types and messages, statistics and
-observer events, and the private members other modules of the reference
-touch.  Semantics kept:
+same constructor, public methods, error types and messages, statistics,
+observer records and snapshots, and the private members other modules of
+the reference read or edit (``_slots``, ``_resident``, ``_inflight``,
+``_outstanding_transfers``, ``_submission_sequence``, ``_state_version``,
+``_sources``, ``_lock``, ``_prefetch``, ``_prefetch_nonblocking``, the
+checkpoint hooks).
 
-* victim = the unleased slot minimising (occupied, last_used_sequence,
-  slot_id) (:495-518); ``ready_only`` probing additionally needs the slot's
-  fill and its readers' use events complete (:497-508);
-* a miss bumps the slot generation, makes the copy stream wait for the
-  previous readers' use events, copies the pinned source on the copy stream
-  and records the slot's ready event (:543-589);
-* finished copies become resident when polled in submission order (:591-609);
-* leases pin a slot generation; release records a use event on every
-  consumer stream (:684-718).
+Where the work happens.  All slot bookkeeping — which slot an expert is in,
+generations, the LRU order, fill submission and publication, use guards,
+counters — lives in the native manager (``csrc/expert_cache.cu``, C ABI
+``sf_cache_*``).  This class owns the tensors (device slots, page-locked
+sources), the ``torch.cuda.Event`` objects that stand for fills, the
+observer calls, and translation between expert keys and the manager's
+expert indices.  The private members above are *views* that read the
+manager's state and write edits through to it, so code that clears
+``_resident`` or edits a slot's ``generation`` keeps working.
 
-What is new here:
+Additions over the reference:
 
-* the copy is issued through ``sf_slot_fill_batch`` (one ``cudaMemcpyAsync``
-  per slot on the copy stream);
-* ``storage`` / ``slot_stride`` expose the slot array to the grouped SwiGLU
-  kernel, which reads expert weights straight from their slots;
-* ``device_slot_table()``: when every source is resident and nothing is in
-  flight (capacity >= sources), the slot of each expert is fixed, so the MoE
-  block can run with no host synchronisation at all.  Hits in that mode are
-  counted on the device (``note_device_hits``) and folded into ``stats()``.
+* ``acquire_many(keys)``: a wave of leases in one native call; every miss of
+  the wave is submitted to the copy engines by that call;
+* ``storage`` for the grouped SwiGLU kernel, which reads expert weights
+  straight from their slots, and ``device_slot_table()`` for the case where
+  every expert is resident (the MoE block then runs with no host
+  synchronisation; its hits are counted on the device and folded into
+  ``stats()``).
 """
 from __future__ import annotations
 
-from collections import deque
+import ctypes
 from dataclasses import dataclass
 from threading import RLock
 from time import perf_counter_ns
-from typing import Hashable, Mapping
+from typing import Hashable, Iterable, Mapping
 
 import torch
 
-from .. import ops
+from .. import _native as N
 from .cache_snapshot import CacheSlotSnapshot, GpuExpertCacheSnapshot, PendingTransferSnapshot
 from .lease import ExpertCacheStats, ExpertLease, NoEvictableSlotError
 from .state import RuntimeEventKind
 
-
-@dataclass(slots=True)
-class _Counters:
-    h2d_submissions: int = 0
-    resident_hits: int = 0
-    inflight_joins: int = 0
-    evictions: int = 0
-
-
-class _Slot:
-    __slots__ = ("slot_id", "tensor", "expert_id", "generation", "active_leases",
-                 "last_used_sequence", "ready_event", "use_events")
-
-    def __init__(self, slot_id: int, tensor: torch.Tensor) -> None:
-        self.slot_id = slot_id
-        self.tensor = tensor
-        self.expert_id = None
-        self.generation = 0
-        self.active_leases = 0
-        self.last_used_sequence = 0
-        self.ready_event = None
-        self.use_events: dict = {}
-
-    def copy_meta(self, tensor: torch.Tensor) -> "_Slot":
-        other = _Slot(self.slot_id, tensor)
-        other.expert_id = self.expert_id
-        other.generation = self.generation
-        other.active_leases = self.active_leases
-        other.last_used_sequence = self.last_used_sequence
-        other.ready_event = self.ready_event
-        other.use_events = dict(self.use_events)
-        return other
+_ABSENT, _INFLIGHT, _RESIDENT = 0, 1, 2
 
 
 @dataclass(frozen=True, slots=True)
 class _Transfer:
+    """One outstanding fill as the reference's transfer records expose it."""
     expert_id: Hashable
     slot_id: int
     generation: int
@@ -88,14 +60,221 @@ class _Transfer:
 class _Checkpoint:
     owner: object
     weights: torch.Tensor
-    slots: tuple
-    resident: dict
-    inflight: dict
-    transfers: tuple
-    counters: _Counters
-    sequence: int
-    submission_sequence: int
-    state_version: int
+    image: bytes
+    events: dict
+    device_hits: int
+
+
+class _NativeState:
+    """One read of the manager's state: counters, slots, expert locations."""
+
+    __slots__ = ("counters", "slots", "where", "home", "fill_seq")
+
+    def __init__(self, cache: "GpuExpertCache", refresh: int) -> None:
+        n_slots, n_exp = cache._n_slots, len(cache._keys)
+        self.counters = N.SfCacheCounters()
+        self.slots = (N.SfCacheSlot * n_slots)()
+        self.where = (ctypes.c_int32 * n_exp)()
+        self.home = (ctypes.c_int32 * n_exp)()
+        self.fill_seq = (ctypes.c_int64 * n_exp)()
+        N.check(N.lib.sf_cache_state(cache._h, refresh, ctypes.byref(self.counters), self.slots,
+                                     self.where, self.home, self.fill_seq), "sf_cache_state")
+
+
+# ------------------------------------------------------------------ views
+
+
+class _SlotView:
+    """A slot as the reference's ``_Slot`` records it; edits write through."""
+
+    __slots__ = ("_cache", "slot_id")
+
+    def __init__(self, cache: "GpuExpertCache", slot_id: int) -> None:
+        self._cache = cache
+        self.slot_id = slot_id
+
+    def _row(self):
+        return _NativeState(self._cache, 0).slots[self.slot_id]
+
+    def _edit(self, field: int, value: int) -> None:
+        N.check(N.lib.sf_cache_slot_edit(self._cache._h, self.slot_id, field, value), "sf_cache_slot_edit")
+
+    @property
+    def tensor(self) -> torch.Tensor:
+        return self._cache._storage[self.slot_id]
+
+    @property
+    def expert_id(self):
+        e = self._row().expert
+        return None if e < 0 else self._cache._keys[e]
+
+    @expert_id.setter
+    def expert_id(self, value) -> None:
+        if value is not None:
+            raise ValueError("a slot's expert can only be cleared")
+        self._edit(N.SF_SLOT_EXPERT, -1)
+
+    @property
+    def generation(self) -> int:
+        return int(self._row().generation)
+
+    @generation.setter
+    def generation(self, value: int) -> None:
+        self._edit(N.SF_SLOT_GENERATION, int(value))
+
+    @property
+    def last_used_sequence(self) -> int:
+        return int(self._row().stamp)
+
+    @last_used_sequence.setter
+    def last_used_sequence(self, value: int) -> None:
+        self._edit(N.SF_SLOT_STAMP, int(value))
+
+    @property
+    def active_leases(self) -> int:
+        return int(self._row().leases)
+
+    @property
+    def ready_event(self):
+        return self._cache._events.get(int(self._row().ready_event))
+
+    @ready_event.setter
+    def ready_event(self, value) -> None:
+        if value is not None:
+            raise ValueError("a slot's ready event can only be cleared")
+        self._edit(N.SF_SLOT_READY, 0)
+
+    @property
+    def use_events(self) -> "_GuardView":
+        return _GuardView(self)
+
+
+class _GuardView:
+    """A slot's use guards: counted and cleared (the events stay native)."""
+
+    __slots__ = ("_slot",)
+
+    def __init__(self, slot: _SlotView) -> None:
+        self._slot = slot
+
+    def __len__(self) -> int:
+        return int(self._slot._row().guards)
+
+    def clear(self) -> None:
+        self._slot._edit(N.SF_SLOT_GUARDS, 0)
+
+
+class _LocationView:
+    """Experts at one location (resident, or in flight) as a read-mostly
+    mapping: resident experts map to their slot, in-flight ones to their
+    transfer record.  ``clear()`` forgets that location for every expert."""
+
+    __slots__ = ("_cache", "_code")
+
+    def __init__(self, cache: "GpuExpertCache", code: int) -> None:
+        self._cache = cache
+        self._code = code
+
+    def _items(self):
+        cache = self._cache
+        st = _NativeState(cache, 1)
+        out = {}
+        for e, key in enumerate(cache._keys):
+            if st.where[e] != self._code:
+                continue
+            slot = int(st.home[e])
+            if self._code == _RESIDENT:
+                out[key] = slot
+            else:
+                row = st.slots[slot]
+                out[key] = _Transfer(key, slot, int(row.generation), int(st.fill_seq[e]),
+                                     cache._events.get(int(row.ready_event)))
+        return out
+
+    def __contains__(self, key) -> bool:
+        e = self._cache._index.get(key)
+        return e is not None and _NativeState(self._cache, 1).where[e] == self._code
+
+    def get(self, key, default=None):
+        return self._items().get(key, default)
+
+    def __getitem__(self, key):
+        return self._items()[key]
+
+    def __len__(self) -> int:
+        st = _NativeState(self._cache, 1)
+        return sum(1 for e in range(len(self._cache._keys)) if st.where[e] == self._code)
+
+    def __bool__(self) -> bool:
+        return len(self) > 0
+
+    def __iter__(self):
+        return iter(self._items())
+
+    def keys(self):
+        return self._items().keys()
+
+    def values(self):
+        return self._items().values()
+
+    def items(self):
+        return self._items().items()
+
+    def clear(self) -> None:
+        N.check(N.lib.sf_cache_forget(self._cache._h, 1 if self._code == _RESIDENT else 2), "sf_cache_forget")
+
+
+class _FillQueueView:
+    """Outstanding fills in submission order (``_Transfer`` records)."""
+
+    __slots__ = ("_cache",)
+
+    def __init__(self, cache: "GpuExpertCache") -> None:
+        self._cache = cache
+
+    def _rows(self):
+        return self._cache._native_fills()
+
+    def __iter__(self):
+        cache = self._cache
+        return iter([_Transfer(cache._keys[f.expert], int(f.slot), int(f.generation), int(f.submission),
+                               cache._events.get(int(f.ready_event))) for f in self._rows()])
+
+    def __len__(self) -> int:
+        return len(self._rows())
+
+    def __bool__(self) -> bool:
+        return len(self) > 0
+
+    def clear(self) -> None:
+        N.check(N.lib.sf_cache_forget(self._cache._h, 4), "sf_cache_forget")
+
+
+# ------------------------------------------------------------------ cache
+
+
+def _pinned_sources(cpu_sources: Mapping, adopt: bool, owned: bool) -> dict:
+    """Validates the host sources and returns them page-locked and
+    contiguous, in source order (adopting tensors that already are)."""
+    items = list(cpu_sources.items())
+    shape, dtype = items[0][1].shape, items[0][1].dtype
+    out = {}
+    for key, src in items:
+        if src.device.type != "cpu":
+            raise ValueError(f"expert {key!r} source must be on CPU")
+        if src.shape != shape:
+            raise ValueError("all expert sources must have the same shape")
+        if src.dtype != dtype:
+            raise ValueError("all expert sources must have the same dtype")
+        if adopt and src.is_pinned() and src.is_contiguous():
+            out[key] = src.detach()
+            continue
+        if owned:
+            raise ValueError("owned expert sources must be contiguous pinned CPU tensors")
+        pinned = torch.empty(src.shape, dtype=src.dtype, device="cpu", pin_memory=True)
+        pinned.copy_(src.detach())
+        out[key] = pinned
+    return out
 
 
 class GpuExpertCache:
@@ -108,61 +287,56 @@ class GpuExpertCache:
             raise ValueError("slot_count must be positive")
         if source_owner is not None and not adopt_pinned_sources:
             raise ValueError("source_owner requires adopt_pinned_sources=True")
-        self.device = torch.device(device)
-        if self.device.type != "cuda":
+        dev = torch.device(device)
+        if dev.type != "cuda":
             raise ValueError("GpuExpertCache requires a CUDA device")
-        if self.device.index is None:
-            self.device = torch.device("cuda", torch.cuda.current_device())
-
-        items = list(cpu_sources.items())
-        shape, dtype = items[0][1].shape, items[0][1].dtype
-        self._sources: dict = {}
-        self._source_order: dict = {}
-        for order, (key, src) in enumerate(items):
-            if src.device.type != "cpu":
-                raise ValueError(f"expert {key!r} source must be on CPU")
-            if src.shape != shape:
-                raise ValueError("all expert sources must have the same shape")
-            if src.dtype != dtype:
-                raise ValueError("all expert sources must have the same dtype")
-            if adopt_pinned_sources and src.is_pinned() and src.is_contiguous():
-                pinned = src.detach()
-            else:
-                if source_owner is not None:
-                    raise ValueError("owned expert sources must be contiguous pinned CPU tensors")
-                pinned = torch.empty(src.shape, dtype=src.dtype, device="cpu", pin_memory=True)
-                pinned.copy_(src.detach())
-            self._sources[key] = pinned
-            self._source_order[key] = order
-
+        self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
+        self._sources = _pinned_sources(cpu_sources, adopt_pinned_sources, source_owner is not None)
+        self._keys = tuple(self._sources)
+        self._index = {k: i for i, k in enumerate(self._keys)}
+        first = self._sources[self._keys[0]]
         with torch.cuda.device(self.device):
-            self.copy_stream = torch.cuda.Stream(device=self.device)
-            self._storage = torch.empty((slot_count, *shape), dtype=dtype, device=self.device)
-            # A recycled allocation may still have readers on the allocating
-            # stream: order the first side-stream write after them.
-            self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+            self._storage = torch.empty((slot_count, *first.shape), dtype=first.dtype, device=self.device)
+            # The slots may reuse memory still read on the allocating stream.
+            self._copy_stream.wait_stream(torch.cuda.current_stream(self.device))
         for name, value in (("cache_id", cache_id), ("queue_id", queue_id)):
             if value is not None and (not isinstance(value, str) or not value):
                 raise ValueError(f"{name} must be a non-empty string")
-        self.cache_id = cache_id or f"cuda-{self.device.index}-stream-{int(self.copy_stream.cuda_stream)}"
+        self.cache_id = cache_id or f"cuda-{self.device.index}-stream-{int(self._copy_stream.cuda_stream)}"
         self.queue_id = queue_id or f"{self.cache_id}-copy"
-        self._slots = [_Slot(i, self._storage[i]) for i in range(slot_count)]
-        self._resident: dict = {}
-        self._inflight: dict = {}
-        self._outstanding_transfers: deque = deque()
-        self._stats = _Counters()
-        self._sequence = 0
-        self._submission_sequence = 0
-        self._state_version = 0
+
+        self._n_slots = slot_count
+        srcs = (ctypes.c_void_p * len(self._keys))(*[self._sources[k].data_ptr() for k in self._keys])
+        h = ctypes.c_void_p()
+        N.check(N.lib.sf_cache_create(slot_count, len(self._keys), self._storage.data_ptr(),
+                                      first.numel() * first.element_size(), srcs,
+                                      self._copy_stream.cuda_stream, ctypes.byref(h)), "sf_cache_create")
+        self._h = h.value
+        self._slots = [_SlotView(self, i) for i in range(slot_count)]
+        self._resident = _LocationView(self, _RESIDENT)
+        self._inflight = _LocationView(self, _INFLIGHT)
+        self._outstanding_transfers = _FillQueueView(self)
+        self._events: dict = {}          # ready-event handle -> torch.cuda.Event
+        self._spare_events: list = []    # created, never used for a fill yet
         self._observer = observer
         self._source_owner = source_owner
         self._closed = False
         self._closing = False
         self._lock = RLock()
-        self._device_hits = None  # lazily created int64 device counter
-        self._slot_table_cache = None  # (state_version, keys, tensor)
+        self._device_hits = None         # int64 device counter of fast-path hits
+        self._table = None               # (state version, keys, device slot table)
 
     # ------------------------------------------------------------ properties
+    @property
+    def copy_stream(self) -> torch.cuda.Stream:
+        return self._copy_stream
+
+    @copy_stream.setter
+    def copy_stream(self, stream: torch.cuda.Stream) -> None:
+        N.check(N.lib.sf_cache_set_copy_stream(self._h, stream.cuda_stream), "sf_cache_set_copy_stream")
+        self._copy_stream = stream
+
     @property
     def storage(self) -> torch.Tensor:
         """``[slot_count, *source_shape]`` device tensor holding every slot."""
@@ -170,7 +344,7 @@ class GpuExpertCache:
 
     @property
     def slot_count(self) -> int:
-        return len(self._slots)
+        return self._n_slots
 
     @property
     def sources_are_pinned(self) -> bool:
@@ -184,240 +358,218 @@ class GpuExpertCache:
     @property
     def active_lease_count(self) -> int:
         with self._lock:
-            return sum(slot.active_leases for slot in self._slots)
+            if self._closed:
+                return 0
+            st = _NativeState(self, 0)
+            return sum(int(st.slots[s].leases) for s in range(self._n_slots))
+
+    @property
+    def _submission_sequence(self) -> int:
+        return int(_NativeState(self, 0).counters.submission_sequence)
+
+    @property
+    def _sequence(self) -> int:
+        return int(_NativeState(self, 0).counters.sequence)
+
+    @property
+    def _state_version(self) -> int:
+        return int(_NativeState(self, 0).counters.state_version)
+
+    @_state_version.setter
+    def _state_version(self, value: int) -> None:
+        N.check(N.lib.sf_cache_set_version(self._h, int(value)), "sf_cache_set_version")
 
     def source_keys(self) -> tuple:
-        return tuple(self._sources)
+        return self._keys
 
-    # -------------------------------------------------------------- acquire
-    def acquire(self, expert_id: Hashable) -> ExpertLease:
-        return self._acquire(expert_id, defer_touch=False)
+    def holds_any(self) -> bool:
+        """Whether any expert is resident or in flight."""
+        st = _NativeState(self, 0)
+        return any(st.where[e] != _ABSENT for e in range(len(self._keys)))
 
-    def _prefetch(self, expert_id: Hashable) -> ExpertLease:
-        return self._acquire(expert_id, defer_touch=True)
+    # ---------------------------------------------------------------- events
+    def _fresh_event_handles(self, n: int):
+        """``n`` created (not yet fill-bound) ready events; the manager records
+        the ones it uses behind their fills."""
+        while len(self._spare_events) < n:
+            ev = torch.cuda.Event(blocking=False)
+            ev.record(self._copy_stream)  # creates the CUDA event; re-recorded after the copy
+            self._spare_events.append(ev)
+        return (ctypes.c_uint64 * n)(*[ev.cuda_event for ev in self._spare_events[:n]])
 
-    def _check_open_and_known(self, expert_id: Hashable) -> None:
+    def _adopt_events(self, handles: Iterable[int]) -> None:
+        used = set(handles)
+        if not used:
+            return
+        keep = []
+        for ev in self._spare_events:
+            if ev.cuda_event in used:
+                self._events[ev.cuda_event] = ev
+            else:
+                keep.append(ev)
+        self._spare_events = keep
+        if len(self._events) > 4 * self._n_slots + 64:
+            self._prune_events()
+
+    def _prune_events(self) -> None:
+        """Drops the Python references to events the manager no longer holds
+        (leases, snapshots and observers keep their own references)."""
+        st = _NativeState(self, 0)
+        live = {int(st.slots[s].ready_event) for s in range(self._n_slots)}
+        live.update(int(f.ready_event) for f in self._native_fills())
+        self._events = {h: ev for h, ev in self._events.items() if h in live}
+
+    def _native_fills(self):
+        n = ctypes.c_int()
+        N.check(N.lib.sf_cache_fills(self._h, None, 0, ctypes.byref(n)), "sf_cache_fills")
+        buf = (N.SfCacheFill * max(n.value, 1))()
+        N.check(N.lib.sf_cache_fills(self._h, buf, len(buf), ctypes.byref(n)), "sf_cache_fills")
+        return list(buf[: n.value])
+
+    # --------------------------------------------------------------- acquire
+    def _check_open(self) -> None:
         if self._closed or self._closing:
             raise RuntimeError("expert cache is closed")
-        if expert_id not in self._sources:
-            raise KeyError(f"unknown expert {expert_id!r}")
+
+    def _indices(self, keys) -> list:
+        out = []
+        for key in keys:
+            e = self._index.get(key)
+            if e is None:
+                raise KeyError(f"unknown expert {key!r}")
+            out.append(e)
+        return out
+
+    def _grant(self, keys, mode: int, defer_touch: bool, probabilities=None) -> list:
+        """Runs one native acquire over ``keys``; returns a lease per key
+        (``None`` where nothing was granted), emitting the observer records
+        of every hit, join, eviction and submission in order."""
+        self._check_open()
+        idx = self._indices(keys)
+        n = len(idx)
+        if n == 0:
+            return []
+        experts = (ctypes.c_int32 * n)(*idx)
+        fresh = self._fresh_event_handles(n) if mode != N.SF_CACHE_RESIDENT_ONLY else None
+        probs = None
+        if probabilities is not None:
+            probs = (ctypes.c_float * len(self._keys))(*[float(probabilities.get(k, 0.0)) for k in self._keys])
+        grants = (N.SfCacheGrant * n)()
+        granted = ctypes.c_int()
+        rc = N.lib.sf_cache_acquire(self._h, experts, n, mode, int(defer_touch), fresh, probs, grants,
+                                    ctypes.byref(granted))
+        if rc == N.SF_ERR_NO_SLOT:
+            raise NoEvictableSlotError("all GPU expert slots have active leases")
+        N.check(rc, "sf_cache_acquire")
+        self._adopt_events(int(g.ready_event) for g in grants if g.kind == N.SF_GRANT_MISS)
+        leases = []
+        for key, g in zip(keys, grants):
+            if g.kind == N.SF_GRANT_NONE:
+                leases.append(None)
+                continue
+            ready = self._events.get(int(g.ready_event))
+            if self._observer is not None:
+                self._report_grant(key, g, ready)
+            leases.append(ExpertLease(self, key, self._index[key], int(g.slot), int(g.generation), ready,
+                                      defer_touch=defer_touch, grant=(int(g.kind), int(g.submission))))
+        return leases
+
+    def _report_grant(self, key, g, ready) -> None:
+        slot, gen = int(g.slot), int(g.generation)
+        if g.kind == N.SF_GRANT_HIT:
+            self._emit(RuntimeEventKind.RESIDENT_HIT, key, slot, gen)
+        elif g.kind == N.SF_GRANT_JOIN:
+            self._emit(RuntimeEventKind.INFLIGHT_JOIN, key, slot, gen,
+                       submission_sequence=int(g.submission), ready_event=ready)
+        else:
+            if g.victim >= 0:
+                self._emit(RuntimeEventKind.EVICT, key, slot, gen, victim_expert_id=self._keys[g.victim])
+            self._emit(RuntimeEventKind.H2D_SUBMIT, key, slot, gen, submission_sequence=int(g.submission),
+                       ready_event=ready)
+
+    def acquire(self, expert_id: Hashable) -> ExpertLease:
+        with self._lock:
+            return self._grant((expert_id,), N.SF_CACHE_ACQUIRE, False)[0]
+
+    def acquire_many(self, expert_ids) -> list:
+        """Leases for ``expert_ids`` in order, as consecutive ``acquire``
+        calls would give them, with every miss submitted by one native call.
+        Stops early (a shorter list) at the first expert for which every
+        slot is leased; raises ``NoEvictableSlotError`` if that is the first."""
+        with self._lock:
+            return [l for l in self._grant(tuple(expert_ids), N.SF_CACHE_ACQUIRE, False) if l is not None]
+
+    def _prefetch(self, expert_id: Hashable) -> ExpertLease:
+        with self._lock:
+            return self._grant((expert_id,), N.SF_CACHE_ACQUIRE, True)[0]
 
     def _prefetch_nonblocking(self, expert_id: Hashable, *, resident_only: bool = False,
                               eviction_probabilities: Mapping | None = None) -> ExpertLease | None:
-        with self._lock:
-            self._check_open_and_known(expert_id)
-            self._reap_completed_transfers()
-            if expert_id in self._resident or expert_id in self._inflight:
-                return self._acquire(expert_id, defer_touch=True)
-            if resident_only:
-                return None
-            if eviction_probabilities is None:
-                slot = self._choose_lru_slot(ready_only=True)
-            else:
-                slot = self._choose_probability_slot(expert_id, eviction_probabilities)
-            if slot is None:
-                return None
-            self._assign_and_submit(slot, expert_id)
-            return self._new_lease(slot, defer_touch=True)
-
-    def _acquire(self, expert_id: Hashable, *, defer_touch: bool) -> ExpertLease:
-        with self._lock:
-            self._check_open_and_known(expert_id)
-            self._reap_completed_transfers()
-            transfer = self._inflight.get(expert_id)
-            if transfer is not None:
-                slot = self._slots[transfer.slot_id]
-                self._emit(RuntimeEventKind.INFLIGHT_JOIN, expert_id, slot,
-                           submission_sequence=transfer.submission_sequence,
-                           ready_event=transfer.ready_event)
-                self._stats.inflight_joins += 1
-                return self._new_lease(slot, defer_touch=defer_touch)
-            slot_id = self._resident.get(expert_id)
-            if slot_id is not None:
-                slot = self._slots[slot_id]
-                self._emit(RuntimeEventKind.RESIDENT_HIT, expert_id, slot)
-                self._stats.resident_hits += 1
-                lease = self._new_lease(slot, defer_touch=defer_touch)
-                lease._ready_confirmed = True  # resident => its copy completed
-                return lease
-            slot = self._choose_lru_slot()
-            if slot is None:
-                raise NoEvictableSlotError("all GPU expert slots have active leases")
-            self._assign_and_submit(slot, expert_id)
-            return self._new_lease(slot, defer_touch=defer_touch)
-
-    # ------------------------------------------------------------ victims
-    @staticmethod
-    def _lru_key(slot: _Slot):
-        return (slot.expert_id is not None, slot.last_used_sequence, slot.slot_id)
-
-    def _slot_writable(self, slot: _Slot) -> bool:
-        copied = (slot.ready_event is None or self._resident.get(slot.expert_id) == slot.slot_id
-                  or slot.ready_event.query())
-        return copied and all(ev.query() for ev in slot.use_events.values())
-
-    def _choose_lru_slot(self, *, ready_only: bool = False) -> _Slot | None:
-        free = [s for s in self._slots if s.active_leases == 0]
-        if not free:
-            return None
-        if not ready_only:
-            return min(free, key=self._lru_key)
-        for slot in sorted(free, key=self._lru_key):
-            if self._slot_writable(slot):
-                return slot
-        return None
-
-    def _choose_probability_slot(self, expert_id: Hashable, probabilities: Mapping) -> _Slot | None:
-        """Replace an unleased, writable expert whose probability is lower
-        than the incoming one's (gpu_expert_cache.py:520-541)."""
-        incoming = probabilities.get(expert_id, 0.0)
-        free = [s for s in self._slots if s.active_leases == 0]
-        order = sorted(free, key=lambda s: (s.expert_id is not None,
-                                            probabilities.get(s.expert_id, 0.0),
-                                            s.last_used_sequence, s.slot_id))
-        for slot in order:
-            if slot.expert_id is not None and probabilities.get(slot.expert_id, 0.0) >= incoming:
-                break
-            if self._slot_writable(slot):
-                return slot
-        return None
-
-    # --------------------------------------------------------------- fills
-    def _assign_and_submit(self, slot: _Slot, expert_id: Hashable) -> None:
-        victim = slot.expert_id
-        if victim is not None:
-            self._resident.pop(victim, None)
-            self._inflight.pop(victim, None)
-            self._stats.evictions += 1
-        slot.generation += 1
-        slot.expert_id = expert_id
-        guards = tuple(slot.use_events.values())
-        slot.use_events.clear()
-        stream = self.copy_stream
-        for guard in guards:
-            stream.wait_event(guard)
-        ops.slot_fill_batch([slot.tensor], [self._sources[expert_id]], stream)
-        ready = torch.cuda.Event(blocking=False)
-        ready.record(stream)
-        slot.ready_event = ready
-        transfer = _Transfer(expert_id, slot.slot_id, slot.generation, self._submission_sequence, ready)
-        self._inflight[expert_id] = transfer
-        self._outstanding_transfers.append(transfer)
-        self._stats.h2d_submissions += 1
-        self._submission_sequence += 1
-        if victim is not None:
-            self._emit(RuntimeEventKind.EVICT, expert_id, slot, victim_expert_id=victim)
-        self._emit(RuntimeEventKind.H2D_SUBMIT, expert_id, slot,
-                   submission_sequence=transfer.submission_sequence, ready_event=ready)
-
-    def _reap_completed_transfers(self) -> None:
-        changed = False
-        pending = self._outstanding_transfers
-        while pending and pending[0].ready_event.query():
-            t = pending.popleft()
-            slot = self._slots[t.slot_id]
-            if slot.expert_id == t.expert_id and slot.generation == t.generation:
-                self._resident[t.expert_id] = t.slot_id
-            if self._inflight.get(t.expert_id) == t:
-                del self._inflight[t.expert_id]
-            changed = True
-        if changed:
-            self._state_version += 1
-
-    def _reap_completed_use_guards(self) -> None:
-        changed = False
-        for slot in self._slots:
-            for sid, ev in list(slot.use_events.items()):
-                if ev.query():
-                    del slot.use_events[sid]
-                    changed = True
-        if changed:
-            self._state_version += 1
-
-    # -------------------------------------------------------------- leases
-    def _touch(self, slot: _Slot) -> None:
-        self._sequence += 1
-        self._state_version += 1
-        slot.last_used_sequence = self._sequence
-
-    def _new_lease(self, slot: _Slot, *, defer_touch: bool) -> ExpertLease:
-        if slot.expert_id is None or slot.ready_event is None:
-            raise RuntimeError("cannot lease an unassigned GPU slot")
-        slot.active_leases += 1
-        if defer_touch:
-            self._state_version += 1
+        if resident_only:
+            mode = N.SF_CACHE_RESIDENT_ONLY
+        elif eviction_probabilities is not None:
+            mode = N.SF_CACHE_PROBABILITY
         else:
-            self._touch(slot)
-        return ExpertLease(self, slot.expert_id, slot.slot_id, slot.generation, slot.ready_event,
-                           _defer_touch=defer_touch)
-
-    def _checked_slot(self, expert_id, slot_id: int, generation: int) -> _Slot:
-        slot = self._slots[slot_id]
-        if slot.expert_id != expert_id or slot.generation != generation or slot.active_leases <= 0:
-            raise RuntimeError("expert lease refers to a reused GPU slot")
-        return slot
-
-    def _lease_tensor(self, expert_id, slot_id: int, generation: int, *, touch: bool = False):
+            mode = N.SF_CACHE_NONBLOCKING
         with self._lock:
-            slot = self._checked_slot(expert_id, slot_id, generation)
-            if touch:
-                self._touch(slot)
-            return slot.tensor
+            return self._grant((expert_id,), mode, True, eviction_probabilities)[0]
 
-    def _record_consume_wait(self, *, expert_id, slot_id, generation, ready_event, stream) -> None:
-        if self._observer is None:
-            return
-        self._observer.record(kind=RuntimeEventKind.CONSUME_WAIT, cache_id=self.cache_id,
-                              queue_id=self.queue_id, expert_id=expert_id, slot_id=slot_id,
-                              generation=generation, ready_event=ready_event,
-                              stream_ids=(int(stream.cuda_stream),))
-
-    def _release(self, expert_id, slot_id: int, generation: int, used_streams: tuple) -> None:
+    # ---------------------------------------------------------------- leases
+    def _lease_wait(self, lease: ExpertLease, stream: torch.cuda.Stream, touch: bool) -> torch.Tensor:
         with self._lock:
-            slot = self._checked_slot(expert_id, slot_id, generation)
-            for stream in used_streams:
-                ev = torch.cuda.Event(blocking=False)
-                ev.record(stream)
-                slot.use_events[stream.cuda_stream] = ev
-            self._emit(RuntimeEventKind.RELEASE, expert_id, slot,
-                       stream_ids=tuple(sorted(int(s.cuda_stream) for s in used_streams)))
-            slot.active_leases -= 1
-            self._touch(slot)
+            N.check(N.lib.sf_cache_wait(self._h, lease._index, lease.slot_id, lease.generation,
+                                        stream.cuda_stream, int(touch)), "expert lease")
+            if self._observer is not None:
+                self._observer.record(kind=RuntimeEventKind.CONSUME_WAIT, cache_id=self.cache_id,
+                                      queue_id=self.queue_id, expert_id=lease.expert_id,
+                                      slot_id=lease.slot_id, generation=lease.generation,
+                                      ready_event=lease.ready_event, stream_ids=(int(stream.cuda_stream),))
+            return self._storage[lease.slot_id]
 
-    def _emit(self, kind, expert_id, slot: _Slot, *, submission_sequence=None, victim_expert_id=None,
-              ready_event=None, stream_ids=()) -> None:
-        if self._observer is None:
-            return
+    def _lease_release(self, lease: ExpertLease, streams: tuple) -> None:
+        with self._lock:
+            N.check(N.lib.sf_cache_check(self._h, lease._index, lease.slot_id, lease.generation),
+                    "expert lease")
+            if self._observer is not None:
+                self._emit(RuntimeEventKind.RELEASE, lease.expert_id, lease.slot_id, lease.generation,
+                           stream_ids=tuple(sorted(int(s.cuda_stream) for s in streams)))
+            handles = (ctypes.c_uint64 * max(len(streams), 1))(*[s.cuda_stream for s in streams])
+            N.check(N.lib.sf_cache_release(self._h, lease._index, lease.slot_id, lease.generation, handles,
+                                           len(streams)), "expert lease")
+
+    def _emit(self, kind, expert_id, slot_id: int, generation: int, *, submission_sequence=None,
+              victim_expert_id=None, ready_event=None, stream_ids=()) -> None:
         self._observer.record(kind=kind, cache_id=self.cache_id, queue_id=self.queue_id,
-                              expert_id=expert_id, slot_id=slot.slot_id, generation=slot.generation,
-                              submission_sequence=submission_sequence,
-                              victim_expert_id=victim_expert_id, ready_event=ready_event,
-                              stream_ids=stream_ids)
+                              expert_id=expert_id, slot_id=slot_id, generation=generation,
+                              submission_sequence=submission_sequence, victim_expert_id=victim_expert_id,
+                              ready_event=ready_event, stream_ids=stream_ids)
 
-    # ---------------------------------------------------------- fast path
+    # ------------------------------------------------------------- fast path
     def device_slot_table(self, keys) -> torch.Tensor | None:
         """int32 device tensor with the slot of each key, or ``None`` unless
-        every source is resident with nothing in flight or leased and the
-        cache holds all sources (so no slot can change while it is used)."""
+        the cache holds every source, all resident, none in flight (so no
+        slot can change while the table is used)."""
         with self._lock:
-            if self._closed or self._closing:
-                raise RuntimeError("expert cache is closed")
-            if len(self._slots) < len(self._sources):
+            self._check_open()
+            if self._n_slots < len(self._keys):
                 return None
-            self._reap_completed_transfers()
-            if self._inflight or len(self._resident) != len(self._sources):
+            table = (ctypes.c_int32 * len(self._keys))()
+            complete = ctypes.c_int()
+            N.check(N.lib.sf_cache_resident_table(self._h, table, ctypes.byref(complete)),
+                    "sf_cache_resident_table")
+            if not complete.value:
                 return None
             keys = tuple(keys)
-            cached = self._slot_table_cache
-            if cached is not None and cached[0] == self._state_version and cached[1] == keys:
-                return cached[2]
-            table = torch.tensor([self._resident.get(k, -1) for k in keys], dtype=torch.int32)
-            table = table.to(self.device, non_blocking=False)
-            self._slot_table_cache = (self._state_version, keys, table)
-            return table
+            version = self._state_version
+            if self._table is not None and self._table[0] == version and self._table[1] == keys:
+                return self._table[2]
+            slots = torch.tensor([table[self._index[k]] if k in self._index else -1 for k in keys],
+                                 dtype=torch.int32).to(self.device)
+            self._table = (version, keys, slots)
+            return slots
 
     def device_hit_counter(self) -> torch.Tensor:
-        """The device int64 scalar that kernels add resident hits to
+        """The device int64 scalar kernels add resident hits to
         (``ops.moe_dispatch(..., active_total=)``); read on the host only
         when the statistics are read."""
         if self._device_hits is None:
@@ -426,106 +578,88 @@ class GpuExpertCache:
 
     def note_device_hits(self, count: torch.Tensor) -> None:
         """Adds a device-side count of resident hits (no host sync)."""
-        if self._device_hits is None:
-            self._device_hits = torch.zeros((), dtype=torch.int64, device=self.device)
-        self._device_hits.add_(count.reshape(()))  # int32 into the int64 total, one launch
+        self.device_hit_counter().add_(count.reshape(()))
 
     def _flush_device_hits(self) -> None:
         if self._device_hits is not None:
-            self._stats.resident_hits += int(self._device_hits.item())
+            N.check(N.lib.sf_cache_add_hits(self._h, int(self._device_hits.item())), "sf_cache_add_hits")
             self._device_hits.zero_()
 
     def prefill_all(self) -> None:
-        """Submit a fill for every non-resident source (warm-up helper)."""
-        for key in self._sources:
-            with self._lock:
-                self._reap_completed_transfers()
-                if key in self._resident or key in self._inflight:
-                    continue
+        """Leases and releases every source once (fills the empty ones)."""
+        for key in self._keys:
+            if key in self._resident or key in self._inflight:
+                continue
             self.acquire(key).release()
 
-    # ---------------------------------------------------------- inspection
+    # ------------------------------------------------------------ inspection
     def stats(self) -> ExpertCacheStats:
         with self._lock:
             self._flush_device_hits()
-            self._reap_completed_use_guards()
-            return self._stats_snapshot()
-
-    def _stats_snapshot(self, *, pending_use_guards: int | None = None) -> ExpertCacheStats:
-        if pending_use_guards is None:
-            pending_use_guards = sum(len(s.use_events) for s in self._slots)
-        return ExpertCacheStats(self._stats.h2d_submissions, self._stats.resident_hits,
-                                self._stats.inflight_joins, self._stats.evictions,
-                                pending_use_guards)
+            c = _NativeState(self, 3).counters
+            return ExpertCacheStats(int(c.h2d_submissions), int(c.resident_hits), int(c.inflight_joins),
+                                    int(c.evictions), int(c.pending_use_guards))
 
     def resident_expert_ids(self) -> tuple:
         with self._lock:
-            self._reap_completed_transfers()
-            return tuple(sorted(self._resident, key=self._source_order.__getitem__))
+            st = _NativeState(self, 1)
+            return tuple(k for e, k in enumerate(self._keys) if st.where[e] == _RESIDENT)
 
     def snapshot(self) -> GpuExpertCacheSnapshot:
         with self._lock:
             self._flush_device_hits()
-            done = {t.submission_sequence: t.ready_event.query() for t in self._outstanding_transfers}
-            guards = {s.slot_id: sum(not ev.query() for ev in s.use_events.values()) for s in self._slots}
-            current = {(t.slot_id, t.generation): t for t in self._inflight.values()}
+            st = _NativeState(self, 0)
+            fills = self._native_fills()
+            done = {int(f.submission): bool(f.done) for f in fills}
             slots = []
-            for s in self._slots:
-                t = current.get((s.slot_id, s.generation))
-                if s.expert_id is None:
+            guards_total = 0
+            for s in range(self._n_slots):
+                row = st.slots[s]
+                e = int(row.expert)
+                if e < 0:
                     ready = False
-                elif t is not None:
-                    ready = done[t.submission_sequence]
+                elif st.where[e] == _INFLIGHT and st.home[e] == s:
+                    ready = done.get(int(st.fill_seq[e]), True)
                 else:
-                    ready = s.expert_id in self._resident
-                slots.append(CacheSlotSnapshot(s.slot_id, s.expert_id, s.generation, s.active_leases,
-                                               s.last_used_sequence, ready, guards[s.slot_id]))
-            pending = tuple(
-                PendingTransferSnapshot(t.expert_id, t.slot_id, t.generation, t.submission_sequence,
-                                        t.ready_event, False)
-                for t in self._outstanding_transfers if not done[t.submission_sequence])
-            return GpuExpertCacheSnapshot(self.cache_id, self.queue_id, len(self._slots),
-                                          self._state_version, self._sequence,
-                                          self._submission_sequence, tuple(slots), pending,
-                                          self._stats_snapshot(pending_use_guards=sum(guards.values())))
+                    ready = st.where[e] == _RESIDENT and st.home[e] == s
+                guards_total += int(row.guards_pending)
+                slots.append(CacheSlotSnapshot(s, None if e < 0 else self._keys[e], int(row.generation),
+                                               int(row.leases), int(row.stamp), bool(ready),
+                                               int(row.guards_pending)))
+            pending = tuple(PendingTransferSnapshot(self._keys[f.expert], int(f.slot), int(f.generation),
+                                                    int(f.submission), self._events.get(int(f.ready_event)),
+                                                    False) for f in fills if not f.done)
+            c = st.counters
+            stats = ExpertCacheStats(int(c.h2d_submissions), int(c.resident_hits), int(c.inflight_joins),
+                                     int(c.evictions), guards_total)
+            return GpuExpertCacheSnapshot(self.cache_id, self.queue_id, self._n_slots, int(c.state_version),
+                                          int(c.sequence), int(c.submission_sequence), tuple(slots),
+                                          pending, stats)
 
-    # ----------------------------------------------------- reset / restore
+    # ------------------------------------------------------- reset / restore
     def _quiescent(self) -> bool:
-        return (all(t.ready_event.query() for t in self._outstanding_transfers)
-                and all(ev.query() for s in self._slots for ev in s.use_events.values()))
+        q = ctypes.c_int()
+        N.check(N.lib.sf_cache_quiescent(self._h, ctypes.byref(q)), "sf_cache_quiescent")
+        return bool(q.value)
 
     def cold_reset(self) -> None:
         with self._lock:
-            if self._closed or self._closing:
-                raise RuntimeError("expert cache is closed")
-            if any(s.active_leases for s in self._slots):
+            self._check_open()
+            if self.active_lease_count:
                 raise RuntimeError("cold reset cannot run while an active lease exists")
             if not self._quiescent():
                 raise RuntimeError("cold reset requires explicit CUDA synchronization")
             if self._device_hits is not None:
                 self._device_hits.zero_()
-            self._resident.clear()
-            self._inflight.clear()
-            self._outstanding_transfers.clear()
-            for s in self._slots:
-                s.expert_id = None
-                s.generation = 0
-                s.active_leases = 0
-                s.last_used_sequence = 0
-                s.ready_event = None
-                s.use_events.clear()
-            self._stats = _Counters()
-            self._sequence = 0
-            self._submission_sequence = 0
-            self._state_version = 0
-            self._slot_table_cache = None
+            N.check(N.lib.sf_cache_reset(self._h, N.SF_CACHE_RESET_COLD), "sf_cache_reset")
+            self._events.clear()
+            self._table = None
 
     def _require_checkpoint_boundary(self) -> None:
-        if self._closed or self._closing:
-            raise RuntimeError("expert cache is closed")
+        self._check_open()
         if self._observer is not None:
             raise RuntimeError("checkpoint restoration requires no active cache observer")
-        if any(s.active_leases for s in self._slots):
+        if self.active_lease_count:
             raise RuntimeError("checkpoint boundary cannot contain active leases")
         if not self._quiescent():
             raise RuntimeError("checkpoint boundary requires explicit CUDA synchronization")
@@ -534,13 +668,13 @@ class GpuExpertCache:
         with self._lock:
             self._require_checkpoint_boundary()
             self._flush_device_hits()
+            need = ctypes.c_size_t()
+            N.check(N.lib.sf_cache_export(self._h, None, 0, ctypes.byref(need)), "sf_cache_export")
+            image = (ctypes.c_uint8 * need.value)()
+            N.check(N.lib.sf_cache_export(self._h, image, need.value, ctypes.byref(need)), "sf_cache_export")
             weights = torch.empty_like(self._storage, device="cpu", pin_memory=True)
             weights.copy_(self._storage.detach())
-            counters = _Counters(**{f: getattr(self._stats, f) for f in _Counters.__slots__})
-            return _Checkpoint(self, weights, tuple(s.copy_meta(weights[s.slot_id]) for s in self._slots),
-                               dict(self._resident), dict(self._inflight),
-                               tuple(self._outstanding_transfers), counters, self._sequence,
-                               self._submission_sequence, self._state_version)
+            return _Checkpoint(self, weights, bytes(image), dict(self._events), 0)
 
     def _restore_checkpoint(self, checkpoint: _Checkpoint) -> dict:
         started = perf_counter_ns()
@@ -553,43 +687,41 @@ class GpuExpertCache:
             copied = perf_counter_ns()
             torch.cuda.current_stream(self.device).synchronize()
             synced = perf_counter_ns()
-            self._slots = [s.copy_meta(self._storage[s.slot_id]) for s in checkpoint.slots]
-            self._resident = dict(checkpoint.resident)
-            self._inflight = dict(checkpoint.inflight)
-            self._outstanding_transfers = deque(checkpoint.transfers)
-            self._stats = _Counters(**{f: getattr(checkpoint.counters, f) for f in _Counters.__slots__})
-            self._sequence = checkpoint.sequence
-            self._submission_sequence = checkpoint.submission_sequence
-            self._state_version = checkpoint.state_version
-            self._slot_table_cache = None
+            buf = (ctypes.c_uint8 * len(checkpoint.image)).from_buffer_copy(checkpoint.image)
+            N.check(N.lib.sf_cache_import(self._h, buf, len(checkpoint.image)), "sf_cache_import")
+            self._events = dict(checkpoint.events)
+            self._table = None
             finished = perf_counter_ns()
             return dict(weight_bytes=checkpoint.weights.numel() * checkpoint.weights.element_size(),
                         weights_pinned=checkpoint.weights.is_pinned(),
                         total_wall_ns=finished - started,
-                        timings_ns=dict(boundary_check=checked - started,
-                                        weight_copy_call=copied - checked,
-                                        stream_synchronize=synced - copied,
-                                        metadata_restore=finished - synced))
+                        timings_ns=dict(boundary_check=checked - started, weight_copy_call=copied - checked,
+                                        stream_synchronize=synced - copied, metadata_restore=finished - synced))
 
     def close(self) -> None:
         with self._lock:
             if self._closed:
                 return
-            if not self._closing and any(s.active_leases for s in self._slots):
+            if not self._closing and self.active_lease_count:
                 raise RuntimeError("expert cache cannot close while an active lease exists")
             self._closing = True
             torch.cuda.synchronize(self.device)
-            self._resident.clear()
-            self._inflight.clear()
-            self._outstanding_transfers.clear()
-            for s in self._slots:
-                s.expert_id = None
-                s.ready_event = None
-                s.use_events.clear()
+            N.lib.sf_cache_destroy(self._h)
+            self._h = None
+            self._events.clear()
+            self._spare_events.clear()
             self._sources.clear()
             owner, self._source_owner = self._source_owner, None
             if owner is not None:
                 owner.close()
-            self._slot_table_cache = None
+            self._table = None
             self._closed = True
             self._closing = False
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order varies
+        h = getattr(self, "_h", None)
+        if h and not getattr(self, "_closed", True):
+            try:
+                N.lib.sf_cache_destroy(h)
+            except Exception:
+                pass

@@ -1,10 +1,17 @@
-"""Expert leases: a caller's claim on one cache slot generation.
+"""Expert leases: a caller's claim on one generation of one cache slot.
 
-Mirrors ``src/specfit/runtime/lease.py``: ``NoEvictableSlotError`` (:13),
-``ExpertCacheStats`` (:18-23) and ``ExpertLease`` (:26-105).  A lease pins
-its slot against eviction until released; ``wait(stream)`` orders ``stream``
-after the slot's fill and returns the slot tensor; ``release()`` records, on
-every stream that waited, the event a later refill of the slot must wait for.
+Interface of ``src/specfit/runtime/lease.py``: ``NoEvictableSlotError``
+(:13), ``ExpertCacheStats`` (:18-23) and ``ExpertLease`` (:26-105) with
+``wait(stream=None) -> Tensor``, ``release()``, the context-manager protocol,
+``expert_id``, ``generation``, ``slot_id`` and ``ready_event``.
+
+A lease here is a handle: its identity is (expert index, slot, generation),
+and every operation is one call into the native slot manager that checks
+that identity first (a lease whose slot was refilled is refused with the
+reference's error).  ``wait`` orders the stream behind the slot's fill
+unless the fill is already published, and applies a deferred LRU touch;
+``release`` hands the manager the streams the lease was used on, which
+become the slot's use guards.
 """
 from __future__ import annotations
 
@@ -31,57 +38,48 @@ class ExpertCacheStats:
 
 
 class ExpertLease:
-    __slots__ = ("_cache", "_expert_id", "_generation", "_released", "_streams", "_touch_pending",
-                 "_ready_confirmed", "ready_event", "slot_id")
+    __slots__ = ("_cache", "_key", "_index", "slot_id", "_generation", "ready_event", "_used",
+                 "_touch_due", "_done", "grant")
 
-    def __init__(self, cache: "GpuExpertCache", expert_id: Hashable, slot_id: int, generation: int,
-                 ready_event, *, _defer_touch: bool = False) -> None:
+    def __init__(self, cache: "GpuExpertCache", key: Hashable, index: int, slot_id: int, generation: int,
+                 ready_event, *, defer_touch: bool = False, grant: tuple = (0, -1)) -> None:
         self._cache = cache
-        self._expert_id = expert_id
-        self._generation = generation
-        self._released = False
-        self._streams: dict = {}
-        self._touch_pending = _defer_touch
-        # Set by the cache when the slot's fill is already known complete, so
-        # a consumer need not wait on its event.
-        self._ready_confirmed = False
+        self._key = key
+        self._index = index
         self.slot_id = slot_id
+        self._generation = generation
         self.ready_event = ready_event
+        self._used: dict = {}          # cuda_stream handle -> stream the slot was read on
+        self._touch_due = defer_touch  # a prefetched lease counts as a use at its first wait
+        self._done = False
+        # How the cache granted it: (SF_GRANT_HIT / _JOIN / _MISS, submission
+        # number of the fill it joined or started, else -1).
+        self.grant = grant
 
     @property
     def expert_id(self) -> Hashable:
-        return self._expert_id
+        return self._key
 
     @property
     def generation(self) -> int:
         return self._generation
 
     def wait(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-        if self._released:
+        if self._done:
             raise RuntimeError("cannot wait on a released expert lease")
-        if stream is None:
-            stream = torch.cuda.current_stream(self._cache.device)
-        if not self._ready_confirmed and self.ready_event is not None:
-            stream.wait_event(self.ready_event)
-        self._streams[stream.cuda_stream] = stream
-        tensor = self._cache._lease_tensor(self._expert_id, self.slot_id, self._generation,
-                                           touch=self._touch_pending)
-        self._touch_pending = False
-        if self._cache._observer is not None:
-            self._cache._record_consume_wait(expert_id=self._expert_id, slot_id=self.slot_id,
-                                             generation=self._generation,
-                                             ready_event=self.ready_event, stream=stream)
-        return tensor
+        s = stream if stream is not None else torch.cuda.current_stream(self._cache.device)
+        view = self._cache._lease_wait(self, s, self._touch_due)
+        self._touch_due = False
+        self._used.setdefault(s.cuda_stream, s)
+        return view
 
     def release(self) -> None:
-        if self._released:
-            return
-        self._cache._release(self._expert_id, self.slot_id, self._generation,
-                             tuple(self._streams.values()))
-        self._released = True
+        if not self._done:
+            self._cache._lease_release(self, tuple(self._used.values()))
+            self._done = True
 
     def __enter__(self) -> "ExpertLease":
-        if self._released:
+        if self._done:
             raise RuntimeError("cannot re-enter a released expert lease")
         return self
 

@@ -7,6 +7,8 @@ The forward pass differs in how it is executed, not in what it computes:
 
 * routes are grouped on the device (``sf_moe_dispatch``, the stable grouping
   of :173-178) and rows gathered once (``sf_moe_gather``, :189-190);
+* a lease wave is one call into the native slot manager, which submits
+  every miss of the wave to the copy engines (``GpuExpertCache.acquire_many``);
 * every expert of a lease wave runs in one grouped SwiGLU launch that reads
   the weights straight from their cache slots (``sf_grouped_swiglu``,
   :38-62 plus the ``mul_(w)`` of :132-138);
@@ -151,14 +153,11 @@ class Qwen3OffloadedExperts(nn.Module):
         stream = torch.cuda.current_stream(dev)
         pos = 0
         while pos < len(order):
-            wave = []
+            # One native call leases the wave and submits all of its misses;
+            # it stops at the first expert with no unleased slot left.
+            leases = self.cache.acquire_many([self._keys[e] for e in order[pos:]])
+            wave = list(zip(order[pos:pos + len(leases)], leases))
             try:
-                try:
-                    for e in order[pos:]:
-                        wave.append((e, self.cache.acquire(ExpertKey(self.layer_id, e))))
-                except NoEvictableSlotError:
-                    if not wave:
-                        raise
                 table = torch.full((self.num_experts + 1 + len(wave),), -1, dtype=torch.int32)
                 for j, (e, lease) in enumerate(wave):
                     lease.wait(stream)
