@@ -150,16 +150,38 @@ def _sha256(path: Path) -> str:
     return h.hexdigest()
 
 
+def _check_file_record(rec: dict, label: str) -> None:
+    """One ``files`` record of a packed-v1 manifest: a relative file name that
+    stays under the checkpoint root, a positive integer size and a lowercase
+    SHA-256 (the record rules of qwen3_packed_checkpoint.py:466-486 and its
+    field validators :391-430, same messages)."""
+    name = rec.get("filename")
+    if not isinstance(name, str) or not name:
+        raise PackedCheckpointError("packed checkpoint manifest field 'filename' must be a nonempty string")
+    rel = Path(name)
+    if rel.is_absolute() or ".." in rel.parts or rel == Path("."):
+        raise PackedCheckpointError(f"packed checkpoint {label} file name must stay under root")
+    digest = rec.get("sha256")
+    if not isinstance(digest, str) or not digest:
+        raise PackedCheckpointError("packed checkpoint manifest field 'sha256' must be a nonempty string")
+    if len(digest) != 64 or any(c not in "0123456789abcdef" for c in digest):
+        raise PackedCheckpointError("packed checkpoint manifest field 'sha256' must be a lowercase SHA256")
+    size = rec.get("size_bytes")
+    if type(size) is not int or size <= 0:
+        raise PackedCheckpointError("packed checkpoint manifest field 'size_bytes' must be a positive integer")
+
+
 def open_packed_checkpoint(root, *, verify_hashes: bool = False,
                            source_metadata_root=None) -> PackedCheckpoint:
     """Read and check a packed-v1 manifest: the checks of the reference's
     ``PackedQwen3Checkpoint.open`` (qwen3_packed_checkpoint.py:156-377) that
     a loader depends on, with its error type and messages -- schema and
     version, completeness, expert layout and dtype, the packed element
-    count, one record per layer in order with the packed shape, unique file
+    count, one record per layer in order with the packed shape, file records
+    (names under the root, positive sizes, well-formed SHA-256), unique file
     names, file presence and sizes, optionally every file's SHA-256, and,
-    with ``source_metadata_root``, that its ``config.json`` (and
-    ``model.safetensors.index.json`` when present) are the ones packed.
+    with ``source_metadata_root``, that its ``config.json`` and
+    ``model.safetensors.index.json`` both exist and are the ones packed.
     Only bf16 experts are accepted (the kernels' dtype)."""
     root = Path(root).resolve()
     mpath = root / "manifest.json"
@@ -211,26 +233,30 @@ def open_packed_checkpoint(root, *, verify_hashes: bool = False,
             raise PackedCheckpointError("packed checkpoint layer tensor shape does not match")
         if rec.get("dtype") != dtype:
             raise PackedCheckpointError("packed checkpoint layer tensor dtype does not match")
-    records = [nonexp] + layers
-    names = [r.get("filename") for r in records]
+    if not isinstance(nonexp, dict):
+        raise PackedCheckpointError("packed checkpoint nonexperts file record must be an object")
+    records = [(nonexp, "nonexperts")] + [(rec, f"layer {l}") for l, rec in enumerate(layers)]
+    for rec, label in records:
+        _check_file_record(rec, label)
+    names = [rec["filename"] for rec, _ in records]
     if len(names) != len(set(names)):
         raise PackedCheckpointError("packed checkpoint file names must be unique")
-    for rec in records:
+    for rec, _ in records:
         path = root / rec["filename"]
         if not path.is_file():
             raise PackedCheckpointError(f"packed checkpoint file is missing: {path}")
-        if path.stat().st_size != int(rec["size_bytes"]):
+        if path.stat().st_size != rec["size_bytes"]:
             raise PackedCheckpointError(f"packed checkpoint file size does not match: {path}")
         if verify_hashes and _sha256(path) != rec["sha256"]:
             raise PackedCheckpointError(f"packed checkpoint file SHA256 does not match: {path}")
     if source_metadata_root is not None:
         meta = Path(source_metadata_root).resolve()
         cfg, index = meta / "config.json", meta / "model.safetensors.index.json"
-        if not cfg.is_file():
+        if not cfg.is_file() or not index.is_file():
             raise PackedCheckpointError("source config or index metadata is missing")
         if _sha256(cfg) != source.get("config_sha256"):
             raise PackedCheckpointError("source config SHA256 does not match packed checkpoint")
-        if index.is_file() and _sha256(index) != source.get("index_sha256"):
+        if _sha256(index) != source.get("index_sha256"):
             raise PackedCheckpointError("source index SHA256 does not match packed checkpoint")
     return PackedCheckpoint(root, manifest, L, E, H, I, packed,
                             tuple(root / r["filename"] for r in layers), root / nonexp["filename"])
@@ -282,12 +308,16 @@ class MappedExpertPool:
         self._registered = []
         with torch.cuda.device(self.device):
             for t in self.layers:
-                nbytes = t.numel() * t.element_size()
-                rc = int(torch.cuda.cudart().cudaHostRegister(t.data_ptr(), nbytes, _HOST_REGISTER_READ_ONLY))
+                # The whole file mapping is registered: torch judges a view
+                # pinned by its storage's base address, and the expert tensor
+                # starts after the safetensors header inside that storage.
+                store = t.untyped_storage()
+                rc = int(torch.cuda.cudart().cudaHostRegister(store.data_ptr(), store.nbytes(),
+                                                              _HOST_REGISTER_READ_ONLY))
                 if rc != 0:
                     self.close()
                     raise RuntimeError(f"cudaHostRegister of a packed expert layer failed ({rc})")
-                self._registered.append(t)
+                self._registered.append(store)
                 if not t.is_pinned():
                     self.close()
                     raise RuntimeError("a registered packed expert layer is not seen as pinned memory")
@@ -303,8 +333,8 @@ class MappedExpertPool:
 
     def close(self) -> None:
         with torch.cuda.device(self.device):
-            for t in self._registered:
-                torch.cuda.cudart().cudaHostUnregister(t.data_ptr())
+            for store in self._registered:
+                torch.cuda.cudart().cudaHostUnregister(store.data_ptr())
         self._registered = []
 
 

@@ -131,6 +131,18 @@ def _edit_manifest(root, fn):
     (lambda m: m["files"]["layers"][1].__setitem__("layer_id", 0), "layer IDs must be contiguous"),
     (lambda m: m["files"]["layers"][0].__setitem__("filename", "nonexperts.safetensors"), "file names must be unique"),
     (lambda m: m["files"]["nonexperts"].__setitem__("size_bytes", 1), "file size does not match"),
+    (lambda m: m["files"]["layers"][0].__setitem__("filename", "/etc/passwd"), "layer 0 file name must stay under root"),
+    (lambda m: m["files"]["layers"][1].__setitem__("filename", "../x.safetensors"), "layer 1 file name must stay under root"),
+    (lambda m: m["files"]["nonexperts"].__setitem__("filename", "."), "nonexperts file name must stay under root"),
+    (lambda m: m["files"]["layers"][0].pop("filename"), "'filename' must be a nonempty string"),
+    (lambda m: m["files"]["layers"][0].__setitem__("filename", 7), "'filename' must be a nonempty string"),
+    (lambda m: m["files"]["nonexperts"].pop("size_bytes"), "'size_bytes' must be a positive integer"),
+    (lambda m: m["files"]["nonexperts"].__setitem__("size_bytes", "12"), "'size_bytes' must be a positive integer"),
+    (lambda m: m["files"]["layers"][1].__setitem__("size_bytes", True), "'size_bytes' must be a positive integer"),
+    (lambda m: m["files"]["layers"][1].pop("sha256"), "'sha256' must be a nonempty string"),
+    (lambda m: m["files"]["layers"][1].__setitem__("sha256", "AB" * 32), "'sha256' must be a lowercase SHA256"),
+    (lambda m: m["files"]["layers"][1].__setitem__("sha256", "ab" * 31), "'sha256' must be a lowercase SHA256"),
+    (lambda m: m["files"].__setitem__("nonexperts", []), "nonexperts file record must be an object"),
 ])
 def test_packed_manifest_mismatches_are_refused(tmp_path, edit, match):
     root = _copy_fixture(tmp_path)
@@ -157,6 +169,23 @@ def test_packed_source_config_must_match(tmp_path):
     cfg["rms_norm_eps"] = 1e-5
     (src / "config.json").write_text(json.dumps(cfg))
     with pytest.raises(PackedCheckpointError, match="source config SHA256 does not match"):
+        open_packed_checkpoint(FIXTURE / "packed", source_metadata_root=src)
+
+
+def test_packed_source_index_is_required(tmp_path):
+    src = tmp_path / "source"
+    shutil.copytree(FIXTURE / "source", src)
+    (src / "model.safetensors.index.json").unlink()
+    with pytest.raises(PackedCheckpointError, match="source config or index metadata is missing"):
+        open_packed_checkpoint(FIXTURE / "packed", source_metadata_root=src)
+
+
+def test_packed_source_index_must_match(tmp_path):
+    src = tmp_path / "source"
+    shutil.copytree(FIXTURE / "source", src)
+    index = src / "model.safetensors.index.json"
+    index.write_text(index.read_text() + "\n")
+    with pytest.raises(PackedCheckpointError, match="source index SHA256 does not match"):
         open_packed_checkpoint(FIXTURE / "packed", source_metadata_root=src)
 
 
