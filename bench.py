@@ -711,43 +711,88 @@ def b200_arm(args):
 
     h2d_peak = pinned_h2d_peak(pool, device)
     policy = ExpertExecutionPolicy(args.policy)
-    loaded.set_expert_execution_policy(policy)
-    before: dict = {}
-    launches0 = ops.LAUNCHES[0]
-    with ClockSampler(device.index) as clocks:
-        ms, ams = timed_steps(runner.step_device, args.steps, args.warmup, world, device,
-                              on_start=lambda: before.update(loaded.cache_stats(),
-                                                             launches=ops.LAUNCHES[0]))
-    launches = ops.LAUNCHES[0] - before["launches"]
-    committed = sum(len(tree.accepted_path(a.cpu().unsqueeze(0))) + 1 for a in ams)
-    total_committed = sum_over_ranks(committed, world, device)
-    value = total_committed / (ms / 1e3)
-    stats24 = loaded.cache_stats()
-    timed_stats = {k: (stats24[k] - before[k]) / args.steps for k in stats24}
-    h2d_roofline = h2d_roofline_of(timed_stats, ms / args.steps, h2d_peak)
-
-    # The same passes under the other execution policy (outputs are the same:
-    # the canonical combine adds in expert-id order whatever the order the
-    # experts run in).
     other = (ExpertExecutionPolicy.EXPERT_ID_ASCENDING if policy is ExpertExecutionPolicy.RESIDENT_FIRST
              else ExpertExecutionPolicy.RESIDENT_FIRST)
-    loaded.set_expert_execution_policy(other)
-    obefore: dict = {}
-    oms, oams = timed_steps(runner.step_device, args.steps, args.warmup, world, device,
-                            on_start=lambda: obefore.update(loaded.cache_stats()))
-    ostats = loaded.cache_stats()
-    ostats = {k: (ostats[k] - obefore[k]) / args.steps for k in ostats}
-    assert all(torch.equal(a, ams[0]) for a in oams), "execution policies gave different argmaxes"
+
+    def timed_with_stats(fn, pol, clocks_out=None):
+        """K timed steps of ``fn`` under policy ``pol``: (ms, results, cache
+        counters per timed step, launches of ours in the timed region)."""
+        loaded.set_expert_execution_policy(pol)
+        before: dict = {}
+        start = lambda: before.update(loaded.cache_stats(), launches=ops.LAUNCHES[0])
+        if clocks_out is not None:
+            with ClockSampler(device.index) as clk:
+                t_ms, res = timed_steps(fn, args.steps, args.warmup, world, device, on_start=start)
+            clocks_out.update(clk.summary())
+        else:
+            t_ms, res = timed_steps(fn, args.steps, args.warmup, world, device, on_start=start)
+        launched = ops.LAUNCHES[0] - before["launches"]
+        after = loaded.cache_stats()
+        return t_ms, res, {k: (after[k] - before[k]) / args.steps for k in after}, launched
+
+    def committed_of(argmaxes) -> int:
+        return sum(len(tree.accepted_path(a.cpu().unsqueeze(0))) + 1 for a in argmaxes)
+
+    # Host-managed caches (the reference's protocol: routes read back per
+    # layer, leases, copy-engine fills), eager, both execution policies.
+    host = {}
+    for pol in (policy, other):
+        t_ms, ams, per_step, _ = timed_with_stats(runner.step_device, pol)
+        host[pol] = (t_ms, ams, per_step)
+    assert all(torch.equal(a, host[policy][1][0]) for a in host[other][1]), \
+        "execution policies gave different argmaxes"
+    loaded.set_expert_execution_policy(policy)
+    h_e2e_ms, h_e2e = timed_steps(runner.step_e2e, args.steps, 1, world, device)
+    host_managed = {
+        pol.value: {"value": round(committed_of(host[pol][1]) / (host[pol][0] / 1e3), 4), "unit": "tokens/s",
+                    "ms_per_step": round(host[pol][0] / args.steps, 3), "cache_per_step": host[pol][2],
+                    "h2d": h2d_roofline_of(host[pol][2], host[pol][0] / args.steps, h2d_peak)}
+        for pol in (policy, other)}
+    host_managed["e2e"] = {"value": round(sum(h_e2e) / (h_e2e_ms / 1e3), 4), "unit": "tokens/s",
+                           "ms_per_step": round(h_e2e_ms / args.steps, 3), "execution_policy": policy.value}
+    host_managed["note"] = ("eager passes; each layer reads its routed experts back, leases them on the host "
+                            "and fills misses with the copy engine")
+
+    # Device-managed caches: the same cache decisions taken on the device,
+    # misses filled by a kernel from page-locked host memory, and the whole
+    # verify pass replayed from one CUDA graph (the headline).
+    from specfit_b200.runtime.verify_graph import VerifyGraph
+
+    torch.cuda.synchronize()
+    loaded.enter_device_managed_caches()
+    vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device, forward=runner.fwd)
+    launched0 = ops.LAUNCHES[0]
+    vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
+    launches_per_pass = (ops.LAUNCHES[0] - launched0) // 3  # two warm-up passes + the captured one
+    dev_runs = {}
+    clock_summary: dict = {}
+    for pol in (other, policy):  # the headline policy last, with the clocks sampled
+        t_ms, ams, per_step, _ = timed_with_stats(lambda: vg.replay().clone(), pol,
+                                                  clock_summary if pol is policy else None)
+        dev_runs[pol] = (t_ms, ams, per_step)
+    assert all(torch.equal(a, host[policy][1][0]) for r in dev_runs.values() for a in r[1]), \
+        "device-managed caches gave different argmaxes"
+    ms, ams, timed_stats = dev_runs[policy]
+    launches = launches_per_pass * args.steps
+    value = sum_over_ranks(committed_of(ams), world, device) / (ms / 1e3)
+    h2d_roofline = h2d_roofline_of(timed_stats, ms / args.steps, h2d_peak)
     other_policy = {"execution_policy": other.value,
-                    "value": round(sum(len(tree.accepted_path(a.cpu().unsqueeze(0))) + 1 for a in oams)
-                                   / (oms / 1e3), 4),
-                    "unit": "tokens/s", "ms_per_step": round(oms / args.steps, 3),
-                    "cache_per_step": ostats,
-                    "h2d": h2d_roofline_of(ostats, oms / args.steps, h2d_peak)}
+                    "value": round(committed_of(dev_runs[other][1]) / (dev_runs[other][0] / 1e3), 4),
+                    "unit": "tokens/s", "ms_per_step": round(dev_runs[other][0] / args.steps, 3),
+                    "cache_per_step": dev_runs[other][2],
+                    "h2d": h2d_roofline_of(dev_runs[other][2], dev_runs[other][0] / args.steps, h2d_peak)}
     loaded.set_expert_execution_policy(policy)
 
-    e2e_ms, e2e_comm = timed_steps(runner.step_e2e, args.steps, 1, world, device)
+    def device_e2e():
+        vg.load(runner.h_ids, runner.h_mask, runner.h_pos)
+        return len(tree.accepted_path(vg.replay().cpu().unsqueeze(0))) + 1
+
+    e2e_ms, e2e_comm = timed_steps(device_e2e, args.steps, 1, world, device)
     e2e_total = sum_over_ranks(sum(e2e_comm), world, device)
+    del vg
+    torch.cuda.synchronize()
+    loaded.leave_device_managed_caches()
+    stats24 = loaded.cache_stats()
 
     # The same passes under predicted cross-layer prefetch (the reference
     # runner's Qwen3ExpertPrefetch: lookahead 1, 2 copies in flight), each
@@ -785,9 +830,12 @@ def b200_arm(args):
         "config": headline_config(args),
         "forward": ("Hugging Face decoder layers" if args.hf_forward else
                     "lean fused layer forward (runtime/lean_forward.py)"),
+        "cache_mode": ("device-managed caches (misses planned and filled on the device), the verify pass "
+                       "replayed from one CUDA graph"),
         "execution_policy": policy.value,
         "cache_per_step": timed_stats,
         "other_policy": other_policy,
+        "host_managed": host_managed,
         "predicted_prefetch": {"value": round(pf_value, 4), "unit": "tokens/s",
                                "ms_per_step": round(pf_ms / args.steps, 3),
                                "predictions": "routes of the previous verify pass",
@@ -796,7 +844,7 @@ def b200_arm(args):
         "e2e": {"value": round(e2e_total / (e2e_ms / 1e3), 4), "unit": "tokens/s",
                 "h2d_bytes_per_step": runner.h2d_bytes, "d2h_bytes_per_step": runner.d2h_bytes,
                 "ms_per_step": round(e2e_ms / args.steps, 3)},
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
         "setup_s": round(build_s, 1),
         "roofline": {"h2d": h2d_roofline},
     }

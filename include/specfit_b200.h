@@ -344,6 +344,47 @@ SF_API int sf_cache_forget(void* cache, int which);
 SF_API int sf_cache_set_version(void* cache, int64_t version);
 SF_API int sf_cache_export(void* cache, void* image, size_t capacity, size_t* needed);
 SF_API int sf_cache_import(void* cache, const void* image, size_t size);
+/* Hand-over with the device-resident directory: slot experts (-1 empty),
+ * generations, last-use stamps, expert->slot of resident experts, the LRU
+ * clock and the counters {h2d, hits, joins, evictions}.  Export needs no
+ * active lease and no fill in flight; adopt installs a state whose assigned
+ * slots all hold published experts. */
+SF_API int sf_cache_export_slots(void* cache, int32_t* slot_expert, int32_t* slot_gen, int64_t* slot_stamp,
+                                 int32_t* expert_slot, int64_t* clock, int64_t* counters);
+SF_API int sf_cache_adopt_slots(void* cache, const int32_t* slot_expert, const int32_t* slot_gen,
+                                const int64_t* slot_stamp, int64_t clock, const int64_t* counters);
+
+/*
+ * Device-resident expert directory (device-managed cache mode).  The slot
+ * bookkeeping of one cache in HBM: slot_expert[S], slot_gen[S],
+ * slot_stamp[S] (int64), expert_slot[E], clock[1] and counters[4] (int64).
+ * sf_dir_plan (one CTA) takes, for the dispatch's active experts (ascending,
+ * or resident ones first), the decisions of the host wave loop: per wave up
+ * to S experts are leased — a resident one keeps its slot, a missing one
+ * evicts the least recently used unleased slot (new generation, a fill
+ * record) — each acquisition and, after the wave, each release advancing the
+ * LRU clock.  Outputs per wave w < waves: wave_table[w][E] (expert -> slot,
+ * -1 outside the wave), wave_active[w][E], wave_count[w], and the fill list
+ * fill_expert[w][S] / fill_slot[w][S] / fill_count[w].  status[0] is set to
+ * 1 if the experts did not fit `waves` waves, 2 on an expert id outside
+ * [0, E).  sf_dir_fill copies wave w's missing experts (fill_count read on
+ * the device) from device-mapped page-locked host memory — expert_src[E]
+ * holds each expert's device address — into storage + slot * slot_stride,
+ * expert_bytes each, with `grid` CTAs of SM loads.  Both are stream-ordered
+ * and allocate nothing.  sf_host_device_address gives the device address of
+ * page-locked, device-mapped host memory (SF_ERR_UNSUPPORTED otherwise).
+ * Replaces the host round trip of qwen3_offloaded_experts.py:112 /
+ * :173-175 (reading the routed experts back before leasing).
+ */
+SF_API int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, void* expert_slot, void* clock,
+                       void* counters, const void* active, const void* num_active, int num_experts,
+                       int num_slots, int waves, int resident_first, void* wave_table, void* wave_active,
+                       void* wave_count, void* fill_expert, void* fill_slot, void* fill_count, void* status,
+                       void* stream);
+SF_API int sf_dir_fill(const void* expert_src, void* storage, int64_t slot_stride_bytes, int64_t expert_bytes,
+                       const void* fill_expert, const void* fill_slot, const void* fill_count, int num_slots,
+                       int grid, void* stream);
+SF_API int sf_host_device_address(const void* host, uint64_t* device_address);
 
 /*
  * Tree attention (GQA): for query row i of head h (kv head h / (Hq/Hkv)),

@@ -136,6 +136,12 @@ SIGNATURES = {
     "sf_cache_set_version": (_i32, [_vp, _i64]),
     "sf_cache_export": (_i32, [_vp, _vp, _sz, ctypes.POINTER(_sz)]),
     "sf_cache_import": (_i32, [_vp, _vp, _sz]),
+    "sf_cache_export_slots": (_i32, [_vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_i64), _vp]),
+    "sf_cache_adopt_slots": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp]),
+    "sf_dir_plan": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                           _vp, _vp, _vp, _vp, _vp]),
+    "sf_dir_fill": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp]),
+    "sf_host_device_address": (_i32, [_vp, ctypes.POINTER(_u64)]),
     "sf_slot_fill_batch": (_i32, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
                                   _i32, _vp]),
     "sf_specfit_select": (_i32, [_i32, _vp, _vp, _vp, _i32, _vp, _vp, _i32, ctypes.c_double,

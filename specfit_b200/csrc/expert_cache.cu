@@ -746,3 +746,75 @@ extern "C" int sf_cache_import(void* h, const void* image, size_t size) {
   for (int32_t s = 0; s < m.nslots; ++s) m.index(s);
   return SF_OK;
 }
+
+// State hand-over with the device-resident directory (expert_directory.cu):
+// export writes the slots, the expert->slot map of published experts, the
+// LRU clock and the counters (h2d, hits, joins, evictions); it needs no
+// lease and no fill still in flight.  adopt installs such a state back: every
+// assigned slot holds a published expert, no fill is outstanding, no guard
+// is pending (the caller synchronised the device).
+extern "C" int sf_cache_export_slots(void* h, int32_t* slot_expert, int32_t* slot_gen, int64_t* slot_stamp,
+                                     int32_t* expert_slot, int64_t* clock, int64_t* counters) {
+  using namespace sf;
+  Manager& m = *as_mgr(h);
+  std::lock_guard<std::mutex> lock(m.mu);
+  if (int rc = retire(m)) return rc;
+  if (int rc = retire_guards(m)) return rc;
+  for (const Slot& s : m.slot)
+    if (s.leases) return set_error(SF_ERR_STATE, "device-managed mode cannot start with an active lease");
+  for (int32_t e = 0; e < m.nexperts; ++e)
+    if (m.where[e] == kInFlight)
+      return set_error(SF_ERR_STATE, "device-managed mode needs every expert fill complete");
+  for (int32_t s = 0; s < m.nslots; ++s) {
+    slot_expert[s] = m.slot[s].expert;
+    slot_gen[s] = (int32_t)m.slot[s].generation;
+    slot_stamp[s] = (int64_t)m.slot[s].stamp;
+  }
+  for (int32_t e = 0; e < m.nexperts; ++e) expert_slot[e] = m.where[e] == kResident ? m.home[e] : -1;
+  *clock = (int64_t)m.seq;
+  counters[0] = m.h2d;
+  counters[1] = m.hits;
+  counters[2] = m.joins;
+  counters[3] = m.evictions;
+  return SF_OK;
+}
+
+extern "C" int sf_cache_adopt_slots(void* h, const int32_t* slot_expert, const int32_t* slot_gen,
+                                    const int64_t* slot_stamp, int64_t clock, const int64_t* counters) {
+  using namespace sf;
+  Manager& m = *as_mgr(h);
+  std::lock_guard<std::mutex> lock(m.mu);
+  for (const Slot& s : m.slot)
+    if (s.leases) return set_error(SF_ERR_STATE, "cannot adopt a device state while a lease is active");
+  for (int32_t s = 0; s < m.nslots; ++s)
+    SF_CHECK_ARG(slot_expert[s] >= -1 && slot_expert[s] < m.nexperts, "slot %d holds an unknown expert", s);
+  m.idle.clear();
+  m.fills.clear();
+  for (int32_t e = 0; e < m.nexperts; ++e) {
+    m.where[e] = kAbsent;
+    m.home[e] = -1;
+    m.fill_seq[e] = -1;
+  }
+  for (int32_t s = 0; s < m.nslots; ++s) {
+    Slot& sl = m.slot[s];
+    for (const Guard& g : sl.guards) m.spare.push_back(g.event);
+    sl.guards.clear();
+    sl.expert = slot_expert[s];
+    sl.generation = (uint32_t)slot_gen[s];
+    sl.stamp = (uint64_t)slot_stamp[s];
+    sl.ready = nullptr;
+    if (sl.expert >= 0) {
+      SF_CHECK_ARG(m.where[sl.expert] == kAbsent, "expert %d is in two slots", sl.expert);
+      m.where[sl.expert] = kResident;
+      m.home[sl.expert] = s;
+    }
+  }
+  for (int32_t s = 0; s < m.nslots; ++s) m.index(s);
+  m.seq = (uint64_t)clock;
+  m.h2d = counters[0];
+  m.hits = counters[1];
+  m.joins = counters[2];
+  m.evictions = counters[3];
+  ++m.version;
+  return SF_OK;
+}

@@ -26,7 +26,12 @@ Additions over the reference:
   straight from their slots, and ``device_slot_table()`` for the case where
   every expert is resident (the MoE block then runs with no host
   synchronisation; its hits are counted on the device and folded into
-  ``stats()``).
+  ``stats()``);
+* device-managed mode (``enter_device_mode`` / ``leave_device_mode``): the
+  bookkeeping moves to HBM (``runtime/expert_directory.py``) and misses are
+  planned and filled on the device, so a pass with misses needs no host
+  round trip; reading ``stats()`` / ``snapshot()`` mirrors the device state
+  back, and host leases are refused until the mode is left.
 """
 from __future__ import annotations
 
@@ -40,6 +45,7 @@ import torch
 
 from .. import _native as N
 from .cache_snapshot import CacheSlotSnapshot, GpuExpertCacheSnapshot, PendingTransferSnapshot
+from .expert_directory import DeviceExpertDirectory
 from .lease import ExpertCacheStats, ExpertLease, NoEvictableSlotError
 from .state import RuntimeEventKind
 
@@ -326,6 +332,8 @@ class GpuExpertCache:
         self._lock = RLock()
         self._device_hits = None         # int64 device counter of fast-path hits
         self._table = None               # (state version, keys, device slot table)
+        self._directory = None           # DeviceExpertDirectory, built on first use
+        self._device_mode = False
 
     # ------------------------------------------------------------ properties
     @property
@@ -431,6 +439,11 @@ class GpuExpertCache:
         if self._closed or self._closing:
             raise RuntimeError("expert cache is closed")
 
+    def _check_host_managed(self) -> None:
+        self._check_open()
+        if self._device_mode:
+            raise RuntimeError("expert cache is device-managed: call leave_device_mode() first")
+
     def _indices(self, keys) -> list:
         out = []
         for key in keys:
@@ -444,7 +457,7 @@ class GpuExpertCache:
         """Runs one native acquire over ``keys``; returns a lease per key
         (``None`` where nothing was granted), emitting the observer records
         of every hit, join, eviction and submission in order."""
-        self._check_open()
+        self._check_host_managed()
         idx = self._indices(keys)
         n = len(idx)
         if n == 0:
@@ -551,7 +564,7 @@ class GpuExpertCache:
         slot can change while the table is used)."""
         with self._lock:
             self._check_open()
-            if self._n_slots < len(self._keys):
+            if self._device_mode or self._n_slots < len(self._keys):
                 return None
             table = (ctypes.c_int32 * len(self._keys))()
             complete = ctypes.c_int()
@@ -587,14 +600,81 @@ class GpuExpertCache:
 
     def prefill_all(self) -> None:
         """Leases and releases every source once (fills the empty ones)."""
+        self._check_host_managed()
         for key in self._keys:
             if key in self._resident or key in self._inflight:
                 continue
             self.acquire(key).release()
 
+    # --------------------------------------------------- device-managed mode
+    @property
+    def device_managed(self) -> bool:
+        return self._device_mode
+
+    @property
+    def directory(self) -> DeviceExpertDirectory | None:
+        """The HBM bookkeeping while device-managed, else ``None``."""
+        return self._directory if self._device_mode else None
+
+    def enter_device_mode(self) -> DeviceExpertDirectory:
+        """Moves the bookkeeping to the device (synchronises the device; needs
+        no active lease and every fill complete).  The sources must be
+        page-locked and device-mapped."""
+        with self._lock:
+            self._check_open()
+            if self._device_mode:
+                return self._directory
+            torch.cuda.synchronize(self.device)
+            self._flush_device_hits()
+            S, E = self._n_slots, len(self._keys)
+            slot_expert, slot_gen = (ctypes.c_int32 * S)(), (ctypes.c_int32 * S)()
+            slot_stamp, expert_slot = (ctypes.c_int64 * S)(), (ctypes.c_int32 * E)()
+            clock, counters = ctypes.c_int64(), (ctypes.c_int64 * 4)()
+            N.check(N.lib.sf_cache_export_slots(self._h, slot_expert, slot_gen, slot_stamp, expert_slot,
+                                                ctypes.byref(clock), counters), "device-managed mode")
+            if self._directory is None:
+                self._directory = DeviceExpertDirectory(self)
+            self._directory.load(dict(
+                slot_expert=torch.tensor(list(slot_expert), dtype=torch.int32),
+                slot_gen=torch.tensor(list(slot_gen), dtype=torch.int32),
+                slot_stamp=torch.tensor(list(slot_stamp), dtype=torch.int64),
+                expert_slot=torch.tensor(list(expert_slot), dtype=torch.int32),
+                clock=clock.value, counters=torch.tensor(list(counters), dtype=torch.int64)))
+            torch.cuda.synchronize(self.device)
+            self._device_mode = True
+            self._table = None
+            return self._directory
+
+    def _mirror_device_state(self) -> None:
+        """Installs the device bookkeeping in the host manager (synchronises
+        the device); the device copy stays authoritative while the mode lasts."""
+        if not self._device_mode:
+            return
+        torch.cuda.synchronize(self.device)
+        st = self._directory.read()
+        if st["status"]:
+            raise RuntimeError(f"device expert directory failed (status {st['status']})")
+        S = self._n_slots
+        se = (ctypes.c_int32 * S)(*st["slot_expert"].tolist())
+        sg = (ctypes.c_int32 * S)(*st["slot_gen"].tolist())
+        ss = (ctypes.c_int64 * S)(*st["slot_stamp"].tolist())
+        cn = (ctypes.c_int64 * 4)(*st["counters"].tolist())
+        N.check(N.lib.sf_cache_adopt_slots(self._h, se, sg, ss, st["clock"], cn), "device-managed mode")
+        self._events.clear()
+
+    def leave_device_mode(self) -> None:
+        """Returns the bookkeeping to the host manager (synchronises the device)."""
+        with self._lock:
+            if not self._device_mode:
+                return
+            self._mirror_device_state()
+            self._device_mode = False
+            self._table = None
+
     # ------------------------------------------------------------ inspection
     def stats(self) -> ExpertCacheStats:
         with self._lock:
+            self._mirror_device_state()
             self._flush_device_hits()
             c = _NativeState(self, 3).counters
             return ExpertCacheStats(int(c.h2d_submissions), int(c.resident_hits), int(c.inflight_joins),
@@ -602,11 +682,13 @@ class GpuExpertCache:
 
     def resident_expert_ids(self) -> tuple:
         with self._lock:
+            self._mirror_device_state()
             st = _NativeState(self, 1)
             return tuple(k for e, k in enumerate(self._keys) if st.where[e] == _RESIDENT)
 
     def snapshot(self) -> GpuExpertCacheSnapshot:
         with self._lock:
+            self._mirror_device_state()
             self._flush_device_hits()
             st = _NativeState(self, 0)
             fills = self._native_fills()
@@ -644,7 +726,7 @@ class GpuExpertCache:
 
     def cold_reset(self) -> None:
         with self._lock:
-            self._check_open()
+            self._check_host_managed()
             if self.active_lease_count:
                 raise RuntimeError("cold reset cannot run while an active lease exists")
             if not self._quiescent():
@@ -656,7 +738,7 @@ class GpuExpertCache:
             self._table = None
 
     def _require_checkpoint_boundary(self) -> None:
-        self._check_open()
+        self._check_host_managed()
         if self._observer is not None:
             raise RuntimeError("checkpoint restoration requires no active cache observer")
         if self.active_lease_count:
@@ -702,6 +784,8 @@ class GpuExpertCache:
         with self._lock:
             if self._closed:
                 return
+            if self._device_mode:
+                self.leave_device_mode()
             if not self._closing and self.active_lease_count:
                 raise RuntimeError("expert cache cannot close while an active lease exists")
             self._closing = True

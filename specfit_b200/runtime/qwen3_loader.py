@@ -291,7 +291,7 @@ def map_packed_layer(path: Path, experts: int, packed: int) -> torch.Tensor:
     return raw[off: off + nbytes].view(torch.bfloat16).view(experts, packed)
 
 
-_HOST_REGISTER_READ_ONLY = 0x08  # cudaHostRegisterReadOnly: the mapping is never written
+_HOST_REGISTER_READ_ONLY = 0x08 | 0x02 | 0x01  # read-only (never written), mapped for kernels, portable
 
 
 class MappedExpertPool:

@@ -98,6 +98,11 @@ class Qwen3OffloadedExperts(nn.Module):
         if self.num_experts == 0:
             raise KeyError(f"unknown expert {ExpertKey(self.layer_id, int(top_k_index.reshape(-1)[0]))!r}")
         h = hidden_states.contiguous()
+        if self.cache.device_managed:
+            if execution_order is not None:
+                raise ValueError("an explicit execution_order needs a host-managed expert cache")
+            ys, d = self._forward_device(h, top_k_index, top_k_weights)
+            return ops.moe_combine(ys, d, top_k_index)
         d = ops.moe_dispatch(top_k_index, self.num_experts)
         xs, ws = ops.moe_gather(h, top_k_weights, d)
         storage = self.cache.storage.view(self.cache.slot_count, -1)
@@ -123,6 +128,8 @@ class Qwen3OffloadedExperts(nn.Module):
         self._validate_inputs(hidden_states, top_k_index, top_k_weights)
         if self._prediction_scheduler is not None or hidden_states.shape[0] == 0 or self.num_experts == 0:
             return None
+        if self.cache.device_managed:
+            return self._forward_device(hidden_states.contiguous(), top_k_index, top_k_weights)
         fixed = self.cache.device_slot_table(self._keys)
         if fixed is None:
             return None
@@ -137,6 +144,34 @@ class Qwen3OffloadedExperts(nn.Module):
         xs, ws = ops.moe_gather(h, top_k_weights, d)
         ys = ops.grouped_swiglu(xs, ws, d, fixed, storage, self.hidden_size, self.intermediate_size,
                                 impl=self.swiglu_impl)
+        return ys, d
+
+    def _forward_device(self, h, top_k_index, top_k_weights):
+        """The layer with a device-managed cache: the directory plans the
+        waves the host path would run (same leases, evictions and fills, in
+        the same order) and each wave's misses are copied from host memory
+        by a kernel, so nothing here waits for the device.  Returns the
+        weighted expert rows in dispatch order and the dispatch."""
+        cache = self.cache
+        directory = cache.directory
+        if cache.source_keys() != self._keys:
+            raise RuntimeError("device-managed mode needs the cache's sources to be this layer's experts "
+                               "in id order")
+        if self.reduction_mode is not ReductionMode.CANONICAL:
+            raise ValueError("device-managed mode reduces canonically only")
+        stream = torch.cuda.current_stream(h.device).cuda_stream
+        d = ops.moe_dispatch(top_k_index, self.num_experts)
+        xs, ws = ops.moe_gather(h, top_k_weights, d)
+        storage = cache.storage.view(cache.slot_count, -1)
+        directory.plan(d, self.execution_policy is ExpertExecutionPolicy.RESIDENT_FIRST, stream)
+        ys = torch.empty(xs.shape[0], self.hidden_size, dtype=h.dtype, device=h.device)
+        act = torch.empty(max(xs.shape[0], 1), self.intermediate_size, dtype=h.dtype, device=h.device)
+        for w in range(directory.waves):  # later waves are empty unless the layer needs more experts than slots
+            directory.fill(w, storage, stream)
+            ops.grouped_swiglu(xs, ws, d, directory.wave_table[w], storage, self.hidden_size,
+                               self.intermediate_size, impl=self.swiglu_impl, active=directory.wave_active[w],
+                               num_active=directory.wave_count[w:w + 1], act_workspace=act, out=ys)
+        ops._launched(1 + directory.waves)  # the plan and one fill per wave (SwiGLU counts itself)
         return ys, d
 
     def _forward_waves(self, h, top_k_index, d, xs, ws, storage, execution_order):

@@ -78,7 +78,9 @@ class ExpertHostPool:
             self.data = torch.from_file(shm_path, shared=True, size=n, dtype=dtype).view(
                 layers, experts, elems)
         nbytes = self.data.numel() * self.data.element_size()
-        rc = torch.cuda.cudart().cudaHostRegister(self.data.data_ptr(), nbytes, 0)
+        # Portable | mapped: page-locked for every context and readable by
+        # kernels (the device-managed cache fills slots with SM loads).
+        rc = torch.cuda.cudart().cudaHostRegister(self.data.data_ptr(), nbytes, 0x01 | 0x02)
         if int(rc) != 0:
             import resource
 
@@ -153,6 +155,23 @@ class LoadedB200Qwen3:
         for c in self.caches:
             c.prefill_all()
         torch.cuda.synchronize()
+
+    def enter_device_managed_caches(self) -> None:
+        """Every layer's cache in device-managed mode (misses planned and
+        filled on the device; a verify pass then needs no host round trip
+        and can be captured in a CUDA graph)."""
+        modules = self._expert_modules()
+        if any(m._prediction_scheduler is not None for m in modules):
+            raise RuntimeError("cannot switch cache mode during predicted prefetch")
+        for m in modules:
+            if m.reduction_mode is not ReductionMode.CANONICAL:
+                raise ValueError("device-managed caches reduce canonically only")
+        for c in self.caches:
+            c.enter_device_mode()
+
+    def leave_device_managed_caches(self) -> None:
+        for c in self.caches:
+            c.leave_device_mode()
 
     def set_expert_execution_policy(self, policy) -> None:
         policy = ExpertExecutionPolicy(policy)

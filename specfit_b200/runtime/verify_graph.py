@@ -1,10 +1,11 @@
 """One verify pass captured as a CUDA graph.
 
-When every layer's expert cache holds all of its experts, the verify forward
+When every layer's expert cache holds all of its experts, or the caches are
+device-managed (misses planned and filled on the device), the verify forward
 (``eagle3_tree.py:1243-1250`` in the reference: the target over the seed +
 tree tokens under the ancestor mask) needs no host synchronisation: routing,
-grouping, the grouped SwiGLU launches and the combine all run from device
-state.  ``VerifyGraph`` captures that forward once for a fixed tree size and
+grouping, fills, the grouped SwiGLU launches and the combine all run from
+device state.  ``VerifyGraph`` captures that forward once for a fixed tree size and
 committed length and replays it, removing the per-op host launch cost of the
 eager Hugging Face forward.
 
@@ -69,9 +70,11 @@ class VerifyGraph:
                 if not moe.use_peer:
                     raise RuntimeError("VerifyGraph needs the expert-parallel layers in peer mode")
                 continue
+            if experts.cache.device_managed:  # misses are planned and filled on the device
+                continue
             if experts.cache.device_slot_table(experts._keys) is None:
                 raise RuntimeError("VerifyGraph needs every expert of every layer resident "
-                                   "(slots >= experts, caches warmed)")
+                                   "(slots >= experts, caches warmed) or device-managed caches")
 
     def load(self, ids, mask, pos) -> None:
         """Copy one tree's inputs into the graph's static buffers (async)."""
