@@ -81,6 +81,8 @@ def parse_args(argv=None):
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-resident", action="store_true", help="skip the 128-slot variant")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the configuration 1, 3 and 4 measurements of the default line")
     p.add_argument("--cpu-layers", type=int, default=1, help="decoder layers timed on the CPU")
     p.add_argument("--mode", choices=("auto", "verify", "ep", "decode", "block", "graph", "sweep",
                                       "kernels"),
@@ -606,6 +608,92 @@ def reference_model_bytes(layers: int) -> int:
     return 2 * (layers * per_layer + 2 * 151936 * 2048 + 2048)
 
 
+def config1_block(device, h2d_peak_gbps=None, reps: int = 5, cpu_reps: int = 3) -> dict:
+    """BASELINE configuration 1 on the GPU: one fp32 MoE block (router +
+    experts + combine), 32 tokens, the seed-0 draw of
+    ``synthetic.config1_inputs``, with "0 slots": the cache's contents are
+    invalidated before every block (``GpuExpertCache.invalidate_contents``,
+    the reference's ``discard_completed_experts``), so every selected expert
+    is streamed from page-locked host memory on every call.  Host-managed
+    (copy-engine fills) and device-managed (kernel fills, no host round
+    trip) blocks are timed with CUDA events; the output is compared with the
+    reference-generated golden of the same input.  The CPU baseline is the
+    stock Hugging Face ``Qwen3MoeSparseMoeBlock`` in fp32 with the same
+    weights on all host cores."""
+    from transformers import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeSparseMoeBlock
+
+    from specfit_b200 import ops, synthetic
+    from specfit_b200.runtime import ExpertKey, GpuExpertCache, Qwen3OffloadedExperts
+    from specfit_b200.runtime.qwen3_verifier import ExpertHostPool
+
+    weights, x = synthetic.config1_inputs(seed=0, tokens=32)
+    E, H, I = weights.router.shape[0], weights.router.shape[1], weights.down.shape[2]
+    pool = ExpertHostPool(1, E, 3 * H * I, dtype=torch.float32)
+    for e in range(E):
+        pool.data[0, e].copy_(weights.packed(e))
+    cache = GpuExpertCache({ExpertKey(0, e): pool.data[0, e] for e in range(E)}, slot_count=E, device=device,
+                           adopt_pinned_sources=True)
+    experts = Qwen3OffloadedExperts(layer_id=0, cache=cache, hidden_size=H, intermediate_size=I)
+    xd, wr = x.to(device), weights.router.to(device)
+
+    def block():
+        _, w, idx = ops.router_topk(xd, wr, 8, True)
+        return experts(xd, idx, w)
+
+    rows = {}
+    out = None
+    for mode in ("host", "device"):
+        times, fills = [], []
+        for i in range(reps + 1):
+            torch.cuda.synchronize()
+            if cache.device_managed:
+                cache.leave_device_mode()
+            cache.invalidate_contents()
+            if mode == "device":
+                cache.enter_device_mode()
+            before = cache.stats().h2d_submissions
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            out = block()
+            b.record()
+            b.synchronize()
+            if i:
+                times.append(a.elapsed_time(b))
+                fills.append(cache.stats().h2d_submissions - before)
+        ms = statistics.median(times)
+        nbytes = statistics.median(fills) * 3 * H * I * 4
+        rows[mode] = {"block_ms": round(ms, 3), "fills_per_block": statistics.median(fills),
+                      "h2d_bytes": int(nbytes), "h2d_GBps": round(nbytes / (ms * 1e-3) / 1e9, 2)}
+        if h2d_peak_gbps:
+            rows[mode]["h2d_frac"] = round(nbytes / (ms * 1e-3) / 1e9 / h2d_peak_gbps, 4)
+    cache.leave_device_mode()
+    golden = np.load(REPO / "tests" / "golden" / "moe_cfg1_f32.npz")
+    err = float(np.abs(out.float().cpu().numpy() - golden["out_specfit"]).max())
+    cache.close()
+    pool.close()
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = Qwen3MoeConfig(hidden_size=H, num_experts=E, num_experts_per_tok=8, moe_intermediate_size=I,
+                         norm_topk_prob=True)
+    ref = Qwen3MoeSparseMoeBlock(cfg).eval()
+    with torch.no_grad():
+        ref.gate.weight.copy_(weights.router)
+        ref.experts.gate_up_proj.copy_(weights.gate_up)
+        ref.experts.down_proj.copy_(weights.down)
+        ref(x[None])
+        t0 = time.perf_counter()
+        for _ in range(cpu_reps):
+            ref(x[None])
+        cpu_ms = (time.perf_counter() - t0) / cpu_reps * 1e3
+    return {"workload": "BASELINE config 1: one fp32 MoE block, 32 tokens, hidden 2048, 128 experts top-8, "
+                        "moe_intermediate 768, 0 cache slots (contents invalidated before every block)",
+            "host_managed": rows["host"], "device_managed": rows["device"],
+            "h2d_peak_GBps": h2d_peak_gbps, "max_abs_err_vs_reference_golden": err,
+            "cpu_baseline": {"block_ms": round(cpu_ms, 2), "cores": torch.get_num_threads(), "kind": "reference",
+                             "sample": "stock HF Qwen3MoeSparseMoeBlock, fp32, same weights and input"}}
+
+
 def cpu_reference_run(args, model_layers: int, steps: int, warmup: int):
     """The reference's CPU path: a stock Hugging Face Qwen3-MoE target on the
     host cores (all threads) — embedding, ``model_layers`` decoder layers
@@ -760,13 +848,18 @@ def b200_arm(args):
 
     torch.cuda.synchronize()
     loaded.enter_device_managed_caches()
-    vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device, forward=runner.fwd)
-    launched0 = ops.LAUNCHES[0]
-    vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
-    launches_per_pass = (ops.LAUNCHES[0] - launched0) // 3  # two warm-up passes + the captured one
     dev_runs = {}
     clock_summary: dict = {}
+    vg = None
     for pol in (other, policy):  # the headline policy last, with the clocks sampled
+        # The policy is an argument of the captured plan kernels: one graph per policy.
+        del vg
+        torch.cuda.synchronize()
+        loaded.set_expert_execution_policy(pol)
+        vg = VerifyGraph(loaded.model, runner.cache, q_len=1 + args.nodes, device=device, forward=runner.fwd)
+        launched0 = ops.LAUNCHES[0]
+        vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
+        launches_per_pass = (ops.LAUNCHES[0] - launched0) // 3  # two warm-up passes + the captured one
         t_ms, ams, per_step, _ = timed_with_stats(lambda: vg.replay().clone(), pol,
                                                   clock_summary if pol is policy else None)
         dev_runs[pol] = (t_ms, ams, per_step)
@@ -921,6 +1014,26 @@ def b200_arm(args):
                                    eager_in_model=eager_block)
         result["roofline"] = dict(swiglu_roofline(loaded, device, 1 + args.nodes, peaks) or {},
                                   h2d=h2d_roofline)
+
+    if world == 1 and not args.no_extras and not args.no_resident and args.slots < cfg.num_experts:
+        # The other BASELINE configurations that run on this target and pool,
+        # each reported under its own key and never fatal to the headline.
+        try:  # configuration 4 on the resident (128-slot, warm) caches left by the resident variant
+            dec, spec = decode_measure(loaded, cfg, args, device, cpu=not args.no_cpu_baseline)
+            spec.release_graphs()
+            keep = ("metric", "value", "unit", "ms_per_step", "e2e", "cycle", "cpu_baseline", "config",
+                    "reference_cost_model", "gpu_launches", "clocks")
+            result["config4"] = {k: dec[k] for k in keep if k in dec}
+        except Exception as err:
+            result["config4"] = {"error": f"{type(err).__name__}: {err}"}
+        try:
+            result["config3"] = sweep_measure(loaded, pool, cfg, args, device)
+        except Exception as err:
+            result["config3"] = {"error": f"{type(err).__name__}: {err}"}
+        try:
+            result["config1"] = config1_block(device, h2d_peak["GBps"])
+        except Exception as err:
+            result["config1"] = {"error": f"{type(err).__name__}: {err}"}
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         per_pass, desc, cores = cpu_reference_sample(args, layers=args.cpu_layers)
@@ -1266,12 +1379,8 @@ def cpu_decode_sample(cfg, verify_tokens: int, ctx: int, rows_per_level: int, le
 
 
 def decode_mode(args):
-    """end-to-end speculative decoding on one B200."""
-    from specfit_b200 import ops, synthetic
-    from specfit_b200.runtime.eagle3_drafter import build_random_drafter
+    """BASELINE configuration 4 alone (``decode_measure``) on a freshly built target."""
     from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
-    from specfit_b200.runtime.speculator import B200TreeSpeculator, BernoulliAcceptance
-    from specfit_b200.selection import SelectionCostModel
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -1281,6 +1390,22 @@ def decode_mode(args):
                                           seed=args.seed)
     apply_kernel_options(loaded, args)
     loaded.warm_all_caches()
+    result, spec = decode_measure(loaded, cfg, args, device, setup_s=time.perf_counter() - t0)
+    print(json.dumps(result), flush=True)
+    spec.release_graphs()
+    loaded.close()
+
+
+def decode_measure(loaded, cfg, args, device, setup_s: float = 0.0, cpu: bool | None = None):
+    """end-to-end speculative decoding on one B200
+    over ``loaded`` (every expert resident).  Returns the result line and the
+    speculator (whose graphs the caller releases)."""
+    from specfit_b200 import ops, synthetic
+    from specfit_b200.runtime.eagle3_drafter import build_random_drafter
+    from specfit_b200.runtime.speculator import B200TreeSpeculator, BernoulliAcceptance
+    from specfit_b200.selection import SelectionCostModel
+
+    t0 = time.perf_counter()
     L = cfg.num_hidden_layers
     aux = (1, 23, 44) if L == 48 else tuple(sorted({1 % L, (L * 23) // 48, (L * 44) // 48}))
     drafter = build_random_drafter(loaded.model, seed=args.seed + 1000, aux_layers=aux)
@@ -1292,7 +1417,7 @@ def decode_mode(args):
                               route_seed=args.seed, graphs=not args.eager_decode,
                               reserve_tokens=args.decode_ctx + args.new_tokens + 16,
                               lean=not args.hf_forward)
-    setup_s = time.perf_counter() - t0
+    setup_s += time.perf_counter() - t0
 
     def run(new_tokens, acceptance_seed):
         spec.acceptance = BernoulliAcceptance(acceptance_seed)
@@ -1390,7 +1515,7 @@ def decode_mode(args):
                                              peaks)
     except Exception as err:  # reported, never fatal to the line
         result["roofline"] = {"error": f"{type(err).__name__}: {err}"}
-    if not args.no_cpu_baseline:
+    if (not args.no_cpu_baseline) if cpu is None else cpu:
         vt = 1 + int(round(mean([c.selected for c in cyc])))
         cycle_s, desc, cores = cpu_decode_sample(cfg, vt, args.decode_ctx, 8, 8)
         result["cpu_baseline"] = {"value": round(per_cycle / cycle_s, 5), "unit": "tokens/s",
@@ -1398,9 +1523,7 @@ def decode_mode(args):
                                   "sample": desc + f"; {per_cycle:.3f} committed tokens per cycle as "
                                             "measured on the GPU run (same seeds)",
                                   "seconds_per_cycle": round(cycle_s, 3)}
-    print(json.dumps(result), flush=True)
-    spec.release_graphs()
-    loaded.close()
+    return result, spec
 
 
 def reference_arm(args):
@@ -1528,32 +1651,23 @@ def graph_mode(args):
     loaded.close()
 
 
-def sweep_mode(args):
-    """the expert-cache sweep.  One 48-layer target
-    whose caches are rebuilt at each slot count over one shared pinned host
-    pool; every layer's routes are replaced by seeded per-layer Zipf(1.1)
+def sweep_measure(loaded, pool, cfg, args, device) -> dict:
+    """BASELINE configuration 3, the expert-cache sweep, on an already built
+    target: every layer's routes are replaced by seeded per-layer Zipf(1.1)
     top-8 routes (``synthetic.zipf_routes``) for the 129 verify rows of a
-    128-node tree.  Per slot count: the cold pass (fresh caches), then warm
-    passes (each starting from the state the previous one left), with their
-    CUDA-event times and fills (H2D submissions).  Derived: H2D GB/s of the
-    warm pass, the fill time exposed beyond the resident (128-slot warm) pass,
-    overlap = 1 - exposed / (fill bytes / warm-up fill rate), and the grouped
-    SwiGLU's phase-1 tiles per SM (its occupancy: 148 persistent CTAs)."""
+    128-node tree, and the caches are rebuilt at each slot count over the
+    shared page-locked pool.  Per slot count: the cold pass (fresh caches,
+    host-managed, eager) and warm passes with device-managed caches replayed
+    from one CUDA graph (each pass starts from the state the previous one
+    left), with CUDA-event times and fills per pass.  Derived: the warm
+    pass's H2D GB/s, the fill time it exposes beyond the resident (128-slot)
+    pass, overlap = 1 - exposed / (fill bytes at the pinned-copy rate), and
+    the grouped SwiGLU's phase-1 tiles per SM (148 persistent CTAs)."""
     from specfit_b200 import synthetic
     from specfit_b200.runtime import GpuExpertCache
-    from specfit_b200.runtime.qwen3_verifier import (ExpertHostPool, build_random_offloaded_qwen3,
-                                                     qwen3_moe_config)
+    from specfit_b200.runtime.verify_graph import VerifyGraph
 
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
-    cfg = qwen3_moe_config(args.layers)
     L, E = cfg.num_hidden_layers, cfg.num_experts
-    elems = 3 * cfg.hidden_size * cfg.moe_intermediate_size
-    pool = ExpertHostPool(L, E, elems)
-    pool.fill_random(args.seed, device)
-    loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=E, config=cfg, seed=args.seed,
-                                          pool=pool)
-    apply_kernel_options(loaded, args)
     nodes = args.sweep_nodes
     T = 1 + nodes
     routes = [torch.from_numpy(synthetic.zipf_routes(T, l, seed=args.seed + 3)).to(device) for l in range(L)]
@@ -1565,8 +1679,7 @@ def sweep_mode(args):
     ctx_ids = torch.randint(0, cfg.vocab_size, (1, args.ctx), generator=gen).to(device)
     tree = make_tree(nodes, args.sweep_depth, args.branch, seed=2, vocab=cfg.vocab_size)
     seed_tok = int(torch.randint(0, cfg.vocab_size, (1,), generator=gen))
-    runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device,
-                          fwd=make_forward(loaded.model, args.hf_forward))
+    peak = pinned_h2d_peak(pool, device)
 
     def set_slots(slots: int) -> None:
         torch.cuda.synchronize()
@@ -1579,59 +1692,83 @@ def sweep_mode(args):
         loaded.caches = tuple(new)
         torch.cuda.empty_cache()
 
-    def one_pass():
+    def timed(fn):
         before = loaded.cache_stats()["h2d_submissions"]
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        runner.step_device()
-        e.record()
-        e.synchronize()
-        return s.elapsed_time(e), loaded.cache_stats()["h2d_submissions"] - before
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b), loaded.cache_stats()["h2d_submissions"] - before
 
-    set_slots(E)
-    t0 = time.perf_counter()
-    loaded.warm_all_caches()
-    fill_gbps = pool.nbytes / (time.perf_counter() - t0) / 1e9
-    one_pass()
-    resident_ms = statistics.median(one_pass()[0] for _ in range(max(args.steps, 3)))
-    active = [len(set(r.reshape(-1).tolist())) for r in routes]
-    tiles = statistics.mean(a * (cfg.moe_intermediate_size // 64) for a in active)
-    rows = []
-    with ClockSampler(device.index) as clocks:
+    try:
+        set_slots(E)
+        loaded.warm_all_caches()
+        runner = VerifyRunner(loaded, ctx_ids, tree, seed_tok, device, fwd=make_forward(loaded.model, False))
+        timed(runner.step_device)
+        resident_ms = statistics.median(timed(runner.step_device)[0] for _ in range(3))
+        active = [len(set(r.reshape(-1).tolist())) for r in routes]
+        tiles = statistics.mean(a * (cfg.moe_intermediate_size // 64) for a in active)
+        rows = []
         for slots in [int(x) for x in args.sweep_slots.split(",")]:
             set_slots(slots)
-            cold_ms, cold_fills = one_pass()
-            warm = [one_pass() for _ in range(max(args.steps, 3))]
+            cold_ms, cold_fills = timed(runner.step_device)
+            loaded.enter_device_managed_caches()
+            vg = VerifyGraph(loaded.model, runner.cache, q_len=T, device=device, forward=runner.fwd)
+            vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
+            warm = [timed(vg.replay) for _ in range(max(args.steps, 3))]
+            del vg
+            torch.cuda.synchronize()
+            loaded.leave_device_managed_caches()
             warm_ms = statistics.median(w[0] for w in warm)
             warm_fills = warm[-1][1]
             fill_bytes = warm_fills * EXPERT_BYTES
             exposed = max(warm_ms - resident_ms, 0.0)
-            busy = fill_bytes / (fill_gbps * 1e9) * 1e3
+            busy = fill_bytes / (peak["GBps"] * 1e9) * 1e3
             rows.append({"slots": slots, "cold_ms": round(cold_ms, 2), "cold_fills": cold_fills,
                          "warm_ms": round(warm_ms, 2), "warm_fills": warm_fills,
                          "warm_h2d_GBps": round(fill_bytes / (warm_ms * 1e-3) / 1e9, 1),
                          "exposed_fill_ms": round(exposed, 2),
                          "overlap": round(1.0 - exposed / busy, 3) if busy > 0 else 1.0})
-    for h in hooks:
-        h.remove()
-    head = next((r for r in rows if r["slots"] == args.slots), rows[0])
+    finally:
+        for h in hooks:
+            h.remove()
+    return {"workload": (f"BASELINE config 3: {L}-layer target, {T} verify rows ({nodes}-node tree), "
+                         f"{args.ctx}-token context, per-layer Zipf(1.1) top-8 routes, slots {args.sweep_slots}; "
+                         "cold = fresh host-managed caches, warm = device-managed caches, one CUDA graph per pass"),
+            "rows": rows, "resident_ms": round(resident_ms, 2), "h2d_peak": peak,
+            "experts_per_layer_mean": round(statistics.mean(active), 1),
+            "swiglu_phase1_tiles_per_sm": round(tiles / num_sms_of(device), 2)}
+
+
+def sweep_mode(args):
+    """``--mode sweep``: configuration 3 alone (``sweep_measure``)."""
+    from specfit_b200.runtime.qwen3_verifier import (ExpertHostPool, build_random_offloaded_qwen3,
+                                                     qwen3_moe_config)
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = qwen3_moe_config(args.layers)
+    pool = ExpertHostPool(cfg.num_hidden_layers, cfg.num_experts, 3 * cfg.hidden_size * cfg.moe_intermediate_size)
+    pool.fill_random(args.seed, device)
+    loaded = build_random_offloaded_qwen3(device=device, slots_per_layer=cfg.num_experts, config=cfg,
+                                          seed=args.seed, pool=pool)
+    apply_kernel_options(loaded, args)
+    with ClockSampler(device.index) as clocks:
+        sweep = sweep_measure(loaded, pool, cfg, args, device)
+    head = next((r for r in sweep["rows"] if r["slots"] == args.slots), sweep["rows"][0])
     result = {
         "metric": "verify passes/s (config 3 sweep, warm cache)",
         "value": round(1e3 / head["warm_ms"], 3), "unit": "passes/s", "n_gpus": 1,
-        "steps": max(args.steps, 3), "warmup": 1, "ms_per_step": head["warm_ms"],
+        "steps": max(args.steps, 3), "warmup": 2, "ms_per_step": head["warm_ms"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init bf16 weights; per-layer Zipf(1.1) top-8 routes replace the router)",
-        "config": {"workload": (f"BASELINE config 3: {L}-layer target, {T} verify rows ({nodes}-node tree), "
-                                f"{args.ctx}-token context, slots {args.sweep_slots}, cold and warm"),
-                   "headline_slots": head["slots"]},
-        "rows": rows,
-        "resident_ms": round(resident_ms, 2),
-        "warm_fill_GBps": round(fill_gbps, 1),
-        "experts_per_layer_mean": round(statistics.mean(active), 1),
-        "swiglu_phase1_tiles_per_sm": round(tiles / num_sms_of(device), 2),
+        "config": {"workload": sweep["workload"], "headline_slots": head["slots"]},
+        **{k: v for k, v in sweep.items() if k != "workload"},
         "clocks": clocks.summary(),
     }
     loaded.close()
+    pool.close()
     print(json.dumps(result), flush=True)
 
 

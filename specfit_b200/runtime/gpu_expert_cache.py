@@ -737,6 +737,19 @@ class GpuExpertCache:
             self._events.clear()
             self._table = None
 
+    def invalidate_contents(self) -> None:
+        """Forgets every slot's expert (each slot's generation advances, its
+        last use and guards are cleared) while keeping the counters and the
+        slot memory: the next access of any expert is a miss.  This is the
+        reference's "0 slots" intervention (``discard_completed_experts``,
+        main_comparison_runtime.py:7-32) as one call; it needs the same
+        quiescent boundary as a checkpoint."""
+        with self._lock:
+            self._require_checkpoint_boundary()
+            N.check(N.lib.sf_cache_reset(self._h, N.SF_CACHE_RESET_DISCARD), "sf_cache_reset")
+            self._events.clear()
+            self._table = None
+
     def _require_checkpoint_boundary(self) -> None:
         self._check_host_managed()
         if self._observer is not None:

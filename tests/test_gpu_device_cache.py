@@ -159,3 +159,62 @@ def test_device_managed_verify_pass_graph_replays_eager():
     finally:
         for m in models:
             m.close()
+
+
+@pytest.mark.parametrize("slots", [3, 6, 16])
+def test_sweep_fills_follow_the_lru_replay(slots):
+    """Configuration 3's shape on a small target: per-layer Zipf(1.1) routes
+    replace the router for a 33-row verify pass; from empty caches, the fills
+    of each of four passes equal the reference's logical LRU replay
+    (src/specfit/replay.py:156-285, oracle/cache_oracle.py) — with
+    host-managed caches and with device-managed ones, where a layer needs
+    more experts than it has slots (waves) or fewer."""
+    from test_gpu_model import make_tree
+
+    from oracle.cache_oracle import replay_passes
+    from specfit_b200 import synthetic
+    from specfit_b200.runtime.kv_cache import ReservedCache
+    from specfit_b200.runtime.lean_forward import LeanQwen3Forward
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
+
+    cfg = qwen3_moe_config(3, hidden=256, experts=16, top_k=4, moe_inter=128, heads=8, kv_heads=2,
+                           head_dim=128, vocab=512)
+    m = build_random_offloaded_qwen3(device=DEV, slots_per_layer=slots, config=cfg, seed=9, std=0.05)
+    try:
+        tree = make_tree(nodes=32, depth=6, seed=3)
+        T = 33
+        routes = [torch.from_numpy(synthetic.zipf_routes(T, l, seed=4, experts=16, top_k=4)).to(DEV)
+                  for l in range(3)]
+        for l, layer in enumerate(m.model.model.layers):
+            layer.mlp.gate.register_forward_hook(
+                lambda mod, a, out, l=l: (out[0], out[1], routes[l]) if out[2].shape[0] == T else None)
+        expected = replay_passes(slots, [r.cpu().numpy().reshape(-1) for r in routes], passes=4)
+        lean = LeanQwen3Forward(m.model)
+        cache = ReservedCache(config=m.model.config, capacity=20 + T)
+        ctx = torch.randint(0, 512, (1, 20), generator=torch.Generator().manual_seed(6)).to(DEV)
+        with torch.no_grad():
+            lean(input_ids=ctx, past_key_values=cache, use_cache=True)
+        ids = tree.verification_token_ids(torch.tensor([[9]], device=DEV))
+        mask = tree.verification_attention_mask(base_kv_length=20, device=DEV)
+        pos = tree.verification_position_ids(base_kv_length=20, device=DEV)
+        outs = {}
+        for mode in ("host", "device"):
+            m.cold_reset_caches()
+            if mode == "device":
+                m.enter_device_managed_caches()
+            fills, logits = [], []
+            for _ in range(4):
+                before = m.cache_stats()["h2d_submissions"]
+                with torch.no_grad():
+                    logits.append(lean(input_ids=ids, attention_mask=mask, position_ids=pos,
+                                       past_key_values=cache, use_cache=True).logits.clone())
+                cache.crop(20)
+                torch.cuda.synchronize()
+                fills.append(m.cache_stats()["h2d_submissions"] - before)
+            assert fills == expected, (mode, fills, expected)
+            outs[mode] = logits
+            m.leave_device_managed_caches()
+        for a, b in zip(outs["host"], outs["device"]):
+            assert torch.equal(a, b)
+    finally:
+        m.close()

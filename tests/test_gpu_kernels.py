@@ -1,8 +1,6 @@
 """Kernel parity on the GPU: each native kernel against the CPU oracle and the
 reference-generated golden fixtures.  Integer outputs must match bit for bit;
 floating-point outputs within the stated tolerances."""
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -17,11 +15,7 @@ DEV = "cuda:0"
 # bf16 tolerance of the verification path (max abs error, cosine).
 ATOL_BF16 = 2e-2
 COS_MIN = 0.999
-# Kernel cases that stay opt-in until they have passed on a B200: they run
-# with SF_TEST_NEW_KERNELS=1.
-NEW_KERNEL = pytest.mark.skipif(os.environ.get("SF_TEST_NEW_KERNELS") != "1",
-                                reason="not yet run on a B200 (set SF_TEST_NEW_KERNELS=1)")
-ATTN_TCGEN05 = pytest.param(3, marks=NEW_KERNEL, id="tcgen05")
+ATTN_TCGEN05 = pytest.param(3, id="tcgen05")
 
 
 @pytest.fixture(scope="module")
@@ -458,7 +452,6 @@ def test_tree_attention_full_mask_and_long_context(ops):
     assert np.abs(got - ref).max() <= ATOL_BF16 and cosine(got, ref) >= COS_MIN
 
 
-@NEW_KERNEL
 def test_tcgen05_tree_attention_full_mask_long_context(ops):
     """The tcgen05 kernel on an arbitrary packed mask over 4,161 keys (many
     splits, merged) and with one split (direct write), against the
