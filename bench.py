@@ -399,7 +399,7 @@ class VerifyRunner:
         return self.h_ids.numel() * 8
 
 
-def timed_steps(fn, steps, warmup, world, device, on_start=None):
+def timed_steps(fn, steps, warmup, world, device, on_start=None, label: str = "timed"):
     """W untimed then K timed calls of ``fn`` between barriers and device
     synchronisations, CUDA events on the current stream; ``on_start`` (if
     given) runs after the warm-up, outside the timed region.  Returns the
@@ -413,7 +413,7 @@ def timed_steps(fn, steps, warmup, world, device, on_start=None):
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
-    torch.cuda.nvtx.range_push("timed")
+    torch.cuda.nvtx.range_push(label)
     start.record()
     for _ in range(steps):
         results.append(fn())
@@ -804,13 +804,16 @@ def b200_arm(args):
 
     def timed_with_stats(fn, pol, clocks_out=None):
         """K timed steps of ``fn`` under policy ``pol``: (ms, results, cache
-        counters per timed step, launches of ours in the timed region)."""
+        counters per timed step, launches of ours in the timed region).  With
+        ``clocks_out`` (the headline) the clocks are sampled and the timed
+        region is the NVTX range "headline"."""
         loaded.set_expert_execution_policy(pol)
         before: dict = {}
         start = lambda: before.update(loaded.cache_stats(), launches=ops.LAUNCHES[0])
         if clocks_out is not None:
             with ClockSampler(device.index) as clk:
-                t_ms, res = timed_steps(fn, args.steps, args.warmup, world, device, on_start=start)
+                t_ms, res = timed_steps(fn, args.steps, args.warmup, world, device, on_start=start,
+                                        label="headline")
             clocks_out.update(clk.summary())
         else:
             t_ms, res = timed_steps(fn, args.steps, args.warmup, world, device, on_start=start)
@@ -1846,6 +1849,32 @@ def kernel_cases(device, only=()):
                           lambda q=q, kv=kv, bits=bits, ctx=ctx, impl=impl:
                           ops.tree_attention(q, kv[0], kv[1], bits, ctx, impl=impl),
                           (ctx + t) * HKV * D * 2 * 2 + 2 * t * HQ * D * 2))
+    if want("dir_plan") or want("dir_fill"):
+        # The device-managed cache's plan and fill kernels at configuration 2's
+        # shape: 24 slots per layer, 40 routed experts, misses from a
+        # page-locked pool of 8 experts.
+        from specfit_b200.runtime import ExpertKey, GpuExpertCache
+        from specfit_b200.runtime.qwen3_verifier import ExpertHostPool
+
+        hp = ExpertHostPool(1, 8, 3 * H * I)
+        hp.data.zero_()
+        srcs = {ExpertKey(0, e): hp.data[0, e % 8] for e in range(E)}
+        cache = GpuExpertCache(srcs, slot_count=24, device=device, adopt_pinned_sources=True)
+        directory = cache.enter_device_mode()
+        idx = torch.from_numpy(np.stack([np.random.default_rng(r).permutation(40)[:K] for r in range(65)])).to(device)
+        d = ops.moe_dispatch(idx, E)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        directory.plan(d, False, stream)
+        store = cache.storage.view(24, -1)
+        if want("dir_plan"):
+            cases.append(("dir_plan", "E=128 S=24, 40 experts",
+                          lambda: directory.plan(d, False, stream), 24 * 16 + 128 * 4 + 6 * (128 * 8 + 24 * 8)))
+        if want("dir_fill"):
+            torch.cuda.synchronize(device)
+            n = int(directory.fill_count[0].item())
+            cases.append(("dir_fill", f"{n} experts of 9.44 MB from page-locked host memory (bytes over PCIe)",
+                          lambda: directory.fill(0, store, stream), n * EXPERT_BYTES))
+        kernel_cases.keep = (hp, cache)  # alive while the cases run
     if want("logsoftmax_topk"):
         for rows in (1, 8):
             logits = randn(rows, V)

@@ -130,6 +130,9 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
   const int lane = threadIdx.x & 31;
   const TileSpace<kPhase> space(H, I);
   const int n_active = *num_active;
+  // A CTA with no tile (an empty wave of a device-managed cache, or a grid
+  // larger than the work) leaves before touching barriers or TMEM.
+  if (n_active <= 0 || (int)blockIdx.x >= n_active * space.m_tiles) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {

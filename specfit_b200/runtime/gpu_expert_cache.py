@@ -36,6 +36,7 @@ Additions over the reference:
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass
 from threading import RLock
 from time import perf_counter_ns
@@ -96,7 +97,7 @@ class _SlotView:
     __slots__ = ("_cache", "slot_id")
 
     def __init__(self, cache: "GpuExpertCache", slot_id: int) -> None:
-        self._cache = cache
+        self._cache = weakref.proxy(cache)  # no reference cycle: a closed cache frees its slots at once
         self.slot_id = slot_id
 
     def _row(self):
@@ -178,7 +179,7 @@ class _LocationView:
     __slots__ = ("_cache", "_code")
 
     def __init__(self, cache: "GpuExpertCache", code: int) -> None:
-        self._cache = cache
+        self._cache = weakref.proxy(cache)
         self._code = code
 
     def _items(self):
@@ -236,7 +237,7 @@ class _FillQueueView:
     __slots__ = ("_cache",)
 
     def __init__(self, cache: "GpuExpertCache") -> None:
-        self._cache = cache
+        self._cache = weakref.proxy(cache)
 
     def _rows(self):
         return self._cache._native_fills()
@@ -807,6 +808,10 @@ class GpuExpertCache:
             self._h = None
             self._events.clear()
             self._spare_events.clear()
+            # Release the device memory now (slots, directory, tables).
+            self._storage = self._storage.new_empty((0,) + tuple(self._storage.shape[1:]))
+            self._directory = None
+            self._device_hits = None
             self._sources.clear()
             owner, self._source_owner = self._source_owner, None
             if owner is not None:
