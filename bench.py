@@ -1043,6 +1043,24 @@ def b200_arm(args):
         result["cpu_baseline"] = {"value": round(1.0 / per_pass, 5), "unit": "tokens/s", "cores": cores,
                                   "kind": "reference", "sample": desc,
                                   "seconds_per_verify_pass": round(per_pass, 3)}
+    if world == 1 and not args.no_extras:
+        # Configuration 5's workload on this one GPU (all 128 experts local):
+        # the N = 1 point of the expert-parallel scaling series, whose N > 1
+        # lines (torchrun) run the same workload sharded over the ranks.
+        torch.cuda.synchronize()
+        loaded.close()
+        pool.close()
+        import gc
+
+        gc.collect()
+        torch.cuda.empty_cache()
+        try:
+            ep = ep_measure(args, 0, 1, device)
+            result["config5_anchor"] = {k: ep[k] for k in ("metric", "value", "unit", "ms_per_step", "e2e",
+                                                           "config", "exchange_variants_ms_per_step",
+                                                           "phases_us_per_layer_max_over_ranks", "roofline")}
+        except Exception as err:
+            result["config5_anchor"] = {"error": f"{type(err).__name__}: {err}"}
     if world > 1:
         import torch.distributed as dist
 
@@ -1183,11 +1201,8 @@ def ep_swiglu_roofline(runner, moe, rank, world, device, peaks, iters=20):
 
 
 def ep_arm(args):
-    """expert-parallel verify over the ranks.
-
-    The prefill and a reference timing use the NCCL exchange; the headline
-    runs the verify pass with the peer-memory exchange, captured as one CUDA
-    graph per rank (no host synchronisation inside a pass)."""
+    """expert-parallel verify over the ranks
+    (``ep_measure``), one process per GPU."""
     rank, world, local = dist_info()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -1198,6 +1213,23 @@ def ep_arm(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    result = ep_measure(args, rank, world, device)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def ep_measure(args, rank: int, world: int, device) -> dict:
+    """Configuration 5 on this rank: the prefill and a reference timing use
+    the NCCL exchange; the headline runs the verify pass with the
+    peer-memory exchange, captured as one CUDA graph per rank (no host
+    synchronisation inside a pass).  One eager peer pass is also timed phase
+    by phase (CUDA events around send / receive / grouped SwiGLU / return /
+    combine of every layer; medians over layers, max over ranks)."""
     from specfit_b200 import ops
     from specfit_b200.runtime.ep_verifier import build_random_ep_qwen3
     from specfit_b200.runtime.qwen3_verifier import qwen3_moe_config
@@ -1220,6 +1252,11 @@ def ep_arm(args):
     peer = loaded.attach_peer_exchange(max_tokens=runner.batch * q)
     loaded.use_peer(True)
     peer_eager_ms, _ = timed_steps(runner.step_device, args.steps, 2, world, device)
+    peer.phase_events = []
+    runner.step_device()
+    phases = peer.phase_times_us()
+    peer.phase_events = None
+    phases = {k: round(max_over_ranks(v, world, device), 2) for k, v in phases.items()}
     times, _ = moe_block_profile(runner)
     vg = VerifyGraph(loaded.model, runner.cache, q_len=q, device=device, batch=runner.batch,
                      forward=runner.fwd)
@@ -1297,19 +1334,14 @@ def ep_arm(args):
             "note": "CUDA events around each layer.mlp in an eager peer-memory pass (router, send "
                     "plan + push, receive wait + grouping + gather, grouped SwiGLU, return, combine)",
         },
+        "phases_us_per_layer_max_over_ranks": phases,
         "roofline": ep_swiglu_roofline(runner, moes[0], rank, world, device, peaks),
         "setup_s": round(setup_s, 1),
     }
     del vg
     torch.cuda.synchronize(device)
     loaded.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        barrier(world)
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result), flush=True)
+    return result
 
 
 def cpu_decode_sample(cfg, verify_tokens: int, ctx: int, rows_per_level: int, levels: int):
@@ -1712,27 +1744,35 @@ def sweep_measure(loaded, pool, cfg, args, device) -> dict:
         resident_ms = statistics.median(timed(runner.step_device)[0] for _ in range(3))
         active = [len(set(r.reshape(-1).tolist())) for r in routes]
         tiles = statistics.mean(a * (cfg.moe_intermediate_size // 64) for a in active)
+        from specfit_b200.runtime import ExpertExecutionPolicy
+
         rows = []
         for slots in [int(x) for x in args.sweep_slots.split(",")]:
             set_slots(slots)
+            loaded.set_expert_execution_policy(ExpertExecutionPolicy.EXPERT_ID_ASCENDING)
             cold_ms, cold_fills = timed(runner.step_device)
+            row = {"slots": slots, "cold_ms": round(cold_ms, 2), "cold_fills": cold_fills}
             loaded.enter_device_managed_caches()
-            vg = VerifyGraph(loaded.model, runner.cache, q_len=T, device=device, forward=runner.fwd)
-            vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
-            warm = [timed(vg.replay) for _ in range(max(args.steps, 3))]
-            del vg
-            torch.cuda.synchronize()
+            for pol in (ExpertExecutionPolicy.EXPERT_ID_ASCENDING, ExpertExecutionPolicy.RESIDENT_FIRST):
+                loaded.set_expert_execution_policy(pol)  # captured into the plan kernels: one graph each
+                vg = VerifyGraph(loaded.model, runner.cache, q_len=T, device=device, forward=runner.fwd)
+                vg.capture(runner.d_ids, runner.d_mask, runner.d_pos, warmup=2)
+                warm = [timed(vg.replay) for _ in range(max(args.steps, 3))]
+                del vg
+                torch.cuda.synchronize()
+                warm_ms = statistics.median(w[0] for w in warm)
+                warm_fills = warm[-1][1]
+                fill_bytes = warm_fills * EXPERT_BYTES
+                exposed = max(warm_ms - resident_ms, 0.0)
+                busy = fill_bytes / (peak["GBps"] * 1e9) * 1e3
+                key = "warm" if pol is ExpertExecutionPolicy.EXPERT_ID_ASCENDING else "warm_resident_first"
+                row[key] = {"ms": round(warm_ms, 2), "fills": warm_fills,
+                            "h2d_GBps": round(fill_bytes / (warm_ms * 1e-3) / 1e9, 1),
+                            "exposed_fill_ms": round(exposed, 2),
+                            "overlap": round(1.0 - exposed / busy, 3) if busy > 0 else 1.0}
             loaded.leave_device_managed_caches()
-            warm_ms = statistics.median(w[0] for w in warm)
-            warm_fills = warm[-1][1]
-            fill_bytes = warm_fills * EXPERT_BYTES
-            exposed = max(warm_ms - resident_ms, 0.0)
-            busy = fill_bytes / (peak["GBps"] * 1e9) * 1e3
-            rows.append({"slots": slots, "cold_ms": round(cold_ms, 2), "cold_fills": cold_fills,
-                         "warm_ms": round(warm_ms, 2), "warm_fills": warm_fills,
-                         "warm_h2d_GBps": round(fill_bytes / (warm_ms * 1e-3) / 1e9, 1),
-                         "exposed_fill_ms": round(exposed, 2),
-                         "overlap": round(1.0 - exposed / busy, 3) if busy > 0 else 1.0})
+            loaded.set_expert_execution_policy(ExpertExecutionPolicy.EXPERT_ID_ASCENDING)
+            rows.append(row)
     finally:
         for h in hooks:
             h.remove()
@@ -1762,8 +1802,8 @@ def sweep_mode(args):
     head = next((r for r in sweep["rows"] if r["slots"] == args.slots), sweep["rows"][0])
     result = {
         "metric": "verify passes/s (config 3 sweep, warm cache)",
-        "value": round(1e3 / head["warm_ms"], 3), "unit": "passes/s", "n_gpus": 1,
-        "steps": max(args.steps, 3), "warmup": 2, "ms_per_step": head["warm_ms"],
+        "value": round(1e3 / head["warm"]["ms"], 3), "unit": "passes/s", "n_gpus": 1,
+        "steps": max(args.steps, 3), "warmup": 2, "ms_per_step": head["warm"]["ms"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init bf16 weights; per-layer Zipf(1.1) top-8 routes replace the router)",
         "config": {"workload": sweep["workload"], "headline_slots": head["slots"]},

@@ -400,7 +400,7 @@ SF_API int sf_host_device_address(const void* host, uint64_t* device_address);
  * eagle3_types.py:450-473).
  */
 /* Implementation choice of sf_tree_attention_ex. */
-#define SF_ATTN_AUTO 0 /* tensor-core kernel when supported (D=128, q rows 4-byte and K/V rows 16-byte aligned), else CUDA cores */
+#define SF_ATTN_AUTO 0 /* tcgen05 kernel for >= 256 packed rows (query rows x heads per KV head) over >= 2,048 keys, else the mma.sync kernel when supported (D=128, q rows 4-byte and K/V rows 16-byte aligned), else CUDA cores */
 #define SF_ATTN_SIMT 1 /* CUDA-core split kernel (any D that is a multiple of 4, <= 128) */
 #define SF_ATTN_MMA 2  /* warp-level tensor-core (mma.sync) split kernel; SF_ERR_INVALID_ARGUMENT if unsupported */
 #define SF_ATTN_TCGEN05 3 /* tcgen05/TMEM kernel, K/V by TMA (D=128, 16-byte aligned q/k/v rows); SF_ERR_INVALID_ARGUMENT if unsupported */

@@ -58,22 +58,37 @@ struct PlanArgs {
 __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   pdl_wait();
   pdl_trigger();
+  // Everything the sequential walk touches lives in shared memory: the walk
+  // (one thread) then never waits on a global load.
   extern __shared__ __align__(16) uint8_t smem[];
   const int E = a.E, S = a.S;
   int64_t* stamp = reinterpret_cast<int64_t*>(smem);
   int32_t* sexp = reinterpret_cast<int32_t*>(stamp + S);
-  int32_t* perm = sexp + S;
+  int32_t* sgen = sexp + S;
+  int32_t* perm = sgen + S;
   int32_t* eslot = perm + S;
   int32_t* order = eslot + E;
-  uint8_t* leased = reinterpret_cast<uint8_t*>(order + E);
-  __shared__ int n_sh, pos_sh, w_sh;
+  int32_t* act_in = order + E;
+  uint8_t* leased = reinterpret_cast<uint8_t*>(act_in + E);
+  __shared__ int n_sh, pos_sh, w_sh, bad_sh;
   const int tid = threadIdx.x, nt = blockDim.x;
 
+  if (tid == 0) {
+    const int n = *a.num_active;
+    n_sh = n < 0 ? 0 : (n > E ? E : n);
+    pos_sh = 0;
+    w_sh = 0;
+    bad_sh = 0;
+  }
   for (int i = tid; i < S; i += nt) {
     stamp[i] = a.slot_stamp[i];
     sexp[i] = a.slot_expert[i];
+    sgen[i] = a.slot_gen[i];
   }
-  for (int i = tid; i < E; i += nt) eslot[i] = a.expert_slot[i];
+  for (int i = tid; i < E; i += nt) {
+    eslot[i] = a.expert_slot[i];
+    act_in[i] = a.active[i];
+  }
   for (int i = tid; i < a.W * E; i += nt) a.wave_table[i] = -1;
   for (int i = tid; i < a.W; i += nt) {
     a.wave_count[i] = 0;
@@ -81,25 +96,22 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   }
   __syncthreads();
   if (tid == 0) {
-    int n = *a.num_active;
-    n = n < 0 ? 0 : (n > E ? E : n);
+    const int n = n_sh;
     int k = 0;
     for (int i = 0; i < n; ++i) {  // ids outside [0, E) are dropped and flagged
-      const int e = a.active[i];
+      const int e = act_in[i];
       if (e < 0 || e >= E) {
-        *a.status = 2;
+        bad_sh = 1;
         continue;
       }
       if (!a.resident_first || eslot[e] >= 0) order[k++] = e;
     }
     if (a.resident_first)
       for (int i = 0; i < n; ++i) {
-        const int e = a.active[i];
+        const int e = act_in[i];
         if (e >= 0 && e < E && eslot[e] < 0) order[k++] = e;
       }
     n_sh = k;
-    pos_sh = 0;
-    w_sh = 0;
   }
   int64_t clock = 0, h2d = 0, hits = 0, evictions = 0;
   if (tid == 0) clock = *a.clock;
@@ -126,6 +138,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
       int32_t* fe = a.fill_expert + (size_t)w * S;
       int32_t* fs = a.fill_slot + (size_t)w * S;
       int q = 0, cnt = 0, nf = 0, pos = pos_sh;
+      const int start = pos;
       for (; pos < n_sh; ++pos) {
         const int e = order[pos];
         int s = eslot[e];
@@ -140,7 +153,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
             eslot[old] = -1;
             ++evictions;
           }
-          a.slot_gen[s] += 1;
+          sgen[s] += 1;
           sexp[s] = e;
           eslot[e] = s;
           ++h2d;
@@ -153,7 +166,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
         table[e] = s;
         act[cnt++] = e;
       }
-      for (int j = 0; j < cnt; ++j) stamp[eslot[act[j]]] = ++clock;  // release, in wave order
+      for (int j = start; j < start + cnt; ++j) stamp[eslot[order[j]]] = ++clock;  // release, in wave order
       a.wave_count[w] = cnt;
       a.fill_count[w] = nf;
       pos_sh = pos;
@@ -164,6 +177,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   for (int i = tid; i < S; i += nt) {
     a.slot_stamp[i] = stamp[i];
     a.slot_expert[i] = sexp[i];
+    a.slot_gen[i] = sgen[i];
   }
   for (int i = tid; i < E; i += nt) a.expert_slot[i] = eslot[i];
   if (tid == 0) {
@@ -171,7 +185,8 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
     a.counters[0] += h2d;
     a.counters[1] += hits;
     a.counters[3] += evictions;
-    if (pos_sh < n_sh) *a.status = 1;
+    if (bad_sh) *a.status = 2;
+    else if (pos_sh < n_sh) *a.status = 1;
   }
 }
 
@@ -243,7 +258,7 @@ extern "C" int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, 
   a.S = num_slots;
   a.W = waves;
   a.resident_first = resident_first;
-  const size_t smem = (size_t)num_slots * (8 + 4 + 4 + 1) + (size_t)num_experts * 8;
+  const size_t smem = (size_t)num_slots * (8 + 4 + 4 + 4 + 1) + (size_t)num_experts * 12;
   SF_CHECK_ARG(smem <= 160 * 1024, "directory too large for one CTA");
   if (smem > 48 * 1024)
     SF_CHECK_CUDA(cudaFuncSetAttribute(dir_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -326,6 +326,13 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
   SF_CHECK_ARG(impl == SF_ATTN_AUTO || impl == SF_ATTN_SIMT || impl == SF_ATTN_MMA ||
                    impl == SF_ATTN_TCGEN05,
                "unknown attention implementation %d", impl);
+  // AUTO takes the tcgen05 kernel where it measured faster than the
+  // warp-level one on the B200: many packed rows over a long context
+  // (65 rows x 8 heads over 4,161 keys: 43.8 vs 64.5 us); short contexts
+  // and few rows stay on mma.sync (65 x 8 over 577 keys: 18.7 vs 23.6 us).
+  if (impl == SF_ATTN_AUTO && (int64_t)p.group * p.q_len >= 256 && p.kv_len >= 2048 &&
+      tree_attention_tc_supports(p, head_dim))
+    impl = SF_ATTN_TCGEN05;
   if (impl == SF_ATTN_TCGEN05) {
     SF_CHECK_ARG(tree_attention_tc_supports(p, head_dim),
                  "the tcgen05 tree attention needs D=128 and 16-byte aligned q/k/v rows");

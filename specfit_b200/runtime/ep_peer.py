@@ -39,6 +39,9 @@ class PeerExchange:
         d.out_row_bytes = hidden_size * torch.empty((), dtype=dtype).element_size()
         self.bytes = int(N.lib.sf_ep_peer_layout(ctypes.byref(d)))
         self.desc = d
+        # When a list, every layer appends its phase events (send, receive,
+        # grouped SwiGLU, return, finish boundaries) for a timing pass.
+        self.phase_events = None
         self._opened: list = []
         self._base = None
         with torch.cuda.device(self.device):
@@ -86,6 +89,20 @@ class PeerExchange:
             raise RuntimeError(f"expert-parallel peer exchange: {where} wait gave up; "
                                f"ranks {ranks} did not arrive")
 
+    PHASES = ("send_pack_push", "receive_wait_group_gather", "grouped_swiglu", "return_push",
+              "return_wait_combine")
+
+    def phase_times_us(self) -> dict:
+        """Median microseconds of each phase over the layers recorded in
+        ``phase_events`` (synchronises the device)."""
+        import statistics
+
+        torch.cuda.synchronize(self.device)
+        rows = [[a.elapsed_time(b) * 1e3 for a, b in zip(m, m[1:])] for m in self.phase_events or []]
+        if not rows:
+            return {}
+        return {name: round(statistics.median(r[i] for r in rows), 2) for i, name in enumerate(self.PHASES)}
+
     def close(self) -> None:
         if self._base is None:
             return
@@ -113,6 +130,15 @@ class PeerExchange:
         if T > d.cap_pairs:
             raise ValueError(f"{T} tokens exceed the peer exchange capacity {d.cap_pairs}")
         stream = torch.cuda.current_stream(dev).cuda_stream
+        marks = [] if self.phase_events is not None else None
+
+        def mark():
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append(ev)
+
+        mark()
         h = hidden.contiguous()
         idx = top_k_index.contiguous()
         w = top_k_weights.contiguous()
@@ -130,6 +156,7 @@ class PeerExchange:
                                       send_counts.data_ptr(), route_row.data_ptr(),
                                       pair_token.data_ptr(), send_err.data_ptr(), stream),
                 "sf_ep_peer_send")
+        mark()
         n = self.world * d.cap_pairs * K
         rows = self.world * d.cap_routes
         buf = torch.empty(El + (El + 1) + 3 * n + El + 2, dtype=torch.int32, device=dev)
@@ -148,14 +175,20 @@ class PeerExchange:
                                       sorted_pos.data_ptr(), inv_pos.data_ptr(), active.data_ptr(),
                                       num_active.data_ptr(), return_src.data_ptr(), err.data_ptr(),
                                       xs.data_ptr(), ws.data_ptr(), stream), "sf_ep_peer_recv")
+        mark()
         disp = ops.Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, err,
                             self.world * d.cap_pairs, K, El)
         ys = ops.grouped_swiglu(xs, ws, disp, moe.slot, moe.storage, moe.hidden, moe.inter)
+        mark()
         N.check(N.lib.sf_ep_peer_return(ctypes.byref(d), ys.data_ptr(), return_src.data_ptr(),
                                         offsets.data_ptr(), stream), "sf_ep_peer_return")
+        mark()
         out = torch.empty(T, d.hidden_size, dtype=self.dtype, device=dev)
         N.check(N.lib.sf_ep_peer_finish(ctypes.byref(d), idx.data_ptr(), route_row.data_ptr(), T, E,
                                         N.SF_REDUCE_MODEL_DTYPE, out.data_ptr(), stream),
                 "sf_ep_peer_finish")
+        mark()
+        if marks is not None:
+            self.phase_events.append(marks)
         ops._launched(8 if T else 7)  # the grouped SwiGLU counts its own two
         return out

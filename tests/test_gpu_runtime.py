@@ -311,3 +311,54 @@ def test_cache_state_follows_the_lru_replay_oracle(rt, slots, experts, seed):
             (ref.h2d_submissions, ref.resident_hits, ref.evictions), i
         assert set(cache.resident_expert_ids()) == set(ref.resident()), i
     cache.close()
+
+
+def test_reference_cache_off_edits_invalidate_the_cache(rt):
+    """The reference's "0 slots" intervention edits private members in place
+    (src/specfit/main_comparison_runtime.py:7-32: clear the resident and
+    in-flight maps and the transfer queue, empty every slot, advance its
+    generation, reset its last use, drop its ready event and use guards,
+    bump the state version).  Those edits work on this cache's views, keep
+    the counters, and make the next access a fill into an empty slot;
+    ``invalidate_contents`` does the same in one call."""
+    cache = rt.GpuExpertCache(make_sources(4), slot_count=2, device=DEV)
+    try:
+        for e in (0, 1):
+            with cache.acquire(e) as lease:
+                lease.wait()
+        torch.cuda.synchronize()
+        before = cache.stats()
+        gens = [s.generation for s in cache._slots]
+        version = cache._state_version
+        with cache._lock:
+            cache._require_checkpoint_boundary()
+            cache._resident.clear()
+            cache._inflight.clear()
+            cache._outstanding_transfers.clear()
+            for slot in cache._slots:
+                slot.expert_id = None
+                slot.generation += 1
+                slot.last_used_sequence = 0
+                slot.ready_event = None
+                if slot.use_events is not None:
+                    slot.use_events.clear()
+            cache._state_version += 1
+        assert cache._state_version > version
+        assert cache.resident_expert_ids() == ()
+        assert [s.generation for s in cache._slots] == [g + 1 for g in gens]
+        assert all(s.expert_id is None and s.last_used_sequence == 0 for s in cache._slots)
+        after = cache.stats()
+        assert (after.h2d_submissions, after.resident_hits, after.evictions) == \
+            (before.h2d_submissions, before.resident_hits, before.evictions)
+        with cache.acquire(0) as lease:
+            lease.wait()
+        st = cache.stats()
+        assert st.h2d_submissions == before.h2d_submissions + 1 and st.evictions == before.evictions
+        torch.cuda.synchronize()
+        cache.invalidate_contents()
+        assert cache.resident_expert_ids() == ()
+        with cache.acquire(3) as lease:
+            lease.wait()
+        assert cache.stats().evictions == before.evictions
+    finally:
+        cache.close()
