@@ -12,26 +12,29 @@ acceptance + KV-cache rollback to the context.
 Reported (one JSON line, rank 0):
   value      committed tokens/s with the step inputs already on the device
              (committed = accepted path + 1; random weights accept nothing,
-             so one token per verify pass), summed over ranks;
-  e2e        the same through host buffers: token ids, mask and positions
-             copied from pinned host memory each step, the argmax read back
-             and the accepted path computed on the host;
-  resident   the same pass with 128 slots per layer (every expert resident,
-             BASELINE configuration 3's 128-slot warm point);
-  moe_block  the MoE verify block (router, dispatch, gather, grouped
-             SwiGLU, combine) of layer 0 at 65 rows over its resident
-             slots, one CUDA graph per block with L2 flushed between
-             replays: us per block and algorithmic HBM GB/s against the
-             measured copy peak; ``eager_in_model`` keeps the per-layer time
-             inside an eager, host-launched verify pass;
-  roofline   the grouped SwiGLU kernel (the dominant kernel of the block)
-             against the measured HBM copy peak;
-  cpu_baseline  the reference's CPU path (Hugging Face Qwen3-MoE decoder
-             layer + lm_head on the host cores), bounded sample.
+             so one token per verify pass), summed over ranks: device-managed
+             expert caches (misses planned and filled on the GPU), the verify
+             pass replayed from one CUDA graph, expert-id-ascending execution;
+  e2e        the same with the step's inputs copied from pinned host memory
+             into the graph's buffers and the argmax read back;
+  other_policy / host_managed  the resident-first policy, and the
+             reference's host-managed protocol (eager, copy-engine fills);
+  resident   the same pass with 128 slots per layer (every expert resident);
+  moe_block  the MoE verify block of layer 0 alone, one CUDA graph per block,
+             L2 flushed between replays;
+  roofline   the grouped SwiGLU kernel against the measured HBM copy peak,
+             and (``h2d``) the headline's fill bytes per step against the
+             pinned-copy peak measured in the same run;
+  config1 / config3 / config4 / config5_anchor  the other BASELINE
+             configurations (fp32 0-slot block; slot sweep; end-to-end
+             speculative decoding; configuration 5's workload on one GPU);
+  cpu_baseline  a bounded sample of the reference's CPU path (stock Hugging
+             Face Qwen3-MoE on the host cores; ``--impl reference`` times the
+             whole 48-layer model).
 
-Multi-GPU (torchrun): independent replicas, one per GPU ("scaling": weak);
-the replicas share one page-locked host copy of the experts through a
-shared-memory file.  ``--impl reference`` times the reference CPU path only.
+Multi-GPU (torchrun, N > 1): configuration 5, expert-parallel over the ranks
+(``ep_arm``, "scaling": strong); ``--impl reference`` times the reference's
+CPU path on rank 0 only.
 """
 from __future__ import annotations
 
@@ -1042,7 +1045,10 @@ def b200_arm(args):
         per_pass, desc, cores = cpu_reference_sample(args, layers=args.cpu_layers)
         result["cpu_baseline"] = {"value": round(1.0 / per_pass, 5), "unit": "tokens/s", "cores": cores,
                                   "kind": "reference", "sample": desc,
-                                  "seconds_per_verify_pass": round(per_pass, 3)}
+                                  "seconds_per_verify_pass": round(per_pass, 3),
+                                  "note": ("a bounded sample: layer 0 routes uncollapsed random hidden states "
+                                           "to ~120 experts, so scaling it to 48 layers overstates the CPU "
+                                           "pass; bench.py --impl reference times all 48 layers")}
     if world == 1 and not args.no_extras:
         # Configuration 5's workload on this one GPU (all 128 experts local):
         # the N = 1 point of the expert-parallel scaling series, whose N > 1
@@ -1858,6 +1864,22 @@ def kernel_cases(device, only=()):
             ys = randn(t * K, H)
             cases.append(("combine", f"T={t}", lambda ys=ys, d=d, idx=idx: ops.moe_combine(ys, d, idx),
                           t * K * H * 2 + t * H * 2 + t * K * 12))
+        if want("combine_add_rmsnorm"):
+            ys, res, hn = randn(t * K, H), randn(t, H), torch.empty(t, H, **bf)
+            nw = torch.ones(H, **bf)
+            cases.append(("combine_add_rmsnorm", f"T={t}",
+                          lambda ys=ys, d=d, idx=idx, res=res, nw=nw, hn=hn:
+                          ops.moe_combine_add_rmsnorm(ys, d, idx, res, nw, 1e-6, out=hn),
+                          t * K * H * 2 + 3 * t * H * 2 + t * K * 12 + H * 2))
+        if want("add_rmsnorm"):
+            xa, res, hn = randn(t, H), randn(t, H), torch.empty(t, H, **bf)
+            nw = torch.ones(H, **bf)
+            st = torch.cuda.current_stream(device).cuda_stream
+            cases.append(("add_rmsnorm", f"T={t}",
+                          lambda xa=xa, res=res, nw=nw, hn=hn, st=st, t=t: N.check(N.lib.sf_add_rmsnorm(
+                              xa.data_ptr(), res.data_ptr(), res.data_ptr(), nw.data_ptr(), 1e-6, t, H,
+                              hn.data_ptr(), st), "sf_add_rmsnorm"),
+                          4 * t * H * 2 + H * 2))
         if want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
             for kind in ("zipf", "uniform"):
                 if kind == "uniform":
@@ -1920,6 +1942,25 @@ def kernel_cases(device, only=()):
             logits = randn(rows, V)
             cases.append(("logsoftmax_topk", f"rows={rows} vocab={V}",
                           lambda logits=logits: ops.logsoftmax_topk(logits, 8, 4.5), rows * V * 2))
+    if want("lm_head"):
+        head = randn(V, H, std=0.02)
+        for rows in (7, 65):
+            xr = randn(rows, H)
+            cases.append(("lm_head", f"rows={rows} fused argmax (ours)",
+                          lambda xr=xr: ops.linear_argmax(xr, head), V * H * 2 + rows * V * 2))
+            cases.append(("lm_head", f"rows={rows} library GEMM + torch argmax",
+                          lambda xr=xr: torch.nn.functional.linear(xr, head).argmax(-1), V * H * 2 + rows * V * 2))
+    if want("qkv"):
+        wq = randn((HQ + 2 * HKV) * D, H, std=0.02)
+        xq = randn(65, H)
+        yq = torch.empty(65, wq.shape[0], **bf)
+        st = torch.cuda.current_stream(device).cuda_stream
+        cases.append(("qkv", "rows=65 2048->5120 (ours)",
+                      lambda: N.check(N.lib.sf_linear_bf16(xq.data_ptr(), 65, H, wq.data_ptr(), wq.shape[0],
+                                                           yq.data_ptr(), st), "sf_linear_bf16"),
+                      wq.numel() * 2 + 65 * (H + wq.shape[0]) * 2))
+        cases.append(("qkv", "rows=65 2048->5120 library GEMM", lambda: torch.nn.functional.linear(xq, wq),
+                      wq.numel() * 2 + 65 * (H + wq.shape[0]) * 2))
     if want("linear"):
         for rows, n_in, n_out in ((7, HQ * D, H), (8, 3 * H, H)):
             xw = randn(rows, n_in)

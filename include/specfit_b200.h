@@ -625,13 +625,28 @@ SF_API int sf_logsoftmax_topk(const void* logits, int64_t rows, int64_t vocab, f
  * out[rows][out_features] = x[rows][in_features] . weight[out_features][in_features]^T
  * in bf16 with fp32 accumulation, rounded once (F.linear without bias), on
  * tcgen05 tensor cores with K split across a CTA cluster and the partial
- * sums added in a fixed order.  For verify-sized inputs: rows <= 32,
+ * sums added in a fixed order.  For verify-sized inputs: rows <= 128,
  * in_features % 64 == 0, x and weight contiguous and 16-byte aligned;
  * otherwise returns SF_ERR_UNSUPPORTED without a message (use a library
  * GEMM).
  */
 SF_API int sf_linear_bf16(const void* x, int64_t rows, int64_t in_features, const void* weight,
                           int64_t out_features, void* out, void* stream);
+
+/*
+ * lm_head + greedy pick in one pass over the weight: out[t, n] (nullable)
+ * = bf16(x[t] . weight[n]) as sf_linear_bf16 computes it, and argmax[t] =
+ * the n with the largest bf16 value, the lowest n among equal ones (what
+ * torch.argmax returns on those logits).  rows <= 128, in_features a multiple
+ * of 64, 16-byte aligned x and weight.  workspace: at least
+ * sf_linear_argmax_workspace_bytes(rows, in_features, out_features) bytes.
+ * Replaces the target's lm_head F.linear and the argmax of the verify step
+ * (src/specfit/runtime/eagle3_tree.py:1252).
+ */
+SF_API size_t sf_linear_argmax_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features);
+SF_API int sf_linear_bf16_argmax(const void* x, int64_t rows, int64_t in_features, const void* weight,
+                                 int64_t out_features, void* out, int64_t* argmax, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 /*
  * One level of a drafted candidate pool (the tree builder's level step,
  * src/specfit/runtime/eagle3_tree.py:611-803): among rows x k children

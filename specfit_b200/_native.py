@@ -174,6 +174,8 @@ SIGNATURES = {
     "sf_kv_compact": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _vp, _i32, _vp, _vp]),
     "sf_logsoftmax_topk": (_i32, [_vp, _i64, _i64, _f32, _i32, _vp, _vp, _vp]),
     "sf_linear_bf16": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "sf_linear_argmax_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "sf_linear_bf16_argmax": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _sz, _vp]),
     "sf_draft_level": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i64, _i32, _i32, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sf_rope_rows": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp]),

@@ -1,13 +1,14 @@
 // Skinny bf16 projection GEMM on tcgen05 for verify-sized row counts.
 //
-//   Y[T, N] = X[T, K] . W[N, K]^T      (F.linear without bias), T <= 32
+//   Y[T, N] = X[T, K] . W[N, K]^T      (F.linear without bias), T <= 128
+//   argmax_n bf16(Y[t, n])              (optional, fused: lm_head + greedy pick)
 //
 // The projections of a verify pass (q|k|v, o, the drafter's layers and
 // lm_head) see a handful of token rows against weight matrices of tens to
 // hundreds of MB, so they are weight-streaming problems: the bound is reading
 // W once from HBM.  Layout "swap AB" as in the grouped SwiGLU: 128 weight
-// rows fill the MMA's M dimension and the T token rows form N (16 or 32),
-// both operands K-major and loaded by TMA with 128-byte swizzling.
+// rows fill the MMA's M dimension and the T token rows form N (16, 32, 64
+// or 128), both operands K-major and loaded by TMA with 128-byte swizzling.
 //
 // Parallelism comes from splitting K: the CTAs of a thread-block cluster
 // (up to 8) share one 128-row tile, each accumulating its K range in TMEM.
@@ -16,6 +17,12 @@
 // shared memory), and after one cluster barrier the owner adds the S
 // partials in rank order (a fixed order: the result does not depend on
 // timing) and rounds once to bf16.
+//
+// With an argmax workspace the same owner pass also reduces its rows of
+// every token: bf16-rounded values, the largest one and, among equal ones,
+// the lowest row (what torch.argmax returns on the bf16 logits); one
+// (value, row) pair per (tile, cluster rank, token) goes to the workspace
+// and a second launch picks each token's winner over them in the same order.
 //
 // Roles per CTA (192 threads): warp 0 lane 0 issues TMA (weights for the
 // first stages before waiting on the preceding kernel, since they do not
@@ -43,7 +50,24 @@ constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMaxSplit = 8;   // portable cluster size
-constexpr uint32_t kTmemCols = 32;
+
+template <int kBN>
+constexpr uint32_t tmem_cols() {  // a power of two >= 32 holding kBN fp32 columns
+  return kBN < 32 ? 32u : (uint32_t)kBN;
+}
+
+struct ArgmaxPart {
+  float value;
+  int32_t row;
+};
+
+// The better of two candidates: larger value, then lower row.
+__device__ __forceinline__ ArgmaxPart better(ArgmaxPart a, ArgmaxPart b) {
+  if (b.row < 0) return a;
+  if (a.row < 0) return b;
+  if (b.value > a.value || (b.value == a.value && b.row < a.row)) return b;
+  return a;
+}
 
 template <int kBN>
 struct __align__(1024) DenseSmem {
@@ -67,8 +91,9 @@ constexpr size_t dense_smem_bytes() {
 template <int kBN>
 __global__ void __launch_bounds__(kThreads)
 dense_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                int T, int N, int K, __nv_bfloat16* __restrict__ y) {
+                int T, int N, int K, __nv_bfloat16* __restrict__ y, ArgmaxPart* __restrict__ argmax_part) {
   constexpr uint32_t kBBytes = kBN * kBK * 2;
+  constexpr uint32_t kTmemCols = tmem_cols<kBN>();
   extern __shared__ uint8_t smem_raw[];
   auto* sm = reinterpret_cast<DenseSmem<kBN>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -190,17 +215,67 @@ dense_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   cluster.sync();  // every split's partial rows have landed with their owner
   const int r0 = min(kBM, crank * rows_per);
   const int nr = min(kBM, r0 + rows_per) - r0;
-  for (int idx = threadIdx.x; idx < nr * T; idx += kThreads) {
-    const int t = idx / nr, r = idx % nr;
-    if (m0 + r0 + r >= N) continue;
-    float acc = 0.f;
-    for (int s = 0; s < split; ++s) acc += sm->part[s * rows_per + r][t];  // rank order
-    y[(int64_t)t * N + m0 + r0 + r] = __float2bfloat16_rn(acc);
+  if (y != nullptr) {
+    for (int idx = threadIdx.x; idx < nr * T; idx += kThreads) {
+      const int t = idx / nr, r = idx % nr;
+      if (m0 + r0 + r >= N) continue;
+      float acc = 0.f;
+      for (int s = 0; s < split; ++s) acc += sm->part[s * rows_per + r][t];  // rank order
+      y[(int64_t)t * N + m0 + r0 + r] = __float2bfloat16_rn(acc);
+    }
+  }
+  if (argmax_part != nullptr) {
+    // One warp per token: lanes stride over this CTA's rows, then a
+    // butterfly keeps the larger value / lower row.
+    for (int t = warp; t < T; t += kThreads / 32) {
+      ArgmaxPart best{0.f, -1};
+      for (int r = lane; r < nr; r += 32) {
+        const int row = m0 + r0 + r;
+        if (row >= N) break;
+        float acc = 0.f;
+        for (int s = 0; s < split; ++s) acc += sm->part[s * rows_per + r][t];  // the same sum as y
+        best = better(best, ArgmaxPart{__bfloat162float(__float2bfloat16_rn(acc)), row});
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) {
+        ArgmaxPart o{__shfl_xor_sync(0xffffffffu, best.value, off),
+                     __shfl_xor_sync(0xffffffffu, best.row, off)};
+        best = better(best, o);
+      }
+      if (lane == 0) argmax_part[((int64_t)blockIdx.y * split + crank) * T + t] = best;
+    }
   }
 }
 
+// Each token's winner over the (tile, rank) candidates, in index order.
+__global__ void __launch_bounds__(256)
+argmax_reduce_kernel(const ArgmaxPart* __restrict__ part, int nparts, int T, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  ArgmaxPart best{0.f, -1};
+  for (int p = lane; p < nparts; p += 32) best = better(best, part[(int64_t)p * T + t]);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    ArgmaxPart o{__shfl_xor_sync(0xffffffffu, best.value, off), __shfl_xor_sync(0xffffffffu, best.row, off)};
+    best = better(best, o);
+  }
+  if (lane == 0) out[t] = best.row;
+}
+
+// Split of K over a cluster: while the tiles alone are fewer than the SMs,
+// keeping the whole grid in one wave (clusters are placed one CTA per SM).
+int dense_split(int N, int K) {
+  const int m_tiles = (N + kBM - 1) / kBM;
+  int split = num_sms() / m_tiles;
+  return std::max(1, std::min(std::min(split, kMaxSplit), K / kBK));
+}
+
 template <int kBN>
-int launch_dense(const void* x, const void* w, void* y, int T, int N, int K, cudaStream_t stream) {
+int launch_dense(const void* x, const void* w, void* y, int T, int N, int K, cudaStream_t stream,
+                 ArgmaxPart* argmax_part = nullptr) {
   static std::atomic<unsigned long long> configured{0};
   if (int rc = once_per_device(configured, [] {
         SF_CHECK_CUDA(cudaFuncSetAttribute(dense_tc_kernel<kBN>,
@@ -223,15 +298,19 @@ int launch_dense(const void* x, const void* w, void* y, int T, int N, int K, cud
     if (int rc = tma_encode_bf16(&tm_x, x, 2, dims, strides, box)) return rc;
   }
   const int m_tiles = (N + kBM - 1) / kBM;
-  const int kb_total = K / kBK;
-  // Split K while the tiles alone are fewer than the SMs, keeping the whole
-  // grid in one wave (clusters are placed one CTA per SM).
-  int split = num_sms() / m_tiles;
-  split = std::max(1, std::min(std::min(split, kMaxSplit), kb_total));
+  const int split = dense_split(N, K);
   SF_CHECK_CUDA(launch_pdl_cluster(dense_tc_kernel<kBN>, dim3((unsigned)split, (unsigned)m_tiles, 1),
                                    dim3(kThreads), dense_smem_bytes<kBN>(), stream, (unsigned)split,
-                                   1u, tm_w, tm_x, T, N, K, static_cast<__nv_bfloat16*>(y)));
+                                   1u, tm_w, tm_x, T, N, K, static_cast<__nv_bfloat16*>(y), argmax_part));
   return SF_OK;
+}
+
+int launch_dense_any(const void* x, const void* w, void* y, int T, int N, int K, cudaStream_t stream,
+                     ArgmaxPart* argmax_part) {
+  if (T <= 16) return launch_dense<16>(x, w, y, T, N, K, stream, argmax_part);
+  if (T <= 32) return launch_dense<32>(x, w, y, T, N, K, stream, argmax_part);
+  if (T <= 64) return launch_dense<64>(x, w, y, T, N, K, stream, argmax_part);
+  return launch_dense<128>(x, w, y, T, N, K, stream, argmax_part);
 }
 
 }  // namespace
@@ -253,10 +332,41 @@ extern "C" int sf_linear_bf16(const void* x, int64_t rows, int64_t in_features, 
   SF_CHECK_ARG(rows >= 0 && in_features > 0 && out_features > 0, "invalid sizes");
   if (rows == 0) return SF_OK;
   SF_CHECK_ARG(x && weight && out, "null pointer argument");
-  if (rows > 32 || in_features % kBK != 0 || in_features >= (1LL << 31) ||
+  if (rows > 128 || in_features % kBK != 0 || in_features >= (1LL << 31) ||
       out_features >= (1LL << 31) || !aligned16(x) || !aligned16(weight))
     return SF_ERR_UNSUPPORTED;  // no message: callers fall back to a library GEMM
   const int T = (int)rows, N = (int)out_features, K = (int)in_features;
-  if (T <= 16) return launch_dense<16>(x, weight, out, T, N, K, as_stream(stream));
-  return launch_dense<32>(x, weight, out, T, N, K, as_stream(stream));
+  return launch_dense_any(x, weight, out, T, N, K, as_stream(stream), nullptr);
+}
+
+extern "C" size_t sf_linear_argmax_workspace_bytes(int64_t rows, int64_t in_features, int64_t out_features) {
+  using namespace sf;
+  if (rows <= 0 || out_features <= 0 || in_features <= 0) return 0;
+  const int64_t m_tiles = (out_features + kBM - 1) / kBM;
+  return (size_t)(m_tiles * kMaxSplit * rows) * sizeof(ArgmaxPart);
+}
+
+extern "C" int sf_linear_bf16_argmax(const void* x, int64_t rows, int64_t in_features, const void* weight,
+                                     int64_t out_features, void* out, int64_t* argmax, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(rows >= 0 && in_features > 0 && out_features > 0, "invalid sizes");
+  if (rows == 0) return SF_OK;
+  SF_CHECK_ARG(x && weight && argmax && workspace, "null pointer argument");
+  SF_CHECK_ARG(rows <= 128, "at most 128 rows");
+  SF_CHECK_ARG(in_features % kBK == 0 && in_features < (1LL << 31) && out_features < (1LL << 31),
+               "in_features must be a multiple of 64");
+  SF_CHECK_ARG(aligned16(x) && aligned16(weight), "x and weight must be 16-byte aligned");
+  if (workspace_bytes < sf_linear_argmax_workspace_bytes(rows, in_features, out_features))
+    return set_error(SF_ERR_WORKSPACE, "argmax workspace needs %zu bytes",
+                     sf_linear_argmax_workspace_bytes(rows, in_features, out_features));
+  const int T = (int)rows, N = (int)out_features, K = (int)in_features;
+  auto* part = static_cast<ArgmaxPart*>(workspace);
+  cudaStream_t s = as_stream(stream);
+  if (int rc = launch_dense_any(x, weight, out, T, N, K, s, part)) return rc;
+  const int nparts = ((N + kBM - 1) / kBM) * dense_split(N, K);
+  SF_CHECK_CUDA(launch_pdl(argmax_reduce_kernel, dim3((unsigned)((T + 7) / 8)), dim3(256), 0, s,
+                           static_cast<const ArgmaxPart*>(part), nparts, T, argmax));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
 }

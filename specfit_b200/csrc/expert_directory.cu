@@ -58,19 +58,23 @@ struct PlanArgs {
 __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   pdl_wait();
   pdl_trigger();
-  // Everything the sequential walk touches lives in shared memory: the walk
-  // (one thread) then never waits on a global load.
+  // Everything the sequential walk reads or writes lives in shared memory
+  // (the wave's outputs are staged there and copied out by all threads), so
+  // the one walking thread never waits on global memory.
   extern __shared__ __align__(16) uint8_t smem[];
   const int E = a.E, S = a.S;
   int64_t* stamp = reinterpret_cast<int64_t*>(smem);
   int32_t* sexp = reinterpret_cast<int32_t*>(stamp + S);
   int32_t* sgen = sexp + S;
   int32_t* perm = sgen + S;
-  int32_t* eslot = perm + S;
+  int32_t* fe_sm = perm + S;
+  int32_t* fs_sm = fe_sm + S;
+  int32_t* eslot = fs_sm + S;
   int32_t* order = eslot + E;
   int32_t* act_in = order + E;
-  uint8_t* leased = reinterpret_cast<uint8_t*>(act_in + E);
-  __shared__ int n_sh, pos_sh, w_sh, bad_sh;
+  int32_t* table_sm = act_in + E;
+  uint8_t* leased = reinterpret_cast<uint8_t*>(table_sm + E);
+  __shared__ int n_sh, pos_sh, w_sh, bad_sh, cnt_sh, nf_sh, start_sh;
   const int tid = threadIdx.x, nt = blockDim.x;
 
   if (tid == 0) {
@@ -89,7 +93,6 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
     eslot[i] = a.expert_slot[i];
     act_in[i] = a.active[i];
   }
-  for (int i = tid; i < a.W * E; i += nt) a.wave_table[i] = -1;
   for (int i = tid; i < a.W; i += nt) {
     a.wave_count[i] = 0;
     a.fill_count[i] = 0;
@@ -115,9 +118,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   }
   int64_t clock = 0, h2d = 0, hits = 0, evictions = 0;
   if (tid == 0) clock = *a.clock;
-  while (true) {
-    __syncthreads();
-    if (pos_sh >= n_sh || w_sh >= a.W) break;
+  for (int w = 0; w < a.W; ++w) {
     // Rank every slot by its LRU key; nothing is leased at a wave's start.
     for (int s = tid; s < S; s += nt) {
       const int occ = sexp[s] >= 0;
@@ -130,13 +131,9 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
       perm[r] = s;
       leased[s] = 0;
     }
+    for (int i = tid; i < E; i += nt) table_sm[i] = -1;
     __syncthreads();
     if (tid == 0) {
-      const int w = w_sh;
-      int32_t* table = a.wave_table + (size_t)w * E;
-      int32_t* act = a.wave_active + (size_t)w * E;
-      int32_t* fe = a.fill_expert + (size_t)w * S;
-      int32_t* fs = a.fill_slot + (size_t)w * S;
       int q = 0, cnt = 0, nf = 0, pos = pos_sh;
       const int start = pos;
       for (; pos < n_sh; ++pos) {
@@ -157,21 +154,37 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
           sexp[s] = e;
           eslot[e] = s;
           ++h2d;
-          fe[nf] = e;
-          fs[nf] = s;
+          fe_sm[nf] = e;
+          fs_sm[nf] = s;
           ++nf;
         }
         leased[s] = 1;
         stamp[s] = ++clock;  // acquire touches the slot
-        table[e] = s;
-        act[cnt++] = e;
+        table_sm[e] = s;
+        ++cnt;
       }
       for (int j = start; j < start + cnt; ++j) stamp[eslot[order[j]]] = ++clock;  // release, in wave order
+      start_sh = start;
+      cnt_sh = cnt;
+      nf_sh = nf;
+      pos_sh = pos;
+    }
+    __syncthreads();
+    // The wave's outputs, written by every thread.
+    const int start = start_sh, cnt = cnt_sh, nf = nf_sh;
+    int32_t* table = a.wave_table + (size_t)w * E;
+    for (int i = tid; i < E; i += nt) table[i] = table_sm[i];
+    for (int i = tid; i < cnt; i += nt) a.wave_active[(size_t)w * E + i] = order[start + i];
+    for (int i = tid; i < nf; i += nt) {
+      a.fill_expert[(size_t)w * S + i] = fe_sm[i];
+      a.fill_slot[(size_t)w * S + i] = fs_sm[i];
+    }
+    if (tid == 0) {
       a.wave_count[w] = cnt;
       a.fill_count[w] = nf;
-      pos_sh = pos;
-      w_sh = w + 1;
     }
+    // Later waves of a layer that needs fewer waves stay empty; their tables
+    // are still written (-1) so a stale wave can never be read.
   }
   __syncthreads();
   for (int i = tid; i < S; i += nt) {
@@ -258,7 +271,7 @@ extern "C" int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, 
   a.S = num_slots;
   a.W = waves;
   a.resident_first = resident_first;
-  const size_t smem = (size_t)num_slots * (8 + 4 + 4 + 4 + 1) + (size_t)num_experts * 12;
+  const size_t smem = (size_t)num_slots * (8 + 4 * 5 + 1) + (size_t)num_experts * 16;
   SF_CHECK_ARG(smem <= 160 * 1024, "directory too large for one CTA");
   if (smem > 48 * 1024)
     SF_CHECK_CUDA(cudaFuncSetAttribute(dir_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

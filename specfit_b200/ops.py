@@ -528,6 +528,31 @@ LINEAR_MAX_OUT = 4096  # measured on B200: wider weights stream as fast through 
 LINEAR_MIN_IN = 4096
 
 
+def linear_argmax(x: torch.Tensor, weight: torch.Tensor, logits: bool = True):
+    """The lm_head and the greedy pick in one pass over the weight:
+    ``(F.linear(x, weight) or None, argmax)`` for bf16 ``x [rows, K]`` (rows
+    <= 128), ``weight [V, K]``.  The argmax is over the bf16-rounded logits,
+    the lowest index among equal maxima (``torch.argmax`` on the logits this
+    call returns); int64 ``[rows]``."""
+    dev = _require_cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("linear_argmax takes bf16 inputs")
+    xx = x.reshape(-1, x.shape[-1]).contiguous()
+    w = weight.contiguous()
+    rows, k = xx.shape
+    v = w.shape[0]
+    y = torch.empty(rows, v, dtype=x.dtype, device=dev) if logits else None
+    am = torch.empty(rows, dtype=torch.int64, device=dev)
+    nbytes = N.lib.sf_linear_argmax_workspace_bytes(rows, k, v)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+    N.check(N.lib.sf_linear_bf16_argmax(xx.data_ptr(), rows, k, w.data_ptr(), v, _ptr(y), am.data_ptr(),
+                                        ws.data_ptr(), nbytes, _stream(dev)), "sf_linear_bf16_argmax")
+    _launched(2 if rows else 0)
+    if y is not None:
+        y = y.reshape(*x.shape[:-1], v)
+    return y, am.reshape(x.shape[:-1])
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``F.linear(x, weight)`` (no bias) for bf16 ``x [..., K]``: the tcgen05
     split-K kernel (``sf_linear_bf16``) when the rows are few (<= 32) and the

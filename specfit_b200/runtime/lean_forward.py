@@ -14,6 +14,9 @@ chain of small torch kernels replaced by:
 * ``sf_qk_norm_rope`` — q/k head norms, rotary embedding, and the cache
   update writing k and v rows straight into the ``ReservedCache`` buffers
   (at the host length, or at the device-side offset in static mode);
+* the lm_head of verify-sized passes with the greedy argmax fused into it
+  (``sf_linear_bf16_argmax``; the result carries ``argmax`` next to
+  ``logits``);
 * ``sf_tree_attention`` per request, the o projection, and the MoE block:
   its gate module (router hooks still fire) and, with every expert resident
   and no hooks on the block, the experts up to the combine, which is fused
@@ -42,9 +45,12 @@ from .tree_attention import _causal_bits, _packed_bits
 
 
 class LeanQwen3Forward:
-    def __init__(self, model) -> None:
+    def __init__(self, model, fused_head: bool = True) -> None:
         cfg = model.config
         self.model = model
+        # Verify-sized passes (<= 128 rows) run the lm_head on the tcgen05
+        # projection kernel with the argmax fused into it (``out.argmax``).
+        self.fused_head = fused_head
         self.H = cfg.hidden_size
         self.hq, self.hkv, self.D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         if self.D != 128:
@@ -167,6 +173,10 @@ class LeanQwen3Forward:
                 for hook in tuple(layer._forward_hooks.values()):
                     hook(layer, (), out)
         keep = T if not logits_to_keep else min(int(logits_to_keep), T)
-        rows = hn.view(B, T, self.H)[:, T - keep:, :]
-        logits = ops.linear(rows.contiguous(), self.model.lm_head.weight)
-        return SimpleNamespace(logits=logits)
+        rows = hn.view(B, T, self.H)[:, T - keep:, :].contiguous()
+        head = self.model.lm_head.weight
+        if self.fused_head and B * keep <= 128 and head.dtype == torch.bfloat16 and self.H % 64 == 0:
+            # lm_head and the greedy pick in one pass over the 151,936-row weight
+            logits, argmax = ops.linear_argmax(rows, head)
+            return SimpleNamespace(logits=logits, argmax=argmax)
+        return SimpleNamespace(logits=ops.linear(rows, head), argmax=None)

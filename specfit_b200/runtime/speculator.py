@@ -50,6 +50,15 @@ from .kv_cache import ReservedCache, compact_tree_cache_
 from .tree_attention import clear_mask_cache
 
 
+
+
+def _verify_argmax(out):
+    """The target's greedy token per verify row: the lean forward's fused
+    lm_head argmax when it produced one (equal, bit for bit, to the argmax of
+    the logits it returns), else the argmax of the logits."""
+    fused = getattr(out, "argmax", None)
+    return fused[0] if fused is not None else out.logits[0].argmax(-1)
+
 class BernoulliAcceptance:
     """p_d ~ Beta(a, b) per depth (drawn once); each verified node at depth d
     is accepted with probability p_d, independently, in node order."""
@@ -245,7 +254,7 @@ class B200TreeSpeculator:
                 vis = visibility_from_ancestors(anc, self._offset, cap)
                 out = self.fwd(input_ids=ids, attention_mask=vis.view(1, 1, q, cap),
                                position_ids=pos.view(1, q), past_key_values=cache, use_cache=True)
-            return ids, out.logits[0].argmax(-1), self._features()
+            return ids, _verify_argmax(out), self._features()
 
         try:
             side = torch.cuda.Stream(device=dev)
@@ -487,7 +496,7 @@ class B200TreeSpeculator:
                     finally:
                         self._override = None
                     q_aux = self._features()
-                    verifier = vout.logits[0].argmax(-1)
+                    verifier = _verify_argmax(vout)
                 tick()
                 td = time.perf_counter()
                 path = self.acceptance.path(tree)

@@ -59,7 +59,11 @@ class VerifyGraph:
         with torch.no_grad():
             out = self.forward(input_ids=self.ids, attention_mask=self.mask, position_ids=self.pos,
                                past_key_values=self.cache, use_cache=True)
-            am = out.logits[0].argmax(-1) if self.batch == 1 else out.logits.argmax(-1)
+            fused = getattr(out, "argmax", None)  # the lean forward's lm_head + argmax kernel
+            if fused is not None:
+                am = fused[0] if self.batch == 1 else fused
+            else:
+                am = out.logits[0].argmax(-1) if self.batch == 1 else out.logits.argmax(-1)
             return out.logits, am
 
     def _require_resident(self) -> None:

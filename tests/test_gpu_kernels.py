@@ -477,6 +477,42 @@ def test_tcgen05_tree_attention_full_mask_long_context(ops):
     assert N.device_status(reset=True) == 0  # no barrier wait of the kernel gave up
 
 
+# ---------------------------------------- K9 projection GEMM + lm_head argmax
+
+
+@pytest.mark.parametrize("rows,k,n", [(7, 2048, 151936), (65, 2048, 151936), (65, 2048, 5120), (33, 4096, 2048),
+                                      (128, 2048, 1000), (1, 64, 130)])
+def test_linear_and_fused_argmax_vs_torch(ops, rows, k, n):
+    """sf_linear_bf16 (rows up to 128) against torch's fp32 product rounded
+    to bf16, and sf_linear_bf16_argmax: the logits it writes equal the
+    unfused call's bit for bit, its argmax equals torch.argmax over those
+    logits exactly, and equals the argmax of the fp32 reference on every row
+    whose two largest reference logits are more than two bf16 ulps apart."""
+    gen = torch.Generator().manual_seed(rows + n)
+    x = torch.randn(rows, k, generator=gen).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(DEV)
+    ref = (x.float() @ w.float().t())
+    y = ops.linear(x, w)  # may route to the library GEMM for some shapes
+    from specfit_b200 import _native as N
+
+    mine = torch.empty(rows, n, dtype=torch.bfloat16, device=DEV)
+    N.check(N.lib.sf_linear_bf16(x.data_ptr(), rows, k, w.data_ptr(), n, mine.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream), "sf_linear_bf16")
+    assert (mine.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    assert torch.nn.functional.cosine_similarity(mine.float().flatten(), ref.flatten(), dim=0).item() >= 0.9999
+    assert (y.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    logits, am = ops.linear_argmax(x, w)
+    torch.cuda.synchronize()
+    assert torch.equal(logits, mine)
+    assert torch.equal(am, logits.argmax(-1))
+    _, am_only = ops.linear_argmax(x, w, logits=False)
+    assert torch.equal(am_only, am)
+    top2 = ref.topk(2, dim=-1).values
+    ulp = torch.ldexp(torch.ones_like(top2[:, 0]), torch.frexp(top2[:, 0].abs())[1] - 8)
+    clear = (top2[:, 0] - top2[:, 1]) > 2 * ulp
+    assert torch.equal(am[clear], ref.argmax(-1)[clear])
+
+
 # ------------------------------------------- drafter log-softmax + top-k
 
 
