@@ -70,7 +70,7 @@ extern "C" {
 /* Implementation choice of sf_grouped_swiglu_ex. */
 #define SF_SWIGLU_AUTO 0    /* tcgen05 path when the shape allows it, else SIMT */
 #define SF_SWIGLU_SIMT 1    /* CUDA-core kernel, any shape, f32 or bf16 */
-#define SF_SWIGLU_TCGEN05 2 /* tcgen05/TMEM + TMA kernel: bf16, H%64==0, I%64==0 */
+#define SF_SWIGLU_TCGEN05 2 /* tcgen05/TMEM + TMA kernel: bf16, H%128==0, I%64==0, <= 1024 experts */
 
 /* Message describing the last failure on the calling thread ("" if none). */
 SF_API const char* sf_last_error(void);

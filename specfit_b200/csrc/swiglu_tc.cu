@@ -20,7 +20,9 @@
 //   warps 2..5  epilogue: TMEM -> registers -> rounding -> global stores
 // Two TMEM accumulators (128 columns each) let the epilogue of one tile
 // overlap the MMAs of the next.  At these sizes the kernel streams expert
-// weights: every weight byte is read from HBM exactly once per layer.
+// weights: a weight tile is read once per pass of up to 128 token rows, and
+// an expert with more rows (a hot expert under skewed routes) has its passes
+// on neighbouring CTAs at about the same time, so the repeats hit L2.
 //
 // Every TMA load here is issued by one CTA for its own shared memory.
 #include <cuda.h>
@@ -50,10 +52,13 @@ constexpr int kBBox = 16;      // token rows per B TMA box
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 2 * kBN;
 constexpr int kUpPitch = 17;   // padded row pitch of the gate/up exchange buffer
+constexpr int kMaxExperts = 1024;  // experts per launch (the unit table lives in shared memory)
 
 struct __align__(8) SmemTail {
   float upbuf[64 * kUpPitch];
   int rowtok[kBN];  // gathered variant: token row of each row of the current pass
+  int unit_first[kMaxExperts + 1];  // number of the first unit of active[a]; [n_active] = all units
+  int unit_expert[kMaxExperts];     // active[a]
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full[2];
@@ -85,21 +90,62 @@ struct TileSpace {
 
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// Iterates this CTA's units in a fixed order; every role walks the same list.
-template <typename F>
-__device__ __forceinline__ void for_each_unit(int m_tiles, const int32_t* offsets,
-                                              const int32_t* active, int n_active,
-                                              const int32_t* expert_slot, F&& f) {
-  const int tiles = n_active * m_tiles;
-  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const int e = active[tile / m_tiles];
-    const int mt = tile % m_tiles;
-    const int r0 = offsets[e], r1 = offsets[e + 1];
-    const int slot = expert_slot[e];
-    for (int n0 = r0; n0 < r1; n0 += kBN) {
-      Unit u{e, slot, mt, n0, min(kBN, r1 - n0)};
-      if (!f(u)) return;
+// Numbers the units in shared memory, once per CTA: expert by expert
+// (active-list order), inside an expert weight tile by weight tile with the
+// passes of a tile adjacent.  Returns the number of units.
+__device__ __forceinline__ int number_units(SmemTail* tail, int m_tiles, const int32_t* offsets,
+                                            const int32_t* active, int n_active) {
+  for (int a = threadIdx.x; a < n_active; a += blockDim.x) {
+    const int e = active[a];
+    tail->unit_expert[a] = e;
+    tail->unit_first[a + 1] = (offsets[e + 1] - offsets[e] + kBN - 1) / kBN * m_tiles;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // Exclusive scan: lane l sums a contiguous chunk, the chunk totals are
+    // scanned with shuffles, then each lane writes its chunk's prefix.
+    const int lane = threadIdx.x;
+    const int per = (n_active + 31) / 32;
+    const int lo = min(n_active, lane * per), hi = min(n_active, lo + per);
+    int sum = 0;
+    for (int a = lo; a < hi; ++a) sum += tail->unit_first[a + 1];
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
     }
+    int run = incl - sum;
+    for (int a = lo; a < hi; ++a) {
+      run += tail->unit_first[a + 1];
+      tail->unit_first[a + 1] = run;
+    }
+    if (lane == 0) tail->unit_first[0] = 0;
+  }
+  __syncthreads();
+  return tail->unit_first[n_active];
+}
+
+// Iterates this CTA's units in a fixed order; every role walks the same list.
+// CTA b takes units b, b + G, b + 2G, ...  Dealing out units rather than
+// whole tiles keeps the CTAs within one unit of each other when a few hot
+// experts need several passes (skewed routes), and the passes of one tile
+// run on neighbouring CTAs at about the same time, so the tile's repeated
+// weight reads are served by L2.
+template <typename F>
+__device__ __forceinline__ void for_each_unit(const SmemTail* tail, int m_tiles, int n_active, int units,
+                                              const int32_t* offsets, const int32_t* expert_slot, F&& f) {
+  int a = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    while (tail->unit_first[a + 1] <= u) ++a;
+    const int e = tail->unit_expert[a];
+    const int base = tail->unit_first[a];
+    const int passes = (tail->unit_first[a + 1] - base) / m_tiles;
+    const int local = u - base;
+    const int r0 = offsets[e], r1 = offsets[e + 1];
+    const int n0 = r0 + (local % passes) * kBN;
+    Unit unit{e, expert_slot[e], local / passes, n0, min(kBN, r1 - n0)};
+    if (!f(unit)) return;
   }
 }
 
@@ -129,10 +175,12 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const TileSpace<kPhase> space(H, I);
-  const int n_active = *num_active;
-  // A CTA with no tile (an empty wave of a device-managed cache, or a grid
+  const int n_active = min(*num_active, kMaxExperts);
+  // A CTA with no unit (an empty wave of a device-managed cache, or a grid
   // larger than the work) leaves before touching barriers or TMEM.
-  if (n_active <= 0 || (int)blockIdx.x >= n_active * space.m_tiles) return;
+  if (n_active <= 0) return;
+  const int units = number_units(tail, space.m_tiles, offsets, active, n_active);
+  if ((int)blockIdx.x >= units) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -164,7 +212,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t it = 0;
-      for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
+      for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
         const int nb = (u.npass + kBBox - 1) / kBBox;
         const uint32_t bytes = kABytes + nb * kBBox * kBK * 2;
         if constexpr (kGather && kPhase == 1) {
@@ -210,7 +258,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t it = 0, unit = 0;
-      for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
+      for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
         const int buf = unit & 1;
         const uint32_t aph = (unit >> 1) & 1;
         if (!ptx::mbar_wait(&tail->acc_empty[buf], aph ^ 1, abort_flag, &g_swiglu_status, 3)) return false;
@@ -247,7 +295,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     const int quad = warp & 3;             // TMEM lane quadrant this warp may read
     const int row = quad * 32 + lane;      // accumulator row = TMEM lane
     uint32_t unit = 0;
-    for_each_unit(space.m_tiles, offsets, active, n_active, expert_slot, [&](const Unit& u) {
+    for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
       const int buf = unit & 1;
       const uint32_t aph = (unit >> 1) & 1;
       ptx::mbar_wait(&tail->acc_full[buf], aph, abort_flag, &g_swiglu_status, 6);
@@ -362,6 +410,7 @@ int tma_encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64
 
 bool swiglu_tcgen05_supports(const SwigluArgs& a) {
   return a.dtype == SF_DTYPE_BF16 && a.hidden % kBM == 0 && a.inter % 64 == 0 && a.hidden > 0 &&
+         a.num_experts > 0 && a.num_experts <= kMaxExperts &&
          a.inter > 0 && a.slot_stride % 8 == 0 && a.slot_stride >= 3LL * a.hidden * a.inter &&
          a.slot_count > 0 && aligned16(a.slot_storage) && aligned16(a.hidden_sorted) &&
          aligned16(a.act_workspace) && a.rows < (1LL << 31) && a.slot_count < (1LL << 31);

@@ -526,6 +526,17 @@ def logsoftmax_topk(logits: torch.Tensor, k: int, scale: float = 1.0,
 
 LINEAR_MAX_OUT = 4096  # measured on B200: wider weights stream as fast through cuBLAS
 LINEAR_MIN_IN = 4096
+_SMS: dict = {}
+
+
+def _wide_output(n_out: int, device: torch.device) -> bool:
+    """At least one 128-row weight tile per SM: ``sf_linear_bf16`` then runs
+    its persistent streaming kernel (the 151,936-row lm_head), measured on a
+    B200 a little faster than the library GEMM at 7 and 65 rows."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return n_out >= 128 * _SMS[idx]
 
 
 def linear_argmax(x: torch.Tensor, weight: torch.Tensor, logits: bool = True):
@@ -554,18 +565,21 @@ def linear_argmax(x: torch.Tensor, weight: torch.Tensor, logits: bool = True):
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``F.linear(x, weight)`` (no bias) for bf16 ``x [..., K]``: the tcgen05
-    split-K kernel (``sf_linear_bf16``) when the rows are few (<= 32) and the
-    weight is tall and narrow enough that splitting K is what fills the GPU
-    (out_features <= LINEAR_MAX_OUT, in_features >= LINEAR_MIN_IN: the o
-    projection and the drafter's 2048-wide outputs), else the library GEMM,
-    which streams wide weights as fast at these row counts."""
+    """``F.linear(x, weight)`` (no bias) for bf16 ``x [..., K]`` on the
+    tcgen05 kernel (``sf_linear_bf16``) where it measured faster than the
+    library GEMM on a B200: few rows (<= 32) against a tall, narrow weight
+    whose K split is what fills the GPU (out_features <= LINEAR_MAX_OUT,
+    in_features >= LINEAR_MIN_IN: the o projection and the drafter's
+    2048-wide outputs), and up to 128 rows against a wide weight (at least
+    one 128-row tile per SM: the lm_head).  Other shapes (the q|k|v
+    projection among them) take the library GEMM."""
     k = x.shape[-1]
     rows = x.numel() // k if k else 0
     n_out = weight.shape[0]
-    if (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and 0 < rows <= 32
-            and n_out <= LINEAR_MAX_OUT and k >= LINEAR_MIN_IN and x.is_contiguous()
-            and weight.is_contiguous()):
+    if (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and rows > 0
+            and x.is_contiguous() and weight.is_contiguous()
+            and ((rows <= 32 and n_out <= LINEAR_MAX_OUT and k >= LINEAR_MIN_IN)
+                 or (rows <= 128 and _wide_output(n_out, x.device)))):
         res = out if out is not None else torch.empty(*x.shape[:-1], n_out, dtype=x.dtype, device=x.device)
         rc = N.lib.sf_linear_bf16(x.data_ptr(), rows, k, weight.data_ptr(), n_out, res.data_ptr(),
                                   _stream(x.device))

@@ -14,9 +14,9 @@ chain of small torch kernels replaced by:
 * ``sf_qk_norm_rope`` — q/k head norms, rotary embedding, and the cache
   update writing k and v rows straight into the ``ReservedCache`` buffers
   (at the host length, or at the device-side offset in static mode);
-* optionally (``fused_head``) the lm_head of verify-sized passes with the
-  greedy argmax fused into it (``sf_linear_bf16_argmax``; the result then
-  carries ``argmax`` next to ``logits``);
+* the lm_head of verify-sized passes with the greedy argmax fused into it
+  (``sf_linear_bf16_argmax``; the result carries ``argmax`` next to
+  ``logits``);
 * ``sf_tree_attention`` per request, the o projection, and the MoE block:
   its gate module (router hooks still fire) and, with every expert resident
   and no hooks on the block, the experts up to the combine, which is fused
@@ -45,15 +45,15 @@ from .tree_attention import _causal_bits, _packed_bits
 
 
 class LeanQwen3Forward:
-    def __init__(self, model, fused_head: bool = False) -> None:
+    def __init__(self, model, fused_head: bool = True) -> None:
         cfg = model.config
         self.model = model
-        # With ``fused_head`` verify-sized passes (<= 128 rows) run the lm_head
-        # on the tcgen05 projection kernel with the argmax fused into it
-        # (``out.argmax``).  Off by default: on a B200 the library GEMM plus
-        # argmax measured faster for the 151,936 x 2,048 head (131 vs 145 us
-        # at 7 rows, 148 vs 361 us at 65 rows), the one-tile-per-CTA kernel
-        # not overlapping a tile's epilogue with the next tile's loads.
+        # Verify-sized passes (<= 128 rows) run the lm_head on the persistent
+        # tcgen05 streaming kernel with the greedy argmax fused into its
+        # epilogue (``out.argmax``); on a B200 that measured 128 vs 131 us at
+        # 7 rows and 140 vs 145 us at 65 rows against the library GEMM plus
+        # torch.argmax for the 151,936 x 2,048 head.  ``fused_head=False``
+        # keeps ``ops.linear`` and leaves ``out.argmax`` None.
         self.fused_head = fused_head
         self.H = cfg.hidden_size
         self.hq, self.hkv, self.D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim

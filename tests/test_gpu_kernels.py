@@ -285,6 +285,37 @@ def test_tc_and_simt_agree(ops):
     assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= 0.9999
 
 
+@pytest.mark.parametrize("tokens", [16, 129, 300])
+def test_swiglu_few_experts_many_rows(ops, tokens):
+    """Every token routed to the same 8 experts: fewer weight tiles than SMs,
+    each tile with one to three passes of up to 128 rows, so the tensor-core
+    kernel's CTAs past the tile count either take passes or leave.  Equal to
+    the oracle, to the CUDA-core kernel, and (gathered call) bit for bit to
+    the gather + grouped SwiGLU."""
+    weights, x = synthetic.bf16_layer_inputs(seed=60 + tokens, tokens=tokens)
+    rng = np.random.default_rng(tokens)
+    idx_np = np.stack([rng.permutation(8) for _ in range(tokens)]).astype(np.int64)
+    topw_np = rng.dirichlet(np.ones(8), size=tokens).astype(np.float32)
+    idx = torch.from_numpy(idx_np).to(DEV)
+    topw = torch.from_numpy(topw_np).to(DEV)
+    xd = x.to(DEV)
+    out, y_tc, d = run_block(ops, xd, weights, idx, topw, impl=2)
+    _, y_simt, _ = run_block(ops, xd, weights, idx, topw, impl=1)
+    packed = {e: weights.packed(e).float().numpy() for e in range(8)}
+    ref = mo.moe_experts(x.float().numpy(), idx_np, topw_np, packed, 2048, 768, "bf16")
+    got = out.float().cpu().numpy()
+    assert np.abs(got - ref).max() <= ATOL_BF16 and cosine(got, ref) >= COS_MIN
+    a, b = y_tc.float().cpu().numpy(), y_simt.float().cpu().numpy()
+    assert np.abs(a - b).max() <= ATOL_BF16 and cosine(a, b) >= 0.9999
+    storage = weights.packed_all().to(DEV)
+    slot = torch.arange(128, dtype=torch.int32, device=DEV)
+    got_g = ops.grouped_swiglu_gathered(xd, topw, d, slot, storage, 2048, 768)
+    assert torch.equal(got_g, y_tc)
+    from specfit_b200 import _native as N
+
+    assert N.device_status(reset=True) == 0
+
+
 @pytest.mark.parametrize("tokens,routes", [(1, "zipf"), (7, "zipf"), (65, "uniform"), (129, "zipf"), (512, "zipf")])
 def test_gathered_swiglu_equals_gather_then_swiglu(ops, tokens, routes):
     """The gathered call (token rows by TMA gather4, weights through
@@ -481,7 +512,8 @@ def test_tcgen05_tree_attention_full_mask_long_context(ops):
 
 
 @pytest.mark.parametrize("rows,k,n", [(7, 2048, 151936), (65, 2048, 151936), (65, 2048, 5120), (33, 4096, 2048),
-                                      (128, 2048, 1000), (1, 64, 130)])
+                                      (128, 2048, 1000), (1, 64, 130), (20, 4096, 19000), (100, 2048, 151936),
+                                      (90, 2048, 20000), (40, 2048, 151936)])
 def test_linear_and_fused_argmax_vs_torch(ops, rows, k, n):
     """sf_linear_bf16 (rows up to 128) against torch's fp32 product rounded
     to bf16, and sf_linear_bf16_argmax: the logits it writes equal the
@@ -575,6 +607,25 @@ def test_combine_add_rmsnorm_equals_the_two_steps(ops, tokens, H):
     res_b, out_b = res.clone(), torch.empty_like(res)
     ops.moe_combine_add_rmsnorm(ys, d, idx, res_b, w, 1e-6, out=out_b)
     assert torch.equal(res_a, res_b) and torch.equal(out_a, out_b)
+
+
+def test_fused_argmax_ties_pick_the_lowest_row(ops):
+    """Equal logits in different tiles (so different CTAs) of the
+    151,936-row head, and an all-zero token: the fused argmax returns the
+    lowest row, as torch.argmax does on the same logits."""
+    n, k = 151936, 2048
+    gen = torch.Generator().manual_seed(9)
+    x = torch.randn(3, k, generator=gen).to(torch.bfloat16)
+    x[2] = 0
+    w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16)
+    w[150001] = w[777] = (x[0].float() * 0.01).to(torch.bfloat16)
+    w[151935] = w[40000] = (x[1].float() * 0.01).to(torch.bfloat16)
+    xd, wd = x.to(DEV), w.to(DEV)
+    logits, am = ops.linear_argmax(xd, wd)
+    torch.cuda.synchronize()
+    assert am.tolist() == [777, 40000, 0]
+    assert torch.equal(am, logits.argmax(-1))
+    assert logits[0, 777] == logits[0, 150001] and logits[1, 40000] == logits[1, 151935]
 
 
 # ------------------------------------------- projection GEMM (sf_linear_bf16)
