@@ -872,6 +872,16 @@ def b200_arm(args):
     assert all(torch.equal(a, host[policy][1][0]) for r in dev_runs.values() for a in r[1]), \
         "device-managed caches gave different argmaxes"
     ms, ams, timed_stats = dev_runs[policy]
+    # The capture counted every wave; a layer whose experts fit its slots
+    # skips its later waves (3 launches each) through the conditional node,
+    # and each layer with later waves adds one join kernel.  The inputs are
+    # the same every step, so the last pass's plans hold for every step.
+    for c in loaded.caches:
+        dr = c.directory
+        if dr is not None and dr.waves > 1:
+            if int(dr.wave_count[1:].sum()) == 0:
+                launches_per_pass -= 3 * (dr.waves - 1)
+            launches_per_pass += 1
     launches = launches_per_pass * args.steps
     value = sum_over_ranks(committed_of(ams), world, device) / (ms / 1e3)
     h2d_roofline = h2d_roofline_of(timed_stats, ms / args.steps, h2d_peak)
@@ -1838,6 +1848,7 @@ def kernel_cases(device, only=()):
         return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
 
     want = lambda name: not only or name in only
+    cur = lambda: torch.cuda.current_stream(device).cuda_stream  # the stream at call time (graph capture)
     cases = []
     storage = slot = router = None
     if want("router") or want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
@@ -1874,11 +1885,10 @@ def kernel_cases(device, only=()):
         if want("add_rmsnorm"):
             xa, res, hn = randn(t, H), randn(t, H), torch.empty(t, H, **bf)
             nw = torch.ones(H, **bf)
-            st = torch.cuda.current_stream(device).cuda_stream
             cases.append(("add_rmsnorm", f"T={t}",
-                          lambda xa=xa, res=res, nw=nw, hn=hn, st=st, t=t: N.check(N.lib.sf_add_rmsnorm(
+                          lambda xa=xa, res=res, nw=nw, hn=hn, t=t: N.check(N.lib.sf_add_rmsnorm(
                               xa.data_ptr(), res.data_ptr(), res.data_ptr(), nw.data_ptr(), 1e-6, t, H,
-                              hn.data_ptr(), st), "sf_add_rmsnorm"),
+                              hn.data_ptr(), cur()), "sf_add_rmsnorm"),
                           4 * t * H * 2 + H * 2))
         if want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
             for kind in ("zipf", "uniform"):
@@ -1930,12 +1940,12 @@ def kernel_cases(device, only=()):
         store = cache.storage.view(24, -1)
         if want("dir_plan"):
             cases.append(("dir_plan", "E=128 S=24, 40 experts",
-                          lambda: directory.plan(d, False, stream), 24 * 16 + 128 * 4 + 6 * (128 * 8 + 24 * 8)))
+                          lambda: directory.plan(d, False, cur()), 24 * 16 + 128 * 4 + 6 * (128 * 8 + 24 * 8)))
         if want("dir_fill"):
             torch.cuda.synchronize(device)
             n = int(directory.fill_count[0].item())
             cases.append(("dir_fill", f"{n} experts of 9.44 MB from page-locked host memory (bytes over PCIe)",
-                          lambda: directory.fill(0, store, stream), n * EXPERT_BYTES))
+                          lambda: directory.fill(0, store, cur()), n * EXPERT_BYTES))
         kernel_cases.keep = (hp, cache)  # alive while the cases run
     if want("logsoftmax_topk"):
         for rows in (1, 8):
@@ -1954,10 +1964,9 @@ def kernel_cases(device, only=()):
         wq = randn((HQ + 2 * HKV) * D, H, std=0.02)
         xq = randn(65, H)
         yq = torch.empty(65, wq.shape[0], **bf)
-        st = torch.cuda.current_stream(device).cuda_stream
         cases.append(("qkv", "rows=65 2048->5120 (ours)",
                       lambda: N.check(N.lib.sf_linear_bf16(xq.data_ptr(), 65, H, wq.data_ptr(), wq.shape[0],
-                                                           yq.data_ptr(), st), "sf_linear_bf16"),
+                                                           yq.data_ptr(), cur()), "sf_linear_bf16"),
                       wq.numel() * 2 + 65 * (H + wq.shape[0]) * 2))
         cases.append(("qkv", "rows=65 2048->5120 library GEMM", lambda: torch.nn.functional.linear(xq, wq),
                       wq.numel() * 2 + 65 * (H + wq.shape[0]) * 2))
@@ -1973,10 +1982,13 @@ def kernel_cases(device, only=()):
 def kernels_mode(args):
     """Each hot kernel alone (``kernel_cases``): per launch, CUDA events
     around it with L2 flushed before it (a 256 MB write outside the events:
-    "cold"), and the mean of back-to-back launches ("warm", the in-pass case
-    where the producer's output is still in L2).  One JSON line per case:
-    us, algorithmic bytes, GB/s and the fraction of the measured HBM copy
-    peak (cold).  Small enough to run whole under a profiler with -k/-c."""
+    "cold"), the mean of back-to-back launches ("warm", the in-pass case
+    where the producer's output is still in L2), and the mean of the same
+    back-to-back launches replayed from one CUDA graph ("graph": no host
+    launch cost between them, as inside the verify pass; null where the case
+    cannot be captured).  One JSON line per case: us, algorithmic bytes,
+    GB/s and the fraction of the measured HBM copy peak (cold).  Small
+    enough to run whole under a profiler with -k/-c."""
     device = torch.device("cuda", 0)
     peaks = measured_peaks()
     only = tuple(k for k in args.kernel.split(",") if k)
@@ -2003,8 +2015,24 @@ def kernels_mode(args):
         torch.cuda.synchronize(device)
         cold = statistics.median(x.elapsed_time(y) * 1e3 for x, y in pairs)
         warm = a.elapsed_time(b) * 1e3 / iters
+        graph_us = None
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(iters):
+                    fn()
+            graph.replay()
+            ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ga.record(stream)
+            graph.replay()
+            gb.record(stream)
+            torch.cuda.synchronize(device)
+            graph_us = round(ga.elapsed_time(gb) * 1e3 / iters, 2)
+            del graph
+        except RuntimeError:
+            torch.cuda.synchronize(device)
         print(json.dumps({"mode": "kernels", "kernel": name, "case": case, "us_cold": round(cold, 2),
-                          "us_warm": round(warm, 2), "algorithmic_bytes": int(algo),
+                          "us_warm": round(warm, 2), "us_graph": graph_us, "algorithmic_bytes": int(algo),
                           "GBps_cold": round(algo / cold / 1e3, 1),
                           "frac_of_hbm_peak_cold": round(algo / cold / 1e3 / peaks["hbm_gbs"], 4),
                           "us_at_peak": round(algo / peaks["hbm_gbs"] / 1e3, 2),

@@ -381,10 +381,37 @@ SF_API int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, void
                        int num_slots, int waves, int resident_first, void* wave_table, void* wave_active,
                        void* wave_count, void* fill_expert, void* fill_slot, void* fill_count, void* status,
                        void* stream);
+/*
+ * sf_dir_plan with a conditional handle (0: none, as sf_dir_plan) of the
+ * graph the launch is captured into: the plan sets it to 1 when some wave
+ * after the first has experts, else 0 (sf_capture_* below).
+ */
+SF_API int sf_dir_plan_ex(void* slot_expert, void* slot_gen, void* slot_stamp, void* expert_slot, void* clock,
+                          void* counters, const void* active, const void* num_active, int num_experts,
+                          int num_slots, int waves, int resident_first, void* wave_table, void* wave_active,
+                          void* wave_count, void* fill_expert, void* fill_slot, void* fill_count, void* status,
+                          uint64_t later_waves, void* stream);
 SF_API int sf_dir_fill(const void* expert_src, void* storage, int64_t slot_stride_bytes, int64_t expert_bytes,
                        const void* fill_expert, const void* fill_slot, const void* fill_count, int num_slots,
                        int grid, void* stream);
 SF_API int sf_host_device_address(const void* host, uint64_t* device_address);
+
+/*
+ * Conditional sections of a captured CUDA graph (no counterpart in the
+ * reference, which runs the wave loop on the host): a device-managed cache's
+ * waves after the first are captured into the body of an IF node, so a layer
+ * whose experts fit its slots launches nothing for them.
+ * sf_capture_cond_handle: a new conditional handle (reset to 0 at every graph
+ * launch) of the graph `stream` is capturing into; SF_ERR_STATE when it is
+ * not capturing.  sf_capture_if_begin: an IF node on `handle` behind the
+ * stream's captured work, made the stream's dependency, and `body_stream`
+ * (another stream) capturing into its body.  sf_capture_if_end: ends the body
+ * capture and adds an empty kernel on `stream` behind the node.
+ */
+SF_API int sf_capture_body_stream(void** stream); /* per device, created once, kept until exit */
+SF_API int sf_capture_cond_handle(void* stream, uint64_t* handle);
+SF_API int sf_capture_if_begin(void* stream, void* body_stream, uint64_t handle);
+SF_API int sf_capture_if_end(void* stream, void* body_stream);
 
 /*
  * Tree attention (GQA): for query row i of head h (kv head h / (Hq/Hkv)),

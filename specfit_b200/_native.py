@@ -140,7 +140,13 @@ SIGNATURES = {
     "sf_cache_adopt_slots": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp]),
     "sf_dir_plan": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
                            _vp, _vp, _vp, _vp, _vp]),
+    "sf_dir_plan_ex": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                              _vp, _vp, _vp, _vp, _u64, _vp]),
     "sf_dir_fill": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp]),
+    "sf_capture_body_stream": (_i32, [ctypes.POINTER(_vp)]),
+    "sf_capture_cond_handle": (_i32, [_vp, ctypes.POINTER(_u64)]),
+    "sf_capture_if_begin": (_i32, [_vp, _vp, _u64]),
+    "sf_capture_if_end": (_i32, [_vp, _vp]),
     "sf_host_device_address": (_i32, [_vp, ctypes.POINTER(_u64)]),
     "sf_slot_fill_batch": (_i32, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
                                   _i32, _vp]),

@@ -53,6 +53,9 @@ struct PlanArgs {
   int32_t* fill_count;   // [W]
   int32_t* status;       // [1] set to 1 if the experts did not fit W waves
   int E, S, W, resident_first;
+  // Conditional handle of a captured graph (0: none): set to whether any
+  // wave after the first has experts, so the graph runs those waves only then.
+  unsigned long long later_waves;
 };
 
 __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
@@ -74,7 +77,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   int32_t* act_in = order + E;
   int32_t* table_sm = act_in + E;
   uint8_t* leased = reinterpret_cast<uint8_t*>(table_sm + E);
-  __shared__ int n_sh, pos_sh, w_sh, bad_sh, cnt_sh, nf_sh, start_sh;
+  __shared__ int n_sh, pos_sh, w_sh, bad_sh, cnt_sh, nf_sh, start_sh, cnt0_sh;
   const int tid = threadIdx.x, nt = blockDim.x;
 
   if (tid == 0) {
@@ -118,7 +121,16 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
   }
   int64_t clock = 0, h2d = 0, hits = 0, evictions = 0;
   if (tid == 0) clock = *a.clock;
+  __syncthreads();  // n_sh is final
   for (int w = 0; w < a.W; ++w) {
+    if (pos_sh >= n_sh && w > 0) {
+      // Every expert has its wave: the rest stay empty (counts are 0 from the
+      // start); their tables are still written (-1) so a stale wave can never
+      // be read.
+      int32_t* table = a.wave_table + (size_t)w * E;
+      for (int i = tid; i < E; i += nt) table[i] = -1;
+      continue;
+    }
     // Rank every slot by its LRU key; nothing is leased at a wave's start.
     for (int s = tid; s < S; s += nt) {
       const int occ = sexp[s] >= 0;
@@ -168,6 +180,7 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
       cnt_sh = cnt;
       nf_sh = nf;
       pos_sh = pos;
+      if (w == 0) cnt0_sh = cnt;
     }
     __syncthreads();
     // The wave's outputs, written by every thread.
@@ -183,8 +196,6 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
       a.wave_count[w] = cnt;
       a.fill_count[w] = nf;
     }
-    // Later waves of a layer that needs fewer waves stay empty; their tables
-    // are still written (-1) so a stale wave can never be read.
   }
   __syncthreads();
   for (int i = tid; i < S; i += nt) {
@@ -200,6 +211,9 @@ __global__ void __launch_bounds__(1024) dir_plan_kernel(PlanArgs a) {
     a.counters[3] += evictions;
     if (bad_sh) *a.status = 2;
     else if (pos_sh < n_sh) *a.status = 1;
+    // Wave 0 holds at most S experts; the later waves have work iff it could
+    // not take them all.
+    if (a.later_waves != 0ull) cudaGraphSetConditional(a.later_waves, n_sh > cnt0_sh ? 1u : 0u);
   }
 }
 
@@ -237,11 +251,12 @@ __global__ void __launch_bounds__(256) dir_fill_kernel(const uint64_t* __restric
 }  // namespace
 }  // namespace sf
 
-extern "C" int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, void* expert_slot,
-                           void* clock, void* counters, const void* active, const void* num_active,
-                           int num_experts, int num_slots, int waves, int resident_first,
-                           void* wave_table, void* wave_active, void* wave_count, void* fill_expert,
-                           void* fill_slot, void* fill_count, void* status, void* stream) {
+extern "C" int sf_dir_plan_ex(void* slot_expert, void* slot_gen, void* slot_stamp, void* expert_slot,
+                              void* clock, void* counters, const void* active, const void* num_active,
+                              int num_experts, int num_slots, int waves, int resident_first,
+                              void* wave_table, void* wave_active, void* wave_count, void* fill_expert,
+                              void* fill_slot, void* fill_count, void* status, uint64_t later_waves,
+                              void* stream) {
   using namespace sf;
   SF_CHECK_ARG(num_experts > 0 && num_experts <= 4096, "num_experts must be in [1, 4096]");
   SF_CHECK_ARG(num_slots > 0 && num_slots <= 4096, "num_slots must be in [1, 4096]");
@@ -271,6 +286,7 @@ extern "C" int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, 
   a.S = num_slots;
   a.W = waves;
   a.resident_first = resident_first;
+  a.later_waves = later_waves;
   const size_t smem = (size_t)num_slots * (8 + 4 * 5 + 1) + (size_t)num_experts * 16;
   SF_CHECK_ARG(smem <= 160 * 1024, "directory too large for one CTA");
   if (smem > 48 * 1024)
@@ -280,6 +296,16 @@ extern "C" int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, 
   SF_CHECK_CUDA(launch_pdl(dir_plan_kernel, dim3(1), dim3(threads), smem, as_stream(stream), a));
   SF_CHECK_LAUNCH();
   return SF_OK;
+}
+
+extern "C" int sf_dir_plan(void* slot_expert, void* slot_gen, void* slot_stamp, void* expert_slot,
+                           void* clock, void* counters, const void* active, const void* num_active,
+                           int num_experts, int num_slots, int waves, int resident_first,
+                           void* wave_table, void* wave_active, void* wave_count, void* fill_expert,
+                           void* fill_slot, void* fill_count, void* status, void* stream) {
+  return sf_dir_plan_ex(slot_expert, slot_gen, slot_stamp, expert_slot, clock, counters, active, num_active,
+                        num_experts, num_slots, waves, resident_first, wave_table, wave_active, wave_count,
+                        fill_expert, fill_slot, fill_count, status, 0, stream);
 }
 
 extern "C" int sf_dir_fill(const void* expert_src, void* storage, int64_t slot_stride_bytes, int64_t expert_bytes,

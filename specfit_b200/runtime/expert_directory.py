@@ -81,15 +81,37 @@ class DeviceExpertDirectory:
                     counters=self.counters.cpu(), status=int(self.status.item()))
 
     # ------------------------------------------------------------- work
-    def plan(self, d, resident_first: bool, stream) -> None:
-        N.check(N.lib.sf_dir_plan(self.slot_expert.data_ptr(), self.slot_gen.data_ptr(),
-                                  self.slot_stamp.data_ptr(), self.expert_slot.data_ptr(),
-                                  self.clock.data_ptr(), self.counters.data_ptr(), d.active.data_ptr(),
-                                  d.num_active.data_ptr(), self.E, self.S, self.waves, int(resident_first),
-                                  self.wave_table.data_ptr(), self.wave_active.data_ptr(),
-                                  self.wave_count.data_ptr(), self.fill_expert.data_ptr(),
-                                  self.fill_slot.data_ptr(), self.fill_count.data_ptr(),
-                                  self.status.data_ptr(), stream), "sf_dir_plan")
+    def plan(self, d, resident_first: bool, stream, later_waves: int = 0) -> None:
+        """Plans every wave of the dispatch ``d``; with ``later_waves`` (a
+        conditional handle of the graph being captured, ``capture_handle``)
+        the plan also sets it to whether any wave after the first has
+        experts."""
+        N.check(N.lib.sf_dir_plan_ex(self.slot_expert.data_ptr(), self.slot_gen.data_ptr(),
+                                     self.slot_stamp.data_ptr(), self.expert_slot.data_ptr(),
+                                     self.clock.data_ptr(), self.counters.data_ptr(), d.active.data_ptr(),
+                                     d.num_active.data_ptr(), self.E, self.S, self.waves, int(resident_first),
+                                     self.wave_table.data_ptr(), self.wave_active.data_ptr(),
+                                     self.wave_count.data_ptr(), self.fill_expert.data_ptr(),
+                                     self.fill_slot.data_ptr(), self.fill_count.data_ptr(),
+                                     self.status.data_ptr(), later_waves, stream), "sf_dir_plan")
+
+    # ----------------------------------------------- captured later waves
+    @staticmethod
+    def capture_handle(stream) -> int:
+        """A conditional handle of the graph ``stream`` is capturing into."""
+        out = ctypes.c_uint64()
+        N.check(N.lib.sf_capture_cond_handle(stream, ctypes.byref(out)), "sf_capture_cond_handle")
+        return out.value
+
+    @staticmethod
+    def later_waves_stream(device) -> torch.cuda.ExternalStream:
+        """The stream the later waves are captured on: the library's own
+        per-device stream (not one of torch's pooled streams, which can be
+        the very stream being captured)."""
+        with torch.cuda.device(device):
+            out = ctypes.c_void_p()
+            N.check(N.lib.sf_capture_body_stream(ctypes.byref(out)), "sf_capture_body_stream")
+        return torch.cuda.ExternalStream(out.value, device=device)
 
     def fill(self, wave: int, storage: torch.Tensor, stream) -> None:
         N.check(N.lib.sf_dir_fill(self.src_addr.data_ptr(), storage.data_ptr(),

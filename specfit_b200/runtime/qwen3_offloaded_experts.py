@@ -163,14 +163,35 @@ class Qwen3OffloadedExperts(nn.Module):
         d = ops.moe_dispatch(top_k_index, self.num_experts)
         xs, ws = ops.moe_gather(h, top_k_weights, d)
         storage = cache.storage.view(cache.slot_count, -1)
-        directory.plan(d, self.execution_policy is ExpertExecutionPolicy.RESIDENT_FIRST, stream)
+        # Under graph capture the waves after the first go into the body of a
+        # conditional node that the plan kernel opens only when the layer
+        # needs more experts than its slots; eagerly, every wave is launched
+        # (an empty one returns at once).
+        later = (directory.capture_handle(stream)
+                 if directory.waves > 1 and torch.cuda.is_current_stream_capturing() else 0)
+        directory.plan(d, self.execution_policy is ExpertExecutionPolicy.RESIDENT_FIRST, stream, later)
         ys = torch.empty(xs.shape[0], self.hidden_size, dtype=h.dtype, device=h.device)
         act = torch.empty(max(xs.shape[0], 1), self.intermediate_size, dtype=h.dtype, device=h.device)
-        for w in range(directory.waves):  # later waves are empty unless the layer needs more experts than slots
-            directory.fill(w, storage, stream)
+
+        def wave(w, st):
+            directory.fill(w, storage, st)
             ops.grouped_swiglu(xs, ws, d, directory.wave_table[w], storage, self.hidden_size,
                                self.intermediate_size, impl=self.swiglu_impl, active=directory.wave_active[w],
                                num_active=directory.wave_count[w:w + 1], act_workspace=act, out=ys)
+
+        wave(0, stream)
+        if later:
+            body = directory.later_waves_stream(h.device)
+            N.check(N.lib.sf_capture_if_begin(stream, body.cuda_stream, later), "sf_capture_if_begin")
+            try:
+                with torch.cuda.stream(body):
+                    for w in range(1, directory.waves):
+                        wave(w, body.cuda_stream)
+            finally:
+                N.check(N.lib.sf_capture_if_end(stream, body.cuda_stream), "sf_capture_if_end")
+        else:
+            for w in range(1, directory.waves):
+                wave(w, stream)
         ops._launched(1 + directory.waves)  # the plan and one fill per wave (SwiGLU counts itself)
         return ys, d
 

@@ -218,3 +218,83 @@ def test_sweep_fills_follow_the_lru_replay(slots):
             assert torch.equal(a, b)
     finally:
         m.close()
+
+
+def test_captured_later_waves_run_only_when_needed():
+    """The waves after a layer's first are captured behind a conditional
+    node that the plan kernel opens only when the layer's experts do not fit
+    its slots.  Routes held in a device buffer (read by the captured pass)
+    switch each layer between 4 experts (one wave with 6 slots) and ~16
+    (three waves) from one replay to the next: every replay gives the eager
+    host-managed pass's logits bit for bit, the caches end in the same state,
+    and the directories show which layers used later waves."""
+    from test_gpu_model import make_tree
+
+    from specfit_b200 import synthetic
+    from specfit_b200.runtime.kv_cache import ReservedCache
+    from specfit_b200.runtime.lean_forward import LeanQwen3Forward
+    from specfit_b200.runtime.qwen3_verifier import build_random_offloaded_qwen3, qwen3_moe_config
+    from specfit_b200.runtime.verify_graph import VerifyGraph
+
+    cfg = qwen3_moe_config(3, hidden=256, experts=16, top_k=4, moe_inter=128, heads=8, kv_heads=2,
+                           head_dim=128, vocab=512)
+    T, L = 13, 3
+    rng = np.random.default_rng(11)
+    few = [torch.from_numpy(np.stack([rng.permutation(4) for _ in range(T)])).to(DEV) for _ in range(L)]
+    many = [torch.from_numpy(synthetic.zipf_routes(T, l, seed=8, experts=16, top_k=4)).to(DEV)
+            for l in range(L)]
+    routes = torch.empty(L, T, 4, dtype=torch.int64, device=DEV)
+    plans = [("few", "many", "few"), ("many", "few", "many"), ("few", "few", "few"), ("many", "many", "many"),
+             ("many", "few", "few")]
+
+    def set_routes(plan):
+        for l, kind in enumerate(plan):
+            routes[l].copy_((few if kind == "few" else many)[l])
+
+    set_routes(plans[0])
+    models = [build_random_offloaded_qwen3(device=DEV, slots_per_layer=6, config=cfg, seed=12, std=0.05)
+              for _ in range(2)]
+    try:
+        for m in models:
+            for l, layer in enumerate(m.model.model.layers):
+                layer.mlp.gate.register_forward_hook(
+                    lambda mod, a, out, l=l: (out[0], out[1], routes[l]) if out[2].shape[0] == T else None)
+        ctx = torch.randint(0, 512, (1, 21), generator=torch.Generator().manual_seed(3)).to(DEV)
+        tree = make_tree(nodes=T - 1, depth=4, seed=2)
+        ids = tree.verification_token_ids(torch.tensor([[7]], device=DEV))
+        mask = tree.verification_attention_mask(base_kv_length=21, device=DEV)
+        pos = tree.verification_position_ids(base_kv_length=21, device=DEV)
+        kv, fwd = [], []
+        for m in models:
+            lean = LeanQwen3Forward(m.model)
+            cache = ReservedCache(config=m.model.config, capacity=21 + T)
+            with torch.no_grad():
+                lean(input_ids=ctx, past_key_values=cache, use_cache=True)
+            kv.append(cache)
+            fwd.append(lean)
+        models[1].enter_device_managed_caches()
+        vg = VerifyGraph(models[1].model, kv[1], q_len=T, device=DEV, forward=fwd[1])
+        vg.capture(ids, mask, pos)  # two warm-up passes run for real
+        for _ in range(2):
+            with torch.no_grad():
+                fwd[0](input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=kv[0], use_cache=True)
+            kv[0].crop(21)
+        for plan in plans:
+            set_routes(plan)
+            with torch.no_grad():
+                ref = fwd[0](input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=kv[0],
+                             use_cache=True).logits.clone()
+            kv[0].crop(21)
+            vg.load(ids, mask, pos)
+            vg.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(vg.logits, ref), plan
+            later = [int(c.directory.wave_count[1:].sum()) > 0 for c in models[1].caches]
+            assert later == [kind == "many" for kind in plan], (plan, later)
+        assert models[0].cache_stats() == models[1].cache_stats()
+        from specfit_b200 import _native as N
+
+        assert N.device_status(reset=True) == 0
+    finally:
+        for m in models:
+            m.close()
