@@ -1921,6 +1921,22 @@ def kernel_cases(device, only=()):
                           lambda q=q, kv=kv, bits=bits, ctx=ctx, impl=impl:
                           ops.tree_attention(q, kv[0], kv[1], bits, ctx, impl=impl),
                           (ctx + t) * HKV * D * 2 * 2 + 2 * t * HQ * D * 2))
+    if want("tree_attention_batched"):
+        # Configuration 5's attention: 8 requests x 65 rows x 32 heads over
+        # 4,161 keys each, one batched launch against one launch per request.
+        B5, T5, C5 = 8, 65, 4096
+        q5 = randn(B5, HQ, T5, D)
+        kv5 = [randn(B5, HKV, C5 + T5 + 31, D) for _ in range(2)]
+        par5 = synthetic.random_tree(T5 - 1, max_depth=6, max_branch=4, seed=5)[1]
+        bits5 = ops.tree_bits_from_parents(par5, device).unsqueeze(0).expand(B5, -1, -1).contiguous()
+        out5 = torch.empty(B5, T5, HQ, D, **bf)
+        k5, v5 = kv5[0][:, :, :C5 + T5], kv5[1][:, :, :C5 + T5]
+        nbytes = B5 * ((C5 + T5) * HKV * D * 2 * 2 + 2 * T5 * HQ * D * 2)
+        cases.append(("tree_attention_batched", f"B={B5} T={T5} ctx={C5} one launch",
+                      lambda: ops.tree_attention_batched(q5, k5, v5, bits5, C5, out=out5), nbytes))
+        cases.append(("tree_attention_batched", f"B={B5} T={T5} ctx={C5} one launch per request",
+                      lambda: [ops.tree_attention(q5[b], k5[b], v5[b], bits5[b], C5, out=out5[b])
+                               for b in range(B5)], nbytes))
     if want("dir_plan") or want("dir_fill"):
         # The device-managed cache's plan and fill kernels at configuration 2's
         # shape: 24 slots per layer, 40 routed experts, misses from a

@@ -447,6 +447,29 @@ SF_API int sf_tree_attention_ex(const void* q, const void* k, const void* v, con
                                 int impl, void* stream);
 
 /*
+ * Several requests' tree attention in one launch of the tcgen05 kernel (the
+ * per-request calls of the verify forward over a batch, eagle3_tree.py:
+ * 1243-1250 with batch > 1): request b's q, k/v, tree bits and output start
+ * b * (q_batch_stride, kv_batch_stride, bits_batch_stride, out_batch_stride)
+ * elements (uint32 words for the bits) after request 0's; every request has
+ * the same q_len, kv_len, prefix_len and head strides.  The key range is
+ * split so that the batch's CTAs fill the SMs.  Returns SF_ERR_UNSUPPORTED,
+ * with no message, for layouts the tcgen05 kernel does not take (D != 128,
+ * strides not multiples of 8 elements, unaligned rows): callers then make
+ * one sf_tree_attention call per request.
+ */
+SF_API size_t sf_tree_attention_batched_workspace_bytes(int batch, int num_heads, int64_t q_len,
+                                                       int64_t kv_len);
+SF_API int sf_tree_attention_batched(const void* q, const void* k, const void* v, const uint32_t* tree_bits,
+                                     int bit_words, int batch, int64_t q_batch_stride,
+                                     int64_t kv_batch_stride, int64_t bits_batch_stride,
+                                     int64_t out_batch_stride, int64_t q_len, int64_t kv_len,
+                                     int64_t prefix_len, int num_heads, int num_kv_heads, int head_dim,
+                                     int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
+                                     int64_t kv_row_stride, float scale, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/*
  * SpecFit exact subtree selection (host function, runs on the calling CPU
  * thread; no GPU work).  Nodes are raw ids 1..num_nodes with parents[raw-1]
  * < raw (0 = the verification seed) and cumulative log-probabilities

@@ -159,6 +159,10 @@ SIGNATURES = {
                                  _i64, _i64, _i64, _i64, _f32, _vp, _vp, _sz, _vp]),
     "sf_tree_attention_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i32, _i32,
                                     _i64, _i64, _i64, _i64, _f32, _vp, _vp, _sz, _i32, _vp]),
+    "sf_tree_attention_batched_workspace_bytes": (_sz, [_i32, _i32, _i64, _i64]),
+    "sf_tree_attention_batched": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+                                         _i64, _i32, _i32, _i32, _i64, _i64, _i64, _i64, _f32, _vp, _vp,
+                                         _sz, _vp]),
     "sf_ep_row_bytes": (_i64, [_i32, _i32, _i32]),
     "sf_ep_send_pack": (_i32, [_vp, _i32, _i64, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64,
                                _vp, _vp, _vp, _vp, _vp]),

@@ -279,14 +279,14 @@ router_topk_kernel(const float* __restrict__ logits, int64_t tokens, int experts
   softmax_topk_warp<kEpl>(val, lane, t, experts, top_k, norm, probs, topk_w, topk_idx);
 }
 
-// One launch for a verify pass of at most kTokTile tokens: a cluster of
-// ceil(E / 8) CTAs (at most 16) of 16 warps.  Each CTA stages the tokens and
-// 8 router rows in shared memory; warp w computes the logits of router row
-// w % 8 for tokens 4 (w / 8) .. 4 (w / 8) + 3, each (token, expert) sum in
-// exactly the lane assignment and order of router_logits_staged, so the
-// logits are the same bits.  CTA 0 then reads every logit of its token rows
-// through distributed shared memory and runs the softmax / top-k of
-// router_topk_kernel.
+// One launch: a cluster of ceil(E / 8) CTAs (at most 16) of 16 warps per
+// tile of kTokTile tokens (grid.x = token tiles).  Each CTA stages its tile's
+// tokens and 8 router rows in shared memory; warp w computes the logits of
+// router row w % 8 for tokens 4 (w / 8) .. 4 (w / 8) + 3, each (token,
+// expert) sum in exactly the lane assignment and order of
+// router_logits_staged, so the logits are the same bits.  CTA 0 of the
+// cluster then reads every logit of the tile's tokens through distributed
+// shared memory and runs the softmax / top-k of router_topk_kernel.
 constexpr int kFusedET = 8;
 constexpr int kFusedGroups = 2;                       // token groups per router row
 constexpr int kFusedTok = kTokTile / kFusedGroups;    // tokens per warp
@@ -303,14 +303,16 @@ router_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, int tokens
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ float lg[kTokTile][kFusedET];
-  T* xs = reinterpret_cast<T*>(smem_raw);        // [tokens][hidden]
-  T* ws = xs + (size_t)tokens * hidden;           // [kFusedET][hidden]
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int ntok = tokens;
+  const int tb = blockIdx.x * kTokTile;  // first token of this cluster's tile
+  const int ntok = min(kTokTile, tokens - tb);
+  x += (int64_t)tb * hidden;
+  T* xs = reinterpret_cast<T*>(smem_raw);        // [ntok][hidden]
+  T* ws = xs + (size_t)ntok * hidden;             // [kFusedET][hidden]
   const int e0 = crank * kFusedET;
   const int nexp = max(0, min(kFusedET, experts - e0));
   const int vec_per_row = hidden * (int)sizeof(T) / 16;
@@ -361,7 +363,7 @@ router_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, int tokens
       if (lane == 0 && t0 + i < ntok) {
         const float r = round_logit(sum, (T*)nullptr);
         lg[t0 + i][ej] = r;
-        if (logits_out) logits_out[(int64_t)(t0 + i) * experts + e0 + ej] = from_f32<T>(r);
+        if (logits_out) logits_out[(int64_t)(tb + t0 + i) * experts + e0 + ej] = from_f32<T>(r);
       }
     }
   }
@@ -374,7 +376,7 @@ router_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, int tokens
       val[j] = e < experts ? *cluster.map_shared_rank(&lg[warp][e % kFusedET], e / kFusedET)
                            : -INFINITY;
     }
-    softmax_topk_warp<kEpl>(val, lane, warp, experts, top_k, norm, probs, topk_w, topk_idx);
+    softmax_topk_warp<kEpl>(val, lane, (int64_t)tb + warp, experts, top_k, norm, probs, topk_w, topk_idx);
   }
   cluster.sync();  // peers keep their shared memory until CTA 0 has read it
 }
@@ -402,7 +404,8 @@ int launch_fused_epl(const T* x, const T* w, int tokens, int H, int E, int K, in
       }))
     return rc;
   const unsigned cluster = (unsigned)((E + kFusedET - 1) / kFusedET);  // <= kFusedMaxCluster
-  SF_CHECK_CUDA(launch_pdl_cluster(router_fused_kernel<T, Acc, kEpl>, dim3(1, cluster, 1),
+  const unsigned tiles = (unsigned)((tokens + kTokTile - 1) / kTokTile);
+  SF_CHECK_CUDA(launch_pdl_cluster(router_fused_kernel<T, Acc, kEpl>, dim3(tiles, cluster, 1),
                                    dim3(kFusedWarps * 32), smem, stream, 1u, cluster, x, w, tokens,
                                    H, E, K, norm, probs, topk_w, topk_idx, logits_out));
   return SF_OK;
@@ -469,7 +472,10 @@ int launch_router(const void* hidden, const void* weight, int64_t tokens, int H,
   const T* w = static_cast<const T*>(weight);
   dim3 grid((unsigned)((tokens + kTokTile - 1) / kTokTile), (unsigned)((E + kExpTile - 1) / kExpTile));
   const bool vec = (H % 8 == 0) && aligned16(x) && aligned16(w);
-  const size_t fused_smem = (size_t)(tokens + kFusedET) * H * sizeof(T);
+  const size_t fused_smem = (size_t)((tokens < kTokTile ? tokens : kTokTile) + kFusedET) * H * sizeof(T);
+  // The cluster launch pays off only for a handful of tokens: at 65 and 512
+  // rows it measured slower on a B200 than the two launches below (15.4 vs
+  // 14.0 us and 56.7 vs 46.3 us inside a graph).
   if (std::is_same<T, __nv_bfloat16>::value && vec && tokens <= kTokTile &&
       E <= kFusedET * kFusedMaxCluster && fused_smem <= 200 * 1024 &&
       fused_clusters_ok<T, Acc>((E + kFusedET - 1) / kFusedET, fused_smem))

@@ -399,7 +399,8 @@ int tma_encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64
                 const cuuint64_t* strides_bytes, const cuuint32_t* box) {
   auto fn = encode_fn();
   if (!fn) return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint32_t elem_strides[3] = {1, 1, 1};
+  if (rank < 1 || rank > 5) return set_error(SF_ERR_INVALID_ARGUMENT, "tensor map rank %d", rank);
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};  // rank <= 5
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
                   strides_bytes, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -191,11 +191,13 @@ __global__ void tree_attn_merge_kernel(Params p, __nv_bfloat16* __restrict__ out
   pdl_trigger();
   const int64_t pair = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (pair >= (int64_t)p.num_heads * p.q_len) return;
-  const int head = (int)(pair / p.q_len);
+  const int64_t per_req = (int64_t)p.num_heads * p.q_len;  // also the stride between splits
+  if (pair >= per_req * p.batch) return;
+  const int req = (int)(pair / per_req);
+  const int head = (int)((pair % per_req) / p.q_len);
   const int row = (int)(pair % p.q_len);
-  const int64_t stride = (int64_t)p.num_heads * p.q_len;  // between splits
-  const int64_t base = (int64_t)head * p.q_len + row;
+  const int64_t stride = per_req;
+  const int64_t base = (int64_t)req * p.splits * per_req + (int64_t)head * p.q_len + row;
   // Lanes read the splits' (max, sum) pairs in parallel (split lane + 32 k).
   float gm = -INFINITY;
   for (int s = lane; s < p.splits; s += 32) gm = fmaxf(gm, p.part_ml[(base + s * stride) * 2]);
@@ -243,7 +245,7 @@ __global__ void tree_attn_merge_kernel(Params p, __nv_bfloat16* __restrict__ out
   }
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (lane * 4 >= p.head_dim) return;
-  __nv_bfloat16* dst = out + ((int64_t)row * p.num_heads + head) * p.head_dim + lane * 4;
+  __nv_bfloat16* dst = out + (int64_t)req * p.out_bs + ((int64_t)row * p.num_heads + head) * p.head_dim + lane * 4;
   __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
   __nv_bfloat162 hi = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
   uint2 packed;
@@ -368,6 +370,76 @@ extern "C" int sf_tree_attention_ex(const void* q, const void* k, const void* v,
   SF_CHECK_LAUNCH();
   SF_CHECK_CUDA(launch_pdl(tree_attn_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0,
                            s, p, static_cast<__nv_bfloat16*>(out)));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}
+
+extern "C" size_t sf_tree_attention_batched_workspace_bytes(int batch, int num_heads, int64_t q_len,
+                                                           int64_t kv_len) {
+  if (batch <= 0) return 0;
+  return (size_t)batch * sf_tree_attention_workspace_bytes(num_heads, q_len, kv_len);
+}
+
+extern "C" int sf_tree_attention_batched(const void* q, const void* k, const void* v,
+                                         const uint32_t* tree_bits, int bit_words, int batch,
+                                         int64_t q_batch_stride, int64_t kv_batch_stride,
+                                         int64_t bits_batch_stride, int64_t out_batch_stride,
+                                         int64_t q_len, int64_t kv_len, int64_t prefix_len, int num_heads,
+                                         int num_kv_heads, int head_dim, int64_t q_head_stride,
+                                         int64_t q_row_stride, int64_t kv_head_stride,
+                                         int64_t kv_row_stride, float scale, void* out, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  using namespace sf;
+  SF_CHECK_ARG(batch > 0 && batch < 65536, "batch must be in [1, 65535]");
+  SF_CHECK_ARG(num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+                   num_heads / num_kv_heads <= kMaxGroup,
+               "num_heads must be a multiple of num_kv_heads, at most 8 per KV head");
+  SF_CHECK_ARG(q_len >= 0 && kv_len >= 0 && prefix_len >= 0 && prefix_len <= kv_len &&
+                   q_len < (1 << 30) && kv_len < (1 << 30),
+               "invalid lengths");
+  if (q_len == 0) return SF_OK;
+  SF_CHECK_ARG(q && k && v && out && workspace, "null pointer argument");
+  SF_CHECK_ARG(kv_len == prefix_len || (tree_bits && (int64_t)bit_words * 32 >= kv_len - prefix_len),
+               "tree_bits must cover kv_len - prefix_len columns");
+  SF_CHECK_ARG(q_batch_stride >= 0 && kv_batch_stride >= 0 && bits_batch_stride >= 0 && out_batch_stride >= 0,
+               "batch strides must be non-negative");
+  if (workspace_bytes < sf_tree_attention_batched_workspace_bytes(batch, num_heads, q_len, kv_len))
+    return set_error(SF_ERR_WORKSPACE, "batched tree attention workspace needs %zu bytes",
+                     sf_tree_attention_batched_workspace_bytes(batch, num_heads, q_len, kv_len));
+  Params p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.bits = tree_bits;
+  p.bit_words = bit_words;
+  p.q_len = (int)q_len;
+  p.kv_len = (int)kv_len;
+  p.prefix_len = (int)prefix_len;
+  p.num_heads = num_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.group = num_heads / num_kv_heads;
+  p.head_dim = head_dim;
+  p.q_hs = q_head_stride;
+  p.q_rs = q_row_stride;
+  p.kv_hs = kv_head_stride;
+  p.kv_rs = kv_row_stride;
+  p.scale = scale;
+  p.part_o = static_cast<float*>(workspace);
+  p.batch = batch;
+  p.q_bs = q_batch_stride;
+  p.kv_bs = kv_batch_stride;
+  p.bits_bs = bits_batch_stride;
+  p.out_bs = out_batch_stride;
+  if (!tree_attention_tc_supports(p, head_dim) || kv_batch_stride % 8 != 0 || q_batch_stride % 8 != 0 ||
+      out_batch_stride % 8 != 0)
+    return SF_ERR_UNSUPPORTED;  // no message: callers run one request per call
+  cudaStream_t s = as_stream(stream);
+  bool merged = false;
+  if (int rc = tree_attention_tc(p, out, &merged, s)) return rc;
+  if (merged) return SF_OK;
+  const int64_t pairs = (int64_t)batch * num_heads * q_len;
+  SF_CHECK_CUDA(launch_pdl(tree_attn_merge_kernel, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0, s, p,
+                           static_cast<__nv_bfloat16*>(out)));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }

@@ -20,8 +20,13 @@ struct AttnParams {
   int64_t q_hs, q_rs, kv_hs, kv_rs;
   float scale;
   int splits, keys_per_split;
-  float* part_o;   // [splits, Hq, Tq, D] unnormalised outputs
-  float* part_ml;  // [splits, Hq, Tq, 2] (row max of scaled scores, row sum)
+  float* part_o;   // [batch, splits, Hq, Tq, D] unnormalised outputs
+  float* part_ml;  // [batch, splits, Hq, Tq, 2] (row max of scaled scores, row sum)
+  // Requests in one launch (the tcgen05 kernel and the merge; 1 elsewhere):
+  // request b's q, k/v, tree bits and output start b * (q_bs, kv_bs,
+  // bits_bs, out_bs) elements (words for the bits) after request 0's.
+  int batch = 1;
+  int64_t q_bs = 0, kv_bs = 0, bits_bs = 0, out_bs = 0;
 };
 
 // Visibility of keys prefix_len + j0 + i, i in [0, 64), as bit i, from a

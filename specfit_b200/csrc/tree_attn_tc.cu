@@ -17,10 +17,14 @@
 //                 S = Q K^T    (M 128, N 128 keys, K 128 d; Q and K K-major)
 //                 O_j = P V    (M 128, N 128 d, K 128 keys; P K-major, V
 //                               MN-major: V rows are keys with d contiguous);
-//   warps 2..5  one packed row per thread (the TMEM lane): Q row -> shared
-//               memory; per block, S row from TMEM, tree mask, online
-//               softmax in fp32, P row (bf16) -> shared memory; then
-//               O = O * exp(m_old - m_new) + O_j in registers.
+//   warps 2..9  two threads per packed row (the TMEM lane; warps w and
+//               w + 4 share a lane quadrant), each owning half of the row's
+//               key columns and half of its output dims: Q half-row ->
+//               shared memory; per block, S half-row from TMEM, tree mask,
+//               online softmax in fp32 (the two halves' row max and row sum
+//               exchanged through shared memory, the sum added in half
+//               order), P half-row (bf16) -> shared memory; then
+//               O = O * exp(m_old - m_new) + O_j over its 64 dims in registers.
 // TMEM: S in columns [0, 128), O_j in [128, 256).  The order of the waits
 // (S_j consumed before P_j is published; O_j consumed before P_{j+1} is
 // published) lets both live in one buffer each.
@@ -50,7 +54,7 @@ constexpr int kD = 128;
 constexpr int kBM = 128;                       // packed query rows per CTA (MMA M)
 constexpr int kKB = 128;                       // keys per block
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;                  // 2 + 8 warps
 constexpr int kMaxSplits = 32;                 // the workspace of sf_tree_attention covers 32
 constexpr int kRegion = 128 * 128;             // one 64-element column region of a 128-row tile (B)
 constexpr int kQBytes = 2 * kRegion;           // Q: 128 rows x 128 d
@@ -70,6 +74,9 @@ struct __align__(8) Tail {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
+  float red_max[2][kBM];  // per half: the half-row's max of visible scaled scores
+  float red_sum[2][kBM];  // per half: the half-row's sum of probabilities
+  int pair_ok[3][2][4];   // per exchange point, half and lane quadrant: the warp's wait succeeded
 };
 
 constexpr size_t kSmemBytes =
@@ -110,7 +117,8 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
   volatile int* abort_flag = &tail->abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = blockIdx.x, tile = blockIdx.y, split = blockIdx.z;
+  const int kvh = blockIdx.x, tile = blockIdx.y;
+  const int req = blockIdx.z / p.splits, split = blockIdx.z % p.splits;  // request, key range
   const int packed_rows = p.group * p.q_len;
   const int key_lo = split * p.keys_per_split;
   const int key_hi = min(p.kv_len, key_lo + p.keys_per_split);
@@ -121,9 +129,9 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       ptx::mbar_init(&tail->kv_full[s], 1);
       ptx::mbar_init(&tail->kv_empty[s], 1);
     }
-    ptx::mbar_init(&tail->q_ready, 128);
+    ptx::mbar_init(&tail->q_ready, 256);
     ptx::mbar_init(&tail->s_full, 1);
-    ptx::mbar_init(&tail->p_full, 128);
+    ptx::mbar_init(&tail->p_full, 256);
     ptx::mbar_init(&tail->o_full, 1);
     ptx::mbar_init(&tail->mma_done, 1);
     tail->abort_flag = 0;
@@ -153,10 +161,10 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         ptx::mbar_arrive_expect_tx(&tail->kv_full[s], kStageBytes);
         uint8_t* st = kv_s + (size_t)s * kStageBytes;
         const int key0 = key_lo + j * kKB;
-        ptx::tma_load_3d(st, &tm_k, &tail->kv_full[s], 0, key0, kvh);
-        ptx::tma_load_3d(st + kRegion, &tm_k, &tail->kv_full[s], 64, key0, kvh);
-        ptx::tma_load_3d(st + kKBytes, &tm_v, &tail->kv_full[s], 0, key0, kvh);
-        ptx::tma_load_3d(st + kKBytes + kRegion, &tm_v, &tail->kv_full[s], 64, key0, kvh);
+        ptx::tma_load_4d(st, &tm_k, &tail->kv_full[s], 0, key0, kvh, req);
+        ptx::tma_load_4d(st + kRegion, &tm_k, &tail->kv_full[s], 64, key0, kvh, req);
+        ptx::tma_load_4d(st + kKBytes, &tm_v, &tail->kv_full[s], 0, key0, kvh, req);
+        ptx::tma_load_4d(st + kKBytes + kRegion, &tm_v, &tail->kv_full[s], 64, key0, kvh, req);
       }
       // Let every load this thread issued land before the CTA can exit.
       volatile int never = 0;
@@ -199,19 +207,29 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       ptx::mbar_wait(&tail->mma_done, 0, &never, &g_attn_tc_status, 6);
     }
   } else {
-    // ---------------- softmax / epilogue (warps 2..5) ----------------
+    // ---------------- softmax / epilogue (warps 2..9) ----------------
     const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;   // 0: keys / dims 0..63 of the row, 1: 64..127
     const int r = quad * 32 + lane;     // tile row == TMEM lane
     const int pr = tile * kBM + r;      // packed row
     const bool rok = pr < packed_rows;
     const int t = rok ? pr % p.q_len : 0;
     const int head = kvh * p.group + (rok ? pr / p.q_len : 0);
+    const uint32_t pair_bar = 1 + quad;  // named barrier of the two warps of this quadrant
+    // Both warps of a quadrant take the same go / stop decision at each
+    // exchange point (a warp that stopped alone would leave its partner
+    // waiting at the named barrier).
+    auto pair_agree = [&](int point, bool mine) -> bool {
+      if (lane == 0) tail->pair_ok[point][half][quad] = mine ? 1 : 0;
+      ptx::named_bar_sync(pair_bar, 64);
+      return tail->pair_ok[point][0][quad] && tail->pair_ok[point][1][quad];
+    };
 
-    // Q row -> shared memory in the swizzled K-major layout (zeros past the rows).
+    // Q half-row -> shared memory in the swizzled K-major layout (zeros past the rows).
     {
-      const __nv_bfloat16* qrow = p.q + (int64_t)head * p.q_hs + (int64_t)t * p.q_rs;
+      const __nv_bfloat16* qrow = p.q + (int64_t)req * p.q_bs + (int64_t)head * p.q_hs + (int64_t)t * p.q_rs;
 #pragma unroll 4
-      for (int c = 0; c < kD / 8; ++c) {
+      for (int c = half * (kD / 16); c < (half + 1) * (kD / 16); ++c) {
         const uint4 v = rok ? *reinterpret_cast<const uint4*>(qrow + c * 8) : make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(q_s + sw128_offset(r, c)) = v;
       }
@@ -220,19 +238,18 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     }
 
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t* rbits = p.bits ? p.bits + (int64_t)t * p.bit_words : nullptr;
-    float o[kD];
+    const uint32_t* rbits = p.bits ? p.bits + (int64_t)req * p.bits_bs + (int64_t)t * p.bit_words : nullptr;
+    constexpr int kHalf = kD / 2;
+    float o[kHalf];
 #pragma unroll
-    for (int i = 0; i < kD; ++i) o[i] = 0.f;
+    for (int i = 0; i < kHalf; ++i) o[i] = 0.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nblocks; ++j) {
-      const int key0 = key_lo + j * kKB;
-      // Visibility of the block's 128 keys for this row, two 64-bit windows.
-      uint64_t win[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int kb = key0 + 64 * h;
+      // Visibility of this half's 64 keys of the block for this row.
+      uint64_t win;
+      {
+        const int kb = key_lo + j * kKB + 64 * half;
         uint64_t w;
         if (rbits) {
           w = tree_mask_window(rbits, p.bit_words, kb - p.prefix_len);
@@ -242,34 +259,40 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         }
         const int valid = key_hi - kb;  // keys of this window inside the split
         if (valid < 64) w &= valid <= 0 ? 0ull : ((1ull << valid) - 1);
-        win[h] = rok ? w : 0ull;
+        win = rok ? w : 0ull;
       }
 
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(&tail->s_full, j & 1, abort_flag, &g_attn_tc_status, 7));
-      if (!ok) break;
-      ptx::tc_fence_after();
+      if (ok) ptx::tc_fence_after();
 
-      // Pass 1: row max of the visible scaled scores.
+      // Pass 1: the half-row max of the visible scaled scores, then the row's.
       float mx = -INFINITY;
+      if (ok) {
 #pragma unroll 1
-      for (int c = 0; c < kKB / 16; ++c) {
-        float sv[16];
-        ptx::tmem_ld_16(trow + kSCol + c * 16, sv);
-        const uint32_t bits16 = (uint32_t)(win[c >> 2] >> ((c & 3) * 16)) & 0xFFFFu;
+        for (int c = 0; c < 4; ++c) {
+          float sv[16];
+          ptx::tmem_ld_16(trow + kSCol + half * 64 + c * 16, sv);
+          const uint32_t bits16 = (uint32_t)(win >> (c * 16)) & 0xFFFFu;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if ((bits16 >> i) & 1u) mx = fmaxf(mx, sv[i] * p.scale);
+          for (int i = 0; i < 16; ++i)
+            if ((bits16 >> i) & 1u) mx = fmaxf(mx, sv[i] * p.scale);
+        }
       }
-      const float mnew = fmaxf(m, mx);
+      tail->red_max[half][r] = mx;
+      if (!pair_agree(0, ok)) {
+        ok = false;
+        break;
+      }
+      const float mnew = fmaxf(m, fmaxf(tail->red_max[0][r], tail->red_max[1][r]));
       const float alpha = (m == -INFINITY) ? 0.f : __expf(m - mnew);
 
-      // Pass 2: probabilities, their fp32 row sum, and the bf16 P row.
+      // Pass 2: probabilities, their fp32 half-row sum, and the bf16 P half-row.
       float sum = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kKB / 16; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float sv[16];
-        ptx::tmem_ld_16(trow + kSCol + c * 16, sv);
-        const uint32_t bits16 = (uint32_t)(win[c >> 2] >> ((c & 3) * 16)) & 0xFFFFu;
+        ptx::tmem_ld_16(trow + kSCol + half * 64 + c * 16, sv);
+        const uint32_t bits16 = (uint32_t)(win >> (c * 16)) & 0xFFFFu;
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
@@ -278,22 +301,28 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           sum += p0 + p1;
           pk[i / 2] = pack_bf16x2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, 2 * c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, 2 * c + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        const int cc = half * 8 + 2 * c;  // 16-byte chunk of the P row
+        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, cc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(p_s + sw128_offset(r, cc + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
-      l = l * alpha + sum;
-      m = mnew;
+      tail->red_sum[half][r] = sum;
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tail->p_full);
+      ptx::named_bar_sync(pair_bar, 64);  // both halves' sums are in shared memory
+      l = l * alpha + (tail->red_sum[0][r] + tail->red_sum[1][r]);
+      m = mnew;
 
       ok = __all_sync(0xffffffffu, ptx::mbar_wait(&tail->o_full, j & 1, abort_flag, &g_attn_tc_status, 8));
-      if (!ok) break;
+      if (!pair_agree(1, ok)) {
+        ok = false;
+        break;
+      }
       ptx::tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kD / 16; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float ov[16];
-        ptx::tmem_ld_16(trow + kOCol + c * 16, ov);
+        ptx::tmem_ld_16(trow + kOCol + half * 64 + c * 16, ov);
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[c * 16 + i] = o[c * 16 + i] * alpha + ov[i];
       }
@@ -303,9 +332,9 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
     if (ok && rok) {
       if (direct) {
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        __nv_bfloat16* dst = out + ((int64_t)t * p.num_heads + head) * kD;
+        __nv_bfloat16* dst = out + (int64_t)req * p.out_bs + ((int64_t)t * p.num_heads + head) * kD + half * kHalf;
 #pragma unroll
-        for (int c = 0; c < kD / 8; ++c) {
+        for (int c = 0; c < kHalf / 8; ++c) {
           uint4 v;
           v.x = pack_bf16x2(o[c * 8 + 0] * inv, o[c * 8 + 1] * inv);
           v.y = pack_bf16x2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
@@ -314,13 +343,15 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
           *reinterpret_cast<uint4*>(dst + c * 8) = v;
         }
       } else {
-        const int64_t idx = ((int64_t)split * p.num_heads + head) * p.q_len + t;
-        float* dst = p.part_o + idx * kD;
+        const int64_t idx = (((int64_t)req * p.splits + split) * p.num_heads + head) * p.q_len + t;
+        float* dst = p.part_o + idx * kD + half * kHalf;
 #pragma unroll
-        for (int c = 0; c < kD / 4; ++c)
+        for (int c = 0; c < kHalf / 4; ++c)
           *reinterpret_cast<float4*>(dst + c * 4) = make_float4(o[c * 4], o[c * 4 + 1], o[c * 4 + 2], o[c * 4 + 3]);
-        p.part_ml[idx * 2] = m;
-        p.part_ml[idx * 2 + 1] = l;
+        if (half == 0) {
+          p.part_ml[idx * 2] = m;
+          p.part_ml[idx * 2 + 1] = l;
+        }
       }
     }
   }
@@ -362,22 +393,41 @@ int tree_attention_tc(AttnParams& p, void* out, bool* merged, cudaStream_t strea
 
   CUtensorMap tm_k, tm_v;
   {
-    cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)p.kv_len, (cuuint64_t)p.num_kv_heads};
-    cuuint64_t strides[2] = {(cuuint64_t)p.kv_rs * 2, (cuuint64_t)p.kv_hs * 2};
-    cuuint32_t box[3] = {64, kKB, 1};
-    if (int rc = tma_encode_bf16(&tm_k, p.k, 3, dims, strides, box)) return rc;
-    if (int rc = tma_encode_bf16(&tm_v, p.v, 3, dims, strides, box)) return rc;
+    // [batch][kv heads][keys][d]: a request is one more coordinate.
+    const int64_t kv_bs = p.batch > 1 ? p.kv_bs : (int64_t)p.num_kv_heads * p.kv_hs;
+    cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)p.kv_len, (cuuint64_t)p.num_kv_heads,
+                          (cuuint64_t)p.batch};
+    cuuint64_t strides[3] = {(cuuint64_t)p.kv_rs * 2, (cuuint64_t)p.kv_hs * 2, (cuuint64_t)kv_bs * 2};
+    cuuint32_t box[4] = {64, kKB, 1, 1};
+    if (int rc = tma_encode_bf16(&tm_k, p.k, 4, dims, strides, box)) return rc;
+    if (int rc = tma_encode_bf16(&tm_v, p.v, 4, dims, strides, box)) return rc;
   }
   const int64_t row_tiles = ((int64_t)p.group * p.q_len + kBM - 1) / kBM;
   const int64_t blocks = ((int64_t)p.kv_len + kKB - 1) / kKB;
-  int64_t want = ((int64_t)num_sms() + p.num_kv_heads * row_tiles - 1) / (p.num_kv_heads * row_tiles);
-  want = std::max<int64_t>(1, std::min<int64_t>(want, std::min<int64_t>(blocks, kMaxSplits)));
-  p.keys_per_split = (int)(((blocks + want - 1) / want) * kKB);
+  // Splits of the key range: the count that minimises (waves of CTAs) x
+  // (key blocks per CTA + a CTA's fixed cost, about two blocks: set-up, the
+  // Q tile, pipeline fill, the partial write), plus a small charge per split
+  // for the merge.
+  const int64_t units = (int64_t)p.batch * p.num_kv_heads * row_tiles;
+  const int64_t sms = num_sms();
+  int64_t best = 1;
+  double best_cost = 1e30;
+  for (int64_t s = 1; s <= std::min<int64_t>(blocks, kMaxSplits); ++s) {
+    const int64_t per = (blocks + s - 1) / s;
+    const int64_t used = (blocks + per - 1) / per;  // splits that get keys
+    const double cost = (double)((units * used + sms - 1) / sms) * ((double)per + 2.0) + 0.05 * (double)used;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  p.keys_per_split = (int)(((blocks + best - 1) / best) * kKB);
   p.splits = (int)((p.kv_len + p.keys_per_split - 1) / p.keys_per_split);
-  p.part_ml = p.part_o + (size_t)p.splits * p.num_heads * p.q_len * kD;
+  p.part_ml = p.part_o + (size_t)p.batch * p.splits * p.num_heads * p.q_len * kD;
   const int direct = p.splits == 1 ? 1 : 0;
   SF_CHECK_ARG(row_tiles < 65536, "too many query rows");
-  dim3 grid((unsigned)p.num_kv_heads, (unsigned)row_tiles, (unsigned)p.splits);
+  SF_CHECK_ARG((int64_t)p.splits * p.batch < 65536, "too many requests for one launch");
+  dim3 grid((unsigned)p.num_kv_heads, (unsigned)row_tiles, (unsigned)(p.splits * p.batch));
   SF_CHECK_CUDA(launch_pdl(tree_attn_tc_kernel, grid, dim3(kThreads), kSmemBytes, stream, tm_k, tm_v, p,
                            static_cast<__nv_bfloat16*>(out), direct));
   SF_CHECK_LAUNCH();

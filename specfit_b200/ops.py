@@ -323,6 +323,41 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits:
     return res
 
 
+
+def tree_attention_batched(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tree_bits: torch.Tensor | None,
+                           prefix_len: int, scale: float | None = None,
+                           out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """``tree_attention`` of B requests in one launch of the tcgen05 kernel:
+    ``q[B, Hq, Tq, D]``, ``k/v[B, Hkv, Tk, D]`` (any batch and head strides,
+    unit stride on D), ``tree_bits[B, Tq, words]`` or None; returns
+    ``[B, Tq, Hq, D]`` bf16, or None where that kernel does not take the
+    layout (the caller then runs ``tree_attention`` per request)."""
+    dev = _require_cuda(q, k, v)
+    b, hq, tq, dim = q.shape
+    _, hkv, tk, _ = k.shape
+    if q.stride(3) != 1 or k.stride(3) != 1 or v.stride(3) != 1 or k.stride() != v.stride():
+        return None
+    res = out if out is not None else torch.empty(b, tq, hq, dim, dtype=q.dtype, device=dev)
+    if res.stride(3) != 1 or res.stride(2) != dim or res.stride(1) != hq * dim:
+        return None
+    if tree_bits is not None:
+        bits = tree_bits if tree_bits.is_contiguous() else tree_bits.contiguous()
+        words, bits_bs = bits.shape[2], bits.stride(0)
+    else:
+        bits, words, bits_bs = None, 0, 0
+    ws_bytes = N.lib.sf_tree_attention_batched_workspace_bytes(b, hq, tq, tk)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    sc = float(dim ** -0.5 if scale is None else scale)
+    rc = N.lib.sf_tree_attention_batched(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(bits), words, b,
+                                         q.stride(0), k.stride(0), bits_bs, res.stride(0), tq, tk, prefix_len,
+                                         hq, hkv, dim, q.stride(1), q.stride(2), k.stride(1), k.stride(2), sc,
+                                         res.data_ptr(), ws.data_ptr(), ws_bytes, _stream(dev))
+    if rc == N.SF_ERR_UNSUPPORTED:
+        return None
+    N.check(rc, "sf_tree_attention_batched")
+    _launched(2)
+    return res
+
 def tree_mask_words(ancestor_sets: torch.Tensor, start: torch.Tensor, words: int,
                     out: torch.Tensor | None = None) -> torch.Tensor:
     """Visibility words over a whole KV buffer for ``tree_attention`` with

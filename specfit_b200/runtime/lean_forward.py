@@ -45,6 +45,13 @@ from .tree_attention import _causal_bits, _packed_bits
 
 
 class LeanQwen3Forward:
+    # Several requests' attention runs as one tcgen05 launch where a single
+    # request would take that kernel too (sf_tree_attention's AUTO rule):
+    # at least 256 packed query rows (query heads per KV head x rows) over
+    # at least 2,048 keys.
+    BATCHED_ATTENTION_MIN_KEYS = 2048
+    BATCHED_ATTENTION_MIN_ROWS = 256
+
     def __init__(self, model, fused_head: bool = True) -> None:
         cfg = model.config
         self.model = model
@@ -118,6 +125,7 @@ class LeanQwen3Forward:
         hn = torch.empty_like(x)
         self._norm(x, None, res, self.layers[0].ln_in, hn, stream)
         static = cache.layers[0].static_offset is not None
+        stacked_bits = None  # (kv_len, [B, T, words]) built once per pass for the batched attention
         for li, L in enumerate(self.layers):
             layer = L.layer
             for hook in tuple(layer.self_attn._forward_pre_hooks.values()):
@@ -159,9 +167,18 @@ class LeanQwen3Forward:
                 bits = _packed_bits(attention_mask, T, kv_len, B)
                 prefix = 0
             attn = torch.empty(B, T, self.hq, self.D, dtype=x.dtype, device=dev)
-            for b in range(B):
-                ops.tree_attention(q[b], cl._kbuf[b, :, :kv_len], cl._vbuf[b, :, :kv_len], bits[b],
-                                   prefix, scale=self.D ** -0.5, out=attn[b])
+            done = None
+            if (B > 1 and kv_len >= self.BATCHED_ATTENTION_MIN_KEYS
+                    and (self.hq // self.hkv) * T >= self.BATCHED_ATTENTION_MIN_ROWS):
+                # Several requests: one launch of the tcgen05 kernel over all of them.
+                if stacked_bits is None or stacked_bits[0] != kv_len:
+                    stacked_bits = (kv_len, torch.stack([bb.reshape(T, -1) for bb in bits]))
+                done = ops.tree_attention_batched(q, cl._kbuf[:, :, :kv_len], cl._vbuf[:, :, :kv_len],
+                                                  stacked_bits[1], prefix, scale=self.D ** -0.5, out=attn)
+            if done is None:
+                for b in range(B):
+                    ops.tree_attention(q[b], cl._kbuf[b, :, :kv_len], cl._vbuf[b, :, :kv_len], bits[b],
+                                       prefix, scale=self.D ** -0.5, out=attn[b])
             o = ops.linear(attn.view(Nt, self.hq * self.D), L.wo)
             self._norm(o, res, res, L.ln_post, hn, stream)
             nxt = self.layers[li + 1].ln_in if li + 1 < len(self.layers) else self.final

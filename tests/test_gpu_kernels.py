@@ -462,6 +462,37 @@ def test_tree_attention_strided_views(ops, impl):
     assert np.abs(out.float().cpu().numpy().transpose(1, 0, 2) - ref).max() <= ATOL_BF16
 
 
+@pytest.mark.parametrize("batch,nodes,ctx,cache", [(8, 64, 4096, 4200), (3, 64, 2048, 2200), (2, 40, 3000, 3041)])
+def test_batched_tree_attention_vs_oracle(ops, batch, nodes, ctx, cache):
+    """Several requests' attention in one tcgen05 launch, with q, K/V cache
+    and output laid out as the lean forward holds them ([B, Hq, T, D],
+    [B, Hkv, capacity, D] read up to kv_len, [B, T, Hq, D]) and a different
+    tree per request: every request equals the fp64 oracle on its own tree,
+    and the single-request call within bf16 rounding."""
+    gen = torch.Generator().manual_seed(batch * 100 + nodes)
+    trees = [synthetic.random_tree(nodes, max_depth=6, max_branch=4, seed=nodes + b)[1] for b in range(batch)]
+    tq = 1 + nodes
+    tk = ctx + tq
+    q = torch.randn(batch, 32, tq, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    kc = torch.randn(batch, 4, cache, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    vc = torch.randn(batch, 4, cache, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    bits = torch.stack([ops.tree_bits_from_parents(t, DEV) for t in trees])
+    out = ops.tree_attention_batched(q, kc[:, :, :tk], vc[:, :, :tk], bits, ctx)
+    assert out is not None and out.shape == (batch, tq, 32, 128)
+    for b in range(batch):
+        mask = to.verification_attention_mask(trees[b], ctx)
+        ref = to.tree_attention(q[b].float().cpu().numpy(), kc[b, :, :tk].float().cpu().numpy(),
+                                vc[b, :, :tk].float().cpu().numpy(), mask)
+        got = out[b].float().cpu().numpy().transpose(1, 0, 2)
+        assert np.abs(got - ref).max() <= ATOL_BF16, b
+        assert cosine(got, ref) >= COS_MIN
+        one = ops.tree_attention(q[b], kc[b, :, :tk], vc[b, :, :tk], bits[b], ctx, impl=3)  # tcgen05
+        assert (one.float() - out[b].float()).abs().max().item() <= ATOL_BF16
+    from specfit_b200 import _native as N
+
+    assert N.device_status(reset=True) == 0
+
+
 def test_tree_attention_full_mask_and_long_context(ops):
     """Arbitrary boolean mask packed over every key (prefix_len 0), a
     4161-key context, 8 query heads per KV head, against the fp64 oracle."""
