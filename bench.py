@@ -116,6 +116,8 @@ def parse_args(argv=None):
                    help="resident expert path: token rows read inside the grouped SwiGLU (TMA gather4)")
     p.add_argument("--kernel", default="",
                    help="--mode kernels: comma-separated kernel names to run (default: all)")
+    p.add_argument("--kernel-rows", default="7,65,512",
+                   help="--mode kernels: the row counts of the per-token cases (router ... grouped_swiglu)")
     return p.parse_args(argv)
 
 
@@ -1831,7 +1833,7 @@ def sweep_mode(args):
     print(json.dumps(result), flush=True)
 
 
-def kernel_cases(device, only=()):
+def kernel_cases(device, only=(), rows=(7, 65, 512)):
     """(name, case, launch, algorithmic bytes) for every hot kernel at the
     sizes the configurations run it at: 7 rows (a decode verify pass), 65
     (configuration 2), 512 (configuration 5's step); bf16 inputs drawn on the
@@ -1856,7 +1858,7 @@ def kernel_cases(device, only=()):
     if want("grouped_swiglu") or "grouped_swiglu_gathered" in only:
         storage = randn(E, 3 * H * I, std=0.02)
         slot = torch.arange(E, dtype=torch.int32, device=device)
-    for t in (7, 65, 512):
+    for t in rows:
         x = randn(t, H)
         idx = torch.from_numpy(synthetic.zipf_routes(t, layer=0, seed=3)).to(device)
         w = torch.softmax(torch.randn(t, K, generator=g, device=device), -1)
@@ -2008,7 +2010,7 @@ def kernels_mode(args):
     device = torch.device("cuda", 0)
     peaks = measured_peaks()
     only = tuple(k for k in args.kernel.split(",") if k)
-    cases = kernel_cases(device, only)
+    cases = kernel_cases(device, only, tuple(int(r) for r in args.kernel_rows.split(",") if r))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     iters = max(args.steps, 3)

@@ -49,6 +49,8 @@ constexpr int kStages = 6;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kBBytes = kBN * kBK * 2;
 constexpr int kBBox = 16;      // token rows per B TMA box
+constexpr int kBWide = 64;     // token rows per wide B box (passes of more than kWideMin rows)
+constexpr int kWideMin = 48;
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 2 * kBN;
 constexpr int kUpPitch = 17;   // padded row pitch of the gate/up exchange buffer
@@ -157,7 +159,7 @@ __device__ __forceinline__ void for_each_unit(const SmemTail* tail, int m_tiles,
 template <int kPhase, bool kGather = false>
 __global__ void __launch_bounds__(kThreads, 1)
 swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                 const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                 const __grid_constant__ CUtensorMap tm_xw, const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                  const int32_t* __restrict__ num_active, const int32_t* __restrict__ expert_slot,
                  const float* __restrict__ w_sorted, int H, int I,
                  __nv_bfloat16* __restrict__ out, const int32_t* __restrict__ sorted_pos = nullptr,
@@ -214,7 +216,12 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       uint32_t it = 0;
       for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
         const int nb = (u.npass + kBBox - 1) / kBBox;
-        const uint32_t bytes = kABytes + nb * kBBox * kBK * 2;
+        // A pass of many rows takes its token rows in one or two wide boxes
+        // (fewer TMA requests per stage); rows past the pass are loaded but
+        // never stored.
+        const bool wide = !kGather && u.npass > kWideMin;
+        const int nw = (u.npass + kBWide - 1) / kBWide;
+        const uint32_t bytes = kABytes + (wide ? nw * kBWide : nb * kBBox) * kBK * 2;
         if constexpr (kGather && kPhase == 1) {
           // Token rows of this pass; rows past it read token 0 (their
           // products are never stored).
@@ -241,6 +248,10 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
               const int* t = &tail->rowtok[g * 4];
               ptx::tma_gather4(b + g * 4 * kBK * 2, &tm_x, &tail->full[s], kb * kBK, t[0], t[1], t[2], t[3]);
             }
+          } else if (wide) {
+            for (int q = 0; q < nw; ++q)
+              ptx::tma_load_2d(b + q * kBWide * kBK * 2, &tm_xw, &tail->full[s], kb * kBK,
+                               u.n0 + q * kBWide);
           } else {
             for (int q = 0; q < nb; ++q)
               ptx::tma_load_2d(b + q * kBBox * kBK * 2, &tm_x, &tail->full[s], kb * kBK,
@@ -444,7 +455,7 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
   const int H = a.hidden, I = a.inter;
   const uint64_t slot_bytes = (uint64_t)a.slot_stride * 2;
   const __nv_bfloat16* storage = static_cast<const __nv_bfloat16*>(a.slot_storage);
-  CUtensorMap tm_w1, tm_x1, tm_w2, tm_x2;
+  CUtensorMap tm_w1, tm_x1, tm_w2, tm_x2, tm_x1w, tm_x2w;
   {
     cuuint64_t dims[3] = {(cuuint64_t)H, (cuuint64_t)(2 * I), (cuuint64_t)a.slot_count};
     cuuint64_t strides[2] = {(cuuint64_t)H * 2, slot_bytes};
@@ -457,6 +468,8 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
     cuuint64_t strides[1] = {(cuuint64_t)H * 2};
     cuuint32_t box[2] = {kBK, gather ? 1u : (cuuint32_t)kBBox};  // gather4 boxes are one row high
     if (int rc = tma_encode_bf16(&tm_x1, a.hidden_sorted, 2, dims, strides, box)) return rc;
+    box[1] = gather ? 1u : (cuuint32_t)kBWide;
+    if (int rc = tma_encode_bf16(&tm_x1w, a.hidden_sorted, 2, dims, strides, box)) return rc;
   }
   {
     cuuint64_t dims[3] = {(cuuint64_t)I, (cuuint64_t)H, (cuuint64_t)a.slot_count};
@@ -469,18 +482,20 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
     cuuint64_t strides[1] = {(cuuint64_t)I * 2};
     cuuint32_t box[2] = {kBK, kBBox};
     if (int rc = tma_encode_bf16(&tm_x2, a.act_workspace, 2, dims, strides, box)) return rc;
+    box[1] = kBWide;
+    if (int rc = tma_encode_bf16(&tm_x2w, a.act_workspace, 2, dims, strides, box)) return rc;
   }
   const int grid = num_sms();
   auto* act = static_cast<__nv_bfloat16*>(a.act_workspace);
   auto* out = static_cast<__nv_bfloat16*>(a.out_sorted);
   if (gather) {
     SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
-                             tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot,
+                             tm_w1, tm_x1, tm_x1w, a.offsets, a.active, a.num_active, a.expert_slot,
                              a.weights_sorted, H, I, act, gather->sorted_pos, gather->top_k,
                              gather->topk_weights));
     SF_CHECK_LAUNCH();
     SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
-                             tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot,
+                             tm_w2, tm_x2, tm_x2w, a.offsets, a.active, a.num_active, a.expert_slot,
                              a.weights_sorted, H, I, out, gather->sorted_pos, gather->top_k,
                              gather->topk_weights));
     SF_CHECK_LAUNCH();
@@ -489,11 +504,11 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
   const int32_t* no_pos = nullptr;
   const float* no_w = nullptr;
   SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
-                           tm_w1, tm_x1, a.offsets, a.active, a.num_active, a.expert_slot,
+                           tm_w1, tm_x1, tm_x1w, a.offsets, a.active, a.num_active, a.expert_slot,
                            a.weights_sorted, H, I, act, no_pos, 1, no_w));
   SF_CHECK_LAUNCH();
   SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
-                           tm_w2, tm_x2, a.offsets, a.active, a.num_active, a.expert_slot,
+                           tm_w2, tm_x2, tm_x2w, a.offsets, a.active, a.num_active, a.expert_slot,
                            a.weights_sorted, H, I, out, no_pos, 1, no_w));
   SF_CHECK_LAUNCH();
   return SF_OK;
