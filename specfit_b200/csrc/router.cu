@@ -145,37 +145,58 @@ router_logits_staged(const T* __restrict__ x, const T* __restrict__ w, int64_t t
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
 
-  for (int ej = warp; ej < nexp; ej += kWarps) {
-    Acc acc[kTokTile];
+  // Warp w computes experts w, w + kWarps, ... of the CTA together (kEW of
+  // them), so each token value is converted once per h-step for all of
+  // them; every (token, expert) sum keeps its own order.
+  constexpr int kEW = (kET + kWarps - 1) / kWarps;
+  Acc acc[kEW][kTokTile];
 #pragma unroll
-    for (int i = 0; i < kTokTile; ++i) acc[i] = Acc(0);
-    const T* wrow = ws + (size_t)ej * hidden;
-    for (int h0 = 8 * lane; h0 < hidden; h0 += 256) {
+  for (int x = 0; x < kEW; ++x)
+#pragma unroll
+    for (int i = 0; i < kTokTile; ++i) acc[x][i] = Acc(0);
+  for (int h0 = 8 * lane; h0 < hidden; h0 += 256) {
+    Acc wf[kEW][8];
+#pragma unroll
+    for (int x = 0; x < kEW; ++x) {
+      const int ej = warp + x * kWarps;
       T wv[8];
+      if (ej < nexp) {
 #pragma unroll
-      for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
-        reinterpret_cast<uint4*>(wv)[q] = reinterpret_cast<const uint4*>(wrow + h0)[q];
+        for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+          reinterpret_cast<uint4*>(wv)[q] = reinterpret_cast<const uint4*>(ws + (size_t)ej * hidden + h0)[q];
+      } else {
 #pragma unroll
-      for (int i = 0; i < kTokTile; ++i) {
-        if (i < ntok) {
-          T xv[8];
+        for (int v = 0; v < 8; ++v) wv[v] = from_f32<T>(0.f);
+      }
 #pragma unroll
-          for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
-            reinterpret_cast<uint4*>(xv)[q] =
-                reinterpret_cast<const uint4*>(xs + (size_t)i * hidden + h0)[q];
+      for (int v = 0; v < 8; ++v) wf[x][v] = (Acc)to_f32(wv[v]);
+    }
 #pragma unroll
-          for (int v = 0; v < 8; ++v)
-            acc[i] = fma((Acc)to_f32(xv[v]), (Acc)to_f32(wv[v]), acc[i]);
+    for (int i = 0; i < kTokTile; ++i) {
+      if (i < ntok) {
+        T xv[8];
+#pragma unroll
+        for (int q = 0; q < (int)(8 * sizeof(T) / 16); ++q)
+          reinterpret_cast<uint4*>(xv)[q] = reinterpret_cast<const uint4*>(xs + (size_t)i * hidden + h0)[q];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const Acc xf = (Acc)to_f32(xv[v]);
+#pragma unroll
+          for (int x = 0; x < kEW; ++x) acc[x][i] = fma(xf, wf[x][v], acc[x][i]);
         }
       }
     }
+  }
+#pragma unroll
+  for (int x = 0; x < kEW; ++x) {
+    const int ej = warp + x * kWarps;
     const int e = e0 + ej;
 #pragma unroll
     for (int i = 0; i < kTokTile; ++i) {
-      Acc s = acc[i];
+      Acc s = acc[x][i];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      if (lane == 0 && i < ntok) {
+      if (lane == 0 && i < ntok && ej < nexp) {
         const float r = round_logit(s, (T*)nullptr);
         logits_f32[(t0 + i) * experts + e] = r;
         if (logits_out) logits_out[(t0 + i) * experts + e] = from_f32<T>(r);
