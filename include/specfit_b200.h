@@ -615,6 +615,28 @@ SF_API int sf_ep_peer_recv(const sf_ep_peer* d, int32_t* counts, int32_t* offset
 /* Store each weighted output row into its source's region. */
 SF_API int sf_ep_peer_return(const sf_ep_peer* d, const void* out_sorted,
                              const int32_t* return_src, const int32_t* offsets, void* stream);
+/*
+ * The return fused into the expert GEMM (instead of sf_ep_peer_return after
+ * sf_grouped_swiglu): sf_ep_peer_return_plan writes, for every sorted row,
+ * the address of its row in its source's region (0 for none) into
+ * dst_row[world * cap_routes]; sf_grouped_swiglu_peer runs the tcgen05
+ * grouped SwiGLU over the received rows (rows = world * cap_routes, experts =
+ * local_experts, act_workspace [rows, intermediate]) with phase 2 storing
+ * each weighted output row straight to dst_row[r] (NVLink stores for a
+ * peer), every CTA counting itself on `ticket` (a device uint32, zero before
+ * the first call; each call leaves it zero) and the last one adding `grid`
+ * to this rank's return counter in every region, exactly what
+ * sf_ep_peer_return adds, so sf_ep_peer_finish is unchanged.  Every rank of
+ * an exchange must use the same form for a layer.  bf16 only.  No
+ * counterpart in the reference, which runs on one GPU (no expert parallelism).
+ */
+SF_API int sf_ep_peer_return_plan(const sf_ep_peer* d, const int32_t* return_src, const int32_t* offsets,
+                                  uint64_t* dst_row, void* stream);
+SF_API int sf_grouped_swiglu_peer(const sf_ep_peer* d, const void* hidden_sorted, const float* weights_sorted,
+                                  const int32_t* offsets, const int32_t* active, const int32_t* num_active,
+                                  const int32_t* expert_slot, const void* slot_storage, int64_t slot_count,
+                                  int64_t slot_stride_elems, int intermediate_size, void* act_workspace,
+                                  const uint64_t* dst_row, uint32_t* ticket, void* stream);
 /* Wait for every destination's outputs and combine them (sf_moe_combine). */
 SF_API int sf_ep_peer_finish(const sf_ep_peer* d, const int64_t* topk_index,
                              const int32_t* route_row, int64_t tokens, int num_experts,

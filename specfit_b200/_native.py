@@ -179,6 +179,9 @@ SIGNATURES = {
                                _vp]),
     "sf_ep_peer_recv": (_i32, [_peer_p, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sf_ep_peer_return": (_i32, [_peer_p, _vp, _vp, _vp, _vp]),
+    "sf_ep_peer_return_plan": (_i32, [_peer_p, _vp, _vp, _vp, _vp]),
+    "sf_grouped_swiglu_peer": (_i32, [_peer_p, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp,
+                                      _vp, _vp]),
     "sf_ep_peer_finish": (_i32, [_peer_p, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
     "sf_tree_mask_words": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp]),
     "sf_kv_compact": (_i32, [_vp, _i32, _i32, _i32, _i64, _i64, _vp, _i32, _vp, _vp]),

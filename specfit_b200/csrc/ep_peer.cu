@@ -29,8 +29,11 @@
 // the ranks that did not arrive in `status`, and return, so a missing rank
 // turns into an error the host reads instead of a hung GPU.  Counts read from
 // peers are clamped to the capacities, so every access stays in bounds.
+#include <cuda.h>
+
 #include "dispatch.cuh"
 #include "ep.cuh"
+#include "swiglu.h"
 
 namespace sf {
 namespace {
@@ -243,6 +246,43 @@ peer_return_kernel(const uint8_t* __restrict__ out_sorted, int64_t out_bytes,
   arrive_all(peers, world, me, L.ret_arrive);
 }
 
+// The return destination of every sorted row (the fused return): row
+// return_src[q] of route q from source s, j-th of that source, goes to
+// peers[s] + ret_rows + (me * cap_routes + j) * out_bytes; other rows get 0.
+// One CTA: the table is cleared, then filled.
+__global__ void __launch_bounds__(1024)
+peer_return_plan_kernel(const int32_t* __restrict__ return_src, const int32_t* __restrict__ n_routes,
+                        const int32_t* __restrict__ counts, const uint64_t* __restrict__ peers, int world,
+                        int me, int64_t cap_pairs, int64_t cap_routes, int K, int64_t out_bytes,
+                        int64_t cap_rows, PeerLayout L, uint64_t* __restrict__ dst_row) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int roff[kMaxWorld + 1];
+  if (threadIdx.x == 0) {
+    int o = 0;
+    for (int s = 0; s < world; ++s) {
+      roff[s] = o;
+      int p = counts[2 * s], r = counts[2 * s + 1];
+      p = p < 0 ? 0 : (p > cap_pairs ? (int)cap_pairs : p);
+      const int64_t rmax = (int64_t)p * K < cap_routes ? (int64_t)p * K : cap_routes;
+      r = r < 0 ? 0 : (r > rmax ? (int)rmax : r);
+      o += r;
+    }
+    roff[world] = o;
+  }
+  for (int64_t i = threadIdx.x; i < cap_rows; i += blockDim.x) dst_row[i] = 0ull;
+  __syncthreads();
+  const int R = min(*n_routes, roff[world]);
+  for (int q = threadIdx.x; q < R; q += blockDim.x) {
+    int s = 0;
+    while (s + 1 < world && q >= roff[s + 1]) ++s;
+    const int64_t j = q - roff[s];
+    const int r = return_src[q];
+    if (r >= 0 && r < cap_rows)
+      dst_row[r] = peers[s] + (uint64_t)L.ret_rows + (uint64_t)((me * cap_routes + j) * out_bytes);
+  }
+}
+
 int check_peer(const sf_ep_peer* d) {
   SF_CHECK_ARG(d != nullptr, "null peer descriptor");
   const int es = elem_size(d->dtype);
@@ -403,6 +443,43 @@ extern "C" int sf_ep_peer_return(const sf_ep_peer* d, const void* out_sorted,
       d->world, d->rank, d->cap_pairs, d->cap_routes, d->top_k, L);
   SF_CHECK_LAUNCH();
   return SF_OK;
+}
+
+extern "C" int sf_ep_peer_return_plan(const sf_ep_peer* d, const int32_t* return_src, const int32_t* offsets,
+                                      uint64_t* dst_row, void* stream) {
+  using namespace sf;
+  if (int rc = check_peer(d)) return rc;
+  SF_CHECK_ARG(return_src && offsets && dst_row, "null pointer argument");
+  const PeerLayout L = peer_layout(*d);
+  const uint8_t* base = static_cast<const uint8_t*>(d->local);
+  SF_CHECK_CUDA(launch_pdl(peer_return_plan_kernel, dim3(1), dim3(1024), 0, as_stream(stream), return_src,
+                           offsets + d->local_experts, reinterpret_cast<const int32_t*>(base + L.recv_counts),
+                           d->peers, d->world, d->rank, d->cap_pairs, d->cap_routes, d->top_k,
+                           d->out_row_bytes, (int64_t)d->world * d->cap_routes, L, dst_row));
+  SF_CHECK_LAUNCH();
+  return SF_OK;
+}
+
+extern "C" int sf_grouped_swiglu_peer(const sf_ep_peer* d, const void* hidden_sorted, const float* weights_sorted,
+                                      const int32_t* offsets, const int32_t* active, const int32_t* num_active,
+                                      const int32_t* expert_slot, const void* slot_storage, int64_t slot_count,
+                                      int64_t slot_stride_elems, int intermediate_size, void* act_workspace,
+                                      const uint64_t* dst_row, uint32_t* ticket, void* stream) {
+  using namespace sf;
+  if (int rc = check_peer(d)) return rc;
+  SF_CHECK_ARG(d->dtype == SF_DTYPE_BF16, "the fused return needs bf16 rows");
+  SF_CHECK_ARG(hidden_sorted && weights_sorted && offsets && active && num_active && expert_slot &&
+                   slot_storage && act_workspace && dst_row && ticket,
+               "null pointer argument");
+  SF_CHECK_ARG(intermediate_size > 0 && slot_count > 0 &&
+                   slot_stride_elems >= 3LL * d->hidden_size * intermediate_size,
+               "slot_stride_elems must cover one packed expert");
+  const PeerLayout L = peer_layout(*d);
+  SwigluArgs a{hidden_sorted, weights_sorted, SF_DTYPE_BF16, offsets, active, num_active, expert_slot,
+               slot_storage, slot_count, slot_stride_elems, d->local_experts, d->hidden_size,
+               intermediate_size, (int64_t)d->world * d->cap_routes, act_workspace, act_workspace};
+  SwigluPeerOut peer{dst_row, ticket, d->peers, L.ret_arrive, d->world, d->rank, (unsigned long long)d->grid};
+  return swiglu_tcgen05_peer(a, peer, as_stream(stream));
 }
 
 extern "C" int sf_ep_peer_finish(const sf_ep_peer* d, const int64_t* topk_index,

@@ -59,6 +59,8 @@ constexpr int kMaxExperts = 1024;  // experts per launch (the unit table lives i
 struct __align__(8) SmemTail {
   float upbuf[64 * kUpPitch];
   int rowtok[kBN];  // gathered variant: token row of each row of the current pass
+  float w_sm[kBN];        // phase 2: routing weight of each row of the unit's pass
+  uint64_t dst_sm[kBN];   // phase 2, fused return: destination of each row of the pass
   int unit_first[kMaxExperts + 1];  // number of the first unit of active[a]; [n_active] = all units
   int unit_expert[kMaxExperts];     // active[a]
   uint64_t full[kStages];
@@ -156,14 +158,26 @@ __device__ __forceinline__ void for_each_unit(const SmemTail* tail, int m_tiles,
 // sorted row r = sorted_pos[r] / top_k) instead of from a gathered copy, and
 // phase 2 reads the routing weight of row r as topk_w[sorted_pos[r]].  The
 // staged tiles, and so every result, are the same as with the copy.
-template <int kPhase, bool kGather = false>
+// The last CTA of a fused-return launch signals every rank (SwigluPeerOut).
+__device__ __forceinline__ void peer_out_arrive(const SwigluPeerOut& p) {
+  __threadfence_system();  // this CTA's row stores, before its ticket
+  const unsigned int t = atomicAdd(p.ticket, 1u);
+  if (t == gridDim.x - 1) {
+    *p.ticket = 0u;
+    __threadfence_system();  // every CTA's ticket (and so its stores), before the arrivals
+    for (int r = 0; r < p.world; ++r)
+      atomicAdd_system(reinterpret_cast<unsigned long long*>(p.peers[r] + p.arrive_off) + p.me, p.per_epoch);
+  }
+}
+
+template <int kPhase, bool kGather = false, bool kPeerOut = false>
 __global__ void __launch_bounds__(kThreads, 1)
 swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                  const __grid_constant__ CUtensorMap tm_xw, const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                  const int32_t* __restrict__ num_active, const int32_t* __restrict__ expert_slot,
                  const float* __restrict__ w_sorted, int H, int I,
                  __nv_bfloat16* __restrict__ out, const int32_t* __restrict__ sorted_pos = nullptr,
-                 int top_k = 1, const float* __restrict__ topk_w = nullptr) {
+                 int top_k = 1, const float* __restrict__ topk_w = nullptr, SwigluPeerOut peer = {}) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
@@ -180,9 +194,19 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
   const int n_active = min(*num_active, kMaxExperts);
   // A CTA with no unit (an empty wave of a device-managed cache, or a grid
   // larger than the work) leaves before touching barriers or TMEM.
-  if (n_active <= 0) return;
+  if (n_active <= 0) {
+    if constexpr (kPeerOut) {
+      if (threadIdx.x == 0) peer_out_arrive(peer);
+    }
+    return;
+  }
   const int units = number_units(tail, space.m_tiles, offsets, active, n_active);
-  if ((int)blockIdx.x >= units) return;
+  if ((int)blockIdx.x >= units) {
+    if constexpr (kPeerOut) {
+      if (threadIdx.x == 0) peer_out_arrive(peer);
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -319,6 +343,16 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
       ptx::tc_fence_after();
       const int chunks = (u.npass + 15) / 16;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * kBN;
+      if constexpr (kPhase == 2) {
+        // The pass's routing weights (and return destinations) once per
+        // unit, instead of one global load per row by every thread.
+        if (row < u.npass) {
+          const int r = u.n0 + row;
+          tail->w_sm[row] = kGather ? topk_w[sorted_pos[r]] : w_sorted[r];
+          if constexpr (kPeerOut) tail->dst_sm[row] = peer.dst_row[r];
+        }
+        ptx::named_bar_sync(1, 128);
+      }
       for (int c = 0; c < chunks; ++c) {
         float v[16];
         ptx::tmem_ld_16(tbase + c * 16, v);
@@ -351,8 +385,14 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
             if (j < u.npass) {
               const int r = u.n0 + j;
               const float y = bf16r(v[i]);
-              const float w = kGather ? topk_w[sorted_pos[r]] : w_sorted[r];
-              out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w);
+              const float w = tail->w_sm[j];
+              if constexpr (kPeerOut) {
+                // Straight into the source rank's return row (over NVLink for a peer).
+                const uint64_t dst = tail->dst_sm[j];
+                if (dst) reinterpret_cast<__nv_bfloat16*>(dst)[col] = __float2bfloat16_rn(y * w);
+              } else {
+                out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w);
+              }
             }
           }
         }
@@ -370,6 +410,10 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     __syncwarp();
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if constexpr (kPeerOut) {
+    __syncthreads();  // every epilogue store of this CTA is issued
+    if (threadIdx.x == 0) peer_out_arrive(peer);
   }
 }
 
@@ -433,7 +477,8 @@ namespace {
 // Encodes the four tensor maps and launches both phases.  With `gather`
 // (the gathered variant) a.hidden_sorted is the unsorted hidden [tokens, H]
 // and phase 1 loads its rows one box row at a time with gather4.
-int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaStream_t stream) {
+int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, const SwigluPeerOut* peer,
+                          cudaStream_t stream) {
   static std::atomic<unsigned long long> configured{0};
   if (int rc = once_per_device(configured, [] {
         int dev = 0, major = 0;
@@ -447,6 +492,8 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
         SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<1, true>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+        SF_CHECK_CUDA(cudaFuncSetAttribute(swiglu_tc_kernel<2, false, true>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         return SF_OK;
       }))
@@ -492,12 +539,12 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
     SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
                              tm_w1, tm_x1, tm_x1w, a.offsets, a.active, a.num_active, a.expert_slot,
                              a.weights_sorted, H, I, act, gather->sorted_pos, gather->top_k,
-                             gather->topk_weights));
+                             gather->topk_weights, SwigluPeerOut{}));
     SF_CHECK_LAUNCH();
     SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
                              tm_w2, tm_x2, tm_x2w, a.offsets, a.active, a.num_active, a.expert_slot,
                              a.weights_sorted, H, I, out, gather->sorted_pos, gather->top_k,
-                             gather->topk_weights));
+                             gather->topk_weights, SwigluPeerOut{}));
     SF_CHECK_LAUNCH();
     return SF_OK;
   }
@@ -505,11 +552,18 @@ int swiglu_tcgen05_launch(const SwigluArgs& a, const SwigluGather* gather, cudaS
   const float* no_w = nullptr;
   SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<1>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
                            tm_w1, tm_x1, tm_x1w, a.offsets, a.active, a.num_active, a.expert_slot,
-                           a.weights_sorted, H, I, act, no_pos, 1, no_w));
+                           a.weights_sorted, H, I, act, no_pos, 1, no_w, SwigluPeerOut{}));
   SF_CHECK_LAUNCH();
+  if (peer) {
+    SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2, false, true>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
+                             tm_w2, tm_x2, tm_x2w, a.offsets, a.active, a.num_active, a.expert_slot,
+                             a.weights_sorted, H, I, out, no_pos, 1, no_w, *peer));
+    SF_CHECK_LAUNCH();
+    return SF_OK;
+  }
   SF_CHECK_CUDA(launch_pdl(swiglu_tc_kernel<2>, dim3(grid), dim3(kThreads), kSmemBytes, stream,
                            tm_w2, tm_x2, tm_x2w, a.offsets, a.active, a.num_active, a.expert_slot,
-                           a.weights_sorted, H, I, out, no_pos, 1, no_w));
+                           a.weights_sorted, H, I, out, no_pos, 1, no_w, SwigluPeerOut{}));
   SF_CHECK_LAUNCH();
   return SF_OK;
 }
@@ -521,7 +575,7 @@ int swiglu_tcgen05(const SwigluArgs& a, cudaStream_t stream) {
     return set_error(SF_ERR_UNSUPPORTED,
                      "tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0 and 16-byte aligned buffers");
   if (a.rows == 0) return SF_OK;
-  return swiglu_tcgen05_launch(a, nullptr, stream);
+  return swiglu_tcgen05_launch(a, nullptr, nullptr, stream);
 }
 
 int swiglu_tcgen05_gathered(const SwigluArgs& a, const SwigluGather& g, cudaStream_t stream) {
@@ -530,7 +584,14 @@ int swiglu_tcgen05_gathered(const SwigluArgs& a, const SwigluGather& g, cudaStre
     return set_error(SF_ERR_UNSUPPORTED,
                      "gathered tcgen05 SwiGLU needs bf16, H%%128==0, I%%64==0, 16-byte aligned buffers "
                      "and rows == tokens * top_k");
-  return swiglu_tcgen05_launch(a, &g, stream);
+  return swiglu_tcgen05_launch(a, &g, nullptr, stream);
+}
+
+int swiglu_tcgen05_peer(const SwigluArgs& a, const SwigluPeerOut& peer, cudaStream_t stream) {
+  if (!swiglu_tcgen05_supports(a) || !device_is_sm100())
+    return set_error(SF_ERR_UNSUPPORTED,
+                     "the fused-return SwiGLU needs the tcgen05 kernel (bf16, H%%128==0, I%%64==0, aligned buffers)");
+  return swiglu_tcgen05_launch(a, nullptr, &peer, stream);
 }
 
 int swiglu_status(int* status, int reset) {

@@ -24,10 +24,15 @@ from .. import ops
 class PeerExchange:
     def __init__(self, *, rank: int, world: int, max_tokens: int, hidden_size: int, top_k: int,
                  local_experts: int, device, dtype=torch.bfloat16, group=None, grid: int = 64,
-                 wait_limit_ms: int = 2000) -> None:
+                 wait_limit_ms: int = 2000, fused_return: bool = True) -> None:
         self.rank, self.world, self.group = rank, world, group
         self.device = torch.device(device)
         self.dtype = dtype
+        # The return all-to-all stored by the expert GEMM's epilogue (bf16,
+        # tcgen05 shapes); otherwise a separate push kernel after it.  Every
+        # rank of an exchange must make the same choice.
+        self.fused_return = fused_return
+        self._ticket = torch.zeros(1, dtype=torch.int32, device=self.device)
         d = N.EpPeer()
         d.world, d.rank, d.top_k, d.hidden_size = world, rank, top_k, hidden_size
         d.dtype = ops.dtype_code(dtype)
@@ -176,13 +181,32 @@ class PeerExchange:
                                       num_active.data_ptr(), return_src.data_ptr(), err.data_ptr(),
                                       xs.data_ptr(), ws.data_ptr(), stream), "sf_ep_peer_recv")
         mark()
-        disp = ops.Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, err,
-                            self.world * d.cap_pairs, K, El)
-        ys = ops.grouped_swiglu(xs, ws, disp, moe.slot, moe.storage, moe.hidden, moe.inter)
-        mark()
-        N.check(N.lib.sf_ep_peer_return(ctypes.byref(d), ys.data_ptr(), return_src.data_ptr(),
-                                        offsets.data_ptr(), stream), "sf_ep_peer_return")
-        mark()
+        if (self.fused_return and self.dtype == torch.bfloat16 and moe.storage.dtype == torch.bfloat16
+                and moe.hidden % 128 == 0 and moe.inter % 64 == 0):
+            # The return rides on the expert GEMM: phase 2 stores each output
+            # row straight into its source's region and the last CTA signals.
+            dst_row = torch.empty(rows, dtype=torch.int64, device=dev)
+            N.check(N.lib.sf_ep_peer_return_plan(ctypes.byref(d), return_src.data_ptr(), offsets.data_ptr(),
+                                                 dst_row.data_ptr(), stream), "sf_ep_peer_return_plan")
+            act = torch.empty(max(rows, 1), moe.inter, dtype=self.dtype, device=dev)
+            N.check(N.lib.sf_grouped_swiglu_peer(ctypes.byref(d), xs.data_ptr(), ws.data_ptr(), offsets.data_ptr(),
+                                                 active.data_ptr(), num_active.data_ptr(), moe.slot.data_ptr(),
+                                                 moe.storage.data_ptr(), moe.storage.shape[0],
+                                                 moe.storage.stride(0), moe.inter, act.data_ptr(),
+                                                 dst_row.data_ptr(), self._ticket.data_ptr(), stream),
+                    "sf_grouped_swiglu_peer")
+            ops._launched(3)  # the plan and the two SwiGLU phases
+            mark()
+            mark()  # (the return has no phase of its own)
+        else:
+            disp = ops.Dispatch(counts, offsets, sorted_pos, inv_pos, active, num_active, err,
+                                self.world * d.cap_pairs, K, El)
+            ys = ops.grouped_swiglu(xs, ws, disp, moe.slot, moe.storage, moe.hidden, moe.inter)
+            mark()
+            N.check(N.lib.sf_ep_peer_return(ctypes.byref(d), ys.data_ptr(), return_src.data_ptr(),
+                                            offsets.data_ptr(), stream), "sf_ep_peer_return")
+            ops._launched(1)
+            mark()
         out = torch.empty(T, d.hidden_size, dtype=self.dtype, device=dev)
         N.check(N.lib.sf_ep_peer_finish(ctypes.byref(d), idx.data_ptr(), route_row.data_ptr(), T, E,
                                         N.SF_REDUCE_MODEL_DTYPE, out.data_ptr(), stream),
@@ -190,5 +214,5 @@ class PeerExchange:
         mark()
         if marks is not None:
             self.phase_events.append(marks)
-        ops._launched(8 if T else 7)  # the grouped SwiGLU counts its own two
+        ops._launched(6 if T else 5)  # send (plan, push), receive (wait, group, gather), finish
         return out

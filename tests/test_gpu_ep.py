@@ -179,18 +179,21 @@ def test_one_rank_ep_model_equals_single_gpu_model():
     assert torch.equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("fused_return", [True, False])
 @pytest.mark.parametrize("tokens", [65, 520, 0])
-def test_peer_exchange_one_rank_equals_single_gpu(tokens, expert_storage):
+def test_peer_exchange_one_rank_equals_single_gpu(tokens, fused_return, expert_storage):
     """The peer-memory exchange run with oneself (push, bounded wait,
     grouping, gather, SwiGLU, return, wait, combine) gives the single-GPU
-    block bit for bit, repeatedly (arrival counters advance per layer)."""
+    block bit for bit, repeatedly (arrival counters advance per layer) —
+    with the return stored by the SwiGLU's epilogue and with the separate
+    return kernel."""
     from specfit_b200.runtime.ep_peer import PeerExchange
 
     g = torch.Generator(device="cuda").manual_seed(tokens)
     moe = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, intermediate_size=I,
                             local_storage=expert_storage, rank=0, world=1)
     peer = PeerExchange(rank=0, world=1, max_tokens=520, hidden_size=H, top_k=K, local_experts=E,
-                        device="cuda")
+                        device="cuda", fused_return=fused_return)
     moe.peer, moe.use_peer = peer, True
     try:
         for rep in range(3):
@@ -202,6 +205,7 @@ def test_peer_exchange_one_rank_equals_single_gpu(tokens, expert_storage):
             torch.cuda.synchronize()
             assert torch.equal(got, want)
         assert peer.status() == (0, 0)
+        assert int(peer._ticket.item()) == 0  # every fused launch leaves its ticket at zero
     finally:
         peer.close()
 
