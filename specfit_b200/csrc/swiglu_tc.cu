@@ -377,6 +377,31 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
             }
           }
           ptx::named_bar_sync(1, 128);
+        } else if constexpr (kPeerOut) {
+          // Straight into the source ranks' return rows (over NVLink for a
+          // peer), 16 bytes at a time: the warp's 32 columns x 16 rows go
+          // through shared memory (the gate/up buffer, idle in phase 2) so
+          // each lane stores whole 8-column pieces of a row.
+          __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(tail->upbuf) + quad * (16 * 32);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = c * 16 + i;
+            const float w = j < u.npass ? tail->w_sm[j] : 0.f;
+            stage[i * 32 + lane] = __float2bfloat16_rn(bf16r(v[i]) * w);
+          }
+          __syncwarp();
+          const int col0 = u.m_tile * kBM + quad * 32;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int piece = k * 32 + lane;  // 16 rows x 4 pieces of 8 columns
+            const int i = piece >> 2, q = piece & 3;
+            const int j = c * 16 + i;
+            const uint64_t dst = j < u.npass ? tail->dst_sm[j] : 0ull;
+            if (dst)
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + col0 + q * 8) =
+                  *reinterpret_cast<const uint4*>(stage + i * 32 + q * 8);
+          }
+          __syncwarp();
         } else {
           const int col = u.m_tile * kBM + row;
 #pragma unroll
@@ -386,13 +411,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
               const int r = u.n0 + j;
               const float y = bf16r(v[i]);
               const float w = tail->w_sm[j];
-              if constexpr (kPeerOut) {
-                // Straight into the source rank's return row (over NVLink for a peer).
-                const uint64_t dst = tail->dst_sm[j];
-                if (dst) reinterpret_cast<__nv_bfloat16*>(dst)[col] = __float2bfloat16_rn(y * w);
-              } else {
-                out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w);
-              }
+              out[(int64_t)r * H + col] = __float2bfloat16_rn(y * w);
             }
           }
         }
