@@ -25,9 +25,12 @@
 //               exchanged through shared memory, the sum added in half
 //               order), P half-row (bf16) -> shared memory; then
 //               O = O * exp(m_old - m_new) + O_j over its 64 dims in registers.
-// TMEM: S in columns [0, 128), O_j in [128, 256).  The order of the waits
-// (S_j consumed before P_j is published; O_j consumed before P_{j+1} is
-// published) lets both live in one buffer each.
+// TMEM: S_j in columns [0, 128) or [128, 256) by the parity of j, O_j in
+// [256, 384).  The MMA warp issues S_{j+1} = Q K_{j+1}^T before O_j = P_j V_j,
+// so the next block's scores are computed while the softmax warps finish
+// block j.  S_{j+1} reuses S_{j-1}'s columns, read before P_{j-1} was
+// published; P_{j+1} is written after O_j has been read back (so after the
+// O_j MMA read P_j); O_j is read back before P_{j+1} is published.
 //
 // Output: with one split the CTA normalises and writes bf16 [Tq, Hq, D];
 // otherwise it writes unnormalised O and (row max, row sum) per split for
@@ -61,14 +64,14 @@ constexpr int kQBytes = 2 * kRegion;           // Q: 128 rows x 128 d
 constexpr int kPBytes = 2 * kRegion;           // P: 128 rows x 128 keys
 constexpr int kKBytes = 2 * kRegion;           // one K block: 128 keys x 128 d
 constexpr int kStageBytes = 2 * kKBytes;       // K and V
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kSCol = 0, kOCol = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSCol = 0, kOCol = 256;  // S_j at kSCol + (j & 1) * 128
 
 struct __align__(8) Tail {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t q_ready;
-  uint64_t s_full;
+  uint64_t s_full[2];
   uint64_t p_full;
   uint64_t o_full;
   uint64_t mma_done;
@@ -130,7 +133,8 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       ptx::mbar_init(&tail->kv_empty[s], 1);
     }
     ptx::mbar_init(&tail->q_ready, 256);
-    ptx::mbar_init(&tail->s_full, 1);
+    ptx::mbar_init(&tail->s_full[0], 1);
+    ptx::mbar_init(&tail->s_full[1], 1);
     ptx::mbar_init(&tail->p_full, 256);
     ptx::mbar_init(&tail->o_full, 1);
     ptx::mbar_init(&tail->mma_done, 1);
@@ -179,16 +183,26 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
       const uint64_t qdesc = ptx::smem_desc_k_sw128(ptx::smem_u32(q_s));
       const uint64_t pdesc = ptx::smem_desc_k_sw128(ptx::smem_u32(p_s));
       bool ok = nblocks == 0 || ptx::mbar_wait(&tail->q_ready, 0, abort_flag, &g_attn_tc_status, 3);
-      for (int j = 0; ok && j < nblocks; ++j) {
+      // S_j = Q K_j^T into the S buffer of j's parity.
+      auto issue_s = [&](int j) -> bool {
         const int s = j % kStages;
-        if (!ptx::mbar_wait(&tail->kv_full[s], (j / kStages) & 1, abort_flag, &g_attn_tc_status, 4)) break;
+        if (!ptx::mbar_wait(&tail->kv_full[s], (j / kStages) & 1, abort_flag, &g_attn_tc_status, 4)) return false;
         ptx::tc_fence_after();
-        const uint32_t st = ptx::smem_u32(kv_s + (size_t)s * kStageBytes);
-        const uint64_t kdesc = ptx::smem_desc_k_sw128(st);
+        const uint64_t kdesc = ptx::smem_desc_k_sw128(ptx::smem_u32(kv_s + (size_t)s * kStageBytes));
+        const uint32_t scol = kSCol + (uint32_t)(j & 1) * 128;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k)
-          ptx::umma_f16(tmem + kSCol, qdesc + kstep_offset(k), kdesc + kstep_offset(k), idesc_s, k != 0);
-        ptx::umma_commit(&tail->s_full);
+          ptx::umma_f16(tmem + scol, qdesc + kstep_offset(k), kdesc + kstep_offset(k), idesc_s, k != 0);
+        ptx::umma_commit(&tail->s_full[j & 1]);
+        return true;
+      };
+      if (ok && nblocks > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < nblocks; ++j) {
+        const int s = j % kStages;
+        const uint32_t st = ptx::smem_u32(kv_s + (size_t)s * kStageBytes);
+        // The next block's scores first (its buffer's last reader, the
+        // softmax of block j - 1, published P_{j-1} before O_{j-1} was issued).
+        if (j + 1 < nblocks && !issue_s(j + 1)) break;
         if (!ptx::mbar_wait(&tail->p_full, j & 1, abort_flag, &g_attn_tc_status, 5)) break;
         ptx::tc_fence_after();
         // V block as the MN-major B operand: 16 keys (two 8-key atoms,
@@ -262,8 +276,10 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         win = rok ? w : 0ull;
       }
 
-      ok = __all_sync(0xffffffffu, ptx::mbar_wait(&tail->s_full, j & 1, abort_flag, &g_attn_tc_status, 7));
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(&tail->s_full[j & 1], (j >> 1) & 1, abort_flag,
+                                                  &g_attn_tc_status, 7));
       if (ok) ptx::tc_fence_after();
+      const uint32_t scol = kSCol + (uint32_t)(j & 1) * 128;
 
       // Pass 1: the half-row max of the visible scaled scores, then the row's.
       float mx = -INFINITY;
@@ -271,7 +287,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float sv[16];
-          ptx::tmem_ld_16(trow + kSCol + half * 64 + c * 16, sv);
+          ptx::tmem_ld_16(trow + scol + half * 64 + c * 16, sv);
           const uint32_t bits16 = (uint32_t)(win >> (c * 16)) & 0xFFFFu;
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -291,7 +307,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float sv[16];
-        ptx::tmem_ld_16(trow + kSCol + half * 64 + c * 16, sv);
+        ptx::tmem_ld_16(trow + scol + half * 64 + c * 16, sv);
         const uint32_t bits16 = (uint32_t)(win >> (c * 16)) & 0xFFFFu;
         uint32_t pk[8];
 #pragma unroll
