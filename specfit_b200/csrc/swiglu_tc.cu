@@ -131,16 +131,18 @@ __device__ __forceinline__ int number_units(SmemTail* tail, int m_tiles, const i
 }
 
 // Iterates this CTA's units in a fixed order; every role walks the same list.
-// CTA b takes units b, b + G, b + 2G, ...  Dealing out units rather than
+// CTA b takes units b, b + G, b + 2G, ... (G working CTAs).  Dealing out units rather than
 // whole tiles keeps the CTAs within one unit of each other when a few hot
 // experts need several passes (skewed routes), and the passes of one tile
 // run on neighbouring CTAs at about the same time, so the tile's repeated
 // weight reads are served by L2.
+// `ctas`: the CTAs that take units (see balanced_ctas).
 template <typename F>
 __device__ __forceinline__ void for_each_unit(const SmemTail* tail, int m_tiles, int n_active, int units,
-                                              const int32_t* offsets, const int32_t* expert_slot, F&& f) {
+                                              int ctas, const int32_t* offsets, const int32_t* expert_slot,
+                                              F&& f) {
   int a = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+  for (int u = blockIdx.x; u < units; u += ctas) {
     while (tail->unit_first[a + 1] <= u) ++a;
     const int e = tail->unit_expert[a];
     const int base = tail->unit_first[a];
@@ -158,6 +160,17 @@ __device__ __forceinline__ void for_each_unit(const SmemTail* tail, int m_tiles,
 // sorted row r = sorted_pos[r] / top_k) instead of from a gathered copy, and
 // phase 2 reads the routing weight of row r as topk_w[sorted_pos[r]].  The
 // staged tiles, and so every result, are the same as with the copy.
+// The CTAs that take units: as few as still finish in the same number of
+// rounds (ceil(units / grid)), so every working CTA takes that many units or
+// one fewer instead of a few CTAs taking one more than the rest; the SMs
+// left idle give their share of HBM bandwidth to the others (a weight
+// stream is bound by the device's bandwidth, not by one SM's).
+__device__ __forceinline__ int balanced_ctas(int units) {
+  const int g = (int)gridDim.x;
+  const int rounds = (units + g - 1) / g;
+  return rounds > 0 ? (units + rounds - 1) / rounds : g;
+}
+
 // The last CTA of a fused-return launch signals every rank (SwigluPeerOut).
 __device__ __forceinline__ void peer_out_arrive(const SwigluPeerOut& p) {
   __threadfence_system();  // this CTA's row stores, before its ticket
@@ -201,7 +214,8 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     return;
   }
   const int units = number_units(tail, space.m_tiles, offsets, active, n_active);
-  if ((int)blockIdx.x >= units) {
+  const int ctas = balanced_ctas(units);
+  if ((int)blockIdx.x >= ctas) {
     if constexpr (kPeerOut) {
       if (threadIdx.x == 0) peer_out_arrive(peer);
     }
@@ -238,7 +252,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       uint32_t it = 0;
-      for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
+      for_each_unit(tail, space.m_tiles, n_active, units, ctas, offsets, expert_slot, [&](const Unit& u) {
         const int nb = (u.npass + kBBox - 1) / kBBox;
         // A pass of many rows takes its token rows in one or two wide boxes
         // (fewer TMA requests per stage); rows past the pass are loaded but
@@ -293,7 +307,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t it = 0, unit = 0;
-      for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
+      for_each_unit(tail, space.m_tiles, n_active, units, ctas, offsets, expert_slot, [&](const Unit& u) {
         const int buf = unit & 1;
         const uint32_t aph = (unit >> 1) & 1;
         if (!ptx::mbar_wait(&tail->acc_empty[buf], aph ^ 1, abort_flag, &g_swiglu_status, 3)) return false;
@@ -330,7 +344,7 @@ swiglu_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant
     const int quad = warp & 3;             // TMEM lane quadrant this warp may read
     const int row = quad * 32 + lane;      // accumulator row = TMEM lane
     uint32_t unit = 0;
-    for_each_unit(tail, space.m_tiles, n_active, units, offsets, expert_slot, [&](const Unit& u) {
+    for_each_unit(tail, space.m_tiles, n_active, units, ctas, offsets, expert_slot, [&](const Unit& u) {
       const int buf = unit & 1;
       const uint32_t aph = (unit >> 1) & 1;
       ptx::mbar_wait(&tail->acc_full[buf], aph, abort_flag, &g_swiglu_status, 6);
