@@ -23,7 +23,7 @@ from .. import ops
 
 class PeerExchange:
     def __init__(self, *, rank: int, world: int, max_tokens: int, hidden_size: int, top_k: int,
-                 local_experts: int, device, dtype=torch.bfloat16, group=None, grid: int = 64,
+                 local_experts: int, device, dtype=torch.bfloat16, group=None, grid: int | None = None,
                  wait_limit_ms: int = 2000, fused_return: bool = True) -> None:
         self.rank, self.world, self.group = rank, world, group
         self.device = torch.device(device)
@@ -37,6 +37,8 @@ class PeerExchange:
         d.world, d.rank, d.top_k, d.hidden_size = world, rank, top_k, hidden_size
         d.dtype = ops.dtype_code(dtype)
         d.local_experts = local_experts
+        if grid is None:  # the push and gather kernels: one CTA per SM (equal on every rank of a box)
+            grid = torch.cuda.get_device_properties(self.device).multi_processor_count
         d.grid, d.wait_limit_ms = grid, wait_limit_ms
         d.cap_pairs = max_tokens
         d.cap_routes = max_tokens * top_k
